@@ -1,0 +1,264 @@
+/* si_cuda.h — C ABI of the B200 (sm_100a) batch-1 K-quant decode backend.
+ *
+ * This is the drop-in boundary that replaces the Metal backend
+ * (`MetalContext`, src/metal.rs) of vrlda/memory-aware-inference on the
+ * batch-1 decode hot path. Every entry point names the reference method it
+ * replaces (file:line inside the reference project). A Rust FFI crate binds
+ * these symbols one-to-one and keeps the reference's
+ * `Result<Vec<f32>, String>` surface: a non-zero status maps to `Err` with the
+ * text of si_last_error().
+ *
+ * Conventions
+ *  - Every function returns an int status: SI_OK (0) or a negative SI_E_*.
+ *  - Plain pointers are HOST memory unless the function name ends in `_dev`;
+ *    `_dev` functions take device pointers and a cudaStream_t (passed as
+ *    void*), enqueue work and return without synchronising.
+ *  - Host-memory entry points are synchronous, like the reference's
+ *    commit-and-wait calls (metal.rs:2320-2337): inputs are copied in, the
+ *    kernel runs, outputs are copied back before the call returns.
+ *  - One context serves one compute thread plus any number of threads that
+ *    upload weights (metal.rs:2585-2640 are called from staging workers);
+ *    uploads are internally serialised.
+ */
+#ifndef SI_CUDA_H
+#define SI_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define SI_OK 0
+#define SI_E_INVALID (-1)  /* shape / length / argument validation failed */
+#define SI_E_CUDA (-2)     /* a CUDA runtime call failed */
+#define SI_E_NOMEM (-3)    /* device or pinned allocation failed */
+#define SI_E_BUDGET (-4)   /* plan does not fit the HBM budget */
+#define SI_E_TIMEOUT (-5)  /* a bounded device or host wait gave up */
+#define SI_E_COMM (-6)     /* NCCL failure */
+#define SI_E_STATE (-7)    /* object used in the wrong state (e.g. KV full) */
+#define SI_E_UNSUPPORTED (-8)
+
+/* ---- GGML tensor types (quant.rs:8-16) ---------------------------------- */
+#define SI_GGML_TYPE_F32 0u
+#define SI_GGML_TYPE_Q4_K 12u
+#define SI_GGML_TYPE_Q5_K 13u
+#define SI_GGML_TYPE_Q6_K 14u
+
+typedef struct si_ctx si_ctx;
+typedef struct si_weight si_weight;
+typedef struct si_model si_model;
+
+/* Context configuration: one explicit struct instead of the reference's
+ * SI_* environment variables (qwen35_runtime.rs:1788-1793, 2288-2293). */
+typedef struct si_ctx_config {
+  uint64_t hbm_budget_bytes; /* bound for model weights+ring+state; 0 = no bound */
+  uint32_t stage_depth;      /* staging-ring depth: default 3, clamped to 1..4 */
+  uint32_t flags;            /* reserved, 0 */
+} si_ctx_config;
+
+/* ---- context (MetalContext::new, metal.rs:2170) ------------------------- */
+int si_ctx_create(int device, const si_ctx_config* cfg, si_ctx** out);
+void si_ctx_destroy(si_ctx* ctx);
+/* Text of the last error on this context (the reference's Err(String)). */
+const char* si_last_error(const si_ctx* ctx);
+/* Text of the last error of a call that had no context (si_ctx_create). */
+const char* si_global_last_error(void);
+/* Number of SMs and the device ordinal the context runs on. */
+int si_ctx_info(const si_ctx* ctx, int* device, int* sm_count);
+/* The context's compute stream (cudaStream_t as void*). */
+void* si_ctx_stream(si_ctx* ctx);
+
+/* ---- telemetry (metal.rs:2312-2445) ------------------------------------- */
+typedef struct si_stats {
+  uint64_t current_allocated_bytes;
+  uint64_t peak_allocated_bytes;     /* peak_allocated_bytes, metal.rs:2339 */
+  uint64_t peak_active_weight_bytes; /* metal.rs:2343 */
+  uint64_t peak_kv_bytes;            /* metal.rs:2347 */
+  uint64_t peak_scratch_bytes;       /* metal.rs:2351 */
+  uint64_t submitted;                /* command_stats, metal.rs:2316 */
+  uint64_t waited;
+  uint64_t wait_nanos;
+} si_stats;
+int si_get_stats(const si_ctx* ctx, si_stats* out);
+int si_reset_peaks(si_ctx* ctx); /* reset_peaks, metal.rs:2358 */
+
+/* ---- weights (QuantWeight, metal.rs:1840-1846) -------------------------- */
+/* upload_quant_weight_private (metal.rs:2502): copy bytes into device memory. */
+int si_weight_upload(si_ctx* ctx, const void* host, uint64_t bytes, uint32_t ggml_type,
+                     si_weight** out);
+/* bind_quant_weight_mapped (metal.rs:2549): keep the bytes in (registered,
+ * pinned) host memory; each use streams them to the device first. The host
+ * bytes must outlive the handle (metal.rs:2614-2617). */
+int si_weight_bind_host(si_ctx* ctx, const void* host, uint64_t bytes, uint32_t ggml_type,
+                        si_weight** out);
+void si_weight_free(si_weight* w);
+uint64_t si_weight_bytes(const si_weight* w);   /* QuantWeight::byte_len */
+uint32_t si_weight_type(const si_weight* w);    /* QuantWeight::ggml_type */
+const void* si_weight_device_ptr(const si_weight* w); /* NULL for host-bound */
+
+/* ---- lossless dequant (quant.rs:18-174), parity use --------------------- */
+int si_dequantize(si_ctx* ctx, uint32_t ggml_type, const void* bytes, uint64_t nbytes,
+                  uint64_t elements, float* out);
+int si_dequantize_dev(si_ctx* ctx, uint32_t ggml_type, const void* bytes_dev,
+                      uint64_t elements, float* out_dev, void* stream);
+/* q4_k_embedding_row (metal.rs:3734): dequantize one Q4_K row. */
+int si_q4_k_embedding_row(si_ctx* ctx, const void* row_bytes, uint64_t nbytes,
+                          uint64_t columns, float* out);
+
+/* ---- K-quant matvec: y = W x, W row-major GGUF super-blocks -------------- */
+/* gguf_quant_matvec_bytes (metal.rs:4000); q4_k_matvec / q5_k_matvec /
+ * q6_k_matvec (metal.rs:3357, 4307, 4325) are this call with a fixed type. */
+int si_gguf_quant_matvec_bytes(si_ctx* ctx, uint32_t ggml_type, const void* w, uint64_t nbytes,
+                               uint64_t rows, uint64_t cols, const float* x, float* y);
+int si_q4_k_matvec(si_ctx* ctx, const void* w, uint64_t nbytes, uint64_t rows, uint64_t cols,
+                   const float* x, float* y);
+int si_q5_k_matvec(si_ctx* ctx, const void* w, uint64_t nbytes, uint64_t rows, uint64_t cols,
+                   const float* x, float* y);
+int si_q6_k_matvec(si_ctx* ctx, const void* w, uint64_t nbytes, uint64_t rows, uint64_t cols,
+                   const float* x, float* y);
+/* gguf_quant_matvec_weight (metal.rs:3923). */
+int si_gguf_quant_matvec_weight(si_ctx* ctx, const si_weight* w, uint64_t rows, uint64_t cols,
+                                const float* x, float* y);
+/* gguf_quant_matvec_many_weights (metal.rs:4652): n <= 4 matrices, one x. */
+int si_gguf_quant_matvec_many_weights(si_ctx* ctx, uint32_t n, const si_weight* const* w,
+                                      const uint64_t* rows, const uint64_t* cols,
+                                      const float* x, float* const* y);
+/* Device form: `w_dev` holds rows*cols/256 blocks of `ggml_type`. */
+int si_qmatvec_dev(si_ctx* ctx, uint32_t ggml_type, const void* w_dev, uint64_t rows,
+                   uint64_t cols, const float* x_dev, float* y_dev, void* stream);
+/* f32_matvec (metal.rs:2983). */
+int si_f32_matvec(si_ctx* ctx, const float* w, uint64_t rows, uint64_t cols, const float* x,
+                  float* y);
+
+/* ---- fused SwiGLU (metal.rs:3402-3732) ----------------------------------- */
+/* q4_k_fused_gate_up (metal.rs:3402): out = SiLU(G x) * (U x). */
+int si_q4_k_fused_gate_up(si_ctx* ctx, const void* gate, const void* up, uint64_t nbytes,
+                          uint64_t rows, uint64_t cols, const float* x, float* out);
+/* q4_k_fused_gate_up_weights (metal.rs:3489). */
+int si_q4_k_fused_gate_up_weights(si_ctx* ctx, const si_weight* gate, const si_weight* up,
+                                  uint64_t rows, uint64_t cols, const float* x, float* out);
+/* gguf_quant_fused_mlp_weights (metal.rs:3569): y = D (SiLU(G x) * (U x)). */
+int si_gguf_quant_fused_mlp_weights(si_ctx* ctx, const si_weight* gate, const si_weight* up,
+                                    const si_weight* down, uint64_t gate_rows, uint64_t cols,
+                                    uint64_t down_rows, const float* x, float* y);
+int si_fused_gate_up_dev(si_ctx* ctx, uint32_t ggml_type, const void* gate_dev,
+                         const void* up_dev, uint64_t rows, uint64_t cols, const float* x_dev,
+                         float* out_dev, void* stream);
+int si_fused_mlp_dev(si_ctx* ctx, uint32_t gate_type, const void* gate_dev, const void* up_dev,
+                     uint32_t down_type, const void* down_dev, uint64_t inter, uint64_t hidden,
+                     const float* x_dev, float* act_dev, float* y_dev, void* stream);
+
+/* ---- Gated DeltaNet primitives (qwen35.rs, metal.rs:3122-3352) ----------- */
+/* gated_delta_step (metal.rs:3122): state [heads][key_dim][value_dim]. */
+int si_gated_delta_step(si_ctx* ctx, const float* q, const float* k, const float* v,
+                        const float* gate, const float* beta, const float* state_in,
+                        uint64_t heads, uint64_t key_dim, uint64_t value_dim, float* out,
+                        float* state_out);
+/* causal_conv1d_step (metal.rs:3263): state [channels][kernel-1], chronological. */
+int si_causal_conv1d_step(si_ctx* ctx, const float* x, const float* state_in, const float* w,
+                          uint64_t channels, uint64_t kernel, float* out, float* state_out);
+/* rms_norm_gated (metal.rs:2773) and rms_norm_heads (metal.rs:2856). */
+int si_rms_norm_gated(si_ctx* ctx, const float* x, const float* gate, const float* w,
+                      uint64_t heads, uint64_t head_dim, float eps, float* out);
+int si_rms_norm_heads(si_ctx* ctx, const float* x, const float* w, uint64_t heads,
+                      uint64_t head_dim, float eps, float* out);
+
+/* ---- attention (metal.rs:6860-7083) -------------------------------------- */
+/* rope (metal.rs:6860): adjacent-pair rotation over the whole head_dim. */
+int si_rope(si_ctx* ctx, const float* x, uint64_t heads, uint64_t head_dim, uint64_t position,
+            float theta, float* out);
+#define SI_CACHE_F32 0
+#define SI_CACHE_BF16 1
+/* AttentionDecodeInput (metal.rs:27-38) plus the cache element type. */
+typedef struct si_attention_decode_input {
+  const float* query;      /* [query_heads * head_dim] */
+  const void* key_cache;   /* [kv_heads][capacity][head_dim], f32 or bf16 bits */
+  const void* value_cache;
+  const float* new_keys;   /* [kv_heads * head_dim] current token, f32 */
+  const float* new_values;
+  uint64_t query_heads, key_value_heads, head_dim, cached_tokens, cache_capacity_tokens;
+  int cache_type;          /* SI_CACHE_F32 or SI_CACHE_BF16 */
+} si_attention_decode_input;
+/* attention_decode (metal.rs:6915). */
+int si_attention_decode(si_ctx* ctx, const si_attention_decode_input* in, float* out);
+
+/* ---- greedy argmax (runtime.rs:4301-4309) -------------------------------- */
+/* Largest finite value under f32::total_cmp; the last index among equals. */
+int si_argmax(si_ctx* ctx, const float* logits, uint64_t n, uint32_t* index);
+
+/* ---- synthetic Qwen3.6-shaped model ------------------------------------- */
+/* Tensor ids of one decoder layer (qwen35_runtime.rs:419-446, 640-657) and of
+ * the globals (stored under layer index == layers). */
+enum {
+  SI_T_ATTN_NORM = 0, SI_T_POST_NORM, SI_T_FFN_GATE, SI_T_FFN_UP, SI_T_FFN_DOWN,
+  SI_T_SSM_QKV, SI_T_SSM_Z, SI_T_SSM_ALPHA, SI_T_SSM_BETA, SI_T_SSM_CONV, SI_T_SSM_A,
+  SI_T_SSM_DT, SI_T_SSM_NORM, SI_T_SSM_OUT,
+  SI_T_ATTN_Q, SI_T_ATTN_K, SI_T_ATTN_V, SI_T_ATTN_O, SI_T_ATTN_QNORM, SI_T_ATTN_KNORM,
+  SI_T_TOKEN_EMBD, SI_T_OUTPUT_NORM, SI_T_OUTPUT,
+  SI_T_COUNT
+};
+
+/* GgufQwen35Config (model.rs:321-442) restricted to what decode needs. */
+typedef struct si_model_config {
+  uint32_t hidden, intermediate, layers, vocab;
+  uint32_t attn_interval;                       /* full attention where (l+1)%interval==0 */
+  uint32_t attn_q_heads, attn_kv_heads, attn_head_dim, rotary_dim;
+  float rope_theta;
+  uint32_t gdn_key_heads, gdn_value_heads, gdn_head_dim, conv_kernel;
+  float rms_eps;
+  uint32_t kv_capacity;                         /* KV positions per attention layer */
+  uint32_t eos_token;                           /* 0xFFFFFFFF = none */
+  uint32_t mlp_type, down_type, head_type;      /* ggml types of gate/up, down, output */
+} si_model_config;
+
+/* Residency / staging plan (qwen35_runtime.rs:1552-1733, planner.rs:174-251). */
+typedef struct si_plan_info {
+  uint64_t budget_bytes;
+  uint64_t resident_weight_bytes;  /* weights uploaded once */
+  uint64_t ring_bytes;             /* staging ring slots */
+  uint64_t state_bytes;            /* GDN state + KV cache */
+  uint64_t scratch_bytes;
+  uint64_t streamed_bytes_per_token;
+  uint32_t resident_layers, streamed_layers, stage_depth, head_resident;
+} si_plan_info;
+
+/* Fill a config with the BASELINE 27B shape (hidden 5120, 64 layers, ...). */
+void si_model_config_qwen36_27b(si_model_config* c);
+/* Build a model with seeded synthetic weights in pinned host memory, plan
+ * residency within ctx's HBM budget, upload the resident set. With a
+ * communicator attached (si_ctx_comm_init) every rank builds only its shard. */
+int si_model_create_synthetic(si_ctx* ctx, const si_model_config* c, uint64_t seed,
+                              si_model** out);
+void si_model_destroy(si_model* m);
+int si_model_plan(const si_model* m, si_plan_info* out);
+/* Host copy of one tensor (the full, unsharded tensor on every rank). */
+int si_model_host_tensor(const si_model* m, uint32_t layer, uint32_t tensor, const void** ptr,
+                         uint64_t* bytes, uint32_t* ggml_type);
+int si_model_reset(si_model* m);                     /* Qwen35Runtime::reset */
+/* embed_token (qwen35_runtime.rs:2122). */
+int si_model_embed(si_model* m, uint32_t token, float* hidden_out);
+/* decode_hidden (qwen35_runtime.rs:1776): hidden is read and overwritten. */
+int si_model_decode_hidden(si_model* m, uint64_t position, float* hidden);
+/* logits (qwen35_runtime.rs:2132). */
+int si_model_logits(si_model* m, const float* hidden, float* logits);
+/* decode_token (qwen35_runtime.rs:2229): embed, decode, logits, argmax. */
+int si_model_decode_token(si_model* m, uint32_t token, uint64_t position, uint32_t* next,
+                          float* logits /* may be NULL */);
+/* run_gguf_generation (runtime.rs:3560): token-by-token prefill, greedy loop.
+ * Writes up to max_new ids; *n_out receives the count (stops after EOS). */
+int si_model_generate(si_model* m, const uint32_t* prompt, uint64_t n_prompt, uint64_t max_new,
+                      uint32_t* out_ids, uint64_t* n_out);
+
+/* ---- multi-GPU row sharding over NCCL ----------------------------------- */
+#define SI_COMM_ID_BYTES 128
+int si_comm_unique_id(void* id_out /* SI_COMM_ID_BYTES */);
+int si_ctx_comm_init(si_ctx* ctx, int nranks, int rank, const void* id);
+int si_ctx_comm_info(const si_ctx* ctx, int* nranks, int* rank);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SI_CUDA_H */

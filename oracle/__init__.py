@@ -1,0 +1,170 @@
+"""ctypes binding of the CPU oracle (oracle/oracle.cpp).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, ``__graft_entry__.smoke()`` and
+``bench.py`` (cpu_baseline and the ``--impl reference`` arm) as the checker /
+CPU baseline. The product path never imports this module.
+
+The oracle restates the reference's CPU code (src/quant.rs, src/qwen35.rs,
+src/qwen35_runtime.rs, src/metal.rs CPU test restatements, src/runtime.rs
+argmax); see the file:line citations in oracle.cpp.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+GGML_F32, GGML_Q4_K, GGML_Q5_K, GGML_Q6_K = 0, 12, 13, 14
+BLOCK_BYTES = {GGML_Q4_K: 144, GGML_Q5_K: 176, GGML_Q6_K: 210}
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+
+
+def build(force: bool = False) -> str:
+    src = os.path.join(_HERE, "oracle.cpp")
+    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+        subprocess.check_call(["make", "-s", "-C", _HERE, "liboracle.so"])
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = C.CDLL(_LIB_PATH)
+        sz, i32, u32 = C.c_size_t, C.c_int, C.c_uint32
+        L.or_dequantize.argtypes = [u32, C.c_void_p, sz, sz, _f32p]
+        L.or_matvec.argtypes = [u32, C.c_void_p, sz, sz, _f32p, _f32p, i32]
+        L.or_fused_gate_up.argtypes = [C.c_void_p, C.c_void_p, sz, sz, _f32p, _f32p, i32]
+        L.or_fused_mlp.argtypes = [u32, C.c_void_p, C.c_void_p, u32, C.c_void_p, sz, sz, _f32p, _f32p, i32]
+        L.or_rms_norm_heads.argtypes = [_f32p, _f32p, sz, sz, C.c_float, _f32p]
+        L.or_gated_rms_norm.argtypes = [_f32p, _f32p, _f32p, sz, sz, C.c_float, _f32p]
+        L.or_causal_conv1d_step.argtypes = [_f32p, _f32p, _f32p, sz, sz, _f32p]
+        L.or_gdn_step.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, sz, sz, sz, _f32p]
+        L.or_rope.argtypes = [_f32p, sz, sz, sz, C.c_float, _f32p]
+        L.or_attention_decode.argtypes = [_f32p, C.c_void_p, C.c_void_p, i32, _f32p, _f32p,
+                                          sz, sz, sz, sz, sz, _f32p]
+        L.or_argmax.argtypes = [_f32p, sz]
+        L.or_argmax.restype = C.c_long
+        L.or_f32_to_bf16.argtypes = [C.c_float]
+        L.or_f32_to_bf16.restype = C.c_uint16
+        L.or_model_create.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, i32]
+        L.or_model_create.restype = C.c_void_p
+        L.or_model_destroy.argtypes = [C.c_void_p]
+        L.or_model_embed.argtypes = [C.c_void_p, u32, _f32p]
+        L.or_model_decode_hidden.argtypes = [C.c_void_p, sz, _f32p]
+        L.or_model_logits.argtypes = [C.c_void_p, _f32p, _f32p]
+        L.or_model_generate.argtypes = [C.c_void_p, C.c_void_p, sz, sz, C.c_void_p]
+        L.or_model_generate.restype = C.c_long
+        L.or_gdn_layer.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, _f32p, _f32p, _f32p,
+                                   C.c_void_p, _f32p, i32]
+        L.or_attention_layer.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, _f32p, sz,
+                                         C.c_void_p, C.c_void_p, C.POINTER(sz), _f32p, i32]
+        _lib = L
+    return _lib
+
+
+def _ptr(a):
+    return a.ctypes.data_as(C.c_void_p) if isinstance(a, np.ndarray) else a
+
+
+class OracleError(RuntimeError):
+    pass
+
+
+def _check(rc, what):
+    if rc != 0:
+        raise OracleError(f"{what} failed with status {rc}")
+
+
+def dequantize(ggml_type: int, data: np.ndarray, elements: int) -> np.ndarray:
+    data = np.ascontiguousarray(data, dtype=np.uint8)
+    out = np.empty(max(elements, 1), np.float32)
+    _check(lib().or_dequantize(ggml_type, _ptr(data), data.size, elements, out), "dequantize")
+    return out[:elements]
+
+
+def matvec(ggml_type: int, w, rows: int, cols: int, x: np.ndarray, threads: int = 0) -> np.ndarray:
+    y = np.empty(rows, np.float32)
+    _check(lib().or_matvec(ggml_type, _ptr(w), rows, cols, np.ascontiguousarray(x, np.float32), y, threads), "matvec")
+    return y
+
+
+def fused_gate_up(gate, up, rows, cols, x, threads=0):
+    out = np.empty(rows, np.float32)
+    _check(lib().or_fused_gate_up(_ptr(gate), _ptr(up), rows, cols, np.ascontiguousarray(x, np.float32), out, threads), "gate_up")
+    return out
+
+
+def fused_mlp(gate_type, gate, up, down_type, down, inter, hidden, x, threads=0):
+    y = np.empty(hidden, np.float32)
+    _check(lib().or_fused_mlp(gate_type, _ptr(gate), _ptr(up), down_type, _ptr(down), inter, hidden,
+                              np.ascontiguousarray(x, np.float32), y, threads), "mlp")
+    return y
+
+
+def rms_norm_heads(x, w, heads, hd, eps):
+    out = np.empty(heads * hd, np.float32)
+    _check(lib().or_rms_norm_heads(np.ascontiguousarray(x, np.float32), np.ascontiguousarray(w, np.float32), heads, hd, eps, out), "rms_norm_heads")
+    return out
+
+
+def gated_rms_norm(x, g, w, heads, hd, eps):
+    out = np.empty(heads * hd, np.float32)
+    _check(lib().or_gated_rms_norm(np.ascontiguousarray(x, np.float32), np.ascontiguousarray(g, np.float32),
+                                   np.ascontiguousarray(w, np.float32), heads, hd, eps, out), "gated_rms_norm")
+    return out
+
+
+def causal_conv1d_step(x, state, w, channels, kernel):
+    """Returns (out, new_state); `state` is not modified."""
+    st = np.array(state, np.float32, copy=True)
+    out = np.empty(channels, np.float32)
+    _check(lib().or_causal_conv1d_step(np.ascontiguousarray(x, np.float32), st, np.ascontiguousarray(w, np.float32),
+                                       channels, kernel, out), "conv")
+    return out, st
+
+
+def gdn_step(q, k, v, g, beta, state, heads, kd, vd):
+    """Returns (out, new_state); `state` is not modified."""
+    st = np.array(state, np.float32, copy=True)
+    out = np.empty(heads * vd, np.float32)
+    f = lambda a: np.ascontiguousarray(a, np.float32)
+    _check(lib().or_gdn_step(st, f(q), f(k), f(v), f(g), f(beta), heads, kd, vd, out), "gdn_step")
+    return out, st
+
+
+def rope(x, heads, hd, pos, theta):
+    out = np.empty(heads * hd, np.float32)
+    _check(lib().or_rope(np.ascontiguousarray(x, np.float32), heads, hd, pos, theta, out), "rope")
+    return out
+
+
+def attention_decode(q, kc, vc, nk, nv, qh, kvh, hd, cached, cap):
+    """kc/vc: float32 (reference layout) or uint16 (bf16 bits) arrays [kvh][cap][hd]."""
+    kc = np.ascontiguousarray(kc)
+    vc = np.ascontiguousarray(vc)
+    ct = 1 if kc.dtype == np.uint16 else 0
+    out = np.empty(qh * hd, np.float32)
+    f = lambda a: np.ascontiguousarray(a, np.float32)
+    _check(lib().or_attention_decode(f(q), _ptr(kc), _ptr(vc), ct, f(nk), f(nv), qh, kvh, hd, cached, cap, out), "attention")
+    return out
+
+
+def argmax(v) -> int:
+    return int(lib().or_argmax(np.ascontiguousarray(v, np.float32), len(v)))
+
+
+def f32_to_bf16(a: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even f32 -> bf16 bits (vectorised restatement)."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    return r
