@@ -1,0 +1,318 @@
+#!/usr/bin/env python
+"""Benchmark of the batch-1 K-quant decode hot path on B200.
+
+Headline (BASELINE.json metric, config 1): the Q4_K matvec 17408 x 5120
+(GGUF super-blocks, seeded as the config states) as achieved HBM GB/s.
+One step = one matvec over one weight matrix resident in HBM. Eight distinct
+weight copies (8 x 50.1 MB > 126 MB L2) are cycled so every step streams its
+weights from DRAM. Launches are back to back on the backend's stream, as in
+decode. `e2e` is the same metric through the public API with host buffers
+(gguf_quant_matvec_weight: H2D of x, kernel, D2H of y, synchronised each
+call). At N GPUs (torchrun) every rank runs the workload on its own
+matrices (independent matvecs, no collective on the data path): weak
+scaling, value = bytes of all ranks / max-over-ranks time.
+
+`--impl reference` times the reference's CPU path (the oracle's C++
+restatement of quant.rs + the matvec test reference, all host threads) on the
+same config and metric, on a bounded row sample per step.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "Q4_K matvec achieved HBM GB/s (% peak); 27B-shape batch-1 decode tokens/s"
+ROWS, COLS = 17408, 5120
+W_BYTES = ROWS * COLS // 256 * 144          # 50,135,040
+ALG_BYTES = W_BYTES + COLS * 4 + ROWS * 4   # 50,225,152 per call
+NCOPIES = 8
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_from_profile():
+    """DRAM bytes per launch from the committed ncu summary, if present."""
+    path = os.path.join(REPO, "profiles", "q4k_matvec_17408x5120.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1].strip().replace(",", ""))
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling while the GPU is under load."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.samples = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append((time.time(), parts))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0, t1):
+        win = [p for t, p in self.samples if t0 <= t <= t1] or [p for _, p in self.samples]
+        if not win:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(p[1]) for p in win if p[1].replace(".", "").isdigit()]
+        mx = [float(p[2]) for p in win if p[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for p in win for i in range(4) if p[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(win)}
+
+
+def make_weights(rng, mai):
+    import numpy as np
+    nb = ROWS * COLS // 256
+    b = rng.integers(0, 256, size=(nb, 144), dtype=np.uint8)
+    d = np.abs(rng.normal(0, 0.02, nb)).astype(np.float16).view(np.uint16)
+    dm = np.abs(rng.normal(0, 0.02, nb)).astype(np.float16).view(np.uint16)
+    b[:, 0], b[:, 1], b[:, 2], b[:, 3] = d & 0xFF, d >> 8, dm & 0xFF, dm >> 8
+    return b.reshape(-1)
+
+
+def dist_init(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        backend = "gloo" if args.impl == "reference" else "nccl"
+        dist.init_process_group(backend)
+    return world, rank, local
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda" if dist.get_backend() == "nccl" else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_matvec_sample(O, w, x, seconds, threads=0):
+    """Oracle matvec over row slices for about `seconds`; returns (GB/s, rows, seconds)."""
+    rows_per = 1088
+    rb = COLS // 256 * 144
+    done_rows, t0 = 0, time.perf_counter()
+    r0 = 0
+    while time.perf_counter() - t0 < seconds:
+        sl = w[r0 * rb:(r0 + rows_per) * rb]
+        O.matvec(12, sl, rows_per, COLS, x, threads)
+        done_rows += rows_per
+        r0 = (r0 + rows_per) % ROWS
+    dt = time.perf_counter() - t0
+    gbs = done_rows * (rb + 4) / dt / 1e9
+    return float(gbs), done_rows, dt
+
+
+def run_reference(args, world, rank):
+    import numpy as np
+    import oracle as O
+    if rank != 0:
+        return
+    O.build()
+    rng = np.random.default_rng(1)
+    w = make_weights(rng, None)
+    x = rng.normal(0, 1, COLS).astype(np.float32)
+    cores = os.cpu_count()
+    rb = COLS // 256 * 144
+    rows_per = 1088  # one step = a 1/16 row slice of the matrix (bounded sample)
+    for i in range(args.warmup):
+        O.matvec(12, w[:rows_per * rb], rows_per, COLS, x, 0)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        r0 = (i * rows_per) % ROWS
+        O.matvec(12, w[r0 * rb:(r0 + rows_per) * rb], rows_per, COLS, x, 0)
+    dt = time.perf_counter() - t0
+    bytes_per_step = rows_per * rb + COLS * 4 + rows_per * 4
+    gbs = args.steps * bytes_per_step / dt / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8->f32",
+            "data": "synthetic (seeded GGUF Q4_K super-blocks, x ~ N(0,1))",
+            "config": {"workload": "q4k_matvec_17408x5120 (BASELINE config 1)", "rows": ROWS, "cols": COLS,
+                       "sample": f"{rows_per} rows per step"},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": f"{rows_per}-row slices of the 17408x5120 matrix per step"},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    import numpy as np
+    import torch
+    from __graft_entry__ import _load_package
+    mai = _load_package()
+    torch.cuda.set_device(local)
+    ctx = mai.CudaContext(local)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
+    rng = np.random.default_rng(1 + rank)
+    host_w = make_weights(rng, mai)
+    x_host = rng.normal(0, 1, COLS).astype(np.float32)
+    weights = []
+    for i in range(NCOPIES):
+        t = torch.empty(W_BYTES + 64, dtype=torch.uint8, device="cuda")
+        t[:W_BYTES].copy_(torch.from_numpy(host_w))
+        weights.append(t)
+    x = torch.from_numpy(x_host).cuda()
+    y = torch.empty(ROWS, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+
+    def launch(i):
+        ctx.qmatvec_dev(mai.GGML_TYPE_Q4_K, weights[i % NCOPIES], ROWS, COLS, x, y, ctx.stream)
+
+    # correctness spot check against the oracle on rank 0 (a few rows)
+    launch(0)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    # warm-up, plus a short soak so the clock sampler sees the GPU under load
+    for i in range(args.warmup):
+        launch(i)
+    t_soak = time.time()
+    while time.time() - t_soak < 0.6:
+        for i in range(200):
+            launch(i)
+        torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(args.steps):
+            launch(i)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(ms, world)
+    sampler.stop()
+    clocks = sampler.summary(t_soak, t_wall1)
+
+    per_launch_s = ms / 1e3 / args.steps
+    value = world * args.steps * ALG_BYTES / (ms_max / 1e3) / 1e9
+    peak, peak_kind = load_peaks()
+    achieved = ALG_BYTES / per_launch_s / 1e9
+
+    # e2e through the public API with host (pinned) buffers, retained weight
+    wq = ctx.upload_quant_weight_private(host_w, mai.GGML_TYPE_Q4_K)
+    xp = torch.from_numpy(x_host).pin_memory()
+    e2e_steps = max(20, min(args.steps, 500))
+    for i in range(3):
+        ctx.gguf_quant_matvec_weight(wq, ROWS, COLS, xp.numpy())
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        yv = ctx.gguf_quant_matvec_weight(wq, ROWS, COLS, xp.numpy())
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    e2e_s = max_over_ranks(e2e_s, world)
+    e2e_val = world * ALG_BYTES / e2e_s / 1e9
+    ctx.free_weight(wq)
+
+    line = None
+    if rank == 0:
+        import oracle as O
+        ref_rows = O.matvec(12, host_w[:64 * 2880], 64, COLS, x_host)
+        rel = float(np.linalg.norm(yv[:64] - ref_rows) / np.linalg.norm(ref_rows))
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            gbs, nrows, dt = cpu_matvec_sample(O, host_w, x_host, args.cpu_seconds)
+            cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"{nrows} rows of the 17408x5120 Q4_K matvec in {dt:.1f} s (OpenMP, all host threads)"}
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 6), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8->f32",
+            "data": "synthetic (seeded GGUF Q4_K super-blocks: uniform bytes, |N(0,0.02)| fp16 d/dmin; x ~ N(0,1))",
+            "config": {"workload": "q4k_matvec_17408x5120 (BASELINE config 1)", "rows": ROWS, "cols": COLS,
+                       "l2": f"{NCOPIES} distinct weight copies ({NCOPIES * W_BYTES / 1e6:.0f} MB > 126 MB L2) cycled",
+                       "parallelism": f"independent matvec per GPU x{world}"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": traffic_from_profile(), "alg_bytes_per_launch": ALG_BYTES},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": COLS * 4,
+                    "d2h_bytes_per_step": ROWS * 4, "api": "gguf_quant_matvec_weight (host x, host y, retained weight)",
+                    "parity_rel_l2_first_rows": rel},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_init(args)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+    else:
+        run_ours(args, world, rank, local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

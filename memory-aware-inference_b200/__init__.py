@@ -1,0 +1,524 @@
+"""Host-side binding of the B200 decode backend (libsi_cuda.so, C ABI in
+include/si_cuda.h).
+
+`CudaContext` mirrors the reference's `MetalContext` surface for the batch-1
+K-quant decode path (src/metal.rs of vrlda/memory-aware-inference): the same
+method names, argument meaning and error behaviour (a failed call raises
+`SiError` carrying the backend's message, the Python face of Rust's
+`Err(String)`). `Model` mirrors `Qwen35Runtime` (src/qwen35_runtime.rs) for a
+seeded synthetic Qwen3.6-shaped model.
+
+There is no CPU fallback: importing this module loads the CUDA library, and a
+missing library is an error.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libsi_cuda.so")
+
+GGML_TYPE_F32, GGML_TYPE_Q4_K, GGML_TYPE_Q5_K, GGML_TYPE_Q6_K = 0, 12, 13, 14
+BLOCK_BYTES = {GGML_TYPE_Q4_K: 144, GGML_TYPE_Q5_K: 176, GGML_TYPE_Q6_K: 210}
+CACHE_F32, CACHE_BF16 = 0, 1
+TENSOR_IDS = ["ATTN_NORM", "POST_NORM", "FFN_GATE", "FFN_UP", "FFN_DOWN", "SSM_QKV", "SSM_Z", "SSM_ALPHA",
+              "SSM_BETA", "SSM_CONV", "SSM_A", "SSM_DT", "SSM_NORM", "SSM_OUT", "ATTN_Q", "ATTN_K", "ATTN_V",
+              "ATTN_O", "ATTN_QNORM", "ATTN_KNORM", "TOKEN_EMBD", "OUTPUT_NORM", "OUTPUT"]
+T = {name: i for i, name in enumerate(TENSOR_IDS)}
+T_COUNT = len(TENSOR_IDS)
+
+
+class SiError(RuntimeError):
+    """A backend call returned a non-zero status (reference: Err(String))."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+class SiCtxConfig(C.Structure):
+    _fields_ = [("hbm_budget_bytes", C.c_uint64), ("stage_depth", C.c_uint32), ("flags", C.c_uint32)]
+
+
+class SiStats(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("current_allocated_bytes", "peak_allocated_bytes",
+                                          "peak_active_weight_bytes", "peak_kv_bytes", "peak_scratch_bytes",
+                                          "submitted", "waited", "wait_nanos")]
+
+
+class SiAttentionDecodeInput(C.Structure):
+    _fields_ = [("query", C.c_void_p), ("key_cache", C.c_void_p), ("value_cache", C.c_void_p),
+                ("new_keys", C.c_void_p), ("new_values", C.c_void_p), ("query_heads", C.c_uint64),
+                ("key_value_heads", C.c_uint64), ("head_dim", C.c_uint64), ("cached_tokens", C.c_uint64),
+                ("cache_capacity_tokens", C.c_uint64), ("cache_type", C.c_int)]
+
+
+class SiModelConfig(C.Structure):
+    _fields_ = [("hidden", C.c_uint32), ("intermediate", C.c_uint32), ("layers", C.c_uint32),
+                ("vocab", C.c_uint32), ("attn_interval", C.c_uint32), ("attn_q_heads", C.c_uint32),
+                ("attn_kv_heads", C.c_uint32), ("attn_head_dim", C.c_uint32), ("rotary_dim", C.c_uint32),
+                ("rope_theta", C.c_float), ("gdn_key_heads", C.c_uint32), ("gdn_value_heads", C.c_uint32),
+                ("gdn_head_dim", C.c_uint32), ("conv_kernel", C.c_uint32), ("rms_eps", C.c_float),
+                ("kv_capacity", C.c_uint32), ("eos_token", C.c_uint32), ("mlp_type", C.c_uint32),
+                ("down_type", C.c_uint32), ("head_type", C.c_uint32)]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
+class SiPlanInfo(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("budget_bytes", "resident_weight_bytes", "ring_bytes", "state_bytes",
+                                          "scratch_bytes", "streamed_bytes_per_token")] + \
+               [(n, C.c_uint32) for n in ("resident_layers", "streamed_layers", "stage_depth", "head_resident")]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
+_lib = None
+
+
+def lib():
+    """Load libsi_cuda.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: run `python memory-aware-inference_b200/build.py` "
+                          "(or __graft_entry__.build()); there is no CPU fallback")
+    L = C.CDLL(LIB_PATH)
+    vp, u64, u32, i32, f32 = C.c_void_p, C.c_uint64, C.c_uint32, C.c_int, C.c_float
+    sig = {
+        "si_ctx_create": ([i32, vp, vp], i32),
+        "si_ctx_destroy": ([vp], None),
+        "si_last_error": ([vp], C.c_char_p),
+        "si_global_last_error": ([], C.c_char_p),
+        "si_ctx_info": ([vp, vp, vp], i32),
+        "si_ctx_stream": ([vp], vp),
+        "si_get_stats": ([vp, vp], i32),
+        "si_reset_peaks": ([vp], i32),
+        "si_weight_upload": ([vp, vp, u64, u32, vp], i32),
+        "si_weight_bind_host": ([vp, vp, u64, u32, vp], i32),
+        "si_weight_free": ([vp], None),
+        "si_weight_bytes": ([vp], u64),
+        "si_weight_type": ([vp], u32),
+        "si_weight_device_ptr": ([vp], vp),
+        "si_dequantize": ([vp, u32, vp, u64, u64, vp], i32),
+        "si_dequantize_dev": ([vp, u32, vp, u64, vp, vp], i32),
+        "si_q4_k_embedding_row": ([vp, vp, u64, u64, vp], i32),
+        "si_gguf_quant_matvec_bytes": ([vp, u32, vp, u64, u64, u64, vp, vp], i32),
+        "si_q4_k_matvec": ([vp, vp, u64, u64, u64, vp, vp], i32),
+        "si_q5_k_matvec": ([vp, vp, u64, u64, u64, vp, vp], i32),
+        "si_q6_k_matvec": ([vp, vp, u64, u64, u64, vp, vp], i32),
+        "si_gguf_quant_matvec_weight": ([vp, vp, u64, u64, vp, vp], i32),
+        "si_gguf_quant_matvec_many_weights": ([vp, u32, vp, vp, vp, vp, vp], i32),
+        "si_qmatvec_dev": ([vp, u32, vp, u64, u64, vp, vp, vp], i32),
+        "si_f32_matvec": ([vp, vp, u64, u64, vp, vp], i32),
+        "si_q4_k_fused_gate_up": ([vp, vp, vp, u64, u64, u64, vp, vp], i32),
+        "si_q4_k_fused_gate_up_weights": ([vp, vp, vp, u64, u64, vp, vp], i32),
+        "si_gguf_quant_fused_mlp_weights": ([vp, vp, vp, vp, u64, u64, u64, vp, vp], i32),
+        "si_fused_gate_up_dev": ([vp, u32, vp, vp, u64, u64, vp, vp, vp], i32),
+        "si_fused_mlp_dev": ([vp, u32, vp, vp, u32, vp, u64, u64, vp, vp, vp, vp], i32),
+        "si_gated_delta_step": ([vp, vp, vp, vp, vp, vp, vp, u64, u64, u64, vp, vp], i32),
+        "si_causal_conv1d_step": ([vp, vp, vp, vp, u64, u64, vp, vp], i32),
+        "si_rms_norm_gated": ([vp, vp, vp, vp, u64, u64, f32, vp], i32),
+        "si_rms_norm_heads": ([vp, vp, vp, u64, u64, f32, vp], i32),
+        "si_rope": ([vp, vp, u64, u64, u64, f32, vp], i32),
+        "si_attention_decode": ([vp, vp, vp], i32),
+        "si_argmax": ([vp, vp, u64, vp], i32),
+        "si_model_config_qwen36_27b": ([vp], None),
+        "si_model_create_synthetic": ([vp, vp, u64, vp], i32),
+        "si_model_destroy": ([vp], None),
+        "si_model_plan": ([vp, vp], i32),
+        "si_model_host_tensor": ([vp, u32, u32, vp, vp, vp], i32),
+        "si_model_reset": ([vp], i32),
+        "si_model_embed": ([vp, u32, vp], i32),
+        "si_model_decode_hidden": ([vp, u64, vp], i32),
+        "si_model_logits": ([vp, vp, vp], i32),
+        "si_model_decode_token": ([vp, u32, u64, vp, vp], i32),
+        "si_model_generate": ([vp, vp, u64, u64, vp, vp], i32),
+        "si_comm_unique_id": ([vp], i32),
+        "si_ctx_comm_init": ([vp, i32, i32, vp], i32),
+        "si_ctx_comm_info": ([vp, vp, vp], i32),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = L
+    return L
+
+
+def _p(a):
+    """Pointer of a numpy array / torch tensor / int address / None."""
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return a
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    if isinstance(a, (bytes, bytearray)):
+        return C.cast(C.c_char_p(bytes(a)), C.c_void_p).value
+    raise TypeError(f"cannot take a pointer of {type(a)}")
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _u8(a):
+    if isinstance(a, (bytes, bytearray)):
+        return np.frombuffer(bytes(a), dtype=np.uint8)
+    return np.ascontiguousarray(a, dtype=np.uint8)
+
+
+@dataclass
+class QuantWeight:
+    """Handle of a device-resident or host-bound quantized matrix (metal.rs:1840-1846)."""
+    handle: int
+    ggml_type: int
+    byte_len: int
+    _host_ref: object = None
+
+
+@dataclass
+class AttentionDecodeInput:
+    """metal.rs:27-38, plus the cache element type (f32 or bf16 bits as uint16)."""
+    query: np.ndarray
+    key_cache: np.ndarray
+    value_cache: np.ndarray
+    new_keys: np.ndarray
+    new_values: np.ndarray
+    query_heads: int
+    key_value_heads: int
+    head_dim: int
+    cached_tokens: int
+    cache_capacity_tokens: int
+
+
+class CudaContext:
+    """B200 replacement of MetalContext (src/metal.rs:1782-2445)."""
+
+    def __init__(self, device: int = 0, hbm_budget_bytes: int = 0, stage_depth: int = 3):
+        L = lib()
+        cfg = SiCtxConfig(hbm_budget_bytes, stage_depth, 0)
+        h = C.c_void_p()
+        rc = L.si_ctx_create(device, C.byref(cfg), C.byref(h))
+        if rc != 0:
+            raise SiError(rc, L.si_global_last_error().decode())
+        self.h = h.value
+        self.device = device
+
+    # -- plumbing -----------------------------------------------------------
+    def _ck(self, rc):
+        if rc != 0:
+            raise SiError(rc, lib().si_last_error(self.h).decode())
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().si_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def stream(self) -> int:
+        return lib().si_ctx_stream(self.h)
+
+    def sm_count(self) -> int:
+        d, s = C.c_int(), C.c_int()
+        self._ck(lib().si_ctx_info(self.h, C.byref(d), C.byref(s)))
+        return s.value
+
+    def stats(self) -> dict:
+        s = SiStats()
+        self._ck(lib().si_get_stats(self.h, C.byref(s)))
+        return {k: getattr(s, k) for k, _ in s._fields_}
+
+    def reset_peaks(self):
+        self._ck(lib().si_reset_peaks(self.h))
+
+    def comm_init(self, nranks: int, rank: int, uid: bytes):
+        buf = C.create_string_buffer(bytes(uid), 128)
+        self._ck(lib().si_ctx_comm_init(self.h, nranks, rank, buf))
+
+    @staticmethod
+    def comm_unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        rc = lib().si_comm_unique_id(buf)
+        if rc != 0:
+            raise SiError(rc, lib().si_global_last_error().decode())
+        return buf.raw
+
+    # -- weights (metal.rs:2502, 2549) --------------------------------------
+    def upload_quant_weight_private(self, weight_bytes, ggml_type: int) -> QuantWeight:
+        b = _u8(weight_bytes)
+        h = C.c_void_p()
+        self._ck(lib().si_weight_upload(self.h, _p(b), b.size, ggml_type, C.byref(h)))
+        return QuantWeight(h.value, ggml_type, b.size)
+
+    def bind_quant_weight_mapped(self, weight_bytes, ggml_type: int) -> QuantWeight:
+        b = _u8(weight_bytes)
+        h = C.c_void_p()
+        self._ck(lib().si_weight_bind_host(self.h, _p(b), b.size, ggml_type, C.byref(h)))
+        return QuantWeight(h.value, ggml_type, b.size, _host_ref=b)
+
+    def free_weight(self, w: QuantWeight):
+        if w.handle:
+            lib().si_weight_free(w.handle)
+            w.handle = 0
+
+    # -- dequant ---------------------------------------------------------------
+    def dequantize(self, ggml_type: int, data, elements: int) -> np.ndarray:
+        b = _u8(data)
+        out = np.empty(max(elements, 1), np.float32)
+        self._ck(lib().si_dequantize(self.h, ggml_type, _p(b), b.size, elements, _p(out)))
+        return out[:elements]
+
+    def q4_k_embedding_row(self, row_bytes, columns: int) -> np.ndarray:
+        b = _u8(row_bytes)
+        out = np.empty(max(columns, 1), np.float32)
+        self._ck(lib().si_q4_k_embedding_row(self.h, _p(b), b.size, columns, _p(out)))
+        return out[:columns]
+
+    # -- matvec (metal.rs:3357, 3923, 4000, 4307, 4325, 4652) ----------------
+    def gguf_quant_matvec_bytes(self, ggml_type, weight_bytes, rows, columns, x) -> np.ndarray:
+        b, xv = _u8(weight_bytes), _f32(x)
+        if xv.size != columns:
+            raise SiError(-1, f"{_label(ggml_type)} matvec dimensions are invalid")
+        y = np.empty(max(rows, 1), np.float32)
+        self._ck(lib().si_gguf_quant_matvec_bytes(self.h, ggml_type, _p(b), b.size, rows, columns, _p(xv), _p(y)))
+        return y[:rows]
+
+    def q4_k_matvec(self, weight_bytes, rows, columns, x):
+        return self.gguf_quant_matvec_bytes(GGML_TYPE_Q4_K, weight_bytes, rows, columns, x)
+
+    def q5_k_matvec(self, weight_bytes, rows, columns, x):
+        return self.gguf_quant_matvec_bytes(GGML_TYPE_Q5_K, weight_bytes, rows, columns, x)
+
+    def q6_k_matvec(self, weight_bytes, rows, columns, x):
+        return self.gguf_quant_matvec_bytes(GGML_TYPE_Q6_K, weight_bytes, rows, columns, x)
+
+    def gguf_quant_matvec_weight(self, weight: QuantWeight, rows, columns, x) -> np.ndarray:
+        return self.gguf_quant_matvec_many_weights([(weight, rows, columns)], x)[0]
+
+    def gguf_quant_matvec_many_weights(self, items, x):
+        xv = _f32(x)
+        n = len(items)
+        ws = (C.c_void_p * n)(*[w.handle for w, _, _ in items])
+        rows = (C.c_uint64 * n)(*[r for _, r, _ in items])
+        cols = (C.c_uint64 * n)(*[c for _, _, c in items])
+        if any(c != xv.size for _, _, c in items):
+            raise SiError(-1, "retained matvec dimensions are invalid")
+        outs = [np.empty(max(r, 1), np.float32) for _, r, _ in items]
+        ys = (C.c_void_p * n)(*[o.ctypes.data for o in outs])
+        self._ck(lib().si_gguf_quant_matvec_many_weights(self.h, n, ws, rows, cols, _p(xv), ys))
+        return [o[:r] for o, (_, r, _) in zip(outs, items)]
+
+    def f32_matvec(self, weights, rows, columns, x):
+        w, xv = _f32(weights), _f32(x)
+        if w.size != rows * columns or xv.size != columns:
+            raise SiError(-1, "F32 matvec dimensions are invalid")
+        y = np.empty(rows, np.float32)
+        self._ck(lib().si_f32_matvec(self.h, _p(w), rows, columns, _p(xv), _p(y)))
+        return y
+
+    # -- fused SwiGLU (metal.rs:3402, 3489, 3569) -----------------------------
+    def q4_k_fused_gate_up(self, gate_weights, up_weights, rows, columns, x):
+        g, u, xv = _u8(gate_weights), _u8(up_weights), _f32(x)
+        if xv.size != columns or g.size != u.size:
+            raise SiError(-1, "Q4_K fused gate/up dimensions are invalid")
+        out = np.empty(max(rows, 1), np.float32)
+        self._ck(lib().si_q4_k_fused_gate_up(self.h, _p(g), _p(u), g.size, rows, columns, _p(xv), _p(out)))
+        return out[:rows]
+
+    def q4_k_fused_gate_up_weights(self, gate: QuantWeight, up: QuantWeight, rows, columns, x):
+        xv = _f32(x)
+        out = np.empty(max(rows, 1), np.float32)
+        self._ck(lib().si_q4_k_fused_gate_up_weights(self.h, gate.handle, up.handle, rows, columns, _p(xv), _p(out)))
+        return out[:rows]
+
+    def gguf_quant_fused_mlp_weights(self, gate, up, down, gate_rows, columns, down_rows, x):
+        xv = _f32(x)
+        y = np.empty(max(down_rows, 1), np.float32)
+        self._ck(lib().si_gguf_quant_fused_mlp_weights(self.h, gate.handle, up.handle, down.handle, gate_rows,
+                                                      columns, down_rows, _p(xv), _p(y)))
+        return y[:down_rows]
+
+    # -- Gated DeltaNet (metal.rs:2773, 2856, 3122, 3263) ---------------------
+    def gated_delta_step(self, query, key, value, gate, beta, state, heads, key_dim, value_dim):
+        q, k, v, g, b, s = map(_f32, (query, key, value, gate, beta, state))
+        if (q.size != heads * key_dim or k.size != q.size or v.size != heads * value_dim or g.size != heads
+                or b.size != heads or s.size != heads * key_dim * value_dim):
+            raise SiError(-1, "Gated DeltaNet input or state dimensions are invalid")
+        out = np.empty(heads * value_dim, np.float32)
+        new_state = np.empty_like(s)
+        self._ck(lib().si_gated_delta_step(self.h, _p(q), _p(k), _p(v), _p(g), _p(b), _p(s), heads, key_dim,
+                                           value_dim, _p(out), _p(new_state)))
+        return out, new_state
+
+    def causal_conv1d_step(self, x, state, weights, channels, kernel_size):
+        xv, s, w = _f32(x), _f32(state), _f32(weights)
+        if xv.size != channels or kernel_size < 2 or s.size != channels * (kernel_size - 1) or \
+                w.size != channels * kernel_size:
+            raise SiError(-1, "causal convolution input, state, or weight lengths are invalid")
+        out = np.empty(channels, np.float32)
+        ns = np.empty_like(s)
+        self._ck(lib().si_causal_conv1d_step(self.h, _p(xv), _p(s), _p(w), channels, kernel_size, _p(out), _p(ns)))
+        return out, ns
+
+    def rms_norm_gated(self, x, gate, weight, heads, head_dim, epsilon):
+        xv, g, w = _f32(x), _f32(gate), _f32(weight)
+        if xv.size != heads * head_dim or g.size != xv.size or w.size != head_dim:
+            raise SiError(-1, "Gated RMSNorm dimensions are invalid")
+        out = np.empty(heads * head_dim, np.float32)
+        self._ck(lib().si_rms_norm_gated(self.h, _p(xv), _p(g), _p(w), heads, head_dim, epsilon, _p(out)))
+        return out
+
+    def rms_norm_heads(self, x, weight, heads, head_dim, epsilon):
+        xv, w = _f32(x), _f32(weight)
+        if xv.size != heads * head_dim or w.size != head_dim:
+            raise SiError(-1, "head RMSNorm dimensions are invalid")
+        out = np.empty(heads * head_dim, np.float32)
+        self._ck(lib().si_rms_norm_heads(self.h, _p(xv), _p(w), heads, head_dim, epsilon, _p(out)))
+        return out
+
+    # -- attention (metal.rs:6860, 6915) ----------------------------------------
+    def rope(self, x, heads, head_dim, position, theta):
+        xv = _f32(x)
+        if xv.size != heads * head_dim:
+            raise SiError(-1, "RoPE dimensions are invalid")
+        out = np.empty(max(xv.size, 1), np.float32)
+        self._ck(lib().si_rope(self.h, _p(xv), heads, head_dim, position, theta, _p(out)))
+        return out[:xv.size]
+
+    def attention_decode(self, inp: AttentionDecodeInput) -> np.ndarray:
+        q, nk, nv = _f32(inp.query), _f32(inp.new_keys), _f32(inp.new_values)
+        kc, vc = np.ascontiguousarray(inp.key_cache), np.ascontiguousarray(inp.value_cache)
+        ct = CACHE_BF16 if kc.dtype == np.uint16 else CACHE_F32
+        if ct == CACHE_F32:
+            kc, vc = _f32(kc), _f32(vc)
+        qh, kvh, hd = inp.query_heads, inp.key_value_heads, inp.head_dim
+        if q.size != qh * hd or nk.size != kvh * hd or nv.size != kvh * hd:
+            raise SiError(-1, "attention query or new key/value lengths are invalid")
+        if kc.size != kvh * inp.cache_capacity_tokens * hd or vc.size != kc.size:
+            raise SiError(-1, "attention cache dimensions are invalid")
+        s = SiAttentionDecodeInput(_p(q), _p(kc), _p(vc), _p(nk), _p(nv), qh, kvh, hd, inp.cached_tokens,
+                                   inp.cache_capacity_tokens, ct)
+        out = np.empty(qh * hd, np.float32)
+        self._ck(lib().si_attention_decode(self.h, C.byref(s), _p(out)))
+        return out
+
+    def argmax(self, logits) -> int:
+        v = _f32(logits)
+        idx = C.c_uint32()
+        self._ck(lib().si_argmax(self.h, _p(v), v.size, C.byref(idx)))
+        return idx.value
+
+    # -- device-pointer forms (torch tensors or raw addresses) ---------------
+    def qmatvec_dev(self, ggml_type, w, rows, cols, x, y, stream=None):
+        self._ck(lib().si_qmatvec_dev(self.h, ggml_type, _p(w), rows, cols, _p(x), _p(y), stream))
+
+    def fused_gate_up_dev(self, ggml_type, gate, up, rows, cols, x, out, stream=None):
+        self._ck(lib().si_fused_gate_up_dev(self.h, ggml_type, _p(gate), _p(up), rows, cols, _p(x), _p(out), stream))
+
+    def fused_mlp_dev(self, gate_type, gate, up, down_type, down, inter, hidden, x, act, y, stream=None):
+        self._ck(lib().si_fused_mlp_dev(self.h, gate_type, _p(gate), _p(up), down_type, _p(down), inter, hidden,
+                                        _p(x), _p(act), _p(y), stream))
+
+    def dequantize_dev(self, ggml_type, w, elements, out, stream=None):
+        self._ck(lib().si_dequantize_dev(self.h, ggml_type, _p(w), elements, _p(out), stream))
+
+
+def _label(t):
+    return {GGML_TYPE_Q4_K: "Q4_K", GGML_TYPE_Q5_K: "Q5_K", GGML_TYPE_Q6_K: "Q6_K"}.get(t, "?")
+
+
+def qwen36_27b_config(**overrides) -> SiModelConfig:
+    """BASELINE config 5 shape (GgufQwen35Config of the 27B model, model.rs:1929-1971)."""
+    c = SiModelConfig()
+    lib().si_model_config_qwen36_27b(C.byref(c))
+    for k, v in overrides.items():
+        setattr(c, k, v)
+    return c
+
+
+class Model:
+    """Synthetic Qwen3.6-shaped decoder (Qwen35Runtime, qwen35_runtime.rs:1519-2267)."""
+
+    def __init__(self, ctx: CudaContext, config: SiModelConfig, seed: int):
+        self.ctx = ctx
+        self.config = config
+        h = C.c_void_p()
+        ctx._ck(lib().si_model_create_synthetic(ctx.h, C.byref(config), seed, C.byref(h)))
+        self.h = h.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().si_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def plan(self) -> dict:
+        p = SiPlanInfo()
+        self.ctx._ck(lib().si_model_plan(self.h, C.byref(p)))
+        return p.as_dict()
+
+    def host_tensor(self, layer: int, tensor: int):
+        """(address, bytes, ggml_type) of this rank's pinned host copy of a tensor."""
+        ptr, nb, ty = C.c_void_p(), C.c_uint64(), C.c_uint32()
+        self.ctx._ck(lib().si_model_host_tensor(self.h, layer, tensor, C.byref(ptr), C.byref(nb), C.byref(ty)))
+        return ptr.value, nb.value, ty.value
+
+    def host_tensor_array(self, layer: int, tensor: int) -> np.ndarray:
+        ptr, nb, ty = self.host_tensor(layer, tensor)
+        if not ptr:
+            return np.empty(0, np.uint8)
+        return np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_uint8)), shape=(nb,))
+
+    def reset(self):
+        self.ctx._ck(lib().si_model_reset(self.h))
+
+    def embed_token(self, token_id: int) -> np.ndarray:
+        out = np.empty(self.config.hidden, np.float32)
+        self.ctx._ck(lib().si_model_embed(self.h, token_id, _p(out)))
+        return out
+
+    def decode_hidden(self, position: int, hidden) -> np.ndarray:
+        h = np.array(hidden, np.float32, copy=True)
+        self.ctx._ck(lib().si_model_decode_hidden(self.h, position, _p(h)))
+        return h
+
+    def logits(self, hidden) -> np.ndarray:
+        h = _f32(hidden)
+        out = np.empty(self.config.vocab, np.float32)
+        self.ctx._ck(lib().si_model_logits(self.h, _p(h), _p(out)))
+        return out
+
+    def decode_token(self, token_id: int, position: int, want_logits: bool = True):
+        nxt = C.c_uint32()
+        logits = np.empty(self.config.vocab, np.float32) if want_logits else None
+        self.ctx._ck(lib().si_model_decode_token(self.h, token_id, position, C.byref(nxt), _p(logits)))
+        return nxt.value, logits
+
+    def generate(self, prompt, max_new_tokens: int):
+        p = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.zeros(max(max_new_tokens, 1), np.uint32)
+        n = C.c_uint64()
+        self.ctx._ck(lib().si_model_generate(self.h, _p(p), p.size, max_new_tokens, _p(out), C.byref(n)))
+        return out[:n.value].tolist()

@@ -1,0 +1,741 @@
+// C ABI: context, weights and the host-memory operator entry points that
+// mirror MetalContext (src/metal.rs) of the reference. Validation order and
+// messages follow the reference methods so Rust callers see the same errors.
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "ctx.h"
+#include "kernels.cuh"
+#include "qmatvec.cuh"
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+struct si_weight {
+  si_ctx* ctx = nullptr;
+  void* dev = nullptr;         // device copy (upload) or nullptr (host-bound)
+  const void* host = nullptr;  // host-bound bytes
+  uint64_t bytes = 0;
+  uint32_t type = 0;
+  bool registered = false;
+};
+
+namespace si {
+
+int fail(si_ctx* ctx, int code, const std::string& msg) {
+  if (ctx) ctx->err = msg;
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(si_ctx* ctx, cudaError_t e, const char* what) {
+  return fail(ctx, e == cudaErrorMemoryAllocation ? SI_E_NOMEM : SI_E_CUDA,
+              std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+void note_alloc(si_ctx* ctx, int64_t delta) {
+  uint64_t now = ctx->allocated.fetch_add(uint64_t(delta)) + uint64_t(delta);
+  uint64_t peak = ctx->peak_allocated.load();
+  while (now > peak && !ctx->peak_allocated.compare_exchange_weak(peak, now)) {
+  }
+}
+
+void note_weights(si_ctx* ctx, int64_t delta) {
+  uint64_t now = ctx->weights.fetch_add(uint64_t(delta)) + uint64_t(delta);
+  uint64_t peak = ctx->peak_weights.load();
+  while (now > peak && !ctx->peak_weights.compare_exchange_weak(peak, now)) {
+  }
+}
+
+int sync_and_check(si_ctx* ctx, const char* what) {
+  auto t0 = std::chrono::steady_clock::now();
+  ctx->submitted++;
+  cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  ctx->waited++;
+  ctx->wait_nanos += uint64_t(std::chrono::duration_cast<std::chrono::nanoseconds>(
+                                  std::chrono::steady_clock::now() - t0)
+                                  .count());
+  if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+  int bits = 0;
+  e = cudaMemcpy(&bits, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+  if (bits) {
+    cudaMemset(ctx->d_err, 0, sizeof(int));
+    return fail(ctx, bits & (KERR_TIMEOUT_FULL | KERR_TIMEOUT_EMPTY | KERR_TIMEOUT_DRAIN)
+                         ? SI_E_TIMEOUT
+                         : SI_E_CUDA,
+                std::string(what) + ": device error bits " + std::to_string(bits));
+  }
+  return SI_OK;
+}
+
+// Copy host bytes into a staging buffer on the compute stream.
+static int h2d(si_ctx* ctx, DevBuf& b, const void* src, size_t bytes, const char* what) {
+  if (!b.ensure(bytes)) return fail(ctx, SI_E_NOMEM, std::string(what) + ": device allocation failed");
+  if (bytes) {
+    cudaError_t e = cudaMemcpyAsync(b.p, src, bytes, cudaMemcpyHostToDevice, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+  }
+  return SI_OK;
+}
+
+static int d2h(si_ctx* ctx, void* dst, const void* src, size_t bytes, const char* what) {
+  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+  return SI_OK;
+}
+
+static const char* type_label(uint32_t t) {
+  return t == SI_GGML_TYPE_Q4_K ? "Q4_K" : t == SI_GGML_TYPE_Q5_K ? "Q5_K" : t == SI_GGML_TYPE_Q6_K ? "Q6_K" : "?";
+}
+
+// Shared validation of quant_k_matvec_dispatch (metal.rs:3847-3858).
+static int check_qmv(si_ctx* ctx, uint32_t type, uint64_t nbytes, uint64_t rows, uint64_t cols,
+                     const char* extra = "") {
+  const uint32_t bb = block_bytes_of(type);
+  if (bb == 0) return fail(ctx, SI_E_UNSUPPORTED, "unsupported quantized weight type");
+  const std::string label = type_label(type);
+  if (rows == 0 || cols == 0 || cols % 256)
+    return fail(ctx, SI_E_INVALID, label + extra + " matvec dimensions are invalid");
+  if (rows > 0xffffffffull || cols > kQmvMaxCols)
+    return fail(ctx, SI_E_UNSUPPORTED, label + " matvec dimensions exceed backend limits");
+  if (nbytes != rows * (cols / 256) * bb)
+    return fail(ctx, SI_E_INVALID, label + extra + " matvec byte length is invalid");
+  return SI_OK;
+}
+
+}  // namespace si
+
+using namespace si;
+
+extern "C" {
+
+const char* si_global_last_error(void) { return g_last_error.c_str(); }
+
+const char* si_last_error(const si_ctx* ctx) { return ctx ? ctx->err.c_str() : g_last_error.c_str(); }
+
+int si_ctx_create(int device, const si_ctx_config* cfg, si_ctx** out) {
+  if (!out) return fail(nullptr, SI_E_INVALID, "null output handle");
+  *out = nullptr;
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaSetDevice");
+  int major = 0, minor = 0, sms = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (major != 10)
+    return fail(nullptr, SI_E_UNSUPPORTED,
+                "this backend is built for sm_100a (B200); device has compute capability " +
+                    std::to_string(major) + "." + std::to_string(minor));
+  auto* c = new si_ctx();
+  c->device = device;
+  c->sm_count = sms;
+  if (cfg) c->cfg = *cfg;
+  if (c->cfg.stage_depth == 0) c->cfg.stage_depth = 3;
+  if (c->cfg.stage_depth > 4) c->cfg.stage_depth = 4;
+  if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess ||
+      (e = cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking)) != cudaSuccess ||
+      (e = cudaMalloc(&c->d_err, 64)) != cudaSuccess ||
+      (e = cudaMalloc(&c->d_argmax, 64)) != cudaSuccess ||
+      (e = cudaMalloc(&c->d_index, 64)) != cudaSuccess) {
+    int rc = cuda_fail(nullptr, e, "context creation");
+    si_ctx_destroy(c);
+    return rc;
+  }
+  cudaMemset(c->d_err, 0, 64);
+  cudaMemset(c->d_argmax, 0, 64);
+  cudaDeviceSynchronize();
+  *out = c;
+  return SI_OK;
+}
+
+int si_comm_destroy_internal(si_ctx* ctx);
+
+void si_ctx_destroy(si_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  si_comm_destroy_internal(ctx);
+  for (auto& b : ctx->in) b.release();
+  for (auto& b : ctx->out) b.release();
+  for (auto& b : ctx->wbuf) b.release();
+  ctx->scratch.release();
+  if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->d_argmax) cudaFree(ctx->d_argmax);
+  if (ctx->d_index) cudaFree(ctx->d_index);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
+  delete ctx;
+}
+
+int si_ctx_info(const si_ctx* ctx, int* device, int* sm_count) {
+  if (!ctx) return SI_E_INVALID;
+  if (device) *device = ctx->device;
+  if (sm_count) *sm_count = ctx->sm_count;
+  return SI_OK;
+}
+
+void* si_ctx_stream(si_ctx* ctx) { return ctx ? ctx->stream : nullptr; }
+
+int si_get_stats(const si_ctx* ctx, si_stats* o) {
+  if (!ctx || !o) return SI_E_INVALID;
+  o->current_allocated_bytes = ctx->allocated.load();
+  o->peak_allocated_bytes = ctx->peak_allocated.load();
+  o->peak_active_weight_bytes = ctx->peak_weights.load();
+  o->peak_kv_bytes = ctx->peak_kv.load();
+  o->peak_scratch_bytes = ctx->peak_scratch.load();
+  o->submitted = ctx->submitted.load();
+  o->waited = ctx->waited.load();
+  o->wait_nanos = ctx->wait_nanos.load();
+  return SI_OK;
+}
+
+int si_reset_peaks(si_ctx* ctx) {
+  if (!ctx) return SI_E_INVALID;
+  ctx->peak_allocated = ctx->allocated.load();
+  ctx->peak_weights = ctx->weights.load();
+  ctx->peak_kv = 0;
+  ctx->peak_scratch = 0;
+  return SI_OK;
+}
+
+// ---- weights ----------------------------------------------------------------
+int si_weight_upload(si_ctx* ctx, const void* host, uint64_t bytes, uint32_t type,
+                     si_weight** out) {
+  if (!ctx || !out || (!host && bytes)) return fail(ctx, SI_E_INVALID, "invalid weight upload arguments");
+  std::lock_guard<std::mutex> lk(ctx->upload_mu);
+  cudaSetDevice(ctx->device);
+  auto* w = new si_weight();
+  w->ctx = ctx;
+  w->bytes = bytes;
+  w->type = type;
+  cudaError_t e = cudaMalloc(&w->dev, bytes + 64);
+  if (e != cudaSuccess) {
+    delete w;
+    return cuda_fail(ctx, e, "quantized weight upload");
+  }
+  cudaMemset(static_cast<uint8_t*>(w->dev) + bytes, 0, 64);
+  e = cudaMemcpyAsync(w->dev, host, bytes, cudaMemcpyHostToDevice, ctx->copy_stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->copy_stream);
+  if (e != cudaSuccess) {
+    cudaFree(w->dev);
+    delete w;
+    return cuda_fail(ctx, e, "quantized weight upload");
+  }
+  note_alloc(ctx, int64_t(bytes + 64));
+  note_weights(ctx, int64_t(bytes));
+  *out = w;
+  return SI_OK;
+}
+
+int si_weight_bind_host(si_ctx* ctx, const void* host, uint64_t bytes, uint32_t type,
+                        si_weight** out) {
+  if (!ctx || !out || !host) return fail(ctx, SI_E_INVALID, "invalid weight binding arguments");
+  auto* w = new si_weight();
+  w->ctx = ctx;
+  w->host = host;
+  w->bytes = bytes;
+  w->type = type;
+  // Page-lock so the per-use copy runs at full PCIe/C2C speed; memory that is
+  // already pinned (or cannot be registered) is used as is.
+  cudaError_t e = cudaHostRegister(const_cast<void*>(host), bytes, cudaHostRegisterReadOnly);
+  if (e == cudaSuccess) w->registered = true;
+  else cudaGetLastError();
+  *out = w;
+  return SI_OK;
+}
+
+void si_weight_free(si_weight* w) {
+  if (!w) return;
+  if (w->dev) {
+    cudaSetDevice(w->ctx->device);
+    cudaFree(w->dev);
+    note_alloc(w->ctx, -int64_t(w->bytes + 64));
+    note_weights(w->ctx, -int64_t(w->bytes));
+  }
+  if (w->registered) cudaHostUnregister(const_cast<void*>(w->host));
+  delete w;
+}
+
+uint64_t si_weight_bytes(const si_weight* w) { return w ? w->bytes : 0; }
+uint32_t si_weight_type(const si_weight* w) { return w ? w->type : 0; }
+const void* si_weight_device_ptr(const si_weight* w) { return w ? w->dev : nullptr; }
+
+}  // extern "C"
+
+namespace si {
+// Device pointer of a weight for this call (host-bound weights are copied
+// into staging buffer `slot`).
+static int weight_dev(si_ctx* ctx, const si_weight* w, int slot, const uint8_t** out) {
+  if (w->dev) {
+    *out = static_cast<const uint8_t*>(w->dev);
+    return SI_OK;
+  }
+  int rc = h2d(ctx, ctx->wbuf[slot], w->host, w->bytes, "mapped weight staging");
+  if (rc) return rc;
+  *out = ctx->wbuf[slot].as<uint8_t>();
+  return SI_OK;
+}
+}  // namespace si
+
+extern "C" {
+
+// ---- dequant -----------------------------------------------------------------
+int si_dequantize_dev(si_ctx* ctx, uint32_t type, const void* bytes_dev, uint64_t elements,
+                      float* out_dev, void* stream) {
+  if (!ctx || block_bytes_of(type) == 0) return fail(ctx, SI_E_UNSUPPORTED, "unsupported quantized type");
+  if (elements == 0 || elements % 256) return fail(ctx, SI_E_INVALID, "element count must be a non-zero multiple of 256");
+  launch_dequant(type, static_cast<const uint8_t*>(bytes_dev), elements, out_dev,
+                 stream ? static_cast<cudaStream_t>(stream) : ctx->stream);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SI_OK : cuda_fail(ctx, e, "dequant launch");
+}
+
+int si_dequantize(si_ctx* ctx, uint32_t type, const void* bytes, uint64_t nbytes,
+                  uint64_t elements, float* out) {
+  if (!ctx) return SI_E_INVALID;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  const uint32_t bb = block_bytes_of(type);
+  const char* label = type_label(type);
+  if (bb == 0) return fail(ctx, SI_E_UNSUPPORTED, "unsupported quantized type");
+  if (elements == 0 || elements % 256)
+    return fail(ctx, SI_E_INVALID, std::string(label) + " element count must be a non-zero multiple of 256");
+  if (nbytes != elements / 256 * bb)
+    return fail(ctx, SI_E_INVALID, std::string(label) + " data has " + std::to_string(nbytes) +
+                                       " bytes; expected " + std::to_string(elements / 256 * bb));
+  int rc = h2d(ctx, ctx->in[0], bytes, nbytes, "dequant input");
+  if (rc) return rc;
+  if (!ctx->out[0].ensure(elements * 4)) return fail(ctx, SI_E_NOMEM, "dequant output allocation failed");
+  launch_dequant(type, ctx->in[0].as<uint8_t>(), elements, ctx->out[0].as<float>(), ctx->stream);
+  if ((rc = d2h(ctx, out, ctx->out[0].p, elements * 4, "dequant readback"))) return rc;
+  return sync_and_check(ctx, "dequant command");
+}
+
+int si_q4_k_embedding_row(si_ctx* ctx, const void* row, uint64_t nbytes, uint64_t columns,
+                          float* out) {
+  if (!ctx) return SI_E_INVALID;
+  if (columns == 0 || columns % 256) return fail(ctx, SI_E_INVALID, "Q4_K embedding dimension is invalid");
+  if (nbytes != columns / 256 * 144) return fail(ctx, SI_E_INVALID, "Q4_K embedding row byte length is invalid");
+  return si_dequantize(ctx, SI_GGML_TYPE_Q4_K, row, nbytes, columns, out);
+}
+
+// ---- matvec --------------------------------------------------------------------
+int si_qmatvec_dev(si_ctx* ctx, uint32_t type, const void* w_dev, uint64_t rows, uint64_t cols,
+                   const float* x_dev, float* y_dev, void* stream) {
+  if (!ctx) return SI_E_INVALID;
+  int rc = check_qmv(ctx, type, rows * (cols / 256) * block_bytes_of(type), rows, cols);
+  if (rc) return rc;
+  QmvParams p = {};
+  p.type = type;
+  p.cols = uint32_t(cols);
+  p.nseg = 1;
+  p.seg[0] = {static_cast<const uint8_t*>(w_dev), y_dev, nullptr, uint32_t(rows), 0};
+  p.items = uint32_t(rows);
+  p.xmode = XM_RAW;
+  p.x = x_dev;
+  p.err = ctx->d_err;
+  std::string msg;
+  // Programmatic dependent launch: back-to-back matvecs overlap the next
+  // kernel's weight prefetch with this one's tail (x/y are read/written only
+  // after griddepcontrol.wait).
+  rc = launch_qmv(p, stream ? static_cast<cudaStream_t>(stream) : ctx->stream, ctx->sm_count,
+                  true, &msg);
+  return rc ? fail(ctx, rc, msg) : SI_OK;
+}
+
+int si_gguf_quant_matvec_bytes(si_ctx* ctx, uint32_t type, const void* w, uint64_t nbytes,
+                               uint64_t rows, uint64_t cols, const float* x, float* y) {
+  if (!ctx) return SI_E_INVALID;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  int rc = check_qmv(ctx, type, nbytes, rows, cols);
+  if (rc) return rc;
+  if ((rc = h2d(ctx, ctx->wbuf[0], w, nbytes, "matvec weight staging"))) return rc;
+  if ((rc = h2d(ctx, ctx->in[0], x, cols * 4, "matvec input"))) return rc;
+  if (!ctx->out[0].ensure(rows * 4)) return fail(ctx, SI_E_NOMEM, "matvec output allocation failed");
+  QmvParams p = {};
+  p.type = type;
+  p.cols = uint32_t(cols);
+  p.nseg = 1;
+  p.seg[0] = {ctx->wbuf[0].as<uint8_t>(), ctx->out[0].as<float>(), nullptr, uint32_t(rows), 0};
+  p.items = uint32_t(rows);
+  p.x = ctx->in[0].as<float>();
+  p.err = ctx->d_err;
+  std::string msg;
+  if ((rc = launch_qmv(p, ctx->stream, ctx->sm_count, false, &msg))) return fail(ctx, rc, msg);
+  if ((rc = d2h(ctx, y, ctx->out[0].p, rows * 4, "matvec readback"))) return rc;
+  return sync_and_check(ctx, (std::string(type_label(type)) + " matvec command").c_str());
+}
+
+int si_q4_k_matvec(si_ctx* ctx, const void* w, uint64_t nbytes, uint64_t rows, uint64_t cols,
+                   const float* x, float* y) {
+  return si_gguf_quant_matvec_bytes(ctx, SI_GGML_TYPE_Q4_K, w, nbytes, rows, cols, x, y);
+}
+int si_q5_k_matvec(si_ctx* ctx, const void* w, uint64_t nbytes, uint64_t rows, uint64_t cols,
+                   const float* x, float* y) {
+  return si_gguf_quant_matvec_bytes(ctx, SI_GGML_TYPE_Q5_K, w, nbytes, rows, cols, x, y);
+}
+int si_q6_k_matvec(si_ctx* ctx, const void* w, uint64_t nbytes, uint64_t rows, uint64_t cols,
+                   const float* x, float* y) {
+  return si_gguf_quant_matvec_bytes(ctx, SI_GGML_TYPE_Q6_K, w, nbytes, rows, cols, x, y);
+}
+
+int si_gguf_quant_matvec_many_weights(si_ctx* ctx, uint32_t n, const si_weight* const* ws,
+                                      const uint64_t* rows, const uint64_t* cols, const float* x,
+                                      float* const* ys) {
+  if (!ctx) return SI_E_INVALID;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (n == 0 || n > 3) return fail(ctx, SI_E_INVALID, "grouped quantized matvec needs 1..3 weights");
+  const uint32_t type = ws[0]->type;
+  uint64_t total = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    if (ws[i]->type != type || cols[i] != cols[0])
+      return fail(ctx, SI_E_INVALID, "grouped quantized matvec weights must share type and columns");
+    int rc = check_qmv(ctx, type, ws[i]->bytes, rows[i], cols[i], " retained");
+    if (rc) return rc;
+    total += rows[i];
+  }
+  int rc = h2d(ctx, ctx->in[0], x, cols[0] * 4, "grouped matvec input");
+  if (rc) return rc;
+  if (!ctx->out[0].ensure(total * 4)) return fail(ctx, SI_E_NOMEM, "grouped matvec output allocation failed");
+  QmvParams p = {};
+  p.type = type;
+  p.cols = uint32_t(cols[0]);
+  p.nseg = n;
+  uint64_t off = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    const uint8_t* wd;
+    if ((rc = weight_dev(ctx, ws[i], int(i), &wd))) return rc;
+    p.seg[i] = {wd, ctx->out[0].as<float>() + off, nullptr, uint32_t(rows[i]), 0};
+    off += rows[i];
+  }
+  p.items = uint32_t(total);
+  p.x = ctx->in[0].as<float>();
+  p.err = ctx->d_err;
+  std::string msg;
+  if ((rc = launch_qmv(p, ctx->stream, ctx->sm_count, false, &msg))) return fail(ctx, rc, msg);
+  off = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    if ((rc = d2h(ctx, ys[i], ctx->out[0].as<float>() + off, rows[i] * 4, "grouped readback"))) return rc;
+    off += rows[i];
+  }
+  return sync_and_check(ctx, "grouped matvec command");
+}
+
+int si_gguf_quant_matvec_weight(si_ctx* ctx, const si_weight* w, uint64_t rows, uint64_t cols,
+                                const float* x, float* y) {
+  if (!ctx || !w) return fail(ctx, SI_E_INVALID, "null weight");
+  if (block_bytes_of(w->type) == 0) return fail(ctx, SI_E_UNSUPPORTED, "unsupported retained quantized weight type");
+  uint64_t r = rows, c = cols;
+  float* yy = y;
+  return si_gguf_quant_matvec_many_weights(ctx, 1, &w, &r, &c, x, &yy);
+}
+
+int si_f32_matvec(si_ctx* ctx, const float* w, uint64_t rows, uint64_t cols, const float* x,
+                  float* y) {
+  if (!ctx) return SI_E_INVALID;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (rows == 0 || cols == 0) return fail(ctx, SI_E_INVALID, "F32 matvec dimensions are invalid");
+  // column counts that are not a multiple of 4 are padded on upload
+  const uint64_t cp = (cols + 3) / 4 * 4;
+  std::vector<float> padded;
+  const float* src = w;
+  std::vector<float> xp;
+  const float* xs = x;
+  if (cp != cols) {
+    padded.assign(rows * cp, 0.f);
+    for (uint64_t r = 0; r < rows; ++r) std::memcpy(&padded[r * cp], w + r * cols, cols * 4);
+    src = padded.data();
+    xp.assign(cp, 0.f);
+    std::memcpy(xp.data(), x, cols * 4);
+    xs = xp.data();
+  }
+  int rc;
+  if ((rc = h2d(ctx, ctx->wbuf[0], src, rows * cp * 4, "F32 matvec weights"))) return rc;
+  if ((rc = h2d(ctx, ctx->in[0], xs, cp * 4, "F32 matvec input"))) return rc;
+  if (!ctx->out[0].ensure(rows * 4)) return fail(ctx, SI_E_NOMEM, "F32 matvec output allocation failed");
+  launch_f32_matvec(ctx->wbuf[0].as<float>(), rows, cp, ctx->in[0].as<float>(), ctx->out[0].as<float>(), ctx->stream);
+  if ((rc = d2h(ctx, y, ctx->out[0].p, rows * 4, "F32 matvec readback"))) return rc;
+  return sync_and_check(ctx, "F32 matvec command");
+}
+
+// ---- fused SwiGLU ------------------------------------------------------------
+int si_fused_gate_up_dev(si_ctx* ctx, uint32_t type, const void* gate_dev, const void* up_dev,
+                         uint64_t rows, uint64_t cols, const float* x_dev, float* out_dev,
+                         void* stream) {
+  if (!ctx) return SI_E_INVALID;
+  int rc = check_qmv(ctx, type, rows * (cols / 256) * block_bytes_of(type), rows, cols, " fused gate/up");
+  if (rc) return rc;
+  QmvParams p = {};
+  p.type = type;
+  p.cols = uint32_t(cols);
+  p.nseg = 2;
+  p.pair = 1;
+  p.seg[0] = {static_cast<const uint8_t*>(gate_dev), out_dev, nullptr, uint32_t(rows), 0};
+  p.seg[1] = {static_cast<const uint8_t*>(up_dev), out_dev, nullptr, uint32_t(rows), 0};
+  p.items = uint32_t(rows);
+  p.x = x_dev;
+  p.err = ctx->d_err;
+  std::string msg;
+  rc = launch_qmv(p, stream ? static_cast<cudaStream_t>(stream) : ctx->stream, ctx->sm_count, true, &msg);
+  return rc ? fail(ctx, rc, msg) : SI_OK;
+}
+
+int si_fused_mlp_dev(si_ctx* ctx, uint32_t gate_type, const void* gate_dev, const void* up_dev,
+                     uint32_t down_type, const void* down_dev, uint64_t inter, uint64_t hidden,
+                     const float* x_dev, float* act_dev, float* y_dev, void* stream) {
+  int rc = si_fused_gate_up_dev(ctx, gate_type, gate_dev, up_dev, inter, hidden, x_dev, act_dev, stream);
+  if (rc) return rc;
+  return si_qmatvec_dev(ctx, down_type, down_dev, hidden, inter, act_dev, y_dev, stream);
+}
+
+static int gate_up_impl(si_ctx* ctx, const uint8_t* g, const uint8_t* u, uint64_t rows,
+                        uint64_t cols, const float* x, float* out) {
+  int rc;
+  if ((rc = h2d(ctx, ctx->in[0], x, cols * 4, "fused gate/up input"))) return rc;
+  if (!ctx->out[0].ensure(rows * 4)) return fail(ctx, SI_E_NOMEM, "fused gate/up output allocation failed");
+  if ((rc = si_fused_gate_up_dev(ctx, SI_GGML_TYPE_Q4_K, g, u, rows, cols, ctx->in[0].as<float>(),
+                                 ctx->out[0].as<float>(), ctx->stream)))
+    return rc;
+  if ((rc = d2h(ctx, out, ctx->out[0].p, rows * 4, "fused gate/up readback"))) return rc;
+  return sync_and_check(ctx, "Q4_K fused gate/up command");
+}
+
+int si_q4_k_fused_gate_up(si_ctx* ctx, const void* gate, const void* up, uint64_t nbytes,
+                          uint64_t rows, uint64_t cols, const float* x, float* out) {
+  if (!ctx) return SI_E_INVALID;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (rows == 0 || cols == 0 || cols % 256)
+    return fail(ctx, SI_E_INVALID, "Q4_K fused gate/up dimensions are invalid");
+  if (nbytes != rows * (cols / 256) * 144)
+    return fail(ctx, SI_E_INVALID, "Q4_K fused gate/up byte length is invalid");
+  int rc;
+  if ((rc = h2d(ctx, ctx->wbuf[0], gate, nbytes, "gate staging"))) return rc;
+  if ((rc = h2d(ctx, ctx->wbuf[1], up, nbytes, "up staging"))) return rc;
+  return gate_up_impl(ctx, ctx->wbuf[0].as<uint8_t>(), ctx->wbuf[1].as<uint8_t>(), rows, cols, x, out);
+}
+
+int si_q4_k_fused_gate_up_weights(si_ctx* ctx, const si_weight* gate, const si_weight* up,
+                                  uint64_t rows, uint64_t cols, const float* x, float* out) {
+  if (!ctx || !gate || !up) return fail(ctx, SI_E_INVALID, "null weight");
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (gate->type != SI_GGML_TYPE_Q4_K || up->type != SI_GGML_TYPE_Q4_K)
+    return fail(ctx, SI_E_INVALID, "Q4_K fused gate/up weights must be Q4_K");
+  if (rows == 0 || cols == 0 || cols % 256)
+    return fail(ctx, SI_E_INVALID, "Q4_K fused gate/up dimensions are invalid");
+  const uint64_t nb = rows * (cols / 256) * 144;
+  if (gate->bytes != nb || up->bytes != nb)
+    return fail(ctx, SI_E_INVALID, "Q4_K fused gate/up byte length is invalid");
+  const uint8_t *g, *u;
+  int rc;
+  if ((rc = weight_dev(ctx, gate, 0, &g)) || (rc = weight_dev(ctx, up, 1, &u))) return rc;
+  return gate_up_impl(ctx, g, u, rows, cols, x, out);
+}
+
+int si_gguf_quant_fused_mlp_weights(si_ctx* ctx, const si_weight* gate, const si_weight* up,
+                                    const si_weight* down, uint64_t gate_rows, uint64_t cols,
+                                    uint64_t down_rows, const float* x, float* y) {
+  if (!ctx || !gate || !up || !down) return fail(ctx, SI_E_INVALID, "null weight");
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (gate->type != up->type || block_bytes_of(gate->type) == 0 || block_bytes_of(down->type) == 0)
+    return fail(ctx, SI_E_INVALID, "fused MLP weights have unsupported types");
+  if (gate_rows == 0 || cols == 0 || cols % 256 || down_rows == 0 || gate_rows % 256)
+    return fail(ctx, SI_E_INVALID, "fused MLP dimensions are invalid");
+  if (gate->bytes != gate_rows * (cols / 256) * block_bytes_of(gate->type) || up->bytes != gate->bytes ||
+      down->bytes != down_rows * (gate_rows / 256) * block_bytes_of(down->type))
+    return fail(ctx, SI_E_INVALID, "fused MLP byte length is invalid");
+  const uint8_t *g, *u, *d;
+  int rc;
+  if ((rc = weight_dev(ctx, gate, 0, &g)) || (rc = weight_dev(ctx, up, 1, &u)) ||
+      (rc = weight_dev(ctx, down, 2, &d)))
+    return rc;
+  if ((rc = h2d(ctx, ctx->in[0], x, cols * 4, "fused MLP input"))) return rc;
+  if (!ctx->out[0].ensure(gate_rows * 4) || !ctx->out[1].ensure(down_rows * 4))
+    return fail(ctx, SI_E_NOMEM, "fused MLP output allocation failed");
+  if ((rc = si_fused_mlp_dev(ctx, gate->type, g, u, down->type, d, gate_rows, cols,
+                             ctx->in[0].as<float>(), ctx->out[0].as<float>(), ctx->out[1].as<float>(),
+                             ctx->stream)))
+    return rc;
+  if ((rc = d2h(ctx, y, ctx->out[1].p, down_rows * 4, "fused MLP readback"))) return rc;
+  return sync_and_check(ctx, "fused MLP command");
+}
+
+// ---- Gated DeltaNet primitives -------------------------------------------------
+int si_gated_delta_step(si_ctx* ctx, const float* q, const float* k, const float* v,
+                        const float* gate, const float* beta, const float* state_in,
+                        uint64_t heads, uint64_t kd, uint64_t vd, float* out, float* state_out) {
+  if (!ctx) return SI_E_INVALID;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (heads == 0 || kd == 0 || vd == 0 || vd > 256)  // metal.rs:3134
+    return fail(ctx, SI_E_INVALID, "Gated DeltaNet dimensions are invalid");
+  const uint64_t hk = heads * kd, sv = hk * vd;
+  int rc;
+  if ((rc = h2d(ctx, ctx->in[0], q, hk * 4, "gdn q")) || (rc = h2d(ctx, ctx->in[1], k, hk * 4, "gdn k")) ||
+      (rc = h2d(ctx, ctx->in[2], v, heads * vd * 4, "gdn v")) ||
+      (rc = h2d(ctx, ctx->in[3], gate, heads * 4, "gdn gate")) ||
+      (rc = h2d(ctx, ctx->in[4], beta, heads * 4, "gdn beta")) ||
+      (rc = h2d(ctx, ctx->in[5], state_in, sv * 4, "gdn state")))
+    return rc;
+  if (!ctx->out[0].ensure(heads * vd * 4)) return fail(ctx, SI_E_NOMEM, "gdn output allocation failed");
+  launch_gdn_step(ctx->in[5].as<float>(), ctx->in[0].as<float>(), ctx->in[1].as<float>(),
+                  ctx->in[2].as<float>(), ctx->in[3].as<float>(), ctx->in[4].as<float>(),
+                  uint32_t(heads), uint32_t(kd), uint32_t(vd), ctx->out[0].as<float>(), ctx->stream);
+  if ((rc = d2h(ctx, out, ctx->out[0].p, heads * vd * 4, "gdn readback")) ||
+      (rc = d2h(ctx, state_out, ctx->in[5].p, sv * 4, "gdn state readback")))
+    return rc;
+  return sync_and_check(ctx, "Gated DeltaNet step command");
+}
+
+int si_causal_conv1d_step(si_ctx* ctx, const float* x, const float* state_in, const float* w,
+                          uint64_t channels, uint64_t kernel, float* out, float* state_out) {
+  if (!ctx) return SI_E_INVALID;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (channels == 0 || kernel < 2) return fail(ctx, SI_E_INVALID, "causal convolution dimensions are invalid");
+  const uint64_t sb = channels * (kernel - 1) * 4;
+  int rc;
+  if ((rc = h2d(ctx, ctx->in[0], x, channels * 4, "conv input")) ||
+      (rc = h2d(ctx, ctx->in[1], state_in, sb, "conv state")) ||
+      (rc = h2d(ctx, ctx->in[2], w, channels * kernel * 4, "conv weights")))
+    return rc;
+  if (!ctx->out[0].ensure(channels * 4) || !ctx->out[1].ensure(sb))
+    return fail(ctx, SI_E_NOMEM, "conv output allocation failed");
+  launch_conv1d_step(ctx->in[0].as<float>(), ctx->in[1].as<float>(), ctx->in[2].as<float>(),
+                     uint32_t(channels), uint32_t(kernel), ctx->out[0].as<float>(),
+                     ctx->out[1].as<float>(), ctx->stream);
+  if ((rc = d2h(ctx, out, ctx->out[0].p, channels * 4, "conv readback")) ||
+      (rc = d2h(ctx, state_out, ctx->out[1].p, sb, "conv state readback")))
+    return rc;
+  return sync_and_check(ctx, "causal convolution command");
+}
+
+static int norm_impl(si_ctx* ctx, const float* x, const float* z, const float* w, uint64_t heads,
+                     uint64_t hd, float eps, float* out, const char* label) {
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (heads == 0 || hd == 0 || !std::isfinite(eps) || eps <= 0.0f)
+    return fail(ctx, SI_E_INVALID, std::string(label) + " dimensions are invalid");
+  const uint64_t n = heads * hd;
+  int rc;
+  if ((rc = h2d(ctx, ctx->in[0], x, n * 4, label)) || (rc = h2d(ctx, ctx->in[1], w, hd * 4, label))) return rc;
+  if (z && (rc = h2d(ctx, ctx->in[2], z, n * 4, label))) return rc;
+  if (!ctx->out[0].ensure(n * 4)) return fail(ctx, SI_E_NOMEM, "norm output allocation failed");
+  if (z)
+    launch_rms_norm_gated(ctx->in[0].as<float>(), ctx->in[2].as<float>(), ctx->in[1].as<float>(),
+                          uint32_t(heads), uint32_t(hd), eps, ctx->out[0].as<float>(), ctx->stream);
+  else
+    launch_rms_norm_heads(ctx->in[0].as<float>(), ctx->in[1].as<float>(), uint32_t(heads),
+                          uint32_t(hd), eps, ctx->out[0].as<float>(), ctx->stream);
+  if ((rc = d2h(ctx, out, ctx->out[0].p, n * 4, label))) return rc;
+  return sync_and_check(ctx, label);
+}
+
+int si_rms_norm_gated(si_ctx* ctx, const float* x, const float* gate, const float* w,
+                      uint64_t heads, uint64_t hd, float eps, float* out) {
+  if (!ctx) return SI_E_INVALID;
+  return norm_impl(ctx, x, gate, w, heads, hd, eps, out, "Gated RMSNorm");
+}
+
+int si_rms_norm_heads(si_ctx* ctx, const float* x, const float* w, uint64_t heads, uint64_t hd,
+                      float eps, float* out) {
+  if (!ctx) return SI_E_INVALID;
+  return norm_impl(ctx, x, nullptr, w, heads, hd, eps, out, "head RMSNorm");
+}
+
+// ---- attention -------------------------------------------------------------------
+}  // extern "C"
+
+namespace si {
+// Inverse RoPE frequencies theta^(-(2i)/d) computed on the host with the
+// reference's expression (metal.rs:1670-1671) so device angles match it.
+void rope_freqs(float theta, uint32_t dims, std::vector<float>* out) {
+  out->resize(dims / 2);
+  for (uint32_t i = 0; i < dims / 2; ++i) {
+    const float e = (2.0f * float(i)) / float(dims);
+    (*out)[i] = std::pow(theta, -e);
+  }
+}
+}  // namespace si
+
+extern "C" {
+
+int si_rope(si_ctx* ctx, const float* x, uint64_t heads, uint64_t hd, uint64_t position,
+            float theta, float* out) {
+  if (!ctx) return SI_E_INVALID;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (heads == 0 || hd == 0 || hd % 2) return fail(ctx, SI_E_INVALID, "RoPE dimensions are invalid");
+  std::vector<float> f;
+  rope_freqs(theta, uint32_t(hd), &f);
+  const uint64_t n = heads * hd;
+  int rc;
+  if ((rc = h2d(ctx, ctx->in[0], x, n * 4, "rope input")) ||
+      (rc = h2d(ctx, ctx->in[1], f.data(), f.size() * 4, "rope table")))
+    return rc;
+  if (!ctx->out[0].ensure(n * 4)) return fail(ctx, SI_E_NOMEM, "rope output allocation failed");
+  launch_rope(ctx->in[0].as<float>(), ctx->in[1].as<float>(), uint32_t(heads), uint32_t(hd),
+              uint32_t(position), ctx->out[0].as<float>(), ctx->stream);
+  if ((rc = d2h(ctx, out, ctx->out[0].p, n * 4, "rope readback"))) return rc;
+  return sync_and_check(ctx, "command");
+}
+
+int si_attention_decode(si_ctx* ctx, const si_attention_decode_input* in, float* out) {
+  if (!ctx || !in) return SI_E_INVALID;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  const uint64_t qh = in->query_heads, kvh = in->key_value_heads, hd = in->head_dim;
+  if (qh == 0 || kvh == 0 || hd == 0 || qh % kvh)
+    return fail(ctx, SI_E_INVALID, "attention head dimensions are invalid");
+  if (hd > 256 || qh / kvh > 8)
+    return fail(ctx, SI_E_UNSUPPORTED, "attention head_dim > 256 or GQA group > 8 is not supported");
+  if (in->cached_tokens > in->cache_capacity_tokens)
+    return fail(ctx, SI_E_INVALID, "attention cached token count exceeds cache capacity");
+  const uint64_t esz = in->cache_type == SI_CACHE_BF16 ? 2 : 4;
+  const uint64_t cache_bytes = kvh * in->cache_capacity_tokens * hd * esz;
+  int rc;
+  if ((rc = h2d(ctx, ctx->in[0], in->query, qh * hd * 4, "attention query")) ||
+      (rc = h2d(ctx, ctx->in[1], in->key_cache, cache_bytes, "attention key cache")) ||
+      (rc = h2d(ctx, ctx->in[2], in->value_cache, cache_bytes, "attention value cache")) ||
+      (rc = h2d(ctx, ctx->in[3], in->new_keys, kvh * hd * 4, "attention new keys")) ||
+      (rc = h2d(ctx, ctx->in[4], in->new_values, kvh * hd * 4, "attention new values")))
+    return rc;
+  const uint32_t chunk = 256;
+  const uint64_t parts = attn_scratch_floats(uint32_t(qh), uint32_t(hd),
+                                             uint32_t(in->cached_tokens + 1), chunk);
+  if (!ctx->scratch.ensure(parts * 4) || !ctx->out[0].ensure(qh * hd * 4))
+    return fail(ctx, SI_E_NOMEM, "attention scratch allocation failed");
+  AttnArgs a = {};
+  a.q = ctx->in[0].as<float>();
+  a.k_new = ctx->in[3].as<float>();
+  a.v_new = ctx->in[4].as<float>();
+  a.k_cache = ctx->in[1].p;
+  a.v_cache = ctx->in[2].p;
+  a.cached = uint32_t(in->cached_tokens);
+  a.position = 0;
+  a.qh = uint32_t(qh);
+  a.kvh = uint32_t(kvh);
+  a.hd = uint32_t(hd);
+  a.cap = uint32_t(in->cache_capacity_tokens);
+  a.cache_bf16 = in->cache_type == SI_CACHE_BF16;
+  a.part = ctx->scratch.as<float>();
+  a.out = ctx->out[0].as<float>();
+  a.chunk = chunk;
+  launch_attention(a, ctx->stream, false);
+  if ((rc = d2h(ctx, out, ctx->out[0].p, qh * hd * 4, "attention readback"))) return rc;
+  return sync_and_check(ctx, "attention command");
+}
+
+int si_argmax(si_ctx* ctx, const float* logits, uint64_t n, uint32_t* index) {
+  if (!ctx || !index) return SI_E_INVALID;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (n == 0 || n > 0xffffffffull) return fail(ctx, SI_E_INVALID, "logits length is invalid");
+  int rc;
+  if ((rc = h2d(ctx, ctx->in[0], logits, n * 4, "argmax input"))) return rc;
+  launch_argmax(ctx->in[0].as<float>(), n, ctx->d_argmax, ctx->d_index, ctx->stream);
+  if ((rc = d2h(ctx, index, ctx->d_index, 4, "argmax readback"))) return rc;
+  if ((rc = sync_and_check(ctx, "argmax command"))) return rc;
+  if (*index == 0xffffffffu) return fail(ctx, SI_E_INVALID, "logits contain no finite values");
+  return SI_OK;
+}
+
+}  // extern "C"

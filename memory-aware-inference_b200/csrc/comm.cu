@@ -1,0 +1,119 @@
+// NCCL communicator attached to a context: one process per GPU, row-sharded
+// weights, all-gather of each sharded output vector over NVLink/NVSwitch.
+#include <nccl.h>
+
+#include <chrono>
+#include <cstring>
+#include <string>
+#include <thread>
+
+#include "comm.h"
+#include "ctx.h"
+
+using namespace si;
+
+struct si_comm_state {
+  ncclComm_t comm = nullptr;
+};
+
+namespace si {
+
+// Poll a non-blocking NCCL operation until it leaves ncclInProgress, bounded
+// by `seconds`; on timeout the communicator is aborted.
+static ncclResult_t wait_nccl(ncclComm_t comm, double seconds) {
+  auto t0 = std::chrono::steady_clock::now();
+  ncclResult_t st = ncclInProgress;
+  while (true) {
+    ncclResult_t r = ncclCommGetAsyncError(comm, &st);
+    if (r != ncclSuccess) return r;
+    if (st != ncclInProgress) return st;
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > seconds)
+      return ncclInProgress;
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+int comm_allgather(si_ctx* ctx, const float* send, float* recv, size_t count, cudaStream_t s) {
+  if (!ctx->comm) return SI_OK;
+  ncclResult_t r = ncclAllGather(send, recv, count, ncclFloat32, ctx->comm->comm, s);
+  if (r != ncclSuccess && r != ncclInProgress)
+    return fail(ctx, SI_E_COMM, std::string("ncclAllGather: ") + ncclGetErrorString(r));
+  return SI_OK;
+}
+
+int comm_allreduce_sum(si_ctx* ctx, const float* send, float* recv, size_t count, cudaStream_t s) {
+  if (!ctx->comm) return SI_OK;
+  ncclResult_t r = ncclAllReduce(send, recv, count, ncclFloat32, ncclSum, ctx->comm->comm, s);
+  if (r != ncclSuccess && r != ncclInProgress)
+    return fail(ctx, SI_E_COMM, std::string("ncclAllReduce: ") + ncclGetErrorString(r));
+  return SI_OK;
+}
+
+int comm_allgather_u64(si_ctx* ctx, const unsigned long long* send, unsigned long long* recv,
+                       cudaStream_t s) {
+  if (!ctx->comm) return SI_OK;
+  ncclResult_t r = ncclAllGather(send, recv, 1, ncclUint64, ctx->comm->comm, s);
+  if (r != ncclSuccess && r != ncclInProgress)
+    return fail(ctx, SI_E_COMM, std::string("ncclAllGather(u64): ") + ncclGetErrorString(r));
+  return SI_OK;
+}
+
+}  // namespace si
+
+extern "C" {
+
+int si_comm_unique_id(void* id_out) {
+  if (!id_out) return SI_E_INVALID;
+  static_assert(sizeof(ncclUniqueId) <= SI_COMM_ID_BYTES, "NCCL id size");
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) return fail(nullptr, SI_E_COMM, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+  std::memset(id_out, 0, SI_COMM_ID_BYTES);
+  std::memcpy(id_out, &id, sizeof(id));
+  return SI_OK;
+}
+
+int si_ctx_comm_init(si_ctx* ctx, int nranks, int rank, const void* id) {
+  if (!ctx || !id || nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(ctx, SI_E_INVALID, "invalid communicator arguments");
+  if (ctx->comm) return fail(ctx, SI_E_STATE, "communicator already initialised");
+  if (nranks == 1) {
+    ctx->nranks = 1;
+    ctx->rank = 0;
+    return SI_OK;
+  }
+  cudaSetDevice(ctx->device);
+  ncclUniqueId uid;
+  std::memcpy(&uid, id, sizeof(uid));
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  auto* st = new si_comm_state();
+  ncclResult_t r = ncclCommInitRankConfig(&st->comm, nranks, uid, rank, &cfg);
+  if (r == ncclInProgress) r = wait_nccl(st->comm, 120.0);
+  if (r != ncclSuccess) {
+    if (st->comm) ncclCommAbort(st->comm);
+    delete st;
+    return fail(ctx, SI_E_COMM, std::string("ncclCommInitRankConfig: ") + ncclGetErrorString(r));
+  }
+  ctx->comm = st;
+  ctx->nranks = nranks;
+  ctx->rank = rank;
+  return SI_OK;
+}
+
+int si_ctx_comm_info(const si_ctx* ctx, int* nranks, int* rank) {
+  if (!ctx) return SI_E_INVALID;
+  if (nranks) *nranks = ctx->nranks;
+  if (rank) *rank = ctx->rank;
+  return SI_OK;
+}
+
+int si_comm_destroy_internal(si_ctx* ctx) {
+  if (!ctx || !ctx->comm) return SI_OK;
+  ncclCommDestroy(ctx->comm->comm);
+  delete ctx->comm;
+  ctx->comm = nullptr;
+  return SI_OK;
+}
+
+}  // extern "C"

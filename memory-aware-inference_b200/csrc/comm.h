@@ -1,0 +1,13 @@
+// Collectives used by the row-sharded model (no-ops without a communicator).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+struct si_ctx;
+
+namespace si {
+int comm_allgather(si_ctx* ctx, const float* send, float* recv, size_t count, cudaStream_t s);
+int comm_allreduce_sum(si_ctx* ctx, const float* send, float* recv, size_t count, cudaStream_t s);
+int comm_allgather_u64(si_ctx* ctx, const unsigned long long* send, unsigned long long* recv,
+                       cudaStream_t s);
+}  // namespace si

@@ -1,0 +1,72 @@
+// Internal definition of the backend context shared by the C-ABI files.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <mutex>
+#include <string>
+
+#include "../../include/si_cuda.h"
+
+struct si_comm_state;
+
+namespace si {
+
+// Grow-only device buffer used as per-call staging for host-memory calls.
+struct DevBuf {
+  void* p = nullptr;
+  size_t cap = 0;
+  ~DevBuf() { release(); }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+  }
+  // Ensures `bytes` (+64 B read-ahead padding for the bulk copies).
+  bool ensure(size_t bytes) {
+    if (bytes + 64 <= cap) return true;
+    release();
+    size_t want = bytes + 64;
+    if (cudaMalloc(&p, want) != cudaSuccess) {
+      p = nullptr;
+      return false;
+    }
+    cap = want;
+    return true;
+  }
+  template <typename T>
+  T* as() const { return static_cast<T*>(p); }
+};
+
+}  // namespace si
+
+struct si_ctx {
+  int device = 0;
+  int sm_count = 0;
+  si_ctx_config cfg{};
+  cudaStream_t stream = nullptr;       // compute
+  cudaStream_t copy_stream = nullptr;  // weight staging
+  int* d_err = nullptr;                // kernel error bits
+  unsigned long long* d_argmax = nullptr;
+  uint32_t* d_index = nullptr;
+  std::string err;
+  std::mutex mu;         // serialises host-memory entry points
+  std::mutex upload_mu;  // serialises weight uploads from staging threads
+  si::DevBuf in[6], out[3], wbuf[3], scratch;
+  // telemetry
+  std::atomic<uint64_t> allocated{0}, peak_allocated{0}, peak_weights{0}, weights{0};
+  std::atomic<uint64_t> peak_kv{0}, peak_scratch{0}, submitted{0}, waited{0}, wait_nanos{0};
+  // NCCL (optional)
+  si_comm_state* comm = nullptr;
+  int nranks = 1, rank = 0;
+};
+
+namespace si {
+int fail(si_ctx* ctx, int code, const std::string& msg);
+int cuda_fail(si_ctx* ctx, cudaError_t e, const char* what);
+// Synchronise the compute stream and convert kernel error bits to a status.
+int sync_and_check(si_ctx* ctx, const char* what);
+void note_alloc(si_ctx* ctx, int64_t delta);
+void note_weights(si_ctx* ctx, int64_t delta);
+}  // namespace si

@@ -1,0 +1,692 @@
+// Non-matvec kernels of the batch-1 decode path (sm_100a).
+//
+// Where the reference fixes an evaluation order (qwen35.rs, metal.rs), the
+// per-element arithmetic here follows it with explicitly rounded operations
+// (__fmul_rn / __fadd_rn prevent FMA contraction), so the dequant is
+// bit-exact and the recurrence/conv match the CPU code to the last ulp of the
+// transcendentals. Reductions that the reference runs serially are done as
+// parallel trees where that is the only difference (within 1e-5 rel-L2).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace si {
+
+// ---------------------------------------------------------------------------
+// Dequantization (quant.rs:18-174), one thread per output element.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float deq_elem(uint32_t type, const uint8_t* blk, int e) {
+  if (type == SI_GGML_TYPE_Q6_K) {
+    const int half = e >> 7, w = e & 127, m = w >> 5, idx = w & 31;
+    const uint8_t* low = blk + half * 64;
+    const uint8_t hb = blk[128 + half * 32 + idx];
+    const uint8_t lb = low[idx + ((m & 1) ? 32 : 0)];
+    const int nib = (m < 2) ? (lb & 0x0f) : (lb >> 4);
+    const int q = (nib | (((hb >> (2 * m)) & 3) << 4)) - 32;
+    const int8_t sc = static_cast<int8_t>(blk[192 + half * 8 + (idx >> 4) + 2 * m]);
+    const float d = half_bits_to_float(uint32_t(blk[208]) | (uint32_t(blk[209]) << 8));
+    return __fmul_rn(__fmul_rn(d, float(sc)), float(q));
+  }
+  const float d = half_bits_to_float(uint32_t(blk[0]) | (uint32_t(blk[1]) << 8));
+  const float mn = half_bits_to_float(uint32_t(blk[2]) | (uint32_t(blk[3]) << 8));
+  const int g = e >> 6, r = e & 63, hi = r >> 5, i = r & 31;
+  uint32_t sc, m;
+  scale_min_k4(2 * g + hi, blk + 4, sc, m);
+  int q;
+  if (type == SI_GGML_TYPE_Q4_K) {
+    const uint8_t b = blk[16 + 32 * g + i];
+    q = hi ? (b >> 4) : (b & 0x0f);
+  } else {
+    const uint8_t b = blk[48 + 32 * g + i];
+    const uint8_t h = blk[16 + i];
+    q = (hi ? (b >> 4) : (b & 0x0f)) + (((h >> (2 * g + hi)) & 1) ? 16 : 0);
+  }
+  const float d1 = __fmul_rn(d, float(sc));
+  const float m1 = __fmul_rn(mn, float(m));
+  return __fsub_rn(__fmul_rn(d1, float(q)), m1);
+}
+
+__global__ void dequant_kernel(uint32_t type, const uint8_t* w, uint64_t n, float* out) {
+  const uint32_t bb = block_bytes_of(type);
+  for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += uint64_t(gridDim.x) * blockDim.x)
+    out[i] = deq_elem(type, w + (i >> 8) * bb, int(i & 255));
+}
+
+void launch_dequant(uint32_t type, const uint8_t* w, uint64_t elements, float* out,
+                    cudaStream_t s) {
+  uint64_t blocks = (elements + 255) / 256;
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  dequant_kernel<<<unsigned(blocks), 256, 0, s>>>(type, w, elements, out);
+}
+
+// ---------------------------------------------------------------------------
+// F32 matvec (metal.rs:263-305), one warp per row.
+// ---------------------------------------------------------------------------
+__global__ void f32_matvec_kernel(const float* w, uint64_t rows, uint64_t cols, const float* x,
+                                  float* y) {
+  const uint64_t row = uint64_t(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float4* wr = reinterpret_cast<const float4*>(w + row * cols);
+  const float4* xv = reinterpret_cast<const float4*>(x);
+  float acc = 0.f;
+  for (uint64_t i = lane; i < cols / 4; i += 32) {
+    const float4 a = __ldg(wr + i), b = xv[i];
+    acc += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) y[row] = acc;
+}
+
+void launch_f32_matvec(const float* w, uint64_t rows, uint64_t cols, const float* x, float* y,
+                       cudaStream_t s) {
+  const unsigned blocks = unsigned((rows + 7) / 8);
+  f32_matvec_kernel<<<blocks, 256, 0, s>>>(w, rows, cols, x, y);
+}
+
+// ---------------------------------------------------------------------------
+// Norms (qwen35.rs:14-86): one CTA per head.
+// ---------------------------------------------------------------------------
+__device__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < int(blockDim.x >> 5); ++i) t += red[i];
+  return t;
+}
+
+__global__ void rms_norm_kernel(const float* x, const float* z, const float* w, uint32_t hd,
+                                float eps, float* out) {
+  __shared__ float red[32];
+  const uint64_t base = uint64_t(blockIdx.x) * hd;
+  float ss = 0.f;
+  for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) ss += x[base + i] * x[base + i];
+  const float tot = block_sum(ss, red);
+  const float inv = 1.0f / sqrtf(tot / float(hd) + eps);
+  for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) {
+    if (z) {
+      const float g = z[base + i];
+      out[base + i] = x[base + i] * inv * w[i] * (g / (1.0f + expf(-g)));
+    } else {
+      out[base + i] = x[base + i] * inv * (1.0f + w[i]);
+    }
+  }
+}
+
+void launch_rms_norm_heads(const float* x, const float* w, uint32_t heads, uint32_t hd,
+                           float eps, float* out, cudaStream_t s) {
+  rms_norm_kernel<<<heads, 256, 0, s>>>(x, nullptr, w, hd, eps, out);
+}
+
+void launch_rms_norm_gated(const float* x, const float* z, const float* w, uint32_t heads,
+                           uint32_t hd, float eps, float* out, cudaStream_t s) {
+  rms_norm_kernel<<<heads, 256, 0, s>>>(x, z, w, hd, eps, out);
+}
+
+// ---------------------------------------------------------------------------
+// Causal conv step (qwen35.rs:93-130), one thread per channel, the
+// reference's accumulation order, state written to a separate buffer.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float conv_channel(float xin, const float* st, const float* wc,
+                                              uint32_t k) {
+  float v = __fmul_rn(xin, wc[k - 1]);
+  for (uint32_t t = 0; t + 1 < k; ++t) v = __fadd_rn(v, __fmul_rn(st[t], wc[t]));
+  return v;
+}
+
+__global__ void conv1d_kernel(const float* x, const float* sin, const float* w, uint32_t C,
+                              uint32_t k, float* out, float* sout) {
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const float* st = sin + uint64_t(c) * (k - 1);
+  const float v = conv_channel(x[c], st, w + uint64_t(c) * k, k);
+  out[c] = v / (1.0f + expf(-v));
+  float* so = sout + uint64_t(c) * (k - 1);
+  for (uint32_t t = 0; t + 2 < k; ++t) so[t] = st[t + 1];
+  so[k - 2] = x[c];
+}
+
+void launch_conv1d_step(const float* x, const float* state_in, const float* w,
+                        uint32_t channels, uint32_t kernel, float* out, float* state_out,
+                        cudaStream_t s) {
+  conv1d_kernel<<<(channels + 255) / 256, 256, 0, s>>>(x, state_in, w, channels, kernel, out,
+                                                        state_out);
+}
+
+// ---------------------------------------------------------------------------
+// Generic recurrent step (qwen35.rs:163-225): one thread per (head, value
+// column); per column the key loops run in the reference's order.
+// ---------------------------------------------------------------------------
+__global__ void gdn_step_kernel(float* S, const float* q, const float* k, const float* v,
+                                const float* g, const float* beta, uint32_t heads, uint32_t kd,
+                                uint32_t vd, float* out) {
+  const uint32_t h = blockIdx.y;
+  const uint32_t j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (h >= heads || j >= vd) return;
+  float* s = S + uint64_t(h) * kd * vd;
+  const float* kk = k + uint64_t(h) * kd;
+  const float* qq = q + uint64_t(h) * kd;
+  const float decay = expf(g[h]);
+  float mem = 0.f;
+  for (uint32_t i = 0; i < kd; ++i) {
+    const float sv = __fmul_rn(s[uint64_t(i) * vd + j], decay);
+    s[uint64_t(i) * vd + j] = sv;
+    mem = __fadd_rn(mem, __fmul_rn(sv, kk[i]));
+  }
+  const float delta = __fmul_rn(__fsub_rn(v[uint64_t(h) * vd + j], mem), beta[h]);
+  float r = 0.f;
+  for (uint32_t i = 0; i < kd; ++i) {
+    const float sv = __fadd_rn(s[uint64_t(i) * vd + j], __fmul_rn(kk[i], delta));
+    s[uint64_t(i) * vd + j] = sv;
+    r = __fadd_rn(r, __fmul_rn(sv, qq[i]));
+  }
+  out[uint64_t(h) * vd + j] = r;
+}
+
+void launch_gdn_step(float* state, const float* q, const float* k, const float* v,
+                     const float* g, const float* beta, uint32_t heads, uint32_t kd,
+                     uint32_t vd, float* out, cudaStream_t s) {
+  dim3 grid((vd + 127) / 128, heads);
+  gdn_step_kernel<<<grid, 128, 0, s>>>(state, q, k, v, g, beta, heads, kd, vd, out);
+}
+
+// ---------------------------------------------------------------------------
+// Fused Gated DeltaNet layer step (qwen35_runtime.rs:541-620 + qwen35.rs).
+// Grid (value_heads, 128/32): one warp per 32 value columns of one head. The
+// warp recomputes the conv + L2 norm of its key head's q/k channels (cheap)
+// and holds its 32 state columns in registers: S is read and written once.
+// ---------------------------------------------------------------------------
+constexpr int kGdnD = 128;
+constexpr int kGdnCols = 32;
+
+__global__ void __launch_bounds__(32) gdn_layer_kernel(const GdnLayerArgs a) {
+  __shared__ float qs[kGdnD], ks[kGdnD];
+  const uint32_t h = blockIdx.x, chunk = blockIdx.y, lane = threadIdx.x;
+  const uint32_t kh = a.key_heads, vh = a.value_heads, K = a.kernel;
+  const uint32_t rep = vh / kh, khead = h / rep;
+  const uint32_t kw = kh * kGdnD;
+  pdl_launch_dependents();
+  pdl_wait();
+  const bool write_qk_state = (h % rep == 0) && chunk == 0;
+  // conv + SiLU for q and k channels of the key head.
+  float sq = 0.f, sk = 0.f;
+  for (uint32_t i = lane; i < kGdnD; i += 32) {
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+      const uint32_t c = part * kw + khead * kGdnD + i;
+      const float* st = a.conv_in + uint64_t(c) * (K - 1);
+      const float v = conv_channel(a.qkv[c], st, a.conv_w + uint64_t(c) * K, K);
+      const float o = v / (1.0f + expf(-v));
+      if (part == 0) {
+        qs[i] = o;
+        sq += o * o;
+      } else {
+        ks[i] = o;
+        sk += o * o;
+      }
+      if (write_qk_state) {
+        float* so = a.conv_out + uint64_t(c) * (K - 1);
+        for (uint32_t t = 0; t + 2 < K; ++t) so[t] = st[t + 1];
+        so[K - 2] = a.qkv[c];
+      }
+    }
+  }
+  // value channel of this lane's column.
+  const uint32_t col = chunk * kGdnCols + lane;
+  const uint32_t cv = 2 * kw + h * kGdnD + col;
+  float vval;
+  {
+    const float* st = a.conv_in + uint64_t(cv) * (K - 1);
+    const float v = conv_channel(a.qkv[cv], st, a.conv_w + uint64_t(cv) * K, K);
+    vval = v / (1.0f + expf(-v));
+    float* so = a.conv_out + uint64_t(cv) * (K - 1);
+    for (uint32_t t = 0; t + 2 < K; ++t) so[t] = st[t + 1];
+    so[K - 2] = a.qkv[cv];
+  }
+  sq = warp_sum(sq);
+  sk = warp_sum(sk);
+  const float invq = 1.0f / sqrtf(sq + 1.0e-6f);
+  const float invk = 1.0f / sqrtf(sk + 1.0e-6f);
+  const float rs = sqrtf(float(kGdnD));
+  __syncwarp();
+  for (uint32_t i = lane; i < kGdnD; i += 32) {
+    qs[i] = __fdiv_rn(qs[i] * invq, rs);
+    ks[i] = ks[i] * invk;
+  }
+  // gates (qwen35_runtime.rs:593-601)
+  float g, beta;
+  if (a.gates) {
+    g = a.gates[h];
+    beta = a.gates[vh + h];
+  } else {
+    const float sp_in = a.alpha[h] + a.dt_bias[h];
+    const float sp = sp_in > 20.0f ? sp_in : log1pf(expf(sp_in));
+    g = -expf(a.a_log[h]) * sp;
+    beta = 1.0f / (1.0f + expf(-a.beta_logit[h]));
+  }
+  __syncwarp();
+  // recurrence on 32 columns, S column in registers.
+  float* S = a.state + uint64_t(h) * kGdnD * kGdnD + col;
+  float s[kGdnD];
+#pragma unroll
+  for (int i = 0; i < kGdnD; ++i) s[i] = S[uint64_t(i) * kGdnD];
+  const float decay = expf(g);
+  float mem = 0.f;
+#pragma unroll
+  for (int i = 0; i < kGdnD; ++i) {
+    s[i] = __fmul_rn(s[i], decay);
+    mem = __fadd_rn(mem, __fmul_rn(s[i], ks[i]));
+  }
+  const float delta = __fmul_rn(__fsub_rn(vval, mem), beta);
+  float r = 0.f;
+#pragma unroll
+  for (int i = 0; i < kGdnD; ++i) {
+    s[i] = __fadd_rn(s[i], __fmul_rn(ks[i], delta));
+    r = __fadd_rn(r, __fmul_rn(s[i], qs[i]));
+  }
+#pragma unroll
+  for (int i = 0; i < kGdnD; ++i) S[uint64_t(i) * kGdnD] = s[i];
+  a.core[h * kGdnD + col] = r;
+}
+
+void launch_gdn_layer(const GdnLayerArgs& a, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.value_heads, kGdnD / kGdnCols);
+  cfg.blockDim = dim3(32);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, gdn_layer_kernel, a);
+}
+
+// ---------------------------------------------------------------------------
+// RoPE (metal.rs:1655-1679) with host-computed inverse frequencies so the
+// angle pos*freq is bit-identical to the CPU reference's.
+// ---------------------------------------------------------------------------
+__global__ void rope_kernel(const float* x, const float* freq, uint32_t heads, uint32_t hd,
+                            uint32_t pos, float* out) {
+  const uint32_t pairs = hd / 2;
+  const uint32_t p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= heads * pairs) return;
+  const uint32_t h = p / pairs, i = p % pairs;
+  const float ang = float(pos) * freq[i];
+  float sn, cs;
+  sincosf(ang, &sn, &cs);
+  const uint64_t o = uint64_t(h) * hd + 2 * i;
+  const float a = x[o], b = x[o + 1];
+  out[o] = a * cs - b * sn;
+  out[o + 1] = a * sn + b * cs;
+}
+
+void launch_rope(const float* x, const float* freq, uint32_t heads, uint32_t hd, uint32_t pos,
+                 float* out, cudaStream_t s) {
+  const uint32_t n = heads * (hd / 2);
+  rope_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, freq, heads, hd, pos, out);
+}
+
+// ---------------------------------------------------------------------------
+// Split-K GQA decode (metal.rs:1681-1766 semantics) over a head-major cache
+// [kvh][cap][hd] (cache.rs:1-4), bf16 or f32 elements, plus the current
+// token's K/V in f32. Grid (chunks, kvh), 256 threads. Each CTA handles all
+// query heads of its KV group for `chunk` tokens, so K/V are read once.
+// ---------------------------------------------------------------------------
+constexpr int kAttnThreads = 256;
+constexpr int kAttnMaxHd = 256;
+constexpr int kAttnMaxGroup = 8;
+
+template <bool BF16>
+__device__ __forceinline__ float cache_elem(const void* c, uint64_t i) {
+  if (BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(c)[i]);
+  return reinterpret_cast<const float*>(c)[i];
+}
+
+// q/k preparation: (1+w) head RMSNorm, then RoPE on the first `rotary` dims.
+__device__ void prep_head(const float* src, const float* norm_w, const float* freq,
+                          uint32_t hd, uint32_t rotary, uint32_t pos, float eps, float* dst,
+                          float* red) {
+  // one warp per head
+  const int lane = threadIdx.x & 31;
+  float inv = 1.0f;
+  if (norm_w) {
+    float ss = 0.f;
+    for (uint32_t i = lane; i < hd; i += 32) ss += src[i] * src[i];
+    ss = warp_sum(ss);
+    inv = 1.0f / sqrtf(ss / float(hd) + eps);
+  }
+  for (uint32_t i = lane; i < hd; i += 32) dst[i] = norm_w ? src[i] * inv * (1.0f + norm_w[i]) : src[i];
+  __syncwarp();
+  if (freq) {
+    for (uint32_t p = lane; p < rotary / 2; p += 32) {
+      const float ang = float(pos) * freq[p];
+      float sn, cs;
+      sincosf(ang, &sn, &cs);
+      const float a = dst[2 * p], b = dst[2 * p + 1];
+      dst[2 * p] = a * cs - b * sn;
+      dst[2 * p + 1] = a * sn + b * cs;
+    }
+  }
+  __syncwarp();
+  (void)red;
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnArgs a) {
+  __shared__ float qs[kAttnMaxGroup][kAttnMaxHd];
+  __shared__ float kn[kAttnMaxHd];
+  __shared__ float sc[kAttnMaxGroup][kAttnThreads];
+  __shared__ float red[kAttnMaxGroup][kAttnThreads / 32];
+  __shared__ float mx[kAttnMaxGroup], sm[kAttnMaxGroup];
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t kvh = blockIdx.y, chunk = blockIdx.x;
+  const uint32_t hd = a.hd, group = a.qh / a.kvh;
+  const uint32_t n = a.dev_pos ? a.dev_pos[0] : a.cached;  // cached tokens
+  const uint32_t pos = a.dev_pos ? a.dev_pos[0] : a.position;
+  const uint32_t total = n + 1;
+  const uint32_t t0 = chunk * a.chunk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t nchunks_live = (total + a.chunk - 1) / a.chunk;
+  float* part = a.part + (uint64_t(chunk) * a.qh) * (hd + 2);
+  if (chunk >= nchunks_live) {
+    // beyond the live length (graph launches size the grid for capacity)
+    for (uint32_t h = threadIdx.x; h < group; h += blockDim.x) {
+      float* ph = part + uint64_t(kvh * group + h) * (hd + 2);
+      ph[hd] = -INFINITY;
+      ph[hd + 1] = 0.f;
+    }
+    return;
+  }
+  const uint32_t cnt = min(a.chunk, total - t0);
+  const bool has_new = (t0 + cnt == total);
+  // prepare queries of the group (and the new key when this chunk holds it)
+  for (uint32_t h = warp; h < group + 1; h += kAttnThreads / 32) {
+    if (h < group) {
+      const uint32_t qhd = kvh * group + h;
+      prep_head(a.q + uint64_t(qhd) * hd, a.q_norm, a.rope_freq, hd, a.rotary, pos, a.eps,
+                qs[h], nullptr);
+    } else if (has_new || a.k_cache_w) {
+      prep_head(a.k_new + uint64_t(kvh) * hd, a.k_norm, a.rope_freq, hd, a.rotary, pos, a.eps,
+                kn, nullptr);
+    }
+  }
+  __syncthreads();
+  const float scale = 1.0f / sqrtf(float(hd));
+  // scores: one thread per token, sequential over dims (reference order)
+  for (uint32_t tt = threadIdx.x; tt < cnt; tt += kAttnThreads) {
+    const uint32_t t = t0 + tt;
+    float acc[kAttnMaxGroup];
+#pragma unroll
+    for (int h = 0; h < kAttnMaxGroup; ++h) acc[h] = 0.f;
+    if (t < n) {
+      const uint64_t base = (uint64_t(kvh) * a.cap + t) * hd;
+      if (BF16 && (hd % 8 == 0)) {
+        const uint4* kr = reinterpret_cast<const uint4*>(
+            reinterpret_cast<const __nv_bfloat16*>(a.k_cache) + base);
+        for (uint32_t d8 = 0; d8 < hd / 8; ++d8) {
+          const uint4 u = __ldg(kr + d8);
+          const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float kv = __uint_as_float((wv[e >> 1] >> ((e & 1) * 16)) << 16);
+            const uint32_t d = d8 * 8 + e;
+#pragma unroll
+            for (int h = 0; h < kAttnMaxGroup; ++h)
+              if (h < int(group)) acc[h] += qs[h][d] * kv;
+          }
+        }
+      } else {
+        for (uint32_t d = 0; d < hd; ++d) {
+          const float kv = cache_elem<BF16>(a.k_cache, base + d);
+#pragma unroll
+          for (int h = 0; h < kAttnMaxGroup; ++h)
+            if (h < int(group)) acc[h] += qs[h][d] * kv;
+        }
+      }
+    } else {
+      for (uint32_t d = 0; d < hd; ++d) {
+        const float kv = kn[d];
+#pragma unroll
+        for (int h = 0; h < kAttnMaxGroup; ++h)
+          if (h < int(group)) acc[h] += qs[h][d] * kv;
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < kAttnMaxGroup; ++h)
+      if (h < int(group)) sc[h][tt] = acc[h];
+  }
+  __syncthreads();
+  // per-head chunk max of score*scale and sum of exp
+  for (uint32_t h = 0; h < group; ++h) {
+    float m = -INFINITY;
+    for (uint32_t tt = threadIdx.x; tt < cnt; tt += kAttnThreads) m = fmaxf(m, sc[h][tt] * scale);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[h][warp] = m;
+  }
+  __syncthreads();
+  if (threadIdx.x < group) {
+    float m = -INFINITY;
+    for (int w = 0; w < kAttnThreads / 32; ++w) m = fmaxf(m, red[threadIdx.x][w]);
+    mx[threadIdx.x] = m;
+  }
+  __syncthreads();
+  for (uint32_t h = 0; h < group; ++h) {
+    float s = 0.f;
+    for (uint32_t tt = threadIdx.x; tt < cnt; tt += kAttnThreads) {
+      const float p = expf(sc[h][tt] * scale - mx[h]);
+      sc[h][tt] = p;
+      s += p;
+    }
+    s = warp_sum(s);
+    if (lane == 0) red[h][warp] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x < group) {
+    float s = 0.f;
+    for (int w = 0; w < kAttnThreads / 32; ++w) s += red[threadIdx.x][w];
+    sm[threadIdx.x] = s;
+  }
+  __syncthreads();
+  // P.V: one thread per dimension
+  for (uint32_t d = threadIdx.x; d < hd; d += kAttnThreads) {
+    float acc[kAttnMaxGroup];
+#pragma unroll
+    for (int h = 0; h < kAttnMaxGroup; ++h) acc[h] = 0.f;
+    for (uint32_t tt = 0; tt < cnt; ++tt) {
+      const uint32_t t = t0 + tt;
+      const float vv = (t < n) ? cache_elem<BF16>(a.v_cache, (uint64_t(kvh) * a.cap + t) * hd + d)
+                               : a.v_new[uint64_t(kvh) * hd + d];
+#pragma unroll
+      for (int h = 0; h < kAttnMaxGroup; ++h)
+        if (h < int(group)) acc[h] += sc[h][tt] * vv;
+    }
+    for (uint32_t h = 0; h < group; ++h) part[uint64_t(kvh * group + h) * (hd + 2) + d] = acc[h];
+  }
+  if (threadIdx.x < group) {
+    float* ph = part + uint64_t(kvh * group + threadIdx.x) * (hd + 2);
+    ph[hd] = mx[threadIdx.x];
+    ph[hd + 1] = sm[threadIdx.x];
+  }
+  // append the new token (bf16) to the cache; position n is never read here
+  if (has_new && a.k_cache_w) {
+    if (n < a.cap) {
+      for (uint32_t d = threadIdx.x; d < hd; d += kAttnThreads) {
+        const uint64_t o = (uint64_t(kvh) * a.cap + n) * hd + d;
+        a.k_cache_w[o] = __bfloat16_as_ushort(__float2bfloat16_rn(kn[d]));
+        a.v_cache_w[o] = __bfloat16_as_ushort(__float2bfloat16_rn(a.v_new[uint64_t(kvh) * hd + d]));
+      }
+    }
+  }
+}
+
+__global__ void attn_combine_kernel(const AttnArgs a, uint32_t nchunks) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t qhd = blockIdx.x, hd = a.hd;
+  float M = -INFINITY;
+  for (uint32_t c = 0; c < nchunks; ++c)
+    M = fmaxf(M, a.part[(uint64_t(c) * a.qh + qhd) * (hd + 2) + hd]);
+  float L = 0.f;
+  for (uint32_t c = 0; c < nchunks; ++c) {
+    const float* ph = a.part + (uint64_t(c) * a.qh + qhd) * (hd + 2);
+    if (ph[hd] > -INFINITY) L += expf(ph[hd] - M) * ph[hd + 1];
+  }
+  for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x) {
+    float acc = 0.f;
+    for (uint32_t c = 0; c < nchunks; ++c) {
+      const float* ph = a.part + (uint64_t(c) * a.qh + qhd) * (hd + 2);
+      if (ph[hd] > -INFINITY) acc += expf(ph[hd] - M) * ph[d];
+    }
+    a.out[uint64_t(qhd) * hd + d] = acc / L;
+  }
+}
+
+uint64_t attn_scratch_floats(uint32_t qh, uint32_t hd, uint32_t total_tokens, uint32_t chunk) {
+  const uint64_t nch = (uint64_t(total_tokens) + chunk - 1) / chunk;
+  return nch * qh * (hd + 2);
+}
+
+void launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
+  // grid sized for the largest length this call can see
+  const uint32_t max_total = a.dev_pos ? a.cap + 1 : a.cached + 1;
+  const uint32_t nch = (max_total + a.chunk - 1) / a.chunk;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nch, a.kvh);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  if (a.cache_bf16)
+    cudaLaunchKernelEx(&cfg, attn_partial_kernel<true>, a);
+  else
+    cudaLaunchKernelEx(&cfg, attn_partial_kernel<false>, a);
+  cfg.gridDim = dim3(a.qh);
+  cfg.blockDim = dim3(256);
+  cudaLaunchKernelEx(&cfg, attn_combine_kernel, a, nch);
+}
+
+// ---------------------------------------------------------------------------
+// Greedy argmax under f32::total_cmp, last index among equal maxima.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned long long argmax_key(float f, uint32_t idx) {
+  const int32_t i = __float_as_int(f);
+  const int32_t t = i ^ int32_t(uint32_t(i >> 31) >> 1);
+  const uint32_t u = uint32_t(t) ^ 0x80000000u;
+  return (static_cast<unsigned long long>(u) << 32) | idx;
+}
+
+__global__ void argmax_kernel(const float* v, uint64_t n, uint32_t base, unsigned long long* key) {
+  unsigned long long best = 0;
+  for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += uint64_t(gridDim.x) * blockDim.x) {
+    const float f = v[i];
+    if (isfinite(f)) {
+      const unsigned long long k = argmax_key(f, uint32_t(i) + base);
+      best = k > best ? k : best;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0 && best) atomicMax(key, best);
+}
+
+// Max over `count` keys (one per rank) -> index; 0xFFFFFFFF when none finite.
+__global__ void argmax_finish(unsigned long long* keys, uint32_t count, uint32_t* index) {
+  unsigned long long k = 0;
+  for (uint32_t i = 0; i < count; ++i) k = keys[i] > k ? keys[i] : k;
+  *index = k ? uint32_t(k & 0xffffffffu) : 0xffffffffu;
+}
+
+void launch_argmax_key(const float* v, uint64_t n, uint32_t base, unsigned long long* key,
+                       cudaStream_t s) {
+  uint64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (blocks == 0) blocks = 1;
+  argmax_kernel<<<unsigned(blocks), 256, 0, s>>>(v, n, base, key);
+}
+
+void launch_argmax_finish(unsigned long long* keys, uint32_t count, uint32_t* index,
+                          cudaStream_t s) {
+  argmax_finish<<<1, 1, 0, s>>>(keys, count, index);
+}
+
+void launch_argmax(const float* v, uint64_t n, unsigned long long* key, uint32_t* index,
+                   cudaStream_t s) {
+  cudaMemsetAsync(key, 0, sizeof(unsigned long long), s);
+  launch_argmax_key(v, n, 0, key, s);
+  launch_argmax_finish(key, 1, index, s);
+}
+
+// ---------------------------------------------------------------------------
+// F32 matvec with the (1+w) RMSNorm of x fused in (alpha/beta projections of
+// the Gated DeltaNet mixer, qwen35_runtime.rs:575-590). One CTA per 8 rows.
+// ---------------------------------------------------------------------------
+__global__ void f32_matvec_norm_kernel(const float* w, uint32_t rows, uint32_t cols, const float* x,
+                                       const float* nw, float eps, float* y) {
+  __shared__ float red[32];
+  float ss = 0.f;
+  for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) ss += x[i] * x[i];
+  const float inv = 1.0f / sqrtf(block_sum(ss, red) / float(cols) + eps);
+  const uint32_t row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* wr = w + uint64_t(row) * cols;
+  float acc = 0.f;
+  for (uint32_t i = lane; i < cols; i += 32) acc += wr[i] * (x[i] * inv * (1.0f + nw[i]));
+  acc = warp_sum(acc);
+  if (lane == 0) y[row] = acc;
+}
+
+void launch_f32_matvec_norm(const float* w, uint32_t rows, uint32_t cols, const float* x,
+                            const float* norm_w, float eps, float* y, cudaStream_t s) {
+  f32_matvec_norm_kernel<<<(rows + 7) / 8, 256, 0, s>>>(w, rows, cols, x, norm_w, eps, y);
+}
+
+// ---------------------------------------------------------------------------
+// Embedding row (qwen35_runtime.rs:2122-2130): the Q4_K row of the token held
+// on this rank (table rows [row_lo, row_hi)) is staged through shared memory
+// and dequantized bit-exactly; other ranks write zeros (summed afterwards).
+// `table` may be mapped host memory (zero-copy read of one row).
+// ---------------------------------------------------------------------------
+__global__ void embed_kernel(const uint8_t* table, uint32_t cols, const uint32_t* d_token,
+                             uint32_t row_lo, uint32_t row_hi, float* out) {
+  extern __shared__ __align__(16) uint8_t row[];
+  const uint32_t tok = *d_token;
+  const bool mine = tok >= row_lo && tok < row_hi;
+  const uint32_t rb = cols / 256 * 144;
+  if (mine) {
+    const uint4* src = reinterpret_cast<const uint4*>(table + uint64_t(tok - row_lo) * rb);
+    for (uint32_t i = threadIdx.x; i < rb / 16; i += blockDim.x) reinterpret_cast<uint4*>(row)[i] = src[i];
+  }
+  __syncthreads();
+  for (uint32_t e = threadIdx.x; e < cols; e += blockDim.x)
+    out[e] = mine ? deq_elem(SI_GGML_TYPE_Q4_K, row + (e >> 8) * 144, int(e & 255)) : 0.0f;
+}
+
+void launch_embed(const uint8_t* table, uint32_t cols, const uint32_t* d_token, uint32_t row_lo,
+                  uint32_t row_hi, float* out, cudaStream_t s) {
+  embed_kernel<<<1, 1024, cols / 256 * 144, s>>>(table, cols, d_token, row_lo, row_hi, out);
+}
+
+__global__ void add_kernel(const float* a, const float* b, float* y, uint64_t n) {
+  const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = a[i] + b[i];
+}
+
+void launch_add(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s) {
+  add_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(a, b, y, n);
+}
+
+}  // namespace si

@@ -1,0 +1,921 @@
+// Synthetic Qwen3.6-shaped decoder on the CUDA backend: seeded weights in
+// pinned host memory, a residency plan inside the HBM budget, a depth-N
+// staging ring for the streamed layers, the per-token layer loop, greedy
+// generation, and row sharding over a NCCL communicator.
+//
+// Reference counterparts: Qwen35Runtime (src/qwen35_runtime.rs:1519-2267):
+// decode_hidden 1776-1941, logits 2132-2192, decode_token 2229-2246, staging
+// 2283-2332; residency selection 1552-1733; planner budget check
+// (src/planner.rs:174-251); run_gguf_generation (src/runtime.rs:3560-3614).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "comm.h"
+#include "common.cuh"
+#include "ctx.h"
+#include "kernels.cuh"
+#include "qmatvec.cuh"
+#include "synth.h"
+
+using namespace si;
+
+
+namespace {
+
+struct RowRange {
+  uint64_t begin, end;
+};
+
+struct LocalTensor {
+  bool present = false;
+  uint32_t type = 0;
+  uint64_t full_rows = 0, cols = 0, rows = 0;  // rows = local rows
+  std::vector<RowRange> ranges;                 // full-tensor rows held locally
+  uint64_t offset = 0, bytes = 0;               // inside the packed layer buffer
+  float mean = 0.f, stdev = 0.f;                // F32 tensors
+};
+
+struct LayerLayout {
+  bool gdn = false;
+  LocalTensor t[SI_T_COUNT];
+  uint64_t bytes = 0;
+};
+
+uint64_t row_bytes_of(uint32_t type, uint64_t cols) {
+  return type == SI_GGML_TYPE_F32 ? cols * 4 : cols / 256 * block_bytes_of(type);
+}
+
+uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+
+}  // namespace
+
+struct si_model {
+  si_ctx* ctx = nullptr;
+  si_model_config c{};
+  uint64_t seed = 0;
+  int n = 1, r = 0;
+  // sharded dims
+  uint32_t kh_l = 0, vh_l = 0, qh_l = 0, kv_lo = 0, kvh_l = 0, H_l = 0, I_l = 0, V_l = 0;
+  std::vector<LayerLayout> layout;  // [layers + 1], globals at index `layers`
+  std::vector<uint8_t*> host;       // pinned packed layer buffers
+  uint8_t* embd_host = nullptr;     // mapped pinned token_embd shard
+  uint8_t* embd_dev = nullptr;
+  // residency
+  std::vector<uint8_t*> dev_layer;  // resident pointer or nullptr (streamed)
+  uint8_t* dev_resident = nullptr;
+  std::vector<uint32_t> streamed;
+  uint32_t depth = 3;
+  uint8_t* slot[4] = {nullptr, nullptr, nullptr, nullptr};
+  cudaEvent_t copy_done[4] = {}, compute_done[4] = {};
+  uint64_t occ_issued = 0, occ_next = 0;  // streamed-layer occurrences
+  si_plan_info plan{};
+  // state
+  std::vector<float*> conv[2];
+  std::vector<float*> rec;
+  std::vector<uint16_t*> kc, vc;
+  std::vector<uint32_t> cached;
+  std::vector<uint32_t> conv_parity;
+  uint8_t* state_block = nullptr;
+  // scratch
+  uint8_t* scratch_block = nullptr;
+  float *hidden, *slice, *qkv, *z, *ab, *core, *core_full, *z_full, *qg, *kk, *vv, *att,
+      *att_full, *gate_full, *gate_l, *act, *act_full, *logits, *logits_full, *rope, *part, *embed;
+  uint32_t* d_token;
+  unsigned long long *d_key, *d_keys;
+  std::vector<float> rope_host;
+};
+
+namespace {
+
+int model_fail(si_model* m, int code, const std::string& msg) { return fail(m ? m->ctx : nullptr, code, msg); }
+
+// Full tensor shapes of one layer / the globals (qwen35_runtime.rs:419-446,
+// 640-657, model.rs:418-441).
+void full_spec(const si_model_config& c, bool gdn, bool globals, LayerLayout* L) {
+  auto set = [&](int id, uint32_t type, uint64_t rows, uint64_t cols, float mean = 0.f, float sd = 0.f) {
+    LocalTensor& t = L->t[id];
+    t.present = true;
+    t.type = type;
+    t.full_rows = rows;
+    t.cols = cols;
+    t.mean = mean;
+    t.stdev = sd;
+  };
+  const uint64_t H = c.hidden, I = c.intermediate, d = c.gdn_head_dim;
+  if (globals) {
+    set(SI_T_OUTPUT_NORM, SI_GGML_TYPE_F32, 1, H, 0.f, 0.1f);
+    set(SI_T_OUTPUT, c.head_type, c.vocab, H);
+    return;  // token_embd is held separately (mapped host memory)
+  }
+  set(SI_T_ATTN_NORM, SI_GGML_TYPE_F32, 1, H, 0.f, 0.1f);
+  set(SI_T_POST_NORM, SI_GGML_TYPE_F32, 1, H, 0.f, 0.1f);
+  set(SI_T_FFN_GATE, c.mlp_type, I, H);
+  set(SI_T_FFN_UP, c.mlp_type, I, H);
+  set(SI_T_FFN_DOWN, c.down_type, H, I);
+  if (gdn) {
+    const uint64_t proj = (2ull * c.gdn_key_heads + c.gdn_value_heads) * d, vw = uint64_t(c.gdn_value_heads) * d;
+    set(SI_T_SSM_QKV, SI_GGML_TYPE_Q4_K, proj, H);
+    set(SI_T_SSM_Z, SI_GGML_TYPE_Q4_K, vw, H);
+    set(SI_T_SSM_ALPHA, SI_GGML_TYPE_F32, c.gdn_value_heads, H, 0.f, 0.02f);
+    set(SI_T_SSM_BETA, SI_GGML_TYPE_F32, c.gdn_value_heads, H, 0.f, 0.02f);
+    set(SI_T_SSM_CONV, SI_GGML_TYPE_F32, proj, c.conv_kernel, 0.f, 0.5f);
+    set(SI_T_SSM_A, SI_GGML_TYPE_F32, c.gdn_value_heads, 1, 0.f, 0.5f);
+    set(SI_T_SSM_DT, SI_GGML_TYPE_F32, c.gdn_value_heads, 1, 0.f, 0.5f);
+    set(SI_T_SSM_NORM, SI_GGML_TYPE_F32, 1, d, 1.f, 0.1f);
+    set(SI_T_SSM_OUT, SI_GGML_TYPE_Q4_K, H, vw);
+  } else {
+    const uint64_t qw = uint64_t(c.attn_q_heads) * c.attn_head_dim, kvw = uint64_t(c.attn_kv_heads) * c.attn_head_dim;
+    set(SI_T_ATTN_Q, SI_GGML_TYPE_Q4_K, 2 * qw, H);
+    set(SI_T_ATTN_K, SI_GGML_TYPE_Q4_K, kvw, H);
+    set(SI_T_ATTN_V, SI_GGML_TYPE_Q4_K, kvw, H);
+    set(SI_T_ATTN_O, SI_GGML_TYPE_Q4_K, H, qw);
+    set(SI_T_ATTN_QNORM, SI_GGML_TYPE_F32, 1, c.attn_head_dim, 0.f, 0.1f);
+    set(SI_T_ATTN_KNORM, SI_GGML_TYPE_F32, 1, c.attn_head_dim, 0.f, 0.1f);
+  }
+}
+
+// Rows of each tensor held by rank r of n (row sharding; outputs are
+// all-gathered so every row's dot product is the 1-GPU one).
+void shard_layer(const si_model& m, LayerLayout* L) {
+  const si_model_config& c = m.c;
+  const uint64_t H = c.hidden, I = c.intermediate, d = c.gdn_head_dim, hd = c.attn_head_dim;
+  const uint64_t n = uint64_t(m.n), r = uint64_t(m.r);
+  for (int id = 0; id < SI_T_COUNT; ++id) {
+    LocalTensor& t = L->t[id];
+    if (!t.present) continue;
+    auto one = [&](uint64_t b, uint64_t e) { t.ranges = {{b, e}}; };
+    switch (id) {
+      case SI_T_FFN_GATE:
+      case SI_T_FFN_UP: one(r * I / n, (r + 1) * I / n); break;
+      case SI_T_FFN_DOWN:
+      case SI_T_SSM_OUT:
+      case SI_T_ATTN_O: one(r * H / n, (r + 1) * H / n); break;
+      case SI_T_OUTPUT: one(r * c.vocab / n, (r + 1) * c.vocab / n); break;
+      case SI_T_SSM_QKV:
+      case SI_T_SSM_CONV: {
+        const uint64_t kw = uint64_t(c.gdn_key_heads) * d;
+        const uint64_t q0 = r * m.kh_l * d, v0 = r * m.vh_l * d;
+        t.ranges = {{q0, q0 + m.kh_l * d}, {kw + q0, kw + q0 + m.kh_l * d}, {2 * kw + v0, 2 * kw + v0 + m.vh_l * d}};
+        break;
+      }
+      case SI_T_SSM_Z: one(r * m.vh_l * d, (r + 1) * m.vh_l * d); break;
+      case SI_T_SSM_ALPHA:
+      case SI_T_SSM_BETA:
+      case SI_T_SSM_A:
+      case SI_T_SSM_DT: one(r * m.vh_l, (r + 1) * m.vh_l); break;
+      case SI_T_ATTN_Q: {
+        const uint64_t qw = uint64_t(c.attn_q_heads) * hd, q0 = r * m.qh_l * hd;
+        t.ranges = {{q0, q0 + m.qh_l * hd}, {qw + q0, qw + q0 + m.qh_l * hd}};
+        break;
+      }
+      case SI_T_ATTN_K:
+      case SI_T_ATTN_V: one(uint64_t(m.kv_lo) * hd, uint64_t(m.kv_lo + m.kvh_l) * hd); break;
+      default: one(0, t.full_rows); break;
+    }
+    t.rows = 0;
+    for (auto& rr : t.ranges) t.rows += rr.end - rr.begin;
+  }
+  uint64_t off = 0;
+  for (int id = 0; id < SI_T_COUNT; ++id) {
+    LocalTensor& t = L->t[id];
+    if (!t.present) continue;
+    t.offset = off;
+    t.bytes = t.rows * row_bytes_of(t.type, t.cols);
+    off = align256(off + t.bytes + 64);
+  }
+  L->bytes = off;
+}
+
+// Generate local tensor `t` of (layer, id) into dst.
+void generate_tensor(uint64_t seed, uint32_t layer, uint32_t id, const LocalTensor& t, uint8_t* dst) {
+  const uint64_t key = tensor_key(seed, layer, id);
+  const uint64_t rb = row_bytes_of(t.type, t.cols);
+  uint8_t* p = dst;
+  for (const RowRange& rr : t.ranges) {
+    for (uint64_t row = rr.begin; row < rr.end; ++row) {
+      if (t.type == SI_GGML_TYPE_F32) {
+        float* f = reinterpret_cast<float*>(p);
+        for (uint64_t cidx = 0; cidx < t.cols; ++cidx)
+          f[cidx] = float(double(t.mean) + double(t.stdev) * gauss(key, row * t.cols + cidx));
+      } else {
+        fill_bytes(key, row * rb, rb, p);
+        const uint32_t bb = block_bytes_of(t.type);
+        const uint64_t bpr = t.cols / 256;
+        for (uint64_t b = 0; b < bpr; ++b) patch_scales(key, t.type, row * bpr + b, p + b * bb);
+      }
+      p += rb;
+    }
+  }
+}
+
+template <typename F>
+void parallel_for(uint64_t n, F f) {
+  unsigned nt = std::max(1u, std::min(64u, std::thread::hardware_concurrency()));
+  std::vector<std::thread> th;
+  std::atomic<uint64_t> next{0};
+  for (unsigned i = 0; i < nt; ++i)
+    th.emplace_back([&] {
+      for (uint64_t k = next++; k < n; k = next++) f(k);
+    });
+  for (auto& t : th) t.join();
+}
+
+int validate_config(const si_model_config& c, int n) {
+  const uint64_t nn = uint64_t(n);
+  if (c.hidden == 0 || c.hidden % 256 || c.intermediate == 0 || c.intermediate % 256 ||
+      c.layers == 0 || c.vocab == 0 || c.attn_interval == 0)
+    return 1;
+  if (c.gdn_head_dim != 128 || c.gdn_key_heads == 0 || c.gdn_value_heads % c.gdn_key_heads ||
+      (uint64_t(c.gdn_value_heads) * 128) % 256 || c.conv_kernel < 2)
+    return 2;
+  if (c.attn_kv_heads == 0 || c.attn_q_heads % c.attn_kv_heads || c.attn_head_dim > 256 ||
+      c.attn_head_dim % 32 || c.attn_q_heads / c.attn_kv_heads > 8 ||
+      (uint64_t(c.attn_q_heads) * c.attn_head_dim) % 256 || c.rotary_dim > c.attn_head_dim ||
+      c.rotary_dim % 2 || c.kv_capacity == 0)
+    return 3;
+  if (!(c.rms_eps > 0.f) || !std::isfinite(c.rms_eps)) return 4;
+  if (block_bytes_of(c.mlp_type) == 0 || block_bytes_of(c.down_type) == 0 || block_bytes_of(c.head_type) == 0)
+    return 5;
+  if (c.hidden % nn || c.intermediate % nn || c.vocab % nn || c.gdn_key_heads % nn ||
+      c.gdn_value_heads % nn || c.attn_q_heads % nn)
+    return 6;
+  const uint32_t group = c.attn_q_heads / c.attn_kv_heads, qh_l = c.attn_q_heads / n;
+  if (group % qh_l && qh_l % group) return 7;
+  return 0;
+}
+
+}  // namespace
+
+extern "C" void si_model_config_qwen36_27b(si_model_config* c) {
+  if (!c) return;
+  std::memset(c, 0, sizeof(*c));
+  c->hidden = 5120;
+  c->intermediate = 17408;
+  c->layers = 64;
+  c->vocab = 248320;
+  c->attn_interval = 4;
+  c->attn_q_heads = 24;
+  c->attn_kv_heads = 4;
+  c->attn_head_dim = 256;
+  c->rotary_dim = 64;
+  c->rope_theta = 1.0e7f;
+  c->gdn_key_heads = 16;
+  c->gdn_value_heads = 48;
+  c->gdn_head_dim = 128;
+  c->conv_kernel = 4;
+  c->rms_eps = 1.0e-6f;
+  c->kv_capacity = 144;
+  c->eos_token = 0xFFFFFFFFu;
+  c->mlp_type = SI_GGML_TYPE_Q4_K;
+  c->down_type = SI_GGML_TYPE_Q6_K;
+  c->head_type = SI_GGML_TYPE_Q6_K;
+}
+
+namespace {
+
+void free_model(si_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->ctx->device);
+  cudaDeviceSynchronize();
+  for (auto* h : m->host)
+    if (h) cudaFreeHost(h);
+  if (m->embd_host) cudaFreeHost(m->embd_host);
+  if (m->dev_resident) cudaFree(m->dev_resident);
+  for (int i = 0; i < 4; ++i) {
+    if (m->slot[i]) cudaFree(m->slot[i]);
+    if (m->copy_done[i]) cudaEventDestroy(m->copy_done[i]);
+    if (m->compute_done[i]) cudaEventDestroy(m->compute_done[i]);
+  }
+  if (m->state_block) cudaFree(m->state_block);
+  if (m->scratch_block) cudaFree(m->scratch_block);
+  note_alloc(m->ctx, -int64_t(m->plan.resident_weight_bytes + m->plan.ring_bytes + m->plan.state_bytes +
+                              m->plan.scratch_bytes));
+  note_weights(m->ctx, -int64_t(m->plan.resident_weight_bytes));
+  delete m;
+}
+
+}  // namespace
+
+extern "C" int si_model_create_synthetic(si_ctx* ctx, const si_model_config* cfg, uint64_t seed,
+                                         si_model** out) {
+  if (!ctx || !cfg || !out) return fail(ctx, SI_E_INVALID, "invalid model arguments");
+  *out = nullptr;
+  const int n = ctx->nranks, r = ctx->rank;
+  if (int v = validate_config(*cfg, n))
+    return fail(ctx, SI_E_INVALID, "model config is invalid (check " + std::to_string(v) + ")");
+  cudaSetDevice(ctx->device);
+  auto* m = new si_model();
+  m->ctx = ctx;
+  m->c = *cfg;
+  m->seed = seed;
+  m->n = n;
+  m->r = r;
+  const si_model_config& c = m->c;
+  m->kh_l = c.gdn_key_heads / n;
+  m->vh_l = c.gdn_value_heads / n;
+  m->qh_l = c.attn_q_heads / n;
+  const uint32_t group = c.attn_q_heads / c.attn_kv_heads;
+  m->kv_lo = (uint32_t(r) * m->qh_l) / group;
+  m->kvh_l = ((uint32_t(r) + 1) * m->qh_l - 1) / group + 1 - m->kv_lo;
+  m->H_l = c.hidden / n;
+  m->I_l = c.intermediate / n;
+  m->V_l = c.vocab / n;
+
+  // ---- layout + pinned host weights -------------------------------------
+  m->layout.resize(c.layers + 1);
+  for (uint32_t l = 0; l <= c.layers; ++l) {
+    LayerLayout& L = m->layout[l];
+    const bool globals = l == c.layers;
+    L.gdn = !globals && ((l + 1) % c.attn_interval != 0);
+    full_spec(c, L.gdn, globals, &L);
+    shard_layer(*m, &L);
+  }
+  m->host.assign(c.layers + 1, nullptr);
+  for (uint32_t l = 0; l <= c.layers; ++l) {
+    cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&m->host[l]), m->layout[l].bytes, cudaHostAllocDefault);
+    if (e != cudaSuccess) {
+      int rc = cuda_fail(ctx, e, "pinned host allocation for model weights");
+      free_model(m);
+      return rc;
+    }
+  }
+  // token_embd shard: vocab rows [r*V/n, (r+1)*V/n), mapped for zero-copy row reads
+  LocalTensor embd;
+  embd.present = true;
+  embd.type = SI_GGML_TYPE_Q4_K;
+  embd.full_rows = c.vocab;
+  embd.cols = c.hidden;
+  embd.ranges = {{uint64_t(r) * c.vocab / n, uint64_t(r + 1) * c.vocab / n}};
+  embd.rows = m->V_l;
+  const uint64_t embd_bytes = embd.rows * row_bytes_of(embd.type, embd.cols);
+  {
+    cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&m->embd_host), embd_bytes + 64, cudaHostAllocMapped);
+    if (e == cudaSuccess) e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&m->embd_dev), m->embd_host, 0);
+    if (e != cudaSuccess) {
+      int rc = cuda_fail(ctx, e, "mapped host allocation for token embeddings");
+      free_model(m);
+      return rc;
+    }
+  }
+  // generate in parallel over (layer, tensor, row-chunk) work items
+  struct Work {
+    uint32_t layer, id;
+    uint64_t range_idx, row0, row1;
+    uint8_t* dst;
+  };
+  std::vector<Work> work;
+  auto add_work = [&](uint32_t layer, uint32_t id, const LocalTensor& t, uint8_t* base) {
+    const uint64_t rb = row_bytes_of(t.type, t.cols);
+    uint64_t local = 0;
+    for (uint64_t ri = 0; ri < t.ranges.size(); ++ri) {
+      const RowRange& rr = t.ranges[ri];
+      const uint64_t step = std::max<uint64_t>(1, (8ull << 20) / std::max<uint64_t>(rb, 1));
+      for (uint64_t a = rr.begin; a < rr.end; a += step) {
+        const uint64_t b = std::min(rr.end, a + step);
+        work.push_back({layer, id, ri, a, b, base + (local + (a - rr.begin)) * rb});
+      }
+      local += rr.end - rr.begin;
+    }
+  };
+  for (uint32_t l = 0; l <= c.layers; ++l)
+    for (int id = 0; id < SI_T_COUNT; ++id)
+      if (m->layout[l].t[id].present) add_work(l, uint32_t(id), m->layout[l].t[id], m->host[l] + m->layout[l].t[id].offset);
+  add_work(c.layers, SI_T_TOKEN_EMBD, embd, m->embd_host);
+  parallel_for(work.size(), [&](uint64_t k) {
+    const Work& w = work[k];
+    const LocalTensor& t = (w.id == SI_T_TOKEN_EMBD) ? embd : m->layout[w.layer].t[w.id];
+    LocalTensor part = t;
+    part.ranges = {{w.row0, w.row1}};
+    generate_tensor(seed, w.layer, w.id, part, w.dst);
+  });
+
+  // ---- residency plan (planner.rs:174-251 budget semantics) --------------
+  m->depth = ctx->cfg.stage_depth ? ctx->cfg.stage_depth : 3;
+  const uint64_t H = c.hidden;
+  const uint64_t proj_l = (2ull * m->kh_l + m->vh_l) * 128;
+  uint64_t state_bytes = 0;
+  for (uint32_t l = 0; l < c.layers; ++l) {
+    if (m->layout[l].gdn)
+      state_bytes += align256(2 * proj_l * (c.conv_kernel - 1) * 4) + align256(uint64_t(m->vh_l) * 128 * 128 * 4);
+    else
+      state_bytes += 2 * align256(uint64_t(m->kvh_l) * c.kv_capacity * c.attn_head_dim * 2);
+  }
+  const uint64_t qw = uint64_t(c.attn_q_heads) * c.attn_head_dim;
+  const uint64_t vw = uint64_t(c.gdn_value_heads) * 128;
+  const uint64_t part_floats = attn_scratch_floats(m->qh_l, c.attn_head_dim, c.kv_capacity + 1, 256);
+  const uint64_t scratch_floats[] = {H, H, proj_l, uint64_t(m->vh_l) * 128, 2ull * m->vh_l,
+                                     uint64_t(m->vh_l) * 128, vw, vw, 2ull * m->qh_l * c.attn_head_dim,
+                                     uint64_t(m->kvh_l) * c.attn_head_dim, uint64_t(m->kvh_l) * c.attn_head_dim,
+                                     uint64_t(m->qh_l) * c.attn_head_dim, qw, qw,
+                                     uint64_t(m->qh_l) * c.attn_head_dim, m->I_l, c.intermediate,
+                                     m->V_l, c.vocab, c.rotary_dim / 2 + 1, part_floats, H};
+  uint64_t scratch_bytes = 0;
+  for (uint64_t f : scratch_floats) scratch_bytes += align256(f * 4);
+  scratch_bytes += 4 * 256;  // token + keys
+  uint64_t max_layer = 0;
+  for (uint32_t l = 0; l < c.layers; ++l) max_layer = std::max(max_layer, m->layout[l].bytes);
+  const uint64_t budget = ctx->cfg.hbm_budget_bytes;
+  const uint64_t globals_bytes = m->layout[c.layers].bytes;
+  uint64_t resident = globals_bytes;
+  std::vector<bool> res(c.layers, false);
+  uint64_t all_layers = 0;
+  for (uint32_t l = 0; l < c.layers; ++l) all_layers += m->layout[l].bytes;
+  bool ring = false;
+  if (budget == 0 || globals_bytes + all_layers + state_bytes + scratch_bytes <= budget) {
+    std::fill(res.begin(), res.end(), true);
+    resident += all_layers;
+  } else {
+    ring = true;
+    const uint64_t fixed = globals_bytes + m->depth * max_layer + state_bytes + scratch_bytes;
+    if (fixed > budget) {
+      std::string msg = "HBM budget " + std::to_string(budget) + " B cannot hold the output head, " +
+                        std::to_string(m->depth) + " staging slots of " + std::to_string(max_layer) +
+                        " B, state and scratch (" + std::to_string(fixed) + " B)";
+      free_model(m);
+      return fail(ctx, SI_E_BUDGET, msg);
+    }
+    uint64_t left = budget - fixed;
+    for (uint32_t l = 0; l < c.layers; ++l) {  // retained prefix layers (qwen35_runtime.rs:1640-1642)
+      if (m->layout[l].bytes > left) break;
+      res[l] = true;
+      left -= m->layout[l].bytes;
+      resident += m->layout[l].bytes;
+    }
+  }
+  m->plan.budget_bytes = budget;
+  m->plan.resident_weight_bytes = resident;
+  m->plan.ring_bytes = ring ? m->depth * max_layer : 0;
+  m->plan.state_bytes = state_bytes;
+  m->plan.scratch_bytes = scratch_bytes;
+  m->plan.stage_depth = ring ? m->depth : 0;
+  m->plan.head_resident = 1;
+  for (uint32_t l = 0; l < c.layers; ++l) {
+    if (res[l]) m->plan.resident_layers++;
+    else {
+      m->plan.streamed_layers++;
+      m->plan.streamed_bytes_per_token += m->layout[l].bytes;
+      m->streamed.push_back(l);
+    }
+  }
+
+  // ---- device allocations -----------------------------------------------
+  auto dmalloc = [&](void** p, uint64_t bytes, const char* what) -> int {
+    cudaError_t e = cudaMalloc(p, bytes ? bytes : 256);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+    return SI_OK;
+  };
+  int rc = dmalloc(reinterpret_cast<void**>(&m->dev_resident), resident, "resident weight allocation");
+  if (rc) {
+    free_model(m);
+    return rc;
+  }
+  m->dev_layer.assign(c.layers + 1, nullptr);
+  {
+    uint64_t off = 0;
+    for (uint32_t l = 0; l <= c.layers; ++l) {
+      if (l < c.layers && !res[l]) continue;
+      m->dev_layer[l] = m->dev_resident + off;
+      cudaMemcpyAsync(m->dev_layer[l], m->host[l], m->layout[l].bytes, cudaMemcpyHostToDevice, ctx->copy_stream);
+      off += m->layout[l].bytes;
+    }
+  }
+  if (ring) {
+    for (uint32_t i = 0; i < m->depth; ++i) {
+      if ((rc = dmalloc(reinterpret_cast<void**>(&m->slot[i]), max_layer, "staging ring slot"))) {
+        free_model(m);
+        return rc;
+      }
+      cudaEventCreateWithFlags(&m->copy_done[i], cudaEventDisableTiming);
+      cudaEventCreateWithFlags(&m->compute_done[i], cudaEventDisableTiming);
+    }
+  }
+  if ((rc = dmalloc(reinterpret_cast<void**>(&m->state_block), state_bytes, "state allocation")) ||
+      (rc = dmalloc(reinterpret_cast<void**>(&m->scratch_block), scratch_bytes, "scratch allocation"))) {
+    free_model(m);
+    return rc;
+  }
+  cudaMemsetAsync(m->state_block, 0, state_bytes, ctx->copy_stream);
+  cudaMemsetAsync(m->scratch_block, 0, scratch_bytes, ctx->copy_stream);
+  {
+    uint8_t* p = m->state_block;
+    m->conv[0].assign(c.layers, nullptr);
+    m->conv[1].assign(c.layers, nullptr);
+    m->rec.assign(c.layers, nullptr);
+    m->kc.assign(c.layers, nullptr);
+    m->vc.assign(c.layers, nullptr);
+    m->cached.assign(c.layers, 0);
+    m->conv_parity.assign(c.layers, 0);
+    for (uint32_t l = 0; l < c.layers; ++l) {
+      if (m->layout[l].gdn) {
+        const uint64_t cs = proj_l * (c.conv_kernel - 1) * 4;
+        m->conv[0][l] = reinterpret_cast<float*>(p);
+        m->conv[1][l] = reinterpret_cast<float*>(p + cs);
+        p += align256(2 * cs);
+        m->rec[l] = reinterpret_cast<float*>(p);
+        p += align256(uint64_t(m->vh_l) * 128 * 128 * 4);
+      } else {
+        const uint64_t kvb = uint64_t(m->kvh_l) * c.kv_capacity * c.attn_head_dim * 2;
+        m->kc[l] = reinterpret_cast<uint16_t*>(p);
+        p += align256(kvb);
+        m->vc[l] = reinterpret_cast<uint16_t*>(p);
+        p += align256(kvb);
+      }
+    }
+    uint8_t* s = m->scratch_block;
+    float** dst[] = {&m->hidden, &m->slice, &m->qkv, &m->z, &m->ab, &m->core, &m->core_full, &m->z_full,
+                     &m->qg, &m->kk, &m->vv, &m->att, &m->att_full, &m->gate_full, &m->gate_l, &m->act,
+                     &m->act_full, &m->logits, &m->logits_full, &m->rope, &m->part, &m->embed};
+    for (size_t i = 0; i < sizeof(dst) / sizeof(dst[0]); ++i) {
+      *dst[i] = reinterpret_cast<float*>(s);
+      s += align256(scratch_floats[i] * 4);
+    }
+    m->d_token = reinterpret_cast<uint32_t*>(s);
+    m->d_key = reinterpret_cast<unsigned long long*>(s + 256);
+    m->d_keys = reinterpret_cast<unsigned long long*>(s + 512);
+  }
+  rope_freqs(c.rope_theta, c.rotary_dim, &m->rope_host);
+  if (!m->rope_host.empty())
+    cudaMemcpyAsync(m->rope, m->rope_host.data(), m->rope_host.size() * 4, cudaMemcpyHostToDevice, ctx->copy_stream);
+  cudaError_t e = cudaStreamSynchronize(ctx->copy_stream);
+  if (e != cudaSuccess) {
+    rc = cuda_fail(ctx, e, "model upload");
+    free_model(m);
+    return rc;
+  }
+  note_alloc(ctx, int64_t(resident + m->plan.ring_bytes + state_bytes + scratch_bytes));
+  note_weights(ctx, int64_t(resident));
+  *out = m;
+  return SI_OK;
+}
+
+extern "C" void si_model_destroy(si_model* m) { free_model(m); }
+
+extern "C" int si_model_plan(const si_model* m, si_plan_info* out) {
+  if (!m || !out) return SI_E_INVALID;
+  *out = m->plan;
+  return SI_OK;
+}
+
+extern "C" int si_model_host_tensor(const si_model* m, uint32_t layer, uint32_t tensor,
+                                    const void** ptr, uint64_t* bytes, uint32_t* type) {
+  if (!m || layer > m->c.layers || tensor >= SI_T_COUNT) return SI_E_INVALID;
+  if (tensor == SI_T_TOKEN_EMBD && layer == m->c.layers) {
+    if (ptr) *ptr = m->embd_host;
+    if (bytes) *bytes = uint64_t(m->V_l) * row_bytes_of(SI_GGML_TYPE_Q4_K, m->c.hidden);
+    if (type) *type = SI_GGML_TYPE_Q4_K;
+    return SI_OK;
+  }
+  const LocalTensor& t = m->layout[layer].t[tensor];
+  if (!t.present) {
+    if (ptr) *ptr = nullptr;
+    if (bytes) *bytes = 0;
+    if (type) *type = 0;
+    return SI_OK;
+  }
+  if (ptr) *ptr = m->host[layer] + t.offset;
+  if (bytes) *bytes = t.bytes;
+  if (type) *type = t.type;
+  return SI_OK;
+}
+
+extern "C" int si_model_reset(si_model* m) {
+  if (!m) return SI_E_INVALID;
+  cudaSetDevice(m->ctx->device);
+  cudaMemsetAsync(m->state_block, 0, m->plan.state_bytes, m->ctx->stream);
+  std::fill(m->cached.begin(), m->cached.end(), 0u);
+  std::fill(m->conv_parity.begin(), m->conv_parity.end(), 0u);
+  return sync_and_check(m->ctx, "model reset");
+}
+
+namespace {
+
+// ---- staging ring ------------------------------------------------------------
+// Occurrence j of the streamed-layer sequence (wrapping across tokens) uses
+// slot j % depth. Copies run on the context's copy stream: occurrence j+depth
+// is issued right after occurrence j's compute has been enqueued, gated by
+// that compute's completion event.
+void issue_copy(si_model* m, uint64_t occ) {
+  const uint32_t s = uint32_t(occ % m->depth);
+  const uint32_t l = m->streamed[occ % m->streamed.size()];
+  cudaStreamWaitEvent(m->ctx->copy_stream, m->compute_done[s], 0);
+  cudaMemcpyAsync(m->slot[s], m->host[l], m->layout[l].bytes, cudaMemcpyHostToDevice, m->ctx->copy_stream);
+  cudaEventRecord(m->copy_done[s], m->ctx->copy_stream);
+}
+
+void ring_prime(si_model* m) {
+  while (m->occ_issued < m->occ_next + m->depth) issue_copy(m, m->occ_issued++);
+}
+
+const uint8_t* tensor_ptr(const si_model* m, const uint8_t* base, uint32_t layer, int id) {
+  return base + m->layout[layer].t[id].offset;
+}
+
+QmvParams qmv_base(si_model* m, uint32_t type, uint32_t cols) {
+  QmvParams p = {};
+  p.type = type;
+  p.cols = cols;
+  p.nseg = 1;
+  p.err = m->ctx->d_err;
+  p.eps = m->c.rms_eps;
+  return p;
+}
+
+int run_qmv(si_model* m, const QmvParams& p) {
+  std::string msg;
+  int rc = launch_qmv(p, m->ctx->stream, m->ctx->sm_count, true, &msg);
+  return rc ? fail(m->ctx, rc, msg) : SI_OK;
+}
+
+// Row-sharded output with residual: rows [H_l*r, H_l*(r+1)) of hidden are
+// updated; with n > 1 they are written to `slice` and all-gathered.
+int residual_matvec(si_model* m, QmvParams p, const uint8_t* w) {
+  const uint32_t r0 = m->H_l * uint32_t(m->r);
+  p.seg[0] = {w, m->n > 1 ? m->slice : m->hidden + r0, m->hidden + r0, m->H_l, 0};
+  p.items = m->H_l;
+  int rc = run_qmv(m, p);
+  if (rc) return rc;
+  if (m->n > 1) return comm_allgather(m->ctx, m->slice, m->hidden, m->H_l, m->ctx->stream);
+  return SI_OK;
+}
+
+int mlp(si_model* m, uint32_t l, const uint8_t* base) {
+  const si_model_config& c = m->c;
+  QmvParams p = qmv_base(m, c.mlp_type, c.hidden);
+  p.nseg = 2;
+  p.pair = 1;
+  p.seg[0] = {tensor_ptr(m, base, l, SI_T_FFN_GATE), m->act, nullptr, m->I_l, 0};
+  p.seg[1] = {tensor_ptr(m, base, l, SI_T_FFN_UP), m->act, nullptr, m->I_l, 0};
+  p.items = m->I_l;
+  p.xmode = XM_RMS1P;
+  p.x = m->hidden;
+  p.xw = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_POST_NORM));
+  int rc = run_qmv(m, p);
+  if (rc) return rc;
+  const float* act = m->act;
+  if (m->n > 1) {
+    if ((rc = comm_allgather(m->ctx, m->act, m->act_full, m->I_l, m->ctx->stream))) return rc;
+    act = m->act_full;
+  }
+  QmvParams d = qmv_base(m, c.down_type, c.intermediate);
+  d.x = act;
+  d.xmode = XM_RAW;
+  return residual_matvec(m, d, tensor_ptr(m, base, l, SI_T_FFN_DOWN));
+}
+
+int gdn_layer(si_model* m, uint32_t l, const uint8_t* base) {
+  const si_model_config& c = m->c;
+  const uint32_t proj_l = (2 * m->kh_l + m->vh_l) * 128, vw_l = m->vh_l * 128;
+  const float* attn_norm = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_ATTN_NORM));
+  QmvParams p = qmv_base(m, SI_GGML_TYPE_Q4_K, c.hidden);
+  p.nseg = 2;
+  p.seg[0] = {tensor_ptr(m, base, l, SI_T_SSM_QKV), m->qkv, nullptr, proj_l, 0};
+  p.seg[1] = {tensor_ptr(m, base, l, SI_T_SSM_Z), m->z, nullptr, vw_l, 0};
+  p.items = proj_l + vw_l;
+  p.xmode = XM_RMS1P;
+  p.x = m->hidden;
+  p.xw = attn_norm;
+  int rc = run_qmv(m, p);
+  if (rc) return rc;
+  // alpha and beta (F32 rows, adjacent in the packed layer)
+  launch_f32_matvec_norm(reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_ALPHA)), m->vh_l,
+                         c.hidden, m->hidden, attn_norm, c.rms_eps, m->ab, m->ctx->stream);
+  launch_f32_matvec_norm(reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_BETA)), m->vh_l,
+                         c.hidden, m->hidden, attn_norm, c.rms_eps, m->ab + m->vh_l, m->ctx->stream);
+  GdnLayerArgs g = {};
+  g.qkv = m->qkv;
+  g.conv_w = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_CONV));
+  const uint32_t par = m->conv_parity[l];
+  g.conv_in = m->conv[par][l];
+  g.conv_out = m->conv[par ^ 1][l];
+  g.state = m->rec[l];
+  g.alpha = m->ab;
+  g.beta_logit = m->ab + m->vh_l;
+  g.a_log = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_A));
+  g.dt_bias = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_DT));
+  g.core = m->core;
+  g.key_heads = m->kh_l;
+  g.value_heads = m->vh_l;
+  g.kernel = c.conv_kernel;
+  launch_gdn_layer(g, m->ctx->stream, false);
+  m->conv_parity[l] = par ^ 1;
+  const float* core = m->core;
+  const float* z = m->z;
+  if (m->n > 1) {
+    if ((rc = comm_allgather(m->ctx, m->core, m->core_full, vw_l, m->ctx->stream)) ||
+        (rc = comm_allgather(m->ctx, m->z, m->z_full, vw_l, m->ctx->stream)))
+      return rc;
+    core = m->core_full;
+    z = m->z_full;
+  }
+  QmvParams o = qmv_base(m, SI_GGML_TYPE_Q4_K, c.gdn_value_heads * 128);
+  o.xmode = XM_GATED;
+  o.x = core;
+  o.xaux = z;
+  o.xw = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_NORM));
+  o.head_dim = 128;
+  return residual_matvec(m, o, tensor_ptr(m, base, l, SI_T_SSM_OUT));
+}
+
+int attn_layer(si_model* m, uint32_t l, const uint8_t* base, uint64_t position) {
+  const si_model_config& c = m->c;
+  const uint32_t hd = c.attn_head_dim, qw_l = m->qh_l * hd, kvw_l = m->kvh_l * hd;
+  if (m->cached[l] >= c.kv_capacity) return fail(m->ctx, SI_E_STATE, "full-attention KV cache capacity exhausted");
+  QmvParams p = qmv_base(m, SI_GGML_TYPE_Q4_K, c.hidden);
+  p.nseg = 3;
+  p.seg[0] = {tensor_ptr(m, base, l, SI_T_ATTN_Q), m->qg, nullptr, 2 * qw_l, 0};
+  p.seg[1] = {tensor_ptr(m, base, l, SI_T_ATTN_K), m->kk, nullptr, kvw_l, 0};
+  p.seg[2] = {tensor_ptr(m, base, l, SI_T_ATTN_V), m->vv, nullptr, kvw_l, 0};
+  p.items = 2 * qw_l + 2 * kvw_l;
+  p.xmode = XM_RMS1P;
+  p.x = m->hidden;
+  p.xw = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_ATTN_NORM));
+  int rc = run_qmv(m, p);
+  if (rc) return rc;
+  AttnArgs a = {};
+  a.q = m->qg;
+  a.k_new = m->kk;
+  a.v_new = m->vv;
+  a.k_cache = m->kc[l];
+  a.v_cache = m->vc[l];
+  a.k_cache_w = m->kc[l];
+  a.v_cache_w = m->vc[l];
+  a.q_norm = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_ATTN_QNORM));
+  a.k_norm = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_ATTN_KNORM));
+  a.rope_freq = c.rotary_dim ? m->rope : nullptr;
+  a.position = uint32_t(position);
+  a.cached = m->cached[l];
+  a.qh = m->qh_l;
+  a.kvh = m->kvh_l;
+  a.hd = hd;
+  a.cap = c.kv_capacity;
+  a.rotary = c.rotary_dim;
+  a.eps = c.rms_eps;
+  a.cache_bf16 = 1;
+  a.part = m->part;
+  a.out = m->att;
+  a.chunk = 256;
+  launch_attention(a, m->ctx->stream, true);
+  m->cached[l]++;
+  const float* att = m->att;
+  const float* gate = m->qg + qw_l;
+  if (m->n > 1) {
+    // gate half of the local q projection is contiguous after the queries
+    if ((rc = comm_allgather(m->ctx, m->att, m->att_full, qw_l, m->ctx->stream)) ||
+        (rc = comm_allgather(m->ctx, m->qg + qw_l, m->gate_full, qw_l, m->ctx->stream)))
+      return rc;
+    att = m->att_full;
+    gate = m->gate_full;
+  }
+  QmvParams o = qmv_base(m, SI_GGML_TYPE_Q4_K, c.attn_q_heads * hd);
+  o.xmode = XM_SIGGATE;
+  o.x = att;
+  o.xaux = gate;
+  return residual_matvec(m, o, tensor_ptr(m, base, l, SI_T_ATTN_O));
+}
+
+// decode_hidden on device buffers: m->hidden is updated in place.
+int decode_layers(si_model* m, uint64_t position) {
+  const si_model_config& c = m->c;
+  const bool ring = !m->streamed.empty();
+  if (ring) ring_prime(m);
+  for (uint32_t l = 0; l < c.layers; ++l) {
+    const uint8_t* base = m->dev_layer[l];
+    uint32_t s = 0;
+    if (!base) {
+      s = uint32_t(m->occ_next % m->depth);
+      cudaStreamWaitEvent(m->ctx->stream, m->copy_done[s], 0);
+      base = m->slot[s];
+    }
+    int rc = m->layout[l].gdn ? gdn_layer(m, l, base) : attn_layer(m, l, base, position);
+    if (!rc) rc = mlp(m, l, base);
+    if (rc) return rc;
+    if (!m->dev_layer[l]) {
+      cudaEventRecord(m->compute_done[s], m->ctx->stream);
+      m->occ_next++;
+      issue_copy(m, m->occ_issued++);
+    }
+  }
+  return SI_OK;
+}
+
+int embed_dev(si_model* m) {
+  const uint32_t lo = m->V_l * uint32_t(m->r);
+  launch_embed(m->embd_dev, m->c.hidden, m->d_token, lo, lo + m->V_l, m->hidden, m->ctx->stream);
+  if (m->n > 1) return comm_allreduce_sum(m->ctx, m->hidden, m->hidden, m->c.hidden, m->ctx->stream);
+  return SI_OK;
+}
+
+// logits slice + global argmax into d_token (and optionally full logits).
+int head_dev(si_model* m, bool gather_logits) {
+  const si_model_config& c = m->c;
+  const uint8_t* base = m->dev_layer[c.layers];
+  QmvParams p = qmv_base(m, c.head_type, c.hidden);
+  p.seg[0] = {tensor_ptr(m, base, c.layers, SI_T_OUTPUT), m->logits, nullptr, m->V_l, 0};
+  p.items = m->V_l;
+  p.xmode = XM_RMS1P;
+  p.x = m->hidden;
+  p.xw = reinterpret_cast<const float*>(tensor_ptr(m, base, c.layers, SI_T_OUTPUT_NORM));
+  int rc = run_qmv(m, p);
+  if (rc) return rc;
+  cudaMemsetAsync(m->d_key, 0, 8, m->ctx->stream);
+  launch_argmax_key(m->logits, m->V_l, m->V_l * uint32_t(m->r), m->d_key, m->ctx->stream);
+  if (m->n > 1) {
+    if ((rc = comm_allgather_u64(m->ctx, m->d_key, m->d_keys, m->ctx->stream))) return rc;
+    launch_argmax_finish(m->d_keys, uint32_t(m->n), m->d_token, m->ctx->stream);
+    if (gather_logits && (rc = comm_allgather(m->ctx, m->logits, m->logits_full, m->V_l, m->ctx->stream)))
+      return rc;
+  } else {
+    launch_argmax_finish(m->d_key, 1, m->d_token, m->ctx->stream);
+  }
+  return SI_OK;
+}
+
+int set_token(si_model* m, uint32_t token) {
+  if (token >= m->c.vocab) return fail(m->ctx, SI_E_INVALID, "Q4_K embedding token id or dimension is invalid");
+  cudaError_t e = cudaMemcpyAsync(m->d_token, &token, 4, cudaMemcpyHostToDevice, m->ctx->stream);
+  return e == cudaSuccess ? SI_OK : cuda_fail(m->ctx, e, "token upload");
+}
+
+}  // namespace
+
+extern "C" int si_model_embed(si_model* m, uint32_t token, float* hidden_out) {
+  if (!m || !hidden_out) return SI_E_INVALID;
+  cudaSetDevice(m->ctx->device);
+  int rc = set_token(m, token);
+  if (!rc) rc = embed_dev(m);
+  if (rc) return rc;
+  cudaMemcpyAsync(hidden_out, m->hidden, m->c.hidden * 4, cudaMemcpyDeviceToHost, m->ctx->stream);
+  return sync_and_check(m->ctx, "embedding command");
+}
+
+extern "C" int si_model_decode_hidden(si_model* m, uint64_t position, float* hidden) {
+  if (!m || !hidden) return SI_E_INVALID;
+  cudaSetDevice(m->ctx->device);
+  cudaMemcpyAsync(m->hidden, hidden, m->c.hidden * 4, cudaMemcpyHostToDevice, m->ctx->stream);
+  int rc = decode_layers(m, position);
+  if (rc) return rc;
+  cudaMemcpyAsync(hidden, m->hidden, m->c.hidden * 4, cudaMemcpyDeviceToHost, m->ctx->stream);
+  return sync_and_check(m->ctx, "decode_hidden");
+}
+
+extern "C" int si_model_logits(si_model* m, const float* hidden, float* logits) {
+  if (!m || !hidden || !logits) return SI_E_INVALID;
+  cudaSetDevice(m->ctx->device);
+  cudaMemcpyAsync(m->hidden, hidden, m->c.hidden * 4, cudaMemcpyHostToDevice, m->ctx->stream);
+  int rc = head_dev(m, true);
+  if (rc) return rc;
+  cudaMemcpyAsync(logits, m->n > 1 ? m->logits_full : m->logits, uint64_t(m->c.vocab) * 4, cudaMemcpyDeviceToHost,
+                  m->ctx->stream);
+  return sync_and_check(m->ctx, "logits");
+}
+
+extern "C" int si_model_decode_token(si_model* m, uint32_t token, uint64_t position, uint32_t* next,
+                                     float* logits) {
+  if (!m) return SI_E_INVALID;
+  cudaSetDevice(m->ctx->device);
+  int rc = set_token(m, token);
+  if (!rc) rc = embed_dev(m);
+  if (!rc) rc = decode_layers(m, position);
+  if (!rc) rc = head_dev(m, logits != nullptr);
+  if (rc) return rc;
+  uint32_t id = 0;
+  cudaMemcpyAsync(&id, m->d_token, 4, cudaMemcpyDeviceToHost, m->ctx->stream);
+  if (logits)
+    cudaMemcpyAsync(logits, m->n > 1 ? m->logits_full : m->logits, uint64_t(m->c.vocab) * 4,
+                    cudaMemcpyDeviceToHost, m->ctx->stream);
+  if ((rc = sync_and_check(m->ctx, "decode_token"))) return rc;
+  if (id == 0xffffffffu) return fail(m->ctx, SI_E_INVALID, "logits contain no finite values");
+  if (next) *next = id;
+  return SI_OK;
+}
+
+extern "C" int si_model_generate(si_model* m, const uint32_t* prompt, uint64_t n_prompt,
+                                 uint64_t max_new, uint32_t* out_ids, uint64_t* n_out) {
+  if (!m || (!prompt && n_prompt) || (!out_ids && max_new) || !n_out) return SI_E_INVALID;
+  if (n_prompt == 0) return fail(m->ctx, SI_E_INVALID, "prompt must contain at least one token");
+  cudaSetDevice(m->ctx->device);
+  *n_out = 0;
+  int rc;
+  // prefill, token by token (runtime.rs:3571-3576)
+  for (uint64_t p = 0; p < n_prompt; ++p) {
+    if ((rc = set_token(m, prompt[p])) || (rc = embed_dev(m)) || (rc = decode_layers(m, p))) return rc;
+  }
+  if ((rc = head_dev(m, false))) return rc;
+  // greedy loop (runtime.rs:3588-3600)
+  for (uint64_t i = 0; i < max_new; ++i) {
+    uint32_t id = 0;
+    cudaMemcpyAsync(&id, m->d_token, 4, cudaMemcpyDeviceToHost, m->ctx->stream);
+    if ((rc = sync_and_check(m->ctx, "generation step"))) return rc;
+    if (id == 0xffffffffu) return fail(m->ctx, SI_E_INVALID, "logits contain no finite values");
+    out_ids[i] = id;
+    *n_out = i + 1;
+    if (id == m->c.eos_token) break;
+    // the token id is already in d_token: embed it directly on the device
+    if ((rc = embed_dev(m)) || (rc = decode_layers(m, n_prompt + i)) || (rc = head_dev(m, false))) return rc;
+  }
+  return sync_and_check(m->ctx, "generation");
+}

@@ -1,0 +1,48 @@
+// Host-visible description of one launch of the K-quant matvec family.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string>
+
+namespace si {
+
+// How the input vector is formed in shared memory before the dot products.
+enum XMode : int {
+  XM_RAW = 0,      // x
+  XM_RMS1P = 1,    // x * rsqrt(mean(x^2) + eps) * (1 + w)    (qwen35.rs:53-86, heads = 1)
+  XM_GATED = 2,    // per head: c * rsqrt(mean(c^2) + eps) * w[d] * SiLU(z)  (qwen35.rs:14-49)
+  XM_SIGGATE = 3,  // a / (1 + exp(-gate))                       (qwen35_runtime.rs:861-865)
+};
+
+struct QmvSeg {
+  const uint8_t* w;     // row-major super-blocks of this segment
+  float* y;             // output rows
+  const float* resid;   // optional residual added in the epilogue (may alias y)
+  uint32_t rows;
+  uint32_t pad;
+};
+
+struct QmvParams {
+  uint32_t type;        // SI_GGML_TYPE_Q4_K / Q5_K / Q6_K
+  uint32_t cols;        // multiple of 256
+  uint32_t nseg;        // 1..4 segments sharing x (grouped matvec)
+  uint32_t pair;        // 1: SwiGLU, seg[0] = gate, seg[1] = up, out = seg[0].y
+  QmvSeg seg[4];
+  uint32_t items;       // output rows in total (pair: rows of the gate)
+  int xmode;
+  const float* x;       // input vector [cols]
+  const float* xw;      // norm weight (XM_RMS1P: [cols], XM_GATED: [head_dim])
+  const float* xaux;    // XM_GATED: z [cols]; XM_SIGGATE: gate [cols]
+  float eps;
+  uint32_t head_dim;    // XM_GATED
+  int* err;             // device error word
+};
+
+// Enqueue one launch. Returns SI_OK or SI_E_* with *msg filled.
+int launch_qmv(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
+               std::string* msg);
+
+// Largest supported column count (x and its partial sums live in shared memory).
+constexpr uint32_t kQmvMaxCols = 32768;
+
+}  // namespace si

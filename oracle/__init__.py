@@ -168,3 +168,54 @@ def f32_to_bf16(a: np.ndarray) -> np.ndarray:
     u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
     r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
     return r
+
+
+class OracleModel:
+    """The oracle's 64-layer (or smaller) decoder over the host tensors of a
+    backend `Model` (its pinned host copy, rank 0 of 1)."""
+
+    def __init__(self, config, host_tensor, threads: int = 0):
+        """config: a ctypes si_model_config; host_tensor(layer, id) -> (addr, bytes, type)."""
+        L = lib()
+        n = (config.layers + 1) * 23
+        ptrs = (C.c_void_p * n)()
+        types = (C.c_uint32 * n)()
+        for layer in range(config.layers + 1):
+            for tid in range(23):
+                addr, _, ty = host_tensor(layer, tid)
+                ptrs[layer * 23 + tid] = addr
+                types[layer * 23 + tid] = ty
+        self._cfg = config
+        self.h = L.or_model_create(C.byref(config), ptrs, types, threads)
+
+    def close(self):
+        if self.h:
+            lib().or_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def embed(self, token):
+        out = np.empty(self._cfg.hidden, np.float32)
+        _check(lib().or_model_embed(self.h, token, out), "embed")
+        return out
+
+    def decode_hidden(self, position, hidden):
+        h = np.array(hidden, np.float32, copy=True)
+        _check(lib().or_model_decode_hidden(self.h, position, h), "decode_hidden")
+        return h
+
+    def logits(self, hidden):
+        out = np.empty(self._cfg.vocab, np.float32)
+        _check(lib().or_model_logits(self.h, np.ascontiguousarray(hidden, np.float32), out), "logits")
+        return out
+
+    def generate(self, prompt, max_new):
+        p = np.ascontiguousarray(prompt, np.uint32)
+        out = np.zeros(max(max_new, 1), np.uint32)
+        n = lib().or_model_generate(self.h, p.ctypes.data_as(C.c_void_p), p.size, max_new,
+                                    out.ctypes.data_as(C.c_void_p))
+        if n < 0:
+            raise OracleError(f"generate failed with {n}")
+        return out[:n].tolist()

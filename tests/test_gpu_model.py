@@ -1,0 +1,86 @@
+"""End-to-end synthetic decode on the GPU against the oracle: greedy token
+IDs must be identical; hidden states and logits within 1e-5 relative L2."""
+import numpy as np
+import pytest
+
+import oracle as O
+from helpers import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def small_config(mai, **kw):
+    base = dict(hidden=512, intermediate=1024, layers=8, vocab=4096, attn_q_heads=4, attn_kv_heads=2,
+                attn_head_dim=128, rotary_dim=32, gdn_key_heads=2, gdn_value_heads=4, kv_capacity=40)
+    base.update(kw)
+    return mai.qwen36_27b_config(**base)
+
+
+@pytest.fixture(scope="module")
+def small_model(mai, ctx):
+    m = mai.Model(ctx, small_config(mai), seed=1234)
+    yield m
+    m.close()
+
+
+def test_plan_fully_resident_without_budget(small_model):
+    p = small_model.plan()
+    assert p["streamed_layers"] == 0 and p["resident_layers"] == 8 and p["ring_bytes"] == 0
+
+
+def test_layer_states_and_hidden_match_oracle(mai, small_model):
+    m = small_model
+    m.reset()
+    orc = O.OracleModel(m.config, m.host_tensor)
+    for pos, tok in enumerate([17, 4095, 0, 2048, 99]):
+        e1, e2 = m.embed_token(tok), orc.embed(tok)
+        assert np.array_equal(e1, e2)  # bit-exact Q4_K row dequant
+        h1 = m.decode_hidden(pos, e1)
+        h2 = orc.decode_hidden(pos, e2)
+        assert rel_l2(h1, h2) < 1e-5, pos
+        l1, l2 = m.logits(h1), orc.logits(h2)
+        assert rel_l2(l1, l2) < 1e-5
+    orc.close()
+
+
+def test_greedy_ids_identical_to_oracle(mai, small_model):
+    m = small_model
+    m.reset()
+    orc = O.OracleModel(m.config, m.host_tensor)
+    prompt = [3, 141, 59, 2653]
+    ids_gpu = m.generate(prompt, 24)
+    ids_cpu = orc.generate(prompt, 24)
+    orc.close()
+    assert ids_gpu == ids_cpu
+    assert len(ids_gpu) == 24
+
+
+def test_streamed_layers_give_identical_ids(mai, ctx, small_model):
+    """A budget below the model size forces the depth-3 staging ring."""
+    full = small_model.plan()
+    total = full["resident_weight_bytes"] + full["state_bytes"] + full["scratch_bytes"]
+    c2 = mai.CudaContext(0, hbm_budget_bytes=int(total * 0.75), stage_depth=3)
+    m2 = mai.Model(c2, small_config(mai), seed=1234)
+    p = m2.plan()
+    assert p["streamed_layers"] > 0 and p["stage_depth"] == 3
+    small_model.reset()
+    prompt = [3, 141, 59, 2653]
+    assert m2.generate(prompt, 16) == small_model.generate(prompt, 16)
+    m2.close()
+    c2.close()
+
+
+def test_budget_too_small_is_rejected(mai):
+    import mai_b200 as M
+    c2 = mai.CudaContext(0, hbm_budget_bytes=1 << 20)
+    with pytest.raises(M.SiError, match="HBM budget"):
+        mai.Model(c2, small_config(mai), seed=1)
+    c2.close()
+
+
+def test_kv_capacity_exhaustion_is_an_error(mai, ctx):
+    import mai_b200 as M
+    m = mai.Model(ctx, small_config(mai, kv_capacity=3), seed=5)
+    with pytest.raises(M.SiError, match="capacity"):
+        m.generate([1, 2], 8)
+    m.close()
