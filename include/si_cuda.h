@@ -234,7 +234,17 @@ int si_model_create_synthetic(si_ctx* ctx, const si_model_config* c, uint64_t se
                               si_model** out);
 void si_model_destroy(si_model* m);
 int si_model_plan(const si_model* m, si_plan_info* out);
-/* Host copy of one tensor (the full, unsharded tensor on every rank). */
+/* The same residency plan without a device or any allocation (planner dry
+ * run, plan_sequential_layers' budget check, planner.rs:174-251). */
+int si_model_plan_dry(const si_model_config* c, int nranks, int rank, uint64_t budget,
+                      uint32_t stage_depth, si_plan_info* out);
+/* Full-tensor row ranges [begin, end) that rank `rank` of `nranks` holds of a
+ * tensor (ranges: 2*max_ranges u64). No device needed. */
+int si_model_shard_rows(const si_model_config* c, int nranks, int rank, uint32_t layer,
+                        uint32_t tensor, uint64_t* ranges, uint32_t max_ranges,
+                        uint32_t* n_ranges);
+/* This rank's pinned host copy of one tensor (its shard; with one rank, the
+ * full tensor). */
 int si_model_host_tensor(const si_model* m, uint32_t layer, uint32_t tensor, const void** ptr,
                          uint64_t* bytes, uint32_t* ggml_type);
 int si_model_reset(si_model* m);                     /* Qwen35Runtime::reset */

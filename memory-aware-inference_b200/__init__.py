@@ -134,6 +134,8 @@ def lib():
         "si_model_create_synthetic": ([vp, vp, u64, vp], i32),
         "si_model_destroy": ([vp], None),
         "si_model_plan": ([vp, vp], i32),
+        "si_model_plan_dry": ([vp, i32, i32, u64, u32, vp], i32),
+        "si_model_shard_rows": ([vp, i32, i32, u32, u32, vp, u32, vp], i32),
         "si_model_host_tensor": ([vp, u32, u32, vp, vp, vp], i32),
         "si_model_reset": ([vp], i32),
         "si_model_embed": ([vp, u32, vp], i32),
@@ -451,6 +453,25 @@ def qwen36_27b_config(**overrides) -> SiModelConfig:
     for k, v in overrides.items():
         setattr(c, k, v)
     return c
+
+
+def plan_dry(config: SiModelConfig, nranks: int = 1, rank: int = 0, budget: int = 0, stage_depth: int = 3) -> dict:
+    """Residency plan of a model without a device (si_model_plan_dry)."""
+    p = SiPlanInfo()
+    rc = lib().si_model_plan_dry(C.byref(config), nranks, rank, budget, stage_depth, C.byref(p))
+    if rc != 0:
+        raise SiError(rc, lib().si_global_last_error().decode())
+    return p.as_dict()
+
+
+def shard_rows(config: SiModelConfig, nranks: int, rank: int, layer: int, tensor: int):
+    """Full-tensor row ranges held by `rank` (si_model_shard_rows)."""
+    buf = (C.c_uint64 * 16)()
+    n = C.c_uint32()
+    rc = lib().si_model_shard_rows(C.byref(config), nranks, rank, layer, tensor, buf, 8, C.byref(n))
+    if rc != 0:
+        raise SiError(rc, lib().si_global_last_error().decode())
+    return [(buf[2 * i], buf[2 * i + 1]) for i in range(n.value)]
 
 
 class Model:

@@ -87,6 +87,7 @@ struct si_model {
   uint32_t* d_token;
   unsigned long long *d_key, *d_keys;
   std::vector<float> rope_host;
+  bool accounted = false;  // device bytes recorded in the context telemetry
 };
 
 namespace {
@@ -248,6 +249,116 @@ int validate_config(const si_model_config& c, int n) {
   return 0;
 }
 
+
+// Shard dimensions and the packed per-layer layout of rank r of n (no CUDA).
+void init_shape(si_model* m) {
+  const si_model_config& c = m->c;
+  const int n = m->n, r = m->r;
+  m->kh_l = c.gdn_key_heads / n;
+  m->vh_l = c.gdn_value_heads / n;
+  m->qh_l = c.attn_q_heads / n;
+  const uint32_t group = c.attn_q_heads / c.attn_kv_heads;
+  m->kv_lo = (uint32_t(r) * m->qh_l) / group;
+  m->kvh_l = ((uint32_t(r) + 1) * m->qh_l - 1) / group + 1 - m->kv_lo;
+  m->H_l = c.hidden / n;
+  m->I_l = c.intermediate / n;
+  m->V_l = c.vocab / n;
+
+  // ---- layout + pinned host weights -------------------------------------
+  m->layout.resize(c.layers + 1);
+  for (uint32_t l = 0; l <= c.layers; ++l) {
+    LayerLayout& L = m->layout[l];
+    const bool globals = l == c.layers;
+    L.gdn = !globals && ((l + 1) % c.attn_interval != 0);
+    full_spec(c, L.gdn, globals, &L);
+    shard_layer(*m, &L);
+  }
+}
+
+// Device scratch vectors of the decode loop, in float counts.
+std::vector<uint64_t> scratch_float_counts(const si_model& m) {
+  const si_model_config& c = m.c;
+  const uint64_t H = c.hidden, proj_l = (2ull * m.kh_l + m.vh_l) * 128;
+  const uint64_t qw = uint64_t(c.attn_q_heads) * c.attn_head_dim, vw = uint64_t(c.gdn_value_heads) * 128;
+  const uint64_t part_floats = attn_scratch_floats(m.qh_l, c.attn_head_dim, c.kv_capacity + 1, 256);
+  return {H, H, proj_l, uint64_t(m.vh_l) * 128, 2ull * m.vh_l, uint64_t(m.vh_l) * 128, vw, vw,
+          2ull * m.qh_l * c.attn_head_dim, uint64_t(m.kvh_l) * c.attn_head_dim,
+          uint64_t(m.kvh_l) * c.attn_head_dim, uint64_t(m.qh_l) * c.attn_head_dim, qw, qw,
+          uint64_t(m.qh_l) * c.attn_head_dim, m.I_l, c.intermediate, m.V_l, c.vocab,
+          c.rotary_dim / 2 + 1, part_floats, H};
+}
+
+// Residency plan inside `budget` (0 = unbounded): the output head and as many
+// leading layers as fit stay resident (the reference's retained prefix,
+// qwen35_runtime.rs:1640-1642); the rest stream through `depth` ring slots of
+// the largest layer. Like plan_sequential_layers (planner.rs:174-251) a plan
+// whose fixed part exceeds the budget is rejected. Pure host code.
+int compute_plan(si_model* m, uint64_t budget, uint32_t depth, std::vector<bool>* res_out,
+                 uint64_t* max_layer_out, std::string* err) {
+  const si_model_config& c = m->c;
+  m->depth = depth ? std::min(depth, 4u) : 3u;
+  const uint64_t proj_l = (2ull * m->kh_l + m->vh_l) * 128;
+  uint64_t state_bytes = 0;
+  for (uint32_t l = 0; l < c.layers; ++l) {
+    if (m->layout[l].gdn)
+      state_bytes += align256(2 * proj_l * (c.conv_kernel - 1) * 4) + align256(uint64_t(m->vh_l) * 128 * 128 * 4);
+    else
+      state_bytes += 2 * align256(uint64_t(m->kvh_l) * c.kv_capacity * c.attn_head_dim * 2);
+  }
+  uint64_t scratch_bytes = 4 * 256;  // token + argmax keys
+  for (uint64_t f : scratch_float_counts(*m)) scratch_bytes += align256(f * 4);
+  uint64_t max_layer = 0, all_layers = 0;
+  for (uint32_t l = 0; l < c.layers; ++l) {
+    max_layer = std::max(max_layer, m->layout[l].bytes);
+    all_layers += m->layout[l].bytes;
+  }
+  const uint64_t globals_bytes = m->layout[c.layers].bytes;
+  uint64_t resident = globals_bytes;
+  std::vector<bool> res(c.layers, false);
+  bool ring = false;
+  if (budget == 0 || globals_bytes + all_layers + state_bytes + scratch_bytes <= budget) {
+    std::fill(res.begin(), res.end(), true);
+    resident += all_layers;
+  } else {
+    ring = true;
+    const uint64_t fixed = globals_bytes + m->depth * max_layer + state_bytes + scratch_bytes;
+    if (fixed > budget) {
+      *err = "HBM budget " + std::to_string(budget) + " B cannot hold the output head, " +
+             std::to_string(m->depth) + " staging slots of " + std::to_string(max_layer) +
+             " B, state and scratch (" + std::to_string(fixed) + " B)";
+      return SI_E_BUDGET;
+    }
+    uint64_t left = budget - fixed;
+    for (uint32_t l = 0; l < c.layers; ++l) {
+      if (m->layout[l].bytes > left) break;
+      res[l] = true;
+      left -= m->layout[l].bytes;
+      resident += m->layout[l].bytes;
+    }
+  }
+  m->plan = si_plan_info{};
+  m->plan.budget_bytes = budget;
+  m->plan.resident_weight_bytes = resident;
+  m->plan.ring_bytes = ring ? m->depth * max_layer : 0;
+  m->plan.state_bytes = state_bytes;
+  m->plan.scratch_bytes = scratch_bytes;
+  m->plan.stage_depth = ring ? m->depth : 0;
+  m->plan.head_resident = 1;
+  m->streamed.clear();
+  for (uint32_t l = 0; l < c.layers; ++l) {
+    if (res[l]) {
+      m->plan.resident_layers++;
+    } else {
+      m->plan.streamed_layers++;
+      m->plan.streamed_bytes_per_token += m->layout[l].bytes;
+      m->streamed.push_back(l);
+    }
+  }
+  *res_out = res;
+  *max_layer_out = max_layer;
+  return SI_OK;
+}
+
 }  // namespace
 
 extern "C" void si_model_config_qwen36_27b(si_model_config* c) {
@@ -292,9 +403,11 @@ void free_model(si_model* m) {
   }
   if (m->state_block) cudaFree(m->state_block);
   if (m->scratch_block) cudaFree(m->scratch_block);
-  note_alloc(m->ctx, -int64_t(m->plan.resident_weight_bytes + m->plan.ring_bytes + m->plan.state_bytes +
-                              m->plan.scratch_bytes));
-  note_weights(m->ctx, -int64_t(m->plan.resident_weight_bytes));
+  if (m->accounted) {
+    note_alloc(m->ctx, -int64_t(m->plan.resident_weight_bytes + m->plan.ring_bytes + m->plan.state_bytes +
+                                m->plan.scratch_bytes));
+    note_weights(m->ctx, -int64_t(m->plan.resident_weight_bytes));
+  }
   delete m;
 }
 
@@ -315,25 +428,22 @@ extern "C" int si_model_create_synthetic(si_ctx* ctx, const si_model_config* cfg
   m->n = n;
   m->r = r;
   const si_model_config& c = m->c;
-  m->kh_l = c.gdn_key_heads / n;
-  m->vh_l = c.gdn_value_heads / n;
-  m->qh_l = c.attn_q_heads / n;
-  const uint32_t group = c.attn_q_heads / c.attn_kv_heads;
-  m->kv_lo = (uint32_t(r) * m->qh_l) / group;
-  m->kvh_l = ((uint32_t(r) + 1) * m->qh_l - 1) / group + 1 - m->kv_lo;
-  m->H_l = c.hidden / n;
-  m->I_l = c.intermediate / n;
-  m->V_l = c.vocab / n;
-
-  // ---- layout + pinned host weights -------------------------------------
-  m->layout.resize(c.layers + 1);
-  for (uint32_t l = 0; l <= c.layers; ++l) {
-    LayerLayout& L = m->layout[l];
-    const bool globals = l == c.layers;
-    L.gdn = !globals && ((l + 1) % c.attn_interval != 0);
-    full_spec(c, L.gdn, globals, &L);
-    shard_layer(*m, &L);
+  init_shape(m);
+  // ---- residency plan, before any allocation -----------------------------
+  std::vector<bool> res;
+  uint64_t max_layer = 0;
+  {
+    std::string perr;
+    if (int prc = compute_plan(m, ctx->cfg.hbm_budget_bytes, ctx->cfg.stage_depth, &res, &max_layer, &perr)) {
+      free_model(m);
+      return fail(ctx, prc, perr);
+    }
   }
+  const uint64_t resident = m->plan.resident_weight_bytes, state_bytes = m->plan.state_bytes,
+                 scratch_bytes = m->plan.scratch_bytes;
+  const bool ring = !m->streamed.empty();
+  const std::vector<uint64_t> scratch_floats = scratch_float_counts(*m);
+  const uint64_t proj_l = (2ull * m->kh_l + m->vh_l) * 128;
   m->host.assign(c.layers + 1, nullptr);
   for (uint32_t l = 0; l <= c.layers; ++l) {
     cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&m->host[l]), m->layout[l].bytes, cudaHostAllocDefault);
@@ -392,75 +502,6 @@ extern "C" int si_model_create_synthetic(si_ctx* ctx, const si_model_config* cfg
     part.ranges = {{w.row0, w.row1}};
     generate_tensor(seed, w.layer, w.id, part, w.dst);
   });
-
-  // ---- residency plan (planner.rs:174-251 budget semantics) --------------
-  m->depth = ctx->cfg.stage_depth ? ctx->cfg.stage_depth : 3;
-  const uint64_t H = c.hidden;
-  const uint64_t proj_l = (2ull * m->kh_l + m->vh_l) * 128;
-  uint64_t state_bytes = 0;
-  for (uint32_t l = 0; l < c.layers; ++l) {
-    if (m->layout[l].gdn)
-      state_bytes += align256(2 * proj_l * (c.conv_kernel - 1) * 4) + align256(uint64_t(m->vh_l) * 128 * 128 * 4);
-    else
-      state_bytes += 2 * align256(uint64_t(m->kvh_l) * c.kv_capacity * c.attn_head_dim * 2);
-  }
-  const uint64_t qw = uint64_t(c.attn_q_heads) * c.attn_head_dim;
-  const uint64_t vw = uint64_t(c.gdn_value_heads) * 128;
-  const uint64_t part_floats = attn_scratch_floats(m->qh_l, c.attn_head_dim, c.kv_capacity + 1, 256);
-  const uint64_t scratch_floats[] = {H, H, proj_l, uint64_t(m->vh_l) * 128, 2ull * m->vh_l,
-                                     uint64_t(m->vh_l) * 128, vw, vw, 2ull * m->qh_l * c.attn_head_dim,
-                                     uint64_t(m->kvh_l) * c.attn_head_dim, uint64_t(m->kvh_l) * c.attn_head_dim,
-                                     uint64_t(m->qh_l) * c.attn_head_dim, qw, qw,
-                                     uint64_t(m->qh_l) * c.attn_head_dim, m->I_l, c.intermediate,
-                                     m->V_l, c.vocab, c.rotary_dim / 2 + 1, part_floats, H};
-  uint64_t scratch_bytes = 0;
-  for (uint64_t f : scratch_floats) scratch_bytes += align256(f * 4);
-  scratch_bytes += 4 * 256;  // token + keys
-  uint64_t max_layer = 0;
-  for (uint32_t l = 0; l < c.layers; ++l) max_layer = std::max(max_layer, m->layout[l].bytes);
-  const uint64_t budget = ctx->cfg.hbm_budget_bytes;
-  const uint64_t globals_bytes = m->layout[c.layers].bytes;
-  uint64_t resident = globals_bytes;
-  std::vector<bool> res(c.layers, false);
-  uint64_t all_layers = 0;
-  for (uint32_t l = 0; l < c.layers; ++l) all_layers += m->layout[l].bytes;
-  bool ring = false;
-  if (budget == 0 || globals_bytes + all_layers + state_bytes + scratch_bytes <= budget) {
-    std::fill(res.begin(), res.end(), true);
-    resident += all_layers;
-  } else {
-    ring = true;
-    const uint64_t fixed = globals_bytes + m->depth * max_layer + state_bytes + scratch_bytes;
-    if (fixed > budget) {
-      std::string msg = "HBM budget " + std::to_string(budget) + " B cannot hold the output head, " +
-                        std::to_string(m->depth) + " staging slots of " + std::to_string(max_layer) +
-                        " B, state and scratch (" + std::to_string(fixed) + " B)";
-      free_model(m);
-      return fail(ctx, SI_E_BUDGET, msg);
-    }
-    uint64_t left = budget - fixed;
-    for (uint32_t l = 0; l < c.layers; ++l) {  // retained prefix layers (qwen35_runtime.rs:1640-1642)
-      if (m->layout[l].bytes > left) break;
-      res[l] = true;
-      left -= m->layout[l].bytes;
-      resident += m->layout[l].bytes;
-    }
-  }
-  m->plan.budget_bytes = budget;
-  m->plan.resident_weight_bytes = resident;
-  m->plan.ring_bytes = ring ? m->depth * max_layer : 0;
-  m->plan.state_bytes = state_bytes;
-  m->plan.scratch_bytes = scratch_bytes;
-  m->plan.stage_depth = ring ? m->depth : 0;
-  m->plan.head_resident = 1;
-  for (uint32_t l = 0; l < c.layers; ++l) {
-    if (res[l]) m->plan.resident_layers++;
-    else {
-      m->plan.streamed_layers++;
-      m->plan.streamed_bytes_per_token += m->layout[l].bytes;
-      m->streamed.push_back(l);
-    }
-  }
 
   // ---- device allocations -----------------------------------------------
   auto dmalloc = [&](void** p, uint64_t bytes, const char* what) -> int {
@@ -548,11 +589,64 @@ extern "C" int si_model_create_synthetic(si_ctx* ctx, const si_model_config* cfg
   }
   note_alloc(ctx, int64_t(resident + m->plan.ring_bytes + state_bytes + scratch_bytes));
   note_weights(ctx, int64_t(resident));
+  m->accounted = true;
   *out = m;
   return SI_OK;
 }
 
 extern "C" void si_model_destroy(si_model* m) { free_model(m); }
+
+extern "C" int si_model_plan_dry(const si_model_config* cfg, int nranks, int rank, uint64_t budget,
+                                 uint32_t depth, si_plan_info* out) {
+  if (!cfg || !out || nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(nullptr, SI_E_INVALID, "invalid plan arguments");
+  if (int v = validate_config(*cfg, nranks))
+    return fail(nullptr, SI_E_INVALID, "model config is invalid (check " + std::to_string(v) + ")");
+  si_model m;
+  m.c = *cfg;
+  m.n = nranks;
+  m.r = rank;
+  init_shape(&m);
+  std::vector<bool> res;
+  uint64_t max_layer = 0;
+  std::string err;
+  if (int rc = compute_plan(&m, budget, depth, &res, &max_layer, &err)) return fail(nullptr, rc, err);
+  *out = m.plan;
+  return SI_OK;
+}
+
+extern "C" int si_model_shard_rows(const si_model_config* cfg, int nranks, int rank, uint32_t layer,
+                                   uint32_t tensor, uint64_t* ranges, uint32_t max_ranges,
+                                   uint32_t* n_ranges) {
+  if (!cfg || !n_ranges || nranks < 1 || rank < 0 || rank >= nranks || layer > cfg->layers ||
+      tensor >= SI_T_COUNT)
+    return fail(nullptr, SI_E_INVALID, "invalid shard query");
+  if (int v = validate_config(*cfg, nranks))
+    return fail(nullptr, SI_E_INVALID, "model config is invalid (check " + std::to_string(v) + ")");
+  si_model m;
+  m.c = *cfg;
+  m.n = nranks;
+  m.r = rank;
+  init_shape(&m);
+  *n_ranges = 0;
+  if (tensor == SI_T_TOKEN_EMBD) {
+    if (layer != cfg->layers) return SI_OK;
+    if (max_ranges < 1) return fail(nullptr, SI_E_INVALID, "range buffer too small");
+    ranges[0] = uint64_t(rank) * cfg->vocab / nranks;
+    ranges[1] = uint64_t(rank + 1) * cfg->vocab / nranks;
+    *n_ranges = 1;
+    return SI_OK;
+  }
+  const LocalTensor& t = m.layout[layer].t[tensor];
+  if (!t.present) return SI_OK;
+  if (t.ranges.size() > max_ranges) return fail(nullptr, SI_E_INVALID, "range buffer too small");
+  for (size_t i = 0; i < t.ranges.size(); ++i) {
+    ranges[2 * i] = t.ranges[i].begin;
+    ranges[2 * i + 1] = t.ranges[i].end;
+  }
+  *n_ranges = uint32_t(t.ranges.size());
+  return SI_OK;
+}
 
 extern "C" int si_model_plan(const si_model* m, si_plan_info* out) {
   if (!m || !out) return SI_E_INVALID;

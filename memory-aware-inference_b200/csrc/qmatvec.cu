@@ -5,18 +5,20 @@
 // (src/metal.rs:310-494, 498-587, 770-1050, 4532-4780 in the reference).
 //
 // Design (one CTA per SM, persistent over a contiguous range of rows):
-//  * A producer warp streams whole rows (2,880 B for a Q4_K 5120-column row)
-//    from HBM into a ring of shared-memory slots with non-tensor bulk async
-//    copies (cp.async.bulk, L2 evict_first), tracked by full/empty mbarriers.
-//  * 16 consumer warps = 32 teams of 16 lanes; a team owns one row at a time.
+//  * A producer warp streams rows in pieces of <= ~4.5 KB (a whole 2,880 B
+//    Q4_K 5120-column row is one piece) from HBM into shared-memory slots with
+//    non-tensor bulk async copies (cp.async.bulk, L2 evict_first), tracked by
+//    full/empty mbarriers. Each team owns >= 2 private slots (double
+//    buffering), so barrier phases never alias.
+//  * 16 consumer warps = up to 32 teams of 16 lanes; a team owns one row.
 //    Lane l of a team always decodes the same 64-element unit of each
 //    super-block (Q4_K/Q5_K: group l%4; Q6_K: half/16-run l%4), so the 6-bit
 //    scale/min extraction pattern is fixed per lane and never diverges.
-//  * Weights are decoded in registers: each 4/5/6-bit quant q becomes the
-//    float 1 + q/2^k by placing its bits in the mantissa (LOP3 + PRMT, no
-//    int->float conversion), multiplied with x by packed fp32 FMA
-//    (fma.rn.f32x2), and the offset is removed per sub-block with the
-//    precomputed sub-block sums of x: sum(q x) = 2^k (A - X).
+//  * Weights are decoded in registers: each quant q is placed in the low
+//    mantissa byte of 2^23 (PRMT, no int->float conversion pipe), 2^23 is
+//    subtracted exactly in pairs (fadd.rn.f32x2), and q*x is accumulated by
+//    packed fp32 FMA (fma.rn.f32x2). The min / -32 offsets are applied per
+//    sub-block with precomputed sub-block sums of x.
 //  * The input vector x (and an optional fused RMSNorm / gated-norm /
 //    sigmoid-gate transform of it) lives in shared memory, with its 16- and
 //    32-element partial sums. Epilogues: store, residual add, SwiGLU pair.
@@ -32,24 +34,60 @@ namespace si {
 
 constexpr int kConsumerWarps = 16;
 constexpr int kThreads = kConsumerWarps * 32 + 32;
-constexpr int kTeams = kConsumerWarps * 2;
+constexpr int kMaxTeams = kConsumerWarps * 2;
 constexpr int kTeamLanes = 16;
 constexpr int kMaxSlots = 64;
-constexpr uint32_t kMaxDynSmem = 227 * 1024;
+constexpr uint32_t kPieceBytes = 4608;  // target bytes of one staged row piece
+constexpr float kBias = 8388608.0f;     // 2^23
 
-__device__ __forceinline__ float mant_float(uint32_t word, int j) {
-  // byte j of `word` becomes bits 16..23 of a float whose top byte is 0x3F.
-  return as_f(__byte_perm(word, 0x3F000000u, 0x7044u | (uint32_t(j) << 8)));
+// Per-format constants. x lives in shared memory with 4 floats of padding
+// after every 2^kPad elements, which makes the float4 loads of the 8 lanes
+// of a quarter-warp hit 8 disjoint bank groups for each format's lane map.
+template <uint32_t TYPE>
+struct Fmt;
+template <>
+struct Fmt<SI_GGML_TYPE_Q4_K> {
+  static constexpr uint32_t BB = 144, kPad = 6, kSum = 32;
+};
+template <>
+struct Fmt<SI_GGML_TYPE_Q5_K> {
+  static constexpr uint32_t BB = 176, kPad = 6, kSum = 32;
+};
+template <>
+struct Fmt<SI_GGML_TYPE_Q6_K> {
+  static constexpr uint32_t BB = 210, kPad = 7, kSum = 16;
+};
+
+template <uint32_t PAD>
+__device__ __forceinline__ uint32_t xi(uint32_t e) {
+  return e + 4u * (e >> PAD);
 }
 
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+// Byte j of `word` as the float 2^23 + byte (exact); subtracting 2^23 (in
+// pairs, fadd.rn.f32x2) leaves the integer exactly.
+__device__ __forceinline__ float bias_float(uint32_t word, int j) {
+  return as_f(__byte_perm(word, 0x4B000000u, 0x7440u | uint32_t(j)));
+}
+
+__device__ __forceinline__ float2 int_pair(uint32_t word, int j) {
+  return __fadd2_rn(make_float2(bias_float(word, j), bias_float(word, j + 1)),
+                    make_float2(-kBias, -kBias));
+}
+
+__device__ __forceinline__ float small_uint_to_float(uint32_t v) {
+  return as_f(0x4B000000u | v) - kBias;  // v < 2^23, exact, no conversion pipe
+}
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) {
+  return *reinterpret_cast<const uint4*>(p);
+}
 
 // 16 bytes from a 2-byte-aligned shared-memory address.
 __device__ __forceinline__ uint4 lds16_a2(const uint8_t* p) {
-  uint32_t off = smem_u32(p) & 3u;
+  const uint32_t off = smem_u32(p) & 3u;
   const uint32_t* w = reinterpret_cast<const uint32_t*>(p - off);
-  uint32_t a = w[0], b = w[1], c = w[2], d = w[3], e = w[4];
-  uint32_t sh = off * 8u;
+  const uint32_t a = w[0], b = w[1], c = w[2], d = w[3], e = w[4];
+  const uint32_t sh = off * 8u;
   return make_uint4(__funnelshift_r(a, b, sh), __funnelshift_r(b, c, sh),
                     __funnelshift_r(c, d, sh), __funnelshift_r(d, e, sh));
 }
@@ -58,16 +96,13 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int k) {
   return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
 }
 
-// ---------------------------------------------------------------------------
-// Q4_K: 144-byte blocks [d f16][dmin f16][12 B scales][128 B quants]. Unit g
-// (0..3) of a block covers quant bytes 32g..32g+31: low nibbles are elements
-// 64g+0..31 (scale index 2g), high nibbles 64g+32..63 (scale index 2g+1).
-// ---------------------------------------------------------------------------
-struct Q4KUnitScales {
-  float d1, m1, d2, m2;
+// 6-bit scale/min pairs (2g, 2g+1) of a K-quant header (quant.rs:176-185),
+// with lane-constant g, as floats.
+struct ScalePairs {
+  float sa, sb, ma, mb;
 };
 
-__device__ __forceinline__ Q4KUnitScales q4k_scales(const uint4& hdr, int g) {
+__device__ __forceinline__ ScalePairs k4_scales(const uint4& hdr, int g) {
   const uint32_t W1 = hdr.y, W2 = hdr.z, W3 = hdr.w;
   const uint32_t sh = 16u * uint32_t(g & 1);
   uint32_t sa, ma, sb, mb;
@@ -82,191 +117,175 @@ __device__ __forceinline__ Q4KUnitScales q4k_scales(const uint4& hdr, int g) {
     ma = ((W3 >> (sh + 4)) & 15u) | (((W2 >> (sh + 6)) & 3u) << 4);
     mb = ((W3 >> (sh + 12)) & 15u) | (((W2 >> (sh + 14)) & 3u) << 4);
   }
-  const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hdr.x));
-  Q4KUnitScales s;
-  s.d1 = dm.x * float(sa);
-  s.m1 = dm.y * float(ma);
-  s.d2 = dm.x * float(sb);
-  s.m2 = dm.y * float(mb);
+  ScalePairs s;
+  s.sa = small_uint_to_float(sa);
+  s.sb = small_uint_to_float(sb);
+  s.ma = small_uint_to_float(ma);
+  s.mb = small_uint_to_float(mb);
   return s;
 }
 
-// A_lo / A_hi for one Q4_K or Q5_K unit: sums of (1 + q/2^k) * x.
-template <int KIND>
-__device__ __forceinline__ void unit_sums_q45(const uint4 qa, const uint4 qb, const uint4 ha,
-                                              const uint4 hb, int g, const float* xp,
-                                              float& alo, float& ahi) {
-  float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const uint32_t w = word_of(k < 4 ? qa : qb, k & 3);
-    uint32_t vl, vh;
-    if (KIND == 4) {
-      // q in mantissa bits 19..22 -> 1 + q/16
-      vl = ((w << 3) & 0x78787878u) | 0x80808080u;
-      vh = ((w >> 1) & 0x78787878u) | 0x80808080u;
-    } else {
-      // Q5_K: q5 = nibble + 16*bit(qh, 2g / 2g+1), placed at bits 18..22 -> 1 + q/32
-      const uint32_t h = word_of(k < 4 ? ha : hb, k & 3);
-      const uint32_t bl = (h >> (2 * g)) & 0x01010101u;
-      const uint32_t bh = (h >> (2 * g + 1)) & 0x01010101u;
-      vl = (((w & 0x0F0F0F0Fu) | (bl << 4)) << 2) | 0x80808080u;
-      vh = ((((w >> 4) & 0x0F0F0F0Fu) | (bh << 4)) << 2) | 0x80808080u;
-    }
-    const float4 xl = *reinterpret_cast<const float4*>(xp + 4 * k);
-    const float4 xh = *reinterpret_cast<const float4*>(xp + 32 + 4 * k);
-    lo = ffma2(make_float2(mant_float(vl, 0), mant_float(vl, 1)), make_float2(xl.x, xl.y), lo);
-    lo = ffma2(make_float2(mant_float(vl, 2), mant_float(vl, 3)), make_float2(xl.z, xl.w), lo);
-    hi = ffma2(make_float2(mant_float(vh, 0), mant_float(vh, 1)), make_float2(xh.x, xh.y), hi);
-    hi = ffma2(make_float2(mant_float(vh, 2), mant_float(vh, 3)), make_float2(xh.z, xh.w), hi);
-  }
-  alo = lo.x + lo.y;
-  ahi = hi.x + hi.y;
-}
-
+// ---------------------------------------------------------------------------
+// Unit decoders. A unit is 64 weights of one super-block that a lane owns:
+// Q4_K/Q5_K group g = lane%4 (quant bytes 32g..32g+31: low nibbles are
+// elements 64g+0..31, high nibbles 64g+32..63); Q6_K half h and 16-run i0
+// with (h, i0/16) = lane%4. Each computes sum_i w_i x_i for NR rows that
+// share x.
+// ---------------------------------------------------------------------------
 template <uint32_t TYPE>
-struct RowDot;
+struct Unit;
 
 template <>
-struct RowDot<SI_GGML_TYPE_Q4_K> {
-  static constexpr uint32_t BB = 144;
+struct Unit<SI_GGML_TYPE_Q4_K> {
   template <int NR>
-  __device__ __forceinline__ static void run(const uint8_t* const* rows, const float* xs,
-                                             const float* xs32, uint32_t cols, int tl,
-                                             float* acc) {
-    const int g = tl & 3;
-    const int nunits = int(cols >> 6);
-    for (int u = tl; u < nunits; u += kTeamLanes) {
-      const int b = u >> 2;
-      const float* xp = xs + b * 256 + g * 64;
-      const float Xl = xs32[b * 8 + g * 2], Xh = xs32[b * 8 + g * 2 + 1];
+  __device__ __forceinline__ static void run(const uint8_t* const* blk, const float* xs,
+                                             const float* xsum, uint32_t b, int l4, float* acc) {
+    const int g = l4;
+    const float* xp = xs + xi<6>(b * 256 + g * 64);
+    const float Xl = xsum[b * 8 + g * 2], Xh = xsum[b * 8 + g * 2 + 1];
+    uint4 hdr[NR], qa[NR], qb[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      hdr[r] = lds128(blk[r]);
+      qa[r] = lds128(blk[r] + 16 + 32 * g);
+      qb[r] = lds128(blk[r] + 32 + 32 * g);
+    }
+    float2 l0[NR], l1[NR], h0[NR], h1[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) l0[r] = l1[r] = h0[r] = h1[r] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float4 xl = *reinterpret_cast<const float4*>(xp + 4 * k);
+      const float4 xh = *reinterpret_cast<const float4*>(xp + 32 + 4 * k);
 #pragma unroll
       for (int r = 0; r < NR; ++r) {
-        const uint8_t* blk = rows[r] + b * BB;
-        const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-        const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * g);
-        const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * g);
-        float alo, ahi;
-        unit_sums_q45<4>(qa, qb, qa, qb, g, xp, alo, ahi);
-        const Q4KUnitScales s = q4k_scales(hdr, g);
-        acc[r] += s.d1 * (16.0f * (alo - Xl)) - s.m1 * Xl;
-        acc[r] += s.d2 * (16.0f * (ahi - Xh)) - s.m2 * Xh;
+        const uint32_t w = word_of(k < 4 ? qa[r] : qb[r], k & 3);
+        const uint32_t lo = w & 0x0F0F0F0Fu;  // q
+        const uint32_t hi = w & 0xF0F0F0F0u;  // 16 q
+        l0[r] = __ffma2_rn(int_pair(lo, 0), make_float2(xl.x, xl.y), l0[r]);
+        l1[r] = __ffma2_rn(int_pair(lo, 2), make_float2(xl.z, xl.w), l1[r]);
+        h0[r] = __ffma2_rn(int_pair(hi, 0), make_float2(xh.x, xh.y), h0[r]);
+        h1[r] = __ffma2_rn(int_pair(hi, 2), make_float2(xh.z, xh.w), h1[r]);
       }
+    }
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      const float Sl = (l0[r].x + l0[r].y) + (l1[r].x + l1[r].y);
+      const float Sh = ((h0[r].x + h0[r].y) + (h1[r].x + h1[r].y)) * 0.0625f;
+      const ScalePairs s = k4_scales(hdr[r], g);
+      const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hdr[r].x));
+      acc[r] += dm.x * (s.sa * Sl + s.sb * Sh) - dm.y * (s.ma * Xl + s.mb * Xh);
     }
   }
 };
 
 template <>
-struct RowDot<SI_GGML_TYPE_Q5_K> {
-  static constexpr uint32_t BB = 176;
+struct Unit<SI_GGML_TYPE_Q5_K> {
   template <int NR>
-  __device__ __forceinline__ static void run(const uint8_t* const* rows, const float* xs,
-                                             const float* xs32, uint32_t cols, int tl,
-                                             float* acc) {
-    const int g = tl & 3;
-    const int nunits = int(cols >> 6);
-    for (int u = tl; u < nunits; u += kTeamLanes) {
-      const int b = u >> 2;
-      const float* xp = xs + b * 256 + g * 64;
-      const float Xl = xs32[b * 8 + g * 2], Xh = xs32[b * 8 + g * 2 + 1];
+  __device__ __forceinline__ static void run(const uint8_t* const* blk, const float* xs,
+                                             const float* xsum, uint32_t b, int l4, float* acc) {
+    const int g = l4;
+    const float* xp = xs + xi<6>(b * 256 + g * 64);
+    const float Xl = xsum[b * 8 + g * 2], Xh = xsum[b * 8 + g * 2 + 1];
 #pragma unroll
-      for (int r = 0; r < NR; ++r) {
-        const uint8_t* blk = rows[r] + b * BB;
-        const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-        const uint4 ha = *reinterpret_cast<const uint4*>(blk + 16);
-        const uint4 hb = *reinterpret_cast<const uint4*>(blk + 32);
-        const uint4 qa = *reinterpret_cast<const uint4*>(blk + 48 + 32 * g);
-        const uint4 qb = *reinterpret_cast<const uint4*>(blk + 64 + 32 * g);
-        float alo, ahi;
-        unit_sums_q45<5>(qa, qb, ha, hb, g, xp, alo, ahi);
-        const Q4KUnitScales s = q4k_scales(hdr, g);
-        acc[r] += s.d1 * (32.0f * (alo - Xl)) - s.m1 * Xl;
-        acc[r] += s.d2 * (32.0f * (ahi - Xh)) - s.m2 * Xh;
+    for (int r = 0; r < NR; ++r) {
+      const uint4 hdr = lds128(blk[r]);
+      const uint4 ha = lds128(blk[r] + 16), hb = lds128(blk[r] + 32);
+      const uint4 qa = lds128(blk[r] + 48 + 32 * g), qb = lds128(blk[r] + 64 + 32 * g);
+      float2 l0 = make_float2(0.f, 0.f), l1 = l0, h0 = l0, h1 = l0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float4 xl = *reinterpret_cast<const float4*>(xp + 4 * k);
+        const float4 xh = *reinterpret_cast<const float4*>(xp + 32 + 4 * k);
+        const uint32_t w = word_of(k < 4 ? qa : qb, k & 3);
+        const uint32_t h = word_of(k < 4 ? ha : hb, k & 3);
+        const uint32_t lo = (w & 0x0F0F0F0Fu) | (((h >> (2 * g)) & 0x01010101u) << 4);
+        const uint32_t hi = ((w >> 4) & 0x0F0F0F0Fu) | (((h >> (2 * g + 1)) & 0x01010101u) << 4);
+        l0 = __ffma2_rn(int_pair(lo, 0), make_float2(xl.x, xl.y), l0);
+        l1 = __ffma2_rn(int_pair(lo, 2), make_float2(xl.z, xl.w), l1);
+        h0 = __ffma2_rn(int_pair(hi, 0), make_float2(xh.x, xh.y), h0);
+        h1 = __ffma2_rn(int_pair(hi, 2), make_float2(xh.z, xh.w), h1);
       }
+      const float Sl = (l0.x + l0.y) + (l1.x + l1.y);
+      const float Sh = (h0.x + h0.y) + (h1.x + h1.y);
+      const ScalePairs s = k4_scales(hdr, g);
+      const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hdr.x));
+      acc[r] += dm.x * (s.sa * Sl + s.sb * Sh) - dm.y * (s.ma * Xl + s.mb * Xh);
     }
   }
 };
 
-// ---------------------------------------------------------------------------
-// Q6_K: 210-byte blocks [ql 128][qh 64][int8 scales 16][d f16]. Unit ul (0..3)
-// is half h = ul/2 and 16-run i0 = 16*(ul%2): q1..q4 of elements
-// 128h + i0 + {0,32,64,96} + (0..15), scales 8h + ul%2 + {0,2,4,6}.
-// ---------------------------------------------------------------------------
 template <>
-struct RowDot<SI_GGML_TYPE_Q6_K> {
-  static constexpr uint32_t BB = 210;
+struct Unit<SI_GGML_TYPE_Q6_K> {
   template <int NR>
-  __device__ __forceinline__ static void run(const uint8_t* const* rows, const float* xs,
-                                             const float* xs16, uint32_t cols, int tl,
-                                             float* acc) {
-    const int ul = tl & 3;
-    const int h = ul >> 1, i0 = (ul & 1) * 16;
-    const int nunits = int(cols >> 6);
-    for (int u = tl; u < nunits; u += kTeamLanes) {
-      const int b = u >> 2;
-      const int e0 = b * 256 + 128 * h + i0;
-      const float* xp = xs + e0;
-      float X[4];
+  __device__ __forceinline__ static void run(const uint8_t* const* blk, const float* xs,
+                                             const float* xsum, uint32_t b, int l4, float* acc) {
+    const int h = l4 >> 1, i0 = (l4 & 1) * 16;
+    const uint32_t e0 = b * 256 + 128 * h + i0;
+    const float* xp = xs + xi<7>(e0);
+    float X[4];
 #pragma unroll
-      for (int m = 0; m < 4; ++m) X[m] = xs16[(e0 >> 4) + 2 * m];
+    for (int m = 0; m < 4; ++m) X[m] = xsum[(e0 >> 4) + 2 * m];
 #pragma unroll
-      for (int r = 0; r < NR; ++r) {
-        const uint8_t* blk = rows[r] + b * BB;
-        const uint4 L1 = lds16_a2(blk + 64 * h + i0);
-        const uint4 L2 = lds16_a2(blk + 64 * h + 32 + i0);
-        const uint4 H = lds16_a2(blk + 128 + 32 * h + i0);
-        const uint8_t* scp = blk + 192 + 8 * h + (ul & 1);
-        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(blk + 208));
-        float2 a[4];
+    for (int r = 0; r < NR; ++r) {
+      const uint8_t* bp = blk[r];
+      const uint4 L1 = lds16_a2(bp + 64 * h + i0);
+      const uint4 L2 = lds16_a2(bp + 64 * h + 32 + i0);
+      const uint4 H = lds16_a2(bp + 128 + 32 * h + i0);
+      const uint8_t* scp = bp + 192 + 8 * h + (l4 & 1);
+      const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(bp + 208));
+      float2 a[4], c[4];
 #pragma unroll
-        for (int m = 0; m < 4; ++m) a[m] = make_float2(0.f, 0.f);
+      for (int m = 0; m < 4; ++m) a[m] = c[m] = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint32_t l1 = word_of(L1, k), l2 = word_of(L2, k), hh = word_of(H, k);
-          uint32_t v[4];
-          v[0] = ((l1 << 1) & 0x1E1E1E1Eu) | ((hh << 5) & 0x60606060u) | 0x80808080u;
-          v[1] = ((l2 << 1) & 0x1E1E1E1Eu) | ((hh << 3) & 0x60606060u) | 0x80808080u;
-          v[2] = ((l1 >> 3) & 0x1E1E1E1Eu) | ((hh << 1) & 0x60606060u) | 0x80808080u;
-          v[3] = ((l2 >> 3) & 0x1E1E1E1Eu) | ((hh >> 1) & 0x60606060u) | 0x80808080u;
-#pragma unroll
-          for (int m = 0; m < 4; ++m) {
-            const float4 xv = *reinterpret_cast<const float4*>(xp + 32 * m + 4 * k);
-            a[m] = ffma2(make_float2(mant_float(v[m], 0), mant_float(v[m], 1)),
-                         make_float2(xv.x, xv.y), a[m]);
-            a[m] = ffma2(make_float2(mant_float(v[m], 2), mant_float(v[m], 3)),
-                         make_float2(xv.z, xv.w), a[m]);
-          }
-        }
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t l1 = word_of(L1, k), l2 = word_of(L2, k), hh = word_of(H, k);
+        uint32_t v[4];
+        v[0] = (l1 & 0x0F0F0F0Fu) | ((hh << 4) & 0x30303030u);
+        v[1] = (l2 & 0x0F0F0F0Fu) | ((hh << 2) & 0x30303030u);
+        v[2] = ((l1 >> 4) & 0x0F0F0F0Fu) | (hh & 0x30303030u);
+        v[3] = ((l2 >> 4) & 0x0F0F0F0Fu) | ((hh >> 2) & 0x30303030u);
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
-          const float sc = float(int(static_cast<int8_t>(scp[2 * m])));
-          const float A = a[m].x + a[m].y;
-          acc[r] += (d * sc) * (64.0f * (A - X[m]) - 32.0f * X[m]);
+          const float4 xv = *reinterpret_cast<const float4*>(xp + 32 * m + 4 * k);
+          a[m] = __ffma2_rn(int_pair(v[m], 0), make_float2(xv.x, xv.y), a[m]);
+          c[m] = __ffma2_rn(int_pair(v[m], 2), make_float2(xv.z, xv.w), c[m]);
         }
       }
+      float t = 0.f;
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float sc = float(int(static_cast<int8_t>(scp[2 * m])));
+        const float S = (a[m].x + a[m].y) + (c[m].x + c[m].y);  // sum q x, q in 0..63
+        t += sc * (S - 32.0f * X[m]);
+      }
+      acc[r] += d * t;
     }
   }
 };
 
 // ---------------------------------------------------------------------------
-// The kernel.
+// Launch geometry (computed on the host).
 // ---------------------------------------------------------------------------
-struct ItemSrc {
-  const uint8_t* g;  // global address of the row
-  float* y;
-  const float* resid;
-  uint32_t row;
+struct QmvGeom {
+  uint32_t piece_blocks;  // super-blocks per staged piece (multiple of 4)
+  uint32_t npieces;       // pieces per row
+  uint32_t slot_bytes;    // bytes of one slot (NR rows)
+  uint32_t row_slot;      // bytes reserved per row inside a slot
+  uint32_t nslots, teams, per_team;
+  uint32_t slots_off;     // shared-memory offset of the slots
+  uint32_t xs_floats;     // padded x length
 };
 
-__device__ __forceinline__ ItemSrc item_src(const QmvParams& p, uint32_t item, uint32_t rb,
-                                            int which) {
-  ItemSrc s;
+__device__ __forceinline__ void row_src(const QmvParams& p, uint32_t item, uint32_t rb, int which,
+                                        const uint8_t** g, float** y, const float** resid,
+                                        uint32_t* row) {
   if (p.pair) {
-    s.g = p.seg[which].w + size_t(item) * rb;
-    s.y = p.seg[0].y;
-    s.resid = p.seg[0].resid;
-    s.row = item;
-    return s;
+    *g = p.seg[which].w + size_t(item) * rb;
+    *y = p.seg[0].y;
+    *resid = p.seg[0].resid;
+    *row = item;
+    return;
   }
   uint32_t r = item;
   int k = 0;
@@ -276,41 +295,47 @@ __device__ __forceinline__ ItemSrc item_src(const QmvParams& p, uint32_t item, u
       r -= p.seg[k].rows;
       ++k;
     }
-  s.g = p.seg[k].w + size_t(r) * rb;
-  s.y = p.seg[k].y;
-  s.resid = p.seg[k].resid;
-  s.row = r;
-  return s;
+  *g = p.seg[k].w + size_t(r) * rb;
+  *y = p.seg[k].y;
+  *resid = p.seg[k].resid;
+  *row = r;
 }
 
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
 }
 
+// Team t of a CTA owns slots [t*per_team, (t+1)*per_team) and processes rows
+// t, t+teams, ... of the CTA's range, each as npieces pieces; its j-th piece
+// uses slot t*per_team + j % per_team in round j / per_team. Only the owning
+// team waits on a slot's full barrier, strictly in round order, so a waiter
+// is never more than one phase ahead of the barrier.
 template <uint32_t TYPE, int NR>
 __global__ void __launch_bounds__(kThreads, 1)
-    qmv_kernel(const __grid_constant__ QmvParams p, uint32_t slot_bytes, uint32_t nslots,
-               uint32_t slots_off) {
+    qmv_kernel(const __grid_constant__ QmvParams p, const __grid_constant__ QmvGeom G) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_abort;
   __shared__ float s_red[kConsumerWarps];
+  constexpr uint32_t BB = Fmt<TYPE>::BB;
+  constexpr uint32_t PAD = Fmt<TYPE>::kPad;
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + nslots;
+  uint64_t* empty = full + G.nslots;
   const uint32_t cols = p.cols;
-  float* xs = reinterpret_cast<float*>(smem + 16 * nslots);
-  float* xs16 = xs + cols;
-  float* xs32 = xs16 + cols / 16;
-  uint8_t* slots = smem + slots_off;
+  float* xs = reinterpret_cast<float*>(smem + 16 * G.nslots);
+  float* xsum = xs + G.xs_floats;
+  uint8_t* slots = smem + G.slots_off;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rb = cols / 256 * RowDot<TYPE>::BB;
+  const uint32_t nb = cols / 256;
+  const uint32_t rb = nb * BB;
   const uint32_t i0 = uint32_t(uint64_t(blockIdx.x) * p.items / gridDim.x);
   const uint32_t i1 = uint32_t(uint64_t(blockIdx.x + 1) * p.items / gridDim.x);
   const uint32_t n_items = i1 - i0;
+  const uint32_t T = G.teams, M = G.per_team, NP = G.npieces, P = G.piece_blocks;
 
   if (threadIdx.x == 0) {
-    for (uint32_t s = 0; s < nslots; ++s) {
+    for (uint32_t s = 0; s < G.nslots; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -321,64 +346,78 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_launch_dependents();
 
   if (warp == kConsumerWarps) {
-    // ---------------- producer: one elected lane streams rows -------------
+    // ---------------- producer: one elected lane streams row pieces --------
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
-      uint32_t issued = 0;
-      for (uint32_t k = 0; k < n_items; ++k) {
-        const uint32_t s = k % nslots, n = k / nslots;
-        if (n > 0 && !mbar_wait_bounded(&empty[s], (n - 1) & 1)) {
-          atomicOr(p.err, KERR_TIMEOUT_EMPTY);
-          s_abort = 1;
-          break;
-        }
-        if (*reinterpret_cast<volatile int*>(&s_abort)) break;
-        uint8_t* dst = slots + size_t(s) * slot_bytes;
-        uint32_t tx = 0;
+      const uint32_t rounds = NP * ((n_items + T - 1) / T);
+      bool abort = false;
+      uint32_t last_j = 0;
+      for (uint32_t j = 0; j < rounds && !abort; ++j) {
+        for (uint32_t t = 0; t < T; ++t) {
+          const uint32_t rl = t + T * (j / NP);
+          if (rl >= n_items) continue;
+          const uint32_t s = t * M + j % M, n = j / M;
+          if (n > 0 && !mbar_wait_bounded(&empty[s], (n - 1) & 1)) {
+            atomicOr(p.err, KERR_TIMEOUT_EMPTY);
+            s_abort = 1;
+            abort = true;
+            break;
+          }
+          if (*reinterpret_cast<volatile int*>(&s_abort)) {
+            abort = true;
+            break;
+          }
+          const uint32_t pc = j % NP;
+          const uint32_t b0 = pc * P, pb = min(P, nb - b0);
+          uintptr_t a0[NR], a1[NR];
+          uint32_t tx = 0;
 #pragma unroll
-        for (int w = 0; w < NR; ++w) {
-          const ItemSrc src = item_src(p, i0 + k, rb, w);
-          const uintptr_t a = reinterpret_cast<uintptr_t>(src.g);
-          const uintptr_t a0 = a & ~uintptr_t(15);
-          const uintptr_t a1 = (a + rb + 15) & ~uintptr_t(15);
-          tx += uint32_t(a1 - a0);
-        }
-        mbar_arrive_expect_tx(&full[s], tx);
+          for (int w = 0; w < NR; ++w) {
+            const uint8_t* g;
+            float* y;
+            const float* rs;
+            uint32_t row;
+            row_src(p, i0 + rl, rb, w, &g, &y, &rs, &row);
+            const uintptr_t a = reinterpret_cast<uintptr_t>(g) + uintptr_t(b0) * BB;
+            a0[w] = a & ~uintptr_t(15);
+            a1[w] = (a + uintptr_t(pb) * BB + 15) & ~uintptr_t(15);
+            tx += uint32_t(a1[w] - a0[w]);
+          }
+          mbar_arrive_expect_tx(&full[s], tx);
+          uint8_t* dst = slots + size_t(s) * G.slot_bytes;
 #pragma unroll
-        for (int w = 0; w < NR; ++w) {
-          const ItemSrc src = item_src(p, i0 + k, rb, w);
-          const uintptr_t a = reinterpret_cast<uintptr_t>(src.g);
-          const uintptr_t a0 = a & ~uintptr_t(15);
-          const uintptr_t a1 = (a + rb + 15) & ~uintptr_t(15);
-          bulk_g2s(dst + w * (slot_bytes / NR), reinterpret_cast<const void*>(a0),
-                   uint32_t(a1 - a0), &full[s], pol);
+          for (int w = 0; w < NR; ++w)
+            bulk_g2s(dst + w * G.row_slot, reinterpret_cast<const void*>(a0[w]), uint32_t(a1[w] - a0[w]),
+                     &full[s], pol);
         }
-        ++issued;
+        last_j = j;
       }
-      if (*reinterpret_cast<volatile int*>(&s_abort)) {
-        // Drain: wait (bounded) until every copy this CTA issued has landed.
-        const uint32_t first = issued > nslots ? issued - nslots : 0;
-        for (uint32_t k = first; k < issued; ++k)
-          if (!mbar_wait_bounded(&full[k % nslots], (k / nslots) & 1))
-            atomicOr(p.err, KERR_TIMEOUT_DRAIN);
+      if (abort) {
+        // Drain: wait (bounded) for the copies still in flight in every slot.
+        for (uint32_t t = 0; t < T; ++t)
+          for (uint32_t q = 0; q < M && q <= last_j; ++q) {
+            const uint32_t j = last_j - q;
+            const uint32_t rl = t + T * (j / NP);
+            if (rl >= n_items) continue;
+            if (!mbar_wait_bounded(&full[t * M + j % M], (j / M) & 1)) atomicOr(p.err, KERR_TIMEOUT_DRAIN);
+          }
       }
     }
     return;
   }
 
-  // ---------------- consumers: build x in shared memory -------------------
+  // ---------------- consumers: build x (padded layout) in shared memory ----
   pdl_wait();
-  const int ct = threadIdx.x;  // 0 .. 511
+  const int ct = threadIdx.x;
   constexpr int NC = kConsumerWarps * 32;
   if (p.xmode == XM_RAW) {
     for (uint32_t i = ct * 4; i < cols; i += NC * 4)
-      *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(p.x + i);
+      *reinterpret_cast<float4*>(xs + xi<PAD>(i)) = *reinterpret_cast<const float4*>(p.x + i);
   } else if (p.xmode == XM_RMS1P) {
     float ss = 0.f;
-    for (uint32_t i = ct; i < cols; i += NC) {
-      const float v = p.x[i];
-      xs[i] = v;
-      ss += v * v;
+    for (uint32_t i = ct * 4; i < cols; i += NC * 4) {
+      const float4 v = *reinterpret_cast<const float4*>(p.x + i);
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     }
     ss = warp_sum(ss);
     if (lane == 0) s_red[warp] = ss;
@@ -387,9 +426,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) tot += s_red[w];
     const float inv = 1.0f / sqrtf(tot / float(cols) + p.eps);
-    for (uint32_t i = ct; i < cols; i += NC) xs[i] = xs[i] * inv * (1.0f + p.xw[i]);
+    for (uint32_t i = ct; i < cols; i += NC) xs[xi<PAD>(i)] = p.x[i] * inv * (1.0f + p.xw[i]);
   } else if (p.xmode == XM_GATED) {
-    // One warp per head (head_dim a multiple of 32).
     const uint32_t hd = p.head_dim, heads = cols / hd;
     for (uint32_t h = warp; h < heads; h += kConsumerWarps) {
       float ss = 0.f;
@@ -402,66 +440,91 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (uint32_t i = lane; i < hd; i += 32) {
         const float v = p.x[h * hd + i];
         const float z = p.xaux[h * hd + i];
-        xs[h * hd + i] = v * inv * p.xw[i] * (z / (1.0f + expf(-z)));
+        xs[xi<PAD>(h * hd + i)] = v * inv * p.xw[i] * (z / (1.0f + expf(-z)));
       }
     }
   } else {  // XM_SIGGATE
     for (uint32_t i = ct; i < cols; i += NC) {
       const float gte = p.xaux[i];
-      xs[i] = p.x[i] / (1.0f + expf(-gte));
+      xs[xi<PAD>(i)] = p.x[i] / (1.0f + expf(-gte));
     }
   }
   consumer_sync();
-  for (uint32_t j = ct; j < cols / 16; j += NC) {
-    const float4* q = reinterpret_cast<const float4*>(xs + 16 * j);
-    float4 a = q[0], b = q[1], c = q[2], d = q[3];
-    xs16[j] = ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w)) +
-              (((c.x + c.y) + (c.z + c.w)) + ((d.x + d.y) + (d.z + d.w)));
+  constexpr uint32_t SUM = Fmt<TYPE>::kSum;
+  for (uint32_t j = ct; j < cols / SUM; j += NC) {
+    const float* q = xs + xi<PAD>(SUM * j);
+    float t = 0.f;
+#pragma unroll
+    for (uint32_t i = 0; i < SUM; i += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(q + i);
+      t += (v.x + v.y) + (v.z + v.w);
+    }
+    xsum[j] = t;
   }
   consumer_sync();
-  for (uint32_t j = ct; j < cols / 32; j += NC) xs32[j] = xs16[2 * j] + xs16[2 * j + 1];
-  consumer_sync();
 
-  // ---------------- consumers: one row (pair) per team ---------------------
-  const int team = ct >> 4, tl = ct & 15;
+  // ---------------- consumers: pieces of rows, per-team private slots ------
+  const uint32_t team = uint32_t(ct) >> 4;
+  const int tl = ct & 15;
+  if (team >= T) return;
   const unsigned tmask = (lane < 16) ? 0x0000ffffu : 0xffff0000u;
-  const float* xsum = (TYPE == SI_GGML_TYPE_Q6_K) ? xs16 : xs32;
-  for (uint32_t k = team; k < n_items; k += kTeams) {
-    const uint32_t s = k % nslots, n = k / nslots;
+  float acc[NR];
+#pragma unroll
+  for (int w = 0; w < NR; ++w) acc[w] = 0.f;
+  for (uint32_t j = 0;; ++j) {
+    const uint32_t rl = team + T * (j / NP);
+    if (rl >= n_items) break;
+    const uint32_t pc = j % NP, s = team * M + j % M, n = j / M;
     if (!mbar_wait_bounded(&full[s], n & 1)) {
       atomicOr(p.err, KERR_TIMEOUT_FULL);
       s_abort = 1;
       break;
     }
-    const uint8_t* base = slots + size_t(s) * slot_bytes;
-    const uint8_t* rows[NR];
-    ItemSrc src0 = item_src(p, i0 + k, rb, 0);
+    const uint32_t b0 = pc * P, pb = min(P, nb - b0);
+    const uint8_t* base = slots + size_t(s) * G.slot_bytes;
+    const uint8_t* rowp[NR];
 #pragma unroll
     for (int w = 0; w < NR; ++w) {
-      const ItemSrc src = item_src(p, i0 + k, rb, w);
-      rows[w] = base + w * (slot_bytes / NR) + (reinterpret_cast<uintptr_t>(src.g) & 15);
+      const uint8_t* g;
+      float* y;
+      const float* rs;
+      uint32_t row;
+      row_src(p, i0 + rl, rb, w, &g, &y, &rs, &row);
+      rowp[w] = base + w * G.row_slot + ((reinterpret_cast<uintptr_t>(g) + uintptr_t(b0) * BB) & 15);
     }
-    float acc[NR];
+    const uint32_t units = pb * 4;
+    for (uint32_t u = tl; u < units; u += kTeamLanes) {
+      const uint8_t* blk[NR];
 #pragma unroll
-    for (int w = 0; w < NR; ++w) acc[w] = 0.f;
-    RowDot<TYPE>::template run<NR>(rows, xs, xsum, cols, tl, acc);
-#pragma unroll
-    for (int w = 0; w < NR; ++w) {
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) acc[w] += __shfl_xor_sync(tmask, acc[w], o);
+      for (int w = 0; w < NR; ++w) blk[w] = rowp[w] + (u >> 2) * BB;
+      Unit<TYPE>::template run<NR>(blk, xs, xsum, b0 + (u >> 2), tl & 3, acc);
     }
     __syncwarp(tmask);
-    if (tl == 0) {
-      mbar_arrive(&empty[s]);
-      float out;
-      if (NR == 2) {
-        const float g = acc[0];
-        out = g / (1.0f + expf(-g)) * acc[NR - 1];
-      } else {
-        out = acc[0];
+    if (tl == 0) mbar_arrive(&empty[s]);
+    if (pc == NP - 1) {
+#pragma unroll
+      for (int w = 0; w < NR; ++w) {
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) acc[w] += __shfl_xor_sync(tmask, acc[w], o);
       }
-      if (src0.resid) out = src0.resid[src0.row] + out;
-      src0.y[src0.row] = out;
+      if (tl == 0) {
+        const uint8_t* g;
+        float* y;
+        const float* rs;
+        uint32_t row;
+        row_src(p, i0 + rl, rb, 0, &g, &y, &rs, &row);
+        float out;
+        if (NR == 2) {
+          const float gv = acc[0];
+          out = gv / (1.0f + expf(-gv)) * acc[NR - 1];
+        } else {
+          out = acc[0];
+        }
+        if (rs) out = rs[row] + out;
+        y[row] = out;
+      }
+#pragma unroll
+      for (int w = 0; w < NR; ++w) acc[w] = 0.f;
     }
   }
 }
@@ -469,31 +532,54 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <uint32_t TYPE, int NR>
 static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
                     std::string* msg) {
-  const uint32_t bb = block_bytes_of(TYPE);
-  const uint32_t rb = p.cols / 256 * bb;
-  const uint32_t slot_one = (rb + 32 + 127) & ~127u;
-  const uint32_t slot_bytes = slot_one * NR;
-  const uint32_t xbytes = 4 * (p.cols + p.cols / 16 + p.cols / 32);
-  // bars (16 B per slot) + x region, rounded to 128; then slots.
-  uint32_t nslots = kMaxSlots;
-  uint32_t slots_off = 0, total = 0;
+  constexpr uint32_t BB = Fmt<TYPE>::BB;
+  constexpr uint32_t PAD = Fmt<TYPE>::kPad;
+  const uint32_t nb = p.cols / 256;
+  QmvGeom G = {};
+  // piece: a multiple of 4 super-blocks of at most ~kPieceBytes
+  uint32_t P = (kPieceBytes / BB) & ~3u;
+  if (P < 4) P = 4;
+  if (nb <= P) P = nb;
+  G.piece_blocks = P;
+  G.npieces = (nb + P - 1) / P;
+  G.row_slot = (P * BB + 32 + 127) & ~127u;
+  G.slot_bytes = G.row_slot * NR;
+  G.xs_floats = p.cols + 4 * (p.cols >> PAD);
+  const uint32_t xbytes = 4 * (G.xs_floats + p.cols / Fmt<TYPE>::kSum);
+  static uint32_t max_dyn = 0;
+  if (max_dyn == 0) {
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa = {};
+    cudaFuncGetAttributes(&fa, qmv_kernel<TYPE, NR>);
+    const uint32_t limit = uint32_t(optin) > uint32_t(fa.sharedSizeBytes) + 256
+                               ? uint32_t(optin) - uint32_t(fa.sharedSizeBytes) - 256
+                               : 0;
+    cudaError_t e = cudaFuncSetAttribute(qmv_kernel<TYPE, NR>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(limit));
+    if (e != cudaSuccess) {
+      if (msg) *msg = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+      return SI_E_CUDA;
+    }
+    max_dyn = limit;
+  }
+  // largest slot count that fits, then teams with >= 2 private slots each
+  uint32_t nslots = kMaxSlots, total = 0;
   for (; nslots >= 2; --nslots) {
-    slots_off = (16 * nslots + xbytes + 127) & ~127u;
-    total = slots_off + nslots * slot_bytes;
-    if (total <= kMaxDynSmem) break;
+    G.slots_off = (16 * nslots + xbytes + 127) & ~127u;
+    total = G.slots_off + nslots * G.slot_bytes;
+    if (total <= max_dyn) break;
   }
   if (nslots < 2) {
-    if (msg) *msg = "matvec row is too long for the shared-memory staging ring";
+    if (msg) *msg = "matvec input vector is too long for the shared-memory staging ring";
     return SI_E_UNSUPPORTED;
   }
-  static bool attr_set[2] = {false, false};
-  (void)attr_set;
-  cudaError_t e = cudaFuncSetAttribute(qmv_kernel<TYPE, NR>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMaxDynSmem));
-  if (e != cudaSuccess) {
-    if (msg) *msg = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
-    return SI_E_CUDA;
-  }
+  G.teams = nslots / 2 < uint32_t(kMaxTeams) ? nslots / 2 : uint32_t(kMaxTeams);
+  G.per_team = nslots / G.teams;
+  G.nslots = G.teams * G.per_team;
+  G.slots_off = (16 * G.nslots + xbytes + 127) & ~127u;
+  total = G.slots_off + G.nslots * G.slot_bytes;
   const uint32_t grid = p.items < uint32_t(sm_count) ? p.items : uint32_t(sm_count);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -505,7 +591,7 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  e = cudaLaunchKernelEx(&cfg, qmv_kernel<TYPE, NR>, p, slot_bytes, nslots, slots_off);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, qmv_kernel<TYPE, NR>, p, G);
   if (e != cudaSuccess) {
     if (msg) *msg = std::string("matvec launch: ") + cudaGetErrorString(e);
     return SI_E_CUDA;
