@@ -25,12 +25,21 @@
 //  * Accumulation is fp32 throughout; team results are combined with
 //    warp shuffles. Tensor cores are not used: batch-1 is not a contraction.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
 #include "qmatvec.cuh"
 
 namespace si {
+
+__device__ unsigned long long g_qmv_ts[16];
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+#define TS(i) if ((G.debug & 128) && blockIdx.x == 0 && threadIdx.x == 0) g_qmv_ts[i] = gtime();
 
 constexpr int kConsumerWarps = 16;
 constexpr int kThreads = kConsumerWarps * 32 + 32;
@@ -103,25 +112,25 @@ struct ScalePairs {
 };
 
 __device__ __forceinline__ ScalePairs k4_scales(const uint4& hdr, int g) {
+  // Branch-free (g is lane-constant but differs within a warp).
   const uint32_t W1 = hdr.y, W2 = hdr.z, W3 = hdr.w;
+  const bool lowg = g < 2;
   const uint32_t sh = 16u * uint32_t(g & 1);
-  uint32_t sa, ma, sb, mb;
-  if (g < 2) {
-    sa = (W1 >> sh) & 63u;
-    sb = (W1 >> (sh + 8)) & 63u;
-    ma = (W2 >> sh) & 63u;
-    mb = (W2 >> (sh + 8)) & 63u;
-  } else {
-    sa = ((W3 >> sh) & 15u) | (((W1 >> (sh + 6)) & 3u) << 4);
-    sb = ((W3 >> (sh + 8)) & 15u) | (((W1 >> (sh + 14)) & 3u) << 4);
-    ma = ((W3 >> (sh + 4)) & 15u) | (((W2 >> (sh + 6)) & 3u) << 4);
-    mb = ((W3 >> (sh + 12)) & 15u) | (((W2 >> (sh + 14)) & 3u) << 4);
-  }
+  const uint32_t A = lowg ? W1 : W3, B = lowg ? W2 : (W3 >> 4);
+  const uint32_t m6 = lowg ? 63u : 15u, hm = lowg ? 0u : 0x30u;
+  const uint32_t sa = ((A >> sh) & m6) | ((W1 >> (sh + 2)) & hm);
+  const uint32_t sb = ((A >> (sh + 8)) & m6) | ((W1 >> (sh + 10)) & hm);
+  const uint32_t ma = ((B >> sh) & m6) | ((W2 >> (sh + 2)) & hm);
+  const uint32_t mb = ((B >> (sh + 8)) & m6) | ((W2 >> (sh + 10)) & hm);
+  const float2 s2 = __fadd2_rn(make_float2(as_f(0x4B000000u | sa), as_f(0x4B000000u | sb)),
+                               make_float2(-kBias, -kBias));
+  const float2 m2 = __fadd2_rn(make_float2(as_f(0x4B000000u | ma), as_f(0x4B000000u | mb)),
+                               make_float2(-kBias, -kBias));
   ScalePairs s;
-  s.sa = small_uint_to_float(sa);
-  s.sb = small_uint_to_float(sb);
-  s.ma = small_uint_to_float(ma);
-  s.mb = small_uint_to_float(mb);
+  s.sa = s2.x;
+  s.sb = s2.y;
+  s.ma = m2.x;
+  s.mb = m2.y;
   return s;
 }
 
@@ -137,53 +146,71 @@ struct Unit;
 
 template <>
 struct Unit<SI_GGML_TYPE_Q4_K> {
-  template <int NR>
+  // NU independent units (blocks b[0..NU)) of NR rows, interleaved for ILP.
+  template <int NR, int NU = 1>
   __device__ __forceinline__ static void run(const uint8_t* const* blk, const float* xs,
-                                             const float* xsum, uint32_t b, int l4, float* acc) {
+                                             const float* xsum, const uint32_t* bb, int l4,
+                                             float* acc) {
     const int g = l4;
-    const float* xp = xs + xi<6>(b * 256 + g * 64);
-    const float Xl = xsum[b * 8 + g * 2], Xh = xsum[b * 8 + g * 2 + 1];
-    uint4 hdr[NR], qa[NR], qb[NR];
+    const float* xp[NU];
+    float Xl[NU], Xh[NU];
+    uint4 hdr[NU][NR], qa[NU][NR], qb[NU][NR];
 #pragma unroll
-    for (int r = 0; r < NR; ++r) {
-      hdr[r] = lds128(blk[r]);
-      qa[r] = lds128(blk[r] + 16 + 32 * g);
-      qb[r] = lds128(blk[r] + 32 + 32 * g);
-    }
-    float2 l0[NR], l1[NR], h0[NR], h1[NR];
-#pragma unroll
-    for (int r = 0; r < NR; ++r) l0[r] = l1[r] = h0[r] = h1[r] = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float4 xl = *reinterpret_cast<const float4*>(xp + 4 * k);
-      const float4 xh = *reinterpret_cast<const float4*>(xp + 32 + 4 * k);
+    for (int v = 0; v < NU; ++v) {
+      xp[v] = xs + xi<6>(bb[v] * 256 + g * 64);
+      Xl[v] = xsum[bb[v] * 8 + g * 2];
+      Xh[v] = xsum[bb[v] * 8 + g * 2 + 1];
 #pragma unroll
       for (int r = 0; r < NR; ++r) {
-        const uint32_t w = word_of(k < 4 ? qa[r] : qb[r], k & 3);
-        const uint32_t lo = w & 0x0F0F0F0Fu;  // q
-        const uint32_t hi = w & 0xF0F0F0F0u;  // 16 q
-        l0[r] = __ffma2_rn(int_pair(lo, 0), make_float2(xl.x, xl.y), l0[r]);
-        l1[r] = __ffma2_rn(int_pair(lo, 2), make_float2(xl.z, xl.w), l1[r]);
-        h0[r] = __ffma2_rn(int_pair(hi, 0), make_float2(xh.x, xh.y), h0[r]);
-        h1[r] = __ffma2_rn(int_pair(hi, 2), make_float2(xh.z, xh.w), h1[r]);
+        const uint8_t* bp = blk[v * NR + r];
+        hdr[v][r] = lds128(bp);
+        qa[v][r] = lds128(bp + 16 + 32 * g);
+        qb[v][r] = lds128(bp + 32 + 32 * g);
+      }
+    }
+    float2 l0[NU][NR], l1[NU][NR], h0[NU][NR], h1[NU][NR];
+#pragma unroll
+    for (int v = 0; v < NU; ++v)
+#pragma unroll
+      for (int r = 0; r < NR; ++r) l0[v][r] = l1[v][r] = h0[v][r] = h1[v][r] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+#pragma unroll
+      for (int v = 0; v < NU; ++v) {
+        const float4 xl = *reinterpret_cast<const float4*>(xp[v] + 4 * k);
+        const float4 xh = *reinterpret_cast<const float4*>(xp[v] + 32 + 4 * k);
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+          const uint32_t w = word_of(k < 4 ? qa[v][r] : qb[v][r], k & 3);
+          const uint32_t lo = w & 0x0F0F0F0Fu;  // q
+          const uint32_t hi = w & 0xF0F0F0F0u;  // 16 q
+          l0[v][r] = __ffma2_rn(int_pair(lo, 0), make_float2(xl.x, xl.y), l0[v][r]);
+          l1[v][r] = __ffma2_rn(int_pair(lo, 2), make_float2(xl.z, xl.w), l1[v][r]);
+          h0[v][r] = __ffma2_rn(int_pair(hi, 0), make_float2(xh.x, xh.y), h0[v][r]);
+          h1[v][r] = __ffma2_rn(int_pair(hi, 2), make_float2(xh.z, xh.w), h1[v][r]);
+        }
       }
     }
 #pragma unroll
-    for (int r = 0; r < NR; ++r) {
-      const float Sl = (l0[r].x + l0[r].y) + (l1[r].x + l1[r].y);
-      const float Sh = ((h0[r].x + h0[r].y) + (h1[r].x + h1[r].y)) * 0.0625f;
-      const ScalePairs s = k4_scales(hdr[r], g);
-      const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hdr[r].x));
-      acc[r] += dm.x * (s.sa * Sl + s.sb * Sh) - dm.y * (s.ma * Xl + s.mb * Xh);
-    }
+    for (int v = 0; v < NU; ++v)
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        const float Sl = (l0[v][r].x + l0[v][r].y) + (l1[v][r].x + l1[v][r].y);
+        const float Sh = ((h0[v][r].x + h0[v][r].y) + (h1[v][r].x + h1[v][r].y)) * 0.0625f;
+        const ScalePairs s = k4_scales(hdr[v][r], g);
+        const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hdr[v][r].x));
+        acc[r] += dm.x * (s.sa * Sl + s.sb * Sh) - dm.y * (s.ma * Xl[v] + s.mb * Xh[v]);
+      }
   }
 };
 
 template <>
 struct Unit<SI_GGML_TYPE_Q5_K> {
-  template <int NR>
+  template <int NR, int NU = 1>
   __device__ __forceinline__ static void run(const uint8_t* const* blk, const float* xs,
-                                             const float* xsum, uint32_t b, int l4, float* acc) {
+                                             const float* xsum, const uint32_t* bb, int l4,
+                                             float* acc) {
+    const uint32_t b = bb[0];
     const int g = l4;
     const float* xp = xs + xi<6>(b * 256 + g * 64);
     const float Xl = xsum[b * 8 + g * 2], Xh = xsum[b * 8 + g * 2 + 1];
@@ -217,9 +244,11 @@ struct Unit<SI_GGML_TYPE_Q5_K> {
 
 template <>
 struct Unit<SI_GGML_TYPE_Q6_K> {
-  template <int NR>
+  template <int NR, int NU = 1>
   __device__ __forceinline__ static void run(const uint8_t* const* blk, const float* xs,
-                                             const float* xsum, uint32_t b, int l4, float* acc) {
+                                             const float* xsum, const uint32_t* bb, int l4,
+                                             float* acc) {
+    const uint32_t b = bb[0];
     const int h = l4 >> 1, i0 = (l4 & 1) * 16;
     const uint32_t e0 = b * 256 + 128 * h + i0;
     const float* xp = xs + xi<7>(e0);
@@ -268,6 +297,9 @@ struct Unit<SI_GGML_TYPE_Q6_K> {
 // Launch geometry (computed on the host).
 // ---------------------------------------------------------------------------
 struct QmvGeom {
+  uint32_t debug;         // experiment switch (0 in production)
+  uint32_t mode;          // 0 single row, 1 SwiGLU pair, 2 two independent rows
+  uint32_t items;         // work items (mode 2: row pairs)
   uint32_t piece_blocks;  // super-blocks per staged piece (multiple of 4)
   uint32_t npieces;       // pieces per row
   uint32_t slot_bytes;    // bytes of one slot (NR rows)
@@ -277,28 +309,54 @@ struct QmvGeom {
   uint32_t xs_floats;     // padded x length
 };
 
-__device__ __forceinline__ void row_src(const QmvParams& p, uint32_t item, uint32_t rb, int which,
-                                        const uint8_t** g, float** y, const float** resid,
-                                        uint32_t* row) {
-  if (p.pair) {
-    *g = p.seg[which].w + size_t(item) * rb;
-    *y = p.seg[0].y;
-    *resid = p.seg[0].resid;
-    *row = item;
-    return;
+struct SegSm {
+  const uint8_t* w;
+  float* y;
+  const float* resid;
+  uint32_t rows;
+};
+
+// Row `which` (0..NR-1) of work item `item`: pair mode = gate/up row `item`;
+// dual mode = rows 2*item and 2*item+1 (the odd tail repeats its row and
+// skips the second store); single mode = row `item`. Segments (grouped
+// matvec) are looked up in the shared-memory table.
+struct RowRef {
+  const uint8_t* g;
+  float* y;
+  const float* resid;
+  uint32_t row;
+  bool store;
+};
+
+__device__ __forceinline__ RowRef row_ref(const SegSm* seg, uint32_t nseg, uint32_t mode,
+                                          uint32_t total, uint32_t item, uint32_t rb, int which) {
+  RowRef r;
+  r.store = true;
+  if (mode == 1) {  // SwiGLU pair
+    r.g = seg[which].w + size_t(item) * rb;
+    r.y = seg[0].y;
+    r.resid = seg[0].resid;
+    r.row = item;
+    return r;
   }
-  uint32_t r = item;
-  int k = 0;
-#pragma unroll
-  for (int i = 0; i < 3; ++i)
-    if (k < int(p.nseg) - 1 && r >= p.seg[k].rows) {
-      r -= p.seg[k].rows;
-      ++k;
+  uint32_t v = item;
+  if (mode == 2) {
+    v = 2 * item + uint32_t(which);
+    if (v >= total) {
+      v = total - 1;
+      r.store = false;
     }
-  *g = p.seg[k].w + size_t(r) * rb;
-  *y = p.seg[k].y;
-  *resid = p.seg[k].resid;
-  *row = r;
+  }
+  uint32_t k = 0;
+  while (k + 1 < nseg && v >= seg[k].rows) {
+    v -= seg[k].rows;
+    ++k;
+  }
+  r.g = seg[k].w + size_t(v) * rb;
+  r.y = seg[k].y;
+  r.resid = seg[k].resid;
+  r.row = v;
+  return r;
 }
 
 __device__ __forceinline__ void consumer_sync() {
@@ -316,9 +374,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_abort;
   __shared__ float s_red[kConsumerWarps];
+  __shared__ SegSm s_seg[4];
   constexpr uint32_t BB = Fmt<TYPE>::BB;
   constexpr uint32_t PAD = Fmt<TYPE>::kPad;
 
+  TS(0);
+  if (G.debug & 32) return;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + G.nslots;
   const uint32_t cols = p.cols;
@@ -329,78 +390,84 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t nb = cols / 256;
   const uint32_t rb = nb * BB;
-  const uint32_t i0 = uint32_t(uint64_t(blockIdx.x) * p.items / gridDim.x);
-  const uint32_t i1 = uint32_t(uint64_t(blockIdx.x + 1) * p.items / gridDim.x);
+  const uint32_t i0 = uint32_t(uint64_t(blockIdx.x) * G.items / gridDim.x);
+  const uint32_t i1 = uint32_t(uint64_t(blockIdx.x + 1) * G.items / gridDim.x);
   const uint32_t n_items = i1 - i0;
   const uint32_t T = G.teams, M = G.per_team, NP = G.npieces, P = G.piece_blocks;
+  const uint32_t nseg = p.nseg, mode = G.mode, total = p.items;
 
-  if (threadIdx.x == 0) {
-    for (uint32_t s = 0; s < G.nslots; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    s_abort = 0;
-    fence_barrier_init();
+  for (uint32_t s = threadIdx.x; s < G.nslots; s += blockDim.x) {
+    mbar_init(&full[s], 1);
+    mbar_init(&empty[s], 1);
   }
+  if (threadIdx.x < 4) {
+    const uint32_t k = threadIdx.x;
+    s_seg[k].w = p.seg[k].w;
+    s_seg[k].y = p.seg[k].y;
+    s_seg[k].resid = p.seg[k].resid;
+    s_seg[k].rows = p.seg[k].rows;
+  }
+  if (threadIdx.x == 0) s_abort = 0;
+  fence_barrier_init();
   __syncthreads();
   pdl_launch_dependents();
+  TS(1);
+  if (G.debug & 64) return;
 
   if (warp == kConsumerWarps) {
-    // ---------------- producer: one elected lane streams row pieces --------
-    if (lane == 0) {
+    // ---------------- producer warp: lane t streams team t's row pieces -----
+    // Each lane issues its own team's copies, so up to 32 bulk copies leave
+    // per warp instruction and no team waits behind another team's slot.
+    const uint32_t t = uint32_t(lane);
+    if (t < T && t < n_items && !(G.debug & 2)) {
       const uint64_t pol = l2_policy_evict_first();
-      const uint32_t rounds = NP * ((n_items + T - 1) / T);
+      uint32_t issued = 0, pc = 0, rl = t, si = 0, round = 0;
       bool abort = false;
-      uint32_t last_j = 0;
-      for (uint32_t j = 0; j < rounds && !abort; ++j) {
-        for (uint32_t t = 0; t < T; ++t) {
-          const uint32_t rl = t + T * (j / NP);
-          if (rl >= n_items) continue;
-          const uint32_t s = t * M + j % M, n = j / M;
-          if (n > 0 && !mbar_wait_bounded(&empty[s], (n - 1) & 1)) {
-            atomicOr(p.err, KERR_TIMEOUT_EMPTY);
-            s_abort = 1;
-            abort = true;
-            break;
-          }
-          if (*reinterpret_cast<volatile int*>(&s_abort)) {
-            abort = true;
-            break;
-          }
-          const uint32_t pc = j % NP;
-          const uint32_t b0 = pc * P, pb = min(P, nb - b0);
-          uintptr_t a0[NR], a1[NR];
-          uint32_t tx = 0;
-#pragma unroll
-          for (int w = 0; w < NR; ++w) {
-            const uint8_t* g;
-            float* y;
-            const float* rs;
-            uint32_t row;
-            row_src(p, i0 + rl, rb, w, &g, &y, &rs, &row);
-            const uintptr_t a = reinterpret_cast<uintptr_t>(g) + uintptr_t(b0) * BB;
-            a0[w] = a & ~uintptr_t(15);
-            a1[w] = (a + uintptr_t(pb) * BB + 15) & ~uintptr_t(15);
-            tx += uint32_t(a1[w] - a0[w]);
-          }
-          mbar_arrive_expect_tx(&full[s], tx);
-          uint8_t* dst = slots + size_t(s) * G.slot_bytes;
-#pragma unroll
-          for (int w = 0; w < NR; ++w)
-            bulk_g2s(dst + w * G.row_slot, reinterpret_cast<const void*>(a0[w]), uint32_t(a1[w] - a0[w]),
-                     &full[s], pol);
+      while (rl < n_items) {
+        const uint32_t s = t * M + si;
+        if (round > 0 && !mbar_wait_bounded(&empty[s], (round - 1) & 1)) {
+          atomicOr(p.err, KERR_TIMEOUT_EMPTY);
+          s_abort = 1;
+          abort = true;
+          break;
         }
-        last_j = j;
+        if (*reinterpret_cast<volatile int*>(&s_abort)) {
+          abort = true;
+          break;
+        }
+        const uint32_t b0 = pc * P, pb = min(P, nb - b0);
+        uintptr_t a0[NR], a1[NR];
+        uint32_t tx = 0;
+#pragma unroll
+        for (int w = 0; w < NR; ++w) {
+          const RowRef rr = row_ref(s_seg, nseg, mode, total, i0 + rl, rb, w);
+          const uintptr_t a = reinterpret_cast<uintptr_t>(rr.g) + uintptr_t(b0) * BB;
+          a0[w] = a & ~uintptr_t(15);
+          a1[w] = (a + uintptr_t(pb) * BB + 15) & ~uintptr_t(15);
+          tx += uint32_t(a1[w] - a0[w]);
+        }
+        mbar_arrive_expect_tx(&full[s], tx);
+        uint8_t* dst = slots + size_t(s) * G.slot_bytes;
+#pragma unroll
+        for (int w = 0; w < NR; ++w)
+          bulk_g2s(dst + w * G.row_slot, reinterpret_cast<const void*>(a0[w]), uint32_t(a1[w] - a0[w]),
+                   &full[s], pol);
+        ++issued;
+        if (++pc == NP) {
+          pc = 0;
+          rl += T;
+        }
+        if (++si == M) {
+          si = 0;
+          ++round;
+        }
       }
       if (abort) {
-        // Drain: wait (bounded) for the copies still in flight in every slot.
-        for (uint32_t t = 0; t < T; ++t)
-          for (uint32_t q = 0; q < M && q <= last_j; ++q) {
-            const uint32_t j = last_j - q;
-            const uint32_t rl = t + T * (j / NP);
-            if (rl >= n_items) continue;
-            if (!mbar_wait_bounded(&full[t * M + j % M], (j / M) & 1)) atomicOr(p.err, KERR_TIMEOUT_DRAIN);
-          }
+        // Drain: wait (bounded) for this team's copies still in flight.
+        for (uint32_t q = 0; q < M && q < issued; ++q) {
+          const uint32_t j = issued - 1 - q;
+          if (!mbar_wait_bounded(&full[t * M + j % M], (j / M) & 1)) atomicOr(p.err, KERR_TIMEOUT_DRAIN);
+        }
       }
     }
     return;
@@ -408,25 +475,42 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---------------- consumers: build x (padded layout) in shared memory ----
   pdl_wait();
+  TS(2);
   const int ct = threadIdx.x;
   constexpr int NC = kConsumerWarps * 32;
-  if (p.xmode == XM_RAW) {
-    for (uint32_t i = ct * 4; i < cols; i += NC * 4)
-      *reinterpret_cast<float4*>(xs + xi<PAD>(i)) = *reinterpret_cast<const float4*>(p.x + i);
-  } else if (p.xmode == XM_RMS1P) {
+  if (G.debug & 4) {
+  } else if (p.xmode == XM_RAW || p.xmode == XM_RMS1P) {
+    // all loads of a chunk are issued before any store (latency overlap)
     float ss = 0.f;
-    for (uint32_t i = ct * 4; i < cols; i += NC * 4) {
-      const float4 v = *reinterpret_cast<const float4*>(p.x + i);
-      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) s_red[warp] = ss;
-    consumer_sync();
-    float tot = 0.f;
+    for (uint32_t base = ct * 4; base < cols; base += NC * 4 * 4) {
+      float4 v[4];
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) tot += s_red[w];
-    const float inv = 1.0f / sqrtf(tot / float(cols) + p.eps);
-    for (uint32_t i = ct; i < cols; i += NC) xs[xi<PAD>(i)] = p.x[i] * inv * (1.0f + p.xw[i]);
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t i = base + q * NC * 4;
+        v[q] = i < cols ? *reinterpret_cast<const float4*>(p.x + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t i = base + q * NC * 4;
+        if (i < cols) {
+          *reinterpret_cast<float4*>(xs + xi<PAD>(i)) = v[q];
+          ss += v[q].x * v[q].x + v[q].y * v[q].y + v[q].z * v[q].z + v[q].w * v[q].w;
+        }
+      }
+    }
+    if (p.xmode == XM_RMS1P) {
+      ss = warp_sum(ss);
+      if (lane == 0) s_red[warp] = ss;
+      consumer_sync();
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) tot += s_red[w];
+      const float inv = 1.0f / sqrtf(tot / float(cols) + p.eps);
+      for (uint32_t i = ct; i < cols; i += NC) {
+        const uint32_t k = xi<PAD>(i);
+        xs[k] = xs[k] * inv * (1.0f + p.xw[i]);
+      }
+    }
   } else if (p.xmode == XM_GATED) {
     const uint32_t hd = p.head_dim, heads = cols / hd;
     for (uint32_t h = warp; h < heads; h += kConsumerWarps) {
@@ -462,6 +546,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     xsum[j] = t;
   }
   consumer_sync();
+  TS(3);
 
   // ---------------- consumers: pieces of rows, per-team private slots ------
   const uint32_t team = uint32_t(ct) >> 4;
@@ -471,11 +556,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   float acc[NR];
 #pragma unroll
   for (int w = 0; w < NR; ++w) acc[w] = 0.f;
-  for (uint32_t j = 0;; ++j) {
-    const uint32_t rl = team + T * (j / NP);
-    if (rl >= n_items) break;
-    const uint32_t pc = j % NP, s = team * M + j % M, n = j / M;
-    if (!mbar_wait_bounded(&full[s], n & 1)) {
+  uint32_t pc = 0, rl = team, si = 0, round = 0;
+  while (rl < n_items) {
+    const uint32_t s = team * M + si;
+    if (!(G.debug & 2) && !mbar_wait_bounded(&full[s], round & 1)) {
       atomicOr(p.err, KERR_TIMEOUT_FULL);
       s_abort = 1;
       break;
@@ -485,48 +569,51 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint8_t* rowp[NR];
 #pragma unroll
     for (int w = 0; w < NR; ++w) {
-      const uint8_t* g;
-      float* y;
-      const float* rs;
-      uint32_t row;
-      row_src(p, i0 + rl, rb, w, &g, &y, &rs, &row);
-      rowp[w] = base + w * G.row_slot + ((reinterpret_cast<uintptr_t>(g) + uintptr_t(b0) * BB) & 15);
+      const RowRef rr = row_ref(s_seg, nseg, mode, total, i0 + rl, rb, w);
+      rowp[w] = base + w * G.row_slot + ((reinterpret_cast<uintptr_t>(rr.g) + uintptr_t(b0) * BB) & 15);
     }
-    const uint32_t units = pb * 4;
+    const uint32_t units = (G.debug & 1) ? 0 : pb * 4;
     for (uint32_t u = tl; u < units; u += kTeamLanes) {
       const uint8_t* blk[NR];
 #pragma unroll
       for (int w = 0; w < NR; ++w) blk[w] = rowp[w] + (u >> 2) * BB;
-      Unit<TYPE>::template run<NR>(blk, xs, xsum, b0 + (u >> 2), tl & 3, acc);
+      const uint32_t bb[1] = {b0 + (u >> 2)};
+      Unit<TYPE>::template run<NR, 1>(blk, xs, xsum, bb, tl & 3, acc);
     }
     __syncwarp(tmask);
     if (tl == 0) mbar_arrive(&empty[s]);
-    if (pc == NP - 1) {
+    if (++pc == NP) {
 #pragma unroll
       for (int w = 0; w < NR; ++w) {
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) acc[w] += __shfl_xor_sync(tmask, acc[w], o);
       }
       if (tl == 0) {
-        const uint8_t* g;
-        float* y;
-        const float* rs;
-        uint32_t row;
-        row_src(p, i0 + rl, rb, 0, &g, &y, &rs, &row);
-        float out;
-        if (NR == 2) {
+        if (mode == 1) {
+          const RowRef rr = row_ref(s_seg, nseg, mode, total, i0 + rl, rb, 0);
           const float gv = acc[0];
-          out = gv / (1.0f + expf(-gv)) * acc[NR - 1];
+          float out = gv / (1.0f + expf(-gv)) * acc[NR - 1];
+          if (rr.resid) out = rr.resid[rr.row] + out;
+          rr.y[rr.row] = out;
         } else {
-          out = acc[0];
+#pragma unroll
+          for (int w = 0; w < NR; ++w) {
+            const RowRef rr = row_ref(s_seg, nseg, mode, total, i0 + rl, rb, w);
+            if (rr.store) rr.y[rr.row] = rr.resid ? rr.resid[rr.row] + acc[w] : acc[w];
+          }
         }
-        if (rs) out = rs[row] + out;
-        y[row] = out;
       }
 #pragma unroll
       for (int w = 0; w < NR; ++w) acc[w] = 0.f;
+      pc = 0;
+      rl += T;
+    }
+    if (++si == M) {
+      si = 0;
+      ++round;
     }
   }
+  TS(4);
 }
 
 template <uint32_t TYPE, int NR>
@@ -541,6 +628,9 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
   if (P < 4) P = 4;
   if (nb <= P) P = nb;
   G.piece_blocks = P;
+  G.mode = p.pair ? 1u : (NR == 2 ? 2u : 0u);
+  G.items = G.mode == 2 ? (p.items + 1) / 2 : p.items;
+  if (const char* dbg = getenv("SI_QMV_DEBUG")) G.debug = uint32_t(atoi(dbg));
   G.npieces = (nb + P - 1) / P;
   G.row_slot = (P * BB + 32 + 127) & ~127u;
   G.slot_bytes = G.row_slot * NR;
@@ -565,7 +655,7 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
     max_dyn = limit;
   }
   // largest slot count that fits, then teams with >= 2 private slots each
-  uint32_t nslots = kMaxSlots, total = 0;
+  uint32_t nslots = (G.debug & 8) ? 24 : kMaxSlots, total = 0;
   for (; nslots >= 2; --nslots) {
     G.slots_off = (16 * nslots + xbytes + 127) & ~127u;
     total = G.slots_off + nslots * G.slot_bytes;
@@ -580,7 +670,7 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
   G.nslots = G.teams * G.per_team;
   G.slots_off = (16 * G.nslots + xbytes + 127) & ~127u;
   total = G.slots_off + G.nslots * G.slot_bytes;
-  const uint32_t grid = p.items < uint32_t(sm_count) ? p.items : uint32_t(sm_count);
+  const uint32_t grid = G.items < uint32_t(sm_count) ? G.items : uint32_t(sm_count);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
@@ -590,7 +680,7 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = (pdl && !(G.debug & 16)) ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, qmv_kernel<TYPE, NR>, p, G);
   if (e != cudaSuccess) {
     if (msg) *msg = std::string("matvec launch: ") + cudaGetErrorString(e);
@@ -599,6 +689,11 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
   return SI_OK;
 }
 
+}  // namespace si
+extern "C" int si_debug_qmv_ts(unsigned long long* out) {
+  return cudaMemcpyFromSymbol(out, si::g_qmv_ts, sizeof(si::g_qmv_ts)) == cudaSuccess ? 0 : -2;
+}
+namespace si {
 int launch_qmv(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
                std::string* msg) {
   if (p.cols == 0 || p.cols % 256 || p.cols > kQmvMaxCols || p.items == 0 || p.nseg == 0 ||
@@ -611,10 +706,12 @@ int launch_qmv(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
     return SI_E_INVALID;
   }
   const bool pair = p.pair != 0;
+  const char* dv = getenv("SI_QMV_DUAL");
+  const bool dual = dv && dv[0] == '1';
   switch (p.type) {
     case SI_GGML_TYPE_Q4_K:
-      return pair ? launch_t<SI_GGML_TYPE_Q4_K, 2>(p, stream, sm_count, pdl, msg)
-                  : launch_t<SI_GGML_TYPE_Q4_K, 1>(p, stream, sm_count, pdl, msg);
+      return (pair || dual) ? launch_t<SI_GGML_TYPE_Q4_K, 2>(p, stream, sm_count, pdl, msg)
+                            : launch_t<SI_GGML_TYPE_Q4_K, 1>(p, stream, sm_count, pdl, msg);
     case SI_GGML_TYPE_Q5_K:
       return pair ? launch_t<SI_GGML_TYPE_Q5_K, 2>(p, stream, sm_count, pdl, msg)
                   : launch_t<SI_GGML_TYPE_Q5_K, 1>(p, stream, sm_count, pdl, msg);
