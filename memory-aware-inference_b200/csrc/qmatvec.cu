@@ -33,15 +33,17 @@
 
 namespace si {
 
-__device__ unsigned long long g_qmv_ts[16];
+__device__ unsigned long long g_qmv_ts[32];
 __device__ __forceinline__ unsigned long long gtime() {
   unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  t = clock64();
   return t;
 }
 #define TS(i) if ((G.debug & 128) && blockIdx.x == 0 && threadIdx.x == 0) g_qmv_ts[i] = gtime();
 
-constexpr int kConsumerWarps = 16;
+// 15 consumer warps + 1 producer = 16 warps: 4 per scheduler, so each thread
+// may use up to 128 registers (a 17th warp would cap them at 96 and spill).
+constexpr int kConsumerWarps = 15;
 constexpr int kThreads = kConsumerWarps * 32 + 32;
 constexpr int kMaxTeams = kConsumerWarps * 2;
 constexpr int kTeamLanes = 16;
@@ -144,63 +146,76 @@ __device__ __forceinline__ ScalePairs k4_scales(const uint4& hdr, int g) {
 template <uint32_t TYPE>
 struct Unit;
 
+__device__ __forceinline__ uint32_t dp4a_uu(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Q4_K with integer sub-block dot products. x is held per 32-element
+// sub-block j as X_i = rint(x_i * 2^(22-e_j)) (|X| < 2^22, the block's
+// largest element keeps a full 23-bit significand) split into three byte
+// planes (two unsigned, the top one signed); sum_i q_i X_i is computed exactly
+// with dp4a (int32, no overflow: 32 * 240 * 255 < 2^31) and scaled back by
+// 2^(e_j-22) in fp32. The quants of one x load serve NR rows.
 template <>
 struct Unit<SI_GGML_TYPE_Q4_K> {
-  // NU independent units (blocks b[0..NU)) of NR rows, interleaved for ILP.
   template <int NR, int NU = 1>
   __device__ __forceinline__ static void run(const uint8_t* const* blk, const float* xs,
                                              const float* xsum, const uint32_t* bb, int l4,
-                                             float* acc) {
+                                             float* acc, uint32_t nsub) {
     const int g = l4;
-    const float* xp[NU];
-    float Xl[NU], Xh[NU];
-    uint4 hdr[NU][NR], qa[NU][NR], qb[NU][NR];
+    const uint32_t b = bb[0];
+    const uint4* xq = reinterpret_cast<const uint4*>(xs) + (68 * b + 17 * g);
+    uint4 hdr[NR], qa[NR], qb[NR];
 #pragma unroll
-    for (int v = 0; v < NU; ++v) {
-      xp[v] = xs + xi<6>(bb[v] * 256 + g * 64);
-      Xl[v] = xsum[bb[v] * 8 + g * 2];
-      Xh[v] = xsum[bb[v] * 8 + g * 2 + 1];
-#pragma unroll
-      for (int r = 0; r < NR; ++r) {
-        const uint8_t* bp = blk[v * NR + r];
-        hdr[v][r] = lds128(bp);
-        qa[v][r] = lds128(bp + 16 + 32 * g);
-        qb[v][r] = lds128(bp + 32 + 32 * g);
-      }
+    for (int r = 0; r < NR; ++r) {
+      hdr[r] = lds128(blk[r]);
+      qa[r] = lds128(blk[r] + 16 + 32 * g);
+      qb[r] = lds128(blk[r] + 32 + 32 * g);
     }
-    float2 l0[NU][NR], l1[NU][NR], h0[NU][NR], h1[NU][NR];
+    uint32_t l0[NR][2], l1[NR][2], h0[NR][2], h1[NR][2];
+    int l2[NR][2], h2[NR][2];
 #pragma unroll
-    for (int v = 0; v < NU; ++v)
+    for (int r = 0; r < NR; ++r)
 #pragma unroll
-      for (int r = 0; r < NR; ++r) l0[v][r] = l1[v][r] = h0[v][r] = h1[v][r] = make_float2(0.f, 0.f);
+      for (int c = 0; c < 2; ++c) l0[r][c] = l1[r][c] = h0[r][c] = h1[r][c] = 0u, l2[r][c] = h2[r][c] = 0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-#pragma unroll
-      for (int v = 0; v < NU; ++v) {
-        const float4 xl = *reinterpret_cast<const float4*>(xp[v] + 4 * k);
-        const float4 xh = *reinterpret_cast<const float4*>(xp[v] + 32 + 4 * k);
-#pragma unroll
-        for (int r = 0; r < NR; ++r) {
-          const uint32_t w = word_of(k < 4 ? qa[v][r] : qb[v][r], k & 3);
-          const uint32_t lo = w & 0x0F0F0F0Fu;  // q
-          const uint32_t hi = w & 0xF0F0F0F0u;  // 16 q
-          l0[v][r] = __ffma2_rn(int_pair(lo, 0), make_float2(xl.x, xl.y), l0[v][r]);
-          l1[v][r] = __ffma2_rn(int_pair(lo, 2), make_float2(xl.z, xl.w), l1[v][r]);
-          h0[v][r] = __ffma2_rn(int_pair(hi, 0), make_float2(xh.x, xh.y), h0[v][r]);
-          h1[v][r] = __ffma2_rn(int_pair(hi, 2), make_float2(xh.z, xh.w), h1[v][r]);
-        }
-      }
-    }
-#pragma unroll
-    for (int v = 0; v < NU; ++v)
+      const int c = k & 1;
+      const uint4 xl = xq[k], xh = xq[8 + k];
 #pragma unroll
       for (int r = 0; r < NR; ++r) {
-        const float Sl = (l0[v][r].x + l0[v][r].y) + (l1[v][r].x + l1[v][r].y);
-        const float Sh = ((h0[v][r].x + h0[v][r].y) + (h1[v][r].x + h1[v][r].y)) * 0.0625f;
-        const ScalePairs s = k4_scales(hdr[v][r], g);
-        const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hdr[v][r].x));
-        acc[r] += dm.x * (s.sa * Sl + s.sb * Sh) - dm.y * (s.ma * Xl[v] + s.mb * Xh[v]);
+        const uint32_t w = word_of(k < 4 ? qa[r] : qb[r], k & 3);
+        const uint32_t lo = w & 0x0F0F0F0Fu;  // q
+        const uint32_t hi = w & 0xF0F0F0F0u;  // 16 q
+        l0[r][c] = dp4a_uu(lo, xl.x, l0[r][c]);
+        l1[r][c] = dp4a_uu(lo, xl.y, l1[r][c]);
+        l2[r][c] = dp4a_us(lo, xl.z, l2[r][c]);
+        h0[r][c] = dp4a_uu(hi, xh.x, h0[r][c]);
+        h1[r][c] = dp4a_uu(hi, xh.y, h1[r][c]);
+        h2[r][c] = dp4a_us(hi, xh.z, h2[r][c]);
       }
+    }
+    const float Xl = xsum[b * 8 + g * 2], Xh = xsum[b * 8 + g * 2 + 1];
+    const float* sc = xsum + nsub;
+    const float sl = sc[b * 8 + g * 2], shs = sc[b * 8 + g * 2 + 1] * 0.0625f;
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      const uint32_t L0 = l0[r][0] + l0[r][1], L1 = l1[r][0] + l1[r][1];
+      const uint32_t H0 = h0[r][0] + h0[r][1], H1 = h1[r][0] + h1[r][1];
+      const int L2 = l2[r][0] + l2[r][1], H2 = h2[r][0] + h2[r][1];
+      const float Sl = (float(L2) * 65536.0f + float(int(L1 * 256u + L0))) * sl;
+      const float Sh = (float(H2) * 65536.0f + float(int(H1 * 256u + H0))) * shs;
+      const ScalePairs s = k4_scales(hdr[r], g);
+      const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hdr[r].x));
+      acc[r] += dm.x * (s.sa * Sl + s.sb * Sh) - dm.y * (s.ma * Xl + s.mb * Xh);
+    }
   }
 };
 
@@ -209,7 +224,7 @@ struct Unit<SI_GGML_TYPE_Q5_K> {
   template <int NR, int NU = 1>
   __device__ __forceinline__ static void run(const uint8_t* const* blk, const float* xs,
                                              const float* xsum, const uint32_t* bb, int l4,
-                                             float* acc) {
+                                             float* acc, uint32_t /*nsub*/) {
     const uint32_t b = bb[0];
     const int g = l4;
     const float* xp = xs + xi<6>(b * 256 + g * 64);
@@ -247,7 +262,7 @@ struct Unit<SI_GGML_TYPE_Q6_K> {
   template <int NR, int NU = 1>
   __device__ __forceinline__ static void run(const uint8_t* const* blk, const float* xs,
                                              const float* xsum, const uint32_t* bb, int l4,
-                                             float* acc) {
+                                             float* acc, uint32_t /*nsub*/) {
     const uint32_t b = bb[0];
     const int h = l4 >> 1, i0 = (l4 & 1) * 16;
     const uint32_t e0 = b * 256 + 128 * h + i0;
@@ -299,6 +314,8 @@ struct Unit<SI_GGML_TYPE_Q6_K> {
 struct QmvGeom {
   uint32_t debug;         // experiment switch (0 in production)
   uint32_t mode;          // 0 single row, 1 SwiGLU pair, 2 two independent rows
+  uint32_t merge;         // adjacent row pairs may be staged by one copy
+  uint32_t team_lanes;    // 16 or 32 lanes per team
   uint32_t items;         // work items (mode 2: row pairs)
   uint32_t piece_blocks;  // super-blocks per staged piece (multiple of 4)
   uint32_t npieces;       // pieces per row
@@ -346,6 +363,13 @@ __device__ __forceinline__ RowRef row_ref(const SegSm* seg, uint32_t nseg, uint3
       v = total - 1;
       r.store = false;
     }
+  }
+  if (nseg == 1) {
+    r.g = seg[0].w + size_t(v) * rb;
+    r.y = seg[0].y;
+    r.resid = seg[0].resid;
+    r.row = v;
+    return r;
   }
   uint32_t k = 0;
   while (k + 1 < nseg && v >= seg[k].rows) {
@@ -408,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     s_seg[k].rows = p.seg[k].rows;
   }
   if (threadIdx.x == 0) s_abort = 0;
-  fence_barrier_init();
+  if (threadIdx.x < G.nslots) fence_barrier_init();
   __syncthreads();
   pdl_launch_dependents();
   TS(1);
@@ -422,6 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (t < T && t < n_items && !(G.debug & 2)) {
       const uint64_t pol = l2_policy_evict_first();
       uint32_t issued = 0, pc = 0, rl = t, si = 0, round = 0;
+      uintptr_t prow[NR];
       bool abort = false;
       while (rl < n_items) {
         const uint32_t s = t * M + si;
@@ -437,21 +462,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint32_t b0 = pc * P, pb = min(P, nb - b0);
         uintptr_t a0[NR], a1[NR];
+        static_assert(NR <= 2, "two rows per slot at most");
         uint32_t tx = 0;
 #pragma unroll
         for (int w = 0; w < NR; ++w) {
-          const RowRef rr = row_ref(s_seg, nseg, mode, total, i0 + rl, rb, w);
-          const uintptr_t a = reinterpret_cast<uintptr_t>(rr.g) + uintptr_t(b0) * BB;
+          if (pc == 0) prow[w] = reinterpret_cast<uintptr_t>(row_ref(s_seg, nseg, mode, total, i0 + rl, rb, w).g);
+          const uintptr_t a = prow[w] + uintptr_t(b0) * BB;
           a0[w] = a & ~uintptr_t(15);
           a1[w] = (a + uintptr_t(pb) * BB + 15) & ~uintptr_t(15);
           tx += uint32_t(a1[w] - a0[w]);
         }
-        mbar_arrive_expect_tx(&full[s], tx);
         uint8_t* dst = slots + size_t(s) * G.slot_bytes;
+        if (NR == 2 && G.merge && a1[0] == a0[NR - 1]) {
+          // two adjacent rows land as one copy (row 1 at dst + row_slot = rb)
+          mbar_arrive_expect_tx(&full[s], uint32_t(a1[NR - 1] - a0[0]));
+          bulk_g2s(dst, reinterpret_cast<const void*>(a0[0]), uint32_t(a1[NR - 1] - a0[0]), &full[s], pol);
+        } else {
+          mbar_arrive_expect_tx(&full[s], tx);
 #pragma unroll
-        for (int w = 0; w < NR; ++w)
-          bulk_g2s(dst + w * G.row_slot, reinterpret_cast<const void*>(a0[w]), uint32_t(a1[w] - a0[w]),
-                   &full[s], pol);
+          for (int w = 0; w < NR; ++w)
+            bulk_g2s(dst + w * G.row_slot, reinterpret_cast<const void*>(a0[w]), uint32_t(a1[w] - a0[w]),
+                     &full[s], pol);
+        }
         ++issued;
         if (++pc == NP) {
           pc = 0;
@@ -536,61 +568,110 @@ __global__ void __launch_bounds__(kThreads, 1)
   consumer_sync();
   constexpr uint32_t SUM = Fmt<TYPE>::kSum;
   for (uint32_t j = ct; j < cols / SUM; j += NC) {
-    const float* q = xs + xi<PAD>(SUM * j);
-    float t = 0.f;
+    float* q = xs + xi<PAD>(SUM * j);
+    float4 v[SUM / 4];
+    float t = 0.f, m = 0.f;
 #pragma unroll
-    for (uint32_t i = 0; i < SUM; i += 4) {
-      const float4 v = *reinterpret_cast<const float4*>(q + i);
-      t += (v.x + v.y) + (v.z + v.w);
+    for (uint32_t i = 0; i < SUM / 4; ++i) {
+      v[i] = *reinterpret_cast<const float4*>(q + 4 * i);
+      t += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
     }
     xsum[j] = t;
+    if (TYPE == SI_GGML_TYPE_Q4_K) {
+      // x as 24-bit fixed point per 32-element sub-block: X = rint(x * 2^(22-e))
+      // with m < 2^e, |X| <= 2^22, X = b2 * 65536 + b1 * 256 + b0; each group of
+      // 4 floats is overwritten in place by {b0 x4, b1 x4, b2 x4 (signed), 0}.
+      // e is clamped to [-100, 129] so 2^(22-e) and 2^(e-22) are normal floats
+      // (a smaller e only lowers the resolution floor below 2^-122).
+      int ex = int((__float_as_uint(m) >> 23) & 0xffu) - 126;
+      ex = ex < -100 ? -100 : (ex > 129 ? 129 : ex);
+      xsum[cols / 32 + j] = __uint_as_float(uint32_t(ex + 105) << 23);
+      const float mul = __uint_as_float(uint32_t(149 - ex) << 23);
+#pragma unroll
+      for (uint32_t i = 0; i < SUM / 4; ++i) {
+        const uint32_t X0 = uint32_t(__float2int_rn(v[i].x * mul)), X1 = uint32_t(__float2int_rn(v[i].y * mul));
+        const uint32_t X2 = uint32_t(__float2int_rn(v[i].z * mul)), X3 = uint32_t(__float2int_rn(v[i].w * mul));
+        uint4 o;
+        o.x = __byte_perm(__byte_perm(X0, X1, 0x0040u), __byte_perm(X2, X3, 0x0040u), 0x5410u);
+        o.y = __byte_perm(__byte_perm(X0, X1, 0x0051u), __byte_perm(X2, X3, 0x0051u), 0x5410u);
+        o.z = __byte_perm(__byte_perm(X0, X1, 0x0062u), __byte_perm(X2, X3, 0x0062u), 0x5410u);
+        o.w = 0u;
+        *reinterpret_cast<uint4*>(q + 4 * i) = o;
+      }
+    }
   }
   consumer_sync();
   TS(3);
 
   // ---------------- consumers: pieces of rows, per-team private slots ------
-  const uint32_t team = uint32_t(ct) >> 4;
-  const int tl = ct & 15;
+  const uint32_t TL = G.team_lanes;
+  const uint32_t team = uint32_t(ct) / TL;
+  const int tl = int(uint32_t(ct) % TL);
   if (team >= T) return;
-  const unsigned tmask = (lane < 16) ? 0x0000ffffu : 0xffff0000u;
+  const unsigned tmask = TL == 32 ? 0xffffffffu : ((lane < 16) ? 0x0000ffffu : 0xffff0000u);
   float acc[NR];
 #pragma unroll
   for (int w = 0; w < NR; ++w) acc[w] = 0.f;
-  uint32_t pc = 0, rl = team, si = 0, round = 0;
+  uint32_t pc = 0, rl = team, si = 0, round = 0, dbg_it = 0;
+  RowRef rows_g[NR];
+#pragma unroll
+  for (int w = 0; w < NR; ++w) rows_g[w] = RowRef{nullptr, nullptr, nullptr, 0u, false};
   while (rl < n_items) {
+    if (dbg_it < 10) { TS(5 + dbg_it); }
+    ++dbg_it;
     const uint32_t s = team * M + si;
     if (!(G.debug & 2) && !mbar_wait_bounded(&full[s], round & 1)) {
       atomicOr(p.err, KERR_TIMEOUT_FULL);
       s_abort = 1;
       break;
     }
+    if (dbg_it <= 2) { TS(16 + 4 * (dbg_it - 1)); }
     const uint32_t b0 = pc * P, pb = min(P, nb - b0);
     const uint8_t* base = slots + size_t(s) * G.slot_bytes;
+    if (pc == 0 && !(G.debug & 512)) {
+#pragma unroll
+      for (int w = 0; w < NR; ++w) rows_g[w] = row_ref(s_seg, nseg, mode, total, i0 + rl, rb, w);
+    }
     const uint8_t* rowp[NR];
 #pragma unroll
-    for (int w = 0; w < NR; ++w) {
-      const RowRef rr = row_ref(s_seg, nseg, mode, total, i0 + rl, rb, w);
-      rowp[w] = base + w * G.row_slot + ((reinterpret_cast<uintptr_t>(rr.g) + uintptr_t(b0) * BB) & 15);
-    }
+    for (int w = 0; w < NR; ++w)
+      rowp[w] = base + w * G.row_slot + ((reinterpret_cast<uintptr_t>(rows_g[w].g) + uintptr_t(b0) * BB) & 15);
     const uint32_t units = (G.debug & 1) ? 0 : pb * 4;
-    for (uint32_t u = tl; u < units; u += kTeamLanes) {
+    for (uint32_t u = tl; u < units; u += TL) {
       const uint8_t* blk[NR];
 #pragma unroll
       for (int w = 0; w < NR; ++w) blk[w] = rowp[w] + (u >> 2) * BB;
       const uint32_t bb[1] = {b0 + (u >> 2)};
-      Unit<TYPE>::template run<NR, 1>(blk, xs, xsum, bb, tl & 3, acc);
+      Unit<TYPE>::template run<NR, 1>(blk, xs, xsum, bb, tl & 3, acc, cols / 32);
     }
+    if (dbg_it <= 2) { TS(17 + 4 * (dbg_it - 1)); }
     __syncwarp(tmask);
     if (tl == 0) mbar_arrive(&empty[s]);
+    if (dbg_it <= 2) { TS(18 + 4 * (dbg_it - 1)); }
     if (++pc == NP) {
+      if (NR == 2) {
+        // transposed reduction: one exchange leaves row (lane & 1) in every
+        // lane, then a single butterfly over the remaining lanes
+        const bool odd = lane & 1;
+        const float send = odd ? acc[0] : acc[NR - 1];
+        const float keep = odd ? acc[NR - 1] : acc[0];
+        float v = keep + __shfl_xor_sync(tmask, send, 1);
+        if (TL == 32) v += __shfl_xor_sync(0xffffffffu, v, 16);
+        v += __shfl_xor_sync(tmask, v, 8);
+        v += __shfl_xor_sync(tmask, v, 4);
+        v += __shfl_xor_sync(tmask, v, 2);
+        const float other = __shfl_xor_sync(tmask, v, 1);
+        acc[0] = odd ? other : v;
+        acc[NR - 1] = odd ? v : other;
+      } else {
+        if (TL == 32) acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 16);
 #pragma unroll
-      for (int w = 0; w < NR; ++w) {
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) acc[w] += __shfl_xor_sync(tmask, acc[w], o);
+        for (int o = 8; o > 0; o >>= 1) acc[0] += __shfl_xor_sync(tmask, acc[0], o);
       }
-      if (tl == 0) {
+      if (tl == 0 && !(G.debug & 256)) {
         if (mode == 1) {
-          const RowRef rr = row_ref(s_seg, nseg, mode, total, i0 + rl, rb, 0);
+          const RowRef& rr = rows_g[0];
           const float gv = acc[0];
           float out = gv / (1.0f + expf(-gv)) * acc[NR - 1];
           if (rr.resid) out = rr.resid[rr.row] + out;
@@ -598,7 +679,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
 #pragma unroll
           for (int w = 0; w < NR; ++w) {
-            const RowRef rr = row_ref(s_seg, nseg, mode, total, i0 + rl, rb, w);
+            const RowRef& rr = rows_g[w];
             if (rr.store) rr.y[rr.row] = rr.resid ? rr.resid[rr.row] + acc[w] : acc[w];
           }
         }
@@ -608,6 +689,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       pc = 0;
       rl += T;
     }
+    if (dbg_it <= 2) { TS(19 + 4 * (dbg_it - 1)); }
     if (++si == M) {
       si = 0;
       ++round;
@@ -633,9 +715,15 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
   if (const char* dbg = getenv("SI_QMV_DEBUG")) G.debug = uint32_t(atoi(dbg));
   G.npieces = (nb + P - 1) / P;
   G.row_slot = (P * BB + 32 + 127) & ~127u;
+  // whole 16-byte-aligned rows in one piece: a row pair can be one copy
+  if (NR == 2 && G.npieces == 1 && (nb * BB) % 16 == 0 && G.mode == 2 && !getenv("SI_QMV_NOMERGE")) {
+    G.merge = 1;
+    G.row_slot = nb * BB;
+  }
   G.slot_bytes = G.row_slot * NR;
   G.xs_floats = p.cols + 4 * (p.cols >> PAD);
-  const uint32_t xbytes = 4 * (G.xs_floats + p.cols / Fmt<TYPE>::kSum);
+  const uint32_t xbytes = 4 * (G.xs_floats + p.cols / Fmt<TYPE>::kSum +
+                                (TYPE == SI_GGML_TYPE_Q4_K ? p.cols / 32 : 0));
   static uint32_t max_dyn = 0;
   if (max_dyn == 0) {
     int dev = 0, optin = 0;
@@ -666,6 +754,11 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
     return SI_E_UNSUPPORTED;
   }
   G.teams = nslots / 2 < uint32_t(kMaxTeams) ? nslots / 2 : uint32_t(kMaxTeams);
+  G.team_lanes = kTeamLanes;
+  if (G.teams <= uint32_t(kConsumerWarps) + 2) {  // one warp per team
+    G.team_lanes = 32;
+    G.teams = G.teams < uint32_t(kConsumerWarps) ? G.teams : uint32_t(kConsumerWarps);
+  }
   G.per_team = nslots / G.teams;
   G.nslots = G.teams * G.per_team;
   G.slots_off = (16 * G.nslots + xbytes + 127) & ~127u;
@@ -710,8 +803,8 @@ int launch_qmv(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
   const bool dual = dv && dv[0] == '1';
   switch (p.type) {
     case SI_GGML_TYPE_Q4_K:
-      return (pair || dual) ? launch_t<SI_GGML_TYPE_Q4_K, 2>(p, stream, sm_count, pdl, msg)
-                            : launch_t<SI_GGML_TYPE_Q4_K, 1>(p, stream, sm_count, pdl, msg);
+      (void)dual;
+      return launch_t<SI_GGML_TYPE_Q4_K, 2>(p, stream, sm_count, pdl, msg);
     case SI_GGML_TYPE_Q5_K:
       return pair ? launch_t<SI_GGML_TYPE_Q5_K, 2>(p, stream, sm_count, pdl, msg)
                   : launch_t<SI_GGML_TYPE_Q5_K, 1>(p, stream, sm_count, pdl, msg);
