@@ -24,6 +24,7 @@
 //    32-element partial sums. Epilogues: store, residual add, SwiGLU pair.
 //  * Accumulation is fp32 throughout; team results are combined with
 //    warp shuffles. Tensor cores are not used: batch-1 is not a contraction.
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -33,17 +34,12 @@
 
 namespace si {
 
-__device__ unsigned long long g_qmv_ts[32];
-__device__ __forceinline__ unsigned long long gtime() {
-  unsigned long long t;
-  t = clock64();
-  return t;
-}
-#define TS(i) if ((G.debug & 128) && blockIdx.x == 0 && threadIdx.x == 0) g_qmv_ts[i] = gtime();
-
-// 15 consumer warps + 1 producer = 16 warps: 4 per scheduler, so each thread
-// may use up to 128 registers (a 17th warp would cap them at 96 and spill).
-constexpr int kConsumerWarps = 15;
+// Two CTAs per SM, each 7 consumer warps + 1 producer: 16 warps per SM (4 per
+// scheduler, up to 128 registers per thread). While one CTA of a kernel
+// drains, a CTA of the next kernel in the stream (programmatic dependent
+// launch) already initialises and prefetches its weights in the other half.
+constexpr int kCtasPerSm = 2;
+constexpr int kConsumerWarps = 7;
 constexpr int kThreads = kConsumerWarps * 32 + 32;
 constexpr int kMaxTeams = kConsumerWarps * 2;
 constexpr int kTeamLanes = 16;
@@ -165,56 +161,62 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
 // 2^(e_j-22) in fp32. The quants of one x load serve NR rows.
 template <>
 struct Unit<SI_GGML_TYPE_Q4_K> {
+  // NU independent units (blocks bb[0..NU)) of NR rows each; one x load
+  // serves the NR rows. blk[v * NR + r] is unit v of row r.
   template <int NR, int NU = 1>
   __device__ __forceinline__ static void run(const uint8_t* const* blk, const float* xs,
                                              const float* xsum, const uint32_t* bb, int l4,
                                              float* acc, uint32_t nsub) {
     const int g = l4;
-    const uint32_t b = bb[0];
-    const uint4* xq = reinterpret_cast<const uint4*>(xs) + (68 * b + 17 * g);
-    uint4 hdr[NR], qa[NR], qb[NR];
+    uint4 hdr[NU][NR], qa[NU][NR], qb[NU][NR];
 #pragma unroll
-    for (int r = 0; r < NR; ++r) {
-      hdr[r] = lds128(blk[r]);
-      qa[r] = lds128(blk[r] + 16 + 32 * g);
-      qb[r] = lds128(blk[r] + 32 + 32 * g);
-    }
-    uint32_t l0[NR][2], l1[NR][2], h0[NR][2], h1[NR][2];
-    int l2[NR][2], h2[NR][2];
-#pragma unroll
-    for (int r = 0; r < NR; ++r)
-#pragma unroll
-      for (int c = 0; c < 2; ++c) l0[r][c] = l1[r][c] = h0[r][c] = h1[r][c] = 0u, l2[r][c] = h2[r][c] = 0;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int c = k & 1;
-      const uint4 xl = xq[k], xh = xq[8 + k];
+    for (int v = 0; v < NU; ++v)
 #pragma unroll
       for (int r = 0; r < NR; ++r) {
-        const uint32_t w = word_of(k < 4 ? qa[r] : qb[r], k & 3);
-        const uint32_t lo = w & 0x0F0F0F0Fu;  // q
-        const uint32_t hi = w & 0xF0F0F0F0u;  // 16 q
-        l0[r][c] = dp4a_uu(lo, xl.x, l0[r][c]);
-        l1[r][c] = dp4a_uu(lo, xl.y, l1[r][c]);
-        l2[r][c] = dp4a_us(lo, xl.z, l2[r][c]);
-        h0[r][c] = dp4a_uu(hi, xh.x, h0[r][c]);
-        h1[r][c] = dp4a_uu(hi, xh.y, h1[r][c]);
-        h2[r][c] = dp4a_us(hi, xh.z, h2[r][c]);
+        hdr[v][r] = lds128(blk[v * NR + r]);
+        qa[v][r] = lds128(blk[v * NR + r] + 16 + 32 * g);
+        qb[v][r] = lds128(blk[v * NR + r] + 32 + 32 * g);
+      }
+    uint32_t l0[NU][NR], l1[NU][NR], h0[NU][NR], h1[NU][NR];
+    int l2[NU][NR], h2[NU][NR];
+#pragma unroll
+    for (int v = 0; v < NU; ++v)
+#pragma unroll
+      for (int r = 0; r < NR; ++r) l0[v][r] = l1[v][r] = h0[v][r] = h1[v][r] = 0u, l2[v][r] = h2[v][r] = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+#pragma unroll
+      for (int v = 0; v < NU; ++v) {
+        const uint4* xq = reinterpret_cast<const uint4*>(xs) + (68 * bb[v] + 17 * g);
+        const uint4 xl = xq[k], xh = xq[8 + k];
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+          const uint32_t w = word_of(k < 4 ? qa[v][r] : qb[v][r], k & 3);
+          const uint32_t lo = w & 0x0F0F0F0Fu;  // q
+          const uint32_t hi = w & 0xF0F0F0F0u;  // 16 q
+          l0[v][r] = dp4a_uu(lo, xl.x, l0[v][r]);
+          l1[v][r] = dp4a_uu(lo, xl.y, l1[v][r]);
+          l2[v][r] = dp4a_us(lo, xl.z, l2[v][r]);
+          h0[v][r] = dp4a_uu(hi, xh.x, h0[v][r]);
+          h1[v][r] = dp4a_uu(hi, xh.y, h1[v][r]);
+          h2[v][r] = dp4a_us(hi, xh.z, h2[v][r]);
+        }
       }
     }
-    const float Xl = xsum[b * 8 + g * 2], Xh = xsum[b * 8 + g * 2 + 1];
-    const float* sc = xsum + nsub;
-    const float sl = sc[b * 8 + g * 2], shs = sc[b * 8 + g * 2 + 1] * 0.0625f;
 #pragma unroll
-    for (int r = 0; r < NR; ++r) {
-      const uint32_t L0 = l0[r][0] + l0[r][1], L1 = l1[r][0] + l1[r][1];
-      const uint32_t H0 = h0[r][0] + h0[r][1], H1 = h1[r][0] + h1[r][1];
-      const int L2 = l2[r][0] + l2[r][1], H2 = h2[r][0] + h2[r][1];
-      const float Sl = (float(L2) * 65536.0f + float(int(L1 * 256u + L0))) * sl;
-      const float Sh = (float(H2) * 65536.0f + float(int(H1 * 256u + H0))) * shs;
-      const ScalePairs s = k4_scales(hdr[r], g);
-      const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hdr[r].x));
-      acc[r] += dm.x * (s.sa * Sl + s.sb * Sh) - dm.y * (s.ma * Xl + s.mb * Xh);
+    for (int v = 0; v < NU; ++v) {
+      const uint32_t b = bb[v];
+      const float Xl = xsum[b * 8 + g * 2], Xh = xsum[b * 8 + g * 2 + 1];
+      const float* sc = xsum + nsub;
+      const float sl = sc[b * 8 + g * 2], shs = sc[b * 8 + g * 2 + 1] * 0.0625f;
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        const float Sl = (float(l2[v][r]) * 65536.0f + float(int(l1[v][r] * 256u + l0[v][r]))) * sl;
+        const float Sh = (float(h2[v][r]) * 65536.0f + float(int(h1[v][r] * 256u + h0[v][r]))) * shs;
+        const ScalePairs s = k4_scales(hdr[v][r], g);
+        const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&hdr[v][r].x));
+        acc[r] += dm.x * (s.sa * Sl + s.sb * Sh) - dm.y * (s.ma * Xl + s.mb * Xh);
+      }
     }
   }
 };
@@ -312,7 +314,6 @@ struct Unit<SI_GGML_TYPE_Q6_K> {
 // Launch geometry (computed on the host).
 // ---------------------------------------------------------------------------
 struct QmvGeom {
-  uint32_t debug;         // experiment switch (0 in production)
   uint32_t mode;          // 0 single row, 1 SwiGLU pair, 2 two independent rows
   uint32_t merge;         // adjacent row pairs may be staged by one copy
   uint32_t team_lanes;    // 16 or 32 lanes per team
@@ -346,7 +347,8 @@ struct RowRef {
 };
 
 __device__ __forceinline__ RowRef row_ref(const SegSm* seg, uint32_t nseg, uint32_t mode,
-                                          uint32_t total, uint32_t item, uint32_t rb, int which) {
+                                          uint32_t total, uint32_t item, uint32_t rb, int which,
+                                          uint32_t nr) {
   RowRef r;
   r.store = true;
   if (mode == 1) {  // SwiGLU pair
@@ -358,7 +360,7 @@ __device__ __forceinline__ RowRef row_ref(const SegSm* seg, uint32_t nseg, uint3
   }
   uint32_t v = item;
   if (mode == 2) {
-    v = 2 * item + uint32_t(which);
+    v = nr * item + uint32_t(which);
     if (v >= total) {
       v = total - 1;
       r.store = false;
@@ -393,7 +395,7 @@ __device__ __forceinline__ void consumer_sync() {
 // team waits on a slot's full barrier, strictly in round order, so a waiter
 // is never more than one phase ahead of the barrier.
 template <uint32_t TYPE, int NR>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     qmv_kernel(const __grid_constant__ QmvParams p, const __grid_constant__ QmvGeom G) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_abort;
@@ -402,8 +404,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t BB = Fmt<TYPE>::BB;
   constexpr uint32_t PAD = Fmt<TYPE>::kPad;
 
-  TS(0);
-  if (G.debug & 32) return;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + G.nslots;
   const uint32_t cols = p.cols;
@@ -435,15 +435,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x < G.nslots) fence_barrier_init();
   __syncthreads();
   pdl_launch_dependents();
-  TS(1);
-  if (G.debug & 64) return;
 
   if (warp == kConsumerWarps) {
     // ---------------- producer warp: lane t streams team t's row pieces -----
     // Each lane issues its own team's copies, so up to 32 bulk copies leave
     // per warp instruction and no team waits behind another team's slot.
     const uint32_t t = uint32_t(lane);
-    if (t < T && t < n_items && !(G.debug & 2)) {
+    if (t < T && t < n_items) {
       const uint64_t pol = l2_policy_evict_first();
       uint32_t issued = 0, pc = 0, rl = t, si = 0, round = 0;
       uintptr_t prow[NR];
@@ -462,19 +460,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint32_t b0 = pc * P, pb = min(P, nb - b0);
         uintptr_t a0[NR], a1[NR];
-        static_assert(NR <= 2, "two rows per slot at most");
+        static_assert(NR <= 4, "four rows per slot at most");
         uint32_t tx = 0;
 #pragma unroll
         for (int w = 0; w < NR; ++w) {
-          if (pc == 0) prow[w] = reinterpret_cast<uintptr_t>(row_ref(s_seg, nseg, mode, total, i0 + rl, rb, w).g);
+          if (pc == 0) prow[w] = reinterpret_cast<uintptr_t>(row_ref(s_seg, nseg, mode, total, i0 + rl, rb, w, NR).g);
           const uintptr_t a = prow[w] + uintptr_t(b0) * BB;
           a0[w] = a & ~uintptr_t(15);
           a1[w] = (a + uintptr_t(pb) * BB + 15) & ~uintptr_t(15);
           tx += uint32_t(a1[w] - a0[w]);
         }
         uint8_t* dst = slots + size_t(s) * G.slot_bytes;
-        if (NR == 2 && G.merge && a1[0] == a0[NR - 1]) {
-          // two adjacent rows land as one copy (row 1 at dst + row_slot = rb)
+        bool adjacent = NR > 1 && G.merge;
+#pragma unroll
+        for (int w = 0; w + 1 < NR; ++w) adjacent = adjacent && (a1[w] == a0[w + 1]);
+        if (adjacent) {
+          // adjacent rows land as one copy (row w at dst + w * row_slot, row_slot = rb)
           mbar_arrive_expect_tx(&full[s], uint32_t(a1[NR - 1] - a0[0]));
           bulk_g2s(dst, reinterpret_cast<const void*>(a0[0]), uint32_t(a1[NR - 1] - a0[0]), &full[s], pol);
         } else {
@@ -507,11 +508,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---------------- consumers: build x (padded layout) in shared memory ----
   pdl_wait();
-  TS(2);
   const int ct = threadIdx.x;
   constexpr int NC = kConsumerWarps * 32;
-  if (G.debug & 4) {
-  } else if (p.xmode == XM_RAW || p.xmode == XM_RMS1P) {
+  if (p.xmode == XM_RAW || p.xmode == XM_RMS1P) {
     // all loads of a chunk are issued before any store (latency overlap)
     float ss = 0.f;
     for (uint32_t base = ct * 4; base < cols; base += NC * 4 * 4) {
@@ -602,7 +601,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   consumer_sync();
-  TS(3);
 
   // ---------------- consumers: pieces of rows, per-team private slots ------
   const uint32_t TL = G.team_lanes;
@@ -613,42 +611,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   float acc[NR];
 #pragma unroll
   for (int w = 0; w < NR; ++w) acc[w] = 0.f;
-  uint32_t pc = 0, rl = team, si = 0, round = 0, dbg_it = 0;
+  uint32_t pc = 0, rl = team, si = 0, round = 0;
   RowRef rows_g[NR];
 #pragma unroll
   for (int w = 0; w < NR; ++w) rows_g[w] = RowRef{nullptr, nullptr, nullptr, 0u, false};
   while (rl < n_items) {
-    if (dbg_it < 10) { TS(5 + dbg_it); }
-    ++dbg_it;
     const uint32_t s = team * M + si;
-    if (!(G.debug & 2) && !mbar_wait_bounded(&full[s], round & 1)) {
+    if (!mbar_wait_bounded(&full[s], round & 1)) {
       atomicOr(p.err, KERR_TIMEOUT_FULL);
       s_abort = 1;
       break;
     }
-    if (dbg_it <= 2) { TS(16 + 4 * (dbg_it - 1)); }
     const uint32_t b0 = pc * P, pb = min(P, nb - b0);
     const uint8_t* base = slots + size_t(s) * G.slot_bytes;
-    if (pc == 0 && !(G.debug & 512)) {
+    if (pc == 0) {
 #pragma unroll
-      for (int w = 0; w < NR; ++w) rows_g[w] = row_ref(s_seg, nseg, mode, total, i0 + rl, rb, w);
+      for (int w = 0; w < NR; ++w) rows_g[w] = row_ref(s_seg, nseg, mode, total, i0 + rl, rb, w, NR);
     }
     const uint8_t* rowp[NR];
 #pragma unroll
     for (int w = 0; w < NR; ++w)
       rowp[w] = base + w * G.row_slot + ((reinterpret_cast<uintptr_t>(rows_g[w].g) + uintptr_t(b0) * BB) & 15);
-    const uint32_t units = (G.debug & 1) ? 0 : pb * 4;
-    for (uint32_t u = tl; u < units; u += TL) {
+    const uint32_t units = pb * 4;
+    uint32_t u = tl;
+    if (TYPE == SI_GGML_TYPE_Q4_K && NR <= 2) {
+      for (; u + TL < units; u += 2 * TL) {
+        const uint8_t* blk[2 * NR];
+        const uint32_t bb[2] = {b0 + (u >> 2), b0 + ((u + TL) >> 2)};
+#pragma unroll
+        for (int w = 0; w < NR; ++w) {
+          blk[w] = rowp[w] + (u >> 2) * BB;
+          blk[NR + w] = rowp[w] + ((u + TL) >> 2) * BB;
+        }
+        Unit<TYPE>::template run<NR, 2>(blk, xs, xsum, bb, tl & 3, acc, cols / 32);
+      }
+    }
+    for (; u < units; u += TL) {
       const uint8_t* blk[NR];
 #pragma unroll
       for (int w = 0; w < NR; ++w) blk[w] = rowp[w] + (u >> 2) * BB;
       const uint32_t bb[1] = {b0 + (u >> 2)};
       Unit<TYPE>::template run<NR, 1>(blk, xs, xsum, bb, tl & 3, acc, cols / 32);
     }
-    if (dbg_it <= 2) { TS(17 + 4 * (dbg_it - 1)); }
     __syncwarp(tmask);
     if (tl == 0) mbar_arrive(&empty[s]);
-    if (dbg_it <= 2) { TS(18 + 4 * (dbg_it - 1)); }
     if (++pc == NP) {
       if (NR == 2) {
         // transposed reduction: one exchange leaves row (lane & 1) in every
@@ -664,12 +670,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float other = __shfl_xor_sync(tmask, v, 1);
         acc[0] = odd ? other : v;
         acc[NR - 1] = odd ? v : other;
+      } else if (NR == 4) {
+        // transposed reduction of four rows: after two exchanges lane l holds
+        // row (l & 3); the butterfly then sums over the remaining lanes
+        const bool b0s = lane & 1, b1s = lane & 2;
+        const float a = (b0s ? acc[1] : acc[0]) + __shfl_xor_sync(tmask, b0s ? acc[0] : acc[1], 1);
+        const float c = (b0s ? acc[NR - 1] : acc[2]) + __shfl_xor_sync(tmask, b0s ? acc[2] : acc[NR - 1], 1);
+        float v = (b1s ? c : a) + __shfl_xor_sync(tmask, b1s ? a : c, 2);
+        if (TL == 32) v += __shfl_xor_sync(0xffffffffu, v, 16);
+        v += __shfl_xor_sync(tmask, v, 8);
+        v += __shfl_xor_sync(tmask, v, 4);
+        acc[0] = v;  // row (tl & 3)
       } else {
         if (TL == 32) acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 16);
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) acc[0] += __shfl_xor_sync(tmask, acc[0], o);
       }
-      if (tl == 0 && !(G.debug & 256)) {
+      if (NR == 4) {
+        if (tl < 4) {
+#pragma unroll
+          for (int w = 0; w < NR; ++w)
+            if (tl == w) {
+              const RowRef& rr = rows_g[w];
+              if (rr.store) rr.y[rr.row] = rr.resid ? rr.resid[rr.row] + acc[0] : acc[0];
+            }
+        }
+      } else if (tl == 0) {
         if (mode == 1) {
           const RowRef& rr = rows_g[0];
           const float gv = acc[0];
@@ -689,13 +715,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       pc = 0;
       rl += T;
     }
-    if (dbg_it <= 2) { TS(19 + 4 * (dbg_it - 1)); }
     if (++si == M) {
       si = 0;
       ++round;
     }
   }
-  TS(4);
 }
 
 template <uint32_t TYPE, int NR>
@@ -710,13 +734,12 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
   if (P < 4) P = 4;
   if (nb <= P) P = nb;
   G.piece_blocks = P;
-  G.mode = p.pair ? 1u : (NR == 2 ? 2u : 0u);
-  G.items = G.mode == 2 ? (p.items + 1) / 2 : p.items;
-  if (const char* dbg = getenv("SI_QMV_DEBUG")) G.debug = uint32_t(atoi(dbg));
+  G.mode = p.pair ? 1u : (NR >= 2 ? 2u : 0u);
+  G.items = G.mode == 2 ? (p.items + NR - 1) / NR : p.items;
   G.npieces = (nb + P - 1) / P;
   G.row_slot = (P * BB + 32 + 127) & ~127u;
   // whole 16-byte-aligned rows in one piece: a row pair can be one copy
-  if (NR == 2 && G.npieces == 1 && (nb * BB) % 16 == 0 && G.mode == 2 && !getenv("SI_QMV_NOMERGE")) {
+  if (NR >= 2 && G.npieces == 1 && (nb * BB) % 16 == 0 && G.mode == 2) {
     G.merge = 1;
     G.row_slot = nb * BB;
   }
@@ -726,9 +749,11 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
                                 (TYPE == SI_GGML_TYPE_Q4_K ? p.cols / 32 : 0));
   static uint32_t max_dyn = 0;
   if (max_dyn == 0) {
-    int dev = 0, optin = 0;
+    int dev = 0, optin = 0, per_sm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    optin = std::min(optin, per_sm / kCtasPerSm - 1024);
     cudaFuncAttributes fa = {};
     cudaFuncGetAttributes(&fa, qmv_kernel<TYPE, NR>);
     const uint32_t limit = uint32_t(optin) > uint32_t(fa.sharedSizeBytes) + 256
@@ -743,7 +768,7 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
     max_dyn = limit;
   }
   // largest slot count that fits, then teams with >= 2 private slots each
-  uint32_t nslots = (G.debug & 8) ? 24 : kMaxSlots, total = 0;
+  uint32_t nslots = kMaxSlots, total = 0;
   for (; nslots >= 2; --nslots) {
     G.slots_off = (16 * nslots + xbytes + 127) & ~127u;
     total = G.slots_off + nslots * G.slot_bytes;
@@ -763,7 +788,8 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
   G.nslots = G.teams * G.per_team;
   G.slots_off = (16 * G.nslots + xbytes + 127) & ~127u;
   total = G.slots_off + G.nslots * G.slot_bytes;
-  const uint32_t grid = G.items < uint32_t(sm_count) ? G.items : uint32_t(sm_count);
+  const uint32_t cap = uint32_t(sm_count) * kCtasPerSm;
+  const uint32_t grid = G.items < cap ? G.items : cap;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
@@ -773,7 +799,7 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = (pdl && !(G.debug & 16)) ? 1 : 0;
+  cfg.numAttrs = pdl ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, qmv_kernel<TYPE, NR>, p, G);
   if (e != cudaSuccess) {
     if (msg) *msg = std::string("matvec launch: ") + cudaGetErrorString(e);
@@ -782,11 +808,6 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
   return SI_OK;
 }
 
-}  // namespace si
-extern "C" int si_debug_qmv_ts(unsigned long long* out) {
-  return cudaMemcpyFromSymbol(out, si::g_qmv_ts, sizeof(si::g_qmv_ts)) == cudaSuccess ? 0 : -2;
-}
-namespace si {
 int launch_qmv(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
                std::string* msg) {
   if (p.cols == 0 || p.cols % 256 || p.cols > kQmvMaxCols || p.items == 0 || p.nseg == 0 ||
@@ -799,11 +820,9 @@ int launch_qmv(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
     return SI_E_INVALID;
   }
   const bool pair = p.pair != 0;
-  const char* dv = getenv("SI_QMV_DUAL");
-  const bool dual = dv && dv[0] == '1';
   switch (p.type) {
     case SI_GGML_TYPE_Q4_K:
-      (void)dual;
+      // two rows per team step share each x load (SwiGLU: gate and up rows)
       return launch_t<SI_GGML_TYPE_Q4_K, 2>(p, stream, sm_count, pdl, msg);
     case SI_GGML_TYPE_Q5_K:
       return pair ? launch_t<SI_GGML_TYPE_Q5_K, 2>(p, stream, sm_count, pdl, msg)
