@@ -185,6 +185,20 @@ typedef struct si_attention_decode_input {
 /* attention_decode (metal.rs:6915). */
 int si_attention_decode(si_ctx* ctx, const si_attention_decode_input* in, float* out);
 
+/* Allocation-free form of si_attention_decode for callers that cannot
+ * allocate device memory at call time (for example while a stream is being
+ * captured, or under a runtime that forbids cudaMalloc after start-up). No
+ * counterpart in the reference. All pointers inside `in` and `out` are
+ * DEVICE pointers; the work is enqueued on `stream` (cudaStream_t as void*,
+ * NULL = legacy default stream) and the call returns without synchronising.
+ * The split-K partials use a fixed 1 MiB array built into the library on every
+ * GPU that loads it: calls needing more (roughly qh * (hd + 2) floats per 256
+ * cached tokens) fail with SI_E_UNSUPPORTED. Calls share that array, so calls
+ * that overlap on the GPU race. The first call on a device looks up the
+ * array's address; make it before any stream capture. Errors are reported
+ * through si_global_last_error(). */
+int si_attention_decode_noalloc_dev(const si_attention_decode_input* in, float* out, void* stream);
+
 /* ---- greedy argmax (runtime.rs:4301-4309) -------------------------------- */
 /* Largest finite value under f32::total_cmp; the last index among equals. */
 int si_argmax(si_ctx* ctx, const float* logits, uint64_t n, uint32_t* index);

@@ -130,6 +130,7 @@ def lib():
         "si_rope": ([vp, vp, u64, u64, u64, f32, vp], i32),
         "si_attention_decode": ([vp, vp, vp], i32),
         "si_argmax": ([vp, vp, u64, vp], i32),
+        "si_attention_decode_noalloc_dev": ([vp, vp, vp], i32),
         "si_model_config_qwen36_27b": ([vp], None),
         "si_model_create_synthetic": ([vp, vp, u64, vp], i32),
         "si_model_destroy": ([vp], None),
@@ -440,6 +441,19 @@ class CudaContext:
 
     def dequantize_dev(self, ggml_type, w, elements, out, stream=None):
         self._ck(lib().si_dequantize_dev(self.h, ggml_type, _p(w), elements, _p(out), stream))
+
+
+def attention_decode_noalloc_dev(query, key_cache, value_cache, new_keys, new_values, query_heads,
+                                 key_value_heads, head_dim, cached_tokens, cache_capacity_tokens,
+                                 cache_type, out, stream=None):
+    """si_attention_decode_noalloc_dev: device pointers (torch tensors or
+    addresses) in and out; allocates nothing; does not synchronise."""
+    s = SiAttentionDecodeInput(_p(query), _p(key_cache), _p(value_cache), _p(new_keys), _p(new_values),
+                               query_heads, key_value_heads, head_dim, cached_tokens, cache_capacity_tokens,
+                               cache_type)
+    rc = lib().si_attention_decode_noalloc_dev(C.byref(s), _p(out), stream)
+    if rc != 0:
+        raise SiError(rc, lib().si_global_last_error().decode())
 
 
 def _label(t):
