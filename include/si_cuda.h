@@ -226,6 +226,9 @@ typedef struct si_model_config {
   uint32_t kv_capacity;                         /* KV positions per attention layer */
   uint32_t eos_token;                           /* 0xFFFFFFFF = none */
   uint32_t mlp_type, down_type, head_type;      /* ggml types of gate/up, down, output */
+  uint32_t weight_init;  /* 0: uniform quant/scale bytes (BASELINE config 1 style);
+                            1: per-sub-block scale 0..8 with min ~ offset*scale and
+                            dmin = d, so Q4_K/Q5_K rows are roughly zero-mean */
 } si_model_config;
 
 /* Residency / staging plan (qwen35_runtime.rs:1552-1733, planner.rs:174-251). */

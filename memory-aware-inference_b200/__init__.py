@@ -64,7 +64,7 @@ class SiModelConfig(C.Structure):
                 ("rope_theta", C.c_float), ("gdn_key_heads", C.c_uint32), ("gdn_value_heads", C.c_uint32),
                 ("gdn_head_dim", C.c_uint32), ("conv_kernel", C.c_uint32), ("rms_eps", C.c_float),
                 ("kv_capacity", C.c_uint32), ("eos_token", C.c_uint32), ("mlp_type", C.c_uint32),
-                ("down_type", C.c_uint32), ("head_type", C.c_uint32)]
+                ("down_type", C.c_uint32), ("head_type", C.c_uint32), ("weight_init", C.c_uint32)]
 
     def as_dict(self):
         return {k: getattr(self, k) for k, _ in self._fields_}

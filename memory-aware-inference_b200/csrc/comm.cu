@@ -33,29 +33,35 @@ static ncclResult_t wait_nccl(ncclComm_t comm, double seconds) {
   }
 }
 
+// A non-blocking communicator may return ncclInProgress from an enqueue; the
+// next call must not start before it reports success. Bounded wait (the
+// enqueue itself, not the GPU work); on timeout the communicator is aborted.
+static int settle(si_ctx* ctx, ncclResult_t r, const char* what) {
+  if (r == ncclInProgress) r = wait_nccl(ctx->comm->comm, 60.0);
+  if (r == ncclInProgress) {
+    ncclCommAbort(ctx->comm->comm);
+    delete ctx->comm;
+    ctx->comm = nullptr;
+    return fail(ctx, SI_E_TIMEOUT, std::string(what) + ": communicator did not become ready; aborted");
+  }
+  if (r != ncclSuccess) return fail(ctx, SI_E_COMM, std::string(what) + ": " + ncclGetErrorString(r));
+  return SI_OK;
+}
+
 int comm_allgather(si_ctx* ctx, const float* send, float* recv, size_t count, cudaStream_t s) {
   if (!ctx->comm) return SI_OK;
-  ncclResult_t r = ncclAllGather(send, recv, count, ncclFloat32, ctx->comm->comm, s);
-  if (r != ncclSuccess && r != ncclInProgress)
-    return fail(ctx, SI_E_COMM, std::string("ncclAllGather: ") + ncclGetErrorString(r));
-  return SI_OK;
+  return settle(ctx, ncclAllGather(send, recv, count, ncclFloat32, ctx->comm->comm, s), "ncclAllGather");
 }
 
 int comm_allreduce_sum(si_ctx* ctx, const float* send, float* recv, size_t count, cudaStream_t s) {
   if (!ctx->comm) return SI_OK;
-  ncclResult_t r = ncclAllReduce(send, recv, count, ncclFloat32, ncclSum, ctx->comm->comm, s);
-  if (r != ncclSuccess && r != ncclInProgress)
-    return fail(ctx, SI_E_COMM, std::string("ncclAllReduce: ") + ncclGetErrorString(r));
-  return SI_OK;
+  return settle(ctx, ncclAllReduce(send, recv, count, ncclFloat32, ncclSum, ctx->comm->comm, s), "ncclAllReduce");
 }
 
 int comm_allgather_u64(si_ctx* ctx, const unsigned long long* send, unsigned long long* recv,
                        cudaStream_t s) {
   if (!ctx->comm) return SI_OK;
-  ncclResult_t r = ncclAllGather(send, recv, 1, ncclUint64, ctx->comm->comm, s);
-  if (r != ncclSuccess && r != ncclInProgress)
-    return fail(ctx, SI_E_COMM, std::string("ncclAllGather(u64): ") + ncclGetErrorString(r));
-  return SI_OK;
+  return settle(ctx, ncclAllGather(send, recv, 1, ncclUint64, ctx->comm->comm, s), "ncclAllGather(u64)");
 }
 
 }  // namespace si

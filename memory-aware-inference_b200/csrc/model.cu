@@ -192,7 +192,8 @@ void shard_layer(const si_model& m, LayerLayout* L) {
 }
 
 // Generate local tensor `t` of (layer, id) into dst.
-void generate_tensor(uint64_t seed, uint32_t layer, uint32_t id, const LocalTensor& t, uint8_t* dst) {
+void generate_tensor(uint64_t seed, uint32_t layer, uint32_t id, const LocalTensor& t, uint8_t* dst,
+                     bool centered) {
   const uint64_t key = tensor_key(seed, layer, id);
   const uint64_t rb = row_bytes_of(t.type, t.cols);
   uint8_t* p = dst;
@@ -206,7 +207,10 @@ void generate_tensor(uint64_t seed, uint32_t layer, uint32_t id, const LocalTens
         fill_bytes(key, row * rb, rb, p);
         const uint32_t bb = block_bytes_of(t.type);
         const uint64_t bpr = t.cols / 256;
-        for (uint64_t b = 0; b < bpr; ++b) patch_scales(key, t.type, row * bpr + b, p + b * bb);
+        for (uint64_t b = 0; b < bpr; ++b) {
+          patch_scales(key, t.type, row * bpr + b, p + b * bb);
+          if (centered && t.type != SI_GGML_TYPE_Q6_K) center_scales(key, t.type, row * bpr + b, p + b * bb);
+        }
       }
       p += rb;
     }
@@ -384,6 +388,7 @@ extern "C" void si_model_config_qwen36_27b(si_model_config* c) {
   c->mlp_type = SI_GGML_TYPE_Q4_K;
   c->down_type = SI_GGML_TYPE_Q6_K;
   c->head_type = SI_GGML_TYPE_Q6_K;
+  c->weight_init = 1;
 }
 
 namespace {
@@ -500,7 +505,7 @@ extern "C" int si_model_create_synthetic(si_ctx* ctx, const si_model_config* cfg
     const LocalTensor& t = (w.id == SI_T_TOKEN_EMBD) ? embd : m->layout[w.layer].t[w.id];
     LocalTensor part = t;
     part.ranges = {{w.row0, w.row1}};
-    generate_tensor(seed, w.layer, w.id, part, w.dst);
+    generate_tensor(seed, w.layer, w.id, part, w.dst, c.weight_init == 1);
   });
 
   // ---- device allocations -----------------------------------------------

@@ -90,4 +90,28 @@ inline void patch_scales(uint64_t k, uint32_t type, uint64_t block, uint8_t* dst
   dst[3] = uint8_t(dm >> 8);
 }
 
+// Centered K-quant scales: every sub-block gets a scale in 0..8 and a min
+// ~ offset * scale with dmin = d (offset 7.5 for Q4_K, 15.5 for Q5_K), so the
+// dequantised row is roughly zero-mean, as in real quantised weights. The 12
+// packed bytes follow the 6-bit layout that get_scale_min reads.
+inline void center_scales(uint64_t k, uint32_t type, uint64_t block, uint8_t* dst) {
+  const uint64_t r = splitmix64((k ^ 0xA5A5A5A5A5A5A5A5ull) + block * kGolden);
+  uint8_t sc[8], mn[8];
+  const double off = type == 13u ? 15.5 : 7.5;
+  const int smax = type == 13u ? 4 : 8;
+  for (int j = 0; j < 8; ++j) {
+    sc[j] = uint8_t(((r >> (8 * j)) & 0xff) % uint64_t(smax + 1));
+    const long m = std::lround(off * sc[j]);
+    mn[j] = uint8_t(m > 63 ? 63 : m);
+  }
+  uint8_t* s = dst + 4;
+  for (int j = 0; j < 4; ++j) {
+    s[j] = uint8_t((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+    s[j + 4] = uint8_t((mn[j] & 63) | ((mn[j + 4] >> 4) << 6));
+    s[j + 8] = uint8_t((sc[j + 4] & 15) | ((mn[j + 4] & 15) << 4));
+  }
+  dst[2] = dst[0];  // dmin = d
+  dst[3] = dst[1];
+}
+
 }  // namespace si
