@@ -690,6 +690,8 @@ int si_attention_decode(si_ctx* ctx, const si_attention_decode_input* in, float*
     return fail(ctx, SI_E_UNSUPPORTED, "attention head_dim > 256 or GQA group > 8 is not supported");
   if (in->cached_tokens > in->cache_capacity_tokens)
     return fail(ctx, SI_E_INVALID, "attention cached token count exceeds cache capacity");
+  if (in->cached_tokens + 1 > kAttnMaxTokens)
+    return fail(ctx, SI_E_UNSUPPORTED, "attention over more than 1048576 tokens is not supported");
   const uint64_t esz = in->cache_type == SI_CACHE_BF16 ? 2 : 4;
   const uint64_t cache_bytes = kvh * in->cache_capacity_tokens * hd * esz;
   int rc;
@@ -700,7 +702,7 @@ int si_attention_decode(si_ctx* ctx, const si_attention_decode_input* in, float*
       (rc = h2d(ctx, ctx->in[4], in->new_values, kvh * hd * 4, "attention new values")))
     return rc;
   const uint32_t chunk = 256;
-  const uint64_t parts = attn_scratch_floats(uint32_t(qh), uint32_t(hd),
+  const uint64_t parts = attn_scratch_floats(uint32_t(qh), uint32_t(kvh), uint32_t(hd),
                                              uint32_t(in->cached_tokens + 1), chunk);
   if (!ctx->scratch.ensure(parts * 4) || !ctx->out[0].ensure(qh * hd * 4))
     return fail(ctx, SI_E_NOMEM, "attention scratch allocation failed");
@@ -720,6 +722,7 @@ int si_attention_decode(si_ctx* ctx, const si_attention_decode_input* in, float*
   a.part = ctx->scratch.as<float>();
   a.out = ctx->out[0].as<float>();
   a.chunk = chunk;
+  a.err = ctx->d_err;
   launch_attention(a, ctx->stream, false);
   if ((rc = d2h(ctx, out, ctx->out[0].p, qh * hd * 4, "attention readback"))) return rc;
   return sync_and_check(ctx, "attention command");

@@ -8,7 +8,7 @@
 // partial results live in a fixed array inside this library instead of in a
 // buffer allocated per call.
 //
-// Limits and sharing: the array holds kNoAllocPartFloats floats (1 MiB) on
+// Limits and sharing: the array holds kNoAllocPartFloats floats (4 MiB) on
 // every GPU that loads the library, for the life of the process. A call whose
 // partials would not fit is rejected. All calls on a device share the array,
 // so calls that overlap on the GPU (different streams, no ordering between
@@ -32,7 +32,7 @@ int fail(si_ctx* ctx, int code, const std::string& msg);
 
 namespace {
 
-constexpr size_t kNoAllocPartFloats = size_t(1) << 18;  // 1 MiB of partials
+constexpr size_t kNoAllocPartFloats = size_t(1) << 20;  // 4 MiB of partials
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) float g_attn_parts[kNoAllocPartFloats];
@@ -73,8 +73,10 @@ extern "C" int si_attention_decode_noalloc_dev(const si_attention_decode_input* 
     return si::fail(nullptr, SI_E_UNSUPPORTED, "attention head_dim > 256 or GQA group > 8 is not supported");
   if (in->cached_tokens > in->cache_capacity_tokens || in->cache_capacity_tokens > 0xffffffffull)
     return si::fail(nullptr, SI_E_INVALID, "attention cached token count exceeds cache capacity");
+  if (in->cached_tokens + 1 > si::kAttnMaxTokens)
+    return si::fail(nullptr, SI_E_UNSUPPORTED, "attention over more than 1048576 tokens is not supported");
   const uint32_t chunk = 256;
-  const uint64_t need = si::attn_scratch_floats(uint32_t(qh), uint32_t(hd), uint32_t(in->cached_tokens + 1), chunk);
+  const uint64_t need = si::attn_scratch_floats(uint32_t(qh), uint32_t(kvh), uint32_t(hd), uint32_t(in->cached_tokens + 1), chunk);
   if (need > kNoAllocPartFloats)
     return si::fail(nullptr, SI_E_UNSUPPORTED,
                     "attention needs " + std::to_string(need) + " scratch floats; the allocation-free entry point holds " +

@@ -6,6 +6,9 @@
 // bit-exact and the recurrence/conv match the CPU code to the last ulp of the
 // transcendentals. Reductions that the reference runs serially are done as
 // parallel trees where that is the only difference (within 1e-5 rel-L2).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -525,53 +528,548 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
   }
 }
 
-__global__ void attn_combine_kernel(const AttnArgs a, uint32_t nchunks) {
+// ---------------------------------------------------------------------------
+// Split-K decode over a bf16 head-major cache on the tensor cores.
+//
+// Grid (splits, kvh), 128 threads (4 warps), one CTA per SM. Split s of KV
+// head h owns the contiguous cached tokens [s*per, (s+1)*per) of that head.
+// Tiles of kFaTile tokens of K and V arrive by 3-D TMA (tensor map
+// {hd, n, kvh}, box {64, kFaTile, 1}, 128-byte swizzle) in a kFaStages-deep
+// shared-memory ring; rows at or beyond the cached length n lie outside the
+// map and arrive as zeros. Warp w owns rows 16w..16w+15 of every tile and
+// keeps its own online-softmax state (running max, partial sum, f32
+// accumulators), so a tile needs one CTA barrier (to recycle the stage):
+//   scores  S = Q K^T on mma.m16n8k16 (bf16 in, f32 accumulate). The A rows
+//           hold the group's queries split into two bf16 terms, q = hi + lo
+//           (rows 0..7 hi, rows 8..15 lo; |q - hi - lo| <= 2^-17 |q|), so the
+//           score of head g is C[g] + C[g+8]. K is bf16 already (exact B).
+//   softmax running max over the quad of lanes holding head g, rescale
+//           factor exp(m_old - m_new), p = exp(s - m_new).
+//   P.V     the score fragments ARE the A fragments of the next MMA: p is
+//           split hi/lo into rows g / g+8 again and multiplied by V through
+//           ldmatrix.trans, accumulating all head dims in registers.
+// The last split also scores the current token (f32 K/V) and appends it to
+// the cache as bf16. Warps merge through shared memory into the CTA's
+// partial (acc, m, l) per query head in part[split][qh][hd+2];
+// attn_merge_kernel combines the splits.
+// ---------------------------------------------------------------------------
+constexpr int kFaThreads = 128;
+constexpr int kFaWarps = kFaThreads / 32;
+constexpr int kFaTile = 16 * kFaWarps;  // tokens per staged tile (16 per warp)
+constexpr int kFaStages = 3;
+constexpr int kFaCtas = 148;            // one CTA per SM on B200
+constexpr uint32_t kFaBox = uint32_t(kFaTile) * 128u;  // one TMA box: kFaTile rows x 128 bytes
+
+__device__ __forceinline__ uint64_t umin64(uint64_t a, uint64_t b) { return a < b ? a : b; }
+
+// bf16 pair (lo element first) of round-to-nearest-even conversions.
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  return uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(lo))) |
+         (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(hi))) << 16);
+}
+// x = hi + lo in bf16: returns the hi pair and writes the lo pair.
+__device__ __forceinline__ uint32_t split_bf16x2(float x0, float x1, uint32_t& lo) {
+  const __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
+  lo = pack_bf16(x0 - __bfloat162float(h0), x1 - __bfloat162float(h1));
+  return uint32_t(__bfloat16_as_ushort(h0)) | (uint32_t(__bfloat16_as_ushort(h1)) << 16);
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// 3-D tiled TMA load (no multicast; the source is this GPU's cache).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Byte offset of (row, 16-byte chunk) inside a 128-byte-swizzled box.
+__device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t chunk) {
+  return row * 128u + ((chunk ^ (row & 7u)) << 4);
+}
+
+template <int HD, int G>
+struct FaLayout {
+  static constexpr uint32_t nbox = HD / 64;                     // boxes per K (or V) tile
+  static constexpr uint32_t stage_bytes = 2u * nbox * kFaBox;    // K boxes then V boxes
+  static constexpr uint32_t pitch = HD + 8;                      // bf16 per row of the query A matrix
+  static constexpr uint32_t qa_off = kFaStages * stage_bytes;    // bf16 [16][pitch]
+  static constexpr uint32_t qs_off = qa_off + 16 * pitch * 2;    // float [G][HD]
+  static constexpr uint32_t kn_off = qs_off + G * HD * 4;        // float [HD]
+  static constexpr uint32_t mw_off = kn_off + HD * 4;            // float m[warps][8], l[warps][8], wt[warps][8]
+  static constexpr uint32_t bar_off = (mw_off + 3 * kFaWarps * 8 * 4 + 15) & ~15u;  // u64 full[kFaStages]
+  static constexpr uint32_t bytes = bar_off + kFaStages * 8 + 1024;  // + alignment slack
+  static_assert(kFaWarps * G * HD * 4 <= kFaStages * stage_bytes, "warp merge aliases the ring");
+};
+
+template <int HD, int G>
+__global__ void __launch_bounds__(kFaThreads, 1)
+    attn_split_bf16_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                           const AttnArgs a, uint32_t nsplit) {
+  using L = FaLayout<HD, G>;
+  constexpr int KS = HD / 16;  // k-steps of the score MMA
+  constexpr int NB = HD / 8;   // 8-dim n-blocks of the P.V MMA
+  extern __shared__ __align__(1024) uint8_t fsm_raw[];
+  // 128-byte swizzled TMA destinations need 1024-byte alignment
+  uint8_t* fsm = fsm_raw + ((1024u - (smem_u32(fsm_raw) & 1023u)) & 1023u);
+  const uint32_t ring = smem_u32(fsm);
+  uint16_t* qa = reinterpret_cast<uint16_t*>(fsm + L::qa_off);
+  float* qs = reinterpret_cast<float*>(fsm + L::qs_off);
+  float* kn = reinterpret_cast<float*>(fsm + L::kn_off);
+  float* mw = reinterpret_cast<float*>(fsm + L::mw_off);  // [warps][8]
+  float* lw = mw + kFaWarps * 8;
+  float* wt = lw + kFaWarps * 8;
+  uint64_t* full = reinterpret_cast<uint64_t*>(fsm + L::bar_off);
+  float* scratch = reinterpret_cast<float*>(fsm);  // ring, reused after the last tile
+
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t hkv = blockIdx.y, split = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;  // MMA fragment row / column pair
+  const uint32_t n = a.cached;
+  const uint32_t per = uint32_t((uint64_t(n) + nsplit - 1) / nsplit);
+  const uint32_t tb = uint32_t(umin64(n, uint64_t(split) * per));
+  const uint32_t te = uint32_t(umin64(n, uint64_t(tb) + per));
+  const bool last = split + 1 == nsplit;
+  const uint32_t ntile = (te - tb + kFaTile - 1) / kFaTile;
+  float* parts = a.part;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kFaStages; ++s) mbar_init(&full[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const uint64_t pol = l2_policy_evict_first();
+  auto issue = [&](uint32_t i) {
+    const int t0 = int(tb + i * kFaTile);
+    const uint32_t st = ring + (i % kFaStages) * L::stage_bytes;
+    uint64_t* bar = &full[i % kFaStages];
+    mbar_arrive_expect_tx(bar, L::stage_bytes);
+#pragma unroll
+    for (uint32_t j = 0; j < L::nbox; ++j) {
+      tma_load_3d(st + j * kFaBox, &tk, int(j * 64), t0, int(hkv), bar, pol);
+      tma_load_3d(st + (L::nbox + j) * kFaBox, &tv, int(j * 64), t0, int(hkv), bar, pol);
+    }
+  };
+  if (threadIdx.x == 0)
+    for (uint32_t i = 0; i < ntile && i < kFaStages; ++i) issue(i);
+
+  // queries of the group (and the current key when this split holds it)
+  for (int h = warp; h < G + 1; h += kFaWarps) {
+    if (h < G)
+      prep_head(a.q + uint64_t(hkv * G + h) * HD, a.q_norm, a.rope_freq, HD, a.rotary, a.position, a.eps,
+                qs + h * HD, nullptr);
+    else if (last)
+      prep_head(a.k_new + uint64_t(hkv) * HD, a.k_norm, a.rope_freq, HD, a.rotary, a.position, a.eps, kn,
+                nullptr);
+  }
+  __syncthreads();
+  // query A matrix: row h = hi(q_h), row 8+h = lo(q_h); rows of absent heads are 0
+  for (int idx = threadIdx.x; idx < 8 * HD; idx += kFaThreads) {
+    const int h = idx / HD, d = idx % HD;
+    const float x = h < G ? qs[h * HD + d] : 0.f;
+    const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+    qa[h * L::pitch + d] = __bfloat16_as_ushort(hi);
+    qa[(8 + h) * L::pitch + d] = __bfloat16_as_ushort(__float2bfloat16_rn(x - __bfloat162float(hi)));
+  }
+  __syncthreads();
+  const uint32_t qa_lane = smem_u32(qa) + (((lane & 7) + ((lane >> 3) & 1) * 8) * L::pitch + (lane >> 4) * 8) * 2;
+
+  float m_run = -INFINITY, l_run = 0.f;
+  float acc[NB][4];
+#pragma unroll
+  for (int b = 0; b < NB; ++b)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[b][e] = 0.f;
+  const float scale = 1.0f / sqrtf(float(HD));
+  bool bad = false;
+
+  for (uint32_t i = 0; i < ntile; ++i) {
+    const uint32_t stg = i % kFaStages;
+    const bool ok = mbar_wait_bounded(&full[stg], (i / kFaStages) & 1);
+    if (__syncthreads_or(!ok)) {
+      // give up: record it, wait (bounded) for this CTA's copies in flight
+      if (threadIdx.x == 0) {
+        if (a.err) atomicOr(a.err, KERR_TIMEOUT_FULL);
+        for (uint32_t j = i; j < ntile && j < i + kFaStages; ++j)
+          if (!mbar_wait_bounded(&full[j % kFaStages], (j / kFaStages) & 1) && a.err)
+            atomicOr(a.err, KERR_TIMEOUT_DRAIN);
+      }
+      bad = true;
+      break;
+    }
+    const uint32_t kt = ring + stg * L::stage_bytes;
+    const uint32_t vt = kt + L::nbox * kFaBox;
+    const int r0 = warp * 16;
+    const int valid = int(te - (tb + i * kFaTile)) - r0;  // rows of this warp that are live
+    if (valid > 0) {
+      // scores of rows r0..r0+15: two n-blocks, even/odd k-steps on separate accumulators
+      float sc[2][2][4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int p = 0; p < 2; ++p)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sc[j][p][e] = 0.f;
+#pragma unroll
+      for (int s = 0; s < KS; s += 2) {
+        uint32_t aA[4], aB[4];
+        ldsm_x4(qa_lane + s * 32, aA);
+        ldsm_x4(qa_lane + (s + 1) * 32, aB);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          uint32_t b[4];
+          ldsm_x4(kt + (s >> 2) * kFaBox + swz(r0 + j * 8 + (lane & 7), (s & 3) * 2 + (lane >> 3)), b);
+          mma_bf16_16816(sc[j][0], aA, b[0], b[1]);
+          mma_bf16_16816(sc[j][1], aB, b[2], b[3]);
+        }
+      }
+      float sv[2][2];
+      float mt = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float v = ((sc[j][0][e] + sc[j][0][e + 2]) + (sc[j][1][e] + sc[j][1][e + 2])) * scale;
+          sv[j][e] = (j * 8 + 2 * c + e) < valid ? v : -INFINITY;
+          mt = fmaxf(mt, sv[j][e]);
+        }
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+      const float mn = fmaxf(m_run, mt);
+      const float al = expf(m_run - mn);
+      float pv[2][2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) pv[j][e] = expf(sv[j][e] - mn);
+      l_run = l_run * al + ((pv[0][0] + pv[0][1]) + (pv[1][0] + pv[1][1]));
+      m_run = mn;
+      uint32_t ap[4];
+      ap[0] = split_bf16x2(pv[0][0], pv[0][1], ap[1]);
+      ap[2] = split_bf16x2(pv[1][0], pv[1][1], ap[3]);
+      const uint32_t vrow = r0 + (lane & 7) + 8 * ((lane >> 3) & 1);
+#pragma unroll
+      for (int pb = 0; pb < NB / 2; ++pb) {
+        const uint32_t dchunk = pb * 2 + (lane >> 4);  // 8-dim chunk of the head
+        uint32_t b[4];
+        ldsm_x4_trans(vt + (dchunk >> 3) * kFaBox + swz(vrow, dchunk & 7), b);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          acc[2 * pb][e] *= al;
+          acc[2 * pb + 1][e] *= al;
+        }
+        mma_bf16_16816(acc[2 * pb], ap, b[0], b[1]);
+        mma_bf16_16816(acc[2 * pb + 1], ap, b[2], b[3]);
+      }
+    }
+    __syncthreads();  // stage free
+    if (threadIdx.x == 0 && i + kFaStages < ntile) issue(i + kFaStages);
+  }
+  if (bad) {
+    m_run = -INFINITY;
+    l_run = 0.f;
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[b][e] = 0.f;
+  }
+
+  if (last && !bad && warp == 0) {
+    // the current token: score from the prepared key, value from v_new
+    float sn = -INFINITY;
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      float d = 0.f;
+      for (int j = lane; j < HD; j += 32) d += qs[h * HD + j] * kn[j];
+      d = warp_sum(d) * scale;
+      if (g == h) sn = d;
+    }
+    if (g < G) {
+      const float mn = fmaxf(m_run, sn);
+      const float al = expf(m_run - mn), p = expf(sn - mn);
+      l_run = l_run * al + (c == 0 ? p : 0.f);
+      m_run = mn;
+      const float* vn = a.v_new + uint64_t(hkv) * HD + 2 * c;
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        acc[b][0] = fmaf(p, vn[b * 8], acc[b][0] * al);
+        acc[b][1] = fmaf(p, vn[b * 8 + 1], acc[b][1] * al);
+        acc[b][2] *= al;
+        acc[b][3] *= al;
+      }
+    }
+  }
+  if (last && a.k_cache_w && n < a.cap) {
+    for (int d = threadIdx.x; d < HD; d += kFaThreads) {
+      const uint64_t o = (uint64_t(hkv) * a.cap + n) * HD + d;
+      a.k_cache_w[o] = __bfloat16_as_ushort(__float2bfloat16_rn(kn[d]));
+      a.v_cache_w[o] = __bfloat16_as_ushort(__float2bfloat16_rn(a.v_new[uint64_t(hkv) * HD + d]));
+    }
+  }
+
+  // ---- merge the warps: partial (acc, m, l) of this split ------------------
+  float lq = l_run + __shfl_xor_sync(0xffffffffu, l_run, 1);
+  lq += __shfl_xor_sync(0xffffffffu, lq, 2);
+  __syncthreads();  // ring no longer read
+  if (g < G) {
+    if (c == 0) {
+      mw[warp * 8 + g] = m_run;
+      lw[warp * 8 + g] = lq;
+    }
+    float* dst = scratch + (warp * G + g) * HD + 2 * c;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      dst[b * 8] = acc[b][0] + acc[b][2];
+      dst[b * 8 + 1] = acc[b][1] + acc[b][3];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int h = threadIdx.x;
+    float M = -INFINITY;
+    for (int w = 0; w < kFaWarps; ++w) M = fmaxf(M, mw[w * 8 + h]);
+    float l = 0.f;
+    for (int w = 0; w < kFaWarps; ++w) {
+      const float x = mw[w * 8 + h] > -INFINITY ? expf(mw[w * 8 + h] - M) : 0.f;
+      wt[w * 8 + h] = x;
+      l += x * lw[w * 8 + h];
+    }
+    float* ph = parts + (uint64_t(split) * a.qh + hkv * G + h) * (HD + 2);
+    ph[HD] = M;
+    ph[HD + 1] = l;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < G * HD; idx += kFaThreads) {
+    const int h = idx / HD, d = idx % HD;
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kFaWarps; ++w) s = fmaf(wt[w * 8 + h], scratch[(w * G + h) * HD + d], s);
+    parts[(uint64_t(split) * a.qh + hkv * G + h) * (HD + 2) + d] = s;
+  }
+
+}
+
+// Merge split partials: out = sum_s w_s acc_s / sum_s w_s l_s with
+// w_s = exp(m_s - max m). Grid (qh, hd/32), 256 threads: lane = head dim,
+// warp w takes splits w, w+8, ...; a batch of kMergeBatch splits is loaded
+// into registers before the split maxima are known, so a merge of up to
+// kMergeBatch splits costs one round trip to L2. Fixed summation order.
+constexpr int kMergeDims = 32;
+constexpr int kMergeWarps = 8;
+constexpr int kMergePerLane = 19;
+constexpr uint32_t kMergeBatch = kMergeWarps * kMergePerLane;  // 152 splits
+constexpr uint32_t kMergeMaxSplits = 4096;
+
+__global__ void __launch_bounds__(kMergeDims * kMergeWarps) attn_merge_kernel(const AttnArgs a, uint32_t nsplit) {
+  __shared__ float sw[kMergeMaxSplits];
+  __shared__ float red[kMergeWarps][kMergeDims + 1];
+  __shared__ float rm[kMergeWarps], rl[kMergeWarps];
   pdl_launch_dependents();
   pdl_wait();
   const uint32_t qhd = blockIdx.x, hd = a.hd;
-  float M = -INFINITY;
-  for (uint32_t c = 0; c < nchunks; ++c)
-    M = fmaxf(M, a.part[(uint64_t(c) * a.qh + qhd) * (hd + 2) + hd]);
-  float L = 0.f;
-  for (uint32_t c = 0; c < nchunks; ++c) {
-    const float* ph = a.part + (uint64_t(c) * a.qh + qhd) * (hd + 2);
-    if (ph[hd] > -INFINITY) L += expf(ph[hd] - M) * ph[hd + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t d = blockIdx.y * kMergeDims + lane;
+  const bool live = d < hd;
+  const uint64_t stride = uint64_t(a.qh) * (hd + 2);
+  const float* base = a.part + uint64_t(qhd) * (hd + 2);
+  // first batch of partial values, independent of the weights
+  float x[kMergePerLane];
+#pragma unroll
+  for (int i = 0; i < kMergePerLane; ++i) {
+    const uint32_t s = warp + kMergeWarps * i;
+    x[i] = (live && s < nsplit) ? __ldcg(base + s * stride + d) : 0.f;
   }
-  for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x) {
-    float acc = 0.f;
-    for (uint32_t c = 0; c < nchunks; ++c) {
-      const float* ph = a.part + (uint64_t(c) * a.qh + qhd) * (hd + 2);
-      if (ph[hd] > -INFINITY) acc += expf(ph[hd] - M) * ph[d];
+  // split maxima and weights
+  float M = -INFINITY;
+  for (uint32_t s = threadIdx.x; s < nsplit; s += blockDim.x) {
+    const float m = __ldcg(base + s * stride + hd);
+    sw[s] = m;
+    M = fmaxf(M, m);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  if (lane == 0) rm[warp] = M;
+  __syncthreads();
+  M = rm[0];
+#pragma unroll
+  for (int w = 1; w < kMergeWarps; ++w) M = fmaxf(M, rm[w]);
+  float l = 0.f;
+  for (uint32_t s = threadIdx.x; s < nsplit; s += blockDim.x) {
+    const float m = sw[s];
+    const float w = m > -INFINITY ? expf(m - M) : 0.f;
+    sw[s] = w;
+    l += w * __ldcg(base + s * stride + hd + 1);
+  }
+  l = warp_sum(l);
+  if (lane == 0) rl[warp] = l;
+  __syncthreads();
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMergePerLane; ++i) {
+    const uint32_t s = warp + kMergeWarps * i;
+    if (s < nsplit) acc = fmaf(sw[s], x[i], acc);
+  }
+  for (uint32_t b0 = kMergeBatch; b0 < nsplit; b0 += kMergeBatch) {  // long generic-kernel caches
+#pragma unroll
+    for (int i = 0; i < kMergePerLane; ++i) {
+      const uint32_t s = b0 + warp + kMergeWarps * i;
+      x[i] = (live && s < nsplit) ? __ldcg(base + s * stride + d) : 0.f;
     }
-    a.out[uint64_t(qhd) * hd + d] = acc / L;
+#pragma unroll
+    for (int i = 0; i < kMergePerLane; ++i) {
+      const uint32_t s = b0 + warp + kMergeWarps * i;
+      if (s < nsplit) acc = fmaf(sw[s], x[i], acc);
+    }
+  }
+  red[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0) {
+    float L = 0.f, o = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMergeWarps; ++w) {
+      L += rl[w];
+      o += red[w][lane];
+    }
+    if (live) a.out[uint64_t(qhd) * hd + d] = o / L;
   }
 }
 
-uint64_t attn_scratch_floats(uint32_t qh, uint32_t hd, uint32_t total_tokens, uint32_t chunk) {
-  const uint64_t nch = (uint64_t(total_tokens) + chunk - 1) / chunk;
-  return nch * qh * (hd + 2);
+// Splits the tensor-core split kernel uses for `n` cached tokens over `kvh` heads:
+// at least one tile per split, one CTA per SM in total.
+static uint32_t fa_splits(uint32_t kvh, uint32_t n) {
+  const uint32_t by_len = (n + kFaTile - 1) / kFaTile;
+  const uint32_t by_sm = kvh >= kFaCtas ? 1u : kFaCtas / kvh;
+  return max(1u, min(by_len, by_sm));
+}
+
+uint64_t attn_scratch_floats(uint32_t qh, uint32_t kvh, uint32_t hd, uint32_t total_tokens, uint32_t chunk) {
+  const uint64_t generic = (uint64_t(total_tokens) + chunk - 1) / chunk;
+  const uint64_t fast = fa_splits(kvh ? kvh : 1, total_tokens);
+  return std::max(generic, fast) * qh * (hd + 2);
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// Tensor map over a head-major bf16 cache [kvh][cap][hd] clipped to the first
+// n tokens of every head (rows >= n read as zeros), box {64, kFaTile, 1}.
+static bool cache_tensor_map(CUtensorMap* map, const void* base, uint32_t hd, uint32_t n, uint32_t kvh,
+                             uint32_t cap) {
+  auto enc = tensor_map_encoder();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+  const cuuint64_t dims[3] = {hd, n ? n : 1u, kvh};
+  const cuuint64_t strides[2] = {cuuint64_t(hd) * 2, cuuint64_t(cap) * hd * 2};
+  const cuuint32_t box[3] = {64, uint32_t(kFaTile), 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int HD, int G>
+static void launch_fa(const CUtensorMap& tk, const CUtensorMap& tv, const AttnArgs& a, cudaLaunchConfig_t cfg,
+                      uint32_t nsplit) {
+  static bool attr_set = false;  // per instantiation; the attribute is per function
+  constexpr uint32_t smem = FaLayout<HD, G>::bytes;
+  if (!attr_set) {
+    cudaFuncSetAttribute(attn_split_bf16_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr_set = true;
+  }
+  cfg.gridDim = dim3(nsplit, a.kvh);
+  cfg.blockDim = dim3(kFaThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchKernelEx(&cfg, attn_split_bf16_kernel<HD, G>, tk, tv, a, nsplit);
+}
+
+template <int HD>
+static bool launch_fa_hd(const AttnArgs& a, const cudaLaunchConfig_t& cfg, uint32_t nsplit, uint32_t g) {
+  CUtensorMap tk, tv;
+  if (!cache_tensor_map(&tk, a.k_cache, HD, a.cached, a.kvh, a.cap) ||
+      !cache_tensor_map(&tv, a.v_cache, HD, a.cached, a.kvh, a.cap))
+    return false;
+  switch (g) {
+    case 1: launch_fa<HD, 1>(tk, tv, a, cfg, nsplit); return true;
+    case 2: launch_fa<HD, 2>(tk, tv, a, cfg, nsplit); return true;
+    case 3: launch_fa<HD, 3>(tk, tv, a, cfg, nsplit); return true;
+    case 4: launch_fa<HD, 4>(tk, tv, a, cfg, nsplit); return true;
+    case 5: launch_fa<HD, 5>(tk, tv, a, cfg, nsplit); return true;
+    case 6: launch_fa<HD, 6>(tk, tv, a, cfg, nsplit); return true;
+    case 7: launch_fa<HD, 7>(tk, tv, a, cfg, nsplit); return true;
+    case 8: launch_fa<HD, 8>(tk, tv, a, cfg, nsplit); return true;
+  }
+  return false;
 }
 
 void launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
-  // grid sized for the largest length this call can see
-  const uint32_t max_total = a.dev_pos ? a.cap + 1 : a.cached + 1;
-  const uint32_t nch = (max_total + a.chunk - 1) / a.chunk;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(nch, a.kvh);
-  cfg.blockDim = dim3(kAttnThreads);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (a.cache_bf16)
-    cudaLaunchKernelEx(&cfg, attn_partial_kernel<true>, a);
-  else
-    cudaLaunchKernelEx(&cfg, attn_partial_kernel<false>, a);
-  cfg.gridDim = dim3(a.qh);
-  cfg.blockDim = dim3(256);
-  cudaLaunchKernelEx(&cfg, attn_combine_kernel, a, nch);
+  const uint32_t g = a.qh / a.kvh;
+  uint32_t nsplit = 0;
+  // the tensor-core split kernel: bf16 cache, hd 128 or 256, group <= 8,
+  // host-known length
+  if (a.cache_bf16 && !a.dev_pos && g >= 1 && g <= 8 && (a.hd == 128 || a.hd == 256)) {
+    // programmatic launch: the kernel waits for its predecessor before it
+    // reads or writes anything
+    cfg.numAttrs = 1;
+    nsplit = fa_splits(a.kvh, a.cached);
+    if (!(a.hd == 256 ? launch_fa_hd<256>(a, cfg, nsplit, g) : launch_fa_hd<128>(a, cfg, nsplit, g))) nsplit = 0;
+  }
+  if (!nsplit) {
+    // generic kernel: any head size <= 256, f32 or bf16 cache
+    const uint32_t max_total = a.dev_pos ? a.cap + 1 : a.cached + 1;
+    nsplit = (max_total + a.chunk - 1) / a.chunk;
+    cfg.gridDim = dim3(nsplit, a.kvh);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = 0;
+    if (a.cache_bf16)
+      cudaLaunchKernelEx(&cfg, attn_partial_kernel<true>, a);
+    else
+      cudaLaunchKernelEx(&cfg, attn_partial_kernel<false>, a);
+  }
+  // the merge always overlaps its launch with the split kernel's tail
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(a.qh, (a.hd + kMergeDims - 1) / kMergeDims);
+  cfg.blockDim = dim3(kMergeDims * kMergeWarps);
+  cfg.dynamicSmemBytes = 0;
+  cudaLaunchKernelEx(&cfg, attn_merge_kernel, a, nsplit);
 }
 
 // ---------------------------------------------------------------------------

@@ -65,10 +65,16 @@ struct AttnArgs {
   int cache_bf16;
   float* part;             // scratch: chunks * qh * (hd + 2) floats
   float* out;              // [qh*hd]
-  uint32_t chunk;          // tokens per split
+  uint32_t chunk;          // tokens per split (generic kernel)
+  int* err;                // device error word for timed-out waits (may be null)
 };
-// Scratch floats the split-K attention needs for a given cache size.
-uint64_t attn_scratch_floats(uint32_t qh, uint32_t hd, uint32_t total_tokens, uint32_t chunk);
+// Longest cache (cached tokens + 1) the attention entry points accept: the
+// generic kernel's 256-token chunks times the merge kernel's split limit.
+constexpr uint64_t kAttnMaxTokens = uint64_t(4096) * 256;
+// Scratch floats the split-K attention needs for a given cache size (an upper
+// bound over both kernels launch_attention may pick).
+uint64_t attn_scratch_floats(uint32_t qh, uint32_t kvh, uint32_t hd, uint32_t total_tokens,
+                             uint32_t chunk);
 void launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 void launch_rope(const float* x, const float* freq, uint32_t heads, uint32_t hd, uint32_t pos,
                  float* out, cudaStream_t s);

@@ -240,7 +240,7 @@ int validate_config(const si_model_config& c, int n) {
   if (c.attn_kv_heads == 0 || c.attn_q_heads % c.attn_kv_heads || c.attn_head_dim > 256 ||
       c.attn_head_dim % 32 || c.attn_q_heads / c.attn_kv_heads > 8 ||
       (uint64_t(c.attn_q_heads) * c.attn_head_dim) % 256 || c.rotary_dim > c.attn_head_dim ||
-      c.rotary_dim % 2 || c.kv_capacity == 0)
+      c.rotary_dim % 2 || c.kv_capacity == 0 || c.kv_capacity + 1 > kAttnMaxTokens)
     return 3;
   if (!(c.rms_eps > 0.f) || !std::isfinite(c.rms_eps)) return 4;
   if (block_bytes_of(c.mlp_type) == 0 || block_bytes_of(c.down_type) == 0 || block_bytes_of(c.head_type) == 0)
@@ -284,7 +284,7 @@ std::vector<uint64_t> scratch_float_counts(const si_model& m) {
   const si_model_config& c = m.c;
   const uint64_t H = c.hidden, proj_l = (2ull * m.kh_l + m.vh_l) * 128;
   const uint64_t qw = uint64_t(c.attn_q_heads) * c.attn_head_dim, vw = uint64_t(c.gdn_value_heads) * 128;
-  const uint64_t part_floats = attn_scratch_floats(m.qh_l, c.attn_head_dim, c.kv_capacity + 1, 256);
+  const uint64_t part_floats = attn_scratch_floats(m.qh_l, m.kvh_l, c.attn_head_dim, c.kv_capacity + 1, 256);
   return {H, H, proj_l, uint64_t(m.vh_l) * 128, 2ull * m.vh_l, uint64_t(m.vh_l) * 128, vw, vw,
           2ull * m.qh_l * c.attn_head_dim, uint64_t(m.kvh_l) * c.attn_head_dim,
           uint64_t(m.kvh_l) * c.attn_head_dim, uint64_t(m.qh_l) * c.attn_head_dim, qw, qw,
@@ -857,6 +857,7 @@ int attn_layer(si_model* m, uint32_t l, const uint8_t* base, uint64_t position) 
   a.part = m->part;
   a.out = m->att;
   a.chunk = 256;
+  a.err = m->ctx->d_err;
   launch_attention(a, m->ctx->stream, true);
   m->cached[l]++;
   const float* att = m->att;

@@ -293,6 +293,30 @@ def test_attention_bf16_cache_config4(ctx, cached):  # BASELINE config 4 shapes
     assert rel_l2(got, ref) < TOL
 
 
+@pytest.mark.parametrize("qh,kvh,hd,cached,cap,kscale", [
+    (8, 8, 128, 63, 64, 1.0),      # group 1, one partial tile
+    (12, 4, 128, 64, 100, 1.0),    # group 3, exactly one tile
+    (20, 4, 128, 65, 65, 3.0),     # group 5, tile + 1 row, full cache
+    (16, 2, 128, 1000, 1024, 3.0),  # group 8, many splits
+    (4, 2, 256, 700, 800, 3.0),    # group 2
+    (28, 4, 256, 5000, 5001, 2.0),  # group 7, uneven splits
+    (6, 1, 256, 3, 16, 1.0),       # fewer tokens than one tile
+])
+def test_attention_bf16_bulk_kernel_shapes(ctx, qh, kvh, hd, cached, cap, kscale):
+    """Head dims 128/256 and every GQA group size through the bulk-copy split
+    kernel; large key scales move the running max between tiles."""
+    import mai_b200 as M
+    rng = np.random.default_rng(qh * 1000 + cached)
+    q = (rng.normal(0, 1, qh * hd) / 4).astype(np.float32)
+    kc = O.f32_to_bf16((kscale * rng.normal(0, 1, kvh * cap * hd)).astype(np.float32))
+    vc = O.f32_to_bf16(rng.normal(0, 1, kvh * cap * hd).astype(np.float32))
+    nk = rng.normal(0, 1, kvh * hd).astype(np.float32)
+    nv = rng.normal(0, 1, kvh * hd).astype(np.float32)
+    got = ctx.attention_decode(M.AttentionDecodeInput(q, kc, vc, nk, nv, qh, kvh, hd, cached, cap))
+    ref = O.attention_decode(q, kc, vc, nk, nv, qh, kvh, hd, cached, cap)
+    assert rel_l2(got, ref) < TOL
+
+
 def test_argmax_semantics(ctx):  # runtime.rs:4301-4309
     assert ctx.argmax([1.0, 3.0, 3.0, 2.0]) == 2
     assert ctx.argmax([np.nan, np.inf, 0.5, -np.inf]) == 2
