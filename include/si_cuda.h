@@ -191,9 +191,10 @@ int si_attention_decode(si_ctx* ctx, const si_attention_decode_input* in, float*
  * counterpart in the reference. All pointers inside `in` and `out` are
  * DEVICE pointers; the work is enqueued on `stream` (cudaStream_t as void*,
  * NULL = legacy default stream) and the call returns without synchronising.
- * The split-K partials use a fixed 1 MiB array built into the library on every
- * GPU that loads it: calls needing more (roughly qh * (hd + 2) floats per 256
- * cached tokens) fail with SI_E_UNSUPPORTED. Calls share that array, so calls
+ * The split-K partials use a fixed 4 MiB array built into the library on every
+ * GPU that loads it: calls needing more (qh * (hd + 2) floats per split; at
+ * most max(ceil((n+1)/256), min(ceil(n/64), 148/kvh)) splits for n cached
+ * tokens) fail with SI_E_UNSUPPORTED. Calls share that array, so calls
  * that overlap on the GPU race. The first call on a device looks up the
  * array's address; make it before any stream capture. Errors are reported
  * through si_global_last_error(). */

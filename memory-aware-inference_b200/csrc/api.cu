@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "comm.h"
 #include "ctx.h"
 #include "kernels.cuh"
 #include "qmatvec.cuh"
@@ -154,13 +155,11 @@ int si_ctx_create(int device, const si_ctx_config* cfg, si_ctx** out) {
   return SI_OK;
 }
 
-int si_comm_destroy_internal(si_ctx* ctx);
-
 void si_ctx_destroy(si_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
-  si_comm_destroy_internal(ctx);
+  comm_destroy(ctx);
   for (auto& b : ctx->in) b.release();
   for (auto& b : ctx->out) b.release();
   for (auto& b : ctx->wbuf) b.release();

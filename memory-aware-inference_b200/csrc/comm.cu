@@ -64,6 +64,13 @@ int comm_allgather_u64(si_ctx* ctx, const unsigned long long* send, unsigned lon
   return settle(ctx, ncclAllGather(send, recv, 1, ncclUint64, ctx->comm->comm, s), "ncclAllGather(u64)");
 }
 
+void comm_destroy(si_ctx* ctx) {
+  if (!ctx || !ctx->comm) return;
+  ncclCommDestroy(ctx->comm->comm);
+  delete ctx->comm;
+  ctx->comm = nullptr;
+}
+
 }  // namespace si
 
 extern "C" {
@@ -111,14 +118,6 @@ int si_ctx_comm_info(const si_ctx* ctx, int* nranks, int* rank) {
   if (!ctx) return SI_E_INVALID;
   if (nranks) *nranks = ctx->nranks;
   if (rank) *rank = ctx->rank;
-  return SI_OK;
-}
-
-int si_comm_destroy_internal(si_ctx* ctx) {
-  if (!ctx || !ctx->comm) return SI_OK;
-  ncclCommDestroy(ctx->comm->comm);
-  delete ctx->comm;
-  ctx->comm = nullptr;
   return SI_OK;
 }
 

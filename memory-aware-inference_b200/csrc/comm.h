@@ -10,4 +10,6 @@ int comm_allgather(si_ctx* ctx, const float* send, float* recv, size_t count, cu
 int comm_allreduce_sum(si_ctx* ctx, const float* send, float* recv, size_t count, cudaStream_t s);
 int comm_allgather_u64(si_ctx* ctx, const unsigned long long* send, unsigned long long* recv,
                        cudaStream_t s);
+// Destroy the context's communicator, if any (context teardown).
+void comm_destroy(si_ctx* ctx);
 }  // namespace si

@@ -4,26 +4,33 @@
 // (+ their rows4 variants), si_q4_k_fused_gate_up and the grouped matvec
 // (src/metal.rs:310-494, 498-587, 770-1050, 4532-4780 in the reference).
 //
-// Design (one CTA per SM, persistent over a contiguous range of rows):
-//  * A producer warp streams rows in pieces of <= ~4.5 KB (a whole 2,880 B
-//    Q4_K 5120-column row is one piece) from HBM into shared-memory slots with
-//    non-tensor bulk async copies (cp.async.bulk, L2 evict_first), tracked by
-//    full/empty mbarriers. Each team owns >= 2 private slots (double
-//    buffering), so barrier phases never alias.
-//  * 16 consumer warps = up to 32 teams of 16 lanes; a team owns one row.
-//    Lane l of a team always decodes the same 64-element unit of each
+// Design (two CTAs per SM, each persistent over a contiguous range of rows):
+//  * Each CTA has 7 consumer warps and 1 producer warp. Lane t of the
+//    producer warp issues team t's copies: rows (a whole 2,880 B Q4_K
+//    5120-column row, or an adjacent pair of rows, merged into one copy)
+//    stream from HBM into shared-memory slots with non-tensor bulk async
+//    copies (cp.async.bulk, L2 evict_first), tracked by full/empty
+//    mbarriers. Each team owns >= 2 private slots (double buffering), so
+//    barrier phases never alias.
+//  * A team is 16 (or 32) lanes and owns NR = 2 rows that share every load of
+//    x. Lane l of a team always decodes the same 64-element unit of each
 //    super-block (Q4_K/Q5_K: group l%4; Q6_K: half/16-run l%4), so the 6-bit
 //    scale/min extraction pattern is fixed per lane and never diverges.
-//  * Weights are decoded in registers: each quant q is placed in the low
-//    mantissa byte of 2^23 (PRMT, no int->float conversion pipe), 2^23 is
-//    subtracted exactly in pairs (fadd.rn.f32x2), and q*x is accumulated by
-//    packed fp32 FMA (fma.rn.f32x2). The min / -32 offsets are applied per
-//    sub-block with precomputed sub-block sums of x.
-//  * The input vector x (and an optional fused RMSNorm / gated-norm /
-//    sigmoid-gate transform of it) lives in shared memory, with its 16- and
-//    32-element partial sums. Epilogues: store, residual add, SwiGLU pair.
-//  * Accumulation is fp32 throughout; team results are combined with
-//    warp shuffles. Tensor cores are not used: batch-1 is not a contraction.
+//  * Q4_K: x is converted once per launch, in shared memory, into exact
+//    24-bit fixed-point byte planes per 32-element sub-block (scale 2^(e-22)
+//    for the sub-block's largest exponent e); each sub-block dot product is
+//    an exact integer sum of dp4a instructions on the raw nibbles, scaled back
+//    in fp32 and accumulated across sub-blocks in fp32.
+//  * Q5_K / Q6_K: each quant q is placed in the low mantissa byte of 2^23
+//    (PRMT, no int->float conversion pipe), 2^23 is subtracted exactly in
+//    pairs (fadd.rn.f32x2), and q*x is accumulated by packed fp32 FMA
+//    (fma.rn.f32x2).
+//  * The min / -32 offsets are applied per sub-block with precomputed
+//    sub-block sums of x. The input vector x (and an optional fused RMSNorm /
+//    gated-norm / sigmoid-gate transform of it) lives in shared memory.
+//    Epilogues: store, residual add, SwiGLU pair.
+//  * Team results are combined with transposed warp-shuffle reductions.
+//    Tensor cores are not used: batch-1 is not a contraction.
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
