@@ -56,17 +56,22 @@ void note_weights(si_ctx* ctx, int64_t delta) {
 int sync_and_check(si_ctx* ctx, const char* what) {
   auto t0 = std::chrono::steady_clock::now();
   ctx->submitted++;
-  cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  // the error word travels with the results: one synchronisation per call
+  cudaError_t e = cudaMemcpyAsync(ctx->h_err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   ctx->waited++;
   ctx->wait_nanos += uint64_t(std::chrono::duration_cast<std::chrono::nanoseconds>(
                                   std::chrono::steady_clock::now() - t0)
                                   .count());
+  if (e == cudaSuccess)
+    for (const auto& pc : ctx->pending) std::memcpy(pc.dst, ctx->h_stage + pc.off, pc.bytes);
+  ctx->pending.clear();
+  ctx->h_stage_used = 0;
   if (e != cudaSuccess) return cuda_fail(ctx, e, what);
-  int bits = 0;
-  e = cudaMemcpy(&bits, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+  const int bits = *ctx->h_err;
   if (bits) {
     cudaMemset(ctx->d_err, 0, sizeof(int));
+    *ctx->h_err = 0;
     return fail(ctx, bits & (KERR_TIMEOUT_FULL | KERR_TIMEOUT_EMPTY | KERR_TIMEOUT_DRAIN)
                          ? SI_E_TIMEOUT
                          : SI_E_CUDA,
@@ -85,9 +90,35 @@ static int h2d(si_ctx* ctx, DevBuf& b, const void* src, size_t bytes, const char
   return SI_OK;
 }
 
+// Device -> caller memory, completed by the next sync_and_check: through the
+// pinned staging buffer when it has room (grown while nothing is pending),
+// else directly.
 static int d2h(si_ctx* ctx, void* dst, const void* src, size_t bytes, const char* what) {
-  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream);
-  if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+  if (bytes == 0) return SI_OK;
+  const size_t need = (ctx->h_stage_used + bytes + 255) & ~size_t(255);
+  if (need > ctx->h_stage_cap && ctx->pending.empty()) {
+    if (ctx->h_stage) cudaFreeHost(ctx->h_stage);
+    ctx->h_stage = nullptr;
+    ctx->h_stage_cap = 0;
+    const size_t cap = std::max(need, size_t(1) << 20);
+    if (cudaHostAlloc(reinterpret_cast<void**>(&ctx->h_stage), cap, cudaHostAllocDefault) == cudaSuccess)
+      ctx->h_stage_cap = cap;
+    else
+      ctx->h_stage = nullptr;
+  }
+  cudaError_t e;
+  if (ctx->h_stage && need <= ctx->h_stage_cap) {
+    e = cudaMemcpyAsync(ctx->h_stage + ctx->h_stage_used, src, bytes, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess) ctx->pending.push_back({dst, ctx->h_stage_used, bytes});
+    ctx->h_stage_used = need;
+  } else {
+    e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream);
+  }
+  if (e != cudaSuccess) {
+    ctx->pending.clear();  // the call fails: none of its readbacks is delivered
+    ctx->h_stage_used = 0;
+    return cuda_fail(ctx, e, what);
+  }
   return SI_OK;
 }
 
@@ -142,6 +173,7 @@ int si_ctx_create(int device, const si_ctx_config* cfg, si_ctx** out) {
   if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess ||
       (e = cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking)) != cudaSuccess ||
       (e = cudaMalloc(&c->d_err, 64)) != cudaSuccess ||
+      (e = cudaHostAlloc(reinterpret_cast<void**>(&c->h_err), 64, cudaHostAllocDefault)) != cudaSuccess ||
       (e = cudaMalloc(&c->d_argmax, 64)) != cudaSuccess ||
       (e = cudaMalloc(&c->d_index, 64)) != cudaSuccess) {
     int rc = cuda_fail(nullptr, e, "context creation");
@@ -165,6 +197,8 @@ void si_ctx_destroy(si_ctx* ctx) {
   for (auto& b : ctx->wbuf) b.release();
   ctx->scratch.release();
   if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->h_err) cudaFreeHost(ctx->h_err);
+  if (ctx->h_stage) cudaFreeHost(ctx->h_stage);
   if (ctx->d_argmax) cudaFree(ctx->d_argmax);
   if (ctx->d_index) cudaFree(ctx->d_index);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);

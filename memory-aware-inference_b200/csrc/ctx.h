@@ -5,6 +5,7 @@
 #include <atomic>
 #include <cstdint>
 #include <mutex>
+#include <vector>
 #include <string>
 
 #include "../../include/si_cuda.h"
@@ -48,6 +49,16 @@ struct si_ctx {
   cudaStream_t stream = nullptr;       // compute
   cudaStream_t copy_stream = nullptr;  // weight staging
   int* d_err = nullptr;                // kernel error bits
+  int* h_err = nullptr;                // pinned copy of d_err, read after each sync
+  // Pinned staging for the readbacks of one host-memory call: the copies are
+  // enqueued into it and copied to the caller's memory after the sync.
+  struct PendingCopy {
+    void* dst;
+    size_t off, bytes;
+  };
+  uint8_t* h_stage = nullptr;
+  size_t h_stage_cap = 0, h_stage_used = 0;
+  std::vector<PendingCopy> pending;
   unsigned long long* d_argmax = nullptr;
   uint32_t* d_index = nullptr;
   std::string err;

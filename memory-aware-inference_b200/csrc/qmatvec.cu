@@ -829,6 +829,22 @@ int launch_qmv(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
   const bool pair = p.pair != 0;
   switch (p.type) {
     case SI_GGML_TYPE_Q4_K:
+      if (!pair && p.xmode == XM_RAW && p.nseg > 1) {
+        // grouped plain matvec: segment by segment, so every segment's rows are
+        // exactly those of a single call on it
+        for (uint32_t i = 0; i < p.nseg; ++i) {
+          QmvParams q = p;
+          q.nseg = 1;
+          q.seg[0] = p.seg[i];
+          q.items = p.seg[i].rows;
+          if (int rc = launch_qmv(q, stream, sm_count, pdl, msg)) return rc;
+        }
+        return SI_OK;
+      }
+      if (qmv_tc_eligible(p)) {
+        const int rc = launch_qmv_tc(p, stream, sm_count, pdl, msg);
+        if (rc != SI_E_UNSUPPORTED) return rc;
+      }
       // two rows per team step share each x load (SwiGLU: gate and up rows)
       return launch_t<SI_GGML_TYPE_Q4_K, 2>(p, stream, sm_count, pdl, msg);
     case SI_GGML_TYPE_Q5_K:

@@ -42,6 +42,11 @@ struct QmvParams {
 int launch_qmv(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
                std::string* msg);
 
+// Plain Q4_K matvec on the tensor cores (qmatvec_tc.cu): eligibility and
+// launch; launch_qmv routes eligible calls there.
+bool qmv_tc_eligible(const QmvParams& p);
+int launch_qmv_tc(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl, std::string* msg);
+
 // Largest supported column count (x and its partial sums live in shared memory).
 constexpr uint32_t kQmvMaxCols = 32768;
 

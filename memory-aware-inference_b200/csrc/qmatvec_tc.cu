@@ -1,0 +1,402 @@
+// Q4_K matvec y = W x on the tensor cores with exact integer sub-block sums.
+//
+// Same contract as qmv_kernel for a plain Q4_K matvec (src/metal.rs:310-494,
+// 3357-3397, 3923 in the reference): fp32 result of sum_i w_i x_i with
+// w_i = d*sc*q - dmin*m (quant.rs:18-65).
+//
+// x as integers. Per 256-column block b, x is scaled by 2^(21-e_b) (e_b =
+// exponent of the block's largest |x|) and rounded: X_i = rint(x_i 2^(21-e_b)),
+// |X_i| <= 2^22, so |x_i - X_i 2^(e_b-21)| <= 2^-22 max|x| in the block. X is
+// split into three signed base-256 digits, X = D0 + 256 D1 + 65536 D2
+// (D0, D1 in [-128, 127], D2 in [-64, 64]), stored in shared memory as the
+// columns 0..2 of the MMA's B operand for every 32-element sub-block.
+//
+// Dot products. For 16 rows and one 32-element sub-block, mma.m16n8k32
+// (u8 x s8 -> s32) multiplies the raw quants (low nibbles as 0..15, high
+// nibbles masked in place as 16*q) by the digit columns: C[row][p] =
+// sum_k q[row][k] D_p[k], exact. The 6-bit sub-block scales are applied in
+// integers (acc_p += sc_j * C_p, |acc| < 2^29), the three digit columns are
+// combined in fp32 once per block, and the block's d, dmin and min term
+// (dmin * sum_j m_j * sum_{i in j} x_i) are applied in fp32.
+//
+// Data movement. Two CTAs per SM (one when the x digits of very wide rows do
+// not fit twice); each CTA owns a band of 16-row groups; the consumer
+// warps are shared out evenly over the groups ("split" warps per group, each
+// taking every split-th 256-column block) and add their partial sums at the
+// end in a fixed order. A producer lane issues one 3-D TMA per 256-column block for
+// the whole band (tensor map {144 B, blocks, rows}, box {144, 1, band rows}),
+// so each row of the staged tile is one 144-byte super-block: the 144-byte
+// row pitch (16 mod 128) makes the fragment loads of 8 rows bank-conflict
+// free. Stages are recycled through full/empty mbarriers with bounded waits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <string>
+
+#include "common.cuh"
+#include "qmatvec.cuh"
+
+namespace si {
+
+constexpr int kTcGroups = 8;                     // 16-row groups per CTA at most
+constexpr int kTcCtasPerSm = 2;
+// Consumer warps; a CTA with ngmax groups gives each group kTcConsumers/ngmax
+// warps ("split"), warp part p taking the blocks i = p (mod split).
+constexpr int kTcConsumers = 12;
+// Every warp phase owns kTcSlots private stages (double buffering): a warp
+// only ever waits on a stage whose previous phase it consumed itself, so an
+// mbarrier parity can never be mistaken for one a full phase ahead. A stage
+// holds one 256-column block of the CTA's band (2,304 B per 16-row group), so
+// the ring is kTcConsumers * kTcSlots * 2,304 B whatever the split.
+constexpr int kTcSlots = 2;
+constexpr uint32_t kTcGroupBlockBytes = 144 * 16;
+constexpr uint32_t kTcRingBytes = kTcConsumers * kTcSlots * kTcGroupBlockBytes;
+constexpr int kTcMaxStages = kTcConsumers * kTcSlots;
+constexpr int kTcThreads = (kTcConsumers + 1) * 32;
+
+constexpr uint32_t kTcMaxBlocks = 80;            // x digits: 1 KiB per block
+
+struct TcArgs {
+  const float* x;
+  float* y;
+  uint32_t rows, nblk, ngroups, nctas;
+  int* err;
+};
+
+__device__ __forceinline__ void mma_u8s8(int* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void tma_load_3d_u8(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
+                                               uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, uint32_t j) { return __byte_perm(w, 0, 0x4440 | j); }
+
+__global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
+    qmv_tc_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
+                  const TcArgs a) {
+  extern __shared__ __align__(128) uint8_t tsm[];
+  uint8_t* ring = tsm;                                          // stages x tile_bytes
+  uint8_t* xd = ring + kTcRingBytes;                            // [blk][8 sb][4 planes][32] s8
+  float* xsum = reinterpret_cast<float*>(xd + a.nblk * 1024);   // [blk][8]
+  float* escale = xsum + a.nblk * 8;                            // [blk]
+  uint64_t* full = reinterpret_cast<uint64_t*>(escale + ((a.nblk + 1) & ~1u));
+  uint64_t* empty = full + kTcMaxStages;
+  uint64_t* xready = empty + kTcMaxStages;                      // [blk]: digits of block written
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t cta = blockIdx.x;
+  const uint32_t g0 = uint32_t(uint64_t(cta) * a.ngroups / a.nctas);
+  const uint32_t g1 = uint32_t(uint64_t(cta + 1) * a.ngroups / a.nctas);
+  const uint32_t ng = g1 - g0;                                   // 16-row groups of this CTA
+  const uint32_t ngmax = (a.ngroups + a.nctas - 1) / a.nctas;
+  const CUtensorMap* map = ng == ngmax ? &map_hi : &map_lo;
+  const uint32_t tile_bytes = kTcGroupBlockBytes * ng;
+  const uint32_t split = kTcConsumers / ngmax;                  // warps per group
+  const uint32_t stage_bytes = kTcGroupBlockBytes * ngmax;
+  // block i -> phase h = i % split, its n-th block (n = i / split) uses stage
+  // h * kTcSlots + n % kTcSlots with parity (n / kTcSlots) & 1
+
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < split * kTcSlots; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], ng);  // the warps of one parity consume a stage
+    }
+    for (uint32_t b = 0; b < a.nblk; ++b) mbar_init(&xready[b], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == kTcConsumers) {
+    // ---- producer: one TMA per 256-column block for the whole band ----
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      const uint32_t window = split * kTcSlots;  // blocks in flight at most
+      for (uint32_t i = 0; i < a.nblk; ++i) {
+        const uint32_t n = i / split, s = (i % split) * kTcSlots + n % kTcSlots;
+        if (n >= uint32_t(kTcSlots) && !mbar_wait_bounded(&empty[s], ((n / kTcSlots) - 1) & 1)) {
+          if (a.err) atomicOr(a.err, KERR_TIMEOUT_EMPTY);
+          // drain what is in flight, then stop issuing
+          for (uint32_t j = (i > window ? i - window : 0); j < i; ++j) {
+            const uint32_t nj = j / split, sj = (j % split) * kTcSlots + nj % kTcSlots;
+            if (!mbar_wait_bounded(&full[sj], (nj / kTcSlots) & 1) && a.err) atomicOr(a.err, KERR_TIMEOUT_DRAIN);
+          }
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], tile_bytes);
+        tma_load_3d_u8(smem_u32(ring + s * stage_bytes), map, 0, int(i), int(g0 * 16), &full[s], pol);
+      }
+    }
+    return;
+  }
+
+  // ---- x -> digit planes, sub-block sums, block scales (consumer warps) ----
+  pdl_wait();
+  for (uint32_t b = warp; b < a.nblk; b += kTcConsumers) {
+    float v[8];
+    const float4* xp = reinterpret_cast<const float4*>(a.x + b * 256 + lane * 8);
+    const float4 u0 = xp[0], u1 = xp[1];
+    v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
+    v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
+    float mx = 0.f, s = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      mx = fmaxf(mx, fabsf(v[k]));
+      s += v[k];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    int e = int((__float_as_uint(mx) >> 23) & 255u) - 127;   // exponent of the block max
+    e = max(e, -100);
+    const float up = __uint_as_float(uint32_t(21 - e + 127) << 23);    // 2^(21-e), exact
+    uint32_t pl[3][2] = {};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int X = __float2int_rn(v[k] * up);
+      const int d0 = ((X + 128) & 255) - 128;
+      const int X1 = (X - d0) >> 8;
+      const int d1 = ((X1 + 128) & 255) - 128;
+      const int d2 = (X1 - d1) >> 8;
+      pl[0][k >> 2] |= uint32_t(d0 & 255) << (8 * (k & 3));
+      pl[1][k >> 2] |= uint32_t(d1 & 255) << (8 * (k & 3));
+      pl[2][k >> 2] |= uint32_t(d2 & 255) << (8 * (k & 3));
+    }
+    // plane p of sub-block sb sits at slot (p + sb) % 4 of the sub-block's
+    // 128 bytes: the fragment loads stay contiguous, the stores spread banks
+    const uint32_t sb = lane >> 2, k0 = (lane & 3) * 8;
+    uint8_t* dst = xd + (b * 8 + sb) * 128 + k0;
+#pragma unroll
+    for (int p = 0; p < 3; ++p)
+      *reinterpret_cast<uint2*>(dst + ((p + sb) & 3) * 32) = make_uint2(pl[p][0], pl[p][1]);
+    *reinterpret_cast<uint2*>(dst + ((3 + sb) & 3) * 32) = make_uint2(0u, 0u);
+    if ((lane & 3) == 0) xsum[b * 8 + sb] = s;
+    // 2^(e-21) / 16: high-nibble sub-blocks are multiplied as 16 q
+    if (lane == 0) escale[b] = __uint_as_float(uint32_t(e - 21 - 4 + 127) << 23);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&xready[b]);  // release: this block's digits, sums and scale
+  }
+
+  const int g = lane >> 2, c = lane & 3;
+  float yg = 0.f, yg8 = 0.f;
+  const uint32_t grp_w = uint32_t(warp) / split, half = uint32_t(warp) % split;  // half: block phase
+  const bool active = grp_w < ng;
+  const uint32_t row_in_band = grp_w * 16 + g;
+  for (uint32_t i = half; i < a.nblk; i += split) {
+    const uint32_t n = i / split, s = half * kTcSlots + n % kTcSlots;
+    if (!active) break;
+    if (!mbar_wait_bounded(&full[s], (n / kTcSlots) & 1)) {
+      if (a.err) atomicOr(a.err, KERR_TIMEOUT_FULL);
+      break;
+    }
+    if (!mbar_wait_bounded(&xready[i], 0)) {
+      if (a.err) atomicOr(a.err, KERR_TIMEOUT_FULL);
+      break;
+    }
+    const uint8_t* r0 = ring + s * stage_bytes + row_in_band * 144;
+    const uint8_t* r8 = r0 + 8 * 144;
+    // header: d, dmin (f16 pair), 12 bytes of packed 6-bit scales / mins
+    const uint32_t h0 = *reinterpret_cast<const uint32_t*>(r0), h8 = *reinterpret_cast<const uint32_t*>(r8);
+    uint32_t sc_lo[2], sc_hi[2], mn_lo[2], mn_hi[2];
+    {
+      const uint32_t* p0 = reinterpret_cast<const uint32_t*>(r0 + 4);
+      const uint32_t* p8 = reinterpret_cast<const uint32_t*>(r8 + 4);
+      const uint32_t w[2][3] = {{p0[0], p0[1], p0[2]}, {p8[0], p8[1], p8[2]}};
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        sc_lo[r] = w[r][0] & 0x3F3F3F3Fu;
+        mn_lo[r] = w[r][1] & 0x3F3F3F3Fu;
+        sc_hi[r] = (w[r][2] & 0x0F0F0F0Fu) | ((w[r][0] >> 2) & 0x30303030u);
+        mn_hi[r] = ((w[r][2] >> 4) & 0x0F0F0F0Fu) | ((w[r][1] >> 2) & 0x30303030u);
+      }
+    }
+    int acc[4] = {0, 0, 0, 0};
+    const uint8_t* xb = xd + i * 1024;
+#pragma unroll
+    for (int grp = 0; grp < 4; ++grp) {
+      // k <-> element map: lane c's k = 4c..4c+3 are elements 8c..8c+3 and its
+      // k = 16+4c..16+4c+3 are elements 8c+4..8c+7, for A and B alike, so both
+      // operands are one 8-byte load per lane (the sum over k is unchanged)
+      const uint32_t off = 16 + 32 * grp + 8 * c;
+      const uint2 q0 = *reinterpret_cast<const uint2*>(r0 + off);
+      const uint2 q8 = *reinterpret_cast<const uint2*>(r8 + off);
+      const uint32_t qa0 = q0.x, qb0 = q0.y, qa8 = q8.x, qb8 = q8.y;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t j = 2 * grp + h;  // sub-block
+        const uint32_t mask = h ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+        const uint32_t A[4] = {qa0 & mask, qa8 & mask, qb0 & mask, qb8 & mask};
+        uint32_t b0 = 0, b1 = 0;
+        if (g < 4) {
+          const uint2 bb = *reinterpret_cast<const uint2*>(xb + j * 128 + ((g + j) & 3) * 32 + 8 * c);
+          b0 = bb.x;
+          b1 = bb.y;
+        }
+        int C[4] = {0, 0, 0, 0};
+        mma_u8s8(C, A, b0, b1);
+        const int m0 = int(byte_of(j < 4 ? sc_lo[0] : sc_hi[0], j & 3)) << (h ? 0 : 4);
+        const int m8 = int(byte_of(j < 4 ? sc_lo[1] : sc_hi[1], j & 3)) << (h ? 0 : 4);
+        acc[0] += m0 * C[0];
+        acc[1] += m0 * C[1];
+        acc[2] += m8 * C[2];
+        acc[3] += m8 * C[3];
+      }
+    }
+    // digit columns: lane c=0 holds D0, D1; lane c=1 holds D2 (and a zero column)
+    float f0 = c == 0 ? fmaf(256.f, float(acc[1]), float(acc[0])) : (c == 1 ? 65536.f * float(acc[0]) : 0.f);
+    float f8 = c == 0 ? fmaf(256.f, float(acc[3]), float(acc[2])) : (c == 1 ? 65536.f * float(acc[2]) : 0.f);
+    f0 += __shfl_xor_sync(0xffffffffu, f0, 1);
+    f8 += __shfl_xor_sync(0xffffffffu, f8, 1);
+    // min term: lane c takes sub-blocks 2c, 2c+1 of both rows, then the quad sums
+    const float* xs = xsum + i * 8 + 2 * c;
+    const uint32_t ml0 = c < 2 ? mn_lo[0] : mn_hi[0], ml8 = c < 2 ? mn_lo[1] : mn_hi[1];
+    const uint32_t jj = (2 * c) & 3;
+    float mt0 = float(byte_of(ml0, jj)) * xs[0] + float(byte_of(ml0, jj + 1)) * xs[1];
+    float mt8 = float(byte_of(ml8, jj)) * xs[0] + float(byte_of(ml8, jj + 1)) * xs[1];
+    mt0 += __shfl_xor_sync(0xffffffffu, mt0, 1);
+    mt8 += __shfl_xor_sync(0xffffffffu, mt8, 1);
+    mt0 += __shfl_xor_sync(0xffffffffu, mt0, 2);
+    mt8 += __shfl_xor_sync(0xffffffffu, mt8, 2);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (c == 0) {
+      const float es = escale[i];
+      const float2 dd0 = __half22float2(*reinterpret_cast<const __half2*>(&h0));
+      const float2 dd8 = __half22float2(*reinterpret_cast<const __half2*>(&h8));
+      yg += dd0.x * es * f0 - dd0.y * mt0;
+      yg8 += dd8.x * es * f8 - dd8.y * mt8;
+    }
+  }
+  // odd-block warps hand their sums to the even-block warps of their group
+  float* red = reinterpret_cast<float*>(ring);  // every stage has been consumed
+  asm volatile("bar.sync 1, %0;" ::"r"(kTcConsumers * 32) : "memory");
+  if (half > 0 && active && c == 0) {
+    red[((half - 1) * kTcGroups + grp_w) * 16 + g] = yg;
+    red[((half - 1) * kTcGroups + grp_w) * 16 + g + 8] = yg8;
+  }
+  static_assert(kTcConsumers * kTcGroups * 16 * 4 <= kTcRingBytes, "reduction buffer");
+  asm volatile("bar.sync 1, %0;" ::"r"(kTcConsumers * 32) : "memory");
+  if (half == 0 && active && c == 0) {
+    for (uint32_t h = 1; h < split; ++h) {
+      yg += red[((h - 1) * kTcGroups + grp_w) * 16 + g];
+      yg8 += red[((h - 1) * kTcGroups + grp_w) * 16 + g + 8];
+    }
+    const uint32_t row = (g0 + grp_w) * 16 + g;
+    if (row < a.rows) a.y[row] = yg;
+    if (row + 8 < a.rows) a.y[row + 8] = yg8;
+  }
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 tc_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// Tensor map over Q4_K rows viewed as [rows][blocks][144 B], box {144, 1, band}.
+static bool q4k_band_map(CUtensorMap* m, const void* w, uint32_t rows, uint32_t nblk, uint32_t band) {
+  auto enc = tc_encoder();
+  if (!enc || (reinterpret_cast<uintptr_t>(w) & 15) || band == 0 || band > 256) return false;
+  const cuuint64_t dims[3] = {144, nblk, rows};
+  const cuuint64_t strides[2] = {144, cuuint64_t(nblk) * 144};
+  const cuuint32_t box[3] = {144, 1, band};
+  const cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(w), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Plain Q4_K matvecs (x as is, no residual, no SwiGLU pairing); a grouped call
+// becomes one launch per segment, so its rows match single calls bit for bit.
+bool qmv_tc_eligible(const QmvParams& p) {
+  if (p.type != SI_GGML_TYPE_Q4_K || p.pair || p.xmode != XM_RAW || p.cols / 256 > kTcMaxBlocks ||
+      (reinterpret_cast<uintptr_t>(p.x) & 15))
+    return false;
+  for (uint32_t i = 0; i < p.nseg; ++i)
+    if (p.seg[i].resid || (reinterpret_cast<uintptr_t>(p.seg[i].w) & 15)) return false;
+  return true;
+}
+
+static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stream, int sm_count, bool pdl,
+                             std::string* msg);
+
+int launch_qmv_tc(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl, std::string* msg) {
+  // every segment must fit before anything is launched (the caller may fall back)
+  for (uint32_t i = 0; i < p.nseg; ++i) {
+    const uint32_t ngroups = (p.seg[i].rows + 15) / 16;
+    if ((ngroups + uint32_t(sm_count) - 1) / uint32_t(sm_count) > uint32_t(kTcGroups)) return SI_E_UNSUPPORTED;
+  }
+  for (uint32_t i = 0; i < p.nseg; ++i)
+    if (int rc = launch_qmv_tc_seg(p, i, stream, sm_count, pdl, msg)) return rc;
+  return SI_OK;
+}
+
+static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stream, int sm_count, bool pdl,
+                             std::string* msg) {
+  const uint32_t rows = p.seg[seg].rows, nblk = p.cols / 256;
+  const uint32_t ngroups = (rows + 15) / 16;
+  const uint32_t smem = kTcRingBytes + nblk * 1024 + nblk * 8 * 4 + ((nblk + 1) & ~1u) * 4 +
+                        2 * kTcMaxStages * 8 + nblk * 8;
+  // CTAs per SM that fit (wide rows carry more x digits than two CTAs can hold)
+  static int smem_per_sm = 0;
+  if (smem_per_sm == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  }
+  const uint32_t fit = std::max(1u, std::min<uint32_t>(kTcCtasPerSm, uint32_t(smem_per_sm) / (smem + 1024)));
+  const uint32_t nctas = std::min<uint32_t>(ngroups, uint32_t(sm_count) * fit);
+  const uint32_t ngmax = (ngroups + nctas - 1) / nctas;
+  if (ngmax > uint32_t(kTcGroups)) return SI_E_UNSUPPORTED;  // caller falls back
+  CUtensorMap hi, lo;
+  if (!q4k_band_map(&hi, p.seg[seg].w, rows, nblk, 16 * ngmax) ||
+      !q4k_band_map(&lo, p.seg[seg].w, rows, nblk, 16 * (ngmax > 1 ? ngmax - 1 : 1)))
+    return SI_E_UNSUPPORTED;
+  static uint32_t attr = 0;
+  if (smem > attr) {
+    cudaError_t e = cudaFuncSetAttribute(qmv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) {
+      if (msg) *msg = std::string("cudaFuncSetAttribute(qmv_tc): ") + cudaGetErrorString(e);
+      return SI_E_CUDA;
+    }
+    attr = smem;
+  }
+  TcArgs a = {p.x, p.seg[seg].y, rows, nblk, ngroups, nctas, p.err};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nctas);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, qmv_tc_kernel, hi, lo, a);
+  if (e != cudaSuccess) {
+    if (msg) *msg = std::string("qmv_tc launch: ") + cudaGetErrorString(e);
+    return SI_E_CUDA;
+  }
+  return SI_OK;
+}
+
+}  // namespace si

@@ -94,6 +94,20 @@ def test_q4k_matvec_full_config1(ctx):  # 17408 x 5120
     assert rel_l2(got, ref) < TOL
 
 
+@pytest.mark.parametrize("rows,cols", [
+    (2368, 5120), (4736, 5120), (7104, 5120), (9472, 5120), (11840, 5120), (14208, 2560),
+    (16576, 1024), (5000, 5120), (5120, 17408), (16, 256), (300, 256), (12288, 5120),
+])
+def test_q4k_tensor_core_matvec_every_split(ctx, rows, cols):
+    """Plain Q4_K matvecs go to the tensor-core kernel; these shapes give a CTA
+    1..8 row groups (so 24..3 warps per group), ragged last groups, one and
+    68 column blocks."""
+    rng = np.random.default_rng(rows + cols)
+    w = random_blocks(rng, 12, rows * cols // 256)
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    assert rel_l2(ctx.q4_k_matvec(w, rows, cols, x), O.matvec(12, w, rows, cols, x)) < TOL
+
+
 def test_q4k_matvec_reference_pattern(ctx):  # metal.rs:7443-7494
     rows, cols = 2, 512
     w = np.zeros(rows * 2 * 144, np.uint8)
