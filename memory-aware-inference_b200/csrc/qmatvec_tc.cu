@@ -64,12 +64,13 @@ struct TcArgs {
   int* err;
 };
 
-__device__ __forceinline__ void mma_u8s8(int* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+// C = A B with a zero accumulator (no register moves to clear C).
+__device__ __forceinline__ void mma_u8s8_zero(int* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+      "{%10,%10,%10,%10};"
+      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
 }
 
 __device__ __forceinline__ void tma_load_3d_u8(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
@@ -195,6 +196,10 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
   const uint32_t grp_w = uint32_t(warp) / split, half = uint32_t(warp) % split;  // half: block phase
   const bool active = grp_w < ng;
   const uint32_t row_in_band = grp_w * 16 + g;
+  // lane offset of digit plane g inside a sub-block, for sub-block index j mod 4
+  uint32_t boff[4];
+#pragma unroll
+  for (int jm = 0; jm < 4; ++jm) boff[jm] = ((g + jm) & 3) * 32 + 8 * c;
   for (uint32_t i = half; i < a.nblk; i += split) {
     const uint32_t n = i / split, s = half * kTcSlots + n % kTcSlots;
     if (!active) break;
@@ -241,12 +246,12 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
         const uint32_t A[4] = {qa0 & mask, qa8 & mask, qb0 & mask, qb8 & mask};
         uint32_t b0 = 0, b1 = 0;
         if (g < 4) {
-          const uint2 bb = *reinterpret_cast<const uint2*>(xb + j * 128 + ((g + j) & 3) * 32 + 8 * c);
+          const uint2 bb = *reinterpret_cast<const uint2*>(xb + j * 128 + boff[j & 3]);
           b0 = bb.x;
           b1 = bb.y;
         }
-        int C[4] = {0, 0, 0, 0};
-        mma_u8s8(C, A, b0, b1);
+        int C[4];
+        mma_u8s8_zero(C, A, b0, b1);
         const int m0 = int(byte_of(j < 4 ? sc_lo[0] : sc_hi[0], j & 3)) << (h ? 0 : 4);
         const int m8 = int(byte_of(j < 4 ? sc_lo[1] : sc_hi[1], j & 3)) << (h ? 0 : 4);
         acc[0] += m0 * C[0];
