@@ -307,6 +307,9 @@ def run_ours(args, world, rank, local):
     torch.cuda.empty_cache()
     kern = measure_kernels(mai, ctx, torch, np) if not args.no_extras else None
     ctx.close()
+    if kern is not None:
+        kern["gdn_layer_config3"] = measure_layer(mai, local, "gdn", 0, 64)
+        kern["attention_layer_config4"] = measure_layer(mai, local, "attention", 8192, 64)
     dec = run_decode(args, mai, torch, np, world, rank, local) if not args.no_decode else None
     if rank == 0:
         line["kernels"] = kern
@@ -393,6 +396,50 @@ def measure_kernels(mai, ctx, torch, np):
                                 "alg_bytes": att_bytes, "note": "24 q / 4 kv heads, hd 256, 8191 cached bf16 positions + 1 new; 100 calls in a CUDA graph",
                                 "launches_per_call": 2}
     return out
+
+
+def measure_layer(mai, local, kind, context=0, tokens=64):
+    """BASELINE config 3 (kind "gdn": one Gated DeltaNet layer, 64 consecutive
+    tokens carrying conv and recurrent state) or config 4 (kind "attention":
+    one full-attention layer over `context` cached bf16 positions), both at the
+    27B shapes with Q4_K projections, inside a one-layer synthetic model whose
+    MLP (intermediate 256) and vocabulary (256) are small. Per-token time is
+    the difference of two greedy generations (1 and 1 + tokens new tokens
+    after the same prompt), so it includes the small MLP and head and one host
+    readback per token."""
+    import numpy as np
+    over = dict(layers=1, intermediate=256, vocab=256, kv_capacity=context + tokens + 4,
+                attn_interval=1 if kind == "attention" else 1000)
+    cfg = mai.qwen36_27b_config(**over)
+    ctx = mai.CudaContext(local)
+    m = mai.Model(ctx, cfg, seed=3)
+    layer_bytes = sum(m.host_tensor(0, t)[1] for t in range(23))
+    head_bytes = m.host_tensor(1, 22)[1] + m.host_tensor(1, 21)[1] + cfg.hidden // 256 * 144
+    if kind == "gdn":
+        vd = cfg.gdn_value_heads * cfg.gdn_head_dim
+        conv_ch = (2 * cfg.gdn_key_heads + cfg.gdn_value_heads) * cfg.gdn_head_dim
+        state_bytes = 2 * cfg.gdn_value_heads * cfg.gdn_head_dim * cfg.gdn_head_dim * 4 + 2 * conv_ch * 3 * 4
+        del vd
+    else:
+        state_bytes = 2 * cfg.attn_kv_heads * (context + tokens // 2) * cfg.attn_head_dim * 2
+    prompt = np.random.default_rng(5).integers(0, cfg.vocab, max(context, 1)).tolist()
+
+    def run(n):
+        m.reset()
+        t0 = time.perf_counter()
+        m.generate(prompt, n)
+        return time.perf_counter() - t0
+    run(2)
+    t1 = min(run(1) for _ in range(2))
+    tn = min(run(1 + tokens) for _ in range(2))
+    us = (tn - t1) / tokens * 1e6
+    per_token = layer_bytes + head_bytes + state_bytes
+    m.close()
+    ctx.close()
+    return {"us_per_token": round(us, 2), "bytes_per_token": per_token, "layer_weight_bytes": layer_bytes,
+            "GBps": round(per_token / us / 1e3, 1), "tokens": tokens, "context": context,
+            "note": "1-layer model (intermediate 256, vocab 256), greedy decode; includes MLP, head, "
+                    "argmax and one host readback per token"}
 
 
 def pinned_h2d_gbps(torch):

@@ -198,84 +198,103 @@ void launch_gdn_step(float* state, const float* q, const float* k, const float* 
 
 // ---------------------------------------------------------------------------
 // Fused Gated DeltaNet layer step (qwen35_runtime.rs:541-620 + qwen35.rs).
-// Grid (value_heads, 128/32): one warp per 32 value columns of one head. The
-// warp recomputes the conv + L2 norm of its key head's q/k channels (cheap)
-// and holds its 32 state columns in registers: S is read and written once.
+// One 128-thread CTA per value head h. Thread t owns channel t of the key
+// head's q and k, value channel t of h and state column t. Every global load
+// of the step (conv inputs, conv states and weights of three channels, the
+// gates, the 128 state values of the column) is issued up front, so the step
+// costs about one memory round trip; the q/k L2 norms are reduced across the
+// CTA. Per column, the recurrence keeps the reference's operation order
+// (qwen35.rs:163-225): S is read and written once.
 // ---------------------------------------------------------------------------
 constexpr int kGdnD = 128;
-constexpr int kGdnCols = 32;
+constexpr int kGdnMaxK = 8;
 
-__global__ void __launch_bounds__(32) gdn_layer_kernel(const GdnLayerArgs a) {
+template <int K>
+__device__ __forceinline__ float conv_silu_fixed(float xin, const float* st, const float* wc) {
+  float v = __fmul_rn(xin, wc[K - 1]);
+#pragma unroll
+  for (int t = 0; t + 1 < K; ++t) v = __fadd_rn(v, __fmul_rn(st[t], wc[t]));
+  return v / (1.0f + expf(-v));
+}
+
+template <int K>
+__global__ void __launch_bounds__(kGdnD) gdn_layer_kernel(const GdnLayerArgs a) {
   __shared__ float qs[kGdnD], ks[kGdnD];
-  const uint32_t h = blockIdx.x, chunk = blockIdx.y, lane = threadIdx.x;
-  const uint32_t kh = a.key_heads, vh = a.value_heads, K = a.kernel;
+  __shared__ float red[2][kGdnD / 32];
+  const uint32_t h = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const uint32_t kh = a.key_heads, vh = a.value_heads;
   const uint32_t rep = vh / kh, khead = h / rep;
   const uint32_t kw = kh * kGdnD;
+  const uint32_t cq = khead * kGdnD + t, ck = kw + cq, cv = 2 * kw + h * kGdnD + t;
   pdl_launch_dependents();
   pdl_wait();
-  const bool write_qk_state = (h % rep == 0) && chunk == 0;
-  // conv + SiLU for q and k channels of the key head.
-  float sq = 0.f, sk = 0.f;
-  for (uint32_t i = lane; i < kGdnD; i += 32) {
-#pragma unroll
-    for (int part = 0; part < 2; ++part) {
-      const uint32_t c = part * kw + khead * kGdnD + i;
-      const float* st = a.conv_in + uint64_t(c) * (K - 1);
-      const float v = conv_channel(a.qkv[c], st, a.conv_w + uint64_t(c) * K, K);
-      const float o = v / (1.0f + expf(-v));
-      if (part == 0) {
-        qs[i] = o;
-        sq += o * o;
-      } else {
-        ks[i] = o;
-        sk += o * o;
-      }
-      if (write_qk_state) {
-        float* so = a.conv_out + uint64_t(c) * (K - 1);
-        for (uint32_t t = 0; t + 2 < K; ++t) so[t] = st[t + 1];
-        so[K - 2] = a.qkv[c];
-      }
-    }
-  }
-  // value channel of this lane's column.
-  const uint32_t col = chunk * kGdnCols + lane;
-  const uint32_t cv = 2 * kw + h * kGdnD + col;
-  float vval;
-  {
-    const float* st = a.conv_in + uint64_t(cv) * (K - 1);
-    const float v = conv_channel(a.qkv[cv], st, a.conv_w + uint64_t(cv) * K, K);
-    vval = v / (1.0f + expf(-v));
-    float* so = a.conv_out + uint64_t(cv) * (K - 1);
-    for (uint32_t t = 0; t + 2 < K; ++t) so[t] = st[t + 1];
-    so[K - 2] = a.qkv[cv];
-  }
-  sq = warp_sum(sq);
-  sk = warp_sum(sk);
-  const float invq = 1.0f / sqrtf(sq + 1.0e-6f);
-  const float invk = 1.0f / sqrtf(sk + 1.0e-6f);
-  const float rs = sqrtf(float(kGdnD));
-  __syncwarp();
-  for (uint32_t i = lane; i < kGdnD; i += 32) {
-    qs[i] = __fdiv_rn(qs[i] * invq, rs);
-    ks[i] = ks[i] * invk;
-  }
-  // gates (qwen35_runtime.rs:593-601)
-  float g, beta;
-  if (a.gates) {
-    g = a.gates[h];
-    beta = a.gates[vh + h];
-  } else {
-    const float sp_in = a.alpha[h] + a.dt_bias[h];
-    const float sp = sp_in > 20.0f ? sp_in : log1pf(expf(sp_in));
-    g = -expf(a.a_log[h]) * sp;
-    beta = 1.0f / (1.0f + expf(-a.beta_logit[h]));
-  }
-  __syncwarp();
-  // recurrence on 32 columns, S column in registers.
-  float* S = a.state + uint64_t(h) * kGdnD * kGdnD + col;
+  // ---- every load of the step, independent of one another ----
+  float* S = a.state + uint64_t(h) * kGdnD * kGdnD + t;
   float s[kGdnD];
 #pragma unroll
   for (int i = 0; i < kGdnD; ++i) s[i] = S[uint64_t(i) * kGdnD];
+  float xin[3], st[3][K - 1], wc[3][K];
+  const uint32_t ch[3] = {cq, ck, cv};
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    xin[j] = a.qkv[ch[j]];
+#pragma unroll
+    for (int u = 0; u + 1 < K; ++u) st[j][u] = a.conv_in[uint64_t(ch[j]) * (K - 1) + u];
+#pragma unroll
+    for (int u = 0; u < K; ++u) wc[j][u] = a.conv_w[uint64_t(ch[j]) * K + u];
+  }
+  float g_in0, g_in1, g_in2, g_in3;
+  if (a.gates) {
+    g_in0 = a.gates[h];
+    g_in1 = a.gates[vh + h];
+    g_in2 = g_in3 = 0.f;
+  } else {
+    g_in0 = a.alpha[h];
+    g_in1 = a.dt_bias[h];
+    g_in2 = a.a_log[h];
+    g_in3 = a.beta_logit[h];
+  }
+  // ---- conv + SiLU, conv state shift ----
+  const float oq = conv_silu_fixed<K>(xin[0], st[0], wc[0]);
+  const float ok = conv_silu_fixed<K>(xin[1], st[1], wc[1]);
+  const float vval = conv_silu_fixed<K>(xin[2], st[2], wc[2]);
+  {
+    const bool write_qk = (h % rep) == 0;  // one value head per key head owns the q/k state
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      if (j < 2 && !write_qk) continue;
+      float* so = a.conv_out + uint64_t(ch[j]) * (K - 1);
+#pragma unroll
+      for (int u = 0; u + 2 < K; ++u) so[u] = st[j][u + 1];
+      so[K - 2] = xin[j];
+    }
+  }
+  // ---- q/k L2 norms over the key head (CTA reduction) ----
+  float sq = warp_sum(oq * oq), sk = warp_sum(ok * ok);
+  if (lane == 0) {
+    red[0][warp] = sq;
+    red[1][warp] = sk;
+  }
+  __syncthreads();
+  sq = (red[0][0] + red[0][1]) + (red[0][2] + red[0][3]);
+  sk = (red[1][0] + red[1][1]) + (red[1][2] + red[1][3]);
+  const float invq = 1.0f / sqrtf(sq + 1.0e-6f);
+  const float invk = 1.0f / sqrtf(sk + 1.0e-6f);
+  qs[t] = __fdiv_rn(oq * invq, sqrtf(float(kGdnD)));
+  ks[t] = ok * invk;
+  // gates (qwen35_runtime.rs:593-601)
+  float g, beta;
+  if (a.gates) {
+    g = g_in0;
+    beta = g_in1;
+  } else {
+    const float sp_in = g_in0 + g_in1;
+    const float sp = sp_in > 20.0f ? sp_in : log1pf(expf(sp_in));
+    g = -expf(g_in2) * sp;
+    beta = 1.0f / (1.0f + expf(-g_in3));
+  }
+  __syncthreads();
+  // ---- recurrence on column t ----
   const float decay = expf(g);
   float mem = 0.f;
 #pragma unroll
@@ -292,20 +311,29 @@ __global__ void __launch_bounds__(32) gdn_layer_kernel(const GdnLayerArgs a) {
   }
 #pragma unroll
   for (int i = 0; i < kGdnD; ++i) S[uint64_t(i) * kGdnD] = s[i];
-  a.core[h * kGdnD + col] = r;
+  a.core[h * kGdnD + t] = r;
 }
 
 void launch_gdn_layer(const GdnLayerArgs& a, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.value_heads, kGdnD / kGdnCols);
-  cfg.blockDim = dim3(32);
+  cfg.gridDim = dim3(a.value_heads);
+  cfg.blockDim = dim3(kGdnD);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaLaunchKernelEx(&cfg, gdn_layer_kernel, a);
+  switch (a.kernel) {
+    case 2: cudaLaunchKernelEx(&cfg, gdn_layer_kernel<2>, a); break;
+    case 3: cudaLaunchKernelEx(&cfg, gdn_layer_kernel<3>, a); break;
+    case 4: cudaLaunchKernelEx(&cfg, gdn_layer_kernel<4>, a); break;
+    case 5: cudaLaunchKernelEx(&cfg, gdn_layer_kernel<5>, a); break;
+    case 6: cudaLaunchKernelEx(&cfg, gdn_layer_kernel<6>, a); break;
+    case 7: cudaLaunchKernelEx(&cfg, gdn_layer_kernel<7>, a); break;
+    case 8: cudaLaunchKernelEx(&cfg, gdn_layer_kernel<8>, a); break;
+    default: break;  // rejected by the model's config validation
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -1131,25 +1159,54 @@ void launch_argmax(const float* v, uint64_t n, unsigned long long* key, uint32_t
 // F32 matvec with the (1+w) RMSNorm of x fused in (alpha/beta projections of
 // the Gated DeltaNet mixer, qwen35_runtime.rs:575-590). One CTA per 8 rows.
 // ---------------------------------------------------------------------------
-__global__ void f32_matvec_norm_kernel(const float* w, uint32_t rows, uint32_t cols, const float* x,
-                                       const float* nw, float eps, float* y) {
+__global__ void __launch_bounds__(256) f32_matvec_norm_kernel(const float* w0, float* y0, const float* w1,
+                                                              float* y1, uint32_t cols, const float* x,
+                                                              const float* nw, float eps) {
+  // one CTA per output row: the row's loads are all in flight at once
   __shared__ float red[32];
-  float ss = 0.f;
-  for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) ss += x[i] * x[i];
-  const float inv = 1.0f / sqrtf(block_sum(ss, red) / float(cols) + eps);
-  const uint32_t row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const float* wr = w + uint64_t(row) * cols;
-  float acc = 0.f;
-  for (uint32_t i = lane; i < cols; i += 32) acc += wr[i] * (x[i] * inv * (1.0f + nw[i]));
-  acc = warp_sum(acc);
-  if (lane == 0) y[row] = acc;
+  const bool second = blockIdx.y == 1;
+  const float* wr = (second ? w1 : w0) + uint64_t(blockIdx.x) * cols;
+  pdl_launch_dependents();
+  float acc = 0.f, ss = 0.f;
+  if ((cols & 3) == 0 && ((reinterpret_cast<uintptr_t>(wr) | reinterpret_cast<uintptr_t>(x) |
+                           reinterpret_cast<uintptr_t>(nw)) & 15) == 0) {
+    const float4* w4 = reinterpret_cast<const float4*>(wr);
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const float4* n4 = reinterpret_cast<const float4*>(nw);
+    pdl_wait();
+    for (uint32_t i = threadIdx.x; i < cols / 4; i += blockDim.x) {
+      const float4 wv = __ldg(w4 + i), xv = x4[i], nv = __ldg(n4 + i);
+      ss += xv.x * xv.x + xv.y * xv.y + xv.z * xv.z + xv.w * xv.w;
+      acc += wv.x * (xv.x * (1.0f + nv.x)) + wv.y * (xv.y * (1.0f + nv.y)) + wv.z * (xv.z * (1.0f + nv.z)) +
+             wv.w * (xv.w * (1.0f + nv.w));
+    }
+  } else {
+    pdl_wait();
+    for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
+      ss += x[i] * x[i];
+      acc += wr[i] * (x[i] * (1.0f + nw[i]));
+    }
+  }
+  // (1+w) RMSNorm of x is a common factor: sum w*x*(1+nw) * inv
+  const float tot = block_sum(ss, red);
+  __syncthreads();
+  const float dot = block_sum(acc, red);
+  const float inv = 1.0f / sqrtf(tot / float(cols) + eps);
+  if (threadIdx.x == 0) (second ? y1 : y0)[blockIdx.x] = dot * inv;
 }
 
-void launch_f32_matvec_norm(const float* w, uint32_t rows, uint32_t cols, const float* x,
-                            const float* norm_w, float eps, float* y, cudaStream_t s) {
-  f32_matvec_norm_kernel<<<(rows + 7) / 8, 256, 0, s>>>(w, rows, cols, x, norm_w, eps, y);
+void launch_f32_matvec_norm2(const float* w0, float* y0, const float* w1, float* y1, uint32_t rows, uint32_t cols,
+                             const float* x, const float* norm_w, float eps, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(rows, w1 ? 2 : 1);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, f32_matvec_norm_kernel, w0, y0, w1, y1, cols, x, norm_w, eps);
 }
 
 // ---------------------------------------------------------------------------

@@ -89,9 +89,10 @@ void launch_argmax_key(const float* v, uint64_t n, uint32_t base, unsigned long 
                        cudaStream_t s);
 void launch_argmax_finish(unsigned long long* keys, uint32_t count, uint32_t* index,
                           cudaStream_t s);
-// F32 matvec whose input is the (1+w) RMSNorm of x (computed per CTA).
-void launch_f32_matvec_norm(const float* w, uint32_t rows, uint32_t cols, const float* x,
-                            const float* norm_w, float eps, float* y, cudaStream_t s);
+// F32 matvecs whose input is the (1+w) RMSNorm of x, for one or two weight
+// matrices of `rows` rows sharing x (the alpha and beta projections).
+void launch_f32_matvec_norm2(const float* w0, float* y0, const float* w1, float* y1, uint32_t rows, uint32_t cols,
+                             const float* x, const float* norm_w, float eps, cudaStream_t s);
 // Dequantize Q4_K embedding row `*d_token` if it lies in [row_lo, row_hi), else zeros.
 void launch_embed(const uint8_t* table, uint32_t cols, const uint32_t* d_token, uint32_t row_lo,
                   uint32_t row_hi, float* out, cudaStream_t s);

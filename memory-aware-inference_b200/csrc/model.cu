@@ -235,7 +235,7 @@ int validate_config(const si_model_config& c, int n) {
       c.layers == 0 || c.vocab == 0 || c.attn_interval == 0)
     return 1;
   if (c.gdn_head_dim != 128 || c.gdn_key_heads == 0 || c.gdn_value_heads % c.gdn_key_heads ||
-      (uint64_t(c.gdn_value_heads) * 128) % 256 || c.conv_kernel < 2)
+      (uint64_t(c.gdn_value_heads) * 128) % 256 || c.conv_kernel < 2 || c.conv_kernel > 8)
     return 2;
   if (c.attn_kv_heads == 0 || c.attn_q_heads % c.attn_kv_heads || c.attn_head_dim > 256 ||
       c.attn_head_dim % 32 || c.attn_q_heads / c.attn_kv_heads > 8 ||
@@ -779,11 +779,10 @@ int gdn_layer(si_model* m, uint32_t l, const uint8_t* base) {
   p.xw = attn_norm;
   int rc = run_qmv(m, p);
   if (rc) return rc;
-  // alpha and beta (F32 rows, adjacent in the packed layer)
-  launch_f32_matvec_norm(reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_ALPHA)), m->vh_l,
-                         c.hidden, m->hidden, attn_norm, c.rms_eps, m->ab, m->ctx->stream);
-  launch_f32_matvec_norm(reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_BETA)), m->vh_l,
-                         c.hidden, m->hidden, attn_norm, c.rms_eps, m->ab + m->vh_l, m->ctx->stream);
+  // alpha and beta (F32 rows, adjacent in the packed layer), one launch
+  launch_f32_matvec_norm2(reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_ALPHA)), m->ab,
+                          reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_BETA)), m->ab + m->vh_l,
+                          m->vh_l, c.hidden, m->hidden, attn_norm, c.rms_eps, m->ctx->stream);
   GdnLayerArgs g = {};
   g.qkv = m->qkv;
   g.conv_w = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_CONV));
