@@ -60,7 +60,14 @@ constexpr uint32_t kTcMaxBlocks = 80;            // x digits: 1 KiB per block
 struct TcArgs {
   const float* x;
   float* y;
+  const float* resid;    // optional residual added in the epilogue (may alias y)
+  const float* xw;       // XM_RMS1P: [cols] (1+w) norm weight; XM_GATED: [head_dim]
+  const float* xaux;     // XM_GATED: z; XM_SIGGATE: gate
+  float eps;
+  int xmode;
+  uint32_t head_dim;     // XM_GATED (64, 128 or 256)
   uint32_t rows, nblk, ngroups, nctas;
+  uint32_t mats;         // 1, or 2 for a SwiGLU pair (gate = map 0, up = map 1)
   int* err;
 };
 
@@ -86,6 +93,7 @@ __device__ __forceinline__ uint32_t byte_of(uint32_t w, uint32_t j) { return __b
 
 __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
     qmv_tc_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
+                  const __grid_constant__ CUtensorMap up_hi, const __grid_constant__ CUtensorMap up_lo,
                   const TcArgs a) {
   extern __shared__ __align__(128) uint8_t tsm[];
   uint8_t* ring = tsm;                                          // stages x tile_bytes
@@ -103,16 +111,20 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
   const uint32_t ng = g1 - g0;                                   // 16-row groups of this CTA
   const uint32_t ngmax = (a.ngroups + a.nctas - 1) / a.nctas;
   const CUtensorMap* map = ng == ngmax ? &map_hi : &map_lo;
-  const uint32_t tile_bytes = kTcGroupBlockBytes * ng;
-  const uint32_t split = kTcConsumers / ngmax;                  // warps per group
-  const uint32_t stage_bytes = kTcGroupBlockBytes * ngmax;
+  const CUtensorMap* map_up = ng == ngmax ? &up_hi : &up_lo;
+  // "virtual groups": the CTA's row groups of each matrix (a SwiGLU pair has
+  // the same rows of gate and up, staged one after the other)
+  const uint32_t nv = ng * a.mats, nvmax = ngmax * a.mats;
+  const uint32_t tile_bytes = kTcGroupBlockBytes * ng;          // one matrix
+  const uint32_t split = kTcConsumers / nvmax;                  // warps per virtual group
+  const uint32_t stage_bytes = kTcGroupBlockBytes * nvmax;
   // block i -> phase h = i % split, its n-th block (n = i / split) uses stage
   // h * kTcSlots + n % kTcSlots with parity (n / kTcSlots) & 1
 
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < split * kTcSlots; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], ng);  // the warps of one parity consume a stage
+      mbar_init(&empty[s], nv);  // the warps of one phase consume a stage
     }
     for (uint32_t b = 0; b < a.nblk; ++b) mbar_init(&xready[b], 1);
     fence_barrier_init();
@@ -136,21 +148,64 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
           }
           break;
         }
-        mbar_arrive_expect_tx(&full[s], tile_bytes);
+        mbar_arrive_expect_tx(&full[s], tile_bytes * a.mats);
         tma_load_3d_u8(smem_u32(ring + s * stage_bytes), map, 0, int(i), int(g0 * 16), &full[s], pol);
+        if (a.mats == 2)
+          tma_load_3d_u8(smem_u32(ring + s * stage_bytes + tile_bytes), map_up, 0, int(i), int(g0 * 16), &full[s],
+                         pol);
       }
     }
     return;
   }
 
-  // ---- x -> digit planes, sub-block sums, block scales (consumer warps) ----
+  // ---- x (transformed as xmode says) -> digit planes, sub-block sums,
+  //      block scales (consumer warps) ----
   pdl_wait();
+  float rms_inv = 1.f;
+  if (a.xmode == XM_RMS1P) {
+    // (1+w) RMSNorm over the whole vector (qwen35.rs:53-86, heads = 1)
+    __shared__ float s_red[kTcConsumers];
+    float ss = 0.f;
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    for (uint32_t i = threadIdx.x; i < a.nblk * 64; i += kTcConsumers * 32) {
+      const float4 u = x4[i];
+      ss += u.x * u.x + u.y * u.y + u.z * u.z + u.w * u.w;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) s_red[warp] = ss;
+    asm volatile("bar.sync 1, %0;" ::"r"(kTcConsumers * 32) : "memory");
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kTcConsumers; ++w) tot += s_red[w];
+    rms_inv = 1.0f / sqrtf(tot / float(a.nblk * 256) + a.eps);
+  }
   for (uint32_t b = warp; b < a.nblk; b += kTcConsumers) {
     float v[8];
-    const float4* xp = reinterpret_cast<const float4*>(a.x + b * 256 + lane * 8);
+    const uint32_t e0 = b * 256 + lane * 8;
+    const float4* xp = reinterpret_cast<const float4*>(a.x + e0);
     const float4 u0 = xp[0], u1 = xp[1];
     v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
     v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
+    if (a.xmode == XM_RMS1P) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = v[k] * rms_inv * (1.0f + a.xw[e0 + k]);
+    } else if (a.xmode == XM_GATED) {
+      // per head of head_dim: x * rsqrt(mean x^2 + eps) * w[d] * SiLU(z) (qwen35.rs:14-49)
+      const uint32_t hl = a.head_dim / 8;  // lanes per head (8, 16 or 32)
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ss += v[k] * v[k];
+      for (uint32_t o = 1; o < hl; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float inv = 1.0f / sqrtf(ss / float(a.head_dim) + a.eps);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float z = a.xaux[e0 + k];
+        v[k] = v[k] * inv * a.xw[(e0 + k) % a.head_dim] * (z / (1.0f + expf(-z)));
+      }
+    } else if (a.xmode == XM_SIGGATE) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = v[k] / (1.0f + expf(-a.xaux[e0 + k]));
+    }
     float mx = 0.f, s = 0.f;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -193,9 +248,11 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
 
   const int g = lane >> 2, c = lane & 3;
   float yg = 0.f, yg8 = 0.f;
-  const uint32_t grp_w = uint32_t(warp) / split, half = uint32_t(warp) % split;  // half: block phase
-  const bool active = grp_w < ng;
-  const uint32_t row_in_band = grp_w * 16 + g;
+  const uint32_t vgrp = uint32_t(warp) / split, half = uint32_t(warp) % split;  // half: block phase
+  const bool active = vgrp < nv;
+  const uint32_t mat = active ? vgrp / ng : 0, grp_w = active ? vgrp % ng : vgrp;
+  // row of this lane inside a stage: matrix `mat`'s tile, then its group
+  const uint32_t row_in_band = mat * ng * 16 + grp_w * 16 + g;
   // lane offset of digit plane g inside a sub-block, for sub-block index j mod 4
   uint32_t boff[4];
 #pragma unroll
@@ -285,23 +342,36 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
       yg8 += dd8.x * es * f8 - dd8.y * mt8;
     }
   }
-  // odd-block warps hand their sums to the even-block warps of their group
+  // the other phases hand their sums to the phase-0 warp of their group
   float* red = reinterpret_cast<float*>(ring);  // every stage has been consumed
+  float* upv = red + kTcConsumers * kTcGroups * 16;  // SwiGLU: up-row totals
+  static_assert((kTcConsumers + 1) * kTcGroups * 16 * 4 <= kTcRingBytes, "reduction buffer");
   asm volatile("bar.sync 1, %0;" ::"r"(kTcConsumers * 32) : "memory");
   if (half > 0 && active && c == 0) {
-    red[((half - 1) * kTcGroups + grp_w) * 16 + g] = yg;
-    red[((half - 1) * kTcGroups + grp_w) * 16 + g + 8] = yg8;
+    red[((half - 1) * kTcGroups + vgrp) * 16 + g] = yg;
+    red[((half - 1) * kTcGroups + vgrp) * 16 + g + 8] = yg8;
   }
-  static_assert(kTcConsumers * kTcGroups * 16 * 4 <= kTcRingBytes, "reduction buffer");
   asm volatile("bar.sync 1, %0;" ::"r"(kTcConsumers * 32) : "memory");
   if (half == 0 && active && c == 0) {
     for (uint32_t h = 1; h < split; ++h) {
-      yg += red[((h - 1) * kTcGroups + grp_w) * 16 + g];
-      yg8 += red[((h - 1) * kTcGroups + grp_w) * 16 + g + 8];
+      yg += red[((h - 1) * kTcGroups + vgrp) * 16 + g];
+      yg8 += red[((h - 1) * kTcGroups + vgrp) * 16 + g + 8];
     }
+    if (mat == 1) {
+      upv[grp_w * 16 + g] = yg;
+      upv[grp_w * 16 + g + 8] = yg8;
+    }
+  }
+  if (a.mats == 2) asm volatile("bar.sync 1, %0;" ::"r"(kTcConsumers * 32) : "memory");
+  if (half == 0 && active && c == 0 && mat == 0) {
     const uint32_t row = (g0 + grp_w) * 16 + g;
-    if (row < a.rows) a.y[row] = yg;
-    if (row + 8 < a.rows) a.y[row + 8] = yg8;
+    float o0 = yg, o8 = yg8;
+    if (a.mats == 2) {  // SwiGLU: SiLU(gate) * up (metal.rs:498-587)
+      o0 = yg / (1.0f + expf(-yg)) * upv[grp_w * 16 + g];
+      o8 = yg8 / (1.0f + expf(-yg8)) * upv[grp_w * 16 + g + 8];
+    }
+    if (row < a.rows) a.y[row] = a.resid ? a.resid[row] + o0 : o0;
+    if (row + 8 < a.rows) a.y[row + 8] = a.resid ? a.resid[row + 8] + o8 : o8;
   }
 }
 
@@ -330,14 +400,23 @@ static bool q4k_band_map(CUtensorMap* m, const void* w, uint32_t rows, uint32_t 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Plain Q4_K matvecs (x as is, no residual, no SwiGLU pairing); a grouped call
-// becomes one launch per segment, so its rows match single calls bit for bit.
+// Q4_K matvecs with any x transform, residual epilogue and SwiGLU pairing; a
+// grouped call becomes one launch per segment (pairs: one launch), so every
+// row matches a single call on its segment bit for bit.
 bool qmv_tc_eligible(const QmvParams& p) {
-  if (p.type != SI_GGML_TYPE_Q4_K || p.pair || p.xmode != XM_RAW || p.cols / 256 > kTcMaxBlocks ||
-      (reinterpret_cast<uintptr_t>(p.x) & 15))
+  if (p.type != SI_GGML_TYPE_Q4_K || p.cols / 256 > kTcMaxBlocks || (reinterpret_cast<uintptr_t>(p.x) & 15))
     return false;
+  if (p.xmode == XM_GATED && p.head_dim != 64 && p.head_dim != 128 && p.head_dim != 256) return false;
+  if ((p.xmode == XM_RMS1P || p.xmode == XM_GATED) && !p.xw) return false;
+  if ((p.xmode == XM_GATED || p.xmode == XM_SIGGATE) && !p.xaux) return false;
+  if (p.pair && (p.nseg != 2 || p.seg[0].rows != p.seg[1].rows)) return false;
+  // measured on B200: the tensor-core kernel wins from about 4096 rows of one
+  // matrix (17408 x 5120: 13.0 vs 17.2 us); below that, and for several
+  // segments that the CUDA-core kernel serves in one launch, it does not
+  if (!p.pair && p.nseg != 1) return false;
+  if (p.seg[0].rows < 4096) return false;
   for (uint32_t i = 0; i < p.nseg; ++i)
-    if (p.seg[i].resid || (reinterpret_cast<uintptr_t>(p.seg[i].w) & 15)) return false;
+    if ((reinterpret_cast<uintptr_t>(p.seg[i].w) & 15)) return false;
   return true;
 }
 
@@ -345,19 +424,20 @@ static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stre
                              std::string* msg);
 
 int launch_qmv_tc(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl, std::string* msg) {
-  // every segment must fit before anything is launched (the caller may fall back)
-  for (uint32_t i = 0; i < p.nseg; ++i) {
+  // every launch must fit before anything is launched (the caller may fall back)
+  const uint32_t mats = p.pair ? 2 : 1;
+  for (uint32_t i = 0; i < (p.pair ? 1u : p.nseg); ++i) {
     const uint32_t ngroups = (p.seg[i].rows + 15) / 16;
-    if ((ngroups + uint32_t(sm_count) - 1) / uint32_t(sm_count) > uint32_t(kTcGroups)) return SI_E_UNSUPPORTED;
+    if ((ngroups + uint32_t(sm_count) - 1) / uint32_t(sm_count) * mats > uint32_t(kTcGroups)) return SI_E_UNSUPPORTED;
   }
-  for (uint32_t i = 0; i < p.nseg; ++i)
+  for (uint32_t i = 0; i < (p.pair ? 1u : p.nseg); ++i)
     if (int rc = launch_qmv_tc_seg(p, i, stream, sm_count, pdl, msg)) return rc;
   return SI_OK;
 }
 
 static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stream, int sm_count, bool pdl,
                              std::string* msg) {
-  const uint32_t rows = p.seg[seg].rows, nblk = p.cols / 256;
+  const uint32_t rows = p.seg[seg].rows, nblk = p.cols / 256, mats = p.pair ? 2 : 1;
   const uint32_t ngroups = (rows + 15) / 16;
   const uint32_t smem = kTcRingBytes + nblk * 1024 + nblk * 8 * 4 + ((nblk + 1) & ~1u) * 4 +
                         2 * kTcMaxStages * 8 + nblk * 8;
@@ -369,13 +449,22 @@ static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stre
     cudaDeviceGetAttribute(&smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
   }
   const uint32_t fit = std::max(1u, std::min<uint32_t>(kTcCtasPerSm, uint32_t(smem_per_sm) / (smem + 1024)));
-  const uint32_t nctas = std::min<uint32_t>(ngroups, uint32_t(sm_count) * fit);
+  uint32_t nctas = std::min<uint32_t>(ngroups, uint32_t(sm_count) * fit);
+  // at most kTcGroups virtual groups per CTA
+  while ((ngroups + nctas - 1) / nctas * mats > uint32_t(kTcGroups)) ++nctas;
+  if (nctas > ngroups) return SI_E_UNSUPPORTED;
   const uint32_t ngmax = (ngroups + nctas - 1) / nctas;
-  if (ngmax > uint32_t(kTcGroups)) return SI_E_UNSUPPORTED;  // caller falls back
-  CUtensorMap hi, lo;
-  if (!q4k_band_map(&hi, p.seg[seg].w, rows, nblk, 16 * ngmax) ||
-      !q4k_band_map(&lo, p.seg[seg].w, rows, nblk, 16 * (ngmax > 1 ? ngmax - 1 : 1)))
+  const uint32_t lo_band = 16 * (ngmax > 1 ? ngmax - 1 : 1);
+  CUtensorMap hi, lo, uhi, ulo;
+  if (!q4k_band_map(&hi, p.seg[seg].w, rows, nblk, 16 * ngmax) || !q4k_band_map(&lo, p.seg[seg].w, rows, nblk, lo_band))
     return SI_E_UNSUPPORTED;
+  if (mats == 2) {
+    if (!q4k_band_map(&uhi, p.seg[1].w, rows, nblk, 16 * ngmax) || !q4k_band_map(&ulo, p.seg[1].w, rows, nblk, lo_band))
+      return SI_E_UNSUPPORTED;
+  } else {
+    uhi = hi;
+    ulo = lo;
+  }
   static uint32_t attr = 0;
   if (smem > attr) {
     cudaError_t e = cudaFuncSetAttribute(qmv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -385,7 +474,21 @@ static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stre
     }
     attr = smem;
   }
-  TcArgs a = {p.x, p.seg[seg].y, rows, nblk, ngroups, nctas, p.err};
+  TcArgs a = {};
+  a.x = p.x;
+  a.y = p.seg[seg].y;
+  a.resid = p.seg[seg].resid;
+  a.xw = p.xw;
+  a.xaux = p.xaux;
+  a.eps = p.eps;
+  a.xmode = p.xmode;
+  a.head_dim = p.head_dim;
+  a.rows = rows;
+  a.nblk = nblk;
+  a.ngroups = ngroups;
+  a.nctas = nctas;
+  a.mats = mats;
+  a.err = p.err;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nctas);
   cfg.blockDim = dim3(kTcThreads);
@@ -396,7 +499,7 @@ static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stre
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, qmv_tc_kernel, hi, lo, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, qmv_tc_kernel, hi, lo, uhi, ulo, a);
   if (e != cudaSuccess) {
     if (msg) *msg = std::string("qmv_tc launch: ") + cudaGetErrorString(e);
     return SI_E_CUDA;

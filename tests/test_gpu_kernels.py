@@ -95,13 +95,14 @@ def test_q4k_matvec_full_config1(ctx):  # 17408 x 5120
 
 
 @pytest.mark.parametrize("rows,cols", [
-    (2368, 5120), (4736, 5120), (7104, 5120), (9472, 5120), (11840, 5120), (14208, 2560),
-    (16576, 1024), (5000, 5120), (5120, 17408), (16, 256), (300, 256), (12288, 5120),
+    (2368, 5120), (4096, 5120), (4736, 5120), (7104, 5120), (9472, 5120), (11840, 5120), (14208, 2560),
+    (16576, 1024), (5000, 5120), (5120, 17408), (16, 256), (300, 256), (12288, 5120), (34816, 512),
 ])
 def test_q4k_tensor_core_matvec_every_split(ctx, rows, cols):
-    """Plain Q4_K matvecs go to the tensor-core kernel; these shapes give a CTA
-    1..8 row groups (so 24..3 warps per group), ragged last groups, one and
-    68 column blocks."""
+    """Plain Q4_K matvecs of 4096 rows and more go to the tensor-core kernel;
+    these shapes give a CTA 1..8 row groups (12..1 warps per group), ragged
+    last groups, 2..68 column blocks, and smaller ones that stay on the
+    CUDA-core kernel."""
     rng = np.random.default_rng(rows + cols)
     w = random_blocks(rng, 12, rows * cols // 256)
     x = rng.normal(0, 1, cols).astype(np.float32)
