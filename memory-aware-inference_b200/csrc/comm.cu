@@ -19,7 +19,9 @@ struct si_comm_state {
 namespace si {
 
 // Poll a non-blocking NCCL operation until it leaves ncclInProgress, bounded
-// by `seconds`; on timeout the communicator is aborted.
+// by `seconds`; on timeout the communicator is aborted. Collective enqueues
+// settle within microseconds, so the first millisecond spins (yielding the
+// core) and only longer waits (communicator set-up) sleep between polls.
 static ncclResult_t wait_nccl(ncclComm_t comm, double seconds) {
   auto t0 = std::chrono::steady_clock::now();
   ncclResult_t st = ncclInProgress;
@@ -27,9 +29,12 @@ static ncclResult_t wait_nccl(ncclComm_t comm, double seconds) {
     ncclResult_t r = ncclCommGetAsyncError(comm, &st);
     if (r != ncclSuccess) return r;
     if (st != ncclInProgress) return st;
-    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > seconds)
-      return ncclInProgress;
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > seconds) return ncclInProgress;
+    if (el < 1e-3)
+      std::this_thread::yield();
+    else
+      std::this_thread::sleep_for(std::chrono::microseconds(20));
   }
 }
 
