@@ -58,6 +58,19 @@ int comm_allgather(si_ctx* ctx, const float* send, float* recv, size_t count, cu
   return settle(ctx, ncclAllGather(send, recv, count, ncclFloat32, ctx->comm->comm, s), "ncclAllGather");
 }
 
+// Two all-gathers issued as one NCCL group: one launch, one latency.
+int comm_allgather2(si_ctx* ctx, const float* s1, float* r1, size_t n1, const float* s2, float* r2, size_t n2,
+                    cudaStream_t s) {
+  if (!ctx->comm) return SI_OK;
+  ncclComm_t c = ctx->comm->comm;
+  ncclResult_t r = ncclGroupStart();
+  if (r == ncclSuccess) r = ncclAllGather(s1, r1, n1, ncclFloat32, c, s);
+  if (r == ncclSuccess || r == ncclInProgress) r = ncclAllGather(s2, r2, n2, ncclFloat32, c, s);
+  const ncclResult_t e = ncclGroupEnd();
+  if (r == ncclSuccess || r == ncclInProgress) r = e;
+  return settle(ctx, r, "ncclAllGather (grouped)");
+}
+
 int comm_allreduce_sum(si_ctx* ctx, const float* send, float* recv, size_t count, cudaStream_t s) {
   if (!ctx->comm) return SI_OK;
   return settle(ctx, ncclAllReduce(send, recv, count, ncclFloat32, ncclSum, ctx->comm->comm, s), "ncclAllReduce");

@@ -7,6 +7,8 @@ struct si_ctx;
 
 namespace si {
 int comm_allgather(si_ctx* ctx, const float* send, float* recv, size_t count, cudaStream_t s);
+int comm_allgather2(si_ctx* ctx, const float* s1, float* r1, size_t n1, const float* s2, float* r2, size_t n2,
+                    cudaStream_t s);
 int comm_allreduce_sum(si_ctx* ctx, const float* send, float* recv, size_t count, cudaStream_t s);
 int comm_allgather_u64(si_ctx* ctx, const unsigned long long* send, unsigned long long* recv,
                        cudaStream_t s);

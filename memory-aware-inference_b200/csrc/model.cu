@@ -803,8 +803,7 @@ int gdn_layer(si_model* m, uint32_t l, const uint8_t* base) {
   const float* core = m->core;
   const float* z = m->z;
   if (m->n > 1) {
-    if ((rc = comm_allgather(m->ctx, m->core, m->core_full, vw_l, m->ctx->stream)) ||
-        (rc = comm_allgather(m->ctx, m->z, m->z_full, vw_l, m->ctx->stream)))
+    if ((rc = comm_allgather2(m->ctx, m->core, m->core_full, vw_l, m->z, m->z_full, vw_l, m->ctx->stream)))
       return rc;
     core = m->core_full;
     z = m->z_full;
@@ -863,8 +862,8 @@ int attn_layer(si_model* m, uint32_t l, const uint8_t* base, uint64_t position) 
   const float* gate = m->qg + qw_l;
   if (m->n > 1) {
     // gate half of the local q projection is contiguous after the queries
-    if ((rc = comm_allgather(m->ctx, m->att, m->att_full, qw_l, m->ctx->stream)) ||
-        (rc = comm_allgather(m->ctx, m->qg + qw_l, m->gate_full, qw_l, m->ctx->stream)))
+    if ((rc = comm_allgather2(m->ctx, m->att, m->att_full, qw_l, m->qg + qw_l, m->gate_full, qw_l,
+                              m->ctx->stream)))
       return rc;
     att = m->att_full;
     gate = m->gate_full;
