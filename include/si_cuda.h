@@ -56,8 +56,12 @@ typedef struct si_model si_model;
 typedef struct si_ctx_config {
   uint64_t hbm_budget_bytes; /* bound for model weights+ring+state; 0 = no bound */
   uint32_t stage_depth;      /* staging-ring depth: default 3, clamped to 1..4 */
-  uint32_t flags;            /* reserved, 0 */
+  uint32_t flags;            /* SI_CTX_FLAG_* bits, 0 = defaults */
 } si_ctx_config;
+/* Row-sharded models exchange their sharded vectors over NVLink peer memory
+ * (CUDA IPC mappings of the ranks' scratch) by default; this flag keeps every
+ * exchange on NCCL collectives instead. */
+#define SI_CTX_FLAG_NCCL_COLLECTIVES 1u
 
 /* ---- context (MetalContext::new, metal.rs:2170) ------------------------- */
 int si_ctx_create(int device, const si_ctx_config* cfg, si_ctx** out);

@@ -25,6 +25,7 @@ LIB_PATH = os.path.join(_HERE, "libsi_cuda.so")
 GGML_TYPE_F32, GGML_TYPE_Q4_K, GGML_TYPE_Q5_K, GGML_TYPE_Q6_K = 0, 12, 13, 14
 BLOCK_BYTES = {GGML_TYPE_Q4_K: 144, GGML_TYPE_Q5_K: 176, GGML_TYPE_Q6_K: 210}
 CACHE_F32, CACHE_BF16 = 0, 1
+CTX_FLAG_NCCL_COLLECTIVES = 1  # sharded models exchange vectors with NCCL, not NVLink peer stores
 TENSOR_IDS = ["ATTN_NORM", "POST_NORM", "FFN_GATE", "FFN_UP", "FFN_DOWN", "SSM_QKV", "SSM_Z", "SSM_ALPHA",
               "SSM_BETA", "SSM_CONV", "SSM_A", "SSM_DT", "SSM_NORM", "SSM_OUT", "ATTN_Q", "ATTN_K", "ATTN_V",
               "ATTN_O", "ATTN_QNORM", "ATTN_KNORM", "TOKEN_EMBD", "OUTPUT_NORM", "OUTPUT"]
@@ -208,9 +209,9 @@ class AttentionDecodeInput:
 class CudaContext:
     """B200 replacement of MetalContext (src/metal.rs:1782-2445)."""
 
-    def __init__(self, device: int = 0, hbm_budget_bytes: int = 0, stage_depth: int = 3):
+    def __init__(self, device: int = 0, hbm_budget_bytes: int = 0, stage_depth: int = 3, flags: int = 0):
         L = lib()
-        cfg = SiCtxConfig(hbm_budget_bytes, stage_depth, 0)
+        cfg = SiCtxConfig(hbm_budget_bytes, stage_depth, flags)
         h = C.c_void_p()
         rc = L.si_ctx_create(device, C.byref(cfg), C.byref(h))
         if rc != 0:

@@ -6,6 +6,7 @@
 #include <cstring>
 #include <string>
 #include <thread>
+#include <vector>
 
 #include "comm.h"
 #include "ctx.h"
@@ -69,6 +70,51 @@ int comm_allgather2(si_ctx* ctx, const float* s1, float* r1, size_t n1, const fl
   const ncclResult_t e = ncclGroupEnd();
   if (r == ncclSuccess || r == ncclInProgress) r = e;
   return settle(ctx, r, "ncclAllGather (grouped)");
+}
+
+// Map a device allocation of every rank into this process: the CUDA IPC
+// handles of `base` travel over the communicator; peers[rank] = base.
+int comm_p2p_map(si_ctx* ctx, void* base, void** peers) {
+  const int n = ctx->nranks, r = ctx->rank;
+  if (!ctx->comm || n < 2) return SI_E_STATE;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, base);
+  if (e != cudaSuccess) return fail(ctx, SI_E_CUDA, std::string("cudaIpcGetMemHandle: ") + cudaGetErrorString(e));
+  constexpr size_t HB = sizeof(cudaIpcMemHandle_t);
+  uint8_t* dh = nullptr;
+  if ((e = cudaMalloc(&dh, HB * n)) != cudaSuccess)
+    return fail(ctx, SI_E_NOMEM, std::string("IPC handle exchange buffer: ") + cudaGetErrorString(e));
+  std::vector<uint8_t> all(HB * n);
+  cudaMemcpyAsync(dh + HB * r, &h, HB, cudaMemcpyHostToDevice, ctx->stream);
+  int rc = settle(ctx, ncclAllGather(dh + HB * r, dh, HB, ncclUint8, ctx->comm->comm, ctx->stream),
+                  "ncclAllGather(IPC handles)");
+  if (!rc) {
+    cudaMemcpyAsync(all.data(), dh, HB * n, cudaMemcpyDeviceToHost, ctx->stream);
+    e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) rc = fail(ctx, SI_E_CUDA, std::string("IPC handle exchange: ") + cudaGetErrorString(e));
+  }
+  cudaFree(dh);
+  if (rc) return rc;
+  for (int p = 0; p < n; ++p) {
+    if (p == r) {
+      peers[p] = base;
+      continue;
+    }
+    cudaIpcMemHandle_t hp;
+    std::memcpy(&hp, all.data() + HB * p, HB);
+    e = cudaIpcOpenMemHandle(&peers[p], hp, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < p; ++q)
+        if (q != r) cudaIpcCloseMemHandle(peers[q]);
+      return fail(ctx, SI_E_CUDA, std::string("cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+    }
+  }
+  return SI_OK;
+}
+
+void comm_p2p_unmap(si_ctx* ctx, void** peers) {
+  for (int p = 0; p < ctx->nranks; ++p)
+    if (p != ctx->rank && peers[p]) cudaIpcCloseMemHandle(peers[p]);
 }
 
 int comm_allreduce_sum(si_ctx* ctx, const float* send, float* recv, size_t count, cudaStream_t s) {

@@ -1101,6 +1101,57 @@ void launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
 }
 
 // ---------------------------------------------------------------------------
+// All-gather over NVLink peer memory (one CTA per destination rank).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) p2p_allgather_kernel(const P2PGather g) {
+  const uint32_t p = blockIdx.x;  // destination rank
+  uint8_t* dst_block = g.block[p];
+#pragma unroll
+  for (int v = 0; v < 2; ++v) {
+    const uint32_t cnt = g.count[v];
+    if (cnt == 0) continue;
+    const float* src = g.send[v];
+    float* dst = reinterpret_cast<float*>(dst_block + g.recv_off[v]) + uint64_t(g.rank) * cnt;
+    if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+      const uint32_t c4 = cnt / 4;
+      for (uint32_t i = threadIdx.x; i < c4; i += blockDim.x)
+        reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
+      for (uint32_t i = c4 * 4 + threadIdx.x; i < cnt; i += blockDim.x) dst[i] = src[i];
+    } else {
+      for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) dst[i] = src[i];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // every thread's stores above are ordered (bar.sync, then this cumulative
+    // system-scope fence) before the flag
+    uint32_t* flag = reinterpret_cast<uint32_t*>(dst_block + g.flag_off + 64ull * g.rank);
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(g.epoch) : "memory");
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    const long long t0 = clock64();
+    for (uint32_t q = 0; q < g.n; ++q) {
+      if (q == g.rank) continue;
+      const uint32_t* f = reinterpret_cast<const uint32_t*>(g.block[g.rank] + g.flag_off + 64ull * q);
+      while (true) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        if (int32_t(v - g.epoch) >= 0) break;
+        if (clock64() - t0 > kWaitCycles) {
+          if (g.err) atomicOr(g.err, KERR_TIMEOUT_FULL);
+          return;
+        }
+      }
+    }
+  }
+}
+
+void launch_p2p_allgather(const P2PGather& g, cudaStream_t s) {
+  p2p_allgather_kernel<<<g.n, 256, 0, s>>>(g);
+}
+
+// ---------------------------------------------------------------------------
 // Greedy argmax under f32::total_cmp, last index among equal maxima.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ unsigned long long argmax_key(float f, uint32_t idx) {

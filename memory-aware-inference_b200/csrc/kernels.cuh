@@ -79,6 +79,24 @@ void launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 void launch_rope(const float* x, const float* freq, uint32_t heads, uint32_t hd, uint32_t pos,
                  float* out, cudaStream_t s);
 
+// All-gather over NVLink peer memory between the ranks' scratch blocks (mapped
+// with CUDA IPC): every rank stores its slice of one or two vectors straight
+// into every rank's receive buffers (same offsets in every block), then
+// raises its flag in each block with a system-scope release; the kernel ends
+// once this rank has seen every peer's flag reach `epoch` (bounded wait; a
+// timeout sets KERR_TIMEOUT_FULL).
+constexpr int kP2PMaxRanks = 8;
+struct P2PGather {
+  uint8_t* block[kP2PMaxRanks];  // every rank's scratch block, mapped here
+  const float* send[2];
+  uint64_t recv_off[2];          // byte offsets of the receive vectors in a block
+  uint32_t count[2];             // floats per rank (count[1] = 0: one vector)
+  uint32_t n, rank, epoch;
+  uint64_t flag_off;             // byte offset of the flag words (64 B per rank)
+  int* err;
+};
+void launch_p2p_allgather(const P2PGather& g, cudaStream_t s);
+
 // Greedy argmax (runtime.rs:4301-4309). `key` is one device u64 scratch word;
 // *index receives the index (0xFFFFFFFF when no finite value exists).
 void launch_argmax(const float* v, uint64_t n, unsigned long long* key, uint32_t* index,

@@ -86,6 +86,11 @@ struct si_model {
       *att_full, *gate_full, *gate_l, *act, *act_full, *logits, *logits_full, *rope, *part, *embed;
   uint32_t* d_token;
   unsigned long long *d_key, *d_keys;
+  // NVLink peer all-gather: every rank's scratch block mapped here (CUDA IPC)
+  bool p2p = false;
+  void* peer_block[kP2PMaxRanks] = {};
+  uint32_t p2p_epoch = 0;
+  uint64_t flag_off = 0;
   std::vector<float> rope_host;
   bool accounted = false;  // device bytes recorded in the context telemetry
 };
@@ -309,7 +314,7 @@ int compute_plan(si_model* m, uint64_t budget, uint32_t depth, std::vector<bool>
     else
       state_bytes += 2 * align256(uint64_t(m->kvh_l) * c.kv_capacity * c.attn_head_dim * 2);
   }
-  uint64_t scratch_bytes = 4 * 256;  // token + argmax keys
+  uint64_t scratch_bytes = 4 * 256 + 64 * kP2PMaxRanks;  // token, argmax keys, peer flags
   for (uint64_t f : scratch_float_counts(*m)) scratch_bytes += align256(f * 4);
   uint64_t max_layer = 0, all_layers = 0;
   for (uint32_t l = 0; l < c.layers; ++l) {
@@ -407,6 +412,7 @@ void free_model(si_model* m) {
     if (m->compute_done[i]) cudaEventDestroy(m->compute_done[i]);
   }
   if (m->state_block) cudaFree(m->state_block);
+  if (m->p2p) comm_p2p_unmap(m->ctx, m->peer_block);
   if (m->scratch_block) cudaFree(m->scratch_block);
   if (m->accounted) {
     note_alloc(m->ctx, -int64_t(m->plan.resident_weight_bytes + m->plan.ring_bytes + m->plan.state_bytes +
@@ -582,6 +588,7 @@ extern "C" int si_model_create_synthetic(si_ctx* ctx, const si_model_config* cfg
     m->d_token = reinterpret_cast<uint32_t*>(s);
     m->d_key = reinterpret_cast<unsigned long long*>(s + 256);
     m->d_keys = reinterpret_cast<unsigned long long*>(s + 512);
+    m->flag_off = uint64_t(s + 1024 - m->scratch_block);
   }
   rope_freqs(c.rope_theta, c.rotary_dim, &m->rope_host);
   if (!m->rope_host.empty())
@@ -591,6 +598,15 @@ extern "C" int si_model_create_synthetic(si_ctx* ctx, const si_model_config* cfg
     rc = cuda_fail(ctx, e, "model upload");
     free_model(m);
     return rc;
+  }
+  // sharded: all-gathers go straight into the peers' scratch blocks over
+  // NVLink (the zeroed flags are in place on every rank: the mapping is itself
+  // a collective); NCCL when the context asks for it or mapping fails
+  if (m->n > 1 && m->n <= kP2PMaxRanks && !(ctx->cfg.flags & SI_CTX_FLAG_NCCL_COLLECTIVES)) {
+    if (comm_p2p_map(ctx, m->scratch_block, m->peer_block) == SI_OK)
+      m->p2p = true;
+    else
+      ctx->err.clear();
   }
   note_alloc(ctx, int64_t(resident + m->plan.ring_bytes + state_bytes + scratch_bytes));
   note_weights(ctx, int64_t(resident));
@@ -731,13 +747,38 @@ int run_qmv(si_model* m, const QmvParams& p) {
 
 // Row-sharded output with residual: rows [H_l*r, H_l*(r+1)) of hidden are
 // updated; with n > 1 they are written to `slice` and all-gathered.
+// All-gather of one or two row-sharded vectors into their full copies (which
+// live in the scratch block): NVLink peer stores when mapped, else NCCL.
+int gather(si_model* m, const float* s1, float* r1, uint32_t n1, const float* s2 = nullptr, float* r2 = nullptr,
+           uint32_t n2 = 0) {
+  if (!m->p2p)
+    return n2 ? comm_allgather2(m->ctx, s1, r1, n1, s2, r2, n2, m->ctx->stream)
+              : comm_allgather(m->ctx, s1, r1, n1, m->ctx->stream);
+  P2PGather g = {};
+  for (int i = 0; i < m->n; ++i) g.block[i] = static_cast<uint8_t*>(m->peer_block[i]);
+  g.send[0] = s1;
+  g.send[1] = s2;
+  g.recv_off[0] = uint64_t(reinterpret_cast<uint8_t*>(r1) - m->scratch_block);
+  g.recv_off[1] = r2 ? uint64_t(reinterpret_cast<uint8_t*>(r2) - m->scratch_block) : 0;
+  g.count[0] = n1;
+  g.count[1] = n2;
+  g.n = uint32_t(m->n);
+  g.rank = uint32_t(m->r);
+  g.epoch = ++m->p2p_epoch;
+  g.flag_off = m->flag_off;
+  g.err = m->ctx->d_err;
+  launch_p2p_allgather(g, m->ctx->stream);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SI_OK : cuda_fail(m->ctx, e, "peer all-gather launch");
+}
+
 int residual_matvec(si_model* m, QmvParams p, const uint8_t* w) {
   const uint32_t r0 = m->H_l * uint32_t(m->r);
   p.seg[0] = {w, m->n > 1 ? m->slice : m->hidden + r0, m->hidden + r0, m->H_l, 0};
   p.items = m->H_l;
   int rc = run_qmv(m, p);
   if (rc) return rc;
-  if (m->n > 1) return comm_allgather(m->ctx, m->slice, m->hidden, m->H_l, m->ctx->stream);
+  if (m->n > 1) return gather(m, m->slice, m->hidden, m->H_l);
   return SI_OK;
 }
 
@@ -756,7 +797,7 @@ int mlp(si_model* m, uint32_t l, const uint8_t* base) {
   if (rc) return rc;
   const float* act = m->act;
   if (m->n > 1) {
-    if ((rc = comm_allgather(m->ctx, m->act, m->act_full, m->I_l, m->ctx->stream))) return rc;
+    if ((rc = gather(m, m->act, m->act_full, m->I_l))) return rc;
     act = m->act_full;
   }
   QmvParams d = qmv_base(m, c.down_type, c.intermediate);
@@ -803,7 +844,7 @@ int gdn_layer(si_model* m, uint32_t l, const uint8_t* base) {
   const float* core = m->core;
   const float* z = m->z;
   if (m->n > 1) {
-    if ((rc = comm_allgather2(m->ctx, m->core, m->core_full, vw_l, m->z, m->z_full, vw_l, m->ctx->stream)))
+    if ((rc = gather(m, m->core, m->core_full, vw_l, m->z, m->z_full, vw_l)))
       return rc;
     core = m->core_full;
     z = m->z_full;
@@ -862,8 +903,7 @@ int attn_layer(si_model* m, uint32_t l, const uint8_t* base, uint64_t position) 
   const float* gate = m->qg + qw_l;
   if (m->n > 1) {
     // gate half of the local q projection is contiguous after the queries
-    if ((rc = comm_allgather2(m->ctx, m->att, m->att_full, qw_l, m->qg + qw_l, m->gate_full, qw_l,
-                              m->ctx->stream)))
+    if ((rc = gather(m, m->att, m->att_full, qw_l, m->qg + qw_l, m->gate_full, qw_l)))
       return rc;
     att = m->att_full;
     gate = m->gate_full;

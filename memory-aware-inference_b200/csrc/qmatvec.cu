@@ -841,12 +841,10 @@ int launch_qmv(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
         }
         return SI_OK;
       }
-#ifndef SI_NO_TC
       if (qmv_tc_eligible(p)) {
         const int rc = launch_qmv_tc(p, stream, sm_count, pdl, msg);
         if (rc != SI_E_UNSUPPORTED) return rc;
       }
-#endif
       // two rows per team step share each x load (SwiGLU: gate and up rows)
       return launch_t<SI_GGML_TYPE_Q4_K, 2>(p, stream, sm_count, pdl, msg);
     case SI_GGML_TYPE_Q5_K:

@@ -4,7 +4,9 @@ One process per GPU (2, 4 or 8, as many as are visible; skipped with fewer
 than two). Every rank builds only its shard of a small Qwen3.6-shaped model,
 decodes greedily with an all-gather of every sharded output vector, and must
 produce the 1-GPU token IDs and logits exactly: sharding changes which GPU
-computes a row, never a row's arithmetic.
+computes a row, never a row's arithmetic. Both transports of the sharded
+vectors are checked: stores into the peers' memory over NVLink (the default)
+and NCCL all-gathers.
 """
 import os
 
@@ -32,21 +34,22 @@ def _decode(mai, ctx):
         m.close()
 
 
-def _worker(rank, world, uid, out):
+def _worker(rank, world, uid, flags, out):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
     sys.path.insert(0, here)
     from conftest import load_package
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     mai = load_package()
-    ctx = mai.CudaContext(rank)
+    ctx = mai.CudaContext(rank, flags=flags)
     ctx.comm_init(world, rank, uid)
     ids, logits = _decode(mai, ctx)
     ctx.close()
     out[rank] = (ids, logits.tobytes())
 
 
-def test_row_sharded_decode_matches_one_gpu(mai):
+@pytest.mark.parametrize("transport", ["nvlink_peer", "nccl"])
+def test_row_sharded_decode_matches_one_gpu(mai, transport):
     import torch
     import torch.multiprocessing as mp
     n = torch.cuda.device_count()
@@ -57,7 +60,8 @@ def test_row_sharded_decode_matches_one_gpu(mai):
     ctx = mgr = None
     mgr = mp.Manager()
     out = mgr.dict()
-    mp.spawn(_worker, args=(world, uid, out), nprocs=world, join=True)
+    flags = mai.CTX_FLAG_NCCL_COLLECTIVES if transport == "nccl" else 0
+    mp.spawn(_worker, args=(world, uid, flags, out), nprocs=world, join=True)
     ctx = mai.CudaContext(0)
     ref_ids, ref_logits = _decode(mai, ctx)
     ctx.close()
