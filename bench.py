@@ -305,12 +305,19 @@ def run_ours(args, world, rank, local):
         del w
     weights.clear()
     torch.cuda.empty_cache()
-    kern = measure_kernels(mai, ctx, torch, np) if not args.no_extras else None
+    # the secondary measurements report a failure in their own sub-object
+    # instead of taking the headline line down with them
+    def guarded(fn, *a):
+        try:
+            return fn(*a)
+        except Exception as e:  # noqa: BLE001 - recorded, not hidden
+            return {"error": f"{type(e).__name__}: {e}"[:300]}
+    kern = guarded(measure_kernels, mai, ctx, torch, np) if not args.no_extras else None
     ctx.close()
-    if kern is not None:
-        kern["gdn_layer_config3"] = measure_layer(mai, local, "gdn", 0, 64)
-        kern["attention_layer_config4"] = measure_layer(mai, local, "attention", 8192, 64)
-    dec = run_decode(args, mai, torch, np, world, rank, local) if not args.no_decode else None
+    if isinstance(kern, dict) and "error" not in kern:
+        kern["gdn_layer_config3"] = guarded(measure_layer, mai, local, "gdn", 0, 64)
+        kern["attention_layer_config4"] = guarded(measure_layer, mai, local, "attention", 8192, 64)
+    dec = guarded(run_decode, args, mai, torch, np, world, rank, local) if not args.no_decode else None
     if rank == 0:
         line["kernels"] = kern
         line["decode"] = dec
