@@ -1,5 +1,7 @@
 // NCCL communicator attached to a context: one process per GPU, row-sharded
-// weights, all-gather of each sharded output vector over NVLink/NVSwitch.
+// weights. NCCL carries set-up (including the exchange of CUDA IPC handles
+// that maps every rank's model scratch into its peers, for the NVLink
+// peer-store all-gathers of kernels.cu) and the collectives that stay on it.
 #include <nccl.h>
 
 #include <chrono>
