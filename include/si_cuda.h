@@ -284,6 +284,41 @@ int si_model_decode_token(si_model* m, uint32_t token, uint64_t position, uint32
 int si_model_generate(si_model* m, const uint32_t* prompt, uint64_t n_prompt, uint64_t max_new,
                       uint32_t* out_ids, uint64_t* n_out);
 
+/* ---- GGUF container (host only; model.rs:583-1236) ------------------------ */
+/* An open GGUF v2/v3 file: metadata and tensor index parsed, payloads left on
+ * disk and read on demand with pread. Errors: si_global_last_error(), with
+ * the reference's messages (model.rs:1034-1120 parse_gguf). */
+typedef struct si_gguf si_gguf;
+/* GgufModelStore::open (model.rs:628-666). */
+int si_gguf_open(const char* path, si_gguf** out);
+void si_gguf_close(si_gguf* g);
+int si_gguf_info(const si_gguf* g, uint32_t* version, uint64_t* tensor_count,
+                 uint64_t* metadata_count);
+/* Entry `index` of the tensor index in file order (GgufTensorInfo,
+ * model.rs:498-505): name (owned by g; a C string, so it ends at an embedded NUL), rank, dims (the first 4, 1-padded), ggml
+ * type, and the resolved payload range [data_start, data_start+data_len) that
+ * runs to the next tensor's offset or to the end of the file. */
+int si_gguf_tensor_info(const si_gguf* g, uint64_t index, const char** name, uint32_t* ndim,
+                        uint64_t* dims, uint32_t* ggml_type, uint64_t* data_start,
+                        uint64_t* data_len);
+/* GgufModelStore::tensor lookup by name (model.rs:668-686). */
+int si_gguf_find_tensor(const si_gguf* g, const char* name, uint64_t* index);
+/* Typed metadata: u64 accepts U8/U16/U32/U64 (required_u32, model.rs:454),
+ * f64 accepts F32/F64 (required_f32, model.rs:476), string (model.rs:444),
+ * array_len (required_array_len, model.rs:487). */
+int si_gguf_meta_u64(const si_gguf* g, const char* key, uint64_t* out);
+int si_gguf_meta_f64(const si_gguf* g, const char* key, double* out);
+int si_gguf_meta_string(const si_gguf* g, const char* key, const char** out);
+int si_gguf_meta_array_len(const si_gguf* g, const char* key, uint64_t* out);
+/* Copy bytes [offset, offset+bytes) of tensor `index`'s payload
+ * (stage_tensor_payload, model.rs:867-886). */
+int si_gguf_read(const si_gguf* g, uint64_t index, uint64_t offset, void* dst, uint64_t bytes);
+/* GgufQwen35Config::from_metadata (model.rs:350-417) plus the rotary width
+ * (qwen35_runtime.rs:811-813) into a decode config; the ggml types of
+ * blk.0.ffn_gate / blk.0.ffn_down / output fill mlp/down/head_type.
+ * kv_capacity 0 picks min(context_length, 4096). */
+int si_gguf_qwen35_config(const si_gguf* g, uint32_t kv_capacity, si_model_config* out);
+
 /* ---- multi-GPU row sharding over NCCL ----------------------------------- */
 #define SI_COMM_ID_BYTES 128
 int si_comm_unique_id(void* id_out /* SI_COMM_ID_BYTES */);

@@ -25,6 +25,8 @@ LIB_PATH = os.path.join(_HERE, "libsi_cuda.so")
 GGML_TYPE_F32, GGML_TYPE_Q4_K, GGML_TYPE_Q5_K, GGML_TYPE_Q6_K = 0, 12, 13, 14
 BLOCK_BYTES = {GGML_TYPE_Q4_K: 144, GGML_TYPE_Q5_K: 176, GGML_TYPE_Q6_K: 210}
 CACHE_F32, CACHE_BF16 = 0, 1
+SI_OK, SI_E_INVALID, SI_E_CUDA, SI_E_NOMEM, SI_E_BUDGET, SI_E_TIMEOUT, SI_E_COMM, SI_E_STATE, SI_E_UNSUPPORTED = \
+    0, -1, -2, -3, -4, -5, -6, -7, -8
 CTX_FLAG_NCCL_COLLECTIVES = 1  # sharded models exchange vectors with NCCL, not NVLink peer stores
 TENSOR_IDS = ["ATTN_NORM", "POST_NORM", "FFN_GATE", "FFN_UP", "FFN_DOWN", "SSM_QKV", "SSM_Z", "SSM_ALPHA",
               "SSM_BETA", "SSM_CONV", "SSM_A", "SSM_DT", "SSM_NORM", "SSM_OUT", "ATTN_Q", "ATTN_K", "ATTN_V",
@@ -145,6 +147,17 @@ def lib():
         "si_model_logits": ([vp, vp, vp], i32),
         "si_model_decode_token": ([vp, u32, u64, vp, vp], i32),
         "si_model_generate": ([vp, vp, u64, u64, vp, vp], i32),
+        "si_gguf_open": ([C.c_char_p, vp], i32),
+        "si_gguf_close": ([vp], None),
+        "si_gguf_info": ([vp, vp, vp, vp], i32),
+        "si_gguf_tensor_info": ([vp, u64, vp, vp, vp, vp, vp, vp], i32),
+        "si_gguf_find_tensor": ([vp, C.c_char_p, vp], i32),
+        "si_gguf_meta_u64": ([vp, C.c_char_p, vp], i32),
+        "si_gguf_meta_f64": ([vp, C.c_char_p, vp], i32),
+        "si_gguf_meta_string": ([vp, C.c_char_p, vp], i32),
+        "si_gguf_meta_array_len": ([vp, C.c_char_p, vp], i32),
+        "si_gguf_read": ([vp, u64, u64, vp, u64], i32),
+        "si_gguf_qwen35_config": ([vp, u32, vp], i32),
         "si_comm_unique_id": ([vp], i32),
         "si_ctx_comm_init": ([vp, i32, i32, vp], i32),
         "si_ctx_comm_info": ([vp, vp, vp], i32),
@@ -487,6 +500,91 @@ def shard_rows(config: SiModelConfig, nranks: int, rank: int, layer: int, tensor
     if rc != 0:
         raise SiError(rc, lib().si_global_last_error().decode())
     return [(buf[2 * i], buf[2 * i + 1]) for i in range(n.value)]
+
+
+def _gck(rc):
+    if rc != 0:
+        raise SiError(rc, lib().si_global_last_error().decode())
+
+
+class GgufFile:
+    """An open GGUF v2/v3 file: metadata and tensor index parsed on the host,
+    payloads read on demand (GgufModelStore, model.rs:583-1030). No device."""
+
+    def __init__(self, path):
+        h = C.c_void_p()
+        _gck(lib().si_gguf_open(os.fsencode(path), C.byref(h)))
+        self.h = h.value
+        ver, nt, nm = C.c_uint32(), C.c_uint64(), C.c_uint64()
+        _gck(lib().si_gguf_info(self.h, C.byref(ver), C.byref(nt), C.byref(nm)))
+        self.version, self.tensor_count, self.metadata_count = ver.value, nt.value, nm.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().si_gguf_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def tensor_info(self, index: int) -> dict:
+        name, nd, ty = C.c_char_p(), C.c_uint32(), C.c_uint32()
+        dims, start, n = (C.c_uint64 * 4)(), C.c_uint64(), C.c_uint64()
+        _gck(lib().si_gguf_tensor_info(self.h, index, C.byref(name), C.byref(nd), dims, C.byref(ty),
+                                       C.byref(start), C.byref(n)))
+        return {"name": name.value.decode(), "shape": [dims[i] for i in range(nd.value)], "ggml_type": ty.value,
+                "data_start": start.value, "data_end": start.value + n.value}
+
+    def tensors(self) -> list:
+        return [self.tensor_info(i) for i in range(self.tensor_count)]
+
+    def find(self, name: str) -> int:
+        idx = C.c_uint64()
+        _gck(lib().si_gguf_find_tensor(self.h, name.encode(), C.byref(idx)))
+        return idx.value
+
+    def meta_u64(self, key: str) -> int:
+        v = C.c_uint64()
+        _gck(lib().si_gguf_meta_u64(self.h, key.encode(), C.byref(v)))
+        return v.value
+
+    def meta_f64(self, key: str) -> float:
+        v = C.c_double()
+        _gck(lib().si_gguf_meta_f64(self.h, key.encode(), C.byref(v)))
+        return v.value
+
+    def meta_string(self, key: str) -> str:
+        v = C.c_char_p()
+        _gck(lib().si_gguf_meta_string(self.h, key.encode(), C.byref(v)))
+        return v.value.decode()
+
+    def meta_array_len(self, key: str) -> int:
+        v = C.c_uint64()
+        _gck(lib().si_gguf_meta_array_len(self.h, key.encode(), C.byref(v)))
+        return v.value
+
+    def read(self, name_or_index, offset: int = 0, nbytes: int = None) -> np.ndarray:
+        idx = self.find(name_or_index) if isinstance(name_or_index, str) else int(name_or_index)
+        if nbytes is None:
+            info = self.tensor_info(idx)
+            nbytes = info["data_end"] - info["data_start"] - offset
+        out = np.empty(nbytes, np.uint8)
+        _gck(lib().si_gguf_read(self.h, idx, offset, _p(out), nbytes))
+        return out
+
+    def qwen35_config(self, kv_capacity: int = 0) -> SiModelConfig:
+        c = SiModelConfig()
+        _gck(lib().si_gguf_qwen35_config(self.h, kv_capacity, C.byref(c)))
+        return c
 
 
 class Model:

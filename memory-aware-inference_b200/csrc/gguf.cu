@@ -1,0 +1,444 @@
+// GGUF container reader (host code): header, typed metadata and tensor index
+// of a GGUF v2/v3 file, parsed as the reference does (src/model.rs:1033-1120
+// parse_gguf, 1155-1205 GgufReader), and the qwen35 execution config derived
+// from its metadata (src/model.rs:350-417 GgufQwen35Config::from_metadata).
+// Tensor payloads are never held here: callers read row ranges with pread.
+#include <fcntl.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cerrno>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/si_cuda.h"
+#include "gguf.h"
+
+namespace si {
+int fail(si_ctx* ctx, int code, const std::string& msg);
+}
+
+namespace {
+
+// Strict UTF-8 check (String::from_utf8 in GgufReader::read_string).
+bool valid_utf8(const std::string& s) {
+  const unsigned char* p = reinterpret_cast<const unsigned char*>(s.data());
+  size_t n = s.size(), i = 0;
+  while (i < n) {
+    unsigned c = p[i];
+    if (c < 0x80) { ++i; continue; }
+    int len = (c >= 0xC2 && c <= 0xDF) ? 2 : (c >= 0xE0 && c <= 0xEF) ? 3 : (c >= 0xF0 && c <= 0xF4) ? 4 : 0;
+    if (!len || i + len > n) return false;
+    unsigned c1 = p[i + 1];
+    if (c == 0xE0 && c1 < 0xA0) return false;   // overlong
+    if (c == 0xED && c1 > 0x9F) return false;   // surrogates
+    if (c == 0xF0 && c1 < 0x90) return false;   // overlong
+    if (c == 0xF4 && c1 > 0x8F) return false;   // above U+10FFFF
+    for (int k = 1; k < len; ++k)
+      if ((p[i + k] & 0xC0) != 0x80) return false;
+    i += len;
+  }
+  return true;
+}
+
+// Sequential reader over the file with bounds checks (GgufReader).
+struct Reader {
+  FILE* f;
+  uint64_t size, offset = 0;
+  std::string err;
+  bool read(void* dst, uint64_t n) {
+    if (!err.empty()) return false;
+    if (n > size || offset > size - n) {
+      err = "GGUF header is truncated";
+      return false;
+    }
+    if (n && fread(dst, 1, n, f) != n) {
+      err = "GGUF read failed";
+      return false;
+    }
+    offset += n;
+    return true;
+  }
+  bool skip(uint64_t n) {
+    if (!err.empty()) return false;
+    if (n > size || offset > size - n) {
+      err = "GGUF header is truncated";
+      return false;
+    }
+    if (fseeko(f, off_t(n), SEEK_CUR) != 0) {
+      err = "GGUF seek failed";
+      return false;
+    }
+    offset += n;
+    return true;
+  }
+  template <typename T>
+  bool pod(T* v) {
+    return read(v, sizeof(T));
+  }
+  bool str(std::string* s) {
+    uint64_t n = 0;
+    if (!pod(&n)) return false;
+    if (n > size - offset) {
+      err = "GGUF header is truncated";
+      return false;
+    }
+    s->resize(n);
+    if (!read(s->data(), n)) return false;
+    if (!valid_utf8(*s)) {
+      err = "GGUF string is not UTF-8";
+      return false;
+    }
+    return true;
+  }
+};
+
+// Element size of the fixed-size metadata value types, 0 for string/array.
+uint64_t value_size(uint32_t t) {
+  switch (t) {
+    case 0: case 1: case 7: return 1;
+    case 2: case 3: return 2;
+    case 4: case 5: case 6: return 4;
+    case 10: case 11: case 12: return 8;
+    default: return 0;
+  }
+}
+
+bool read_value(Reader& r, uint32_t type, si::GgufValue* v, int depth) {
+  v->type = type;
+  switch (type) {
+    case 0: { uint8_t x; if (!r.pod(&x)) return false; v->u = x; v->i = x; v->f = x; return true; }
+    case 1: { int8_t x; if (!r.pod(&x)) return false; v->i = x; v->u = uint64_t(int64_t(x)); v->f = x; return true; }
+    case 2: { uint16_t x; if (!r.pod(&x)) return false; v->u = x; v->i = x; v->f = x; return true; }
+    case 3: { int16_t x; if (!r.pod(&x)) return false; v->i = x; v->u = uint64_t(int64_t(x)); v->f = x; return true; }
+    case 4: { uint32_t x; if (!r.pod(&x)) return false; v->u = x; v->i = x; v->f = x; return true; }
+    case 5: { int32_t x; if (!r.pod(&x)) return false; v->i = x; v->u = uint64_t(int64_t(x)); v->f = x; return true; }
+    case 6: { float x; if (!r.pod(&x)) return false; v->f = x; return true; }
+    case 7: { uint8_t x; if (!r.pod(&x)) return false; v->u = x != 0; v->i = x != 0; return true; }
+    case 8: return r.str(&v->s);
+    case 9: {
+      uint32_t et = 0;
+      uint64_t count = 0;
+      if (!r.pod(&et) || !r.pod(&count)) return false;
+      if (depth > 4) {
+        r.err = "GGUF arrays nest too deeply";
+        return false;
+      }
+      v->elem_type = et;
+      v->count = count;
+      const uint64_t es = value_size(et);
+      if (count == 0) return true;  // element type is never read
+      if (es) {  // fixed-size elements: skip them (only the length is kept)
+        if (count > r.size / es) {
+          r.err = "GGUF header is truncated";
+          return false;
+        }
+        return r.skip(count * es);
+      }
+      if (et != 8 && et != 9) {
+        r.err = "unsupported GGUF metadata type " + std::to_string(et);
+        return false;
+      }
+      for (uint64_t i = 0; i < count; ++i) {
+        si::GgufValue e;
+        if (!read_value(r, et, &e, depth + 1)) return false;
+      }
+      return true;
+    }
+    case 10: { uint64_t x; if (!r.pod(&x)) return false; v->u = x; v->i = int64_t(x); v->f = double(x); return true; }
+    case 11: { int64_t x; if (!r.pod(&x)) return false; v->i = x; v->u = uint64_t(x); v->f = double(x); return true; }
+    case 12: { double x; if (!r.pod(&x)) return false; v->f = x; return true; }
+    default:
+      r.err = "unsupported GGUF metadata type " + std::to_string(type);
+      return false;
+  }
+}
+
+}  // namespace
+
+namespace si {
+
+// U8/U16/U32/U64: the types required_u32 (model.rs:454-469) accepts.
+bool gguf_is_unsigned(const GgufValue& v) { return v.type == 0 || v.type == 2 || v.type == 4 || v.type == 10; }
+
+int gguf_parse(const char* path, si_gguf** out, std::string* err) {
+  *out = nullptr;
+  FILE* f = fopen(path, "rb");
+  if (!f) {
+    *err = std::string("open GGUF model ") + path + ": " + std::strerror(errno);
+    return SI_E_INVALID;
+  }
+  struct stat st;
+  if (fstat(fileno(f), &st) != 0) {
+    *err = std::string("stat GGUF model ") + path + ": " + std::strerror(errno);
+    fclose(f);
+    return SI_E_INVALID;
+  }
+  Reader r{f, uint64_t(st.st_size)};
+  auto g = new si_gguf();
+  g->path = path;
+  g->file_size = uint64_t(st.st_size);
+  auto bad = [&](const std::string& msg) {
+    *err = msg;
+    fclose(f);
+    delete g;
+    return SI_E_INVALID;
+  };
+  char magic[4];
+  if (!r.read(magic, 4)) return bad(r.err);
+  if (std::memcmp(magic, "GGUF", 4) != 0) return bad("GGUF header has invalid magic");
+  uint32_t version = 0;
+  uint64_t ntensors = 0, nmeta = 0;
+  if (!r.pod(&version)) return bad(r.err);
+  if (version != 2 && version != 3) return bad("unsupported GGUF version " + std::to_string(version));
+  if (!r.pod(&ntensors) || !r.pod(&nmeta)) return bad(r.err);
+  g->version = version;
+  for (uint64_t i = 0; i < nmeta; ++i) {
+    std::string key;
+    uint32_t type = 0;
+    GgufValue v;
+    if (!r.str(&key) || !r.pod(&type) || !read_value(r, type, &v, 0)) return bad(r.err);
+    if (!g->meta.emplace(key, v).second) return bad("GGUF metadata contains duplicate keys");
+  }
+  g->tensors.reserve(std::min<uint64_t>(ntensors, r.size / 24));  // an entry takes 24 B at least
+  for (uint64_t i = 0; i < ntensors; ++i) {
+    g->tensors.emplace_back();
+    GgufTensor& t = g->tensors.back();
+    uint32_t nd = 0;
+    if (!r.str(&t.name) || !r.pod(&nd)) return bad(r.err);
+    if (nd > (r.size - r.offset) / 8) return bad("GGUF header is truncated");
+    t.ndim = nd;
+    t.dims.resize(nd);
+    for (uint32_t d = 0; d < nd; ++d)
+      if (!r.pod(&t.dims[d])) return bad(r.err);
+    if (!r.pod(&t.type) || !r.pod(&t.offset)) return bad(r.err);
+    g->index[t.name] = i;  // a later entry of the same name wins (BTreeMap collect)
+  }
+  uint64_t alignment = 32;
+  auto it = g->meta.find("general.alignment");
+  if (it != g->meta.end() && (it->second.type == 4 || it->second.type == 10)) alignment = it->second.u;
+  if (alignment == 0 || (alignment & (alignment - 1))) return bad("GGUF alignment must be a non-zero power of two");
+  const uint64_t data_base = (r.offset + alignment - 1) / alignment * alignment;
+  // a tensor's bytes run from its offset to the next tensor's (by offset) or
+  // to the end of the file
+  std::vector<uint64_t> order(ntensors);
+  for (uint64_t i = 0; i < ntensors; ++i) order[i] = i;
+  std::stable_sort(order.begin(), order.end(),  // sort_by_key is stable
+            [&](uint64_t a, uint64_t b) { return g->tensors[a].offset < g->tensors[b].offset; });
+  for (uint64_t k = 0; k < ntensors; ++k) {
+    GgufTensor& t = g->tensors[order[k]];
+    if (t.offset > g->file_size || data_base > g->file_size - t.offset)
+      return bad("GGUF tensor " + t.name + " exceeds file size");
+    const uint64_t start = data_base + t.offset;
+    const uint64_t end = k + 1 < ntensors ? data_base + g->tensors[order[k + 1]].offset : g->file_size;
+    if (start > end || end > g->file_size) return bad("GGUF tensor " + t.name + " exceeds file size");
+    t.data_start = start;
+    t.data_len = end - start;
+  }
+  fclose(f);
+  g->fd = open(path, O_RDONLY);
+  if (g->fd < 0) return bad(std::string("open GGUF model ") + path + ": " + std::strerror(errno));
+  *out = g;
+  return SI_OK;
+}
+
+int gguf_read(const si_gguf* g, uint64_t offset, void* dst, uint64_t bytes, std::string* err) {
+  uint8_t* p = static_cast<uint8_t*>(dst);
+  while (bytes) {
+    const ssize_t got = pread(g->fd, p, size_t(std::min<uint64_t>(bytes, uint64_t(1) << 30)), off_t(offset));
+    if (got <= 0) {
+      *err = "GGUF read of " + g->path + " failed: " + (got < 0 ? std::strerror(errno) : "unexpected end of file");
+      return SI_E_INVALID;
+    }
+    p += got;
+    offset += uint64_t(got);
+    bytes -= uint64_t(got);
+  }
+  return SI_OK;
+}
+
+const GgufValue* gguf_meta(const si_gguf* g, const std::string& key) {
+  auto it = g->meta.find(key);
+  return it == g->meta.end() ? nullptr : &it->second;
+}
+
+}  // namespace si
+
+// ---- C ABI -------------------------------------------------------------------
+extern "C" {
+
+int si_gguf_open(const char* path, si_gguf** out) {
+  if (!path || !out) return si::fail(nullptr, SI_E_INVALID, "invalid GGUF arguments");
+  std::string err;
+  int rc = si::gguf_parse(path, out, &err);
+  return rc ? si::fail(nullptr, rc, err) : SI_OK;
+}
+
+void si_gguf_close(si_gguf* g) {
+  if (!g) return;
+  if (g->fd >= 0) close(g->fd);
+  delete g;
+}
+
+int si_gguf_info(const si_gguf* g, uint32_t* version, uint64_t* tensor_count, uint64_t* metadata_count) {
+  if (!g) return SI_E_INVALID;
+  if (version) *version = g->version;
+  if (tensor_count) *tensor_count = g->tensors.size();
+  if (metadata_count) *metadata_count = g->meta.size();
+  return SI_OK;
+}
+
+int si_gguf_tensor_info(const si_gguf* g, uint64_t index, const char** name, uint32_t* ndim, uint64_t* dims,
+                        uint32_t* ggml_type, uint64_t* data_start, uint64_t* data_len) {
+  if (!g || index >= g->tensors.size()) return si::fail(nullptr, SI_E_INVALID, "GGUF tensor index out of range");
+  const si::GgufTensor& t = g->tensors[index];
+  if (name) *name = t.name.c_str();
+  if (ndim) *ndim = t.ndim;
+  if (dims)
+    for (uint32_t d = 0; d < 4; ++d) dims[d] = d < t.ndim ? t.dims[d] : 1;  // first 4 of ndim
+  if (ggml_type) *ggml_type = t.type;
+  if (data_start) *data_start = t.data_start;
+  if (data_len) *data_len = t.data_len;
+  return SI_OK;
+}
+
+int si_gguf_find_tensor(const si_gguf* g, const char* name, uint64_t* index) {
+  if (!g || !name || !index) return SI_E_INVALID;
+  auto it = g->index.find(name);
+  if (it == g->index.end()) return si::fail(nullptr, SI_E_INVALID, std::string("unknown GGUF tensor ") + name);
+  *index = it->second;
+  return SI_OK;
+}
+
+int si_gguf_meta_u64(const si_gguf* g, const char* key, uint64_t* out) {
+  const si::GgufValue* v = g && key ? si::gguf_meta(g, key) : nullptr;
+  if (!v) return si::fail(nullptr, SI_E_INVALID, std::string("GGUF metadata is missing ") + (key ? key : ""));
+  if (!si::gguf_is_unsigned(*v))
+    return si::fail(nullptr, SI_E_INVALID, std::string("GGUF metadata ") + key + " has unexpected value");
+  *out = v->u;
+  return SI_OK;
+}
+
+int si_gguf_meta_f64(const si_gguf* g, const char* key, double* out) {
+  const si::GgufValue* v = g && key ? si::gguf_meta(g, key) : nullptr;
+  if (!v) return si::fail(nullptr, SI_E_INVALID, std::string("GGUF metadata is missing ") + (key ? key : ""));
+  if (v->type != 6 && v->type != 12)
+    return si::fail(nullptr, SI_E_INVALID, std::string("GGUF metadata ") + key + " has unexpected value");
+  *out = v->f;
+  return SI_OK;
+}
+
+int si_gguf_meta_string(const si_gguf* g, const char* key, const char** out) {
+  const si::GgufValue* v = g && key ? si::gguf_meta(g, key) : nullptr;
+  if (!v) return si::fail(nullptr, SI_E_INVALID, std::string("GGUF metadata is missing ") + (key ? key : ""));
+  if (v->type != 8) return si::fail(nullptr, SI_E_INVALID, std::string("GGUF metadata ") + key + " has unexpected value");
+  *out = v->s.c_str();
+  return SI_OK;
+}
+
+int si_gguf_meta_array_len(const si_gguf* g, const char* key, uint64_t* out) {
+  const si::GgufValue* v = g && key ? si::gguf_meta(g, key) : nullptr;
+  if (!v) return si::fail(nullptr, SI_E_INVALID, std::string("GGUF metadata is missing ") + (key ? key : ""));
+  if (v->type != 9) return si::fail(nullptr, SI_E_INVALID, std::string("GGUF metadata ") + key + " has unexpected value");
+  *out = v->count;
+  return SI_OK;
+}
+
+int si_gguf_read(const si_gguf* g, uint64_t index, uint64_t offset, void* dst, uint64_t bytes) {
+  if (!g || (!dst && bytes) || index >= g->tensors.size()) return si::fail(nullptr, SI_E_INVALID, "invalid GGUF read");
+  const si::GgufTensor& t = g->tensors[index];
+  if (offset > t.data_len || bytes > t.data_len - offset)
+    return si::fail(nullptr, SI_E_INVALID, "GGUF read beyond tensor " + t.name);
+  std::string err;
+  int rc = si::gguf_read(g, t.data_start + offset, dst, bytes, &err);
+  return rc ? si::fail(nullptr, rc, err) : SI_OK;
+}
+
+int si_gguf_qwen35_config(const si_gguf* g, uint32_t kv_capacity, si_model_config* c) {
+  if (!g || !c) return si::fail(nullptr, SI_E_INVALID, "invalid GGUF config arguments");
+  const char* arch = nullptr;
+  if (int rc = si_gguf_meta_string(g, "general.architecture", &arch)) return rc;
+  if (std::string(arch) != "qwen35")
+    return si::fail(nullptr, SI_E_UNSUPPORTED, std::string("unsupported GGUF architecture ") + arch + "; expected qwen35");
+  uint64_t H, I, L, qh, kvh, kl, vl, ctxlen, interval, inner, state, groups, conv, rank, eos, vocab, rot;
+  double eps, theta;
+  const struct {
+    const char* key;
+    uint64_t* dst;
+  } ints[] = {{"qwen35.embedding_length", &H},         {"qwen35.feed_forward_length", &I},
+              {"qwen35.block_count", &L},              {"qwen35.attention.head_count", &qh},
+              {"qwen35.attention.head_count_kv", &kvh}, {"qwen35.attention.key_length", &kl},
+              {"qwen35.attention.value_length", &vl},  {"qwen35.context_length", &ctxlen},
+              {"tokenizer.ggml.eos_token_id", &eos},   {"qwen35.full_attention_interval", &interval},
+              {"qwen35.ssm.inner_size", &inner},       {"qwen35.ssm.state_size", &state},
+              {"qwen35.ssm.group_count", &groups},     {"qwen35.ssm.conv_kernel", &conv},
+              {"qwen35.ssm.time_step_rank", &rank}};
+  // required_u32 (model.rs:454-469): unsigned types only, and it must fit u32
+  auto req_u32 = [&](const char* key, uint64_t* dst) -> int {
+    if (int rc = si_gguf_meta_u64(g, key, dst)) return rc;
+    if (*dst > 0xFFFFFFFFull) return si::fail(nullptr, SI_E_INVALID, std::string("GGUF metadata ") + key + " overflows u32");
+    return SI_OK;
+  };
+  for (const auto& e : ints) {
+    if (e.dst == &ctxlen) {  // vocab and the floats come between these in from_metadata
+      if (int rc = si_gguf_meta_array_len(g, "tokenizer.ggml.tokens", &vocab)) return rc;
+    }
+    if (e.dst == &eos) {
+      if (int rc = si_gguf_meta_f64(g, "qwen35.attention.layer_norm_rms_epsilon", &eps)) return rc;
+      if (int rc = si_gguf_meta_f64(g, "qwen35.rope.freq_base", &theta)) return rc;
+    }
+    if (int rc = req_u32(e.key, e.dst)) return rc;
+  }
+  const float eps_f = float(eps), theta_f = float(theta);
+  if (!H || !I || !L || !qh || !kvh || !kl || !vl || !vocab || !ctxlen || !interval || !inner || !state ||
+      !groups || !conv || !rank || !std::isfinite(eps_f) || eps_f <= 0.f || !std::isfinite(theta_f) || theta_f <= 1.f)
+    return si::fail(nullptr, SI_E_INVALID, "Qwen3.6 GGUF config contains invalid dimensions");
+  if (qh % kvh) return si::fail(nullptr, SI_E_INVALID, "Qwen3.6 attention heads must be divisible by key/value heads");
+  if (inner % state) return si::fail(nullptr, SI_E_INVALID, "Qwen3.6 SSM inner size must be divisible by state size");
+  // the runtime reads the rotary width separately (qwen35_runtime.rs:811-813)
+  {
+    const si::GgufValue* v = si::gguf_meta(g, "qwen35.rope.dimension_count");
+    if (!v || (v->type != 4 && v->type != 10) || v->u > 0xFFFFFFFFull)
+      return si::fail(nullptr, SI_E_INVALID, "GGUF model is missing qwen35.rope.dimension_count");
+    rot = v->u;
+  }
+  if (vocab > 0xFFFFFFFFull) return si::fail(nullptr, SI_E_INVALID, "Qwen3.6 GGUF vocabulary overflows u32");
+  // one head width per attention layer and one dt/alpha/beta row per value head
+  if (vl != kl) return si::fail(nullptr, SI_E_UNSUPPORTED, "attention value_length must equal key_length");
+  if (rank != inner / state) return si::fail(nullptr, SI_E_UNSUPPORTED, "SSM time_step_rank must equal inner_size / state_size");
+  si_model_config_qwen36_27b(c);
+  c->hidden = uint32_t(H);
+  c->intermediate = uint32_t(I);
+  c->layers = uint32_t(L);
+  c->vocab = uint32_t(vocab);
+  c->attn_interval = uint32_t(interval);
+  c->attn_q_heads = uint32_t(qh);
+  c->attn_kv_heads = uint32_t(kvh);
+  c->attn_head_dim = uint32_t(kl);
+  c->rotary_dim = uint32_t(rot);
+  c->rope_theta = theta_f;
+  c->gdn_key_heads = uint32_t(groups);                  // ssm_key_heads (model.rs:419-421)
+  c->gdn_value_heads = uint32_t(inner / state);         // ssm_value_heads (model.rs:424-426)
+  c->gdn_head_dim = uint32_t(state);                    // ssm_key_dim / ssm_value_dim
+  c->conv_kernel = uint32_t(conv);
+  c->rms_eps = eps_f;
+  c->eos_token = uint32_t(eos);
+  c->kv_capacity = kv_capacity ? kv_capacity : uint32_t(std::min<uint64_t>(ctxlen, 4096));
+  c->weight_init = 0;
+  // the config's per-role types are those of the first layer / the head
+  auto type_of = [&](const std::string& name, uint32_t* t) {
+    auto it = g->index.find(name);
+    if (it != g->index.end()) *t = g->tensors[it->second].type;
+  };
+  type_of("blk.0.ffn_gate.weight", &c->mlp_type);
+  type_of("blk.0.ffn_down.weight", &c->down_type);
+  type_of("output.weight", &c->head_type);
+  return SI_OK;
+}
+
+}  // extern "C"
