@@ -254,6 +254,15 @@ void si_model_config_qwen36_27b(si_model_config* c);
  * communicator attached (si_ctx_comm_init) every rank builds only its shard. */
 int si_model_create_synthetic(si_ctx* ctx, const si_model_config* c, uint64_t seed,
                               si_model** out);
+/* A model from a qwen35 GGUF file (Qwen35Runtime over GgufModelStore,
+ * qwen35_runtime.rs:1519-1750; model.rs:628-790): config from the metadata,
+ * every layer's tensors checked for kind, type, shape and payload size before
+ * any allocation, each rank's row shards read from the file into pinned host
+ * memory, then the same residency plan and decode path as the synthetic
+ * model. Projections may be Q4_K/Q5_K/Q6_K per tensor; token_embd must be
+ * Q4_K; norms, conv, alpha/beta, ssm_a and ssm_dt must be F32. kv_capacity 0
+ * picks min(context_length, 4096). */
+int si_model_create_gguf(si_ctx* ctx, const char* path, uint32_t kv_capacity, si_model** out);
 void si_model_destroy(si_model* m);
 int si_model_plan(const si_model* m, si_plan_info* out);
 /* The same residency plan without a device or any allocation (planner dry

@@ -136,6 +136,7 @@ def lib():
         "si_attention_decode_noalloc_dev": ([vp, vp, vp], i32),
         "si_model_config_qwen36_27b": ([vp], None),
         "si_model_create_synthetic": ([vp, vp, u64, vp], i32),
+        "si_model_create_gguf": ([vp, C.c_char_p, u32, vp], i32),
         "si_model_destroy": ([vp], None),
         "si_model_plan": ([vp, vp], i32),
         "si_model_plan_dry": ([vp, i32, i32, u64, u32, vp], i32),
@@ -596,6 +597,19 @@ class Model:
         h = C.c_void_p()
         ctx._ck(lib().si_model_create_synthetic(ctx.h, C.byref(config), seed, C.byref(h)))
         self.h = h.value
+
+    @classmethod
+    def from_gguf(cls, ctx: CudaContext, path, kv_capacity: int = 0) -> "Model":
+        """Load a qwen35 GGUF file (si_model_create_gguf): config from its
+        metadata, this rank's row shards read from the file."""
+        with GgufFile(path) as g:
+            config = g.qwen35_config(kv_capacity)
+        m = cls.__new__(cls)
+        m.ctx, m.config = ctx, config
+        h = C.c_void_p()
+        ctx._ck(lib().si_model_create_gguf(ctx.h, os.fsencode(path), kv_capacity, C.byref(h)))
+        m.h = h.value
+        return m
 
     def close(self):
         if getattr(self, "h", None):

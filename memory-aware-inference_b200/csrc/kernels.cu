@@ -1295,4 +1295,15 @@ void launch_add(const float* a, const float* b, float* y, uint64_t n, cudaStream
   add_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(a, b, y, n);
 }
 
+// SwiGLU of separately computed gate and up rows: y = silu(g) * u, the
+// formula of the fused pair epilogue.
+__global__ void swiglu_kernel(const float* g, const float* u, float* y, uint64_t n) {
+  const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = g[i] / (1.0f + expf(-g[i])) * u[i];
+}
+
+void launch_swiglu(const float* g, const float* u, float* y, uint64_t n, cudaStream_t s) {
+  swiglu_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(g, u, y, n);
+}
+
 }  // namespace si

@@ -122,5 +122,7 @@ void rope_freqs(float theta, uint32_t dims, std::vector<float>* out);
 
 // Residual add y = a + b (length n).
 void launch_add(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s);
+// y = silu(g) * u (length n): the MLP when gate and up differ in type.
+void launch_swiglu(const float* g, const float* u, float* y, uint64_t n, cudaStream_t s);
 
 }  // namespace si

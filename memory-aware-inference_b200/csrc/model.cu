@@ -8,7 +8,12 @@
 // 2283-2332; residency selection 1552-1733; planner budget check
 // (src/planner.rs:174-251); run_gguf_generation (src/runtime.rs:3560-3614).
 #include <algorithm>
+#include <array>
+#include <atomic>
 #include <cmath>
+#include <functional>
+#include <memory>
+#include <mutex>
 #include <cstring>
 #include <string>
 #include <thread>
@@ -17,6 +22,7 @@
 #include "comm.h"
 #include "common.cuh"
 #include "ctx.h"
+#include "gguf.h"
 #include "kernels.cuh"
 #include "qmatvec.cuh"
 #include "synth.h"
@@ -61,6 +67,9 @@ struct si_model {
   // sharded dims
   uint32_t kh_l = 0, vh_l = 0, qh_l = 0, kv_lo = 0, kvh_l = 0, H_l = 0, I_l = 0, V_l = 0;
   std::vector<LayerLayout> layout;  // [layers + 1], globals at index `layers`
+  // per-tensor ggml types read from a GGUF file ([layers + 1]); empty: the
+  // config's per-role types
+  std::vector<std::array<uint32_t, SI_T_COUNT>> ttype;
   std::vector<uint8_t*> host;       // pinned packed layer buffers
   uint8_t* embd_host = nullptr;     // mapped pinned token_embd shard
   uint8_t* embd_dev = nullptr;
@@ -83,7 +92,7 @@ struct si_model {
   // scratch
   uint8_t* scratch_block = nullptr;
   float *hidden, *slice, *qkv, *z, *ab, *core, *core_full, *z_full, *qg, *kk, *vv, *att,
-      *att_full, *gate_full, *gate_l, *act, *act_full, *logits, *logits_full, *rope, *part, *embed;
+      *att_full, *gate_full, *gate_l, *act, *act_full, *logits, *logits_full, *rope, *part, *embed, *up;
   uint32_t* d_token;
   unsigned long long *d_key, *d_keys;
   // NVLink peer all-gather: every rank's scratch block mapped here (CUDA IPC)
@@ -280,6 +289,9 @@ void init_shape(si_model* m) {
     const bool globals = l == c.layers;
     L.gdn = !globals && ((l + 1) % c.attn_interval != 0);
     full_spec(c, L.gdn, globals, &L);
+    if (!m->ttype.empty())
+      for (int id = 0; id < SI_T_COUNT; ++id)
+        if (L.t[id].present) L.t[id].type = m->ttype[l][id];
     shard_layer(*m, &L);
   }
 }
@@ -294,7 +306,7 @@ std::vector<uint64_t> scratch_float_counts(const si_model& m) {
           2ull * m.qh_l * c.attn_head_dim, uint64_t(m.kvh_l) * c.attn_head_dim,
           uint64_t(m.kvh_l) * c.attn_head_dim, uint64_t(m.qh_l) * c.attn_head_dim, qw, qw,
           uint64_t(m.qh_l) * c.attn_head_dim, m.I_l, c.intermediate, m.V_l, c.vocab,
-          c.rotary_dim / 2 + 1, part_floats, H};
+          c.rotary_dim / 2 + 1, part_floats, H, m.I_l};
 }
 
 // Residency plan inside `budget` (0 = unbounded): the output head and as many
@@ -424,9 +436,18 @@ void free_model(si_model* m) {
 
 }  // namespace
 
-extern "C" int si_model_create_synthetic(si_ctx* ctx, const si_model_config* cfg, uint64_t seed,
-                                         si_model** out) {
-  if (!ctx || !cfg || !out) return fail(ctx, SI_E_INVALID, "invalid model arguments");
+namespace {
+
+// Writes the local rows `part.ranges` of tensor (layer, id) to dst; returns
+// SI_OK or an SI_E_* status with *err filled. Called from several threads.
+using FillFn = std::function<int(uint32_t layer, uint32_t id, const LocalTensor& part, uint8_t* dst,
+                                 std::string* err)>;
+
+// Plan, fill the pinned host shards with `fill`, upload the resident set and
+// set up state, scratch and the staging ring (shared by the synthetic and the
+// GGUF-file constructors).
+int create_model(si_ctx* ctx, const si_model_config* cfg, uint64_t seed,
+                 std::vector<std::array<uint32_t, SI_T_COUNT>> types, const FillFn& fill, si_model** out) {
   *out = nullptr;
   const int n = ctx->nranks, r = ctx->rank;
   if (int v = validate_config(*cfg, n))
@@ -438,6 +459,7 @@ extern "C" int si_model_create_synthetic(si_ctx* ctx, const si_model_config* cfg
   m->seed = seed;
   m->n = n;
   m->r = r;
+  m->ttype = std::move(types);
   const si_model_config& c = m->c;
   init_shape(m);
   // ---- residency plan, before any allocation -----------------------------
@@ -506,13 +528,29 @@ extern "C" int si_model_create_synthetic(si_ctx* ctx, const si_model_config* cfg
     for (int id = 0; id < SI_T_COUNT; ++id)
       if (m->layout[l].t[id].present) add_work(l, uint32_t(id), m->layout[l].t[id], m->host[l] + m->layout[l].t[id].offset);
   add_work(c.layers, SI_T_TOKEN_EMBD, embd, m->embd_host);
+  std::atomic<bool> fill_failed{false};
+  std::mutex fill_mu;
+  std::string fill_err;
+  int fill_rc = SI_OK;
   parallel_for(work.size(), [&](uint64_t k) {
+    if (fill_failed.load(std::memory_order_relaxed)) return;
     const Work& w = work[k];
     const LocalTensor& t = (w.id == SI_T_TOKEN_EMBD) ? embd : m->layout[w.layer].t[w.id];
     LocalTensor part = t;
     part.ranges = {{w.row0, w.row1}};
-    generate_tensor(seed, w.layer, w.id, part, w.dst, c.weight_init == 1);
+    std::string e;
+    if (int frc = fill(w.layer, w.id, part, w.dst, &e)) {
+      std::lock_guard<std::mutex> lk(fill_mu);
+      if (!fill_failed.exchange(true)) {
+        fill_rc = frc;
+        fill_err = e;
+      }
+    }
   });
+  if (fill_failed.load()) {
+    free_model(m);
+    return fail(ctx, fill_rc, fill_err);
+  }
 
   // ---- device allocations -----------------------------------------------
   auto dmalloc = [&](void** p, uint64_t bytes, const char* what) -> int {
@@ -580,7 +618,7 @@ extern "C" int si_model_create_synthetic(si_ctx* ctx, const si_model_config* cfg
     uint8_t* s = m->scratch_block;
     float** dst[] = {&m->hidden, &m->slice, &m->qkv, &m->z, &m->ab, &m->core, &m->core_full, &m->z_full,
                      &m->qg, &m->kk, &m->vv, &m->att, &m->att_full, &m->gate_full, &m->gate_l, &m->act,
-                     &m->act_full, &m->logits, &m->logits_full, &m->rope, &m->part, &m->embed};
+                     &m->act_full, &m->logits, &m->logits_full, &m->rope, &m->part, &m->embed, &m->up};
     for (size_t i = 0; i < sizeof(dst) / sizeof(dst[0]); ++i) {
       *dst[i] = reinterpret_cast<float*>(s);
       s += align256(scratch_floats[i] * 4);
@@ -613,6 +651,131 @@ extern "C" int si_model_create_synthetic(si_ctx* ctx, const si_model_config* cfg
   m->accounted = true;
   *out = m;
   return SI_OK;
+}
+
+}  // namespace
+
+extern "C" int si_model_create_synthetic(si_ctx* ctx, const si_model_config* cfg, uint64_t seed,
+                                         si_model** out) {
+  if (!ctx || !cfg || !out) return fail(ctx, SI_E_INVALID, "invalid model arguments");
+  const bool centered = cfg->weight_init == 1;
+  return create_model(ctx, cfg, seed, {},
+                      [seed, centered](uint32_t layer, uint32_t id, const LocalTensor& part, uint8_t* dst,
+                                       std::string*) {
+                        generate_tensor(seed, layer, id, part, dst, centered);
+                        return SI_OK;
+                      },
+                      out);
+}
+
+namespace {
+
+// GGUF tensor names of the decoder roles (qwen35_runtime.rs:419-446, 638-657;
+// globals: token_embd / output_norm / output, 2122-2150).
+const char* const kGgufNames[SI_T_COUNT] = {
+    "attn_norm.weight", "post_attention_norm.weight", "ffn_gate.weight", "ffn_up.weight", "ffn_down.weight",
+    "attn_qkv.weight",  "attn_gate.weight",           "ssm_alpha.weight", "ssm_beta.weight", "ssm_conv1d.weight",
+    "ssm_a",            "ssm_dt.bias",                "ssm_norm.weight", "ssm_out.weight",  "attn_q.weight",
+    "attn_k.weight",    "attn_v.weight",              "attn_output.weight", "attn_q_norm.weight",
+    "attn_k_norm.weight", "token_embd.weight",        "output_norm.weight", "output.weight"};
+
+std::string gguf_name(uint32_t layer, uint32_t layers, int id) {
+  if (layer == layers) return kGgufNames[id];
+  return "blk." + std::to_string(layer) + "." + kGgufNames[id];
+}
+
+struct GgufCloser {
+  void operator()(si_gguf* g) const { si_gguf_close(g); }
+};
+
+}  // namespace
+
+extern "C" int si_model_create_gguf(si_ctx* ctx, const char* path, uint32_t kv_capacity, si_model** out) {
+  if (!ctx || !path || !out) return fail(ctx, SI_E_INVALID, "invalid model arguments");
+  *out = nullptr;
+  si_gguf* raw = nullptr;
+  {
+    std::string err;
+    if (int rc = gguf_parse(path, &raw, &err)) return fail(ctx, rc, err);
+  }
+  std::shared_ptr<si_gguf> g(raw, GgufCloser());
+  si_model_config c;
+  if (int rc = si_gguf_qwen35_config(g.get(), kv_capacity, &c)) return fail(ctx, rc, si_global_last_error());
+  c.weight_init = 0;
+  // every tensor of every layer: present, of the layer's kind
+  // (qwen35_layer_kind, model.rs:748-783), of an executable type, with the
+  // shape the config implies and a payload that covers it
+  std::vector<std::array<uint32_t, SI_T_COUNT>> types(c.layers + 1);
+  std::vector<std::array<uint64_t, SI_T_COUNT>> starts(c.layers + 1);
+  for (uint32_t l = 0; l <= c.layers; ++l) {
+    const bool globals = l == c.layers;
+    bool gdn = false;
+    if (!globals) {
+      const std::string pre = "blk." + std::to_string(l) + ".";
+      const bool has_delta = g->index.count(pre + "ssm_a") != 0;
+      const bool has_attn = g->index.count(pre + "attn_q.weight") != 0;
+      if (has_delta == has_attn)
+        return fail(ctx, SI_E_INVALID, "Qwen3.6 layer " + std::to_string(l) + " does not have exactly one execution kind");
+      const bool want_attn = (l + 1) % c.attn_interval == 0;
+      if (has_attn != want_attn)
+        return fail(ctx, SI_E_INVALID, "Qwen3.6 layer " + std::to_string(l) + " tensor kind " +
+                                           (has_delta ? "GatedDeltaNet" : "FullAttention") +
+                                           " disagrees with interval " + std::to_string(c.attn_interval));
+      gdn = has_delta;
+    }
+    LayerLayout L;
+    full_spec(c, gdn, globals, &L);
+    if (globals) {  // the embedding table is held apart from the layer buffers
+      L.t[SI_T_TOKEN_EMBD].present = true;
+      L.t[SI_T_TOKEN_EMBD].type = SI_GGML_TYPE_Q4_K;
+      L.t[SI_T_TOKEN_EMBD].full_rows = c.vocab;
+      L.t[SI_T_TOKEN_EMBD].cols = c.hidden;
+    }
+    for (int id = 0; id < SI_T_COUNT; ++id) {
+      const LocalTensor& want = L.t[id];
+      if (!want.present) continue;
+      const std::string name = gguf_name(l, c.layers, id);
+      auto it = g->index.find(name);
+      if (it == g->index.end()) return fail(ctx, SI_E_INVALID, "unknown GGUF tensor " + name);
+      const GgufTensor& t = g->tensors[it->second];
+      const bool f32_role = want.type == SI_GGML_TYPE_F32;
+      uint64_t elems = 1;
+      for (uint64_t d : t.dims) elems = (d && elems > UINT64_MAX / d) ? UINT64_MAX : elems * d;
+      if (f32_role) {
+        if (t.type != SI_GGML_TYPE_F32)  // f32_values (qwen35_runtime.rs:168-198)
+          return fail(ctx, SI_E_UNSUPPORTED, "tensor " + name + " is not F32 (type " + std::to_string(t.type) + ")");
+        if (elems != want.full_rows * want.cols)
+          return fail(ctx, SI_E_INVALID, "tensor " + name + " has " + std::to_string(elems) + " F32 values; expected " +
+                                             std::to_string(want.full_rows * want.cols));
+      } else {
+        // token_embd: q4_k_embedding_tensor; projections: any K-quant
+        const bool ok = id == SI_T_TOKEN_EMBD ? t.type == SI_GGML_TYPE_Q4_K : block_bytes_of(t.type) != 0;
+        if (!ok)
+          return fail(ctx, SI_E_UNSUPPORTED, "tensor " + name + " has unsupported type " + std::to_string(t.type) +
+                                                 (id == SI_T_TOKEN_EMBD ? " (token embeddings must be Q4_K)" : ""));
+        if (t.ndim != 2 || t.dims[0] != want.cols || t.dims[1] != want.full_rows)
+          return fail(ctx, SI_E_INVALID, "tensor " + name + " shape does not match the model config");
+      }
+      const uint64_t need = want.full_rows * row_bytes_of(t.type, want.cols);
+      if (t.data_len < need)
+        return fail(ctx, SI_E_INVALID, "tensor " + name + " payload is " + std::to_string(t.data_len) +
+                                           " bytes; expected " + std::to_string(need));
+      types[l][id] = t.type;
+      starts[l][id] = t.data_start;
+    }
+  }
+  // each rank reads only its row ranges of each tensor
+  auto fill = [g, starts](uint32_t layer, uint32_t id, const LocalTensor& part, uint8_t* dst, std::string* err) {
+    const uint64_t rb = row_bytes_of(part.type, part.cols);
+    uint8_t* p = dst;
+    for (const RowRange& rr : part.ranges) {
+      const uint64_t bytes = (rr.end - rr.begin) * rb;
+      if (int rc = gguf_read(g.get(), starts[layer][id] + rr.begin * rb, p, bytes, err)) return rc;
+      p += bytes;
+    }
+    return SI_OK;
+  };
+  return create_model(ctx, &c, 0, std::move(types), fill, out);
 }
 
 extern "C" void si_model_destroy(si_model* m) { free_model(m); }
@@ -745,6 +908,29 @@ int run_qmv(si_model* m, const QmvParams& p) {
   return rc ? fail(m->ctx, rc, msg) : SI_OK;
 }
 
+uint32_t type_of(const si_model* m, uint32_t layer, int id) { return m->layout[layer].t[id].type; }
+
+// A grouped matvec whose segments share x: one launch when every segment has
+// the same type, else one launch per segment (a GGUF file may mix K-quants
+// within a layer).
+int run_group(si_model* m, QmvParams p, const uint32_t* types) {
+  bool same = true;
+  for (uint32_t i = 1; i < p.nseg; ++i) same = same && types[i] == types[0];
+  if (same) {
+    p.type = types[0];
+    return run_qmv(m, p);
+  }
+  for (uint32_t i = 0; i < p.nseg; ++i) {
+    QmvParams q = p;
+    q.nseg = 1;
+    q.seg[0] = p.seg[i];
+    q.items = p.seg[i].rows;
+    q.type = types[i];
+    if (int rc = run_qmv(m, q)) return rc;
+  }
+  return SI_OK;
+}
+
 // Row-sharded output with residual: rows [H_l*r, H_l*(r+1)) of hidden are
 // updated; with n > 1 they are written to `slice` and all-gathered.
 // All-gather of one or two row-sharded vectors into their full copies (which
@@ -784,7 +970,8 @@ int residual_matvec(si_model* m, QmvParams p, const uint8_t* w) {
 
 int mlp(si_model* m, uint32_t l, const uint8_t* base) {
   const si_model_config& c = m->c;
-  QmvParams p = qmv_base(m, c.mlp_type, c.hidden);
+  const uint32_t tg = type_of(m, l, SI_T_FFN_GATE), tu = type_of(m, l, SI_T_FFN_UP);
+  QmvParams p = qmv_base(m, tg, c.hidden);
   p.nseg = 2;
   p.pair = 1;
   p.seg[0] = {tensor_ptr(m, base, l, SI_T_FFN_GATE), m->act, nullptr, m->I_l, 0};
@@ -793,14 +980,23 @@ int mlp(si_model* m, uint32_t l, const uint8_t* base) {
   p.xmode = XM_RMS1P;
   p.x = m->hidden;
   p.xw = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_POST_NORM));
-  int rc = run_qmv(m, p);
+  int rc;
+  if (tg == tu) {
+    rc = run_qmv(m, p);  // fused SwiGLU pair
+  } else {
+    p.pair = 0;
+    p.seg[1].y = m->up;
+    const uint32_t types[2] = {tg, tu};
+    rc = run_group(m, p, types);
+    if (!rc) launch_swiglu(m->act, m->up, m->act, m->I_l, m->ctx->stream);
+  }
   if (rc) return rc;
   const float* act = m->act;
   if (m->n > 1) {
     if ((rc = gather(m, m->act, m->act_full, m->I_l))) return rc;
     act = m->act_full;
   }
-  QmvParams d = qmv_base(m, c.down_type, c.intermediate);
+  QmvParams d = qmv_base(m, type_of(m, l, SI_T_FFN_DOWN), c.intermediate);
   d.x = act;
   d.xmode = XM_RAW;
   return residual_matvec(m, d, tensor_ptr(m, base, l, SI_T_FFN_DOWN));
@@ -818,7 +1014,8 @@ int gdn_layer(si_model* m, uint32_t l, const uint8_t* base) {
   p.xmode = XM_RMS1P;
   p.x = m->hidden;
   p.xw = attn_norm;
-  int rc = run_qmv(m, p);
+  const uint32_t types[2] = {type_of(m, l, SI_T_SSM_QKV), type_of(m, l, SI_T_SSM_Z)};
+  int rc = run_group(m, p, types);
   if (rc) return rc;
   // alpha and beta (F32 rows, adjacent in the packed layer), one launch
   launch_f32_matvec_norm2(reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_ALPHA)), m->ab,
@@ -849,7 +1046,7 @@ int gdn_layer(si_model* m, uint32_t l, const uint8_t* base) {
     core = m->core_full;
     z = m->z_full;
   }
-  QmvParams o = qmv_base(m, SI_GGML_TYPE_Q4_K, c.gdn_value_heads * 128);
+  QmvParams o = qmv_base(m, type_of(m, l, SI_T_SSM_OUT), c.gdn_value_heads * 128);
   o.xmode = XM_GATED;
   o.x = core;
   o.xaux = z;
@@ -871,7 +1068,8 @@ int attn_layer(si_model* m, uint32_t l, const uint8_t* base, uint64_t position) 
   p.xmode = XM_RMS1P;
   p.x = m->hidden;
   p.xw = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_ATTN_NORM));
-  int rc = run_qmv(m, p);
+  const uint32_t types[3] = {type_of(m, l, SI_T_ATTN_Q), type_of(m, l, SI_T_ATTN_K), type_of(m, l, SI_T_ATTN_V)};
+  int rc = run_group(m, p, types);
   if (rc) return rc;
   AttnArgs a = {};
   a.q = m->qg;
@@ -908,7 +1106,7 @@ int attn_layer(si_model* m, uint32_t l, const uint8_t* base, uint64_t position) 
     att = m->att_full;
     gate = m->gate_full;
   }
-  QmvParams o = qmv_base(m, SI_GGML_TYPE_Q4_K, c.attn_q_heads * hd);
+  QmvParams o = qmv_base(m, type_of(m, l, SI_T_ATTN_O), c.attn_q_heads * hd);
   o.xmode = XM_SIGGATE;
   o.x = att;
   o.xaux = gate;
@@ -951,7 +1149,7 @@ int embed_dev(si_model* m) {
 int head_dev(si_model* m, bool gather_logits) {
   const si_model_config& c = m->c;
   const uint8_t* base = m->dev_layer[c.layers];
-  QmvParams p = qmv_base(m, c.head_type, c.hidden);
+  QmvParams p = qmv_base(m, type_of(m, c.layers, SI_T_OUTPUT), c.hidden);
   p.seg[0] = {tensor_ptr(m, base, c.layers, SI_T_OUTPUT), m->logits, nullptr, m->V_l, 0};
   p.items = m->V_l;
   p.xmode = XM_RMS1P;
