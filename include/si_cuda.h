@@ -133,6 +133,18 @@ int si_gguf_quant_matvec_many_weights(si_ctx* ctx, uint32_t n, const si_weight* 
 /* Device form: `w_dev` holds rows*cols/256 blocks of `ggml_type`. */
 int si_qmatvec_dev(si_ctx* ctx, uint32_t ggml_type, const void* w_dev, uint64_t rows,
                    uint64_t cols, const float* x_dev, float* y_dev, void* stream);
+/* Batched matvec for up to 8 inputs with one traversal of the weights
+ * (gguf_quant_matmul_many_bytes / _weight, metal.rs:4067-4230; kernels
+ * si_q{4,5,6}_k_matmul_many, metal.rs:1055-1267). inputs: batch x cols f32,
+ * candidate-major; outputs: batch x rows f32, candidate-major. */
+int si_gguf_quant_matmul_many_bytes(si_ctx* ctx, uint32_t ggml_type, const void* weights, uint64_t nbytes,
+                                    uint64_t rows, uint64_t cols, uint64_t batch, const float* inputs,
+                                    float* outputs);
+int si_gguf_quant_matmul_many_weight(si_ctx* ctx, const si_weight* weight, uint64_t rows, uint64_t cols,
+                                     uint64_t batch, const float* inputs, float* outputs);
+/* Device-pointer form on `stream` (NULL: the context's stream). */
+int si_qmatmul_many_dev(si_ctx* ctx, uint32_t ggml_type, const void* weights_dev, uint64_t rows, uint64_t cols,
+                        uint64_t batch, const float* x_dev, float* y_dev, void* stream);
 /* f32_matvec (metal.rs:2983). */
 int si_f32_matvec(si_ctx* ctx, const float* w, uint64_t rows, uint64_t cols, const float* x,
                   float* y);
@@ -327,6 +339,26 @@ int si_gguf_read(const si_gguf* g, uint64_t index, uint64_t offset, void* dst, u
  * blk.0.ffn_gate / blk.0.ffn_down / output fill mlp/down/head_type.
  * kv_capacity 0 picks min(context_length, 4096). */
 int si_gguf_qwen35_config(const si_gguf* g, uint32_t kv_capacity, si_model_config* out);
+
+/* ---- batched verifier (unsharded models) ---------------------------------- */
+/* decode_tokens_many (qwen35_runtime.rs:2048-2120): embed n <= 8 candidate
+ * tokens and run every layer over the window with one traversal of each
+ * weight matrix (qwen35_decoder_block_many, 879-1289); candidate k sees the
+ * GDN and KV state left by candidates < k, as sequential decode would, and
+ * all n are committed to the state. hidden_out (may be NULL): n x hidden f32.
+ * The final hidden states also stay on the device for si_model_logits_many.
+ * A window that would overflow a KV cache is refused before any state
+ * changes. Sharded models: SI_E_UNSUPPORTED. */
+int si_model_decode_tokens_many(si_model* m, const uint32_t* tokens, const uint64_t* positions, uint32_t n,
+                                float* hidden_out);
+/* logits_many (qwen35_runtime.rs:2194-2227): output norm and head for n
+ * hidden states (host n x hidden, or NULL: the device states of the last
+ * decode_tokens_many of n tokens). logits (may be NULL): n x vocab; ids (may
+ * be NULL): greedy argmax per candidate (runtime.rs:4301-4309). */
+int si_model_logits_many(si_model* m, const float* hidden, uint32_t n, float* logits, uint32_t* ids);
+/* decode_tokens_many then logits_many without a host round trip. */
+int si_model_verify_many(si_model* m, const uint32_t* tokens, const uint64_t* positions, uint32_t n,
+                         uint32_t* ids, float* logits);
 
 /* ---- multi-GPU row sharding over NCCL ----------------------------------- */
 #define SI_COMM_ID_BYTES 128

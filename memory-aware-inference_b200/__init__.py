@@ -121,6 +121,9 @@ def lib():
         "si_gguf_quant_matvec_many_weights": ([vp, u32, vp, vp, vp, vp, vp], i32),
         "si_qmatvec_dev": ([vp, u32, vp, u64, u64, vp, vp, vp], i32),
         "si_f32_matvec": ([vp, vp, u64, u64, vp, vp], i32),
+        "si_gguf_quant_matmul_many_bytes": ([vp, u32, vp, u64, u64, u64, u64, vp, vp], i32),
+        "si_gguf_quant_matmul_many_weight": ([vp, vp, u64, u64, u64, vp, vp], i32),
+        "si_qmatmul_many_dev": ([vp, u32, vp, u64, u64, u64, vp, vp, vp], i32),
         "si_q4_k_fused_gate_up": ([vp, vp, vp, u64, u64, u64, vp, vp], i32),
         "si_q4_k_fused_gate_up_weights": ([vp, vp, vp, u64, u64, vp, vp], i32),
         "si_gguf_quant_fused_mlp_weights": ([vp, vp, vp, vp, u64, u64, u64, vp, vp], i32),
@@ -148,6 +151,9 @@ def lib():
         "si_model_logits": ([vp, vp, vp], i32),
         "si_model_decode_token": ([vp, u32, u64, vp, vp], i32),
         "si_model_generate": ([vp, vp, u64, u64, vp, vp], i32),
+        "si_model_decode_tokens_many": ([vp, vp, vp, u32, vp], i32),
+        "si_model_logits_many": ([vp, vp, u32, vp, vp], i32),
+        "si_model_verify_many": ([vp, vp, vp, u32, vp, vp], i32),
         "si_gguf_open": ([C.c_char_p, vp], i32),
         "si_gguf_close": ([vp], None),
         "si_gguf_info": ([vp, vp, vp, vp], i32),
@@ -342,6 +348,25 @@ class CudaContext:
         ys = (C.c_void_p * n)(*[o.ctypes.data for o in outs])
         self._ck(lib().si_gguf_quant_matvec_many_weights(self.h, n, ws, rows, cols, _p(xv), ys))
         return [o[:r] for o, (_, r, _) in zip(outs, items)]
+
+    def gguf_quant_matmul_many_bytes(self, ggml_type, weight_bytes, rows, columns, batch, inputs) -> np.ndarray:
+        """MetalContext::gguf_quant_matmul_many_bytes: `batch` inputs (batch x
+        columns) against one matrix; returns batch x rows."""
+        w = _u8(weight_bytes)
+        x = _f32(inputs)
+        y = np.empty((batch, rows), np.float32)
+        self._ck(lib().si_gguf_quant_matmul_many_bytes(self.h, ggml_type, _p(w), w.size, rows, columns, batch,
+                                                       _p(x), _p(y)))
+        return y
+
+    def gguf_quant_matmul_many_weight(self, weight: QuantWeight, rows, columns, batch, inputs) -> np.ndarray:
+        x = _f32(inputs)
+        y = np.empty((batch, rows), np.float32)
+        self._ck(lib().si_gguf_quant_matmul_many_weight(self.h, weight.handle, rows, columns, batch, _p(x), _p(y)))
+        return y
+
+    def qmatmul_many_dev(self, ggml_type, w, rows, cols, batch, x, y, stream=None):
+        self._ck(lib().si_qmatmul_many_dev(self.h, ggml_type, _p(w), rows, cols, batch, _p(x), _p(y), stream))
 
     def f32_matvec(self, weights, rows, columns, x):
         w, xv = _f32(weights), _f32(x)
@@ -663,6 +688,34 @@ class Model:
         logits = np.empty(self.config.vocab, np.float32) if want_logits else None
         self.ctx._ck(lib().si_model_decode_token(self.h, token_id, position, C.byref(nxt), _p(logits)))
         return nxt.value, logits
+
+    def decode_tokens_many(self, tokens, positions, want_hidden: bool = True):
+        """Qwen35Runtime::decode_tokens_many: hidden states (n x hidden) of a
+        1..8 token window, every layer's weights traversed once."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(positions, dtype=np.uint64)
+        out = np.empty((t.size, self.config.hidden), np.float32) if want_hidden else None
+        self.ctx._ck(lib().si_model_decode_tokens_many(self.h, _p(t), _p(p), t.size, _p(out)))
+        return out
+
+    def logits_many(self, hidden=None, n: int = None, want_logits: bool = True):
+        """Qwen35Runtime::logits_many: (logits n x vocab or None, greedy ids).
+        hidden=None uses the device states of the last decode_tokens_many."""
+        h = None if hidden is None else _f32(hidden).reshape(-1, self.config.hidden)
+        n = h.shape[0] if h is not None else n
+        logits = np.empty((n, self.config.vocab), np.float32) if want_logits else None
+        ids = np.empty(n, np.uint32)
+        self.ctx._ck(lib().si_model_logits_many(self.h, _p(h), n, _p(logits), _p(ids)))
+        return logits, ids.tolist()
+
+    def verify_many(self, tokens, positions, want_logits: bool = False):
+        """decode_tokens_many + logits_many: (greedy ids, logits or None)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(positions, dtype=np.uint64)
+        logits = np.empty((t.size, self.config.vocab), np.float32) if want_logits else None
+        ids = np.empty(t.size, np.uint32)
+        self.ctx._ck(lib().si_model_verify_many(self.h, _p(t), _p(p), t.size, _p(ids), _p(logits)))
+        return ids.tolist(), logits
 
     def generate(self, prompt, max_new_tokens: int):
         p = np.ascontiguousarray(prompt, dtype=np.uint32)

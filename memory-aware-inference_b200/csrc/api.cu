@@ -468,6 +468,99 @@ int si_gguf_quant_matvec_weight(si_ctx* ctx, const si_weight* w, uint64_t rows, 
   return si_gguf_quant_matvec_many_weights(ctx, 1, &w, &r, &c, x, &yy);
 }
 
+// Batched matvec over host or retained weights (metal.rs:4067-4230): inputs
+// [batch][cols], outputs [batch][rows].
+static int qmm_host(si_ctx* ctx, uint32_t type, const uint8_t* w_dev, uint64_t rows, uint64_t cols,
+                    uint64_t batch, const float* inputs, float* outputs) {
+  int rc = h2d(ctx, ctx->in[0], inputs, batch * cols * 4, "batched matvec input");
+  if (rc) return rc;
+  if (!ctx->out[0].ensure(batch * rows * 4)) return fail(ctx, SI_E_NOMEM, "batched matvec output allocation failed");
+  QmmParams p = {};
+  p.type = type;
+  p.rows = uint32_t(rows);
+  p.cols = uint32_t(cols);
+  p.batch = uint32_t(batch);
+  p.w = w_dev;
+  p.x = ctx->in[0].as<float>();
+  p.ldx = cols;
+  p.y = ctx->out[0].as<float>();
+  p.ldy = rows;
+  p.err = ctx->d_err;
+  const uint64_t need = qmm_tc_scratch_bytes(uint32_t(rows), uint32_t(cols), uint32_t(batch), ctx->sm_count);
+  if (ctx->scratch.ensure(need)) {
+    p.scratch = ctx->scratch.p;
+    p.scratch_bytes = need;
+  }
+  std::string msg;
+  if ((rc = launch_qmm(p, ctx->stream, ctx->sm_count, false, &msg))) return fail(ctx, rc, msg);
+  if ((rc = d2h(ctx, outputs, ctx->out[0].p, batch * rows * 4, "batched matvec readback"))) return rc;
+  return sync_and_check(ctx, "batched quantized matvec command");
+}
+
+int si_gguf_quant_matmul_many_bytes(si_ctx* ctx, uint32_t type, const void* w, uint64_t nbytes, uint64_t rows,
+                                    uint64_t cols, uint64_t batch, const float* inputs, float* outputs) {
+  if (!ctx) return SI_E_INVALID;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (batch == 0 || batch > kQmmMaxBatch || rows == 0 || cols == 0 || cols % 256 || rows > 0xffffffffull ||
+      cols > kQmvMaxCols)
+    return fail(ctx, SI_E_INVALID, "batched quantized matvec dimensions are invalid");
+  if (!inputs || !outputs || !w) return fail(ctx, SI_E_INVALID, "batched quantized input length is invalid");
+  const uint32_t bb = block_bytes_of(type);
+  if (bb == 0) return fail(ctx, SI_E_UNSUPPORTED, "unsupported batched quantized weight type");
+  if (nbytes != rows * (cols / 256) * bb) return fail(ctx, SI_E_INVALID, "batched quantized weight byte length is invalid");
+  int rc = h2d(ctx, ctx->wbuf[0], w, nbytes, "batched matvec weight staging");
+  if (rc) return rc;
+  return qmm_host(ctx, type, ctx->wbuf[0].as<uint8_t>(), rows, cols, batch, inputs, outputs);
+}
+
+int si_gguf_quant_matmul_many_weight(si_ctx* ctx, const si_weight* w, uint64_t rows, uint64_t cols, uint64_t batch,
+                                     const float* inputs, float* outputs) {
+  if (!ctx || !w) return fail(ctx, SI_E_INVALID, "null weight");
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (batch == 0 || batch > kQmmMaxBatch || rows == 0 || cols == 0 || cols % 256 || rows > 0xffffffffull ||
+      cols > kQmvMaxCols)
+    return fail(ctx, SI_E_INVALID, "batched retained quantized dimensions are invalid");
+  if (!inputs || !outputs) return fail(ctx, SI_E_INVALID, "batched retained quantized input length is invalid");
+  const uint32_t bb = block_bytes_of(w->type);
+  if (bb == 0) return fail(ctx, SI_E_UNSUPPORTED, "unsupported retained batched quantized type");
+  if (w->bytes != rows * (cols / 256) * bb) return fail(ctx, SI_E_INVALID, "retained batched weight byte length is invalid");
+  const uint8_t* wd;
+  int rc = weight_dev(ctx, w, 0, &wd);
+  if (rc) return rc;
+  return qmm_host(ctx, w->type, wd, rows, cols, batch, inputs, outputs);
+}
+
+int si_qmatmul_many_dev(si_ctx* ctx, uint32_t type, const void* w_dev, uint64_t rows, uint64_t cols, uint64_t batch,
+                        const float* x_dev, float* y_dev, void* stream) {
+  if (!ctx) return SI_E_INVALID;
+  if (batch == 0 || batch > kQmmMaxBatch || rows == 0 || cols == 0 || cols % 256 || rows > 0xffffffffull)
+    return fail(ctx, SI_E_INVALID, "batched quantized matvec dimensions are invalid");
+  QmmParams p = {};
+  p.type = type;
+  p.rows = uint32_t(rows);
+  p.cols = uint32_t(cols);
+  p.batch = uint32_t(batch);
+  p.w = static_cast<const uint8_t*>(w_dev);
+  p.x = x_dev;
+  p.ldx = cols;
+  p.y = y_dev;
+  p.ldy = rows;
+  p.err = ctx->d_err;
+  // the tensor-core form's scratch is the context's (calls on one context
+  // are serialised on the host, and kernels on one stream in order)
+  const uint64_t need = qmm_tc_scratch_bytes(uint32_t(rows), uint32_t(cols), uint32_t(batch), ctx->sm_count);
+  {
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (ctx->scratch.ensure(need)) {
+      p.scratch = ctx->scratch.p;
+      p.scratch_bytes = need;
+    }
+  }
+  std::string msg;
+  int rc = launch_qmm(p, stream ? static_cast<cudaStream_t>(stream) : ctx->stream, ctx->sm_count, true, &msg);
+  return rc ? fail(ctx, rc, msg) : SI_OK;
+}
+
 int si_f32_matvec(si_ctx* ctx, const float* w, uint64_t rows, uint64_t cols, const float* x,
                   float* y) {
   if (!ctx) return SI_E_INVALID;

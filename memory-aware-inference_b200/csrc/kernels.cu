@@ -1306,4 +1306,17 @@ void launch_swiglu(const float* g, const float* u, float* y, uint64_t n, cudaStr
   swiglu_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(g, u, y, n);
 }
 
+// Gated attention output of `batch` candidates (qwen35_runtime.rs:1206-1214):
+// out[k][i] = a[k][i] / (1 + exp(-gate[k][i])).
+__global__ void siggate_many_kernel(const float* a, uint64_t lda, const float* gate, uint64_t ldg, float* out,
+                                    uint64_t ldo, uint32_t n) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x, k = blockIdx.y;
+  if (i < n) out[k * ldo + i] = a[k * lda + i] / (1.0f + expf(-gate[k * ldg + i]));
+}
+
+void launch_siggate_many(const float* a, uint64_t lda, const float* gate, uint64_t ldg, float* out, uint64_t ldo,
+                         uint32_t n, uint32_t batch, cudaStream_t s) {
+  siggate_many_kernel<<<dim3((n + 255) / 256, batch), 256, 0, s>>>(a, lda, gate, ldg, out, ldo, n);
+}
+
 }  // namespace si

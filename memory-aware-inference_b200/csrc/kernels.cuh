@@ -124,5 +124,8 @@ void rope_freqs(float theta, uint32_t dims, std::vector<float>* out);
 void launch_add(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s);
 // y = silu(g) * u (length n): the MLP when gate and up differ in type.
 void launch_swiglu(const float* g, const float* u, float* y, uint64_t n, cudaStream_t s);
+// out[k][i] = a[k][i] / (1 + exp(-gate[k][i])) for k < batch, i < n.
+void launch_siggate_many(const float* a, uint64_t lda, const float* gate, uint64_t ldg, float* out, uint64_t ldo,
+                         uint32_t n, uint32_t batch, cudaStream_t s);
 
 }  // namespace si

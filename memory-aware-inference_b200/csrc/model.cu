@@ -95,6 +95,15 @@ struct si_model {
       *att_full, *gate_full, *gate_l, *act, *act_full, *logits, *logits_full, *rope, *part, *embed, *up;
   uint32_t* d_token;
   unsigned long long *d_key, *d_keys;
+  // batched verifier (decode_tokens_many): candidate-major buffers for up to
+  // kQmmMaxBatch tokens, inside the scratch block (unsharded models only)
+  float *b_hid = nullptr, *b_xn, *b_xg, *b_qkv, *b_z, *b_ab, *b_core, *b_qg, *b_kk, *b_vv, *b_att, *b_act,
+        *b_up, *b_logits;
+  unsigned long long* b_keys;
+  uint32_t *b_ids, *b_tokens;
+  uint8_t* b_qmm = nullptr;  // tensor-core batched matvec scratch (digits, tables, panel sums)
+  uint64_t b_qmm_bytes = 0;
+  uint32_t b_valid = 0;  // candidates whose final hidden states are in b_hid
   // NVLink peer all-gather: every rank's scratch block mapped here (CUDA IPC)
   bool p2p = false;
   void* peer_block[kP2PMaxRanks] = {};
@@ -309,6 +318,40 @@ std::vector<uint64_t> scratch_float_counts(const si_model& m) {
           c.rotary_dim / 2 + 1, part_floats, H, m.I_l};
 }
 
+// Candidate-major buffers of the batched verifier, in float counts (b_hid,
+// b_xn, b_xg, b_qkv, b_z, b_ab, b_core, b_qg, b_kk, b_vv, b_att, b_act, b_up,
+// b_logits), then 8-byte argmax keys and two u32 arrays.
+std::vector<uint64_t> batch_float_counts(const si_model& m) {
+  const si_model_config& c = m.c;
+  if (m.n != 1) return {};
+  const uint64_t K = kQmmMaxBatch, H = c.hidden, d = c.gdn_head_dim;
+  const uint64_t proj = (2ull * c.gdn_key_heads + c.gdn_value_heads) * d, vw = uint64_t(c.gdn_value_heads) * d;
+  const uint64_t qw = uint64_t(c.attn_q_heads) * c.attn_head_dim, kvw = uint64_t(c.attn_kv_heads) * c.attn_head_dim;
+  return {K * H, K * H, K * std::max(vw, qw), K * proj, K * vw, K * 2 * c.gdn_value_heads, K * vw,
+          K * 2 * qw, K * kvw, K * kvw, K * qw, K * c.intermediate, K * c.intermediate, K * c.vocab};
+}
+
+// Largest tensor-core batched-matvec scratch over the model's matrices.
+uint64_t batch_qmm_bytes(const si_model& m) {
+  const si_model_config& c = m.c;
+  const uint32_t H = c.hidden, d = c.gdn_head_dim, K = kQmmMaxBatch;
+  const uint32_t proj = (2 * c.gdn_key_heads + c.gdn_value_heads) * d, vw = c.gdn_value_heads * d;
+  const uint32_t qw = c.attn_q_heads * c.attn_head_dim, kvw = c.attn_kv_heads * c.attn_head_dim;
+  const uint32_t shapes[][2] = {{proj, H}, {vw, H}, {2 * qw, H}, {kvw, H}, {c.intermediate, H},
+                                {H, c.intermediate}, {H, vw}, {H, qw}, {c.vocab, H}};
+  uint64_t b = 0;
+  for (const auto& s : shapes) b = std::max(b, qmm_tc_scratch_bytes(s[0], s[1], K, 148));
+  return b;
+}
+
+uint64_t batch_bytes(const si_model& m) {
+  const std::vector<uint64_t> f = batch_float_counts(m);
+  if (f.empty()) return 0;
+  uint64_t b = 256;  // alignment slack after the peer flags
+  for (uint64_t v : f) b += align256(v * 4);
+  return b + 3 * 256 + align256(batch_qmm_bytes(m));  // keys, ids, tokens, matvec scratch
+}
+
 // Residency plan inside `budget` (0 = unbounded): the output head and as many
 // leading layers as fit stay resident (the reference's retained prefix,
 // qwen35_runtime.rs:1640-1642); the rest stream through `depth` ring slots of
@@ -328,6 +371,7 @@ int compute_plan(si_model* m, uint64_t budget, uint32_t depth, std::vector<bool>
   }
   uint64_t scratch_bytes = 4 * 256 + 64 * kP2PMaxRanks;  // token, argmax keys, peer flags
   for (uint64_t f : scratch_float_counts(*m)) scratch_bytes += align256(f * 4);
+  scratch_bytes += batch_bytes(*m);
   uint64_t max_layer = 0, all_layers = 0;
   for (uint32_t l = 0; l < c.layers; ++l) {
     max_layer = std::max(max_layer, m->layout[l].bytes);
@@ -627,6 +671,21 @@ int create_model(si_ctx* ctx, const si_model_config* cfg, uint64_t seed,
     m->d_key = reinterpret_cast<unsigned long long*>(s + 256);
     m->d_keys = reinterpret_cast<unsigned long long*>(s + 512);
     m->flag_off = uint64_t(s + 1024 - m->scratch_block);
+    const std::vector<uint64_t> bf = batch_float_counts(*m);
+    if (!bf.empty()) {
+      uint8_t* b = m->scratch_block + align256(m->flag_off + 64 * kP2PMaxRanks);
+      float** bdst[] = {&m->b_hid, &m->b_xn, &m->b_xg, &m->b_qkv, &m->b_z, &m->b_ab, &m->b_core,
+                        &m->b_qg, &m->b_kk, &m->b_vv, &m->b_att, &m->b_act, &m->b_up, &m->b_logits};
+      for (size_t i = 0; i < bf.size(); ++i) {
+        *bdst[i] = reinterpret_cast<float*>(b);
+        b += align256(bf[i] * 4);
+      }
+      m->b_keys = reinterpret_cast<unsigned long long*>(b);
+      m->b_ids = reinterpret_cast<uint32_t*>(b + 256);
+      m->b_tokens = reinterpret_cast<uint32_t*>(b + 512);
+      m->b_qmm = b + 768;
+      m->b_qmm_bytes = batch_qmm_bytes(*m);
+    }
   }
   rope_freqs(c.rope_theta, c.rotary_dim, &m->rope_host);
   if (!m->rope_host.empty())
@@ -1113,8 +1172,10 @@ int attn_layer(si_model* m, uint32_t l, const uint8_t* base, uint64_t position) 
   return residual_matvec(m, o, tensor_ptr(m, base, l, SI_T_ATTN_O));
 }
 
-// decode_hidden on device buffers: m->hidden is updated in place.
-int decode_layers(si_model* m, uint64_t position) {
+// The layer loop over resident layers and the staging ring; `body` runs one
+// layer from its device copy.
+template <typename F>
+int run_layers(si_model* m, F body) {
   const si_model_config& c = m->c;
   const bool ring = !m->streamed.empty();
   if (ring) ring_prime(m);
@@ -1126,9 +1187,7 @@ int decode_layers(si_model* m, uint64_t position) {
       cudaStreamWaitEvent(m->ctx->stream, m->copy_done[s], 0);
       base = m->slot[s];
     }
-    int rc = m->layout[l].gdn ? gdn_layer(m, l, base) : attn_layer(m, l, base, position);
-    if (!rc) rc = mlp(m, l, base);
-    if (rc) return rc;
+    if (int rc = body(l, base)) return rc;
     if (!m->dev_layer[l]) {
       cudaEventRecord(m->compute_done[s], m->ctx->stream);
       m->occ_next++;
@@ -1136,6 +1195,14 @@ int decode_layers(si_model* m, uint64_t position) {
     }
   }
   return SI_OK;
+}
+
+// decode_hidden on device buffers: m->hidden is updated in place.
+int decode_layers(si_model* m, uint64_t position) {
+  return run_layers(m, [&](uint32_t l, const uint8_t* base) {
+    int rc = m->layout[l].gdn ? gdn_layer(m, l, base) : attn_layer(m, l, base, position);
+    return rc ? rc : mlp(m, l, base);
+  });
 }
 
 int embed_dev(si_model* m) {
@@ -1254,4 +1321,235 @@ extern "C" int si_model_generate(si_model* m, const uint32_t* prompt, uint64_t n
     if ((rc = embed_dev(m)) || (rc = decode_layers(m, n_prompt + i)) || (rc = head_dev(m, false))) return rc;
   }
   return sync_and_check(m->ctx, "generation");
+}
+
+// ---- batched verifier (qwen35_runtime.rs:879-1289, 2048-2120, 2194-2227) ----
+namespace {
+
+// One batched matvec over `batch` candidate inputs [batch][ldx]; out rows
+// [batch][ldy], optionally accumulated onto resid (y may alias resid).
+int run_qmm(si_model* m, uint32_t type, const uint8_t* w, uint32_t rows, uint32_t cols, uint32_t batch,
+            const float* x, uint64_t ldx, float* y, uint64_t ldy, const float* resid = nullptr) {
+  QmmParams p = {};
+  p.type = type;
+  p.rows = rows;
+  p.cols = cols;
+  p.batch = batch;
+  p.w = w;
+  p.x = x;
+  p.ldx = ldx;
+  p.y = y;
+  p.ldy = ldy;
+  p.resid = resid;
+  p.ldr = ldy;
+  p.scratch = m->b_qmm;
+  p.scratch_bytes = m->b_qmm_bytes;
+  p.err = m->ctx->d_err;
+  std::string msg;
+  int rc = launch_qmm(p, m->ctx->stream, m->ctx->sm_count, true, &msg);
+  return rc ? fail(m->ctx, rc, msg) : SI_OK;
+}
+
+// GDN token mixer for a candidate window: projections batched, conv and
+// recurrence candidate by candidate (each sees the previous one's state),
+// gated norm batched, ssm_out batched onto the residual.
+int gdn_many(si_model* m, uint32_t l, const uint8_t* base, uint32_t K) {
+  const si_model_config& c = m->c;
+  const uint32_t H = c.hidden, vh = c.gdn_value_heads, proj = (2 * c.gdn_key_heads + vh) * 128, vw = vh * 128;
+  const float* attn_norm = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_ATTN_NORM));
+  launch_rms_norm_heads(m->b_hid, attn_norm, K, H, c.rms_eps, m->b_xn, m->ctx->stream);
+  int rc = run_qmm(m, type_of(m, l, SI_T_SSM_QKV), tensor_ptr(m, base, l, SI_T_SSM_QKV), proj, H, K, m->b_xn, H,
+                   m->b_qkv, proj);
+  if (!rc)
+    rc = run_qmm(m, type_of(m, l, SI_T_SSM_Z), tensor_ptr(m, base, l, SI_T_SSM_Z), vw, H, K, m->b_xn, H, m->b_z, vw);
+  if (rc) return rc;
+  for (uint32_t k = 0; k < K; ++k) {
+    float* ab = m->b_ab + uint64_t(k) * 2 * vh;
+    launch_f32_matvec_norm2(reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_ALPHA)), ab,
+                            reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_BETA)), ab + vh, vh, H,
+                            m->b_hid + uint64_t(k) * H, attn_norm, c.rms_eps, m->ctx->stream);
+    GdnLayerArgs g = {};
+    g.qkv = m->b_qkv + uint64_t(k) * proj;
+    g.conv_w = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_CONV));
+    const uint32_t par = m->conv_parity[l];
+    g.conv_in = m->conv[par][l];
+    g.conv_out = m->conv[par ^ 1][l];
+    g.state = m->rec[l];
+    g.alpha = ab;
+    g.beta_logit = ab + vh;
+    g.a_log = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_A));
+    g.dt_bias = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_DT));
+    g.core = m->b_core + uint64_t(k) * vw;
+    g.key_heads = c.gdn_key_heads;
+    g.value_heads = vh;
+    g.kernel = c.conv_kernel;
+    launch_gdn_layer(g, m->ctx->stream, false);
+    m->conv_parity[l] = par ^ 1;
+  }
+  launch_rms_norm_gated(m->b_core, m->b_z, reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_NORM)),
+                        K * vh, 128, c.rms_eps, m->b_xg, m->ctx->stream);
+  return run_qmm(m, type_of(m, l, SI_T_SSM_OUT), tensor_ptr(m, base, l, SI_T_SSM_OUT), H, vw, K, m->b_xg, vw,
+                 m->b_hid, H, m->b_hid);
+}
+
+// Full-attention mixer for a candidate window: q/k/v batched, then per
+// candidate norm + RoPE at its position, cache append and attention over the
+// cache so far; gating batched; the output projection batched onto the residual.
+int attn_many(si_model* m, uint32_t l, const uint8_t* base, uint32_t K, const uint64_t* positions) {
+  const si_model_config& c = m->c;
+  const uint32_t H = c.hidden, hd = c.attn_head_dim, qw = c.attn_q_heads * hd, kvw = c.attn_kv_heads * hd;
+  launch_rms_norm_heads(m->b_hid, reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_ATTN_NORM)), K, H,
+                        c.rms_eps, m->b_xn, m->ctx->stream);
+  int rc = run_qmm(m, type_of(m, l, SI_T_ATTN_Q), tensor_ptr(m, base, l, SI_T_ATTN_Q), 2 * qw, H, K, m->b_xn, H,
+                   m->b_qg, 2 * qw);
+  if (!rc)
+    rc = run_qmm(m, type_of(m, l, SI_T_ATTN_K), tensor_ptr(m, base, l, SI_T_ATTN_K), kvw, H, K, m->b_xn, H, m->b_kk,
+                 kvw);
+  if (!rc)
+    rc = run_qmm(m, type_of(m, l, SI_T_ATTN_V), tensor_ptr(m, base, l, SI_T_ATTN_V), kvw, H, K, m->b_xn, H, m->b_vv,
+                 kvw);
+  if (rc) return rc;
+  for (uint32_t k = 0; k < K; ++k) {
+    AttnArgs a = {};
+    a.q = m->b_qg + uint64_t(k) * 2 * qw;
+    a.k_new = m->b_kk + uint64_t(k) * kvw;
+    a.v_new = m->b_vv + uint64_t(k) * kvw;
+    a.k_cache = m->kc[l];
+    a.v_cache = m->vc[l];
+    a.k_cache_w = m->kc[l];
+    a.v_cache_w = m->vc[l];
+    a.q_norm = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_ATTN_QNORM));
+    a.k_norm = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_ATTN_KNORM));
+    a.rope_freq = c.rotary_dim ? m->rope : nullptr;
+    a.position = uint32_t(positions[k]);
+    a.cached = m->cached[l];
+    a.qh = c.attn_q_heads;
+    a.kvh = c.attn_kv_heads;
+    a.hd = hd;
+    a.cap = c.kv_capacity;
+    a.rotary = c.rotary_dim;
+    a.eps = c.rms_eps;
+    a.cache_bf16 = 1;
+    a.part = m->part;
+    a.out = m->b_att + uint64_t(k) * qw;
+    a.chunk = 256;
+    a.err = m->ctx->d_err;
+    launch_attention(a, m->ctx->stream, false);
+    m->cached[l]++;
+  }
+  // the gate half of each candidate's q projection follows its queries
+  launch_siggate_many(m->b_att, qw, m->b_qg + qw, 2 * qw, m->b_xg, qw, qw, K, m->ctx->stream);
+  return run_qmm(m, type_of(m, l, SI_T_ATTN_O), tensor_ptr(m, base, l, SI_T_ATTN_O), H, qw, K, m->b_xg, qw,
+                 m->b_hid, H, m->b_hid);
+}
+
+int mlp_many(si_model* m, uint32_t l, const uint8_t* base, uint32_t K) {
+  const si_model_config& c = m->c;
+  const uint32_t H = c.hidden, I = c.intermediate;
+  launch_rms_norm_heads(m->b_hid, reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_POST_NORM)), K, H,
+                        c.rms_eps, m->b_xn, m->ctx->stream);
+  int rc = run_qmm(m, type_of(m, l, SI_T_FFN_GATE), tensor_ptr(m, base, l, SI_T_FFN_GATE), I, H, K, m->b_xn, H,
+                   m->b_act, I);
+  if (!rc)
+    rc = run_qmm(m, type_of(m, l, SI_T_FFN_UP), tensor_ptr(m, base, l, SI_T_FFN_UP), I, H, K, m->b_xn, H, m->b_up, I);
+  if (rc) return rc;
+  launch_swiglu(m->b_act, m->b_up, m->b_act, uint64_t(K) * I, m->ctx->stream);
+  return run_qmm(m, type_of(m, l, SI_T_FFN_DOWN), tensor_ptr(m, base, l, SI_T_FFN_DOWN), H, I, K, m->b_act, I,
+                 m->b_hid, H, m->b_hid);
+}
+
+int check_batch(si_model* m, uint32_t n, const char* what) {
+  if (n == 0 || n > kQmmMaxBatch)
+    return fail(m->ctx, SI_E_INVALID, std::string("Qwen3.6 ") + what + " must contain 1..8 tokens");
+  if (m->n != 1 || !m->b_hid)
+    return fail(m->ctx, SI_E_UNSUPPORTED, "batched verification runs on an unsharded model");
+  return SI_OK;
+}
+
+// Embed the window's tokens and run every layer over it (hidden states stay
+// in b_hid).
+int decode_many_dev(si_model* m, const uint32_t* tokens, const uint64_t* positions, uint32_t K) {
+  const si_model_config& c = m->c;
+  for (uint32_t k = 0; k < K; ++k)
+    if (tokens[k] >= c.vocab) return fail(m->ctx, SI_E_INVALID, "token id is out of range");
+  for (uint32_t l = 0; l < c.layers; ++l)
+    if (!m->layout[l].gdn && m->cached[l] + K > c.kv_capacity)
+      return fail(m->ctx, SI_E_STATE, "batched full-attention KV cache capacity exhausted");
+  cudaMemcpyAsync(m->b_tokens, tokens, K * 4, cudaMemcpyHostToDevice, m->ctx->stream);
+  for (uint32_t k = 0; k < K; ++k)
+    launch_embed(m->embd_dev, c.hidden, m->b_tokens + k, 0, c.vocab, m->b_hid + uint64_t(k) * c.hidden,
+                 m->ctx->stream);
+  m->b_valid = 0;
+  int rc = run_layers(m, [&](uint32_t l, const uint8_t* base) {
+    int r = m->layout[l].gdn ? gdn_many(m, l, base, K) : attn_many(m, l, base, K, positions);
+    return r ? r : mlp_many(m, l, base, K);
+  });
+  if (!rc) m->b_valid = K;
+  return rc;
+}
+
+// Output norm, head and per-candidate argmax over b_hid.
+int logits_many_dev(si_model* m, uint32_t K) {
+  const si_model_config& c = m->c;
+  const uint8_t* base = m->dev_layer[c.layers];
+  launch_rms_norm_heads(m->b_hid, reinterpret_cast<const float*>(tensor_ptr(m, base, c.layers, SI_T_OUTPUT_NORM)),
+                        K, c.hidden, c.rms_eps, m->b_xn, m->ctx->stream);
+  int rc = run_qmm(m, type_of(m, c.layers, SI_T_OUTPUT), tensor_ptr(m, base, c.layers, SI_T_OUTPUT), c.vocab,
+                   c.hidden, K, m->b_xn, c.hidden, m->b_logits, c.vocab);
+  if (rc) return rc;
+  cudaMemsetAsync(m->b_keys, 0, K * 8, m->ctx->stream);
+  for (uint32_t k = 0; k < K; ++k) {
+    launch_argmax_key(m->b_logits + uint64_t(k) * c.vocab, c.vocab, 0, m->b_keys + k, m->ctx->stream);
+    launch_argmax_finish(m->b_keys + k, 1, m->b_ids + k, m->ctx->stream);
+  }
+  return SI_OK;
+}
+
+int read_many(si_model* m, uint32_t K, float* logits, uint32_t* ids, const char* what) {
+  std::vector<uint32_t> idv(K);
+  cudaMemcpyAsync(idv.data(), m->b_ids, K * 4, cudaMemcpyDeviceToHost, m->ctx->stream);
+  if (logits)
+    cudaMemcpyAsync(logits, m->b_logits, uint64_t(K) * m->c.vocab * 4, cudaMemcpyDeviceToHost, m->ctx->stream);
+  if (int rc = sync_and_check(m->ctx, what)) return rc;
+  for (uint32_t k = 0; k < K; ++k)
+    if (idv[k] == 0xffffffffu) return fail(m->ctx, SI_E_INVALID, "logits contain no finite values");
+  if (ids) std::memcpy(ids, idv.data(), K * 4);
+  return SI_OK;
+}
+
+}  // namespace
+
+extern "C" int si_model_decode_tokens_many(si_model* m, const uint32_t* tokens, const uint64_t* positions,
+                                           uint32_t n, float* hidden_out) {
+  if (!m || !tokens || !positions) return SI_E_INVALID;
+  if (int rc = check_batch(m, n, "candidate window")) return rc;
+  cudaSetDevice(m->ctx->device);
+  if (int rc = decode_many_dev(m, tokens, positions, n)) return rc;
+  if (hidden_out)
+    cudaMemcpyAsync(hidden_out, m->b_hid, uint64_t(n) * m->c.hidden * 4, cudaMemcpyDeviceToHost, m->ctx->stream);
+  return sync_and_check(m->ctx, "decode_tokens_many");
+}
+
+extern "C" int si_model_logits_many(si_model* m, const float* hidden, uint32_t n, float* logits, uint32_t* ids) {
+  if (!m) return SI_E_INVALID;
+  if (int rc = check_batch(m, n, "batched logits")) return rc;
+  cudaSetDevice(m->ctx->device);
+  if (hidden) {
+    cudaMemcpyAsync(m->b_hid, hidden, uint64_t(n) * m->c.hidden * 4, cudaMemcpyHostToDevice, m->ctx->stream);
+    m->b_valid = n;
+  } else if (m->b_valid != n) {
+    return fail(m->ctx, SI_E_STATE, "no device hidden states for this window: pass hidden");
+  }
+  if (int rc = logits_many_dev(m, n)) return rc;
+  return read_many(m, n, logits, ids, "logits_many");
+}
+
+extern "C" int si_model_verify_many(si_model* m, const uint32_t* tokens, const uint64_t* positions, uint32_t n,
+                                    uint32_t* ids, float* logits) {
+  if (!m || !tokens || !positions) return SI_E_INVALID;
+  if (int rc = check_batch(m, n, "candidate window")) return rc;
+  cudaSetDevice(m->ctx->device);
+  if (int rc = decode_many_dev(m, tokens, positions, n)) return rc;
+  if (int rc = logits_many_dev(m, n)) return rc;
+  return read_many(m, n, logits, ids, "verify_many");
 }

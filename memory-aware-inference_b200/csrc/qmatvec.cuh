@@ -47,6 +47,26 @@ int launch_qmv(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
 bool qmv_tc_eligible(const QmvParams& p);
 int launch_qmv_tc(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl, std::string* msg);
 
+// Batched matvec Y[k] = W X[k] (+ R[k]) for k < batch, one weight traversal.
+constexpr uint32_t kQmmMaxBatch = 8;
+struct QmmParams {
+  uint32_t type, rows, cols, batch;
+  const uint8_t* w;
+  const float* x;       // x[k * ldx + c], 16-byte aligned, ldx % 4 == 0
+  float* y;             // y[k * ldy + r]
+  const float* resid;   // optional: y = resid + W x, resid[k * ldr + r] (may alias y)
+  uint64_t ldx, ldy, ldr;
+  void* scratch;        // device scratch for the tensor-core form (256-byte aligned), may be null
+  uint64_t scratch_bytes;
+  int* err;
+};
+int launch_qmm(const QmmParams& p, cudaStream_t stream, int sm_count, bool pdl, std::string* msg);
+// Tensor-core form for Q4_K (qmatmul_many_tc.cu): scratch it needs, whether a
+// call qualifies, and the launch (SI_E_UNSUPPORTED: use the CUDA-core form).
+uint64_t qmm_tc_scratch_bytes(uint32_t rows, uint32_t cols, uint32_t batch, int sm_count);
+bool qmm_tc_eligible(const QmmParams& p);
+int launch_qmm_tc(const QmmParams& p, cudaStream_t stream, int sm_count, bool pdl, std::string* msg);
+
 // Largest supported column count (x and its partial sums live in shared memory).
 constexpr uint32_t kQmvMaxCols = 32768;
 

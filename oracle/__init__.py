@@ -98,6 +98,14 @@ def matvec(ggml_type: int, w, rows: int, cols: int, x: np.ndarray, threads: int 
     return y
 
 
+def matmul_many(ggml_type: int, w, rows: int, cols: int, batch: int, inputs, threads: int = 0) -> np.ndarray:
+    """si_q{4,5,6}_k_matmul_many (metal.rs:1083-1127): candidate k's output is
+    the dequantised matrix times inputs[k]; one oracle matvec per candidate.
+    Returns batch x rows."""
+    x = np.ascontiguousarray(inputs, np.float32).reshape(batch, cols)
+    return np.stack([matvec(ggml_type, w, rows, cols, x[k], threads) for k in range(batch)])
+
+
 def fused_gate_up(gate, up, rows, cols, x, threads=0):
     out = np.empty(rows, np.float32)
     _check(lib().or_fused_gate_up(_ptr(gate), _ptr(up), rows, cols, np.ascontiguousarray(x, np.float32), out, threads), "gate_up")
