@@ -1,4 +1,4 @@
-// Batched Q4_K matvec on the tensor cores: Y[k] = W X[k] for k < K <= 8 with
+// Batched Q4_K / Q6_K matvec on the tensor cores: Y[k] = W X[k] for k < K <= 8 with
 // one traversal of W (the verifier's weight pass, src/metal.rs:1055-1127,
 // 4067-4230; qwen35_runtime.rs:879-1289), exact integer sub-block sums.
 //
@@ -27,8 +27,15 @@
 // an f16 MMA pair (the 6-bit mins are exact in f16; the sums are hi + lo f16)
 // in the same fragment layout, subtracted before the block is added to the
 // running sums. The epilogue adds a group's phases in shared memory in a
-// fixed order. Matrices wider than a panel (34 blocks) run as column panels
+// fixed order. Matrices wider than a panel (33 blocks) run as column panels
 // writing partial sums that a small kernel adds in panel order.
+//
+// Q6_K: the int8 scales cover 16 elements, so the digits are laid out per
+// 16-element group and each group and plane is one m16n8k16 MMA (lane c holds
+// elements 4c..4c+3 of the group); the 6-bit quants are assembled in
+// registers from the low-nibble and high-bit words (loaded as 16-bit pairs:
+// 210-byte super-blocks leave rows 2-byte aligned), and the -32 offset is
+// the min term sum_G 32 sc_G xsum_G, one full-k f16 MMA pair.
 #include <algorithm>
 #include <string>
 
@@ -42,8 +49,12 @@ namespace {
 constexpr int kQtWarps = 16;
 constexpr int kQtThreads = kQtWarps * 32;
 constexpr uint32_t kQtSmemMax = 227 * 1024;
-constexpr uint32_t kQtDigBlock = 8 * 3 * 256;   // [8 sub-blocks][3 planes][8 candidates][32 B]
-constexpr uint32_t kQtXsBlock = 2 * 8 * 4 * 4;  // [hi/lo][8 candidates][4 lanes] f16 pairs
+// Digits of one 256-column block: Q4_K [8 sub-blocks][3 planes][8 candidates]
+// [32 B]; Q6_K [16 groups][3 planes][8 candidates][16 B].
+constexpr uint32_t kQtDigBlock = 8 * 3 * 256;
+// Sub-block sums of one block as f16 hi/lo pairs in MMA fragment order:
+// Q4_K [hi/lo][8 candidates][4 lanes] (256 B used); Q6_K [hi/lo][8][4][2].
+constexpr uint32_t kQtXsBlock = 512;
 constexpr uint32_t kQtPrefetch = 4;             // blocks prefetched into L2 ahead of the loads
 
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
@@ -69,6 +80,35 @@ __device__ __forceinline__ uint4 ldw_u4(const uint8_t* p, uint64_t pol) {
 // L2 prefetch of `bytes` (multiple of 16) at a 16-byte aligned address.
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ldw_u16(const uint8_t* p, uint64_t pol) {
+  unsigned short v;
+  asm volatile("ld.global.nc.L2::cache_hint.u16 %0, [%1], %2;" : "=h"(v) : "l"(p), "l"(pol));
+  return v;
+}
+
+// Four bytes at a 2-byte aligned address (Q6_K super-blocks are 210 B).
+__device__ __forceinline__ uint32_t ldw_u32_a2(const uint8_t* p, uint64_t pol) {
+  return ldw_u16(p, pol) | (ldw_u16(p + 2, pol) << 16);
+}
+
+// D = A B (k = 16, u8 x s8 -> s32, zero accumulator).
+__device__ __forceinline__ void mma_u8s8_k16(int* c, uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+      : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+}
+
+// D += A B, f16 inputs, f32 accumulate, all 16 k used.
+__device__ __forceinline__ void mma_f16_k16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                            uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ void mma_u8s8(int* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
@@ -99,9 +139,10 @@ struct PrepArgs {
   const float* x;
   uint64_t ldx;
   uint32_t K, nblk;
+  uint32_t q6;       // 1: Q6_K layouts (16-element groups), 0: Q4_K
   uint8_t* dig;      // [nblk][kQtDigBlock]
   float* esc;        // [nblk][8]
-  uint32_t* xs16;    // [nblk][2][8][4]
+  uint32_t* xs16;    // [nblk][kQtXsBlock / 4]
 };
 
 // One warp per (block, candidate slot 0..7); slots >= K write zeros.
@@ -125,11 +166,17 @@ __global__ void __launch_bounds__(32) qmm_prep_kernel(const PrepArgs a) {
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  s += __shfl_xor_sync(0xffffffffu, s, 1);
-  s += __shfl_xor_sync(0xffffffffu, s, 2);  // sub-block j = lane / 4, in every lane of the quad
+  s += __shfl_xor_sync(0xffffffffu, s, 1);  // Q6_K: group lane / 2, in both lanes of the pair
+  float s16 = s;
+  s += __shfl_xor_sync(0xffffffffu, s, 2);  // Q4_K: sub-block lane / 4, in every lane of the quad
   int e = int((__float_as_uint(mx) >> 23) & 255u) - 127;
-  e = max(e, -100);
+  e = min(max(e, -100), 126);
   const float up = __uint_as_float(uint32_t(21 - e + 127) << 23);  // 2^(21-e), exact
+  // sums in units of 2^e (|s| < 64 for a 32-element sub-block): in f16 range
+  // whatever the input's magnitude; the kernels fold 2^e back in
+  const float unit = __uint_as_float(uint32_t(127 - e) << 23);
+  s *= unit;
+  s16 *= unit;
   uint32_t pl[3][2] = {};
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -142,28 +189,46 @@ __global__ void __launch_bounds__(32) qmm_prep_kernel(const PrepArgs a) {
     pl[1][i >> 2] |= uint32_t(d1 & 255) << (8 * (i & 3));
     pl[2][i >> 2] |= uint32_t(d2 & 255) << (8 * (i & 3));
   }
-  const uint32_t j = lane >> 2, c = lane & 3;
   uint8_t* blk = a.dig + uint64_t(b) * kQtDigBlock;
+  uint32_t* xs = a.xs16 + uint64_t(b) * (kQtXsBlock / 4);
+  if (!a.q6) {
+    const uint32_t j = lane >> 2, c = lane & 3;
 #pragma unroll
-  for (int p = 0; p < 3; ++p)
-    *reinterpret_cast<uint2*>(blk + (j * 3 + p) * 256 + k * 32 + 8 * c) = make_uint2(pl[p][0], pl[p][1]);
-  // 2^(e-21) per digit unit and 1/16 for the high nibbles being multiplied as
-  // 16 q (the low-nibble scales are multiplied by 16)
-  if (lane == 0) a.esc[uint64_t(b) * 8 + k] = live ? __uint_as_float(uint32_t(e - 25 + 127) << 23) : 0.f;
-  // sub-block sums j = 2q, 2q+1 as f16 hi + lo pairs: the min-term MMA's B
-  // fragment of lane (g = k, c = q)
-  const float s_next = __shfl_down_sync(0xffffffffu, s, 4);  // sum of sub-block j + 1
-  if ((lane & 7) == 0) {
-    const uint32_t q = lane >> 3;
-    const float h0 = __half2float(__float2half_rn(s)), h1 = __half2float(__float2half_rn(s_next));
-    uint32_t* xs = a.xs16 + uint64_t(b) * 64;
-    xs[(0 * 8 + k) * 4 + q] = pack_f16x2(h0, h1);
-    xs[(1 * 8 + k) * 4 + q] = pack_f16x2(s - h0, s_next - h1);
+    for (int p = 0; p < 3; ++p)
+      *reinterpret_cast<uint2*>(blk + (j * 3 + p) * 256 + k * 32 + 8 * c) = make_uint2(pl[p][0], pl[p][1]);
+    // 2^(e-21) per digit unit and 1/16 for the high nibbles being multiplied
+    // as 16 q (the low-nibble scales are multiplied by 16)
+    if (lane == 0) a.esc[uint64_t(b) * 8 + k] = live ? __uint_as_float(uint32_t(e - 25 + 127) << 23) : 0.f;
+    // sub-block sums j = 2q, 2q+1 as f16 hi + lo pairs: the min-term MMA's B
+    // fragment of lane (g = k, c = q)
+    const float s_next = __shfl_down_sync(0xffffffffu, s, 4);  // sum of sub-block j + 1
+    if ((lane & 7) == 0) {
+      const uint32_t q = lane >> 3;
+      const float h0 = __half2float(__float2half_rn(s)), h1 = __half2float(__float2half_rn(s_next));
+      xs[(0 * 8 + k) * 4 + q] = pack_f16x2(h0, h1);
+      xs[(1 * 8 + k) * 4 + q] = pack_f16x2(s - h0, s_next - h1);
+    }
+  } else {
+    const uint32_t G = lane >> 1;  // 16-element group of this lane's 8 elements
+#pragma unroll
+    for (int p = 0; p < 3; ++p)
+      *reinterpret_cast<uint2*>(blk + (G * 3 + p) * 128 + k * 16 + 8 * (lane & 1)) = make_uint2(pl[p][0], pl[p][1]);
+    if (lane == 0) a.esc[uint64_t(b) * 8 + k] = live ? __uint_as_float(uint32_t(e - 21 + 127) << 23) : 0.f;
+    // group sums G = 2c, 2c+1 (b0) and 2c+8, 2c+9 (b1) of the full-k f16
+    // MMA's B fragment of lane (g = k, c), as hi + lo pairs
+    const float s_next = __shfl_down_sync(0xffffffffu, s16, 2);  // sum of group G + 1
+    if ((lane & 3) == 0) {
+      const uint32_t c = (lane & 15) >> 2, slot = lane >> 4;
+      const float h0 = __half2float(__float2half_rn(s16)), h1 = __half2float(__float2half_rn(s_next));
+      xs[((0 * 8 + k) * 4 + c) * 2 + slot] = pack_f16x2(h0, h1);
+      xs[((1 * 8 + k) * 4 + c) * 2 + slot] = pack_f16x2(s16 - h0, s_next - h1);
+    }
   }
 }
 
 struct QtArgs {
   const uint8_t* w;
+  const uint8_t* w_end;  // one past the matrix (the Q6_K L2 prefetch stays inside)
   uint32_t rows, nblk, K;
   const uint8_t* dig;
   const float* esc;
@@ -180,13 +245,14 @@ struct QtArgs {
   int* err;
 };
 
-__global__ void __launch_bounds__(kQtThreads, 1) qmm_tc_q4k_kernel(const QtArgs a) {
+template <uint32_t TYPE>
+__global__ void __launch_bounds__(kQtThreads, 1) qmm_tc_kernel(const QtArgs a) {
   extern __shared__ __align__(128) uint8_t sm[];
   const uint32_t panel = blockIdx.y, b0 = panel * a.pb, nb = min(a.pb, a.nblk - b0);
   uint8_t* sdig = sm;
   float* sesc = reinterpret_cast<float*>(sdig + nb * kQtDigBlock);
   uint32_t* sxs = reinterpret_cast<uint32_t*>(sesc + nb * 8);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sxs + nb * 64);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sxs + nb * (kQtXsBlock / 4));
   float* red = reinterpret_cast<float*>(sm + a.red_off);  // [warp][16 rows][8 candidates]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
 
@@ -210,7 +276,7 @@ __global__ void __launch_bounds__(kQtThreads, 1) qmm_tc_q4k_kernel(const QtArgs 
     const uint32_t tab = nb * 32 + nb * kQtXsBlock;
     mbar_arrive_expect_tx(&bar[0], tab + kQtDigBlock);
     bulk_g2s(sesc, a.esc + uint64_t(b0) * 8, nb * 32, &bar[0], pol);
-    bulk_g2s(sxs, a.xs16 + uint64_t(b0) * 64, nb * kQtXsBlock, &bar[0], pol);
+    bulk_g2s(sxs, a.xs16 + uint64_t(b0) * (kQtXsBlock / 4), nb * kQtXsBlock, &bar[0], pol);
     bulk_g2s(sdig, a.dig + uint64_t(b0) * kQtDigBlock, kQtDigBlock, &bar[0], pol);
     for (uint32_t i = 1; i < nb; ++i) {
       mbar_arrive_expect_tx(&bar[i], kQtDigBlock);
@@ -228,7 +294,117 @@ __global__ void __launch_bounds__(kQtThreads, 1) qmm_tc_q4k_kernel(const QtArgs 
     // C-fragment layout: [0] row g cand 2c, [1] row g cand 2c+1, [2] row g+8
     // cand 2c, [3] row g+8 cand 2c+1
     float yk[4] = {0.f, 0.f, 0.f, 0.f};
-    if (active) {
+    if (active && TYPE == SI_GGML_TYPE_Q6_K) {
+      const uint32_t grp = g0 + gl;
+      const uint32_t r0 = min(grp * 16 + g, a.rows - 1), r8 = min(grp * 16 + g + 8, a.rows - 1);
+      const uint8_t* w0 = a.w + (uint64_t(r0) * a.nblk + b0) * 210;
+      const uint8_t* w8 = a.w + (uint64_t(r8) * a.nblk + b0) * 210;
+      // lanes 0..15 prefetch the 16-byte aligned envelope of row grp*16+lane's
+      // blocks ahead into L2 (never past the matrix)
+      const uint8_t* wp = a.w + (uint64_t(min(grp * 16 + (lane & 15), a.rows - 1)) * a.nblk + b0) * 210;
+      auto prefetch = [&](uint32_t blk) {
+        const uint8_t* env = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(wp + blk * 210) & ~uintptr_t(15));
+        if (env + 224 <= a.w_end) prefetch_l2(env, 224);
+      };
+      if (lane < 16)
+        for (uint32_t d = 0; d <= kQtPrefetch; ++d)
+          if (phase + d * split < nb) prefetch(phase + d * split);
+      for (uint32_t i = phase; i < nb; i += split) {
+        if (lane < 16 && i + (kQtPrefetch + 1) * split < nb) prefetch(i + (kQtPrefetch + 1) * split);
+        const uint8_t* p0 = w0 + i * 210;
+        const uint8_t* p8 = w8 + i * 210;
+        // int8 scales (bytes 192..207) and d (208) of rows g and g+8
+        uint32_t sw0[4], sw8[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          sw0[t] = ldw_u32_a2(p0 + 192 + 4 * t, wpol);
+          sw8[t] = ldw_u32_a2(p8 + 192 + 4 * t, wpol);
+        }
+        const float dd0 = half_bits_to_float(ldw_u16(p0 + 208, wpol));
+        const float dd8 = half_bits_to_float(ldw_u16(p8 + 208, wpol));
+        // quants: per half and 16-element half-group, the low-bit words of
+        // m = 0,2 and m = 1,3 and the high-bit word, 4 bytes for lane c
+        uint32_t ql0[2][2][2], ql8[2][2][2], qh0[2][2], qh8[2][2];
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            qh0[hf][hh] = ldw_u32_a2(p0 + 128 + hf * 32 + 16 * hh + 4 * c, wpol);
+            qh8[hf][hh] = ldw_u32_a2(p8 + 128 + hf * 32 + 16 * hh + 4 * c, wpol);
+#pragma unroll
+            for (int mp = 0; mp < 2; ++mp) {
+              ql0[hf][mp][hh] = ldw_u32_a2(p0 + hf * 64 + mp * 32 + 16 * hh + 4 * c, wpol);
+              ql8[hf][mp][hh] = ldw_u32_a2(p8 + hf * 64 + mp * 32 + 16 * hh + 4 * c, wpol);
+            }
+          }
+        if (!table_ready) {
+          if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bar[0], 0))) {
+            timed_out = true;
+            break;
+          }
+          table_ready = true;
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bar[i], 0))) {
+          timed_out = true;
+          break;
+        }
+        int acc[3][4];
+#pragma unroll
+        for (int p = 0; p < 3; ++p) acc[p][0] = acc[p][1] = acc[p][2] = acc[p][3] = 0;
+        const uint8_t* xb = sdig + i * kQtDigBlock + g * 16 + 4 * c;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+          for (int m = 0; m < 4; ++m)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const int G = hf * 8 + 2 * m + hh;  // 16-element group: scale index and digit row
+              const uint32_t l0 = ql0[hf][m & 1][hh], l8 = ql8[hf][m & 1][hh];
+              const uint32_t a0 = (m < 2 ? (l0 & 0x0F0F0F0Fu) : ((l0 >> 4) & 0x0F0F0F0Fu)) |
+                                  (((qh0[hf][hh] >> (2 * m)) & 0x03030303u) << 4);
+              const uint32_t a8 = (m < 2 ? (l8 & 0x0F0F0F0Fu) : ((l8 >> 4) & 0x0F0F0F0Fu)) |
+                                  (((qh8[hf][hh] >> (2 * m)) & 0x03030303u) << 4);
+              const int s0 = int(int8_t(uint8_t(byte_of(sw0[G >> 2], G & 3))));
+              const int s8 = int(int8_t(uint8_t(byte_of(sw8[G >> 2], G & 3))));
+#pragma unroll
+              for (int p = 0; p < 3; ++p) {
+                const uint32_t bb = *reinterpret_cast<const uint32_t*>(xb + (G * 3 + p) * 128);
+                int C[4];
+                mma_u8s8_k16(C, a0, a8, bb);
+                acc[p][0] += s0 * C[0];
+                acc[p][1] += s0 * C[1];
+                acc[p][2] += s8 * C[2];
+                acc[p][3] += s8 * C[3];
+              }
+            }
+        // the -32 offset: sum over groups of 32 sc_G (exact in f16) times the
+        // group sums (f16 hi + lo), f32 accumulate
+        float mt[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+          auto sc32 = [](uint32_t w, uint32_t j) { return 32.f * float(int(int8_t(uint8_t(byte_of(w, j))))); };
+          const bool hi = c >= 2;  // groups 2c, 2c+1 (word c/2) and 2c+8, 2c+9 (word 2 + c/2)
+          const uint32_t jl = (2 * c) & 3;
+          const uint32_t w00 = hi ? sw0[1] : sw0[0], w08 = hi ? sw8[1] : sw8[0];
+          const uint32_t w20 = hi ? sw0[3] : sw0[2], w28 = hi ? sw8[3] : sw8[2];
+          const uint32_t a0 = pack_f16x2(sc32(w00, jl), sc32(w00, jl + 1));
+          const uint32_t a1 = pack_f16x2(sc32(w08, jl), sc32(w08, jl + 1));
+          const uint32_t a2 = pack_f16x2(sc32(w20, jl), sc32(w20, jl + 1));
+          const uint32_t a3 = pack_f16x2(sc32(w28, jl), sc32(w28, jl + 1));
+          const uint2 bh = *reinterpret_cast<const uint2*>(sxs + i * (kQtXsBlock / 4) + ((0 * 8 + g) * 4 + c) * 2);
+          const uint2 bl = *reinterpret_cast<const uint2*>(sxs + i * (kQtXsBlock / 4) + ((1 * 8 + g) * 4 + c) * 2);
+          mma_f16_k16(mt, a0, a1, a2, a3, bh.x, bh.y);
+          mma_f16_k16(mt, a0, a1, a2, a3, bl.x, bl.y);
+        }
+        const float2 es = *reinterpret_cast<const float2*>(sesc + i * 8 + 2 * c);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const float f = fmaf(65536.f, float(acc[2][v]), fmaf(256.f, float(acc[1][v]), float(acc[0][v])));
+          // esc = 2^(e-21) per digit unit; the sums are in units of 2^e = esc 2^21
+          yk[v] += (v < 2 ? dd0 : dd8) * ((v & 1 ? es.y : es.x) * fmaf(-2097152.f, mt[v], f));
+        }
+      }
+    }
+    if (active && TYPE == SI_GGML_TYPE_Q4_K) {
       const uint32_t grp = g0 + gl;
       const uint32_t r0 = min(grp * 16 + g, a.rows - 1), r8 = min(grp * 16 + g + 8, a.rows - 1);
       const uint8_t* w0 = a.w + (uint64_t(r0) * a.nblk + b0) * 144;
@@ -319,7 +495,7 @@ __global__ void __launch_bounds__(kQtThreads, 1) qmm_tc_q4k_kernel(const QtArgs 
           const uint32_t jj = (2 * c) & 3;
           const uint32_t a0 = pack_f16x2(float(byte_of(ml0, jj)), float(byte_of(ml0, jj + 1)));
           const uint32_t a1 = pack_f16x2(float(byte_of(ml8, jj)), float(byte_of(ml8, jj + 1)));
-          const uint32_t* xs = sxs + i * 64;
+          const uint32_t* xs = sxs + i * (kQtXsBlock / 4);
           mma_f16(mt, a0, a1, xs[(0 * 8 + g) * 4 + c]);
           mma_f16(mt, a0, a1, xs[(1 * 8 + g) * 4 + c]);
         }
@@ -330,7 +506,9 @@ __global__ void __launch_bounds__(kQtThreads, 1) qmm_tc_q4k_kernel(const QtArgs 
         for (int v = 0; v < 4; ++v) {
           const float f = fmaf(65536.f, float(acc[2][v]), fmaf(256.f, float(acc[1][v]), float(acc[0][v])));
           const float d = v < 2 ? dd0.x : dd8.x, dm = v < 2 ? dd0.y : dd8.y;
-          yk[v] += d * (v & 1 ? es.y : es.x) * f - dm * mt[v];
+          // esc = 2^(e-25) (digit unit / 16); the sums are in units of 2^e = esc 2^25
+          const float e1 = v & 1 ? es.y : es.x;
+          yk[v] += d * e1 * f - dm * (e1 * 33554432.f) * mt[v];
         }
       }
     }
@@ -415,8 +593,10 @@ uint64_t qmm_tc_scratch_bytes(uint32_t rows, uint32_t cols, uint32_t batch, int 
 }
 
 bool qmm_tc_eligible(const QmmParams& p) {
-  return p.type == SI_GGML_TYPE_Q4_K && p.batch >= 2 && p.batch <= kQmmMaxBatch && p.rows >= 16 &&
-         !(reinterpret_cast<uintptr_t>(p.w) & 15) && p.scratch && !(reinterpret_cast<uintptr_t>(p.scratch) & 255);
+  const bool q4 = p.type == SI_GGML_TYPE_Q4_K, q6 = p.type == SI_GGML_TYPE_Q6_K;
+  return (q4 || q6) && p.batch >= 2 && p.batch <= kQmmMaxBatch && p.rows >= 16 &&
+         !(reinterpret_cast<uintptr_t>(p.w) & (q4 ? 15u : 1u)) && p.scratch &&
+         !(reinterpret_cast<uintptr_t>(p.scratch) & 255);
 }
 
 int launch_qmm_tc(const QmmParams& p, cudaStream_t s, int sm_count, bool pdl, std::string* msg) {
@@ -428,6 +608,7 @@ int launch_qmm_tc(const QmmParams& p, cudaStream_t s, int sm_count, bool pdl, st
   pa.ldx = p.ldx;
   pa.K = p.batch;
   pa.nblk = p.cols / 256;
+  pa.q6 = p.type == SI_GGML_TYPE_Q6_K;
   pa.dig = sc;
   pa.esc = reinterpret_cast<float*>(sc + align256u(g.dig_bytes));
   pa.xs16 = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(pa.esc) + align256u(g.esc_bytes));
@@ -446,6 +627,7 @@ int launch_qmm_tc(const QmmParams& p, cudaStream_t s, int sm_count, bool pdl, st
 
   QtArgs a = {};
   a.w = p.w;
+  a.w_end = p.w + uint64_t(p.rows) * pa.nblk * (pa.q6 ? 210 : 144);
   a.rows = p.rows;
   a.nblk = pa.nblk;
   a.K = p.batch;
@@ -462,11 +644,12 @@ int launch_qmm_tc(const QmmParams& p, cudaStream_t s, int sm_count, bool pdl, st
   a.part = part;
   a.red_off = g.red_off;
   a.err = p.err;
+  auto kern = pa.q6 ? qmm_tc_kernel<SI_GGML_TYPE_Q6_K> : qmm_tc_kernel<SI_GGML_TYPE_Q4_K>;
   if (e == cudaSuccess) {
-    static bool smem_set = false;  // the first call raises the kernel's shared memory limit
-    if (!smem_set) {
-      e = cudaFuncSetAttribute(qmm_tc_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kQtSmemMax));
-      smem_set = e == cudaSuccess;
+    static bool smem_set[2] = {false, false};  // the first call raises each kernel's shared memory limit
+    if (!smem_set[pa.q6]) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kQtSmemMax));
+      smem_set[pa.q6] = e == cudaSuccess;
     }
   }
   if (e == cudaSuccess) {
@@ -477,7 +660,7 @@ int launch_qmm_tc(const QmmParams& p, cudaStream_t s, int sm_count, bool pdl, st
     mc.stream = s;
     mc.attrs = attr;
     mc.numAttrs = 1;  // after the prep kernel: its tail overlaps this prologue
-    e = cudaLaunchKernelEx(&mc, qmm_tc_q4k_kernel, a);
+    e = cudaLaunchKernelEx(&mc, kern, a);
   }
   if (e == cudaSuccess && g.panels > 1) {
     qmm_reduce_kernel<<<dim3((p.rows + 255) / 256, p.batch), 256, 0, s>>>(part, g.panels, p.batch, p.rows, p.y,

@@ -30,6 +30,23 @@ def test_matmul_many_matches_oracle(mai, ctx, ty, rows, cols, batch):
         assert rel_l2(y[k], ref[k]) < 1e-5, k
 
 
+@pytest.mark.parametrize("ty", [Q4, Q6])
+def test_matmul_many_large_and_tiny_inputs(mai, ctx, ty):
+    """Inputs far from unit scale: the tensor-core form keeps its per-block
+    sums in units of the block's own power of two."""
+    rng = np.random.default_rng(11 + ty)
+    rows, cols, batch = 512, 2048, 6
+    w = random_blocks(rng, ty, rows * cols // 256)
+    x = rng.normal(0, 1, (batch, cols)).astype(np.float32)
+    x[:2] *= 3e6
+    x[2:4] *= 1e-6
+    x[4, :256] = 0.0  # an all-zero block
+    y = ctx.gguf_quant_matmul_many_bytes(ty, w, rows, cols, batch, x)
+    ref = O.matmul_many(ty, w, rows, cols, batch, x)
+    for k in range(batch):
+        assert rel_l2(y[k], ref[k]) < 1e-5, k
+
+
 def test_matmul_many_retained_weight_and_device_form(mai, ctx):
     import torch
     rng = np.random.default_rng(5)
