@@ -347,8 +347,9 @@ def time_cuda(torch, fn, iters, stream):
 
 
 def measure_kernels(mai, ctx, torch, np):
-    """Fused SwiGLU MLP and split-K attention over the bf16
-    KV cache (config 4), device-resident inputs, back-to-back launches."""
+    """Fused SwiGLU MLP, split-K attention over the bf16
+    KV cache (config 4) and the K = 8 batched verifier matvecs, device-resident
+    inputs, back-to-back launches."""
     rng = np.random.default_rng(7)
     H, I = 5120, 17408
     st = torch.cuda.ExternalStream(ctx.stream)
@@ -402,6 +403,26 @@ def measure_kernels(mai, ctx, torch, np):
     out["attention_config4"] = {"us_per_call": round(us, 2), "GBps": round(att_bytes / us / 1e3, 1),
                                 "alg_bytes": att_bytes, "note": "24 q / 4 kv heads, hd 256, 8191 cached bf16 positions + 1 new; 100 calls in a CUDA graph",
                                 "launches_per_call": 2}
+    del kvs
+    # batched verifier matvecs (si_q{4,5,6}_k_matmul_many, metal.rs:1055-1267):
+    # K = 8 inputs against one matrix, beside K single matvecs of the same matrix
+    for name, ty, rows, cols, bb in (("matmul_many_q4k_17408x5120_K8", 12, I, H, 144),
+                                     ("matmul_many_q6k_5120x17408_K8", 14, H, I, 210)):
+        K, copies = 8, 4
+        d_at = (0, 2) if ty == 12 else (208,)
+        ws = [torch.from_numpy(q_blocks(rng, np, rows * cols // 256, bb, d_at)).to(dev) for _ in range(copies)]
+        xk = torch.randn(K, cols, device=dev)
+        yk = torch.empty(K, rows, device=dev)
+        us_k = time_cuda(torch, lambda i: ctx.qmatmul_many_dev(ty, ws[i % copies], rows, cols, K, xk, yk, ctx.stream),
+                         40, st)
+        us_1 = time_cuda(torch, lambda i: ctx.qmatvec_dev(ty, ws[i % copies], rows, cols, xk[0], yk[0], ctx.stream),
+                         40, st)
+        wbytes = rows * cols // 256 * bb
+        out[name] = {"us_per_call": round(us_k, 2), "us_per_candidate": round(us_k / K, 2),
+                     "single_matvec_us": round(us_1, 2), "speedup_vs_K_matvecs": round(K * us_1 / us_k, 2),
+                     "weight_GBps": round(wbytes / us_k / 1e3, 1), "alg_bytes": wbytes + K * (rows + cols) * 4,
+                     "note": f"{copies} weight copies cycled; prep + main (+ panel reduce) launches per call"}
+        del ws
     return out
 
 
