@@ -70,6 +70,15 @@ void si_ctx_destroy(si_ctx* ctx);
 const char* si_last_error(const si_ctx* ctx);
 /* Text of the last error of a call that had no context (si_ctx_create). */
 const char* si_global_last_error(void);
+/* metal::probe (metal.rs:18-24, 1770-1779): the device's name, its memory
+ * (the working-set bound: total HBM bytes), the SM count, the compute
+ * capability and the number of visible devices. No context needed. */
+typedef struct si_device_info {
+  char name[256];
+  uint64_t total_bytes;
+  uint32_t sm_count, cc_major, cc_minor, device_count;
+} si_device_info;
+int si_device_probe(int device, si_device_info* out);
 /* Number of SMs and the device ordinal the context runs on. */
 int si_ctx_info(const si_ctx* ctx, int* device, int* sm_count);
 /* The context's compute stream (cudaStream_t as void*). */

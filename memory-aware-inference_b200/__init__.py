@@ -47,6 +47,21 @@ class SiCtxConfig(C.Structure):
     _fields_ = [("hbm_budget_bytes", C.c_uint64), ("stage_depth", C.c_uint32), ("flags", C.c_uint32)]
 
 
+class SiDeviceInfo(C.Structure):
+    _fields_ = [("name", C.c_char * 256), ("total_bytes", C.c_uint64), ("sm_count", C.c_uint32),
+                ("cc_major", C.c_uint32), ("cc_minor", C.c_uint32), ("device_count", C.c_uint32)]
+
+
+def device_probe(device: int = 0) -> dict:
+    """metal::probe (metal.rs:1770-1779) for a CUDA device."""
+    info = SiDeviceInfo()
+    rc = lib().si_device_probe(device, C.byref(info))
+    if rc != 0:
+        raise SiError(rc, lib().si_global_last_error().decode())
+    return {"name": info.name.decode(), "total_bytes": info.total_bytes, "sm_count": info.sm_count,
+            "cc": (info.cc_major, info.cc_minor), "device_count": info.device_count}
+
+
 class SiStats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("current_allocated_bytes", "peak_allocated_bytes",
                                           "peak_active_weight_bytes", "peak_kv_bytes", "peak_scratch_bytes",
@@ -101,6 +116,7 @@ def lib():
         "si_last_error": ([vp], C.c_char_p),
         "si_global_last_error": ([], C.c_char_p),
         "si_ctx_info": ([vp, vp, vp], i32),
+        "si_device_probe": ([i32, vp], i32),
         "si_ctx_stream": ([vp], vp),
         "si_get_stats": ([vp, vp], i32),
         "si_reset_peaks": ([vp], i32),

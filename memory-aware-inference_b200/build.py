@@ -2,8 +2,8 @@
 
 Usage: python memory-aware-inference_b200/build.py [--force]
 Objects go to memory-aware-inference_b200/_build/, the library to
-memory-aware-inference_b200/libsi_cuda.so (both git-ignored; the .so travels
-with the repository snapshot to the GPU box).
+memory-aware-inference_b200/libsi_cuda.so and the si-bench command line next
+to it (all git-ignored; they travel with the repository snapshot to the GPU box).
 """
 import concurrent.futures as cf
 import glob
@@ -16,6 +16,7 @@ REPO = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libsi_cuda.so")
+CLI = os.path.join(HERE, "si-bench")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -71,7 +72,24 @@ def build(force=False, verbose=False):
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}")
+    build_cli(force)
     return LIB
+
+
+def build_cli(force=False):
+    """The si-bench command line (cli/si_bench.cpp): host C++ over the C ABI,
+    linked against libsi_cuda.so beside it."""
+    src = os.path.join(HERE, "cli", "si_bench.cpp")
+    deps = [src, LIB, os.path.join(REPO, "include", "si_cuda.h")]
+    if not force and os.path.exists(CLI) and os.path.getmtime(CLI) >= max(os.path.getmtime(d) for d in deps):
+        return CLI
+    _, libdir = _nccl_dirs()
+    cmd = ["g++", "-O2", "-std=c++17", "-Wall", "-I", os.path.join(REPO, "include"), src, "-o", CLI, "-L", HERE,
+           "-l:libsi_cuda.so", "-Wl,-rpath,$ORIGIN", "-Wl,-rpath-link," + libdir]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"si-bench build failed:\n{r.stderr}")
+    return CLI
 
 
 if __name__ == "__main__":

@@ -3,6 +3,7 @@
 // messages follow the reference methods so Rust callers see the same errors.
 #include <chrono>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -204,6 +205,27 @@ void si_ctx_destroy(si_ctx* ctx) {
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
   delete ctx;
+}
+
+int si_device_probe(int device, si_device_info* out) {
+  if (!out) return fail(nullptr, SI_E_INVALID, "invalid probe arguments");
+  std::memset(out, 0, sizeof(*out));
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return fail(nullptr, SI_E_CUDA, "no CUDA device found");
+  }
+  if (device < 0 || device >= n) return fail(nullptr, SI_E_INVALID, "device ordinal out of range");
+  cudaDeviceProp p;
+  if ((e = cudaGetDeviceProperties(&p, device)) != cudaSuccess) return cuda_fail(nullptr, e, "device properties");
+  std::snprintf(out->name, sizeof(out->name), "%s", p.name);
+  out->total_bytes = p.totalGlobalMem;
+  out->sm_count = uint32_t(p.multiProcessorCount);
+  out->cc_major = uint32_t(p.major);
+  out->cc_minor = uint32_t(p.minor);
+  out->device_count = uint32_t(n);
+  return SI_OK;
 }
 
 int si_ctx_info(const si_ctx* ctx, int* device, int* sm_count) {

@@ -1,0 +1,146 @@
+"""si-bench command line (memory-aware-inference_b200/cli/si_bench.cpp): the
+reference's argument parsing, reports and exit codes (src/main.rs:1-276,
+src/lib.rs:45-264). CPU tests use the mock backend and the error paths; the
+GPU test runs the CUDA backend on a synthetic model and checks its ids
+against the Python API."""
+import json
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from conftest import PKG_DIR, load_package
+
+CLI = os.path.join(PKG_DIR, "si-bench")
+
+
+def run(*args):
+    load_package().lib()  # built alongside the library
+    assert os.path.exists(CLI), "si-bench is built by build.py"
+    r = subprocess.run([CLI, *args], capture_output=True, text=True, timeout=600)
+    return r.returncode, r.stdout, r.stderr
+
+
+def test_help_and_no_arguments_print_usage():
+    for args in ([], ["--help"], ["--model", "m", "-h"]):
+        rc, out, _ = run(*args)
+        assert rc == 0 and out.startswith("Usage: si-bench --model PATH --backend")
+
+
+def test_validates_required_arguments():  # main.rs:182-188
+    rc, _, err = run("--backend", "mock")
+    assert rc == 1 and "error: --model is required" in err
+    rc, _, err = run("--model", "m", "--prompt", "hi")
+    assert rc == 1 and "--backend is required" in err
+    rc, _, err = run("--model", "m", "--backend", "mock")
+    assert rc == 1 and "--prompt is required" in err
+    rc, _, err = run("--model", "m", "--backend", "rocm", "--prompt", "hi")
+    assert rc == 1 and "unsupported backend: rocm" in err
+
+
+@pytest.mark.parametrize("args,message", [
+    (["--model"], "missing value for --model"),
+    (["--max-tokens", "0"], "--max-tokens must be a positive integer"),
+    (["--context", "x"], "--context must be a positive integer"),
+    (["--repetitions", "-2"], "--repetitions must be a positive integer"),
+    (["--warmup", "-1"], "--warmup must be a non-negative integer"),
+    (["--output", "xml"], "--output must be text or json"),
+    (["--frobnicate", "1"], "unknown option: --frobnicate"),
+    (["--prompt-ids", "1,,2"], "--prompt-ids must be comma-separated token ids"),
+])
+def test_argument_errors_exit_1(args, message):
+    rc, _, err = run("--model", "m", "--backend", "mock", "--prompt", "hi", *args)
+    assert rc == 1 and message in err and "Usage:" in err
+
+
+def test_mock_json_report():  # main.rs:191-212, lib.rs:210-230
+    rc, out, _ = run("--model", "m", "--backend", "mock", "--prompt", "hello big world", "--output", "json",
+                     "--max-tokens", "3", "--warmup", "0")
+    assert rc == 0
+    d = json.loads(out)
+    assert list(d) == ["model_path", "backend", "prompt_tokens", "generated_tokens", "warmup_runs", "prefill_ms",
+                       "decode_ms", "prefill_tok_s", "decode_tok_s", "total_tok_s", "peak_vram_mib", "peak_ram_mib",
+                       "output_match", "generated_output"]
+    assert (d["backend"], d["prompt_tokens"], d["generated_tokens"], d["warmup_runs"]) == ("mock", 3, 3, 0)
+    assert d["generated_output"] == "mock-0 mock-1 mock-2"
+    assert (d["peak_vram_mib"], d["peak_ram_mib"], d["output_match"]) == (64, 32, None)
+
+
+def test_mock_text_report_and_escaping():
+    path = 'model\\"x\nq'
+    rc, out, _ = run("--model", path, "--backend", "mock", "--prompt", "a", "--max-tokens", "16")
+    lines = out.splitlines()
+    assert rc == 0 and lines[0] == "model=model\\\"x" and lines[1] == "q"
+    keys = [l.split("=")[0] for l in lines[2:]]
+    assert keys == ["backend", "prompt_tokens", "generated_tokens", "warmup_runs", "prefill_ms", "decode_ms",
+                    "prefill_tok_s", "decode_tok_s", "total_tok_s", "peak_vram_mib", "peak_ram_mib", "output_match",
+                    "generated_output"]
+    assert "peak_vram_mib=66" in lines  # 64 + 16 / 8
+    rc, out, _ = run("--model", path, "--backend", "mock", "--prompt", "a", "--output", "json")
+    assert rc == 0 and '"model_path":"model\\\\\\"x\\nq"' in out and json.loads(out)["model_path"] == path
+
+
+def test_mock_compares_expected_output():  # lib.rs:232-238; exit code 2 on a mismatch (main.rs:24-28)
+    rc, out, _ = run("--model", "m", "--backend", "mock", "--prompt", "hi", "--max-tokens", "2",
+                     "--expected-output", "mock-0 mock-1", "--output", "json")
+    assert rc == 0 and json.loads(out)["output_match"] is True
+    rc, out, _ = run("--model", "m", "--backend", "mock", "--prompt", "hi", "--max-tokens", "2",
+                     "--expected-output", "mock-0 mock-2", "--output", "json")
+    assert rc == 2 and json.loads(out)["output_match"] is False
+
+
+@pytest.mark.parametrize("args,message", [
+    (["--prompt", "hello"], "no tokenizer: pass the prompt as token ids with --prompt-ids"),
+    (["--prompt-ids", "1,2", "--chunk-rows", "16"], "does not accept --chunk-rows"),
+    (["--prompt-ids", "1,2", "--quality-fixture", "q.json"], "omit --quality-fixture"),
+])
+def test_cuda_backend_refusals_before_any_device_work(args, message):
+    rc, _, err = run("--model", "synthetic:small", "--backend", "cuda-resident", *args)
+    assert rc == 1 and message in err
+
+
+def test_cuda_backend_model_checks(tmp_path):
+    bogus = tmp_path / "x.bin"
+    bogus.write_bytes(b"NOPE" + bytes(64))
+    rc, _, err = run("--model", str(bogus), "--backend", "metal-resident", "--prompt-ids", "1")
+    assert rc == 1 and "unsupported model container" in err
+    rc, _, err = run("--model", str(tmp_path), "--backend", "cuda-streaming", "--prompt-ids", "1")
+    assert rc == 1 and "Safetensors" in err
+    rc, _, err = run("--model", "synthetic:70b", "--backend", "cuda-resident", "--prompt-ids", "1")
+    assert rc == 1 and "unknown synthetic model" in err
+
+
+def test_cuda_backend_without_a_device_fails_cleanly():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a device is present")
+    rc, _, err = run("--model", "synthetic:small", "--backend", "cuda-resident", "--prompt-ids", "1,2")
+    assert rc == 1 and "error: device probe" in err
+
+
+@pytest.mark.gpu
+def test_cuda_backend_ids_match_the_python_api(mai, ctx):
+    rc, out, err = run("--model", "synthetic:small", "--backend", "cuda-resident", "--prompt-ids", "5,77,1024",
+                       "--max-tokens", "6", "--context", "64", "--warmup", "0", "--repetitions", "2",
+                       "--output", "json")
+    assert rc == 0, err
+    d = json.loads(out)
+    cfg = mai.qwen36_27b_config(hidden=512, intermediate=1024, layers=8, vocab=4096, attn_q_heads=4,
+                                attn_kv_heads=2, attn_head_dim=128, rotary_dim=32, gdn_key_heads=2,
+                                gdn_value_heads=4, kv_capacity=64)
+    m = mai.Model(ctx, cfg, seed=27)
+    ids = m.generate([5, 77, 1024], 6)
+    m.close()
+    assert d["generated_token_ids"] == ids and d["repetition_outputs_match"] is True
+    assert d["prompt_tokens"] == 3 and d["generated_tokens"] == len(ids) and d["device"]
+    assert d["peak_vram_mib"] > 0 and d["decode_tok_s"] > 0
+    expected = " ".join(str(i) for i in ids)
+    rc, out, _ = run("--model", "synthetic:small", "--backend", "metal-streaming", "--retain-layers", "2",
+                     "--prompt-ids", "5,77,1024", "--max-tokens", "6", "--context", "64", "--warmup", "0",
+                     "--repetitions", "1", "--expected-output", expected)
+    assert rc == 0 and "output_match=true" in out
+    rc, _, _ = run("--model", "synthetic:small", "--backend", "cuda-resident", "--prompt-ids", "5,77,1024",
+                   "--max-tokens", "6", "--context", "64", "--warmup", "0", "--repetitions", "1",
+                   "--expected-output", expected + " 1")
+    assert rc == 2
