@@ -369,6 +369,57 @@ int si_model_logits_many(si_model* m, const float* hidden, uint32_t n, float* lo
 int si_model_verify_many(si_model* m, const uint32_t* tokens, const uint64_t* positions, uint32_t n,
                          uint32_t* ids, float* logits);
 
+/* ---- planner traces (planner.rs:10-251; SI-003 planner interface) -------- */
+/* ActionKind, MemoryTier and PlannerMode of the reference (SI_TIER_HBM plays
+ * the reference's Metal tier). */
+enum { SI_ACT_PREFETCH = 0, SI_ACT_EXECUTE, SI_ACT_RETAIN, SI_ACT_EVICT, SI_ACT_WAIT, SI_ACT_RELEASE };
+enum { SI_TIER_MAPPED_SOURCE = 0, SI_TIER_PINNED_HOST, SI_TIER_HBM, SI_TIER_CPU, SI_TIER_NVME };
+enum { SI_MODE_RESIDENT = 0, SI_MODE_MMAP, SI_MODE_LAYER_STREAM, SI_MODE_SUBLAYER_STREAM, SI_MODE_OVERLAP,
+       SI_MODE_HETEROGENEOUS };
+typedef struct si_trace si_trace;
+/* One action (PlannerAction, planner.rs:39-50); tensor_ids comma-separated.
+ * Strings handed out by si_trace_action_at are owned by the trace. */
+typedef struct si_trace_action {
+  uint32_t kind, tier;
+  const char* operation_id;
+  const char* tensor_ids;
+  uint64_t bytes, started_ns, ended_ns;
+  const char* queue;
+  const char* reason;
+} si_trace_action;
+typedef struct si_trace_summary_info {
+  uint32_t mode, observed;                 /* observed: peaks were sampled */
+  uint64_t actions;
+  uint64_t planned_peak_hbm_bytes;          /* from the recorded residency */
+  uint64_t observed_peak_hbm_bytes, observed_peak_rss_bytes;
+  uint64_t resident_hbm_tensors, resident_hbm_bytes;  /* at the end of the trace */
+} si_trace_summary_info;
+si_trace* si_trace_create(uint32_t mode);
+void si_trace_destroy(si_trace* t);
+/* PlannerTrace::record (planner.rs:96-155): rejects an action that names no
+ * tensor, ends before it starts, executes a non-resident tensor or evicts one
+ * that is not resident; prefetch/retain in HBM update the planned peak. */
+int si_trace_record(si_trace* t, const si_trace_action* action);
+int si_trace_count(const si_trace* t, uint64_t* n);
+int si_trace_action_at(const si_trace* t, uint64_t index, si_trace_action* out);
+int si_trace_summary(const si_trace* t, si_trace_summary_info* out);
+/* plan_sequential_layers (planner.rs:174-251): prefetch, execute, evict per
+ * layer; tensor ids and bytes are the layers' tensors in order. */
+int si_plan_sequential_layers(uint32_t layers, const char* const* operation_ids, const uint32_t* tensor_counts,
+                              const char* const* tensor_ids, const uint64_t* tensor_bytes, uint64_t budget_bytes,
+                              si_trace** out);
+/* The model's real trace (the scheduler the reference's planner anticipates,
+ * planner.rs:1-5): between begin and end, every ring copy (prefetch), layer
+ * and head execution and slot reuse (evict) is recorded with CUDA event
+ * timestamps on its stream; resident and already staged layers are retained.
+ * trace_end synchronises, replays the actions in time order through
+ * si_trace_record and checks the SI-003 invariants on the measured times: no
+ * execution starts before its prefetch has landed, and no layer is evicted
+ * (its slot overwritten) before its execution ends. Observed peaks are the
+ * context's device peak and the process RSS. */
+int si_model_trace_begin(si_model* m);
+int si_model_trace_end(si_model* m, si_trace** out);
+
 /* ---- multi-GPU row sharding over NCCL ----------------------------------- */
 #define SI_COMM_ID_BYTES 128
 int si_comm_unique_id(void* id_out /* SI_COMM_ID_BYTES */);

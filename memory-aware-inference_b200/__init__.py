@@ -62,6 +62,25 @@ def device_probe(device: int = 0) -> dict:
             "cc": (info.cc_major, info.cc_minor), "device_count": info.device_count}
 
 
+ACT_PREFETCH, ACT_EXECUTE, ACT_RETAIN, ACT_EVICT, ACT_WAIT, ACT_RELEASE = range(6)
+ACT_NAMES = ["prefetch", "execute", "retain", "evict", "wait", "release"]
+TIER_MAPPED_SOURCE, TIER_PINNED_HOST, TIER_HBM, TIER_CPU, TIER_NVME = range(5)
+MODE_RESIDENT, MODE_MMAP, MODE_LAYER_STREAM, MODE_SUBLAYER_STREAM, MODE_OVERLAP, MODE_HETEROGENEOUS = range(6)
+
+
+class SiTraceAction(C.Structure):
+    _fields_ = [("kind", C.c_uint32), ("tier", C.c_uint32), ("operation_id", C.c_char_p),
+                ("tensor_ids", C.c_char_p), ("bytes", C.c_uint64), ("started_ns", C.c_uint64),
+                ("ended_ns", C.c_uint64), ("queue", C.c_char_p), ("reason", C.c_char_p)]
+
+
+class SiTraceSummary(C.Structure):
+    _fields_ = [("mode", C.c_uint32), ("observed", C.c_uint32), ("actions", C.c_uint64),
+                ("planned_peak_hbm_bytes", C.c_uint64), ("observed_peak_hbm_bytes", C.c_uint64),
+                ("observed_peak_rss_bytes", C.c_uint64), ("resident_hbm_tensors", C.c_uint64),
+                ("resident_hbm_bytes", C.c_uint64)]
+
+
 class SiStats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("current_allocated_bytes", "peak_allocated_bytes",
                                           "peak_active_weight_bytes", "peak_kv_bytes", "peak_scratch_bytes",
@@ -181,6 +200,15 @@ def lib():
         "si_gguf_meta_array_len": ([vp, C.c_char_p, vp], i32),
         "si_gguf_read": ([vp, u64, u64, vp, u64], i32),
         "si_gguf_qwen35_config": ([vp, u32, vp], i32),
+        "si_trace_create": ([u32], vp),
+        "si_trace_destroy": ([vp], None),
+        "si_trace_record": ([vp, vp], i32),
+        "si_trace_count": ([vp, vp], i32),
+        "si_trace_action_at": ([vp, u64, vp], i32),
+        "si_trace_summary": ([vp, vp], i32),
+        "si_plan_sequential_layers": ([u32, vp, vp, vp, vp, u64, vp], i32),
+        "si_model_trace_begin": ([vp], i32),
+        "si_model_trace_end": ([vp, vp], i32),
         "si_comm_unique_id": ([vp], i32),
         "si_ctx_comm_init": ([vp, i32, i32, vp], i32),
         "si_ctx_comm_info": ([vp, vp, vp], i32),
@@ -629,6 +657,63 @@ class GgufFile:
         return c
 
 
+class Trace:
+    """A planner trace (PlannerTrace, planner.rs:62-170): actions validated as
+    they are recorded against the residency they imply."""
+
+    def __init__(self, mode: int = MODE_LAYER_STREAM, handle=None):
+        self.h = handle if handle is not None else lib().si_trace_create(mode)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().si_trace_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def record(self, kind, operation_id, tensor_ids, nbytes, started_ns=0, ended_ns=0, tier=TIER_HBM, queue="",
+               reason=""):
+        a = SiTraceAction(kind, tier, operation_id.encode(), ",".join(tensor_ids).encode(), nbytes, started_ns,
+                          ended_ns, queue.encode(), reason.encode())
+        _gck(lib().si_trace_record(self.h, C.byref(a)))
+
+    def actions(self) -> list:
+        n = C.c_uint64()
+        _gck(lib().si_trace_count(self.h, C.byref(n)))
+        out = []
+        for i in range(n.value):
+            a = SiTraceAction()
+            _gck(lib().si_trace_action_at(self.h, i, C.byref(a)))
+            out.append({"kind": ACT_NAMES[a.kind], "tier": a.tier, "operation_id": a.operation_id.decode(),
+                        "tensor_ids": a.tensor_ids.decode().split(",") if a.tensor_ids else [],
+                        "bytes": a.bytes, "started_ns": a.started_ns, "ended_ns": a.ended_ns,
+                        "queue": a.queue.decode(), "reason": a.reason.decode()})
+        return out
+
+    def summary(self) -> dict:
+        s = SiTraceSummary()
+        _gck(lib().si_trace_summary(self.h, C.byref(s)))
+        return {k: getattr(s, k) for k, _ in s._fields_}
+
+
+def plan_sequential_layers(layers, budget_bytes: int) -> Trace:
+    """plan_sequential_layers (planner.rs:174-251): layers = [(operation_id,
+    [(tensor_id, bytes), ...]), ...]."""
+    n = len(layers)
+    ops = (C.c_char_p * max(n, 1))(*[op.encode() for op, _ in layers])
+    counts = (C.c_uint32 * max(n, 1))(*[len(t) for _, t in layers])
+    flat = [t for _, ts in layers for t in ts]
+    ids = (C.c_char_p * max(len(flat), 1))(*[tid.encode() for tid, _ in flat])
+    nbytes = (C.c_uint64 * max(len(flat), 1))(*[b for _, b in flat])
+    h = C.c_void_p()
+    _gck(lib().si_plan_sequential_layers(n, ops, counts, ids, nbytes, budget_bytes, C.byref(h)))
+    return Trace(handle=h.value)
+
+
 class Model:
     """Synthetic Qwen3.6-shaped decoder (Qwen35Runtime, qwen35_runtime.rs:1519-2267)."""
 
@@ -704,6 +789,16 @@ class Model:
         logits = np.empty(self.config.vocab, np.float32) if want_logits else None
         self.ctx._ck(lib().si_model_decode_token(self.h, token_id, position, C.byref(nxt), _p(logits)))
         return nxt.value, logits
+
+    def trace_begin(self):
+        """Start recording the ring's prefetch / execute / evict actions."""
+        self.ctx._ck(lib().si_model_trace_begin(self.h))
+
+    def trace_end(self) -> Trace:
+        """The measured trace since trace_begin, validated (SI-003 invariants)."""
+        h = C.c_void_p()
+        self.ctx._ck(lib().si_model_trace_end(self.h, C.byref(h)))
+        return Trace(handle=h.value)
 
     def decode_tokens_many(self, tokens, positions, want_hidden: bool = True):
         """Qwen35Runtime::decode_tokens_many: hidden states (n x hidden) of a

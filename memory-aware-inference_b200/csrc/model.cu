@@ -7,13 +7,17 @@
 // decode_hidden 1776-1941, logits 2132-2192, decode_token 2229-2246, staging
 // 2283-2332; residency selection 1552-1733; planner budget check
 // (src/planner.rs:174-251); run_gguf_generation (src/runtime.rs:3560-3614).
+#include <unistd.h>
+
 #include <algorithm>
 #include <array>
 #include <atomic>
 #include <cmath>
 #include <functional>
+#include <map>
 #include <memory>
 #include <mutex>
+#include <cstdio>
 #include <cstring>
 #include <string>
 #include <thread>
@@ -23,6 +27,7 @@
 #include "common.cuh"
 #include "ctx.h"
 #include "gguf.h"
+#include "planner.h"
 #include "kernels.cuh"
 #include "qmatvec.cuh"
 #include "synth.h"
@@ -111,6 +116,20 @@ struct si_model {
   uint64_t flag_off = 0;
   std::vector<float> rope_host;
   bool accounted = false;  // device bytes recorded in the context telemetry
+  // measured planner trace (si_model_trace_begin / _end)
+  struct TraceRec {
+    uint32_t kind;
+    int layer;          // layer index; layers = the output head
+    int slot;           // ring slot, -1 for a resident layer
+    cudaEvent_t e0, e1; // null: at the start of the trace (retained before it)
+    uint64_t bytes;
+  };
+  bool tracing = false;
+  std::vector<cudaEvent_t> tr_pool;
+  size_t tr_used = 0;
+  std::vector<TraceRec> tr_recs;
+  cudaEvent_t tr_base = nullptr;
+  int slot_layer[4] = {-1, -1, -1, -1};  // layer staged in each ring slot
 };
 
 namespace {
@@ -470,6 +489,8 @@ void free_model(si_model* m) {
   if (m->state_block) cudaFree(m->state_block);
   if (m->p2p) comm_p2p_unmap(m->ctx, m->peer_block);
   if (m->scratch_block) cudaFree(m->scratch_block);
+  for (cudaEvent_t e : m->tr_pool) cudaEventDestroy(e);
+  if (m->tr_base) cudaEventDestroy(m->tr_base);
   if (m->accounted) {
     note_alloc(m->ctx, -int64_t(m->plan.resident_weight_bytes + m->plan.ring_bytes + m->plan.state_bytes +
                                 m->plan.scratch_bytes));
@@ -935,13 +956,57 @@ namespace {
 // slot j % depth. Copies run on the context's copy stream: occurrence j+depth
 // is issued right after occurrence j's compute has been enqueued, gated by
 // that compute's completion event.
+// A timing event from the trace pool (recorded on a stream by the caller).
+cudaEvent_t trace_event(si_model* m) {
+  if (m->tr_used == m->tr_pool.size()) {
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    m->tr_pool.push_back(e);
+  }
+  return m->tr_pool[m->tr_used++];
+}
+
 void issue_copy(si_model* m, uint64_t occ) {
   const uint32_t s = uint32_t(occ % m->depth);
   const uint32_t l = m->streamed[occ % m->streamed.size()];
   cudaStreamWaitEvent(m->ctx->copy_stream, m->compute_done[s], 0);
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (m->tracing) {
+    e0 = trace_event(m);
+    e1 = trace_event(m);
+    cudaEventRecord(e0, m->ctx->copy_stream);
+    // the copy overwrites the slot: its previous occupant is evicted here
+    if (m->slot_layer[s] >= 0)
+      m->tr_recs.push_back({SI_ACT_EVICT, m->slot_layer[s], int(s), e0, e0, m->layout[m->slot_layer[s]].bytes});
+  }
   cudaMemcpyAsync(m->slot[s], m->host[l], m->layout[l].bytes, cudaMemcpyHostToDevice, m->ctx->copy_stream);
   cudaEventRecord(m->copy_done[s], m->ctx->copy_stream);
+  if (m->tracing) {
+    cudaEventRecord(e1, m->ctx->copy_stream);
+    m->tr_recs.push_back({SI_ACT_PREFETCH, int(l), int(s), e0, e1, m->layout[l].bytes});
+  }
+  m->slot_layer[s] = int(l);
 }
+
+// Execution of layer `l` (or the head, l == layers) bracketed by events on
+// the compute stream when tracing.
+struct TraceScope {
+  si_model* m;
+  int layer, slot;
+  cudaEvent_t e0 = nullptr;
+  TraceScope(si_model* mm, int l, int s) : m(mm), layer(l), slot(s) {
+    if (m->tracing) {
+      e0 = trace_event(m);
+      cudaEventRecord(e0, m->ctx->stream);
+    }
+  }
+  ~TraceScope() {
+    if (!e0) return;
+    cudaEvent_t e1 = trace_event(m);
+    cudaEventRecord(e1, m->ctx->stream);
+    m->tr_recs.push_back({SI_ACT_EXECUTE, layer, slot, e0, e1, m->layout[layer].bytes});
+  }
+};
 
 void ring_prime(si_model* m) {
   while (m->occ_issued < m->occ_next + m->depth) issue_copy(m, m->occ_issued++);
@@ -1187,7 +1252,12 @@ int run_layers(si_model* m, F body) {
       cudaStreamWaitEvent(m->ctx->stream, m->copy_done[s], 0);
       base = m->slot[s];
     }
-    if (int rc = body(l, base)) return rc;
+    int rc;
+    {
+      TraceScope ts(m, int(l), m->dev_layer[l] ? -1 : int(s));
+      rc = body(l, base);
+    }
+    if (rc) return rc;
     if (!m->dev_layer[l]) {
       cudaEventRecord(m->compute_done[s], m->ctx->stream);
       m->occ_next++;
@@ -1215,6 +1285,7 @@ int embed_dev(si_model* m) {
 // logits slice + global argmax into d_token (and optionally full logits).
 int head_dev(si_model* m, bool gather_logits) {
   const si_model_config& c = m->c;
+  TraceScope ts(m, int(c.layers), -1);
   const uint8_t* base = m->dev_layer[c.layers];
   QmvParams p = qmv_base(m, type_of(m, c.layers, SI_T_OUTPUT), c.hidden);
   p.seg[0] = {tensor_ptr(m, base, c.layers, SI_T_OUTPUT), m->logits, nullptr, m->V_l, 0};
@@ -1491,6 +1562,7 @@ int decode_many_dev(si_model* m, const uint32_t* tokens, const uint64_t* positio
 // Output norm, head and per-candidate argmax over b_hid.
 int logits_many_dev(si_model* m, uint32_t K) {
   const si_model_config& c = m->c;
+  TraceScope ts(m, int(c.layers), -1);
   const uint8_t* base = m->dev_layer[c.layers];
   launch_rms_norm_heads(m->b_hid, reinterpret_cast<const float*>(tensor_ptr(m, base, c.layers, SI_T_OUTPUT_NORM)),
                         K, c.hidden, c.rms_eps, m->b_xn, m->ctx->stream);
@@ -1552,4 +1624,152 @@ extern "C" int si_model_verify_many(si_model* m, const uint32_t* tokens, const u
   if (int rc = decode_many_dev(m, tokens, positions, n)) return rc;
   if (int rc = logits_many_dev(m, n)) return rc;
   return read_many(m, n, logits, ids, "verify_many");
+}
+
+// ---- measured planner trace -------------------------------------------------
+namespace {
+
+// A resident layer is "blk.N"; a copy staged in a ring slot is "blk.N@ring-S"
+// (one layer can sit in two slots at once when fewer layers stream than the
+// ring has slots).
+std::string layer_tensor(const si_model* m, int l, int slot) {
+  const std::string base = l == int(m->c.layers) ? std::string("output") : "blk." + std::to_string(l);
+  return slot >= 0 ? base + "@ring-" + std::to_string(slot) : base;
+}
+
+std::string layer_op(const si_model* m, int l) {
+  return l == int(m->c.layers) ? std::string("output") : "layer-" + std::to_string(l);
+}
+
+uint64_t process_rss() {
+  FILE* f = std::fopen("/proc/self/statm", "r");
+  unsigned long long size = 0, res = 0;
+  if (f) {
+    if (std::fscanf(f, "%llu %llu", &size, &res) != 2) res = 0;
+    std::fclose(f);
+  }
+  return uint64_t(res) * uint64_t(sysconf(_SC_PAGESIZE));
+}
+
+}  // namespace
+
+extern "C" int si_model_trace_begin(si_model* m) {
+  if (!m) return SI_E_INVALID;
+  if (m->tracing) return fail(m->ctx, SI_E_STATE, "a trace is already being recorded");
+  cudaSetDevice(m->ctx->device);
+  if (!m->tr_base && cudaEventCreate(&m->tr_base) != cudaSuccess)
+    return fail(m->ctx, SI_E_CUDA, "trace event creation failed");
+  m->tr_recs.clear();
+  m->tr_used = 0;
+  // time zero on the compute stream; the copy stream starts after it
+  cudaEventRecord(m->tr_base, m->ctx->stream);
+  cudaStreamWaitEvent(m->ctx->copy_stream, m->tr_base, 0);
+  // what is in HBM when the trace starts: the resident layers and head, and
+  // whatever the ring has already staged
+  for (uint32_t l = 0; l <= m->c.layers; ++l)
+    if (m->dev_layer[l]) m->tr_recs.push_back({SI_ACT_RETAIN, int(l), -1, nullptr, nullptr, m->layout[l].bytes});
+  for (uint32_t s = 0; s < m->depth; ++s)
+    if (!m->streamed.empty() && m->slot_layer[s] >= 0)
+      m->tr_recs.push_back({SI_ACT_RETAIN, m->slot_layer[s], int(s), nullptr, nullptr,
+                            m->layout[m->slot_layer[s]].bytes});
+  m->tracing = true;
+  return SI_OK;
+}
+
+extern "C" int si_model_trace_end(si_model* m, si_trace** out) {
+  if (!m || !out) return SI_E_INVALID;
+  *out = nullptr;
+  if (!m->tracing) return fail(m->ctx, SI_E_STATE, "no trace is being recorded");
+  m->tracing = false;
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->copy_stream);
+  if (int rc = sync_and_check(m->ctx, "trace")) return rc;
+  auto ns_of = [&](cudaEvent_t e) -> uint64_t {
+    if (!e) return 0;
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, m->tr_base, e) != cudaSuccess || ms < 0.f) return 0;
+    return uint64_t(double(ms) * 1e6);
+  };
+  struct Item {
+    si::TraceAction a;
+    size_t rec;
+    int order;
+  };
+  std::vector<Item> items;
+  items.reserve(m->tr_recs.size());
+  for (size_t i = 0; i < m->tr_recs.size(); ++i) {
+    const auto& r = m->tr_recs[i];
+    si::TraceAction a;
+    a.kind = r.kind;
+    a.tier = SI_TIER_HBM;
+    a.op = layer_op(m, r.layer);
+    a.tensors = {layer_tensor(m, r.layer, r.slot)};
+    a.bytes = r.bytes;
+    a.started_ns = ns_of(r.e0);
+    a.ended_ns = std::max(a.started_ns, ns_of(r.e1));
+    const std::string where = r.slot >= 0 ? "ring slot " + std::to_string(r.slot) : std::string("resident");
+    switch (r.kind) {
+      case SI_ACT_RETAIN:
+        a.queue = "transfer";
+        a.reason = r.slot >= 0 ? "staged in " + where + " before the trace began" : "resident for the whole run";
+        break;
+      case SI_ACT_PREFETCH:
+        a.queue = "transfer";
+        a.reason = "stage streamed layer into " + where + " ahead of its execution";
+        break;
+      case SI_ACT_EVICT:
+        a.queue = "transfer";
+        a.reason = "overwrite " + where + " with the next streamed layer";
+        break;
+      default:
+        a.queue = "compute";
+        a.reason = "execute with its weights " + (r.slot >= 0 ? "in " + where : std::string("resident"));
+    }
+    // at equal start times: retained, evicted, prefetched, then executed
+    const int order = r.kind == SI_ACT_RETAIN ? 0 : r.kind == SI_ACT_EVICT ? 1 : r.kind == SI_ACT_PREFETCH ? 2 : 3;
+    items.push_back({std::move(a), i, order});
+  }
+  std::stable_sort(items.begin(), items.end(), [](const Item& x, const Item& y) {
+    return x.a.started_ns != y.a.started_ns ? x.a.started_ns < y.a.started_ns : x.order < y.order;
+  });
+  auto* t = new si_trace();
+  t->core.mode = m->streamed.empty() ? SI_MODE_RESIDENT : SI_MODE_OVERLAP;
+  std::string err;
+  // SI-003 invariants on the measured device times (timer resolution ~0.5 us):
+  // an execution starts after its prefetch landed; an eviction starts after
+  // the evicted layer's last execution ended
+  constexpr float kTol = 1e-3f;  // ms
+  std::map<std::pair<int, int>, cudaEvent_t> landed, done;  // (layer, slot)
+  for (const Item& it : items) {
+    const auto& r = m->tr_recs[it.rec];
+    float ms = 0.f;
+    const std::pair<int, int> key{r.layer, r.slot};
+    if (r.kind == SI_ACT_PREFETCH) landed[key] = r.e1;
+    if (r.kind == SI_ACT_EXECUTE) {
+      if (r.slot >= 0 && landed.count(key) && landed[key] &&
+          cudaEventElapsedTime(&ms, landed[key], r.e0) == cudaSuccess && ms < -kTol)
+        err = "SI-003: " + layer_op(m, r.layer) + " started " + std::to_string(-ms * 1e3) +
+              " us before its prefetch landed";
+      done[key] = r.e1;
+    }
+    if (r.kind == SI_ACT_EVICT && done.count(key) &&
+        cudaEventElapsedTime(&ms, done[key], r.e0) == cudaSuccess && ms < -kTol)
+      err = "SI-003: " + layer_op(m, r.layer) + " was evicted " + std::to_string(-ms * 1e3) +
+            " us before its execution ended";
+    if (!err.empty()) break;
+    if (int rc = t->core.record(it.a, &err)) {
+      delete t;
+      return fail(m->ctx, rc, err);
+    }
+  }
+  if (!err.empty()) {
+    delete t;
+    return fail(m->ctx, SI_E_STATE, err);
+  }
+  t->core.observed = true;
+  t->core.observed_peak_hbm = m->ctx->peak_allocated.load();
+  t->core.observed_peak_rss = process_rss();
+  m->tr_recs.clear();
+  *out = t;
+  return SI_OK;
 }
