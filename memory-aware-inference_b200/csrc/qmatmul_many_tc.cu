@@ -1,4 +1,4 @@
-// Batched Q4_K / Q6_K matvec on the tensor cores: Y[k] = W X[k] for k < K <= 8 with
+// Batched Q4_K / Q5_K / Q6_K matvec on the tensor cores: Y[k] = W X[k] for k < K <= 8 with
 // one traversal of W (the verifier's weight pass, src/metal.rs:1055-1127,
 // 4067-4230; qwen35_runtime.rs:879-1289), exact integer sub-block sums.
 //
@@ -29,6 +29,9 @@
 // running sums. The epilogue adds a group's phases in shared memory in a
 // fixed order. Matrices wider than a panel (33 blocks) run as column panels
 // writing partial sums that a small kernel adds in panel order.
+//
+// Q5_K: the Q4_K path with the 5-bit quants (nibble | high bit << 4) built in
+// registers instead of the masked nibbles, and the block scale 2^(e-21).
 //
 // Q6_K: the int8 scales cover 16 elements, so the digits are laid out per
 // 16-element group and each group and plane is one m16n8k16 MMA (lane c holds
@@ -139,7 +142,8 @@ struct PrepArgs {
   const float* x;
   uint64_t ldx;
   uint32_t K, nblk;
-  uint32_t q6;       // 1: Q6_K layouts (16-element groups), 0: Q4_K
+  uint32_t q6;       // 1: Q6_K layouts (16-element groups), 0: Q4_K / Q5_K
+  int esc_bias;      // block scale 2^(e + esc_bias): -25 for Q4_K (the 16 q trick), -21 otherwise
   uint8_t* dig;      // [nblk][kQtDigBlock]
   float* esc;        // [nblk][8]
   uint32_t* xs16;    // [nblk][kQtXsBlock / 4]
@@ -198,7 +202,7 @@ __global__ void __launch_bounds__(32) qmm_prep_kernel(const PrepArgs a) {
       *reinterpret_cast<uint2*>(blk + (j * 3 + p) * 256 + k * 32 + 8 * c) = make_uint2(pl[p][0], pl[p][1]);
     // 2^(e-21) per digit unit and 1/16 for the high nibbles being multiplied
     // as 16 q (the low-nibble scales are multiplied by 16)
-    if (lane == 0) a.esc[uint64_t(b) * 8 + k] = live ? __uint_as_float(uint32_t(e - 25 + 127) << 23) : 0.f;
+    if (lane == 0) a.esc[uint64_t(b) * 8 + k] = live ? __uint_as_float(uint32_t(e + a.esc_bias + 127) << 23) : 0.f;
     // sub-block sums j = 2q, 2q+1 as f16 hi + lo pairs: the min-term MMA's B
     // fragment of lane (g = k, c = q)
     const float s_next = __shfl_down_sync(0xffffffffu, s, 4);  // sum of sub-block j + 1
@@ -404,31 +408,40 @@ __global__ void __launch_bounds__(kQtThreads, 1) qmm_tc_kernel(const QtArgs a) {
         }
       }
     }
-    if (active && TYPE == SI_GGML_TYPE_Q4_K) {
+    if (active && (TYPE == SI_GGML_TYPE_Q4_K || TYPE == SI_GGML_TYPE_Q5_K)) {
+      // Q5_K: the Q4_K layout plus a high-bit plane (qh, bytes 16..47) before
+      // the nibbles (bytes 48..175)
+      constexpr bool q5 = TYPE == SI_GGML_TYPE_Q5_K;
+      constexpr uint32_t BB = q5 ? 176 : 144, QS = q5 ? 48 : 16;
       const uint32_t grp = g0 + gl;
       const uint32_t r0 = min(grp * 16 + g, a.rows - 1), r8 = min(grp * 16 + g + 8, a.rows - 1);
-      const uint8_t* w0 = a.w + (uint64_t(r0) * a.nblk + b0) * 144;
-      const uint8_t* w8 = a.w + (uint64_t(r8) * a.nblk + b0) * 144;
+      const uint8_t* w0 = a.w + (uint64_t(r0) * a.nblk + b0) * BB;
+      const uint8_t* w8 = a.w + (uint64_t(r8) * a.nblk + b0) * BB;
       // lanes 0..15 prefetch row grp*16+lane of the blocks ahead into L2
-      const uint8_t* wp = a.w + (uint64_t(min(grp * 16 + (lane & 15), a.rows - 1)) * a.nblk + b0) * 144;
+      const uint8_t* wp = a.w + (uint64_t(min(grp * 16 + (lane & 15), a.rows - 1)) * a.nblk + b0) * BB;
       if (lane < 16)
         for (uint32_t d = 1; d <= kQtPrefetch + 1; ++d)
-          if (phase + d * split < nb) prefetch_l2(wp + (phase + d * split) * 144, 144);
+          if (phase + d * split < nb) prefetch_l2(wp + (phase + d * split) * BB, BB);
       uint4 h0, h8;
-      uint2 q0[4], q8[4];
+      uint2 q0[4], q8[4], qh0 = make_uint2(0u, 0u), qh8 = make_uint2(0u, 0u);
       auto load = [&](uint32_t i) {
-        h0 = ldw_u4(w0 + i * 144, wpol);
-        h8 = ldw_u4(w8 + i * 144, wpol);
+        h0 = ldw_u4(w0 + i * BB, wpol);
+        h8 = ldw_u4(w8 + i * BB, wpol);
+        if (q5) {
+          qh0 = ldw_u2(w0 + i * BB + 16 + 8 * c, wpol);
+          qh8 = ldw_u2(w8 + i * BB + 16 + 8 * c, wpol);
+        }
 #pragma unroll
         for (int gr = 0; gr < 4; ++gr) {
-          q0[gr] = ldw_u2(w0 + i * 144 + 16 + 32 * gr + 8 * c, wpol);
-          q8[gr] = ldw_u2(w8 + i * 144 + 16 + 32 * gr + 8 * c, wpol);
+          q0[gr] = ldw_u2(w0 + i * BB + QS + 32 * gr + 8 * c, wpol);
+          q8[gr] = ldw_u2(w8 + i * BB + QS + 32 * gr + 8 * c, wpol);
         }
       };
       uint32_t i = phase;
       if (i < nb) load(i);
       for (; i < nb; i += split) {
         const uint4 ch0 = h0, ch8 = h8;
+        const uint2 cqh0 = qh0, cqh8 = qh8;
         uint2 cq0[4], cq8[4];
 #pragma unroll
         for (int gr = 0; gr < 4; ++gr) {
@@ -437,7 +450,7 @@ __global__ void __launch_bounds__(kQtThreads, 1) qmm_tc_kernel(const QtArgs a) {
         }
         if (i + split < nb) load(i + split);  // one block ahead in registers
         if (lane < 16 && i + (kQtPrefetch + 2) * split < nb)
-          prefetch_l2(wp + (i + (kQtPrefetch + 2) * split) * 144, 144);
+          prefetch_l2(wp + (i + (kQtPrefetch + 2) * split) * BB, BB);
         // the decision to stop is the warp's (its lanes then run MMAs together)
         if (!table_ready) {
           if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bar[0], 0))) {
@@ -471,10 +484,27 @@ __global__ void __launch_bounds__(kQtThreads, 1) qmm_tc_kernel(const QtArgs a) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const uint32_t j = 2 * gr + h;
-            const uint32_t mask = h ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
-            const uint32_t A[4] = {cq0[gr].x & mask, cq8[gr].x & mask, cq0[gr].y & mask, cq8[gr].y & mask};
-            const int m0 = int(byte_of(j < 4 ? sc_lo[0] : sc_hi[0], j & 3)) << (h ? 0 : 4);
-            const int m8 = int(byte_of(j < 4 ? sc_lo[1] : sc_hi[1], j & 3)) << (h ? 0 : 4);
+            uint32_t A[4];
+            int m0 = int(byte_of(j < 4 ? sc_lo[0] : sc_hi[0], j & 3));
+            int m8 = int(byte_of(j < 4 ? sc_lo[1] : sc_hi[1], j & 3));
+            if (q5) {
+              // 5-bit quants 0..31: the nibble plus bit j of the high-bit bytes
+              auto q5w = [&](uint32_t w, uint32_t hb) {
+                return (h ? ((w >> 4) & 0x0F0F0F0Fu) : (w & 0x0F0F0F0Fu)) | (((hb >> j) & 0x01010101u) << 4);
+              };
+              A[0] = q5w(cq0[gr].x, cqh0.x);
+              A[1] = q5w(cq8[gr].x, cqh8.x);
+              A[2] = q5w(cq0[gr].y, cqh0.y);
+              A[3] = q5w(cq8[gr].y, cqh8.y);
+            } else {
+              const uint32_t mask = h ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+              A[0] = cq0[gr].x & mask;
+              A[1] = cq8[gr].x & mask;
+              A[2] = cq0[gr].y & mask;
+              A[3] = cq8[gr].y & mask;
+              m0 <<= h ? 0 : 4;
+              m8 <<= h ? 0 : 4;
+            }
 #pragma unroll
             for (int p = 0; p < 3; ++p) {
               const uint2 bb = *reinterpret_cast<const uint2*>(xb + (j * 3 + p) * 256);
@@ -506,9 +536,10 @@ __global__ void __launch_bounds__(kQtThreads, 1) qmm_tc_kernel(const QtArgs a) {
         for (int v = 0; v < 4; ++v) {
           const float f = fmaf(65536.f, float(acc[2][v]), fmaf(256.f, float(acc[1][v]), float(acc[0][v])));
           const float d = v < 2 ? dd0.x : dd8.x, dm = v < 2 ? dd0.y : dd8.y;
-          // esc = 2^(e-25) (digit unit / 16); the sums are in units of 2^e = esc 2^25
+          // esc = 2^(e-25) for Q4_K (digit unit / 16), 2^(e-21) for Q5_K; the
+          // sums are in units of 2^e
           const float e1 = v & 1 ? es.y : es.x;
-          yk[v] += d * e1 * f - dm * (e1 * 33554432.f) * mt[v];
+          yk[v] += d * e1 * f - dm * (e1 * (q5 ? 2097152.f : 33554432.f)) * mt[v];
         }
       }
     }
@@ -593,9 +624,10 @@ uint64_t qmm_tc_scratch_bytes(uint32_t rows, uint32_t cols, uint32_t batch, int 
 }
 
 bool qmm_tc_eligible(const QmmParams& p) {
-  const bool q4 = p.type == SI_GGML_TYPE_Q4_K, q6 = p.type == SI_GGML_TYPE_Q6_K;
-  return (q4 || q6) && p.batch >= 2 && p.batch <= kQmmMaxBatch && p.rows >= 16 &&
-         !(reinterpret_cast<uintptr_t>(p.w) & (q4 ? 15u : 1u)) && p.scratch &&
+  const bool q6 = p.type == SI_GGML_TYPE_Q6_K;
+  const bool k4 = p.type == SI_GGML_TYPE_Q4_K || p.type == SI_GGML_TYPE_Q5_K;  // 16-byte loads
+  return (k4 || q6) && p.batch >= 2 && p.batch <= kQmmMaxBatch && p.rows >= 16 &&
+         !(reinterpret_cast<uintptr_t>(p.w) & (k4 ? 15u : 1u)) && p.scratch &&
          !(reinterpret_cast<uintptr_t>(p.scratch) & 255);
 }
 
@@ -609,6 +641,7 @@ int launch_qmm_tc(const QmmParams& p, cudaStream_t s, int sm_count, bool pdl, st
   pa.K = p.batch;
   pa.nblk = p.cols / 256;
   pa.q6 = p.type == SI_GGML_TYPE_Q6_K;
+  pa.esc_bias = p.type == SI_GGML_TYPE_Q4_K ? -25 : -21;
   pa.dig = sc;
   pa.esc = reinterpret_cast<float*>(sc + align256u(g.dig_bytes));
   pa.xs16 = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(pa.esc) + align256u(g.esc_bytes));
@@ -627,7 +660,7 @@ int launch_qmm_tc(const QmmParams& p, cudaStream_t s, int sm_count, bool pdl, st
 
   QtArgs a = {};
   a.w = p.w;
-  a.w_end = p.w + uint64_t(p.rows) * pa.nblk * (pa.q6 ? 210 : 144);
+  a.w_end = p.w + uint64_t(p.rows) * pa.nblk * block_bytes_of(p.type);
   a.rows = p.rows;
   a.nblk = pa.nblk;
   a.K = p.batch;
@@ -644,12 +677,15 @@ int launch_qmm_tc(const QmmParams& p, cudaStream_t s, int sm_count, bool pdl, st
   a.part = part;
   a.red_off = g.red_off;
   a.err = p.err;
-  auto kern = pa.q6 ? qmm_tc_kernel<SI_GGML_TYPE_Q6_K> : qmm_tc_kernel<SI_GGML_TYPE_Q4_K>;
+  const int ti = p.type == SI_GGML_TYPE_Q4_K ? 0 : p.type == SI_GGML_TYPE_Q5_K ? 1 : 2;
+  auto kern = ti == 0 ? qmm_tc_kernel<SI_GGML_TYPE_Q4_K>
+            : ti == 1 ? qmm_tc_kernel<SI_GGML_TYPE_Q5_K>
+                      : qmm_tc_kernel<SI_GGML_TYPE_Q6_K>;
   if (e == cudaSuccess) {
-    static bool smem_set[2] = {false, false};  // the first call raises each kernel's shared memory limit
-    if (!smem_set[pa.q6]) {
+    static bool smem_set[3] = {false, false, false};  // the first call raises each kernel's shared memory limit
+    if (!smem_set[ti]) {
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kQtSmemMax));
-      smem_set[pa.q6] = e == cudaSuccess;
+      smem_set[ti] = e == cudaSuccess;
     }
   }
   if (e == cudaSuccess) {
