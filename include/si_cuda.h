@@ -151,7 +151,9 @@ int si_gguf_quant_matmul_many_bytes(si_ctx* ctx, uint32_t ggml_type, const void*
                                     float* outputs);
 int si_gguf_quant_matmul_many_weight(si_ctx* ctx, const si_weight* weight, uint64_t rows, uint64_t cols,
                                      uint64_t batch, const float* inputs, float* outputs);
-/* Device-pointer form on `stream` (NULL: the context's stream). */
+/* Device-pointer form on `stream` (NULL: the context's stream). Its
+ * tensor-core scratch (digits, scales, panel sums) is the context's: calls on
+ * one context must not overlap on the GPU. */
 int si_qmatmul_many_dev(si_ctx* ctx, uint32_t ggml_type, const void* weights_dev, uint64_t rows, uint64_t cols,
                         uint64_t batch, const float* x_dev, float* y_dev, void* stream);
 /* f32_matvec (metal.rs:2983). */
