@@ -345,6 +345,22 @@ int si_gguf_meta_array_len(const si_gguf* g, const char* key, uint64_t* out);
 /* Copy bytes [offset, offset+bytes) of tensor `index`'s payload
  * (stage_tensor_payload, model.rs:867-886). */
 int si_gguf_read(const si_gguf* g, uint64_t index, uint64_t offset, void* dst, uint64_t bytes);
+/* qwen35_layer_kind (model.rs:748-783): ssm_a present = Gated DeltaNet,
+ * attn_q.weight present = full attention; exactly one, and agreeing with the
+ * full-attention interval. */
+#define SI_LAYER_GATED_DELTA_NET 0u
+#define SI_LAYER_FULL_ATTENTION 1u
+int si_gguf_qwen35_layer_kind(const si_gguf* g, uint32_t layer, uint32_t* kind);
+/* GgufTensorInfo::element_count / expected_payload_bytes (model.rs:512-573):
+ * *known = 0 for types other than F32, F16, BF16 and the K-quants. */
+int si_gguf_tensor_payload(const si_gguf* g, uint64_t index, uint64_t* elements, uint64_t* expected_bytes,
+                           uint32_t* known);
+/* detect_model_format (model.rs:42-78) without loading any payload: a
+ * directory whose manifest.json says format "safetensors" and dtype
+ * "bfloat16", or a file starting with the GGUF magic. */
+#define SI_FORMAT_SAFETENSORS 1u
+#define SI_FORMAT_GGUF 2u
+int si_detect_model_format(const char* path, uint32_t* format);
 /* GgufQwen35Config::from_metadata (model.rs:350-417) plus the rotary width
  * (qwen35_runtime.rs:811-813) into a decode config; the ggml types of
  * blk.0.ffn_gate / blk.0.ffn_down / output fill mlp/down/head_type.

@@ -200,6 +200,9 @@ def lib():
         "si_gguf_meta_array_len": ([vp, C.c_char_p, vp], i32),
         "si_gguf_read": ([vp, u64, u64, vp, u64], i32),
         "si_gguf_qwen35_config": ([vp, u32, vp], i32),
+        "si_gguf_qwen35_layer_kind": ([vp, u32, vp], i32),
+        "si_gguf_tensor_payload": ([vp, u64, vp, vp, vp], i32),
+        "si_detect_model_format": ([C.c_char_p, vp], i32),
         "si_trace_create": ([u32], vp),
         "si_trace_destroy": ([vp], None),
         "si_trace_record": ([vp, vp], i32),
@@ -577,6 +580,13 @@ def _gck(rc):
         raise SiError(rc, lib().si_global_last_error().decode())
 
 
+def detect_model_format(path) -> str:
+    """detect_model_format (model.rs:42-78): "gguf" or "safetensors"."""
+    f = C.c_uint32()
+    _gck(lib().si_detect_model_format(os.fsencode(path), C.byref(f)))
+    return "gguf" if f.value == 2 else "safetensors"
+
+
 class GgufFile:
     """An open GGUF v2/v3 file: metadata and tensor index parsed on the host,
     payloads read on demand (GgufModelStore, model.rs:583-1030). No device."""
@@ -650,6 +660,21 @@ class GgufFile:
         out = np.empty(nbytes, np.uint8)
         _gck(lib().si_gguf_read(self.h, idx, offset, _p(out), nbytes))
         return out
+
+    def layer_kind(self, layer: int) -> str:
+        """qwen35_layer_kind (model.rs:748-783): "gated_delta_net" or "full_attention"."""
+        k = C.c_uint32()
+        _gck(lib().si_gguf_qwen35_layer_kind(self.h, layer, C.byref(k)))
+        return "full_attention" if k.value == 1 else "gated_delta_net"
+
+    def layer_kinds(self) -> list:
+        return [self.layer_kind(l) for l in range(self.meta_u64("qwen35.block_count"))]
+
+    def tensor_payload(self, index: int):
+        """(element_count, expected_payload_bytes or None) (model.rs:512-573)."""
+        n, b, k = C.c_uint64(), C.c_uint64(), C.c_uint32()
+        _gck(lib().si_gguf_tensor_payload(self.h, index, C.byref(n), C.byref(b), C.byref(k)))
+        return n.value, (b.value if k.value else None)
 
     def qwen35_config(self, kv_capacity: int = 0) -> SiModelConfig:
         c = SiModelConfig()

@@ -8,6 +8,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <cctype>
 #include <cerrno>
 #include <cmath>
 #include <cstdio>
@@ -359,25 +360,210 @@ int si_gguf_read(const si_gguf* g, uint64_t index, uint64_t offset, void* dst, u
   return rc ? si::fail(nullptr, rc, err) : SI_OK;
 }
 
-int si_gguf_qwen35_config(const si_gguf* g, uint32_t kv_capacity, si_model_config* c) {
-  if (!g || !c) return si::fail(nullptr, SI_E_INVALID, "invalid GGUF config arguments");
+}  // extern "C"
+
+namespace {
+
+// A strict reader of one JSON document whose top level is an object: the
+// string-valued top-level fields are returned, every other value is checked
+// and skipped (the manifest test of detect_model_format, model.rs:46-62).
+struct JsonReader {
+  const std::string& s;
+  size_t i = 0;
+  std::string err;
+  void ws() {
+    while (i < s.size() && (s[i] == ' ' || s[i] == '\n' || s[i] == '\r' || s[i] == '\t')) ++i;
+  }
+  bool fail_at(const char* what) {
+    if (err.empty()) err = std::string("invalid model manifest JSON: ") + what + " at byte " + std::to_string(i);
+    return false;
+  }
+  bool str(std::string* out) {
+    if (i >= s.size() || s[i] != '"') return fail_at("expected a string");
+    ++i;
+    while (i < s.size() && s[i] != '"') {
+      char ch = s[i++];
+      if (static_cast<unsigned char>(ch) < 0x20) return fail_at("control character in a string");
+      if (ch == '\\') {
+        if (i >= s.size()) return fail_at("unterminated escape");
+        const char e = s[i++];
+        switch (e) {
+          case '"': ch = '"'; break;
+          case '\\': ch = '\\'; break;
+          case '/': ch = '/'; break;
+          case 'b': ch = '\b'; break;
+          case 'f': ch = '\f'; break;
+          case 'n': ch = '\n'; break;
+          case 'r': ch = '\r'; break;
+          case 't': ch = '\t'; break;
+          case 'u': {
+            if (i + 4 > s.size()) return fail_at("short unicode escape");
+            for (int k = 0; k < 4; ++k)
+              if (!std::isxdigit(static_cast<unsigned char>(s[i + k]))) return fail_at("bad unicode escape");
+            const unsigned cp = unsigned(std::stoul(s.substr(i, 4), nullptr, 16));
+            i += 4;
+            if (out) {  // the fields compared here are ASCII; other code points are kept as UTF-8
+              if (cp < 0x80) {
+                out->push_back(char(cp));
+              } else if (cp < 0x800) {
+                out->push_back(char(0xC0 | (cp >> 6)));
+                out->push_back(char(0x80 | (cp & 63)));
+              } else {
+                out->push_back(char(0xE0 | (cp >> 12)));
+                out->push_back(char(0x80 | ((cp >> 6) & 63)));
+                out->push_back(char(0x80 | (cp & 63)));
+              }
+            }
+            continue;
+          }
+          default:
+            return fail_at("bad escape");
+        }
+      }
+      if (out) out->push_back(ch);
+    }
+    if (i >= s.size()) return fail_at("unterminated string");
+    ++i;
+    return true;
+  }
+  bool value(int depth, std::string* as_string, bool* is_string) {
+    if (depth > 64) return fail_at("nesting too deep");
+    ws();
+    if (i >= s.size()) return fail_at("expected a value");
+    const char ch = s[i];
+    if (is_string) *is_string = ch == '"';
+    if (ch == '"') return str(as_string);
+    if (ch == '{' || ch == '[') {
+      const char close = ch == '{' ? '}' : ']';
+      ++i;
+      ws();
+      if (i < s.size() && s[i] == close) {
+        ++i;
+        return true;
+      }
+      for (;;) {
+        ws();
+        if (ch == '{') {
+          if (!str(nullptr)) return false;
+          ws();
+          if (i >= s.size() || s[i] != ':') return fail_at("expected ':'");
+          ++i;
+        }
+        if (!value(depth + 1, nullptr, nullptr)) return false;
+        ws();
+        if (i < s.size() && s[i] == ',') {
+          ++i;
+          continue;
+        }
+        if (i < s.size() && s[i] == close) {
+          ++i;
+          return true;
+        }
+        return fail_at("expected ',' or a closing bracket");
+      }
+    }
+    for (const char* lit : {"true", "false", "null"})
+      if (s.compare(i, std::strlen(lit), lit) == 0) {
+        i += std::strlen(lit);
+        return true;
+      }
+    // number: -?(0|[1-9][0-9]*)(.[0-9]+)?([eE][+-]?[0-9]+)?
+    size_t j = i;
+    if (j < s.size() && s[j] == '-') ++j;
+    if (j >= s.size() || !std::isdigit(static_cast<unsigned char>(s[j]))) return fail_at("expected a value");
+    if (s[j] == '0') ++j;
+    else while (j < s.size() && std::isdigit(static_cast<unsigned char>(s[j]))) ++j;
+    if (j < s.size() && s[j] == '.') {
+      ++j;
+      if (j >= s.size() || !std::isdigit(static_cast<unsigned char>(s[j]))) return fail_at("bad number");
+      while (j < s.size() && std::isdigit(static_cast<unsigned char>(s[j]))) ++j;
+    }
+    if (j < s.size() && (s[j] == 'e' || s[j] == 'E')) {
+      ++j;
+      if (j < s.size() && (s[j] == '+' || s[j] == '-')) ++j;
+      if (j >= s.size() || !std::isdigit(static_cast<unsigned char>(s[j]))) return fail_at("bad number");
+      while (j < s.size() && std::isdigit(static_cast<unsigned char>(s[j]))) ++j;
+    }
+    i = j;
+    return true;
+  }
+};
+
+bool json_top_level_strings(const std::string& text, std::map<std::string, std::string>* out, std::string* err) {
+  JsonReader r{text};
+  r.ws();
+  if (r.i >= text.size() || text[r.i] != '{') {
+    *err = "invalid model manifest JSON: expected an object";
+    return false;
+  }
+  ++r.i;
+  r.ws();
+  if (r.i < text.size() && text[r.i] == '}') {
+    ++r.i;
+  } else {
+    for (;;) {
+      std::string key;
+      r.ws();
+      if (!r.str(&key)) break;
+      r.ws();
+      if (r.i >= text.size() || text[r.i] != ':') {
+        r.fail_at("expected ':'");
+        break;
+      }
+      ++r.i;
+      std::string v;
+      bool is_str = false;
+      if (!r.value(1, &v, &is_str)) break;
+      if (is_str) (*out)[key] = v;
+      r.ws();
+      if (r.i < text.size() && text[r.i] == ',') {
+        ++r.i;
+        continue;
+      }
+      if (r.i < text.size() && text[r.i] == '}') {
+        ++r.i;
+        break;
+      }
+      r.fail_at("expected ',' or '}'");
+      break;
+    }
+  }
+  if (r.err.empty()) {
+    r.ws();
+    if (r.i != text.size()) r.fail_at("trailing characters");
+  }
+  if (!r.err.empty()) {
+    *err = r.err;
+    return false;
+  }
+  return true;
+}
+
+// GgufQwen35Config (model.rs:321-348) as read by from_metadata.
+struct Qwen35Meta {
+  uint64_t H, I, L, qh, kvh, kl, vl, ctxlen, interval, inner, state, groups, conv, rank, eos, vocab;
+  float eps, theta;
+};
+
+// GgufQwen35Config::from_metadata (model.rs:350-417): the same keys, types,
+// evaluation order and checks.
+int qwen35_from_metadata(const si_gguf* g, Qwen35Meta* q) {
   const char* arch = nullptr;
   if (int rc = si_gguf_meta_string(g, "general.architecture", &arch)) return rc;
   if (std::string(arch) != "qwen35")
     return si::fail(nullptr, SI_E_UNSUPPORTED, std::string("unsupported GGUF architecture ") + arch + "; expected qwen35");
-  uint64_t H, I, L, qh, kvh, kl, vl, ctxlen, interval, inner, state, groups, conv, rank, eos, vocab, rot;
-  double eps, theta;
+  double eps = 0, theta = 0;
   const struct {
     const char* key;
     uint64_t* dst;
-  } ints[] = {{"qwen35.embedding_length", &H},         {"qwen35.feed_forward_length", &I},
-              {"qwen35.block_count", &L},              {"qwen35.attention.head_count", &qh},
-              {"qwen35.attention.head_count_kv", &kvh}, {"qwen35.attention.key_length", &kl},
-              {"qwen35.attention.value_length", &vl},  {"qwen35.context_length", &ctxlen},
-              {"tokenizer.ggml.eos_token_id", &eos},   {"qwen35.full_attention_interval", &interval},
-              {"qwen35.ssm.inner_size", &inner},       {"qwen35.ssm.state_size", &state},
-              {"qwen35.ssm.group_count", &groups},     {"qwen35.ssm.conv_kernel", &conv},
-              {"qwen35.ssm.time_step_rank", &rank}};
+  } ints[] = {{"qwen35.embedding_length", &q->H},         {"qwen35.feed_forward_length", &q->I},
+              {"qwen35.block_count", &q->L},              {"qwen35.attention.head_count", &q->qh},
+              {"qwen35.attention.head_count_kv", &q->kvh}, {"qwen35.attention.key_length", &q->kl},
+              {"qwen35.attention.value_length", &q->vl},  {"qwen35.context_length", &q->ctxlen},
+              {"tokenizer.ggml.eos_token_id", &q->eos},   {"qwen35.full_attention_interval", &q->interval},
+              {"qwen35.ssm.inner_size", &q->inner},       {"qwen35.ssm.state_size", &q->state},
+              {"qwen35.ssm.group_count", &q->groups},     {"qwen35.ssm.conv_kernel", &q->conv},
+              {"qwen35.ssm.time_step_rank", &q->rank}};
   // required_u32 (model.rs:454-469): unsigned types only, and it must fit u32
   auto req_u32 = [&](const char* key, uint64_t* dst) -> int {
     if (int rc = si_gguf_meta_u64(g, key, dst)) return rc;
@@ -385,21 +571,40 @@ int si_gguf_qwen35_config(const si_gguf* g, uint32_t kv_capacity, si_model_confi
     return SI_OK;
   };
   for (const auto& e : ints) {
-    if (e.dst == &ctxlen) {  // vocab and the floats come between these in from_metadata
-      if (int rc = si_gguf_meta_array_len(g, "tokenizer.ggml.tokens", &vocab)) return rc;
+    if (e.dst == &q->ctxlen) {  // vocab and the floats come between these in from_metadata
+      if (int rc = si_gguf_meta_array_len(g, "tokenizer.ggml.tokens", &q->vocab)) return rc;
     }
-    if (e.dst == &eos) {
+    if (e.dst == &q->eos) {
       if (int rc = si_gguf_meta_f64(g, "qwen35.attention.layer_norm_rms_epsilon", &eps)) return rc;
       if (int rc = si_gguf_meta_f64(g, "qwen35.rope.freq_base", &theta)) return rc;
     }
     if (int rc = req_u32(e.key, e.dst)) return rc;
   }
-  const float eps_f = float(eps), theta_f = float(theta);
-  if (!H || !I || !L || !qh || !kvh || !kl || !vl || !vocab || !ctxlen || !interval || !inner || !state ||
-      !groups || !conv || !rank || !std::isfinite(eps_f) || eps_f <= 0.f || !std::isfinite(theta_f) || theta_f <= 1.f)
+  q->eps = float(eps);
+  q->theta = float(theta);
+  if (!q->H || !q->I || !q->L || !q->qh || !q->kvh || !q->kl || !q->vl || !q->vocab || !q->ctxlen || !q->interval ||
+      !q->inner || !q->state || !q->groups || !q->conv || !q->rank || !std::isfinite(q->eps) || q->eps <= 0.f ||
+      !std::isfinite(q->theta) || q->theta <= 1.f)
     return si::fail(nullptr, SI_E_INVALID, "Qwen3.6 GGUF config contains invalid dimensions");
-  if (qh % kvh) return si::fail(nullptr, SI_E_INVALID, "Qwen3.6 attention heads must be divisible by key/value heads");
-  if (inner % state) return si::fail(nullptr, SI_E_INVALID, "Qwen3.6 SSM inner size must be divisible by state size");
+  if (q->qh % q->kvh)
+    return si::fail(nullptr, SI_E_INVALID, "Qwen3.6 attention heads must be divisible by key/value heads");
+  if (q->inner % q->state)
+    return si::fail(nullptr, SI_E_INVALID, "Qwen3.6 SSM inner size must be divisible by state size");
+  return SI_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int si_gguf_qwen35_config(const si_gguf* g, uint32_t kv_capacity, si_model_config* c) {
+  if (!g || !c) return si::fail(nullptr, SI_E_INVALID, "invalid GGUF config arguments");
+  Qwen35Meta q;
+  if (int rc = qwen35_from_metadata(g, &q)) return rc;
+  uint64_t H = q.H, I = q.I, L = q.L, qh = q.qh, kvh = q.kvh, kl = q.kl, vl = q.vl, ctxlen = q.ctxlen,
+           interval = q.interval, inner = q.inner, state = q.state, groups = q.groups, conv = q.conv, rank = q.rank,
+           eos = q.eos, vocab = q.vocab, rot = 0;
+  const float eps_f = q.eps, theta_f = q.theta;
   // the runtime reads the rotary width separately (qwen35_runtime.rs:811-813)
   {
     const si::GgufValue* v = si::gguf_meta(g, "qwen35.rope.dimension_count");
@@ -439,6 +644,105 @@ int si_gguf_qwen35_config(const si_gguf* g, uint32_t kv_capacity, si_model_confi
   type_of("blk.0.ffn_down.weight", &c->down_type);
   type_of("output.weight", &c->head_type);
   return SI_OK;
+}
+
+
+int si_gguf_qwen35_layer_kind(const si_gguf* g, uint32_t layer, uint32_t* kind) {
+  if (!g || !kind) return si::fail(nullptr, SI_E_INVALID, "invalid layer kind arguments");
+  Qwen35Meta q;
+  if (int rc = qwen35_from_metadata(g, &q)) return rc;
+  if (layer >= q.L)
+    return si::fail(nullptr, SI_E_INVALID, "Qwen3.6 layer " + std::to_string(layer) + " exceeds " +
+                                               std::to_string(q.L) + " layers");
+  const std::string pre = "blk." + std::to_string(layer);
+  const bool has_delta = g->index.count(pre + ".ssm_a") != 0;
+  const bool has_attn = g->index.count(pre + ".attn_q.weight") != 0;
+  if (has_delta == has_attn)
+    return si::fail(nullptr, SI_E_INVALID,
+                    "Qwen3.6 layer " + std::to_string(layer) + " does not have exactly one execution kind");
+  const bool want_attn = (uint64_t(layer) + 1) % q.interval == 0;
+  if (has_attn != want_attn)
+    return si::fail(nullptr, SI_E_INVALID, "Qwen3.6 layer " + std::to_string(layer) + " tensor kind " +
+                                               (has_delta ? "GatedDeltaNet" : "FullAttention") +
+                                               " disagrees with interval " + std::to_string(q.interval));
+  *kind = has_attn ? SI_LAYER_FULL_ATTENTION : SI_LAYER_GATED_DELTA_NET;
+  return SI_OK;
+}
+
+int si_gguf_tensor_payload(const si_gguf* g, uint64_t index, uint64_t* elements, uint64_t* expected_bytes,
+                           uint32_t* known) {
+  if (!g || index >= g->tensors.size()) return si::fail(nullptr, SI_E_INVALID, "GGUF tensor index out of range");
+  const si::GgufTensor& t = g->tensors[index];
+  // element_count (model.rs:512-518)
+  uint64_t n = 1;
+  for (uint64_t d : t.dims) {
+    if (d && n > UINT64_MAX / d)
+      return si::fail(nullptr, SI_E_INVALID, "GGUF tensor " + t.name + " element count overflows");
+    n *= d;
+  }
+  if (elements) *elements = n;
+  // expected_payload_bytes (model.rs:532-573): F32, F16/BF16 and the K-quants
+  uint64_t bytes = 0;
+  bool k = true;
+  if (t.type == 0) {
+    if (n > UINT64_MAX / 4) k = false;
+    bytes = n * 4;
+  } else if (t.type == 1 || t.type == 30) {
+    if (n > UINT64_MAX / 2) k = false;
+    bytes = n * 2;
+  } else if (t.type == SI_GGML_TYPE_Q4_K || t.type == SI_GGML_TYPE_Q5_K || t.type == SI_GGML_TYPE_Q6_K) {
+    const char* label = t.type == SI_GGML_TYPE_Q4_K ? "Q4_K" : t.type == SI_GGML_TYPE_Q5_K ? "Q5_K" : "Q6_K";
+    if (n % 256)
+      return si::fail(nullptr, SI_E_INVALID, std::string("GGUF ") + label + " tensor " + t.name + " has " +
+                                                 std::to_string(n) + " elements; expected a multiple of 256");
+    const uint64_t bb = t.type == SI_GGML_TYPE_Q4_K ? 144 : t.type == SI_GGML_TYPE_Q5_K ? 176 : 210;
+    if (n / 256 > UINT64_MAX / bb) k = false;
+    bytes = n / 256 * bb;
+  } else {
+    k = false;
+  }
+  if (expected_bytes) *expected_bytes = k ? bytes : 0;
+  if (known) *known = k ? 1 : 0;
+  return SI_OK;
+}
+
+int si_detect_model_format(const char* path, uint32_t* format) {
+  if (!path || !format) return si::fail(nullptr, SI_E_INVALID, "invalid model format arguments");
+  struct stat st;
+  if (stat(path, &st) != 0) return si::fail(nullptr, SI_E_INVALID, std::string("stat model ") + path + ": " + std::strerror(errno));
+  if (S_ISDIR(st.st_mode)) {
+    // a BF16 Safetensors artifact: manifest.json with format "safetensors" and
+    // dtype "bfloat16" (model.rs:46-62)
+    const std::string manifest = std::string(path) + "/manifest.json";
+    FILE* f = std::fopen(manifest.c_str(), "rb");
+    if (!f) return si::fail(nullptr, SI_E_INVALID, "read model manifest " + manifest + ": " + std::strerror(errno));
+    std::string text;
+    char buf[4096];
+    size_t got;
+    while ((got = std::fread(buf, 1, sizeof(buf), f)) > 0) text.append(buf, got);
+    std::fclose(f);
+    std::map<std::string, std::string> fields;
+    std::string err;
+    if (!json_top_level_strings(text, &fields, &err)) return si::fail(nullptr, SI_E_INVALID, err);
+    if (fields.count("format") && fields["format"] == "safetensors" && fields.count("dtype") &&
+        fields["dtype"] == "bfloat16") {
+      *format = SI_FORMAT_SAFETENSORS;
+      return SI_OK;
+    }
+    return si::fail(nullptr, SI_E_INVALID, "model directory is not a BF16 Safetensors artifact");
+  }
+  FILE* f = std::fopen(path, "rb");
+  if (!f) return si::fail(nullptr, SI_E_INVALID, std::string("open model ") + path + ": " + std::strerror(errno));
+  char magic[4];
+  const size_t n = std::fread(magic, 1, 4, f);
+  std::fclose(f);
+  if (n < 4) return si::fail(nullptr, SI_E_INVALID, "failed to fill whole buffer");  // read_exact's error
+  if (std::memcmp(magic, "GGUF", 4) == 0) {
+    *format = SI_FORMAT_GGUF;
+    return SI_OK;
+  }
+  return si::fail(nullptr, SI_E_INVALID, std::string("unsupported model container ") + path +
+                                             "; expected a Safetensors directory or GGUF file");
 }
 
 }  // extern "C"

@@ -255,3 +255,73 @@ def test_seeded_mutations_agree_with_oracle(mai, tmp_path):
                         (t["name"].split("\0")[0], t["ggml_type"], t["data_start"], t["data_end"])
         agree += 1
     assert agree == 300 and accepted > 10
+
+
+def test_detects_safetensors_directories_and_gguf_files(mai, tmp_path):  # model.rs:1881-1902
+    root = tmp_path / "m"
+    root.mkdir()
+    (root / "manifest.json").write_text('{"model":"test","revision":"r","format":"safetensors","dtype":"bfloat16",'
+                                        '"total_weight_bytes":0,"files":[]}')
+    gguf = root / "tiny.gguf"
+    gguf.write_bytes(b"GGUF")
+    assert mai.detect_model_format(root) == "safetensors"
+    assert mai.detect_model_format(gguf) == "gguf"
+    # the manifest must say BF16 Safetensors; other containers are refused
+    (root / "manifest.json").write_text('{"format":"safetensors","dtype":"float16","files":[{"a":[1,2.5e3,true,null]}]}')
+    with pytest.raises(mai.SiError, match="not a BF16 Safetensors artifact"):
+        mai.detect_model_format(root)
+    (root / "manifest.json").write_text('{"format": "safetensors", "dtype": ')
+    with pytest.raises(mai.SiError, match="invalid model manifest JSON"):
+        mai.detect_model_format(root)
+    (root / "manifest.json").write_text('{"format":"safe\\u0074ensors","dtype":"bfloat16"} ')
+    assert mai.detect_model_format(root) == "safetensors"
+    other = tmp_path / "x.bin"
+    other.write_bytes(b"NOPE")
+    with pytest.raises(mai.SiError, match="unsupported model container"):
+        mai.detect_model_format(other)
+    with pytest.raises(mai.SiError, match="stat model"):
+        mai.detect_model_format(tmp_path / "missing")
+    empty = tmp_path / "empty"
+    empty.mkdir()
+    with pytest.raises(mai.SiError, match="read model manifest"):
+        mai.detect_model_format(empty)
+
+
+def _kind_metadata(layers, interval):
+    return kat_metadata(qwen35__block_count=(W.U32, layers), qwen35__full_attention_interval=(W.U32, interval))
+
+
+def test_layer_kinds_follow_tensors_and_interval(mai, tmp_path):
+    """qwen35_layer_kinds (model.rs:748-790), checked as the reference's real
+    GGUF test checks a 64-layer file (model.rs:2199-2204), on an 8-layer one."""
+    names = []
+    for l in range(8):
+        names.append(f"blk.{l}.attn_q.weight" if (l + 1) % 4 == 0 else f"blk.{l}.ssm_a")
+    tensors = [(n, [4], 0, bytes(16)) for n in names]
+    with open_bytes(mai, tmp_path, W.build(_kind_metadata(8, 4), tensors)) as g:
+        kinds = g.layer_kinds()
+        assert kinds[0] == "gated_delta_net" and kinds[3] == "full_attention" and kinds[7] == "full_attention"
+        assert kinds.count("full_attention") == 2
+        with pytest.raises(mai.SiError, match="exceeds 8 layers"):
+            g.layer_kind(8)
+    # a layer with both kinds, a layer with neither, and a kind against the interval
+    bad = [("blk.0.ssm_a", [4], 0, bytes(16)), ("blk.0.attn_q.weight", [4], 0, bytes(16)),
+           ("blk.2.ssm_a", [4], 0, bytes(16)), ("blk.3.ssm_a", [4], 0, bytes(16))]
+    with open_bytes(mai, tmp_path, W.build(_kind_metadata(4, 4), bad), "bad.gguf") as g:
+        with pytest.raises(mai.SiError, match="exactly one execution kind"):
+            g.layer_kind(0)
+        with pytest.raises(mai.SiError, match="exactly one execution kind"):
+            g.layer_kind(1)
+        with pytest.raises(mai.SiError, match="GatedDeltaNet disagrees with interval 4"):
+            g.layer_kind(3)
+
+
+def test_expected_payload_bytes(mai, tmp_path):  # GgufTensorInfo::expected_payload_bytes, model.rs:532-573
+    tensors = [("f32", [3, 5], 0, bytes(60)), ("f16", [7], 1, bytes(14)), ("bf16", [2, 2], 30, bytes(8)),
+               ("q4", [512, 3], 12, bytes(6 * 144)), ("q5", [256], 13, bytes(176)), ("q6", [256, 2], 14, bytes(420)),
+               ("q8_0", [32], 8, bytes(34)), ("bad_q4", [100], 12, bytes(144))]
+    with open_bytes(mai, tmp_path, W.build(_meta(), tensors)) as g:
+        got = [g.tensor_payload(i) for i in range(7)]
+        assert got == [(15, 60), (7, 14), (4, 8), (1536, 864), (256, 176), (512, 420), (32, None)]
+        with pytest.raises(mai.SiError, match="GGUF Q4_K tensor bad_q4 has 100 elements; expected a multiple of 256"):
+            g.tensor_payload(7)
