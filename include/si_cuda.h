@@ -96,7 +96,9 @@ typedef struct si_stats {
   uint64_t wait_nanos;
 } si_stats;
 int si_get_stats(const si_ctx* ctx, si_stats* out);
-int si_reset_peaks(si_ctx* ctx); /* reset_peaks, metal.rs:2358 */
+int si_reset_peaks(si_ctx* ctx);
+/* sample_allocated (metal.rs:2374-2378): fold the current allocation into the peak. */
+int si_sample_allocated(si_ctx* ctx); /* reset_peaks, metal.rs:2358 */
 
 /* ---- weights (QuantWeight, metal.rs:1840-1846) -------------------------- */
 /* upload_quant_weight_private (metal.rs:2502): copy bytes into device memory. */
@@ -159,6 +161,32 @@ int si_qmatmul_many_dev(si_ctx* ctx, uint32_t ggml_type, const void* weights_dev
 /* f32_matvec (metal.rs:2983). */
 int si_f32_matvec(si_ctx* ctx, const float* w, uint64_t rows, uint64_t cols, const float* x,
                   float* y);
+
+/* ---- staged layers (metal.rs:1852-1869, 2585-2637) ------------------------ */
+/* A packed decoder layer: upload_staged_qwen_layer_private copies it to device
+ * memory once (each named range at its own 256-byte aligned offset, so every
+ * view meets the kernels' alignment); bind_staged_qwen_layer_shared keeps it in
+ * the caller's host memory (page-locked when possible; the bytes must outlive
+ * the layer). Ranges: name -> [start, end) in the packed bytes. Views from
+ * si_staged_layer_weight (PrivateStagedQwenLayer::quant_weight) are freed with
+ * si_weight_free before the layer. */
+typedef struct si_staged_layer si_staged_layer;
+int si_staged_layer_upload(si_ctx* ctx, const void* packed, uint64_t bytes, uint32_t n_ranges,
+                           const char* const* names, const uint64_t* starts, const uint64_t* ends,
+                           si_staged_layer** out);
+int si_staged_layer_bind_host(si_ctx* ctx, const void* packed, uint64_t bytes, uint32_t n_ranges,
+                              const char* const* names, const uint64_t* starts, const uint64_t* ends,
+                              si_staged_layer** out);
+int si_staged_layer_weight(const si_staged_layer* layer, const char* name, uint32_t ggml_type, si_weight** out);
+void si_staged_layer_free(si_staged_layer* layer);
+/* gguf_quant_matvec_many_bytes (metal.rs:4878): n matrices of any K-quant type
+ * sharing x (cols columns). */
+int si_gguf_quant_matvec_many_bytes(si_ctx* ctx, uint32_t n, const uint32_t* ggml_types,
+                                    const void* const* weights, const uint64_t* nbytes, const uint64_t* rows,
+                                    uint64_t cols, const float* x, float* const* y);
+/* f32_matvec_many_gguf_tensors (metal.rs:4780): n F32 matrices sharing x. */
+int si_f32_matvec_many(si_ctx* ctx, uint32_t n, const float* const* weights, const uint64_t* rows, uint64_t cols,
+                       const float* x, float* const* y);
 
 /* ---- fused SwiGLU (metal.rs:3402-3732) ----------------------------------- */
 /* q4_k_fused_gate_up (metal.rs:3402): out = SiLU(G x) * (U x). */
@@ -355,6 +383,14 @@ int si_gguf_qwen35_layer_kind(const si_gguf* g, uint32_t layer, uint32_t* kind);
  * *known = 0 for types other than F32, F16, BF16 and the K-quants. */
 int si_gguf_tensor_payload(const si_gguf* g, uint64_t index, uint64_t* elements, uint64_t* expected_bytes,
                            uint32_t* known);
+/* gguf_matvec_tensor_rows (metal.rs:5003-5015): rows [row_start,
+ * row_start+row_count) of tensor `index` (F32 or a K-quant), read from the
+ * file, times x (dims[0] columns). */
+int si_gguf_matvec_tensor_rows(si_ctx* ctx, const si_gguf* g, uint64_t index, uint64_t row_start,
+                               uint64_t row_count, const float* x, float* y);
+/* q4_k_embedding_tensor (metal.rs:3785-3811): row `token` of a rank-2 Q4_K
+ * tensor, read from the file and dequantised (bit-exact). */
+int si_gguf_q4_k_embedding(si_ctx* ctx, const si_gguf* g, uint64_t index, uint64_t token, float* out);
 /* detect_model_format (model.rs:42-78) without loading any payload: a
  * directory whose manifest.json says format "safetensors" and dtype
  * "bfloat16", or a file starting with the GGUF magic. */

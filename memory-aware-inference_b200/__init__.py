@@ -156,6 +156,15 @@ def lib():
         "si_gguf_quant_matvec_many_weights": ([vp, u32, vp, vp, vp, vp, vp], i32),
         "si_qmatvec_dev": ([vp, u32, vp, u64, u64, vp, vp, vp], i32),
         "si_f32_matvec": ([vp, vp, u64, u64, vp, vp], i32),
+        "si_f32_matvec_many": ([vp, u32, vp, vp, u64, vp, vp], i32),
+        "si_gguf_quant_matvec_many_bytes": ([vp, u32, vp, vp, vp, vp, u64, vp, vp], i32),
+        "si_staged_layer_upload": ([vp, vp, u64, u32, vp, vp, vp, vp], i32),
+        "si_staged_layer_bind_host": ([vp, vp, u64, u32, vp, vp, vp, vp], i32),
+        "si_staged_layer_weight": ([vp, C.c_char_p, u32, vp], i32),
+        "si_staged_layer_free": ([vp], None),
+        "si_gguf_matvec_tensor_rows": ([vp, vp, u64, u64, u64, vp, vp], i32),
+        "si_gguf_q4_k_embedding": ([vp, vp, u64, u64, vp], i32),
+        "si_sample_allocated": ([vp], i32),
         "si_gguf_quant_matmul_many_bytes": ([vp, u32, vp, u64, u64, u64, u64, vp, vp], i32),
         "si_gguf_quant_matmul_many_weight": ([vp, vp, u64, u64, u64, vp, vp], i32),
         "si_qmatmul_many_dev": ([vp, u32, vp, u64, u64, u64, vp, vp, vp], i32),
@@ -256,6 +265,48 @@ class QuantWeight:
     ggml_type: int
     byte_len: int
     _host_ref: object = None
+
+
+class StagedLayer:
+    """PrivateStagedQwenLayer (metal.rs:1852-1869): a packed layer promoted to
+    device memory (or bound in host memory) with named tensor ranges."""
+
+    def __init__(self, ctx, packed, ranges, upload=True):
+        self.ctx = ctx
+        self._bytes = _u8(packed)  # kept alive: a bound layer reads it on every use
+        names = list(ranges)
+        n = len(names)
+        enc = (C.c_char_p * max(n, 1))(*[k.encode() for k in names])
+        starts = (C.c_uint64 * max(n, 1))(*[ranges[k][0] for k in names])
+        ends = (C.c_uint64 * max(n, 1))(*[ranges[k][1] for k in names])
+        h = C.c_void_p()
+        fn = lib().si_staged_layer_upload if upload else lib().si_staged_layer_bind_host
+        ctx._ck(fn(ctx.h, _p(self._bytes), self._bytes.size, n, enc, starts, ends, C.byref(h)))
+        self.h = h.value
+        self._views = []
+
+    def quant_weight(self, name: str, ggml_type: int) -> "QuantWeight":
+        h = C.c_void_p()
+        self.ctx._ck(lib().si_staged_layer_weight(self.h, name.encode(), ggml_type, C.byref(h)))
+        w = QuantWeight(h.value, ggml_type, lib().si_weight_bytes(h.value), self)
+        self._views.append(w)
+        return w
+
+    def close(self):
+        if getattr(self, "h", None):
+            for w in self._views:  # views the caller has not freed already
+                if w.handle:
+                    lib().si_weight_free(w.handle)
+                    w.handle = 0
+            self._views = []
+            lib().si_staged_layer_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 @dataclass
@@ -414,6 +465,63 @@ class CudaContext:
 
     def qmatmul_many_dev(self, ggml_type, w, rows, cols, batch, x, y, stream=None):
         self._ck(lib().si_qmatmul_many_dev(self.h, ggml_type, _p(w), rows, cols, batch, _p(x), _p(y), stream))
+
+    def sample_allocated(self):
+        """MetalContext::sample_allocated: fold the current allocation into the peak."""
+        self._ck(lib().si_sample_allocated(self.h))
+
+    def gguf_quant_matvec_many_bytes(self, tensors, x):
+        """MetalContext::gguf_quant_matvec_many_bytes: tensors = [(ggml_type,
+        bytes, rows, columns)] sharing x; returns one output per tensor."""
+        n = len(tensors)
+        xs = _f32(x)
+        arrs = [_u8(b) for _, b, _, _ in tensors]
+        outs = [np.empty(r, np.float32) for _, _, r, _ in tensors]
+        types = (C.c_uint32 * n)(*[t for t, _, _, _ in tensors])
+        ptrs = (C.c_void_p * n)(*[a.ctypes.data for a in arrs])
+        nbytes = (C.c_uint64 * n)(*[a.size for a in arrs])
+        rows = (C.c_uint64 * n)(*[r for _, _, r, _ in tensors])
+        ys = (C.c_void_p * n)(*[o.ctypes.data for o in outs])
+        cols = tensors[0][3] if tensors else 0
+        if any(t[3] != cols for t in tensors):
+            raise SiError(SI_E_INVALID, "staged quantized matvec group input length is invalid")
+        self._ck(lib().si_gguf_quant_matvec_many_bytes(self.h, n, types, ptrs, nbytes, rows, cols, _p(xs), ys))
+        return outs
+
+    def f32_matvec_many(self, matrices, x):
+        """MetalContext::f32_matvec_many_gguf_tensors: F32 matrices (rows x cols) sharing x."""
+        n = len(matrices)
+        ms = [np.ascontiguousarray(m, np.float32) for m in matrices]
+        outs = [np.empty(m.shape[0], np.float32) for m in ms]
+        cols = ms[0].shape[1] if ms else 0
+        ptrs = (C.c_void_p * n)(*[m.ctypes.data for m in ms])
+        rows = (C.c_uint64 * n)(*[m.shape[0] for m in ms])
+        ys = (C.c_void_p * n)(*[o.ctypes.data for o in outs])
+        self._ck(lib().si_f32_matvec_many(self.h, n, ptrs, rows, cols, _p(_f32(x)), ys))
+        return outs
+
+    def upload_staged_layer_private(self, packed, ranges) -> "StagedLayer":
+        """MetalContext::upload_staged_qwen_layer_private: ranges = {name: (start, end)}."""
+        return StagedLayer(self, packed, ranges, upload=True)
+
+    def bind_staged_layer_shared(self, packed, ranges) -> "StagedLayer":
+        """MetalContext::bind_staged_qwen_layer_shared (the bytes stay in host memory)."""
+        return StagedLayer(self, packed, ranges, upload=False)
+
+    def gguf_matvec_tensor_rows(self, gguf: "GgufFile", name_or_index, row_start, row_count, x) -> np.ndarray:
+        """MetalContext::gguf_matvec_tensor_rows over a tensor of an open GGUF file."""
+        idx = gguf.find(name_or_index) if isinstance(name_or_index, str) else int(name_or_index)
+        y = np.empty(row_count, np.float32)
+        self._ck(lib().si_gguf_matvec_tensor_rows(self.h, gguf.h, idx, row_start, row_count, _p(_f32(x)), _p(y)))
+        return y
+
+    def q4_k_embedding_tensor(self, gguf: "GgufFile", name_or_index, token_id) -> np.ndarray:
+        """MetalContext::q4_k_embedding_tensor over a tensor of an open GGUF file."""
+        idx = gguf.find(name_or_index) if isinstance(name_or_index, str) else int(name_or_index)
+        cols = gguf.tensor_info(idx)["shape"][0]
+        out = np.empty(cols, np.float32)
+        self._ck(lib().si_gguf_q4_k_embedding(self.h, gguf.h, idx, token_id, _p(out)))
+        return out
 
     def f32_matvec(self, weights, rows, columns, x):
         w, xv = _f32(weights), _f32(x)

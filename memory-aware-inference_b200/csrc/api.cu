@@ -5,12 +5,14 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <string>
 #include <vector>
 
 #include "common.cuh"
 #include "comm.h"
 #include "ctx.h"
+#include "gguf.h"
 #include "kernels.cuh"
 #include "qmatvec.cuh"
 
@@ -25,6 +27,21 @@ struct si_weight {
   uint64_t bytes = 0;
   uint32_t type = 0;
   bool registered = false;
+  bool view = false;  // a view into a staged layer: the layer owns the memory
+};
+
+// A packed decoder layer promoted to device memory or bound in host memory
+// (PrivateStagedQwenLayer, metal.rs:1852-1869).
+struct si_staged_layer {
+  si_ctx* ctx = nullptr;
+  uint8_t* dev = nullptr;      // upload: each range at its own 256-byte aligned offset
+  const uint8_t* host = nullptr;  // bind: the caller's packed bytes
+  bool registered = false;
+  uint64_t bytes = 0, dev_bytes = 0;
+  struct Range {
+    uint64_t start, end, dev_off;
+  };
+  std::map<std::string, Range> ranges;
 };
 
 namespace si {
@@ -307,6 +324,10 @@ int si_weight_bind_host(si_ctx* ctx, const void* host, uint64_t bytes, uint32_t 
 
 void si_weight_free(si_weight* w) {
   if (!w) return;
+  if (w->view) {
+    delete w;
+    return;
+  }
   if (w->dev) {
     cudaSetDevice(w->ctx->device);
     cudaFree(w->dev);
@@ -886,6 +907,169 @@ int si_argmax(si_ctx* ctx, const float* logits, uint64_t n, uint32_t* index) {
   if ((rc = d2h(ctx, index, ctx->d_index, 4, "argmax readback"))) return rc;
   if ((rc = sync_and_check(ctx, "argmax command"))) return rc;
   if (*index == 0xffffffffu) return fail(ctx, SI_E_INVALID, "logits contain no finite values");
+  return SI_OK;
+}
+
+// ---- staged layers, grouped and file-backed matvecs (metal.rs:2585-2637,
+//      4780-4990, 5003-5015, 3785-3811) and allocation sampling (2374-2378) ----
+
+static int staged_create(si_ctx* ctx, const void* packed, uint64_t bytes, uint32_t n, const char* const* names,
+                         const uint64_t* starts, const uint64_t* ends, bool upload, si_staged_layer** out) {
+  if (!ctx || !out) return fail(ctx, SI_E_INVALID, "invalid staged layer arguments");
+  *out = nullptr;
+  if (!packed || bytes == 0)
+    return fail(ctx, SI_E_INVALID, upload ? "cannot promote an empty staged Qwen layer" : "cannot bind an empty staged Qwen layer");
+  if (n && (!names || !starts || !ends)) return fail(ctx, SI_E_INVALID, "invalid staged layer ranges");
+  auto* L = new si_staged_layer();
+  L->ctx = ctx;
+  L->bytes = bytes;
+  uint64_t off = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    if (!names[i] || starts[i] > ends[i] || ends[i] > bytes) {
+      delete L;
+      return fail(ctx, SI_E_INVALID, std::string("staged range of ") + (names[i] ? names[i] : "?") + " is out of bounds");
+    }
+    L->ranges[names[i]] = {starts[i], ends[i], off};
+    off = (off + (ends[i] - starts[i]) + 64 + 255) & ~uint64_t(255);  // read-ahead pad, 256-byte aligned
+  }
+  if (upload) {
+    std::lock_guard<std::mutex> lk(ctx->upload_mu);
+    cudaSetDevice(ctx->device);
+    L->dev_bytes = std::max<uint64_t>(off, 256);
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&L->dev), L->dev_bytes);
+    if (e != cudaSuccess) {
+      delete L;
+      return cuda_fail(ctx, e, "packed Qwen layer private upload");
+    }
+    cudaMemsetAsync(L->dev, 0, L->dev_bytes, ctx->copy_stream);
+    for (const auto& r : L->ranges)
+      if (r.second.end > r.second.start)
+        cudaMemcpyAsync(L->dev + r.second.dev_off, static_cast<const uint8_t*>(packed) + r.second.start,
+                        r.second.end - r.second.start, cudaMemcpyHostToDevice, ctx->copy_stream);
+    if ((e = cudaStreamSynchronize(ctx->copy_stream)) != cudaSuccess) {
+      cudaFree(L->dev);
+      delete L;
+      return cuda_fail(ctx, e, "packed Qwen layer private upload");
+    }
+    note_alloc(ctx, int64_t(L->dev_bytes));
+  } else {
+    L->host = static_cast<const uint8_t*>(packed);
+    if (cudaHostRegister(const_cast<void*>(packed), bytes, cudaHostRegisterReadOnly) == cudaSuccess)
+      L->registered = true;
+    else
+      cudaGetLastError();
+  }
+  *out = L;
+  return SI_OK;
+}
+
+int si_staged_layer_upload(si_ctx* ctx, const void* packed, uint64_t bytes, uint32_t n, const char* const* names,
+                           const uint64_t* starts, const uint64_t* ends, si_staged_layer** out) {
+  return staged_create(ctx, packed, bytes, n, names, starts, ends, true, out);
+}
+
+int si_staged_layer_bind_host(si_ctx* ctx, const void* packed, uint64_t bytes, uint32_t n, const char* const* names,
+                              const uint64_t* starts, const uint64_t* ends, si_staged_layer** out) {
+  return staged_create(ctx, packed, bytes, n, names, starts, ends, false, out);
+}
+
+int si_staged_layer_weight(const si_staged_layer* L, const char* name, uint32_t ggml_type, si_weight** out) {
+  if (!L || !name || !out) return fail(L ? L->ctx : nullptr, SI_E_INVALID, "invalid staged weight arguments");
+  *out = nullptr;
+  auto it = L->ranges.find(name);
+  if (it == L->ranges.end()) return fail(L->ctx, SI_E_INVALID, std::string("unknown staged tensor ") + name);
+  auto* w = new si_weight();
+  w->ctx = L->ctx;
+  w->view = true;
+  w->bytes = it->second.end - it->second.start;
+  w->type = ggml_type;
+  if (L->dev) w->dev = L->dev + it->second.dev_off;
+  else w->host = L->host + it->second.start;
+  *out = w;
+  return SI_OK;
+}
+
+void si_staged_layer_free(si_staged_layer* L) {
+  if (!L) return;
+  if (L->dev) {
+    cudaSetDevice(L->ctx->device);
+    cudaFree(L->dev);
+    note_alloc(L->ctx, -int64_t(L->dev_bytes));
+  }
+  if (L->registered) cudaHostUnregister(const_cast<uint8_t*>(L->host));
+  delete L;
+}
+
+int si_gguf_quant_matvec_many_bytes(si_ctx* ctx, uint32_t n, const uint32_t* types, const void* const* weights,
+                                    const uint64_t* nbytes, const uint64_t* rows, uint64_t cols, const float* x,
+                                    float* const* ys) {
+  if (!ctx) return SI_E_INVALID;
+  if (n == 0) return fail(ctx, SI_E_INVALID, "staged quantized matvec group requires at least one tensor");
+  if (cols == 0 || !x || !types || !weights || !nbytes || !rows || !ys)
+    return fail(ctx, SI_E_INVALID, "staged quantized matvec group input length is invalid");
+  for (uint32_t i = 0; i < n; ++i)
+    if (int rc = si_gguf_quant_matvec_bytes(ctx, types[i], weights[i], nbytes[i], rows[i], cols, x, ys[i])) return rc;
+  return SI_OK;
+}
+
+int si_f32_matvec_many(si_ctx* ctx, uint32_t n, const float* const* weights, const uint64_t* rows, uint64_t cols,
+                       const float* x, float* const* ys) {
+  if (!ctx) return SI_E_INVALID;
+  if (n == 0) return fail(ctx, SI_E_INVALID, "GGUF F32 matvec group requires at least one tensor");
+  if (cols == 0 || !x || !weights || !rows || !ys)
+    return fail(ctx, SI_E_INVALID, "GGUF F32 matvec group input length is invalid");
+  for (uint32_t i = 0; i < n; ++i)
+    if (int rc = si_f32_matvec(ctx, weights[i], rows[i], cols, x, ys[i])) return rc;
+  return SI_OK;
+}
+
+int si_gguf_matvec_tensor_rows(si_ctx* ctx, const si_gguf* g, uint64_t index, uint64_t row_start, uint64_t row_count,
+                               const float* x, float* y) {
+  if (!ctx || !g || !x || !y) return fail(ctx, SI_E_INVALID, "invalid tensor-rows matvec arguments");
+  if (index >= g->tensors.size()) return fail(ctx, SI_E_INVALID, "GGUF tensor index out of range");
+  const GgufTensor& t = g->tensors[index];
+  if (t.ndim < 2) return fail(ctx, SI_E_INVALID, "tensor " + t.name + " is not a matrix");
+  const uint64_t cols = t.dims[0], total_rows = t.dims[1];
+  if (row_count == 0 || row_start > total_rows || row_count > total_rows - row_start)
+    return fail(ctx, SI_E_INVALID, "tensor " + t.name + " rows are out of range");
+  uint64_t rb;
+  if (t.type == SI_GGML_TYPE_F32) {
+    rb = cols * 4;
+  } else if (block_bytes_of(t.type) && cols % 256 == 0) {
+    rb = cols / 256 * block_bytes_of(t.type);
+  } else {
+    return fail(ctx, SI_E_UNSUPPORTED, "tensor " + t.name + " has no matvec for type " + std::to_string(t.type));
+  }
+  if (row_start + row_count > t.data_len / rb) return fail(ctx, SI_E_INVALID, "tensor " + t.name + " payload is too short");
+  std::vector<uint8_t> buf(row_count * rb);
+  std::string err;
+  if (int rc = gguf_read(g, t.data_start + row_start * rb, buf.data(), buf.size(), &err)) return fail(ctx, rc, err);
+  if (t.type == SI_GGML_TYPE_F32)
+    return si_f32_matvec(ctx, reinterpret_cast<const float*>(buf.data()), row_count, cols, x, y);
+  return si_gguf_quant_matvec_bytes(ctx, t.type, buf.data(), buf.size(), row_count, cols, x, y);
+}
+
+int si_gguf_q4_k_embedding(si_ctx* ctx, const si_gguf* g, uint64_t index, uint64_t token, float* out) {
+  if (!ctx || !g || !out) return fail(ctx, SI_E_INVALID, "invalid embedding arguments");
+  if (index >= g->tensors.size()) return fail(ctx, SI_E_INVALID, "GGUF tensor index out of range");
+  const GgufTensor& t = g->tensors[index];
+  if (t.type != SI_GGML_TYPE_Q4_K || t.ndim != 2) return fail(ctx, SI_E_INVALID, "Q4_K embedding requires a rank-2 Q4_K tensor");
+  const uint64_t cols = t.dims[0], rows = t.dims[1];
+  if (token >= rows || cols % 256) return fail(ctx, SI_E_INVALID, "Q4_K embedding token id or dimension is invalid");
+  const uint64_t rb = cols / 256 * 144;
+  if ((token + 1) * rb > t.data_len) return fail(ctx, SI_E_INVALID, "Q4_K embedding row exceeds the tensor payload");
+  std::vector<uint8_t> row(rb);
+  std::string err;
+  if (int rc = gguf_read(g, t.data_start + token * rb, row.data(), rb, &err)) return fail(ctx, rc, err);
+  return si_q4_k_embedding_row(ctx, row.data(), rb, cols, out);
+}
+
+int si_sample_allocated(si_ctx* ctx) {
+  if (!ctx) return SI_E_INVALID;
+  const uint64_t cur = ctx->allocated.load();
+  uint64_t peak = ctx->peak_allocated.load();
+  while (cur > peak && !ctx->peak_allocated.compare_exchange_weak(peak, cur)) {
+  }
   return SI_OK;
 }
 

@@ -1,0 +1,100 @@
+"""The rest of MetalContext's surface the runtime binds (metal.rs:2374-2378,
+2585-2637, 3785-3811, 4780-4990, 5003-5015): staged layers promoted to device
+memory or bound in host memory, grouped matvecs over bytes and F32 matrices,
+file-backed row-range matvecs and embeddings, allocation sampling; each
+against the oracle."""
+import numpy as np
+import pytest
+
+import gguf_writer as W
+import oracle as O
+from helpers import random_blocks, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+Q4, Q5, Q6 = 12, 13, 14
+
+
+def test_staged_layer_private_and_shared(mai, ctx):
+    rng = np.random.default_rng(1)
+    a = random_blocks(rng, Q4, 512 * 1024 // 256)   # 512 x 1024 Q4_K
+    b = random_blocks(rng, Q6, 256 * 512 // 256)    # 256 x 512 Q6_K
+    c = random_blocks(rng, Q5, 64 * 256 // 256)     # 64 x 256 Q5_K
+    # packed with unaligned offsets, as a staging thread may pack them
+    packed = np.concatenate([np.zeros(3, np.uint8), a, np.zeros(5, np.uint8), b, c])
+    o_a, o_b = 3, 3 + a.size + 5
+    o_c = o_b + b.size
+    ranges = {"blk.0.ffn_gate.weight": (o_a, o_a + a.size), "blk.0.ffn_down.weight": (o_b, o_b + b.size),
+              "blk.0.attn_qkv.weight": (o_c, o_c + c.size)}
+    x1024 = rng.normal(0, 1, 1024).astype(np.float32)
+    x512 = rng.normal(0, 1, 512).astype(np.float32)
+    x256 = rng.normal(0, 1, 256).astype(np.float32)
+    for upload in (True, False):
+        layer = ctx.upload_staged_layer_private(packed, ranges) if upload else ctx.bind_staged_layer_shared(packed, ranges)
+        wa = layer.quant_weight("blk.0.ffn_gate.weight", Q4)
+        wb = layer.quant_weight("blk.0.ffn_down.weight", Q6)
+        wc = layer.quant_weight("blk.0.attn_qkv.weight", Q5)
+        assert rel_l2(ctx.gguf_quant_matvec_weight(wa, 512, 1024, x1024), O.matvec(Q4, a, 512, 1024, x1024)) < 1e-5
+        assert rel_l2(ctx.gguf_quant_matvec_weight(wb, 256, 512, x512), O.matvec(Q6, b, 256, 512, x512)) < 1e-5
+        assert rel_l2(ctx.gguf_quant_matvec_weight(wc, 64, 256, x256), O.matvec(Q5, c, 64, 256, x256)) < 1e-5
+        with pytest.raises(mai.SiError, match="unknown staged tensor"):
+            layer.quant_weight("blk.0.nope", Q4)
+        ctx.free_weight(wa)  # a view freed early is not freed again by the layer
+        layer.close()
+    with pytest.raises(mai.SiError, match="cannot promote an empty staged Qwen layer"):
+        ctx.upload_staged_layer_private(np.zeros(0, np.uint8), {})
+    with pytest.raises(mai.SiError, match="out of bounds"):
+        ctx.upload_staged_layer_private(packed, {"x": (0, packed.size + 1)})
+
+
+def test_grouped_matvecs_over_bytes_and_f32(mai, ctx):
+    rng = np.random.default_rng(2)
+    cols = 768
+    ts = [(Q4, random_blocks(rng, Q4, 300 * cols // 256), 300), (Q6, random_blocks(rng, Q6, 40 * cols // 256), 40),
+          (Q5, random_blocks(rng, Q5, 5 * cols // 256), 5)]
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    outs = ctx.gguf_quant_matvec_many_bytes([(t, w, r, cols) for t, w, r in ts], x)
+    for (t, w, r), y in zip(ts, outs):
+        assert rel_l2(y, O.matvec(t, w, r, cols, x)) < 1e-5
+    with pytest.raises(mai.SiError, match="at least one tensor"):
+        ctx.gguf_quant_matvec_many_bytes([], x)
+    for c2 in (5120, 130):
+        ms = [rng.normal(0, 0.02, (48, c2)).astype(np.float32), rng.normal(0, 0.02, (7, c2)).astype(np.float32)]
+        x2 = rng.normal(0, 1, c2).astype(np.float32)
+        for m, y in zip(ms, ctx.f32_matvec_many(ms, x2)):
+            assert rel_l2(y, m.astype(np.float64) @ x2.astype(np.float64)) < 1e-5
+
+
+def test_file_backed_rows_and_embedding(mai, ctx, tmp_path):
+    rng = np.random.default_rng(3)
+    q5 = random_blocks(rng, Q5, 100 * 512 // 256)
+    f32 = rng.normal(0, 0.1, (40, 96)).astype(np.float32)
+    emb = random_blocks(rng, Q4, 50 * 256 // 256)
+    path = tmp_path / "t.gguf"
+    W.write(path, [("general.architecture", W.STRING, "qwen35")],
+            [("w", [512, 100], Q5, q5.tobytes()), ("f", [96, 40], 0, f32.tobytes()),
+             ("token_embd.weight", [256, 50], Q4, emb.tobytes())])
+    x = rng.normal(0, 1, 512).astype(np.float32)
+    x96 = rng.normal(0, 1, 96).astype(np.float32)
+    with mai.GgufFile(path) as g:
+        y = ctx.gguf_matvec_tensor_rows(g, "w", 30, 25, x)
+        rb = 512 // 256 * 176
+        assert rel_l2(y, O.matvec(Q5, q5[30 * rb:55 * rb], 25, 512, x)) < 1e-5
+        yf = ctx.gguf_matvec_tensor_rows(g, "f", 3, 10, x96)
+        assert rel_l2(yf, f32[3:13].astype(np.float64) @ x96.astype(np.float64)) < 1e-5
+        with pytest.raises(mai.SiError, match="rows are out of range"):
+            ctx.gguf_matvec_tensor_rows(g, "w", 90, 11, x)
+        e = ctx.q4_k_embedding_tensor(g, "token_embd.weight", 17)
+        assert np.array_equal(e.view(np.uint32), O.dequantize(Q4, emb[17 * 144:18 * 144], 256).view(np.uint32))
+        with pytest.raises(mai.SiError, match="token id or dimension is invalid"):
+            ctx.q4_k_embedding_tensor(g, "token_embd.weight", 50)
+        with pytest.raises(mai.SiError, match="rank-2 Q4_K tensor"):
+            ctx.q4_k_embedding_tensor(g, "w", 0)
+
+
+def test_sample_allocated_folds_into_the_peak(mai, ctx):
+    ctx.reset_peaks()
+    before = ctx.stats()
+    ctx.sample_allocated()
+    after = ctx.stats()
+    assert after["peak_allocated_bytes"] >= before["current_allocated_bytes"]
