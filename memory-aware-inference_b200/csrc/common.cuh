@@ -4,6 +4,8 @@
 #pragma once
 
 #include <cuda_runtime.h>
+
+#include <atomic>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -117,6 +119,22 @@ __device__ __forceinline__ void scale_min_k4(int index, const uint8_t* s, uint32
     sc = (s[index + 4] & 0x0fu) | ((s[index - 4] >> 6) << 4);
     mn = (s[index + 4] >> 4) | ((s[index] >> 6) << 4);
   }
+}
+
+constexpr int kMaxDevices = 64;
+
+// Raise a kernel's dynamic shared memory limit to `bytes` on the current
+// device, once: function attributes belong to a device, so `cache[d]` keeps the
+// limit set so far on device d (a process may drive several devices).
+template <typename F>
+inline cudaError_t raise_smem_limit(F kernel, uint32_t bytes, std::atomic<uint32_t>* cache) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+  if (cache[dev].load(std::memory_order_relaxed) >= bytes) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+  if (e == cudaSuccess) cache[dev].store(bytes, std::memory_order_relaxed);
+  return e;
 }
 
 __host__ __device__ constexpr uint32_t block_bytes_of(uint32_t type) {

@@ -1029,12 +1029,9 @@ static bool cache_tensor_map(CUtensorMap* map, const void* base, uint32_t hd, ui
 template <int HD, int G>
 static void launch_fa(const CUtensorMap& tk, const CUtensorMap& tv, const AttnArgs& a, cudaLaunchConfig_t cfg,
                       uint32_t nsplit) {
-  static bool attr_set = false;  // per instantiation; the attribute is per function
+  static std::atomic<uint32_t> smem_limit[kMaxDevices];  // per instantiation and device
   constexpr uint32_t smem = FaLayout<HD, G>::bytes;
-  if (!attr_set) {
-    cudaFuncSetAttribute(attn_split_bf16_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr_set = true;
-  }
+  raise_smem_limit(attn_split_bf16_kernel<HD, G>, smem, smem_limit);  // a failure shows in the launch
   cfg.gridDim = dim3(nsplit, a.kvh);
   cfg.blockDim = dim3(kFaThreads);
   cfg.dynamicSmemBytes = smem;

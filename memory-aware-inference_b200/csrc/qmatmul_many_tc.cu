@@ -682,11 +682,8 @@ int launch_qmm_tc(const QmmParams& p, cudaStream_t s, int sm_count, bool pdl, st
             : ti == 1 ? qmm_tc_kernel<SI_GGML_TYPE_Q5_K>
                       : qmm_tc_kernel<SI_GGML_TYPE_Q6_K>;
   if (e == cudaSuccess) {
-    static bool smem_set[3] = {false, false, false};  // the first call raises each kernel's shared memory limit
-    if (!smem_set[ti]) {
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kQtSmemMax));
-      smem_set[ti] = e == cudaSuccess;
-    }
+    static std::atomic<uint32_t> smem_limit[3][kMaxDevices];  // per type and device
+    e = raise_smem_limit(kern, kQtSmemMax, smem_limit[ti]);
   }
   if (e == cudaSuccess) {
     cudaLaunchConfig_t mc = {};

@@ -754,10 +754,14 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
   G.xs_floats = p.cols + 4 * (p.cols >> PAD);
   const uint32_t xbytes = 4 * (G.xs_floats + p.cols / Fmt<TYPE>::kSum +
                                 (TYPE == SI_GGML_TYPE_Q4_K ? p.cols / 32 : 0));
-  static uint32_t max_dyn = 0;
+  // per instantiation and device: the attribute belongs to the current device
+  static std::atomic<uint32_t> max_dyn_dev[kMaxDevices];
+  int cur_dev = 0;
+  cudaGetDevice(&cur_dev);
+  std::atomic<uint32_t>& max_dyn_slot = max_dyn_dev[cur_dev >= 0 && cur_dev < kMaxDevices ? cur_dev : 0];
+  uint32_t max_dyn = max_dyn_slot.load(std::memory_order_relaxed);
   if (max_dyn == 0) {
-    int dev = 0, optin = 0, per_sm = 0;
-    cudaGetDevice(&dev);
+    int dev = cur_dev, optin = 0, per_sm = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
     optin = std::min(optin, per_sm / kCtasPerSm - 1024);
@@ -773,6 +777,7 @@ static int launch_t(const QmvParams& p, cudaStream_t stream, int sm_count, bool 
       return SI_E_CUDA;
     }
     max_dyn = limit;
+    max_dyn_slot.store(limit, std::memory_order_relaxed);
   }
   // largest slot count that fits, then teams with >= 2 private slots each
   uint32_t nslots = kMaxSlots, total = 0;

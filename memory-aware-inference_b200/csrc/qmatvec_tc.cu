@@ -466,14 +466,10 @@ static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stre
     uhi = hi;
     ulo = lo;
   }
-  static uint32_t attr = 0;
-  if (smem > attr) {
-    cudaError_t e = cudaFuncSetAttribute(qmv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) {
-      if (msg) *msg = std::string("cudaFuncSetAttribute(qmv_tc): ") + cudaGetErrorString(e);
-      return SI_E_CUDA;
-    }
-    attr = smem;
+  static std::atomic<uint32_t> smem_limit[kMaxDevices];
+  if (cudaError_t e = raise_smem_limit(qmv_tc_kernel, smem, smem_limit)) {
+    if (msg) *msg = std::string("cudaFuncSetAttribute(qmv_tc): ") + cudaGetErrorString(e);
+    return SI_E_CUDA;
   }
   TcArgs a = {};
   a.x = p.x;
