@@ -373,6 +373,12 @@ int si_gguf_meta_array_len(const si_gguf* g, const char* key, uint64_t* out);
 /* Copy bytes [offset, offset+bytes) of tensor `index`'s payload
  * (stage_tensor_payload, model.rs:867-886). */
 int si_gguf_read(const si_gguf* g, uint64_t index, uint64_t offset, void* dst, uint64_t bytes);
+/* Metadata keys in byte order (the reference keeps them in a BTreeMap), and a
+ * key's value summarised as si-gguf-inspect prints it (summarize,
+ * src/bin/si-gguf-inspect.rs:84-101: "U32(5120)", "F32(1e-6)",
+ * "string(\"qwen35\")", "array(len=N, first=[...])"). Strings are owned by g. */
+int si_gguf_meta_key_at(const si_gguf* g, uint64_t index, const char** key);
+int si_gguf_meta_summary(const si_gguf* g, const char* key, const char** out);
 /* qwen35_layer_kind (model.rs:748-783): ssm_a present = Gated DeltaNet,
  * attn_q.weight present = full attention; exactly one, and agreeing with the
  * full-attention interval. */

@@ -210,6 +210,8 @@ def lib():
         "si_gguf_read": ([vp, u64, u64, vp, u64], i32),
         "si_gguf_qwen35_config": ([vp, u32, vp], i32),
         "si_gguf_qwen35_layer_kind": ([vp, u32, vp], i32),
+        "si_gguf_meta_key_at": ([vp, u64, vp], i32),
+        "si_gguf_meta_summary": ([vp, C.c_char_p, vp], i32),
         "si_gguf_tensor_payload": ([vp, u64, vp, vp, vp], i32),
         "si_detect_model_format": ([C.c_char_p, vp], i32),
         "si_trace_create": ([u32], vp),
@@ -767,6 +769,17 @@ class GgufFile:
             nbytes = info["data_end"] - info["data_start"] - offset
         out = np.empty(nbytes, np.uint8)
         _gck(lib().si_gguf_read(self.h, idx, offset, _p(out), nbytes))
+        return out
+
+    def metadata(self) -> dict:
+        """Every metadata key (in the store's byte order) with its value
+        summarised as si-gguf-inspect prints it."""
+        out = {}
+        for i in range(self.metadata_count):
+            k, v = C.c_char_p(), C.c_char_p()
+            _gck(lib().si_gguf_meta_key_at(self.h, i, C.byref(k)))
+            _gck(lib().si_gguf_meta_summary(self.h, k.value, C.byref(v)))
+            out[k.value.decode()] = v.value.decode()
         return out
 
     def layer_kind(self, layer: int) -> str:

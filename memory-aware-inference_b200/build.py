@@ -77,18 +77,20 @@ def build(force=False, verbose=False):
 
 
 def build_cli(force=False):
-    """The si-bench command line (cli/si_bench.cpp): host C++ over the C ABI,
-    linked against libsi_cuda.so beside it."""
-    src = os.path.join(HERE, "cli", "si_bench.cpp")
-    deps = [src, LIB, os.path.join(REPO, "include", "si_cuda.h")]
-    if not force and os.path.exists(CLI) and os.path.getmtime(CLI) >= max(os.path.getmtime(d) for d in deps):
-        return CLI
+    """The command-line programs (cli/*.cpp: si-bench, si-gguf-inspect): host
+    C++ over the C ABI, linked against libsi_cuda.so beside them."""
     _, libdir = _nccl_dirs()
-    cmd = ["g++", "-O2", "-std=c++17", "-Wall", "-I", os.path.join(REPO, "include"), src, "-o", CLI, "-L", HERE,
-           "-l:libsi_cuda.so", "-Wl,-rpath,$ORIGIN", "-Wl,-rpath-link," + libdir]
-    r = subprocess.run(cmd, capture_output=True, text=True)
-    if r.returncode != 0:
-        raise RuntimeError(f"si-bench build failed:\n{r.stderr}")
+    for name, src in (("si-bench", "si_bench.cpp"), ("si-gguf-inspect", "si_gguf_inspect.cpp")):
+        out = os.path.join(HERE, name)
+        src = os.path.join(HERE, "cli", src)
+        deps = [src, LIB, os.path.join(REPO, "include", "si_cuda.h")]
+        if not force and os.path.exists(out) and os.path.getmtime(out) >= max(os.path.getmtime(d) for d in deps):
+            continue
+        cmd = ["g++", "-O2", "-std=c++17", "-Wall", "-I", os.path.join(REPO, "include"), src, "-o", out, "-L", HERE,
+               "-l:libsi_cuda.so", "-Wl,-rpath,$ORIGIN", "-Wl,-rpath-link," + libdir]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"{name} build failed:\n{r.stderr}")
     return CLI
 
 

@@ -12,7 +12,9 @@
 #include <cerrno>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <iterator>
 #include <map>
 #include <string>
 #include <vector>
@@ -134,12 +136,19 @@ bool read_value(Reader& r, uint32_t type, si::GgufValue* v, int depth) {
       v->count = count;
       const uint64_t es = value_size(et);
       if (count == 0) return true;  // element type is never read
-      if (es) {  // fixed-size elements: skip them (only the length is kept)
+      // the first elements are kept as a preview (the inspection summary);
+      // decode needs only the length
+      const uint64_t keep = std::min<uint64_t>(count, si::kGgufPreview);
+      if (es) {  // fixed-size elements: the rest are skipped
         if (count > r.size / es) {
           r.err = "GGUF header is truncated";
           return false;
         }
-        return r.skip(count * es);
+        for (uint64_t i = 0; i < keep; ++i) {
+          v->preview.emplace_back();
+          if (!read_value(r, et, &v->preview.back(), depth + 1)) return false;
+        }
+        return r.skip((count - keep) * es);
       }
       if (et != 8 && et != 9) {
         r.err = "unsupported GGUF metadata type " + std::to_string(et);
@@ -148,6 +157,7 @@ bool read_value(Reader& r, uint32_t type, si::GgufValue* v, int depth) {
       for (uint64_t i = 0; i < count; ++i) {
         si::GgufValue e;
         if (!read_value(r, et, &e, depth + 1)) return false;
+        if (i < keep) v->preview.push_back(std::move(e));
       }
       return true;
     }
@@ -261,6 +271,112 @@ int gguf_read(const si_gguf* g, uint64_t offset, void* dst, uint64_t bytes, std:
     bytes -= uint64_t(got);
   }
   return SI_OK;
+}
+
+namespace {
+
+// Rust's Debug of a float: the shortest digits that read back to the same
+// value; exponential form ("1e-6", "1.5e20") when |x| < 1e-4 or |x| >= 1e16,
+// else decimal with at least one fractional digit ("10000000.0", "0.1").
+std::string rust_float_debug(double x, bool is_f32) {
+  if (std::isnan(x)) return "NaN";
+  if (std::isinf(x)) return x < 0 ? "-inf" : "inf";
+  if (x == 0) return std::signbit(x) ? "-0.0" : "0.0";
+  char buf[64];
+  int p = 1;
+  for (; p <= 17; ++p) {
+    std::snprintf(buf, sizeof(buf), "%.*e", p - 1, x);
+    const double back = std::strtod(buf, nullptr);
+    if (is_f32 ? float(back) == float(x) : back == x) break;
+  }
+  // buf = [-]D[.DDD]e[+-]XX
+  std::string t = buf, digits;
+  const size_t epos = t.find('e');
+  for (size_t i = 0; i < epos; ++i)
+    if (std::isdigit(static_cast<unsigned char>(t[i]))) digits += t[i];
+  const int e10 = std::atoi(t.c_str() + epos + 1);
+  while (digits.size() > 1 && digits.back() == '0') digits.pop_back();
+  const double ax = std::fabs(x);
+  const bool expo = is_f32 ? (float(ax) < 1e-4f || float(ax) >= 1e16f) : (ax < 1e-4 || ax >= 1e16);
+  std::string out = x < 0 ? "-" : "";
+  if (expo) {
+    out += digits.substr(0, 1);
+    if (digits.size() > 1) out += "." + digits.substr(1);
+    out += "e" + std::to_string(e10);
+  } else if (e10 >= 0) {
+    std::string ip = digits.substr(0, std::min<size_t>(digits.size(), size_t(e10) + 1));
+    while (ip.size() < size_t(e10) + 1) ip += '0';
+    const std::string fp = digits.size() > size_t(e10) + 1 ? digits.substr(size_t(e10) + 1) : "0";
+    out += ip + "." + fp;
+  } else {
+    out += "0." + std::string(size_t(-e10 - 1), '0') + digits;
+  }
+  return out;
+}
+
+// Rust's Debug of a str: quoted, with \t \r \n \0 \\ \" escaped and other
+// control characters as \u{..}; other characters as they are.
+std::string rust_str_debug(const std::string& v) {
+  std::string o = "\"";
+  for (unsigned char ch : v) {
+    switch (ch) {
+      case '\t': o += "\\t"; break;
+      case '\r': o += "\\r"; break;
+      case '\n': o += "\\n"; break;
+      case '\0': o += "\\0"; break;
+      case '\\': o += "\\\\"; break;
+      case '"': o += "\\\""; break;
+      default:
+        if (ch < 0x20 || ch == 0x7f) {
+          char b[16];
+          std::snprintf(b, sizeof(b), "\\u{%x}", ch);
+          o += b;
+        } else {
+          o += char(ch);
+        }
+    }
+  }
+  return o + "\"";
+}
+
+// The first `n` characters (Unicode scalar values) of UTF-8 text.
+std::string utf8_prefix(const std::string& v, size_t n) {
+  size_t i = 0, chars = 0;
+  while (i < v.size() && chars < n) {
+    const unsigned char c = static_cast<unsigned char>(v[i]);
+    i += c < 0x80 ? 1 : c < 0xE0 ? 2 : c < 0xF0 ? 3 : 4;
+    ++chars;
+  }
+  return v.substr(0, std::min(i, v.size()));
+}
+
+}  // namespace
+
+std::string gguf_summary(const GgufValue& v) {
+  switch (v.type) {
+    case 0: return "U8(" + std::to_string(v.u) + ")";
+    case 1: return "I8(" + std::to_string(v.i) + ")";
+    case 2: return "U16(" + std::to_string(v.u) + ")";
+    case 3: return "I16(" + std::to_string(v.i) + ")";
+    case 4: return "U32(" + std::to_string(v.u) + ")";
+    case 5: return "I32(" + std::to_string(v.i) + ")";
+    case 6: return "F32(" + rust_float_debug(v.f, true) + ")";
+    case 7: return std::string("Bool(") + (v.u ? "true" : "false") + ")";
+    case 8: {
+      if (v.s.size() > 160)
+        return "string(len=" + std::to_string(v.s.size()) + ", prefix=" + rust_str_debug(utf8_prefix(v.s, 160)) + ")";
+      return "string(" + rust_str_debug(v.s) + ")";
+    }
+    case 9: {
+      std::string o = "array(len=" + std::to_string(v.count) + ", first=[";
+      for (size_t k = 0; k < v.preview.size(); ++k) o += (k ? ", " : "") + gguf_summary(v.preview[k]);
+      return o + "])";
+    }
+    case 10: return "U64(" + std::to_string(v.u) + ")";
+    case 11: return "I64(" + std::to_string(v.i) + ")";
+    case 12: return "F64(" + rust_float_debug(v.f, false) + ")";
+    default: return "?";
+  }
 }
 
 const GgufValue* gguf_meta(const si_gguf* g, const std::string& key) {
@@ -743,6 +859,24 @@ int si_detect_model_format(const char* path, uint32_t* format) {
   }
   return si::fail(nullptr, SI_E_INVALID, std::string("unsupported model container ") + path +
                                              "; expected a Safetensors directory or GGUF file");
+}
+
+
+int si_gguf_meta_key_at(const si_gguf* g, uint64_t index, const char** key) {
+  if (!g || !key || index >= g->meta.size()) return si::fail(nullptr, SI_E_INVALID, "GGUF metadata index out of range");
+  auto it = g->meta.begin();
+  std::advance(it, long(index));
+  *key = it->first.c_str();
+  return SI_OK;
+}
+
+int si_gguf_meta_summary(const si_gguf* g, const char* key, const char** out) {
+  const si::GgufValue* v = g && key ? si::gguf_meta(g, key) : nullptr;
+  if (!v || !out) return si::fail(nullptr, SI_E_INVALID, std::string("GGUF metadata is missing ") + (key ? key : ""));
+  auto& slot = g->summaries[key];
+  if (slot.empty()) slot = si::gguf_summary(*v);
+  *out = slot.c_str();
+  return SI_OK;
 }
 
 }  // extern "C"

@@ -9,15 +9,23 @@ struct si_gguf;
 
 namespace si {
 
-// One metadata value (GgufValue, model.rs:583-600). Arrays keep only their
-// element type and length: decode reads no array contents.
+constexpr uint64_t kGgufPreview = 3;  // array elements kept for the inspection summary
+
+// One metadata value (GgufValue, model.rs:583-600). Arrays keep their element
+// type, their length and their first kGgufPreview elements: decode reads no
+// array contents.
 struct GgufValue {
   uint32_t type = 0, elem_type = 0;
   uint64_t u = 0, count = 0;
   int64_t i = 0;
   double f = 0;
   std::string s;
+  std::vector<GgufValue> preview;
 };
+
+// summarize (src/bin/si-gguf-inspect.rs:84-101) of one value, with Rust's
+// Debug formatting of the variants.
+std::string gguf_summary(const GgufValue& v);
 
 // One tensor-index entry with its resolved byte range (GgufTensorInfo).
 struct GgufTensor {
@@ -42,4 +50,5 @@ struct si_gguf {
   std::map<std::string, si::GgufValue> meta;
   std::vector<si::GgufTensor> tensors;
   std::map<std::string, uint64_t> index;
+  mutable std::map<std::string, std::string> summaries;  // si_gguf_meta_summary results
 };

@@ -144,3 +144,60 @@ def test_cuda_backend_ids_match_the_python_api(mai, ctx):
                    "--max-tokens", "6", "--context", "64", "--warmup", "0", "--repetitions", "1",
                    "--expected-output", expected + " 1")
     assert rc == 2
+
+
+INSPECT = os.path.join(PKG_DIR, "si-gguf-inspect")
+
+
+def inspect(*args):
+    load_package().lib()
+    r = subprocess.run([INSPECT, *args], capture_output=True, text=True, timeout=120)
+    return r.returncode, r.stdout, r.stderr
+
+
+def test_gguf_inspect_report(tmp_path):
+    """si-gguf-inspect (src/bin/si-gguf-inspect.rs): the same lines, sections
+    and value summaries (Rust Debug formatting of the metadata variants)."""
+    import gguf_writer as W
+    meta = [("general.architecture", W.STRING, "qwen35"), ("eps", W.F32, 1e-6), ("theta", W.F32, 1e7),
+            ("f64", W.F64, 0.1), ("big", W.F64, 1.5e20), ("e16", W.F64, 1e16), ("e15", W.F64, 1e15),
+            ("tiny", W.F64, 1e-5), ("quarter", W.F64, 0.0001), ("neg", W.I32, -7), ("flag", W.BOOL, 1),
+            ("long", W.STRING, "x" * 200 + "é"), ("arr", W.ARRAY, (W.STRING, ["a", 'b"q', "c", "d"])),
+            ("nums", W.ARRAY, (W.U16, [1, 2])), ("ctl", W.STRING, "a\tb\x01"), ("none", W.ARRAY, (W.U8, []))]
+    tensors = [(f"blk.{i:02d}.w", [256, 1], 12, bytes(144)) for i in range(14)]
+    tensors += [("output.weight", [256, 2], 14, bytes(420)), ("output_norm.weight", [256], 0, bytes(1024))]
+    path = tmp_path / "m.gguf"
+    W.write(path, meta, tensors)
+    rc, out, _ = inspect("--model", str(path))
+    assert rc == 0
+    lines = out.splitlines()
+    assert lines[0] == f"model={path}" and lines[1] == "tensors=16"
+    q4 = [l for l in lines if l.startswith("q4_k_tensor=")]
+    assert len(q4) == 12 and q4[0] == "q4_k_tensor=blk.00.w shape=[256, 1] bytes=160 elements=256"
+    assert "tensor_type_counts={0: 1, 12: 14, 14: 1}" in lines
+    assert "special_tensor=output.weight type=14 shape=[256, 2] bytes=448" in lines
+    assert "special_tensor=output_norm.weight type=0 shape=[256] bytes=1024" in lines
+    assert [l for l in lines if l.startswith("non_q4_tensor=")] == [
+        "non_q4_tensor=output.weight type=14 shape=[256, 2] bytes=448",
+        "non_q4_tensor=output_norm.weight type=0 shape=[256] bytes=1024"]
+    md = dict(l[len("metadata."):].split("=", 1) for l in lines if l.startswith("metadata."))
+    assert list(md) == sorted(md)
+    assert md["general.architecture"] == 'string("qwen35")'
+    assert md["eps"] == "F32(1e-6)" and md["theta"] == "F32(10000000.0)"
+    assert md["f64"] == "F64(0.1)" and md["big"] == "F64(1.5e20)" and md["e16"] == "F64(1e16)"
+    assert md["e15"] == "F64(1000000000000000.0)" and md["tiny"] == "F64(1e-5)" and md["quarter"] == "F64(0.0001)"
+    assert md["neg"] == "I32(-7)" and md["flag"] == "Bool(true)"
+    assert md["long"] == 'string(len=202, prefix="' + "x" * 160 + '")'
+    assert md["arr"] == 'array(len=4, first=[string("a"), string("b\\"q"), string("c")])'
+    assert md["nums"] == "array(len=2, first=[U16(1), U16(2)])" and md["none"] == "array(len=0, first=[])"
+    assert md["ctl"] == 'string("a\\tb\\u{1}")'
+
+
+def test_gguf_inspect_usage_and_errors(tmp_path):
+    for args in ([], ["--model"], ["--path", "x"], ["--model", "a", "--other", "b"]):
+        rc, _, err = inspect(*args)
+        assert rc == 2 and "Usage: si-gguf-inspect --model PATH" in err
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"NOPE")
+    rc, _, err = inspect("--model", str(bad))
+    assert rc == 1 and "error: GGUF header has invalid magic" in err

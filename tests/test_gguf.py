@@ -325,3 +325,14 @@ def test_expected_payload_bytes(mai, tmp_path):  # GgufTensorInfo::expected_payl
         assert got == [(15, 60), (7, 14), (4, 8), (1536, 864), (256, 176), (512, 420), (32, None)]
         with pytest.raises(mai.SiError, match="GGUF Q4_K tensor bad_q4 has 100 elements; expected a multiple of 256"):
             g.tensor_payload(7)
+
+
+def test_metadata_summaries(mai, tmp_path):
+    data = W.build(kat_metadata(), [])
+    with open_bytes(mai, tmp_path, data) as g:
+        md = g.metadata()
+    assert list(md) == sorted(md)
+    assert md["qwen35.embedding_length"] == "U32(5120)"
+    assert md["qwen35.attention.layer_norm_rms_epsilon"] == "F32(1e-6)"
+    assert md["qwen35.rope.freq_base"] == "F32(10000000.0)"
+    assert md["tokenizer.ggml.tokens"] == 'array(len=248320, first=[string("a"), string("a"), string("a")])'
