@@ -330,6 +330,15 @@ int si_model_shard_rows(const si_model_config* c, int nranks, int rank, uint32_t
 int si_model_host_tensor(const si_model* m, uint32_t layer, uint32_t tensor, const void** ptr,
                          uint64_t* bytes, uint32_t* ggml_type);
 int si_model_reset(si_model* m);                     /* Qwen35Runtime::reset */
+/* snapshot_states / restore_states (qwen35_runtime.rs:1764-1775): a device
+ * copy of every layer's recurrent, conv and KV state with the token counts,
+ * for rolling a speculative window back (si-qwen35-spec-probe.rs:155-169).
+ * Restoring into a model of another layout or context is refused with
+ * SI_E_INVALID. Free a snapshot before its context. */
+typedef struct si_model_snapshot si_model_snapshot;
+int si_model_snapshot_states(si_model* m, si_model_snapshot** out);
+int si_model_restore_states(si_model* m, const si_model_snapshot* s);
+void si_model_snapshot_free(si_model_snapshot* s);
 /* embed_token (qwen35_runtime.rs:2122). */
 int si_model_embed(si_model* m, uint32_t token, float* hidden_out);
 /* decode_hidden (qwen35_runtime.rs:1776): hidden is read and overwritten. */

@@ -190,6 +190,9 @@ def lib():
         "si_model_shard_rows": ([vp, i32, i32, u32, u32, vp, u32, vp], i32),
         "si_model_host_tensor": ([vp, u32, u32, vp, vp, vp], i32),
         "si_model_reset": ([vp], i32),
+        "si_model_snapshot_states": ([vp, vp], i32),
+        "si_model_restore_states": ([vp, vp], i32),
+        "si_model_snapshot_free": ([vp], None),
         "si_model_embed": ([vp, u32, vp], i32),
         "si_model_decode_hidden": ([vp, u64, vp], i32),
         "si_model_logits": ([vp, vp, vp], i32),
@@ -860,6 +863,34 @@ def plan_sequential_layers(layers, budget_bytes: int) -> Trace:
     return Trace(handle=h.value)
 
 
+class StateSnapshot:
+    """A model's layer states at one point of decoding (si_model_snapshot).
+    It holds a reference to its context. If that context was closed first,
+    close() only drops the handle: the device copy stays allocated until the
+    process exits, because freeing it would touch the destroyed context."""
+
+    def __init__(self, ctx: "CudaContext", handle):
+        self.ctx, self.h = ctx, handle
+
+    def close(self):
+        if getattr(self, "h", None):
+            if getattr(self.ctx, "h", None):
+                lib().si_model_snapshot_free(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class Model:
     """Synthetic Qwen3.6-shaped decoder (Qwen35Runtime, qwen35_runtime.rs:1519-2267)."""
 
@@ -913,6 +944,17 @@ class Model:
 
     def reset(self):
         self.ctx._ck(lib().si_model_reset(self.h))
+
+    def snapshot_states(self) -> "StateSnapshot":
+        """Qwen35Runtime::snapshot_states: a device copy of every layer's
+        recurrent, conv and KV state (qwen35_runtime.rs:1764-1766)."""
+        h = C.c_void_p()
+        self.ctx._ck(lib().si_model_snapshot_states(self.h, C.byref(h)))
+        return StateSnapshot(self.ctx, h.value)
+
+    def restore_states(self, snapshot: "StateSnapshot"):
+        """Qwen35Runtime::restore_states (qwen35_runtime.rs:1768-1775)."""
+        self.ctx._ck(lib().si_model_restore_states(self.h, snapshot.h))
 
     def embed_token(self, token_id: int) -> np.ndarray:
         out = np.empty(self.config.hidden, np.float32)

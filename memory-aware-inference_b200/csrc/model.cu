@@ -949,6 +949,68 @@ extern "C" int si_model_reset(si_model* m) {
   return sync_and_check(m->ctx, "model reset");
 }
 
+// Qwen35Runtime::snapshot_states / restore_states (qwen35_runtime.rs:1764-1775):
+// the whole state block (conv and recurrent states, KV caches) copied device
+// to device on the context's stream, with the per-layer token counts and conv
+// parities kept on the host. The weights, the ring and the verifier's hidden
+// states are not part of it, as in the reference.
+struct si_model_snapshot {
+  si_ctx* ctx = nullptr;
+  uint8_t* block = nullptr;
+  uint64_t bytes = 0;
+  std::vector<uint32_t> cached, conv_parity;
+};
+
+extern "C" int si_model_snapshot_states(si_model* m, si_model_snapshot** out) {
+  if (!m || !out) return SI_E_INVALID;
+  *out = nullptr;
+  si_ctx* ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  auto* s = new si_model_snapshot();
+  s->ctx = ctx;
+  s->bytes = m->plan.state_bytes;
+  s->cached = m->cached;
+  s->conv_parity = m->conv_parity;
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&s->block), s->bytes ? s->bytes : 256);
+  if (e != cudaSuccess) {
+    s->block = nullptr;
+    delete s;
+    return cuda_fail(ctx, e, "state snapshot allocation");
+  }
+  note_alloc(ctx, int64_t(s->bytes));
+  e = cudaMemcpyAsync(s->block, m->state_block, s->bytes, cudaMemcpyDeviceToDevice, ctx->stream);
+  const int rc = e != cudaSuccess ? cuda_fail(ctx, e, "state snapshot copy") : sync_and_check(ctx, "state snapshot");
+  if (rc) {
+    si_model_snapshot_free(s);
+    return rc;
+  }
+  *out = s;
+  return SI_OK;
+}
+
+extern "C" int si_model_restore_states(si_model* m, const si_model_snapshot* s) {
+  if (!m || !s) return SI_E_INVALID;
+  si_ctx* ctx = m->ctx;
+  if (s->ctx != ctx || s->bytes != m->plan.state_bytes || s->cached.size() != m->cached.size())
+    return fail(ctx, SI_E_INVALID, "Qwen3.6 state snapshot depth does not match runtime");
+  cudaSetDevice(ctx->device);
+  cudaError_t e = cudaMemcpyAsync(m->state_block, s->block, s->bytes, cudaMemcpyDeviceToDevice, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "state restore copy");
+  m->cached = s->cached;
+  m->conv_parity = s->conv_parity;
+  return sync_and_check(ctx, "state restore");
+}
+
+extern "C" void si_model_snapshot_free(si_model_snapshot* s) {
+  if (!s) return;
+  if (s->block) {
+    cudaSetDevice(s->ctx->device);
+    cudaFree(s->block);
+    note_alloc(s->ctx, -int64_t(s->bytes));
+  }
+  delete s;
+}
+
 namespace {
 
 // ---- staging ring ------------------------------------------------------------

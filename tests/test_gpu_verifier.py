@@ -3,6 +3,8 @@
 verify_many of a small model against sequential decode by the oracle and by
 the GPU itself (qwen35_runtime.rs:879-1289, 2048-2227; the reference's
 si-qwen35-batch-probe compares the same pair)."""
+import gc
+
 import numpy as np
 import pytest
 
@@ -177,3 +179,57 @@ def test_window_overflowing_the_kv_cache_is_refused_without_state_change(mai, ct
         a.verify_many(list(range(9)), list(range(9)))
     a.close()
     b.close()
+
+
+def test_snapshot_restore_rolls_a_speculative_window_back(mai, ctx):
+    """The speculative probes' loop (si-qwen35-spec-probe.rs:155-169):
+    snapshot the states, verify a window, restore. Decoding then continues
+    like a model that never saw the window, and the snapshot restores again."""
+    cfg = small_config(mai)
+    a, b = mai.Model(ctx, cfg, seed=13), mai.Model(ctx, cfg, seed=13)
+    prompt = [7, 70, 700]
+    prefill(a, prompt)
+    prefill(b, prompt)
+    pos = len(prompt)
+    gc.collect()  # no earlier test's objects are freed inside the measured span
+    before = ctx.stats()["current_allocated_bytes"]
+    snap = a.snapshot_states()
+    assert ctx.stats()["current_allocated_bytes"] == before + a.plan()["state_bytes"]
+    window = [11, 12, 13, 14, 15]
+    positions = list(range(pos, pos + len(window)))
+    a.verify_many(window, positions)
+    a.restore_states(snap)
+    # the window's keys and values stay in the cache past the restored token
+    # count; attention never reads them, so ids are exact and logits agree
+    for k, tok in enumerate([11, 12, 99, 5]):
+        na, la = a.decode_token(tok, pos + k)
+        nb, lb = b.decode_token(tok, pos + k)
+        assert na == nb, k
+        assert rel_l2(la, lb) < 1e-6, k
+    a.restore_states(snap)
+    b.reset()
+    prefill(b, prompt)
+    ids_a, lo_a = a.verify_many(window, positions, want_logits=True)
+    ids_b, lo_b = b.verify_many(window, positions, want_logits=True)
+    assert ids_a == ids_b
+    assert max(rel_l2(lo_a[k], lo_b[k]) for k in range(len(window))) < 1e-6
+    snap.close()
+    assert ctx.stats()["current_allocated_bytes"] == before
+    a.close()
+    b.close()
+
+
+def test_snapshot_of_another_layout_is_refused(mai, ctx):
+    """restore_states refuses a snapshot of a different depth
+    (qwen35_runtime.rs:1768-1772) and leaves the model usable."""
+    a = mai.Model(ctx, small_config(mai), seed=2)
+    b = mai.Model(ctx, small_config(mai, layers=4), seed=2)
+    snap = b.snapshot_states()
+    with pytest.raises(mai.SiError, match="snapshot depth does not match") as e:
+        a.restore_states(snap)
+    assert e.value.status == mai.SI_E_INVALID
+    ref = mai.Model(ctx, small_config(mai), seed=2)
+    assert a.decode_token(3, 0)[0] == ref.decode_token(3, 0)[0]
+    snap.close()
+    for m in (a, b, ref):
+        m.close()
