@@ -298,6 +298,32 @@ typedef struct si_plan_info {
   uint32_t resident_layers, streamed_layers, stage_depth, head_resident;
 } si_plan_info;
 
+/* Which layers stay resident in HBM: the layer-granular forms of the
+ * reference's residency selection (new_with_retained_layers_and_head,
+ * qwen35_runtime.rs:1552-1733). A layer is retained when it is one of the
+ * first `prefix_layers` (retained_layers), when stride != 0 and
+ * layer % stride == offset % stride (retains_stride_layer, 2270-2272), or when
+ * it is listed in `layers` (SI_RETAIN_FULL_LAYERS, parse_layer_set 2275-2280).
+ * The output head is always resident. Without SI_RETAIN_EXACT the remaining
+ * budget is filled with further leading layers, and a model that fits whole
+ * stays whole; with it every other layer streams through the ring, as in the
+ * reference. A retained set that the budget cannot hold beside the head, the
+ * ring, state and scratch is refused with SI_E_BUDGET; a listed layer past the
+ * model's depth with SI_E_INVALID. The reference's tensor-level forms (gate/up
+ * only, down only, attention only, Q6_K tensors only) are not offered: the ring
+ * streams whole packed layers. */
+typedef struct si_retention {
+  uint32_t prefix_layers;
+  uint32_t stride, offset;
+  const uint32_t* layers; /* may be NULL when n_layers is 0 */
+  uint32_t n_layers;
+  uint32_t flags;         /* SI_RETAIN_* */
+} si_retention;
+#define SI_RETAIN_EXACT 1u
+/* The policy for models created on `ctx` afterwards; NULL restores the
+ * default (the budget-filled prefix). */
+int si_ctx_set_retention(si_ctx* ctx, const si_retention* r);
+
 /* Fill a config with the BASELINE 27B shape (hidden 5120, 64 layers, ...). */
 void si_model_config_qwen36_27b(si_model_config* c);
 /* Build a model with seeded synthetic weights in pinned host memory, plan
@@ -320,6 +346,14 @@ int si_model_plan(const si_model* m, si_plan_info* out);
  * run, plan_sequential_layers' budget check, planner.rs:174-251). */
 int si_model_plan_dry(const si_model_config* c, int nranks, int rank, uint64_t budget,
                       uint32_t stage_depth, si_plan_info* out);
+/* The dry run under a retention policy (NULL: the default). resident, when
+ * not NULL, receives c->layers flags: 1 for a resident layer, 0 for a
+ * streamed one. */
+int si_model_plan_dry_retained(const si_model_config* c, int nranks, int rank, uint64_t budget,
+                               uint32_t stage_depth, const si_retention* r, si_plan_info* out,
+                               uint8_t* resident);
+/* Which layers of a created model are resident (layers flags, as above). */
+int si_model_resident_layers(const si_model* m, uint8_t* resident, uint32_t layers);
 /* Full-tensor row ranges [begin, end) that rank `rank` of `nranks` holds of a
  * tensor (ranges: 2*max_ranges u64). No device needed. */
 int si_model_shard_rows(const si_model_config* c, int nranks, int rank, uint32_t layer,

@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import re
 from dataclasses import dataclass
 
 import numpy as np
@@ -116,6 +117,38 @@ class SiPlanInfo(C.Structure):
         return {k: getattr(self, k) for k, _ in self._fields_}
 
 
+class SiRetention(C.Structure):
+    _fields_ = [("prefix_layers", C.c_uint32), ("stride", C.c_uint32), ("offset", C.c_uint32),
+                ("layers", C.POINTER(C.c_uint32)), ("n_layers", C.c_uint32), ("flags", C.c_uint32)]
+
+
+RETAIN_EXACT = 1
+
+
+def retention(prefix_layers: int = 0, stride: int = 0, offset: int = 0, layers=(), exact: bool = False):
+    """A whole-layer retention policy (si_retention): the first
+    `prefix_layers` layers (retained_layers), every layer with
+    layer % stride == offset % stride (retains_stride_layer), and the listed
+    `layers` (SI_RETAIN_FULL_LAYERS) stay resident; `exact` streams all
+    others (qwen35_runtime.rs:1552-1733, 2270-2280)."""
+    arr = (C.c_uint32 * max(len(layers), 1))(*layers)
+    r = SiRetention(prefix_layers, stride, offset, C.cast(arr, C.POINTER(C.c_uint32)), len(layers),
+                    RETAIN_EXACT if exact else 0)
+    r._keep = arr
+    return r
+
+
+def parse_layer_set(text: str) -> list:
+    """parse_layer_set (qwen35_runtime.rs:2275-2280): comma-separated layer
+    numbers; items that are not numbers are skipped; sorted, no repeats."""
+    out = set()
+    for item in text.split(","):
+        item = item.strip()
+        if re.fullmatch(r"\+?[0-9]+", item):  # what usize's FromStr accepts
+            out.add(int(item))
+    return sorted(out)
+
+
 _lib = None
 
 
@@ -187,6 +220,9 @@ def lib():
         "si_model_destroy": ([vp], None),
         "si_model_plan": ([vp, vp], i32),
         "si_model_plan_dry": ([vp, i32, i32, u64, u32, vp], i32),
+        "si_model_plan_dry_retained": ([vp, i32, i32, u64, u32, vp, vp, vp], i32),
+        "si_model_resident_layers": ([vp, vp, u32], i32),
+        "si_ctx_set_retention": ([vp, vp], i32),
         "si_model_shard_rows": ([vp, i32, i32, u32, u32, vp, u32, vp], i32),
         "si_model_host_tensor": ([vp, u32, u32, vp, vp, vp], i32),
         "si_model_reset": ([vp], i32),
@@ -374,6 +410,11 @@ class CudaContext:
 
     def reset_peaks(self):
         self._ck(lib().si_reset_peaks(self.h))
+
+    def set_retention(self, retention: "SiRetention" = None):
+        """The retention policy of models created on this context afterwards
+        (si_ctx_set_retention); None restores the budget-filled prefix."""
+        self._ck(lib().si_ctx_set_retention(self.h, C.byref(retention) if retention is not None else None))
 
     def comm_init(self, nranks: int, rank: int, uid: bytes):
         buf = C.create_string_buffer(bytes(uid), 128)
@@ -669,13 +710,20 @@ def qwen36_27b_config(**overrides) -> SiModelConfig:
     return c
 
 
-def plan_dry(config: SiModelConfig, nranks: int = 1, rank: int = 0, budget: int = 0, stage_depth: int = 3) -> dict:
-    """Residency plan of a model without a device (si_model_plan_dry)."""
+def plan_dry(config: SiModelConfig, nranks: int = 1, rank: int = 0, budget: int = 0, stage_depth: int = 3,
+             retention: SiRetention = None) -> dict:
+    """Residency plan of a model without a device (si_model_plan_dry, or
+    si_model_plan_dry_retained under a retention policy). The dict carries
+    the per-layer residency as `resident` (a list of bools)."""
     p = SiPlanInfo()
-    rc = lib().si_model_plan_dry(C.byref(config), nranks, rank, budget, stage_depth, C.byref(p))
+    flags = (C.c_uint8 * max(config.layers, 1))()
+    rc = lib().si_model_plan_dry_retained(C.byref(config), nranks, rank, budget, stage_depth,
+                                          C.byref(retention) if retention is not None else None, C.byref(p), flags)
     if rc != 0:
         raise SiError(rc, lib().si_global_last_error().decode())
-    return p.as_dict()
+    d = p.as_dict()
+    d["resident"] = [bool(flags[i]) for i in range(config.layers)]
+    return d
 
 
 def shard_rows(config: SiModelConfig, nranks: int, rank: int, layer: int, tensor: int):
@@ -929,6 +977,12 @@ class Model:
         p = SiPlanInfo()
         self.ctx._ck(lib().si_model_plan(self.h, C.byref(p)))
         return p.as_dict()
+
+    def resident_layers(self) -> list:
+        """Per layer, whether it is resident in HBM (si_model_resident_layers)."""
+        flags = (C.c_uint8 * max(self.config.layers, 1))()
+        self.ctx._ck(lib().si_model_resident_layers(self.h, flags, self.config.layers))
+        return [bool(flags[i]) for i in range(self.config.layers)]
 
     def host_tensor(self, layer: int, tensor: int):
         """(address, bytes, ggml_type) of this rank's pinned host copy of a tensor."""

@@ -40,6 +40,14 @@ struct DevBuf {
   T* as() const { return static_cast<T*>(p); }
 };
 
+// Whole-layer retention policy of the models created on a context
+// (si_ctx_set_retention); `set` false = the budget-filled prefix.
+struct Retention {
+  bool set = false;
+  uint32_t prefix = 0, stride = 0, offset = 0, flags = 0;
+  std::vector<uint32_t> layers;
+};
+
 }  // namespace si
 
 struct si_ctx {
@@ -71,6 +79,7 @@ struct si_ctx {
   // NCCL (optional)
   si_comm_state* comm = nullptr;
   int nranks = 1, rank = 0;
+  si::Retention retention;
 };
 
 namespace si {

@@ -371,12 +371,35 @@ uint64_t batch_bytes(const si_model& m) {
   return b + 3 * 256 + align256(batch_qmm_bytes(m));  // keys, ids, tokens, matvec scratch
 }
 
+// The C struct of a retention policy as the context keeps it (NULL: none).
+int retention_from(const si_retention* r, Retention* out, std::string* err) {
+  *out = Retention{};
+  if (!r) return SI_OK;
+  if (r->n_layers && !r->layers) {
+    *err = "retention policy lists layers without an array";
+    return SI_E_INVALID;
+  }
+  if (r->flags & ~SI_RETAIN_EXACT) {
+    *err = "unknown retention flags " + std::to_string(r->flags);
+    return SI_E_INVALID;
+  }
+  out->set = true;
+  out->prefix = r->prefix_layers;
+  out->stride = r->stride;
+  out->offset = r->offset;
+  out->flags = r->flags;
+  out->layers.assign(r->layers, r->layers + r->n_layers);
+  return SI_OK;
+}
+
 // Residency plan inside `budget` (0 = unbounded): the output head and as many
 // leading layers as fit stay resident (the reference's retained prefix,
 // qwen35_runtime.rs:1640-1642); the rest stream through `depth` ring slots of
-// the largest layer. Like plan_sequential_layers (planner.rs:174-251) a plan
-// whose fixed part exceeds the budget is rejected. Pure host code.
-int compute_plan(si_model* m, uint64_t budget, uint32_t depth, std::vector<bool>* res_out,
+// the largest layer. A retention policy (si_ctx_set_retention) names layers
+// that must stay resident first; with SI_RETAIN_EXACT nothing else does. Like
+// plan_sequential_layers (planner.rs:174-251) a plan whose fixed part exceeds
+// the budget is rejected. Pure host code.
+int compute_plan(si_model* m, uint64_t budget, uint32_t depth, const Retention* ret, std::vector<bool>* res_out,
                  uint64_t* max_layer_out, std::string* err) {
   const si_model_config& c = m->c;
   m->depth = depth ? std::min(depth, 4u) : 3u;
@@ -397,27 +420,70 @@ int compute_plan(si_model* m, uint64_t budget, uint32_t depth, std::vector<bool>
     all_layers += m->layout[l].bytes;
   }
   const uint64_t globals_bytes = m->layout[c.layers].bytes;
+  // the policy's layers (retained_layers, retains_stride_layer, the explicit
+  // set; qwen35_runtime.rs:1552-1733, 2270-2280)
+  std::vector<bool> want(c.layers, false);
+  const bool policy = ret && ret->set, exact = policy && (ret->flags & SI_RETAIN_EXACT);
+  uint64_t want_bytes = 0;
+  uint32_t n_want = 0;
+  if (policy) {
+    for (uint32_t l : ret->layers)
+      if (l >= c.layers) {
+        *err = "retained layer " + std::to_string(l) + " is outside the model's " + std::to_string(c.layers) +
+               " layers";
+        return SI_E_INVALID;
+      }
+    for (uint32_t l = 0; l < c.layers; ++l)
+      want[l] = l < ret->prefix || (ret->stride && l % ret->stride == ret->offset % ret->stride);
+    for (uint32_t l : ret->layers) want[l] = true;
+    for (uint32_t l = 0; l < c.layers; ++l)
+      if (want[l]) {
+        want_bytes += m->layout[l].bytes;
+        n_want++;
+      }
+  }
   uint64_t resident = globals_bytes;
   std::vector<bool> res(c.layers, false);
   bool ring = false;
-  if (budget == 0 || globals_bytes + all_layers + state_bytes + scratch_bytes <= budget) {
+  const uint64_t whole = globals_bytes + all_layers + state_bytes + scratch_bytes;
+  if ((!exact && (budget == 0 || whole <= budget)) || (exact && n_want == c.layers)) {
+    if (budget != 0 && whole > budget) {
+      *err = "HBM budget " + std::to_string(budget) + " B cannot hold the retained layers, the output head, " +
+             "state and scratch (" + std::to_string(whole) + " B)";
+      return SI_E_BUDGET;
+    }
     std::fill(res.begin(), res.end(), true);
     resident += all_layers;
   } else {
     ring = true;
     const uint64_t fixed = globals_bytes + m->depth * max_layer + state_bytes + scratch_bytes;
-    if (fixed > budget) {
+    if (budget != 0 && fixed > budget) {
       *err = "HBM budget " + std::to_string(budget) + " B cannot hold the output head, " +
              std::to_string(m->depth) + " staging slots of " + std::to_string(max_layer) +
              " B, state and scratch (" + std::to_string(fixed) + " B)";
       return SI_E_BUDGET;
     }
-    uint64_t left = budget - fixed;
-    for (uint32_t l = 0; l < c.layers; ++l) {
-      if (m->layout[l].bytes > left) break;
-      res[l] = true;
-      left -= m->layout[l].bytes;
-      resident += m->layout[l].bytes;
+    uint64_t left = budget == 0 ? UINT64_MAX : budget - fixed;
+    if (want_bytes > left) {
+      *err = "HBM budget " + std::to_string(budget) + " B leaves " + std::to_string(left) +
+             " B beside the output head, ring, state and scratch, but the " + std::to_string(n_want) +
+             " retained layers need " + std::to_string(want_bytes) + " B";
+      return SI_E_BUDGET;
+    }
+    left -= want_bytes;
+    for (uint32_t l = 0; l < c.layers; ++l)
+      if (want[l]) {
+        res[l] = true;
+        resident += m->layout[l].bytes;
+      }
+    if (!exact) {
+      for (uint32_t l = 0; l < c.layers; ++l) {
+        if (res[l]) continue;
+        if (m->layout[l].bytes > left) break;
+        res[l] = true;
+        left -= m->layout[l].bytes;
+        resident += m->layout[l].bytes;
+      }
     }
   }
   m->plan = si_plan_info{};
@@ -532,7 +598,8 @@ int create_model(si_ctx* ctx, const si_model_config* cfg, uint64_t seed,
   uint64_t max_layer = 0;
   {
     std::string perr;
-    if (int prc = compute_plan(m, ctx->cfg.hbm_budget_bytes, ctx->cfg.stage_depth, &res, &max_layer, &perr)) {
+    if (int prc = compute_plan(m, ctx->cfg.hbm_budget_bytes, ctx->cfg.stage_depth, &ctx->retention, &res,
+                               &max_layer, &perr)) {
       free_model(m);
       return fail(ctx, prc, perr);
     }
@@ -862,6 +929,12 @@ extern "C" void si_model_destroy(si_model* m) { free_model(m); }
 
 extern "C" int si_model_plan_dry(const si_model_config* cfg, int nranks, int rank, uint64_t budget,
                                  uint32_t depth, si_plan_info* out) {
+  return si_model_plan_dry_retained(cfg, nranks, rank, budget, depth, nullptr, out, nullptr);
+}
+
+extern "C" int si_model_plan_dry_retained(const si_model_config* cfg, int nranks, int rank, uint64_t budget,
+                                          uint32_t depth, const si_retention* r, si_plan_info* out,
+                                          uint8_t* resident) {
   if (!cfg || !out || nranks < 1 || rank < 0 || rank >= nranks)
     return fail(nullptr, SI_E_INVALID, "invalid plan arguments");
   if (int v = validate_config(*cfg, nranks))
@@ -874,8 +947,28 @@ extern "C" int si_model_plan_dry(const si_model_config* cfg, int nranks, int ran
   std::vector<bool> res;
   uint64_t max_layer = 0;
   std::string err;
-  if (int rc = compute_plan(&m, budget, depth, &res, &max_layer, &err)) return fail(nullptr, rc, err);
+  Retention ret;
+  if (int rc = retention_from(r, &ret, &err)) return fail(nullptr, rc, err);
+  if (int rc = compute_plan(&m, budget, depth, &ret, &res, &max_layer, &err)) return fail(nullptr, rc, err);
   *out = m.plan;
+  if (resident)
+    for (uint32_t l = 0; l < cfg->layers; ++l) resident[l] = res[l] ? 1 : 0;
+  return SI_OK;
+}
+
+extern "C" int si_model_resident_layers(const si_model* m, uint8_t* resident, uint32_t layers) {
+  if (!m || !resident) return SI_E_INVALID;
+  if (layers != m->c.layers) return fail(m->ctx, SI_E_INVALID, "resident-layer query needs one flag per layer");
+  for (uint32_t l = 0; l < layers; ++l) resident[l] = m->dev_layer[l] ? 1 : 0;
+  return SI_OK;
+}
+
+extern "C" int si_ctx_set_retention(si_ctx* ctx, const si_retention* r) {
+  if (!ctx) return SI_E_INVALID;
+  Retention ret;
+  std::string err;
+  if (int rc = retention_from(r, &ret, &err)) return fail(ctx, rc, err);
+  ctx->retention = std::move(ret);
   return SI_OK;
 }
 

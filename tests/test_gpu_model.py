@@ -70,6 +70,22 @@ def test_streamed_layers_give_identical_ids(mai, ctx, small_model):
     c2.close()
 
 
+def test_interleaved_retention_gives_identical_ids(mai, ctx, small_model):
+    """Resident layers between streamed ones (retention policy: layers 1 and
+    2 mod 4, nothing else resident): the ring skips the resident layers and
+    decoding matches the fully resident model."""
+    c2 = mai.CudaContext(0, stage_depth=2)
+    c2.set_retention(mai.retention(stride=4, offset=1, layers=[6], exact=True))
+    m2 = mai.Model(c2, small_config(mai), seed=1234)
+    assert m2.resident_layers() == [l % 4 == 1 or l == 6 for l in range(8)]
+    assert m2.plan()["streamed_layers"] == 5 and m2.plan()["stage_depth"] == 2
+    small_model.reset()
+    prompt = [3, 141, 59, 2653]
+    assert m2.generate(prompt, 12) == small_model.generate(prompt, 12)
+    m2.close()
+    c2.close()
+
+
 def test_budget_too_small_is_rejected(mai):
     import mai_b200 as M
     c2 = mai.CudaContext(0, hbm_budget_bytes=1 << 20)

@@ -1,0 +1,110 @@
+"""Whole-layer retention policies of the residency plan (si_retention; the
+layer-granular forms of new_with_retained_layers_and_head,
+qwen35_runtime.rs:1552-1733, retains_stride_layer 2270-2272 and
+parse_layer_set 2275-2280). The plan is host code, so these run on CPU
+through the dry planner."""
+import pytest
+
+from conftest import load_package
+
+GB = 1 << 30
+
+
+@pytest.fixture(scope="module")
+def mai():
+    return load_package()
+
+
+@pytest.fixture(scope="module")
+def cfg(mai):
+    return mai.qwen36_27b_config()
+
+
+@pytest.fixture(scope="module")
+def whole(mai, cfg):
+    return mai.plan_dry(cfg)
+
+
+def test_default_is_the_budget_filled_prefix(mai, cfg):
+    p = mai.plan_dry(cfg, budget=4 * GB)
+    q = mai.plan_dry(cfg, budget=4 * GB, retention=None)
+    assert p == q
+    n = p["resident_layers"]
+    assert p["resident"] == [l < n for l in range(cfg.layers)] and p["streamed_layers"] == 55
+
+
+def test_exact_prefix_streams_every_other_layer(mai, cfg, whole):
+    """retained_layers = 3 and nothing else: the reference's
+    new_with_retained_layers_and_head(.., 3, true)."""
+    p = mai.plan_dry(cfg, retention=mai.retention(prefix_layers=3, exact=True))
+    assert p["resident"] == [l < 3 for l in range(cfg.layers)]
+    assert p["streamed_layers"] == 61 and p["stage_depth"] == 3 and p["ring_bytes"] > 0
+    # every layer's bytes are either resident or streamed once per token
+    assert p["resident_weight_bytes"] + p["streamed_bytes_per_token"] == whole["resident_weight_bytes"]
+
+
+def test_stride_retains_every_fourth_layer(mai, cfg):
+    """stride 4, offset 7 keeps layers with l % 4 == 3: the attention layers."""
+    p = mai.plan_dry(cfg, retention=mai.retention(stride=4, offset=7, exact=True))
+    assert p["resident"] == [l % 4 == 3 for l in range(cfg.layers)]
+    assert p["resident_layers"] == 16
+
+
+def test_explicit_layer_set(mai, cfg):
+    layers = mai.parse_layer_set("0, 5,x,63,5,,+7, -1, 2.0")
+    assert layers == [0, 5, 7, 63]
+    p = mai.plan_dry(cfg, retention=mai.retention(layers=layers, exact=True))
+    assert [l for l in range(cfg.layers) if p["resident"][l]] == [0, 5, 7, 63]
+
+
+def test_union_of_prefix_stride_and_set(mai, cfg):
+    r = mai.retention(prefix_layers=2, stride=16, offset=0, layers=[40], exact=True)
+    p = mai.plan_dry(cfg, retention=r)
+    assert [l for l in range(cfg.layers) if p["resident"][l]] == [0, 1, 16, 32, 40, 48]
+
+
+def test_non_exact_policy_fills_the_budget_after_the_set(mai, cfg):
+    base = mai.plan_dry(cfg, budget=4 * GB)
+    p = mai.plan_dry(cfg, budget=4 * GB, retention=mai.retention(layers=[63]))
+    assert p["resident"][63]
+    lead = [l for l in range(63) if p["resident"][l]]
+    assert lead == list(range(len(lead)))  # then a prefix, as far as it fits
+    assert len(lead) <= base["resident_layers"]
+    fixed = p["resident_weight_bytes"] + p["ring_bytes"] + p["state_bytes"] + p["scratch_bytes"]
+    assert fixed <= 4 * GB
+
+
+def test_non_exact_policy_keeps_a_model_that_fits_whole(mai, cfg, whole):
+    p = mai.plan_dry(cfg, retention=mai.retention(prefix_layers=1))
+    assert p["streamed_layers"] == 0 and p["ring_bytes"] == 0 and p == {**whole, "resident": p["resident"]}
+
+
+def test_exact_policy_of_every_layer_needs_no_ring(mai, cfg):
+    p = mai.plan_dry(cfg, retention=mai.retention(prefix_layers=cfg.layers, exact=True))
+    assert p["streamed_layers"] == 0 and p["ring_bytes"] == 0 and p["stage_depth"] == 0
+    with pytest.raises(mai.SiError, match="cannot hold the retained layers") as e:
+        mai.plan_dry(cfg, budget=4 * GB, retention=mai.retention(prefix_layers=cfg.layers, exact=True))
+    assert e.value.status == mai.SI_E_BUDGET
+
+
+def test_retained_set_over_budget_is_refused(mai, cfg):
+    with pytest.raises(mai.SiError, match="retained layers need") as e:
+        mai.plan_dry(cfg, budget=4 * GB, retention=mai.retention(prefix_layers=20))
+    assert e.value.status == mai.SI_E_BUDGET
+
+
+def test_invalid_policies_are_refused(mai, cfg):
+    with pytest.raises(mai.SiError, match="outside the model's 64 layers") as e:
+        mai.plan_dry(cfg, retention=mai.retention(layers=[64]))
+    assert e.value.status == mai.SI_E_INVALID
+    r = mai.retention()
+    r.flags = 6
+    with pytest.raises(mai.SiError, match="unknown retention flags"):
+        mai.plan_dry(cfg, retention=r)
+
+
+def test_every_rank_retains_the_same_layers(mai, cfg):
+    r = mai.retention(stride=8, offset=1, exact=True)
+    flags = {mai.plan_dry(cfg, n, k, 0, 3, r)["resident"] == [l % 8 == 1 for l in range(cfg.layers)]
+             for n in (1, 2, 4, 8) for k in range(n)}
+    assert flags == {True}
