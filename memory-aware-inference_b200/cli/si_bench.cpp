@@ -318,21 +318,6 @@ Measured generate(si_ctx* ctx, si_model* m, const std::vector<uint32_t>& prompt,
   return r;
 }
 
-// The smallest budget whose plan keeps the first `layers` layers resident.
-uint64_t budget_for_layers(const si_model_config& c, uint64_t layers, uint32_t depth) {
-  si_plan_info all;
-  check(si_model_plan_dry(&c, 1, 0, 0, depth, &all), nullptr, "plan");
-  if (layers >= all.resident_layers) return 0;
-  uint64_t lo = 1, hi = all.resident_weight_bytes + all.state_bytes + all.scratch_bytes + (1ull << 30);
-  while (lo < hi) {
-    const uint64_t mid = lo + (hi - lo) / 2;
-    si_plan_info p;
-    if (si_model_plan_dry(&c, 1, 0, mid, depth, &p) == SI_OK && p.resident_layers >= layers) hi = mid;
-    else lo = mid + 1;
-  }
-  return lo;
-}
-
 // run_gguf_resident (runtime.rs:3380-3555) on the CUDA backend
 int run_cuda(const Config& c) {
   if (c.repetitions == 0) throw Failure{"measured repetitions must be non-zero"};
@@ -388,13 +373,20 @@ int run_cuda(const Config& c) {
   const bool streaming = c.backend == "cuda-streaming" || c.backend == "metal-streaming";
   si_ctx_config cc = {};
   cc.stage_depth = 3;
-  if (streaming)
-    cc.hbm_budget_bytes = c.retain_layers ? budget_for_layers(mc, c.retain_layers, 3)
-                                          : uint64_t(c.hbm_budget_gb * double(1ull << 30));
+  // --retain-layers N: the first N layers resident and every other layer
+  // streamed (new_with_retained_layers_and_head, qwen35_runtime.rs:1552);
+  // otherwise the budget decides
+  if (streaming && !c.retain_layers) cc.hbm_budget_bytes = uint64_t(c.hbm_budget_gb * double(1ull << 30));
   si_device_info dev;
   check(si_device_probe(c.device, &dev), nullptr, "device probe");
   si_ctx* ctx = nullptr;
   check(si_ctx_create(c.device, &cc, &ctx), nullptr, "context");
+  if (streaming && c.retain_layers) {
+    si_retention keep = {};
+    keep.prefix_layers = uint32_t(c.retain_layers);
+    keep.flags = SI_RETAIN_EXACT;
+    check(si_ctx_set_retention(ctx, &keep), ctx, "retention");
+  }
   si_model* m = nullptr;
   std::vector<Measured> runs;
   si_plan_info plan{};
