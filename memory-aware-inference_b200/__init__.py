@@ -334,6 +334,9 @@ class StagedLayer:
         return w
 
     def close(self):
+        if getattr(self, "h", None) and not getattr(self.ctx, "h", None):
+            self.h = None  # freeing would touch the destroyed context; the copy stays until exit
+            return
         if getattr(self, "h", None):
             for w in self._views:  # views the caller has not freed already
                 if w.handle:
@@ -963,8 +966,11 @@ class Model:
         return m
 
     def close(self):
+        """Destroy the model. After its context was closed this only drops the
+        handle: si_model_destroy would touch the destroyed context."""
         if getattr(self, "h", None):
-            lib().si_model_destroy(self.h)
+            if getattr(self.ctx, "h", None):
+                lib().si_model_destroy(self.h)
             self.h = None
 
     def __del__(self):
