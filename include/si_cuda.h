@@ -97,6 +97,15 @@ typedef struct si_stats {
 } si_stats;
 int si_get_stats(const si_ctx* ctx, si_stats* out);
 int si_reset_peaks(si_ctx* ctx);
+/* Host-side fault injection for tests of the failure paths (the reference
+ * turns every such failure into Err(String); no GPU fault is involved). The
+ * call at `site` that follows `skip` further calls there fails once, as the
+ * real call fails: an allocation with SI_E_NOMEM, a file read as a short
+ * read. Process-wide; site 0 disarms every site. */
+#define SI_FAULT_PINNED_ALLOC 1u /* pinned host memory of a model's weights */
+#define SI_FAULT_DEVICE_ALLOC 2u /* device memory: weights, staged layers, models, snapshots */
+#define SI_FAULT_FILE_READ 3u    /* GGUF header reads and payload preads */
+int si_fault_inject(uint32_t site, uint32_t skip);
 /* sample_allocated (metal.rs:2374-2378): fold the current allocation into the peak. */
 int si_sample_allocated(si_ctx* ctx); /* reset_peaks, metal.rs:2358 */
 

@@ -223,6 +223,7 @@ def lib():
         "si_model_plan_dry_retained": ([vp, i32, i32, u64, u32, vp, vp, vp], i32),
         "si_model_resident_layers": ([vp, vp, u32], i32),
         "si_ctx_set_retention": ([vp, vp], i32),
+        "si_fault_inject": ([u32, u32], i32),
         "si_model_shard_rows": ([vp, i32, i32, u32, u32, vp, u32, vp], i32),
         "si_model_host_tensor": ([vp, u32, u32, vp, vp, vp], i32),
         "si_model_reset": ([vp], i32),
@@ -740,6 +741,18 @@ def shard_rows(config: SiModelConfig, nranks: int, rank: int, layer: int, tensor
 
 
 def _gck(rc):
+    if rc != 0:
+        raise SiError(rc, lib().si_global_last_error().decode())
+
+
+FAULT_PINNED_ALLOC, FAULT_DEVICE_ALLOC, FAULT_FILE_READ = 1, 2, 3
+
+
+def fault_inject(site: int, skip: int = 0):
+    """Arm a host-side fault (si_fault_inject): the call at `site` after
+    `skip` further calls fails once, as the real call would. site 0 disarms
+    every site."""
+    rc = lib().si_fault_inject(site, skip)
     if rc != 0:
         raise SiError(rc, lib().si_global_last_error().decode())
 

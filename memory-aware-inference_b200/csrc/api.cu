@@ -12,6 +12,7 @@
 #include "common.cuh"
 #include "comm.h"
 #include "ctx.h"
+#include "fault.h"
 #include "gguf.h"
 #include "kernels.cuh"
 #include "qmatvec.cuh"
@@ -45,6 +46,17 @@ struct si_staged_layer {
 };
 
 namespace si {
+
+// Armed sites count down the calls still to pass; -1 = disarmed.
+std::atomic<int64_t> g_fault[SI_FAULT_SITES] = {{-1}, {-1}, {-1}, {-1}};
+
+bool fault_fire(uint32_t site) {
+  if (site == 0 || site >= SI_FAULT_SITES) return false;
+  int64_t v = g_fault[site].load(std::memory_order_relaxed);
+  while (v >= 0)
+    if (g_fault[site].compare_exchange_weak(v, v - 1)) return v == 0;
+  return false;
+}
 
 int fail(si_ctx* ctx, int code, const std::string& msg) {
   if (ctx) ctx->err = msg;
@@ -286,8 +298,9 @@ int si_weight_upload(si_ctx* ctx, const void* host, uint64_t bytes, uint32_t typ
   w->ctx = ctx;
   w->bytes = bytes;
   w->type = type;
-  cudaError_t e = cudaMalloc(&w->dev, bytes + 64);
+  cudaError_t e = fault_fire(SI_FAULT_DEVICE_ALLOC) ? cudaErrorMemoryAllocation : cudaMalloc(&w->dev, bytes + 64);
   if (e != cudaSuccess) {
+    w->dev = nullptr;
     delete w;
     return cuda_fail(ctx, e, "quantized weight upload");
   }
@@ -936,8 +949,10 @@ static int staged_create(si_ctx* ctx, const void* packed, uint64_t bytes, uint32
     std::lock_guard<std::mutex> lk(ctx->upload_mu);
     cudaSetDevice(ctx->device);
     L->dev_bytes = std::max<uint64_t>(off, 256);
-    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&L->dev), L->dev_bytes);
+    cudaError_t e = fault_fire(SI_FAULT_DEVICE_ALLOC) ? cudaErrorMemoryAllocation
+                                                      : cudaMalloc(reinterpret_cast<void**>(&L->dev), L->dev_bytes);
     if (e != cudaSuccess) {
+      L->dev = nullptr;
       delete L;
       return cuda_fail(ctx, e, "packed Qwen layer private upload");
     }
@@ -1062,6 +1077,16 @@ int si_gguf_q4_k_embedding(si_ctx* ctx, const si_gguf* g, uint64_t index, uint64
   std::string err;
   if (int rc = gguf_read(g, t.data_start + token * rb, row.data(), rb, &err)) return fail(ctx, rc, err);
   return si_q4_k_embedding_row(ctx, row.data(), rb, cols, out);
+}
+
+int si_fault_inject(uint32_t site, uint32_t skip) {
+  if (site >= si::SI_FAULT_SITES) return si::fail(nullptr, SI_E_INVALID, "unknown fault site " + std::to_string(site));
+  if (site == 0) {
+    for (auto& f : si::g_fault) f.store(-1);
+    return SI_OK;
+  }
+  si::g_fault[site].store(int64_t(skip));
+  return SI_OK;
 }
 
 int si_sample_allocated(si_ctx* ctx) {

@@ -21,6 +21,7 @@
 
 #include "../../include/si_cuda.h"
 #include "gguf.h"
+#include "fault.h"
 
 namespace si {
 int fail(si_ctx* ctx, int code, const std::string& msg);
@@ -60,7 +61,7 @@ struct Reader {
       err = "GGUF header is truncated";
       return false;
     }
-    if (n && fread(dst, 1, n, f) != n) {
+    if (n && (si::fault_fire(SI_FAULT_FILE_READ) || fread(dst, 1, n, f) != n)) {
       err = "GGUF read failed";
       return false;
     }
@@ -261,7 +262,9 @@ int gguf_parse(const char* path, si_gguf** out, std::string* err) {
 int gguf_read(const si_gguf* g, uint64_t offset, void* dst, uint64_t bytes, std::string* err) {
   uint8_t* p = static_cast<uint8_t*>(dst);
   while (bytes) {
-    const ssize_t got = pread(g->fd, p, size_t(std::min<uint64_t>(bytes, uint64_t(1) << 30)), off_t(offset));
+    const ssize_t got = si::fault_fire(SI_FAULT_FILE_READ)
+                            ? 0
+                            : pread(g->fd, p, size_t(std::min<uint64_t>(bytes, uint64_t(1) << 30)), off_t(offset));
     if (got <= 0) {
       *err = "GGUF read of " + g->path + " failed: " + (got < 0 ? std::strerror(errno) : "unexpected end of file");
       return SI_E_INVALID;

@@ -26,6 +26,7 @@
 #include "comm.h"
 #include "common.cuh"
 #include "ctx.h"
+#include "fault.h"
 #include "gguf.h"
 #include "planner.h"
 #include "kernels.cuh"
@@ -611,8 +612,11 @@ int create_model(si_ctx* ctx, const si_model_config* cfg, uint64_t seed,
   const uint64_t proj_l = (2ull * m->kh_l + m->vh_l) * 128;
   m->host.assign(c.layers + 1, nullptr);
   for (uint32_t l = 0; l <= c.layers; ++l) {
-    cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&m->host[l]), m->layout[l].bytes, cudaHostAllocDefault);
+    cudaError_t e = fault_fire(SI_FAULT_PINNED_ALLOC)
+                        ? cudaErrorMemoryAllocation
+                        : cudaHostAlloc(reinterpret_cast<void**>(&m->host[l]), m->layout[l].bytes, cudaHostAllocDefault);
     if (e != cudaSuccess) {
+      m->host[l] = nullptr;
       int rc = cuda_fail(ctx, e, "pinned host allocation for model weights");
       free_model(m);
       return rc;
@@ -628,7 +632,10 @@ int create_model(si_ctx* ctx, const si_model_config* cfg, uint64_t seed,
   embd.rows = m->V_l;
   const uint64_t embd_bytes = embd.rows * row_bytes_of(embd.type, embd.cols);
   {
-    cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&m->embd_host), embd_bytes + 64, cudaHostAllocMapped);
+    cudaError_t e = fault_fire(SI_FAULT_PINNED_ALLOC)
+                        ? cudaErrorMemoryAllocation
+                        : cudaHostAlloc(reinterpret_cast<void**>(&m->embd_host), embd_bytes + 64, cudaHostAllocMapped);
+    if (e != cudaSuccess) m->embd_host = nullptr;
     if (e == cudaSuccess) e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&m->embd_dev), m->embd_host, 0);
     if (e != cudaSuccess) {
       int rc = cuda_fail(ctx, e, "mapped host allocation for token embeddings");
@@ -686,8 +693,11 @@ int create_model(si_ctx* ctx, const si_model_config* cfg, uint64_t seed,
 
   // ---- device allocations -----------------------------------------------
   auto dmalloc = [&](void** p, uint64_t bytes, const char* what) -> int {
-    cudaError_t e = cudaMalloc(p, bytes ? bytes : 256);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+    cudaError_t e = fault_fire(SI_FAULT_DEVICE_ALLOC) ? cudaErrorMemoryAllocation : cudaMalloc(p, bytes ? bytes : 256);
+    if (e != cudaSuccess) {
+      *p = nullptr;
+      return cuda_fail(ctx, e, what);
+    }
     return SI_OK;
   };
   int rc = dmalloc(reinterpret_cast<void**>(&m->dev_resident), resident, "resident weight allocation");
@@ -1064,7 +1074,9 @@ extern "C" int si_model_snapshot_states(si_model* m, si_model_snapshot** out) {
   s->bytes = m->plan.state_bytes;
   s->cached = m->cached;
   s->conv_parity = m->conv_parity;
-  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&s->block), s->bytes ? s->bytes : 256);
+  cudaError_t e = fault_fire(SI_FAULT_DEVICE_ALLOC)
+                      ? cudaErrorMemoryAllocation
+                      : cudaMalloc(reinterpret_cast<void**>(&s->block), s->bytes ? s->bytes : 256);
   if (e != cudaSuccess) {
     s->block = nullptr;
     delete s;
