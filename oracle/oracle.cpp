@@ -11,7 +11,8 @@
 // restatement is pinned against every known-answer test the reference holds
 // for the path (src/quant.rs:213-280, src/qwen35.rs:232-296,
 // src/cache.rs:173-291, src/metal.rs:7362-7602 and 8252-8404); those KATs are
-// replayed in tests/test_oracle_kats.py.
+// replayed in tests/test_oracle_kats.py. The KV-cache container the cache.rs
+// tests exercise is restated in oracle/kv_cache.py.
 //
 // Floating point follows Rust semantics: IEEE binary32, no FMA contraction
 // (build with -ffp-contract=off), left-to-right evaluation, sequential sums.

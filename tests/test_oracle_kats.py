@@ -234,3 +234,88 @@ def test_fused_gate_up_pattern():  # metal.rs:7496-7540 expectation
     u = O.matvec(O.GGML_Q4_K, up, rows, cols, x)
     o = O.fused_gate_up(gate, up, rows, cols, x)
     assert np.allclose(o, g / (1 + np.exp(-g)) * u, rtol=1e-6)
+
+
+# ---- KvCache (cache.rs:173-291) ----------------------------------------------
+from oracle.kv_cache import CacheError, KvCache  # noqa: E402
+
+
+def _addr(a):
+    return a.__array_interface__["data"][0]
+
+
+def test_kv_prefill_lands_in_head_major_capacity_layout():  # cache.rs:177-197
+    c = KvCache(2, 2, 3)
+    c.append_sequence([1, 2, 3, 4, 5, 6, 7, 8], [10, 20, 30, 40, 50, 60, 70, 80], 2)
+    assert c.cached_tokens == 2 and c.remaining_tokens() == 1 and c.active_bytes() == 64
+    assert c.keys.tolist() == [1, 2, 5, 6, 0, 0, 3, 4, 7, 8, 0, 0]
+    assert c.values[0:4].tolist() == [10, 20, 50, 60] and c.values[6:10].tolist() == [30, 40, 70, 80]
+
+
+def test_kv_rejects_bad_token_shape_and_capacity_overflow():  # cache.rs:199-207
+    c = KvCache(1, 2, 1)
+    with pytest.raises(CacheError):
+        c.append_token([1.0], [2.0, 3.0])
+    c.append_token([1.0, 2.0], [3.0, 4.0])
+    with pytest.raises(CacheError, match="capacity exhausted"):
+        c.append_token([5.0, 6.0], [7.0, 8.0])
+    with pytest.raises(CacheError, match="non-zero"):
+        KvCache(0, 2, 1)
+
+
+def test_kv_clear_reuses_capacity():  # cache.rs:209-219
+    c = KvCache(2, 4, 8)
+    p = _addr(c.keys)
+    c.append_token([0.0] * 8, [0.0] * 8)
+    c.clear()
+    assert c.cached_tokens == 0 and _addr(c.keys) == p
+
+
+def test_kv_truncate_discards_suffix_in_place():  # cache.rs:221-237
+    c = KvCache(1, 2, 4)
+    c.append_sequence([1, 2, 3, 4], [5, 6, 7, 8], 2)
+    pk, pv = _addr(c.keys), _addr(c.values)
+    c.truncate_to(1)
+    assert c.cached_tokens == 1 and (_addr(c.keys), _addr(c.values)) == (pk, pv)
+    assert c.keys[:2].tolist() == [1, 2] and c.values[:2].tolist() == [5, 6]
+
+
+def test_kv_truncate_rejects_future_position():  # cache.rs:239-246
+    c = KvCache(1, 2, 2)
+    c.append_token([1, 2], [3, 4])
+    with pytest.raises(CacheError, match="future position"):
+        c.truncate_to(2)
+
+
+def test_kv_copy_prefix_reuses_destination():  # cache.rs:248-266
+    src = KvCache(1, 2, 4)
+    src.append_sequence([1, 2, 3, 4], [5, 6, 7, 8], 2)
+    dst = KvCache(1, 2, 4)
+    dst.append_sequence([9, 10, 11, 12], [13, 14, 15, 16], 2)
+    p = _addr(dst.keys)
+    dst.copy_prefix_from(src)
+    assert _addr(dst.keys) == p and dst.cached_tokens == 2
+    assert dst.keys[:4].tolist() == [1, 2, 3, 4] and dst.values[:4].tolist() == [5, 6, 7, 8]
+
+
+def test_kv_copy_prefix_compact_source_into_larger_destination():  # cache.rs:268-290
+    src = KvCache(2, 2, 3)
+    src.append_sequence([1, 2, 3, 4, 5, 6, 7, 8], [11, 12, 13, 14, 15, 16, 17, 18], 2)
+    dst = KvCache(2, 2, 8)
+    dst.copy_prefix_from(src)
+    assert dst.cached_tokens == 2
+    assert dst.keys[:4].tolist() == [1, 2, 5, 6] and dst.keys[16:20].tolist() == [3, 4, 7, 8]
+    assert dst.values[:4].tolist() == [11, 12, 15, 16] and dst.values[16:20].tolist() == [13, 14, 17, 18]
+    with pytest.raises(CacheError, match="layouts do not match"):
+        KvCache(2, 2, 1).copy_prefix_from(src)
+
+
+def test_kv_cache_feeds_the_attention_oracle():  # cache.rs:1-4 layout read by metal.rs:1707
+    """A cache built by appends is what the attention restatement reads:
+    the same output as the hand-built capacity-strided cache above."""
+    c = KvCache(1, 2, 4)
+    c.append_sequence([1, 0, 0, 1], [10, 0, 20, 0], 2)
+    q = np.array([1, 1], np.float32)
+    o = O.attention_decode(q, c.keys, c.values, [1, -1], [30, 0], 1, 1, 2, c.cached_tokens, c.capacity_tokens)
+    compact = O.attention_decode(q, c.keys[:4], c.values[:4], [1, -1], [30, 0], 1, 1, 2, 2, 2)
+    assert np.allclose(o, compact, atol=1e-6)
