@@ -441,6 +441,12 @@ int si_gguf_qwen35_layer_kind(const si_gguf* g, uint32_t layer, uint32_t* kind);
  * *known = 0 for types other than F32, F16, BF16 and the K-quants. */
 int si_gguf_tensor_payload(const si_gguf* g, uint64_t index, uint64_t* elements, uint64_t* expected_bytes,
                            uint32_t* known);
+/* gguf_quant_matvec_many_tensors (metal.rs:4532-4638): n K-quant tensors of
+ * an open GGUF file that share x (x_len must equal their column count), with
+ * the reference's checks: same columns, rank 2, a K-quant type, a payload that
+ * covers rows x cols. Each payload is read from the file for the call. */
+int si_gguf_quant_matvec_many_tensors(si_ctx* ctx, const si_gguf* g, uint32_t n, const uint64_t* indices,
+                                      const float* x, uint64_t x_len, float* const* ys);
 /* gguf_matvec_tensor_rows (metal.rs:5003-5015): rows [row_start,
  * row_start+row_count) of tensor `index` (F32 or a K-quant), read from the
  * file, times x (dims[0] columns). */

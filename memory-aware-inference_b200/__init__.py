@@ -196,6 +196,7 @@ def lib():
         "si_staged_layer_weight": ([vp, C.c_char_p, u32, vp], i32),
         "si_staged_layer_free": ([vp], None),
         "si_gguf_matvec_tensor_rows": ([vp, vp, u64, u64, u64, vp, vp], i32),
+        "si_gguf_quant_matvec_many_tensors": ([vp, vp, u32, vp, vp, u64, vp], i32),
         "si_gguf_q4_k_embedding": ([vp, vp, u64, u64, vp], i32),
         "si_sample_allocated": ([vp], i32),
         "si_gguf_quant_matmul_many_bytes": ([vp, u32, vp, u64, u64, u64, u64, vp, vp], i32),
@@ -564,6 +565,18 @@ class CudaContext:
         y = np.empty(row_count, np.float32)
         self._ck(lib().si_gguf_matvec_tensor_rows(self.h, gguf.h, idx, row_start, row_count, _p(_f32(x)), _p(y)))
         return y
+
+    def gguf_quant_matvec_many_tensors(self, gguf: "GgufFile", names_or_indices, x) -> list:
+        """MetalContext::gguf_quant_matvec_many_tensors: several K-quant tensors
+        of an open GGUF file against one input."""
+        idx = [gguf.find(t) if isinstance(t, str) else int(t) for t in names_or_indices]
+        xs = _f32(x)
+        outs = [np.empty(gguf.tensor_info(i)["shape"][1] if len(gguf.tensor_info(i)["shape"]) > 1 else 0,
+                         np.float32) for i in idx]
+        ia = (C.c_uint64 * max(len(idx), 1))(*idx)
+        ya = (C.c_void_p * max(len(idx), 1))(*[o.ctypes.data for o in outs])
+        self._ck(lib().si_gguf_quant_matvec_many_tensors(self.h, gguf.h, len(idx), ia, _p(xs), xs.size, ya))
+        return outs
 
     def q4_k_embedding_tensor(self, gguf: "GgufFile", name_or_index, token_id) -> np.ndarray:
         """MetalContext::q4_k_embedding_tensor over a tensor of an open GGUF file."""

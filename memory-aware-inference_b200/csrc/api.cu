@@ -1064,6 +1064,41 @@ int si_gguf_matvec_tensor_rows(si_ctx* ctx, const si_gguf* g, uint64_t index, ui
   return si_gguf_quant_matvec_bytes(ctx, t.type, buf.data(), buf.size(), row_count, cols, x, y);
 }
 
+int si_gguf_quant_matvec_many_tensors(si_ctx* ctx, const si_gguf* g, uint32_t n, const uint64_t* indices,
+                                      const float* x, uint64_t x_len, float* const* ys) {
+  if (!ctx) return SI_E_INVALID;
+  if (!g || (n && (!indices || !ys))) return fail(ctx, SI_E_INVALID, "invalid grouped tensor matvec arguments");
+  if (n == 0) return fail(ctx, SI_E_INVALID, "quantized matvec group requires at least one tensor");
+  for (uint32_t i = 0; i < n; ++i)
+    if (indices[i] >= g->tensors.size()) return fail(ctx, SI_E_INVALID, "GGUF tensor index out of range");
+  const GgufTensor& t0 = g->tensors[indices[0]];
+  if (t0.ndim == 0) return fail(ctx, SI_E_INVALID, "quantized matvec tensor is not a matrix");
+  const uint64_t cols = t0.dims[0];
+  if (!x || x_len != cols) return fail(ctx, SI_E_INVALID, "quantized matvec group input length is invalid");
+  std::vector<uint64_t> expected(n);
+  for (uint32_t i = 0; i < n; ++i) {
+    const GgufTensor& t = g->tensors[indices[i]];
+    const uint64_t bb = block_bytes_of(t.type);
+    if (t.ndim != 2 || t.dims[0] != cols || !bb)
+      return fail(ctx, SI_E_INVALID, "quantized matvec group tensor shapes or types differ");
+    const uint64_t rows = t.dims[1], blocks = cols / 256;
+    if ((blocks && rows > UINT64_MAX / blocks) || (rows * blocks && bb > UINT64_MAX / (rows * blocks)))
+      return fail(ctx, SI_E_INVALID, "quantized matvec group byte length overflows");
+    expected[i] = rows * blocks * bb;
+    if (t.data_len < expected[i]) return fail(ctx, SI_E_INVALID, "quantized matvec group tensor is truncated");
+  }
+  std::vector<uint8_t> buf;
+  std::string err;
+  for (uint32_t i = 0; i < n; ++i) {
+    const GgufTensor& t = g->tensors[indices[i]];
+    buf.resize(expected[i]);
+    if (int rc = gguf_read(g, t.data_start, buf.data(), buf.size(), &err)) return fail(ctx, rc, err);
+    if (int rc = si_gguf_quant_matvec_bytes(ctx, t.type, buf.data(), buf.size(), t.dims[1], cols, x, ys[i]))
+      return rc;
+  }
+  return SI_OK;
+}
+
 int si_gguf_q4_k_embedding(si_ctx* ctx, const si_gguf* g, uint64_t index, uint64_t token, float* out) {
   if (!ctx || !g || !out) return fail(ctx, SI_E_INVALID, "invalid embedding arguments");
   if (index >= g->tensors.size()) return fail(ctx, SI_E_INVALID, "GGUF tensor index out of range");

@@ -98,3 +98,30 @@ def test_sample_allocated_folds_into_the_peak(mai, ctx):
     ctx.sample_allocated()
     after = ctx.stats()
     assert after["peak_allocated_bytes"] >= before["current_allocated_bytes"]
+
+
+def test_grouped_matvec_over_file_tensors(mai, ctx, tmp_path):
+    """gguf_quant_matvec_many_tensors (metal.rs:4532-4638): mixed K-quant
+    tensors of one file against one input, and the reference's refusals."""
+    rng = np.random.default_rng(12)
+    cols = 512
+    mats = {"q4": (Q4, 70), "q5": (Q5, 33), "q6": (Q6, 128)}
+    blobs = {k: random_blocks(rng, ty, rows * cols // 256) for k, (ty, rows) in mats.items()}
+    f32 = rng.normal(0, 1, (8, cols)).astype(np.float32)
+    path = tmp_path / "g.gguf"
+    W.write(path, [("general.architecture", W.STRING, "qwen35")],
+            [(k, [cols, rows], ty, blobs[k].tobytes()) for k, (ty, rows) in mats.items()]
+            + [("f", [cols, 8], 0, f32.tobytes()), ("narrow", [256, 4], Q4, random_blocks(rng, Q4, 4).tobytes())])
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    with mai.GgufFile(path) as g:
+        ys = ctx.gguf_quant_matvec_many_tensors(g, ["q4", "q5", "q6"], x)
+        for (k, (ty, rows)), y in zip(mats.items(), ys):
+            assert rel_l2(y, O.matvec(ty, blobs[k], rows, cols, x)) < 1e-5, k
+        with pytest.raises(mai.SiError, match="requires at least one tensor"):
+            ctx.gguf_quant_matvec_many_tensors(g, [], x)
+        with pytest.raises(mai.SiError, match="input length is invalid"):
+            ctx.gguf_quant_matvec_many_tensors(g, ["q4"], x[:256])
+        with pytest.raises(mai.SiError, match="shapes or types differ"):
+            ctx.gguf_quant_matvec_many_tensors(g, ["q4", "f"], x)
+        with pytest.raises(mai.SiError, match="shapes or types differ"):
+            ctx.gguf_quant_matvec_many_tensors(g, ["q4", "narrow"], x)
