@@ -150,6 +150,37 @@ def gdn_step(q, k, v, g, beta, state, heads, kd, vd):
     return out, st
 
 
+def gdn_step_parallel(q, k, v, g, beta, state, heads, kd, vd):
+    """si_gated_delta_step_parallel (src/metal.rs:688-740), the reference's
+    other formulation of the recurrence: one lane per (head, value column)
+    decays its state column while summing memory = S^T k and S^T q over the
+    keys in order, then delta = (v - memory) * beta, S += k delta, and
+    out = S_decayed^T q + delta * (k . q). f32 throughout; returns (out,
+    new_state) without modifying `state`."""
+    f32 = np.float32
+    q = np.asarray(q, f32).reshape(heads, kd)
+    k = np.asarray(k, f32).reshape(heads, kd)
+    v = np.asarray(v, f32).reshape(heads, vd)
+    st = np.array(state, f32, copy=True).reshape(heads, kd, vd)
+    out = np.empty((heads, vd), f32)
+    for h in range(heads):
+        kq = f32(0)
+        for i in range(kd):
+            kq = f32(kq + k[h, i] * q[h, i])
+        decay = f32(np.exp(f32(g[h])))
+        memory = np.zeros(vd, f32)
+        qsum = np.zeros(vd, f32)
+        for i in range(kd):
+            st[h, i] = st[h, i] * decay
+            memory = memory + st[h, i] * k[h, i]
+            qsum = qsum + st[h, i] * q[h, i]
+        delta = (v[h] - memory) * f32(beta[h])
+        for i in range(kd):
+            st[h, i] = st[h, i] + k[h, i] * delta
+        out[h] = qsum + delta * kq
+    return out.reshape(-1), st.reshape(-1)
+
+
 def rope(x, heads, hd, pos, theta):
     out = np.empty(heads * hd, np.float32)
     _check(lib().or_rope(np.ascontiguousarray(x, np.float32), heads, hd, pos, theta, out), "rope")

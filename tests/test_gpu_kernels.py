@@ -235,6 +235,11 @@ def test_gdn_step_random_matches_oracle(ctx):
     o1, s1 = ctx.gated_delta_step(q, k, v, g, beta, s, h, d, d)
     o2, s2 = O.gdn_step(q, k, v, g, beta, s, h, d, d)
     assert rel_l2(o1, o2) < TOL and rel_l2(s1, s2) < TOL
+    # and against the reference's parallel formulation (metal.rs:688-740) on
+    # the first heads
+    n = 4
+    o3, s3 = O.gdn_step_parallel(q[:n * d], k[:n * d], v[:n * d], g[:n], beta[:n], s[:n * d * d], n, d, d)
+    assert rel_l2(o1[:n * d], o3) < TOL and rel_l2(s1[:n * d * d], s3) < TOL
 
 
 def test_conv_kat_and_random(ctx):  # metal.rs:7387-7409

@@ -319,3 +319,26 @@ def test_kv_cache_feeds_the_attention_oracle():  # cache.rs:1-4 layout read by m
     o = O.attention_decode(q, c.keys, c.values, [1, -1], [30, 0], 1, 1, 2, c.cached_tokens, c.capacity_tokens)
     compact = O.attention_decode(q, c.keys[:4], c.values[:4], [1, -1], [30, 0], 1, 1, 2, 2, 2)
     assert np.allclose(o, compact, atol=1e-6)
+
+
+def test_gdn_parallel_formulation_agrees_with_the_serial_one():  # metal.rs:630-740
+    """The reference ships two formulations of the recurrence with different
+    summation orders; both sit within the 1e-5 parity tolerance of each
+    other, so the tolerance covers either as the reference's answer."""
+    rng = np.random.default_rng(21)
+    h, d = 4, 128
+    q = rng.normal(0, 0.1, h * d).astype(np.float32)
+    k = rng.normal(0, 0.1, h * d).astype(np.float32)
+    v = rng.normal(0, 1, h * d).astype(np.float32)
+    g = -np.log1p(np.exp(rng.normal(0, 1, h))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.normal(0, 1, h)))).astype(np.float32)
+    s = rng.normal(0, 0.1, h * d * d).astype(np.float32)
+    o1, s1 = O.gdn_step(q, k, v, g, beta, s, h, d, d)
+    o2, s2 = O.gdn_step_parallel(q, k, v, g, beta, s, h, d, d)
+    rel = lambda a, b: float(np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b.astype(np.float64)))
+    assert rel(o1, o2) < 1e-5 and rel(s1, s2) < 1e-5
+    # the two-token known answer (qwen35.rs:273-288) through the parallel form
+    o, st = O.gdn_step_parallel([1, 0], [1, 0], [2], [0], [0.5], [0, 0], 1, 2, 1)
+    assert o.tolist() == [1.0] and st.tolist() == [1.0, 0.0]
+    o, st = O.gdn_step_parallel([0, 1], [0, 1], [4], [math.log(0.5)], [1.0], st, 1, 2, 1)
+    assert o.tolist() == [4.0] and st.tolist() == [0.5, 4.0]
