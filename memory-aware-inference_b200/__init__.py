@@ -277,7 +277,8 @@ def lib():
 
 
 def _p(a):
-    """Pointer of a numpy array / torch tensor / int address / None."""
+    """Address of a numpy array / torch tensor / int address / None. The
+    result is a bare integer: the caller keeps `a` alive across the call."""
     if a is None:
         return None
     if isinstance(a, int):
@@ -286,8 +287,10 @@ def _p(a):
         return a.ctypes.data
     if hasattr(a, "data_ptr"):
         return a.data_ptr()
-    if isinstance(a, (bytes, bytearray)):
-        return C.cast(C.c_char_p(bytes(a)), C.c_void_p).value
+    if isinstance(a, bytes):  # the caller's own object, not a copy
+        return C.cast(C.c_char_p(a), C.c_void_p).value
+    if isinstance(a, bytearray):
+        return C.addressof((C.c_char * len(a)).from_buffer(a)) if a else None
     raise TypeError(f"cannot take a pointer of {type(a)}")
 
 
@@ -548,7 +551,8 @@ class CudaContext:
         ptrs = (C.c_void_p * n)(*[m.ctypes.data for m in ms])
         rows = (C.c_uint64 * n)(*[m.shape[0] for m in ms])
         ys = (C.c_void_p * n)(*[o.ctypes.data for o in outs])
-        self._ck(lib().si_f32_matvec_many(self.h, n, ptrs, rows, cols, _p(_f32(x)), ys))
+        xs = _f32(x)  # held for the call: _p returns a bare address
+        self._ck(lib().si_f32_matvec_many(self.h, n, ptrs, rows, cols, _p(xs), ys))
         return outs
 
     def upload_staged_layer_private(self, packed, ranges) -> "StagedLayer":
@@ -563,7 +567,8 @@ class CudaContext:
         """MetalContext::gguf_matvec_tensor_rows over a tensor of an open GGUF file."""
         idx = gguf.find(name_or_index) if isinstance(name_or_index, str) else int(name_or_index)
         y = np.empty(row_count, np.float32)
-        self._ck(lib().si_gguf_matvec_tensor_rows(self.h, gguf.h, idx, row_start, row_count, _p(_f32(x)), _p(y)))
+        xs = _f32(x)  # held for the call: _p returns a bare address
+        self._ck(lib().si_gguf_matvec_tensor_rows(self.h, gguf.h, idx, row_start, row_count, _p(xs), _p(y)))
         return y
 
     def gguf_quant_matvec_many_tensors(self, gguf: "GgufFile", names_or_indices, x) -> list:
