@@ -289,6 +289,37 @@ struct Measured {
 // run_gguf_generation (runtime.rs:3557-3614): the prompt advances the state
 // token by token and its last step yields the first greedy id (prefill); each
 // non-EOS generated id, the last requested one included, advances it once more.
+// SI_PROFILE_QWEN35 (qwen35_runtime.rs:1786, 1920-1926, 2185-2190): one line
+// per layer and per output head on stderr, in the reference's format. The
+// reference times each layer on the host; here the layer loop only enqueues
+// work, so the times are the device's, taken from the measured trace of the
+// call (CUDA events around each layer's kernels).
+template <typename F>
+void profiled(si_ctx* ctx, si_model* m, F call) {
+  static const bool on = std::getenv("SI_PROFILE_QWEN35") != nullptr;
+  if (!on) {
+    call();
+    return;
+  }
+  check(si_model_trace_begin(m), ctx, "profile trace");
+  call();
+  si_trace* t = nullptr;
+  check(si_model_trace_end(m, &t), ctx, "profile trace");
+  uint64_t n = 0;
+  si_trace_count(t, &n);
+  for (uint64_t i = 0; i < n; ++i) {
+    si_trace_action a;
+    if (si_trace_action_at(t, i, &a) != SI_OK || a.kind != SI_ACT_EXECUTE) continue;
+    const double ms = double(a.ended_ns - a.started_ns) / 1e6;
+    const std::string op = a.operation_id;
+    if (op == "output")
+      std::fprintf(stderr, "si_qwen35_output_head ms=%.3f\n", ms);
+    else if (op.rfind("layer-", 0) == 0)
+      std::fprintf(stderr, "si_qwen35_layer layer=%s ms=%.3f\n", op.c_str() + 6, ms);
+  }
+  si_trace_destroy(t);
+}
+
 Measured generate(si_ctx* ctx, si_model* m, const std::vector<uint32_t>& prompt, uint32_t max_new, uint32_t eos,
                   uint64_t hidden) {
   Measured r{};
@@ -297,17 +328,21 @@ Measured generate(si_ctx* ctx, si_model* m, const std::vector<uint32_t>& prompt,
   auto t0 = std::chrono::steady_clock::now();
   for (size_t p = 0; p + 1 < prompt.size(); ++p) {
     check(si_model_embed(m, prompt[p], h.data()), ctx, "embed");
-    check(si_model_decode_hidden(m, p, h.data()), ctx, "decode");
+    profiled(ctx, m, [&] { check(si_model_decode_hidden(m, p, h.data()), ctx, "decode"); });
     peak_rss = std::max(peak_rss, rss_bytes());
   }
   uint32_t next = 0;
-  check(si_model_decode_token(m, prompt.back(), prompt.size() - 1, &next, nullptr), ctx, "prefill");
+  profiled(ctx, m, [&] {
+    check(si_model_decode_token(m, prompt.back(), prompt.size() - 1, &next, nullptr), ctx, "prefill");
+  });
   r.prefill = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
   t0 = std::chrono::steady_clock::now();
   for (uint32_t i = 0; i < max_new; ++i) {
     r.ids.push_back(next);
     if (next == eos) break;
-    check(si_model_decode_token(m, next, prompt.size() + i, &next, nullptr), ctx, "decode_token");
+    profiled(ctx, m, [&] {
+      check(si_model_decode_token(m, next, prompt.size() + i, &next, nullptr), ctx, "decode_token");
+    });
     peak_rss = std::max(peak_rss, rss_bytes());
   }
   r.decode = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();

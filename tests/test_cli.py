@@ -5,6 +5,7 @@ GPU test runs the CUDA backend on a synthetic model and checks its ids
 against the Python API."""
 import json
 import os
+import re
 import subprocess
 
 import numpy as np
@@ -15,10 +16,11 @@ from conftest import PKG_DIR, load_package
 CLI = os.path.join(PKG_DIR, "si-bench")
 
 
-def run(*args):
+def run(*args, env=None):
     load_package().lib()  # built alongside the library
     assert os.path.exists(CLI), "si-bench is built by build.py"
-    r = subprocess.run([CLI, *args], capture_output=True, text=True, timeout=600)
+    r = subprocess.run([CLI, *args], capture_output=True, text=True, timeout=600,
+                       env=None if env is None else {**os.environ, **env})
     return r.returncode, r.stdout, r.stderr
 
 
@@ -144,6 +146,26 @@ def test_cuda_backend_ids_match_the_python_api(mai, ctx):
                    "--max-tokens", "6", "--context", "64", "--warmup", "0", "--repetitions", "1",
                    "--expected-output", expected + " 1")
     assert rc == 2
+
+
+@pytest.mark.gpu
+def test_profile_lines_per_layer_and_head():
+    """SI_PROFILE_QWEN35 (qwen35_runtime.rs:1920-1926, 2185-2190): a line per
+    layer per decode step and a line per output head, with device times. Three
+    prompt ids and six new tokens are 9 steps of 8 layers, 7 of them with the
+    head (the last prompt id and every generated id)."""
+    rc, out, err = run("--model", "synthetic:small", "--backend", "metal-streaming", "--retain-layers", "2",
+                       "--prompt-ids", "5,77,1024", "--max-tokens", "6", "--context", "64", "--warmup", "0",
+                       "--repetitions", "1", env={"SI_PROFILE_QWEN35": "1"})
+    assert rc == 0, err
+    layers = re.findall(r"^si_qwen35_layer layer=(\d+) ms=(\d+\.\d{3})$", err, re.M)
+    heads = re.findall(r"^si_qwen35_output_head ms=(\d+\.\d{3})$", err, re.M)
+    assert len(layers) == 72 and len(heads) == 7
+    assert sorted({int(l) for l, _ in layers}) == list(range(8))
+    assert all(float(ms) > 0 for _, ms in layers) and all(float(ms) > 0 for ms in heads)
+    rc, _, err = run("--model", "synthetic:small", "--backend", "cuda-resident", "--prompt-ids", "5,77,1024",
+                     "--max-tokens", "2", "--context", "64", "--warmup", "0", "--repetitions", "1")
+    assert rc == 0 and "si_qwen35_layer" not in err
 
 
 INSPECT = os.path.join(PKG_DIR, "si-gguf-inspect")
