@@ -30,6 +30,8 @@
 #include "gguf.h"
 #include "planner.h"
 #include "kernels.cuh"
+
+#include <nvtx3/nvToolsExt.h>
 #include "qmatvec.cuh"
 #include "synth.h"
 
@@ -1156,18 +1158,27 @@ void issue_copy(si_model* m, uint64_t occ) {
 }
 
 // Execution of layer `l` (or the head, l == layers) bracketed by events on
-// the compute stream when tracing.
+// the compute stream when tracing, and always by an NVTX range named like the
+// trace's operation ("layer-N", "output") for profilers; the range covers the
+// host-side enqueue of the layer's work.
 struct TraceScope {
   si_model* m;
   int layer, slot;
   cudaEvent_t e0 = nullptr;
   TraceScope(si_model* mm, int l, int s) : m(mm), layer(l), slot(s) {
+    char name[32];
+    if (l == int(m->c.layers))
+      std::snprintf(name, sizeof(name), "output");
+    else
+      std::snprintf(name, sizeof(name), "layer-%d", l);
+    nvtxRangePushA(name);
     if (m->tracing) {
       e0 = trace_event(m);
       cudaEventRecord(e0, m->ctx->stream);
     }
   }
   ~TraceScope() {
+    nvtxRangePop();
     if (!e0) return;
     cudaEvent_t e1 = trace_event(m);
     cudaEventRecord(e1, m->ctx->stream);
