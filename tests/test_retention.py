@@ -108,3 +108,18 @@ def test_every_rank_retains_the_same_layers(mai, cfg):
     flags = {mai.plan_dry(cfg, n, k, 0, 3, r)["resident"] == [l % 8 == 1 for l in range(cfg.layers)]
              for n in (1, 2, 4, 8) for k in range(n)}
     assert flags == {True}
+
+
+def test_stage_depth_defaults_to_three_and_clamps_at_four(mai, cfg):  # qwen35_runtime.rs:2357-2364
+    """stage_pipeline_depth: unset or 0 gives 3, 2 stays 2, 99 clamps to 4
+    (the reference's unparsable-string case has no counterpart: the depth is
+    an integer field here)."""
+    stream_all = mai.retention(exact=True)
+    depth = {d: mai.plan_dry(cfg, 1, 0, 0, d, stream_all)["stage_depth"] for d in (0, 2, 99)}
+    assert depth == {0: 3, 2: 2, 99: 4}
+    assert mai.plan_dry(cfg, retention=stream_all)["stage_depth"] == 3
+
+
+def test_layer_set_parse_kat():  # qwen35_runtime.rs:2366-2372
+    mai = load_package()
+    assert mai.parse_layer_set("0, 8,invalid,8, 63") == [0, 8, 63]
