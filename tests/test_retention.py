@@ -123,3 +123,14 @@ def test_stage_depth_defaults_to_three_and_clamps_at_four(mai, cfg):  # qwen35_r
 def test_layer_set_parse_kat():  # qwen35_runtime.rs:2366-2372
     mai = load_package()
     assert mai.parse_layer_set("0, 8,invalid,8, 63") == [0, 8, 63]
+
+
+def test_stride_residency_kat(mai):  # qwen35_runtime.rs:2340-2347
+    """retains_stride_layer: stride 2 offset 0 keeps layer 0 not 1, offset 1
+    keeps 1 not 0, stride 0 keeps nothing. (The neighbouring output-prefetch
+    test has no counterpart: the output head is always resident here.)"""
+    c = mai.qwen36_27b_config(layers=4)
+    res = lambda **kw: mai.plan_dry(c, retention=mai.retention(exact=True, **kw))["resident"]
+    assert res(stride=2, offset=0) == [True, False, True, False]
+    assert res(stride=2, offset=1) == [False, True, False, True]
+    assert res(stride=0, offset=1) == [False] * 4
