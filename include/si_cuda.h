@@ -94,8 +94,13 @@ typedef struct si_stats {
   uint64_t submitted;                /* command_stats, metal.rs:2316 */
   uint64_t waited;
   uint64_t wait_nanos;
+  uint64_t async_submitted;          /* `_dev` enqueues (also counted in submitted) */
 } si_stats;
 int si_get_stats(const si_ctx* ctx, si_stats* out);
+/* CommandStatsSnapshot::delta_since (metal.rs:1891-1947): the command
+ * counters (submitted, async_submitted, waited, wait_nanos) of `after` minus
+ * those of `before`, saturating at 0; the byte fields are `after`'s. */
+int si_stats_delta(const si_stats* after, const si_stats* before, si_stats* out);
 int si_reset_peaks(si_ctx* ctx);
 /* Host-side fault injection for tests of the failure paths (the reference
  * turns every such failure into Err(String); no GPU fault is involved). The

@@ -85,7 +85,7 @@ class SiTraceSummary(C.Structure):
 class SiStats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("current_allocated_bytes", "peak_allocated_bytes",
                                           "peak_active_weight_bytes", "peak_kv_bytes", "peak_scratch_bytes",
-                                          "submitted", "waited", "wait_nanos")]
+                                          "submitted", "waited", "wait_nanos", "async_submitted")]
 
 
 class SiAttentionDecodeInput(C.Structure):
@@ -225,6 +225,7 @@ def lib():
         "si_model_resident_layers": ([vp, vp, u32], i32),
         "si_ctx_set_retention": ([vp, vp], i32),
         "si_fault_inject": ([u32, u32], i32),
+        "si_stats_delta": ([vp, vp, vp], i32),
         "si_model_shard_rows": ([vp, i32, i32, u32, u32, vp, u32, vp], i32),
         "si_model_host_tensor": ([vp, u32, u32, vp, vp, vp], i32),
         "si_model_reset": ([vp], i32),
@@ -761,6 +762,18 @@ def shard_rows(config: SiModelConfig, nranks: int, rank: int, layer: int, tensor
 def _gck(rc):
     if rc != 0:
         raise SiError(rc, lib().si_global_last_error().decode())
+
+
+def stats_delta(after: dict, before: dict) -> dict:
+    """CommandStatsSnapshot::delta_since (si_stats_delta): the command
+    counters of `after` minus `before`, saturating at 0."""
+    a = SiStats(*[after.get(k, 0) for k, _ in SiStats._fields_])
+    b = SiStats(*[before.get(k, 0) for k, _ in SiStats._fields_])
+    out = SiStats()
+    rc = lib().si_stats_delta(C.byref(a), C.byref(b), C.byref(out))
+    if rc != 0:
+        raise SiError(rc, "invalid stats")
+    return {k: getattr(out, k) for k, _ in out._fields_}
 
 
 FAULT_PINNED_ALLOC, FAULT_DEVICE_ALLOC, FAULT_FILE_READ = 1, 2, 3

@@ -76,6 +76,14 @@ void note_alloc(si_ctx* ctx, int64_t delta) {
   }
 }
 
+// An enqueue that returns without waiting (the `_dev` entry points): the
+// reference's record_async_submission (metal.rs:1891-1947) counts it as a
+// submission and as an async one.
+void note_async_submission(si_ctx* ctx) {
+  ctx->submitted++;
+  ctx->async_submitted++;
+}
+
 void note_weights(si_ctx* ctx, int64_t delta) {
   uint64_t now = ctx->weights.fetch_add(uint64_t(delta)) + uint64_t(delta);
   uint64_t peak = ctx->peak_weights.load();
@@ -276,6 +284,18 @@ int si_get_stats(const si_ctx* ctx, si_stats* o) {
   o->submitted = ctx->submitted.load();
   o->waited = ctx->waited.load();
   o->wait_nanos = ctx->wait_nanos.load();
+  o->async_submitted = ctx->async_submitted.load();
+  return SI_OK;
+}
+
+int si_stats_delta(const si_stats* after, const si_stats* before, si_stats* out) {
+  if (!after || !before || !out) return SI_E_INVALID;
+  auto sat = [](uint64_t a, uint64_t b) { return a > b ? a - b : 0; };
+  *out = *after;
+  out->submitted = sat(after->submitted, before->submitted);
+  out->async_submitted = sat(after->async_submitted, before->async_submitted);
+  out->waited = sat(after->waited, before->waited);
+  out->wait_nanos = sat(after->wait_nanos, before->wait_nanos);
   return SI_OK;
 }
 
@@ -375,7 +395,7 @@ static int weight_dev(si_ctx* ctx, const si_weight* w, int slot, const uint8_t**
 extern "C" {
 
 // ---- dequant -----------------------------------------------------------------
-int si_dequantize_dev(si_ctx* ctx, uint32_t type, const void* bytes_dev, uint64_t elements,
+static int dequantize_dev_impl(si_ctx* ctx, uint32_t type, const void* bytes_dev, uint64_t elements,
                       float* out_dev, void* stream) {
   if (!ctx || block_bytes_of(type) == 0) return fail(ctx, SI_E_UNSUPPORTED, "unsupported quantized type");
   if (elements == 0 || elements % 256) return fail(ctx, SI_E_INVALID, "element count must be a non-zero multiple of 256");
@@ -383,6 +403,13 @@ int si_dequantize_dev(si_ctx* ctx, uint32_t type, const void* bytes_dev, uint64_
                  stream ? static_cast<cudaStream_t>(stream) : ctx->stream);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SI_OK : cuda_fail(ctx, e, "dequant launch");
+}
+
+int si_dequantize_dev(si_ctx* ctx, uint32_t type, const void* bytes_dev, uint64_t elements,
+                      float* out_dev, void* stream) {
+  const int rc = dequantize_dev_impl(ctx, type, bytes_dev, elements, out_dev, stream);
+  if (rc == SI_OK) note_async_submission(ctx);
+  return rc;
 }
 
 int si_dequantize(si_ctx* ctx, uint32_t type, const void* bytes, uint64_t nbytes,
@@ -414,7 +441,7 @@ int si_q4_k_embedding_row(si_ctx* ctx, const void* row, uint64_t nbytes, uint64_
 }
 
 // ---- matvec --------------------------------------------------------------------
-int si_qmatvec_dev(si_ctx* ctx, uint32_t type, const void* w_dev, uint64_t rows, uint64_t cols,
+static int qmatvec_dev_impl(si_ctx* ctx, uint32_t type, const void* w_dev, uint64_t rows, uint64_t cols,
                    const float* x_dev, float* y_dev, void* stream) {
   if (!ctx) return SI_E_INVALID;
   int rc = check_qmv(ctx, type, rows * (cols / 256) * block_bytes_of(type), rows, cols);
@@ -435,6 +462,13 @@ int si_qmatvec_dev(si_ctx* ctx, uint32_t type, const void* w_dev, uint64_t rows,
   rc = launch_qmv(p, stream ? static_cast<cudaStream_t>(stream) : ctx->stream, ctx->sm_count,
                   true, &msg);
   return rc ? fail(ctx, rc, msg) : SI_OK;
+}
+
+int si_qmatvec_dev(si_ctx* ctx, uint32_t type, const void* w_dev, uint64_t rows, uint64_t cols,
+                   const float* x_dev, float* y_dev, void* stream) {
+  const int rc = qmatvec_dev_impl(ctx, type, w_dev, rows, cols, x_dev, y_dev, stream);
+  if (rc == SI_OK) note_async_submission(ctx);
+  return rc;
 }
 
 int si_gguf_quant_matvec_bytes(si_ctx* ctx, uint32_t type, const void* w, uint64_t nbytes,
@@ -586,7 +620,7 @@ int si_gguf_quant_matmul_many_weight(si_ctx* ctx, const si_weight* w, uint64_t r
   return qmm_host(ctx, w->type, wd, rows, cols, batch, inputs, outputs);
 }
 
-int si_qmatmul_many_dev(si_ctx* ctx, uint32_t type, const void* w_dev, uint64_t rows, uint64_t cols, uint64_t batch,
+static int qmatmul_many_dev_impl(si_ctx* ctx, uint32_t type, const void* w_dev, uint64_t rows, uint64_t cols, uint64_t batch,
                         const float* x_dev, float* y_dev, void* stream) {
   if (!ctx) return SI_E_INVALID;
   if (batch == 0 || batch > kQmmMaxBatch || rows == 0 || cols == 0 || cols % 256 || rows > 0xffffffffull)
@@ -615,6 +649,13 @@ int si_qmatmul_many_dev(si_ctx* ctx, uint32_t type, const void* w_dev, uint64_t 
   std::string msg;
   int rc = launch_qmm(p, stream ? static_cast<cudaStream_t>(stream) : ctx->stream, ctx->sm_count, true, &msg);
   return rc ? fail(ctx, rc, msg) : SI_OK;
+}
+
+int si_qmatmul_many_dev(si_ctx* ctx, uint32_t type, const void* w_dev, uint64_t rows, uint64_t cols, uint64_t batch,
+                        const float* x_dev, float* y_dev, void* stream) {
+  const int rc = qmatmul_many_dev_impl(ctx, type, w_dev, rows, cols, batch, x_dev, y_dev, stream);
+  if (rc == SI_OK) note_async_submission(ctx);
+  return rc;
 }
 
 int si_f32_matvec(si_ctx* ctx, const float* w, uint64_t rows, uint64_t cols, const float* x,
@@ -646,7 +687,7 @@ int si_f32_matvec(si_ctx* ctx, const float* w, uint64_t rows, uint64_t cols, con
 }
 
 // ---- fused SwiGLU ------------------------------------------------------------
-int si_fused_gate_up_dev(si_ctx* ctx, uint32_t type, const void* gate_dev, const void* up_dev,
+static int fused_gate_up_dev_impl(si_ctx* ctx, uint32_t type, const void* gate_dev, const void* up_dev,
                          uint64_t rows, uint64_t cols, const float* x_dev, float* out_dev,
                          void* stream) {
   if (!ctx) return SI_E_INVALID;
@@ -667,12 +708,29 @@ int si_fused_gate_up_dev(si_ctx* ctx, uint32_t type, const void* gate_dev, const
   return rc ? fail(ctx, rc, msg) : SI_OK;
 }
 
+int si_fused_gate_up_dev(si_ctx* ctx, uint32_t type, const void* gate_dev, const void* up_dev,
+                         uint64_t rows, uint64_t cols, const float* x_dev, float* out_dev,
+                         void* stream) {
+  const int rc = fused_gate_up_dev_impl(ctx, type, gate_dev, up_dev, rows, cols, x_dev, out_dev, stream);
+  if (rc == SI_OK) note_async_submission(ctx);
+  return rc;
+}
+
+static int fused_mlp_dev_impl(si_ctx* ctx, uint32_t gate_type, const void* gate_dev, const void* up_dev,
+                     uint32_t down_type, const void* down_dev, uint64_t inter, uint64_t hidden,
+                     const float* x_dev, float* act_dev, float* y_dev, void* stream) {
+  int rc = fused_gate_up_dev_impl(ctx, gate_type, gate_dev, up_dev, inter, hidden, x_dev, act_dev, stream);
+  if (rc) return rc;
+  return qmatvec_dev_impl(ctx, down_type, down_dev, hidden, inter, act_dev, y_dev, stream);
+}
+
 int si_fused_mlp_dev(si_ctx* ctx, uint32_t gate_type, const void* gate_dev, const void* up_dev,
                      uint32_t down_type, const void* down_dev, uint64_t inter, uint64_t hidden,
                      const float* x_dev, float* act_dev, float* y_dev, void* stream) {
-  int rc = si_fused_gate_up_dev(ctx, gate_type, gate_dev, up_dev, inter, hidden, x_dev, act_dev, stream);
-  if (rc) return rc;
-  return si_qmatvec_dev(ctx, down_type, down_dev, hidden, inter, act_dev, y_dev, stream);
+  const int rc =
+      fused_mlp_dev_impl(ctx, gate_type, gate_dev, up_dev, down_type, down_dev, inter, hidden, x_dev, act_dev, y_dev, stream);
+  if (rc == SI_OK) note_async_submission(ctx);
+  return rc;
 }
 
 static int gate_up_impl(si_ctx* ctx, const uint8_t* g, const uint8_t* u, uint64_t rows,
@@ -680,7 +738,7 @@ static int gate_up_impl(si_ctx* ctx, const uint8_t* g, const uint8_t* u, uint64_
   int rc;
   if ((rc = h2d(ctx, ctx->in[0], x, cols * 4, "fused gate/up input"))) return rc;
   if (!ctx->out[0].ensure(rows * 4)) return fail(ctx, SI_E_NOMEM, "fused gate/up output allocation failed");
-  if ((rc = si_fused_gate_up_dev(ctx, SI_GGML_TYPE_Q4_K, g, u, rows, cols, ctx->in[0].as<float>(),
+  if ((rc = fused_gate_up_dev_impl(ctx, SI_GGML_TYPE_Q4_K, g, u, rows, cols, ctx->in[0].as<float>(),
                                  ctx->out[0].as<float>(), ctx->stream)))
     return rc;
   if ((rc = d2h(ctx, out, ctx->out[0].p, rows * 4, "fused gate/up readback"))) return rc;
@@ -738,7 +796,7 @@ int si_gguf_quant_fused_mlp_weights(si_ctx* ctx, const si_weight* gate, const si
   if ((rc = h2d(ctx, ctx->in[0], x, cols * 4, "fused MLP input"))) return rc;
   if (!ctx->out[0].ensure(gate_rows * 4) || !ctx->out[1].ensure(down_rows * 4))
     return fail(ctx, SI_E_NOMEM, "fused MLP output allocation failed");
-  if ((rc = si_fused_mlp_dev(ctx, gate->type, g, u, down->type, d, gate_rows, cols,
+  if ((rc = fused_mlp_dev_impl(ctx, gate->type, g, u, down->type, d, gate_rows, cols,
                              ctx->in[0].as<float>(), ctx->out[0].as<float>(), ctx->out[1].as<float>(),
                              ctx->stream)))
     return rc;

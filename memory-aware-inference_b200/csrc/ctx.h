@@ -75,7 +75,7 @@ struct si_ctx {
   si::DevBuf in[6], out[3], wbuf[3], scratch;
   // telemetry
   std::atomic<uint64_t> allocated{0}, peak_allocated{0}, peak_weights{0}, weights{0};
-  std::atomic<uint64_t> peak_kv{0}, peak_scratch{0}, submitted{0}, waited{0}, wait_nanos{0};
+  std::atomic<uint64_t> peak_kv{0}, peak_scratch{0}, submitted{0}, waited{0}, wait_nanos{0}, async_submitted{0};
   // NCCL (optional)
   si_comm_state* comm = nullptr;
   int nranks = 1, rank = 0;
@@ -89,4 +89,5 @@ int cuda_fail(si_ctx* ctx, cudaError_t e, const char* what);
 int sync_and_check(si_ctx* ctx, const char* what);
 void note_alloc(si_ctx* ctx, int64_t delta);
 void note_weights(si_ctx* ctx, int64_t delta);
+void note_async_submission(si_ctx* ctx);
 }  // namespace si
