@@ -48,3 +48,15 @@ def test_config_helper():
     assert (c.attn_q_heads, c.attn_kv_heads, c.attn_head_dim, c.rotary_dim) == (24, 4, 256, 64)
     assert (c.gdn_key_heads, c.gdn_value_heads, c.gdn_head_dim, c.conv_kernel) == (16, 48, 128, 4)
     assert abs(c.rope_theta - 1e7) < 1 and c.attn_interval == 4
+
+
+def test_every_entry_point_is_documented_for_binders():
+    """INTEGRATION.md names every function the header declares, so a binding
+    author sees the whole surface."""
+    import re
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    header = open(os.path.join(root, "include", "si_cuda.h")).read()
+    doc = open(os.path.join(root, "INTEGRATION.md")).read()
+    names = sorted(set(re.findall(r"\b(si_[a-z0-9_]+)\s*\(", header)))
+    missing = [n for n in names if not re.search(r"\b%s\b" % n, doc)]
+    assert not missing, missing
