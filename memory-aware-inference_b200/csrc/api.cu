@@ -1139,10 +1139,10 @@ int si_gguf_quant_matvec_many_tensors(si_ctx* ctx, const si_gguf* g, uint32_t n,
     const uint64_t bb = block_bytes_of(t.type);
     if (t.ndim != 2 || t.dims[0] != cols || !bb)
       return fail(ctx, SI_E_INVALID, "quantized matvec group tensor shapes or types differ");
-    const uint64_t rows = t.dims[1], blocks = cols / 256;
-    if ((blocks && rows > UINT64_MAX / blocks) || (rows * blocks && bb > UINT64_MAX / (rows * blocks)))
+    uint64_t row_bytes = 0;
+    if (__builtin_mul_overflow(cols / 256, uint64_t(bb), &row_bytes) ||
+        __builtin_mul_overflow(row_bytes, t.dims[1], &expected[i]))
       return fail(ctx, SI_E_INVALID, "quantized matvec group byte length overflows");
-    expected[i] = rows * blocks * bb;
     if (t.data_len < expected[i]) return fail(ctx, SI_E_INVALID, "quantized matvec group tensor is truncated");
   }
   std::vector<uint8_t> buf;

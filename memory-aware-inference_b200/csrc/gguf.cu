@@ -191,7 +191,7 @@ int gguf_parse(const char* path, si_gguf** out, std::string* err) {
     fclose(f);
     return SI_E_INVALID;
   }
-  Reader r{f, uint64_t(st.st_size)};
+  Reader r{f, uint64_t(st.st_size), 0, {}};
   auto g = new si_gguf();
   g->path = path;
   g->file_size = uint64_t(st.st_size);
@@ -609,7 +609,7 @@ struct JsonReader {
 };
 
 bool json_top_level_strings(const std::string& text, std::map<std::string, std::string>* out, std::string* err) {
-  JsonReader r{text};
+  JsonReader r{text, 0, {}};
   r.ws();
   if (r.i >= text.size() || text[r.i] != '{') {
     *err = "invalid model manifest JSON: expected an object";

@@ -207,7 +207,6 @@ void launch_gdn_step(float* state, const float* q, const float* k, const float* 
 // (qwen35.rs:163-225): S is read and written once.
 // ---------------------------------------------------------------------------
 constexpr int kGdnD = 128;
-constexpr int kGdnMaxK = 8;
 
 template <int K>
 __device__ __forceinline__ float conv_silu_fixed(float xin, const float* st, const float* wc) {

@@ -137,8 +137,6 @@ struct si_model {
 
 namespace {
 
-int model_fail(si_model* m, int code, const std::string& msg) { return fail(m ? m->ctx : nullptr, code, msg); }
-
 // Full tensor shapes of one layer / the globals (qwen35_runtime.rs:419-446,
 // 640-657, model.rs:418-441).
 void full_spec(const si_model_config& c, bool gdn, bool globals, LayerLayout* L) {
