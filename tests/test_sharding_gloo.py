@@ -116,7 +116,7 @@ def test_two_gloo_ranks_agree_on_shards_and_timing():
     mai = load_package()
     c = mai.qwen36_27b_config()
     world = 2
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()  # no fork of this multi-threaded process
     out = mgr.dict()
     mp.spawn(_worker, args=(world, _free_port(), out), nprocs=world, join=True)
     for rank in range(world):
