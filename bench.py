@@ -119,9 +119,13 @@ def dist_init(args):
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
+        import datetime
         import torch.distributed as dist
         backend = "gloo" if args.impl == "reference" else "nccl"
-        dist.init_process_group(backend)
+        # a rank that dies or never joins ends the others' next collective (or
+        # the rendezvous) with an error after this long, not torch's 30 minutes
+        timeout = datetime.timedelta(seconds=float(os.environ.get("SI_DIST_TIMEOUT_S", "600")))
+        dist.init_process_group(backend, timeout=timeout)
     return world, rank, local
 
 

@@ -129,3 +129,48 @@ def test_two_gloo_ranks_agree_on_shards_and_timing():
             full = mai.shard_rows(c, 1, 0, layer, t)
             assert len(cov) == sum(e - b for b, e in full)
             assert all(len(v) == 1 for v in cov.values())
+
+
+def _failing_worker(rank, world, port, mode, out):
+    """Rank 1 either never joins the group or leaves it between steps; rank 0
+    must get an error from the rendezvous or its next collective, not hang."""
+    import sys
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), SI_DIST_TIMEOUT_S="5")
+    sys.path.insert(0, REPO)
+    import bench
+
+    class Args:
+        impl = "reference"  # gloo
+
+    if rank == 1:
+        if mode == "never_joins":
+            return
+        bench.dist_init(Args())
+        dist.barrier()  # one step together, then leave before the next
+        dist.destroy_process_group()
+        return
+    t0 = time.time()
+    try:
+        bench.dist_init(Args())
+        if mode == "leaves":
+            dist.barrier()
+            time.sleep(1.0)
+        bench.max_over_ranks(1.0, world)
+        out[rank] = ("no error", time.time() - t0)
+    except Exception as e:  # the failure arrives on the host as an exception
+        out[rank] = (type(e).__name__, time.time() - t0)
+
+
+@pytest.mark.parametrize("mode", ["never_joins", "leaves"])
+def test_a_missing_rank_is_reported_not_waited_for(mode):
+    world = 2
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.spawn(_failing_worker, args=(world, _free_port(), mode, out), nprocs=world, join=True)
+    kind, seconds = out[0]
+    assert kind != "no error"
+    assert seconds < 60
+    if mode == "never_joins":
+        assert seconds >= 4  # the rendezvous waited for the configured 5 s, then failed
