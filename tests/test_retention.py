@@ -134,3 +134,45 @@ def test_stride_residency_kat(mai):  # qwen35_runtime.rs:2340-2347
     assert res(stride=2, offset=0) == [True, False, True, False]
     assert res(stride=2, offset=1) == [False, True, False, True]
     assert res(stride=0, offset=1) == [False] * 4
+
+
+def test_plan_invariants_hold_for_random_policies(mai):
+    """Property test over random shapes, budgets, depths, ranks and policies:
+    every layer's bytes are either resident or streamed once per token; a
+    budgeted plan fits its budget; an exact policy keeps exactly its layers;
+    a non-exact one keeps at least them; failures are statuses, not crashes."""
+    from hypothesis import given, settings, strategies as st
+
+    @settings(max_examples=300, deadline=None, derandomize=True)
+    @given(layers=st.sampled_from([4, 8, 12, 64]), hidden=st.sampled_from([512, 1024, 5120]),
+           vocab=st.sampled_from([2048, 248320]), frac=st.one_of(st.just(0.0), st.floats(0.55, 1.3)),
+           depth=st.integers(0, 6),
+           nranks=st.sampled_from([1, 2, 4]), prefix=st.integers(0, 70), stride=st.integers(0, 9),
+           offset=st.integers(0, 9), listed=st.lists(st.integers(0, 63), max_size=5), exact=st.booleans())
+    def check(layers, hidden, vocab, frac, depth, nranks, prefix, stride, offset, listed, exact):
+        c = mai.qwen36_27b_config(layers=layers, hidden=hidden, vocab=vocab, intermediate=2 * hidden,
+                                  kv_capacity=64)
+        listed = [l for l in listed if l < layers]
+        rank = nranks - 1
+        whole = mai.plan_dry(c, nranks, rank, 0, 3)
+        budget = int((whole["resident_weight_bytes"] + whole["state_bytes"] + whole["scratch_bytes"]) * frac)
+        r = mai.retention(prefix_layers=prefix, stride=stride, offset=offset, layers=listed, exact=exact)
+        want = [l < prefix or (stride and l % stride == offset % stride) or l in listed for l in range(layers)]
+        try:
+            p = mai.plan_dry(c, nranks, rank, budget, depth, r)
+        except mai.SiError as e:
+            assert e.status == mai.SI_E_BUDGET and budget > 0, str(e)
+            return
+        assert p["resident_weight_bytes"] + p["streamed_bytes_per_token"] == whole["resident_weight_bytes"]
+        assert p["resident_layers"] + p["streamed_layers"] == layers == len(p["resident"])
+        assert p["resident_layers"] == sum(p["resident"])
+        if budget:
+            assert p["resident_weight_bytes"] + p["ring_bytes"] + p["state_bytes"] + p["scratch_bytes"] <= budget
+        if exact:
+            assert p["resident"] == want
+        else:
+            assert all(p["resident"][l] for l in range(layers) if want[l])
+        assert (p["ring_bytes"] > 0) == (p["streamed_layers"] > 0)
+        assert p["stage_depth"] == (0 if not p["streamed_layers"] else (min(depth, 4) if depth else 3))
+
+    check()
