@@ -446,6 +446,18 @@ int si_gguf_qwen35_layer_kind(const si_gguf* g, uint32_t layer, uint32_t* kind);
  * *known = 0 for types other than F32, F16, BF16 and the K-quants. */
 int si_gguf_tensor_payload(const si_gguf* g, uint64_t index, uint64_t* elements, uint64_t* expected_bytes,
                            uint32_t* known);
+/* GgufModelStore::stage_qwen35_layer_packed (model.rs:920-985): the tensors
+ * of blk.<layer>. other than F32 ones and those named in `excluded`, ordered
+ * by file offset and read as runs (a tensor that starts within 4096 bytes of
+ * the current run's end extends it; the bytes between are read too), packed
+ * back to back. The ranges, in name order, locate each tensor in the packed
+ * bytes; the pair feeds si_staged_layer_upload / _bind_host directly. */
+typedef struct si_gguf_packed si_gguf_packed;
+int si_gguf_stage_layer_packed(const si_gguf* g, uint32_t layer, const char* const* excluded, uint32_t n_excluded,
+                               si_gguf_packed** out);
+int si_gguf_packed_info(const si_gguf_packed* p, const void** bytes, uint64_t* nbytes, uint32_t* n_ranges);
+int si_gguf_packed_range(const si_gguf_packed* p, uint32_t i, const char** name, uint64_t* start, uint64_t* end);
+void si_gguf_packed_free(si_gguf_packed* p);
 /* gguf_quant_matvec_many_tensors (metal.rs:4532-4638): n K-quant tensors of
  * an open GGUF file that share x (x_len must equal their column count), with
  * the reference's checks: same columns, rank 2, a K-quant type, a payload that

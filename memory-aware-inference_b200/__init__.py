@@ -197,6 +197,10 @@ def lib():
         "si_staged_layer_free": ([vp], None),
         "si_gguf_matvec_tensor_rows": ([vp, vp, u64, u64, u64, vp, vp], i32),
         "si_gguf_quant_matvec_many_tensors": ([vp, vp, u32, vp, vp, u64, vp], i32),
+        "si_gguf_stage_layer_packed": ([vp, u32, vp, u32, vp], i32),
+        "si_gguf_packed_info": ([vp, vp, vp, vp], i32),
+        "si_gguf_packed_range": ([vp, u32, vp, vp, vp], i32),
+        "si_gguf_packed_free": ([vp], None),
         "si_gguf_q4_k_embedding": ([vp, vp, u64, u64, vp], i32),
         "si_sample_allocated": ([vp], i32),
         "si_gguf_quant_matmul_many_bytes": ([vp, u32, vp, u64, u64, u64, u64, vp, vp], i32),
@@ -894,6 +898,29 @@ class GgufFile:
         n, b, k = C.c_uint64(), C.c_uint64(), C.c_uint32()
         _gck(lib().si_gguf_tensor_payload(self.h, index, C.byref(n), C.byref(b), C.byref(k)))
         return n.value, (b.value if k.value else None)
+
+    def stage_layer_packed(self, layer: int, excluded=()):
+        """GgufModelStore::stage_qwen35_layer_packed: (packed bytes, {name:
+        (start, end)}) of a layer's quantized tensors, read from the file as
+        merged runs; the pair feeds CudaContext.upload_staged_layer_private."""
+        names = [n.encode() for n in excluded]
+        arr = (C.c_char_p * max(len(names), 1))(*names)
+        h = C.c_void_p()
+        _gck(lib().si_gguf_stage_layer_packed(self.h, layer, arr, len(names), C.byref(h)))
+        try:
+            ptr, nb, nr = C.c_void_p(), C.c_uint64(), C.c_uint32()
+            _gck(lib().si_gguf_packed_info(h, C.byref(ptr), C.byref(nb), C.byref(nr)))
+            data = np.empty(nb.value, np.uint8)
+            if nb.value:
+                C.memmove(data.ctypes.data, ptr.value, nb.value)
+            ranges = {}
+            for i in range(nr.value):
+                name, a, b = C.c_char_p(), C.c_uint64(), C.c_uint64()
+                _gck(lib().si_gguf_packed_range(h, i, C.byref(name), C.byref(a), C.byref(b)))
+                ranges[name.value.decode()] = (a.value, b.value)
+            return data, ranges
+        finally:
+            lib().si_gguf_packed_free(h)
 
     def qwen35_config(self, kv_capacity: int = 0) -> SiModelConfig:
         c = SiModelConfig()

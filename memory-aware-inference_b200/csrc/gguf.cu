@@ -8,6 +8,8 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <memory>
+#include <set>
 #include <cctype>
 #include <cerrno>
 #include <cmath>
@@ -478,6 +480,87 @@ int si_gguf_read(const si_gguf* g, uint64_t index, uint64_t offset, void* dst, u
   int rc = si::gguf_read(g, t.data_start + offset, dst, bytes, &err);
   return rc ? si::fail(nullptr, rc, err) : SI_OK;
 }
+
+}  // extern "C"
+
+// A layer's payloads packed for staging (StagedQwenLayer, model.rs:588-592).
+struct si_gguf_packed {
+  std::vector<uint8_t> bytes;
+  std::vector<std::string> names;  // sorted, as the reference's BTreeMap
+  std::vector<uint64_t> starts, ends;
+};
+
+extern "C" {
+
+int si_gguf_stage_layer_packed(const si_gguf* g, uint32_t layer, const char* const* excluded, uint32_t n_excluded,
+                               si_gguf_packed** out) {
+  if (!g || !out || (n_excluded && !excluded)) return si::fail(nullptr, SI_E_INVALID, "invalid staging arguments");
+  *out = nullptr;
+  std::set<std::string> skip;
+  for (uint32_t i = 0; i < n_excluded; ++i)
+    if (excluded[i]) skip.insert(excluded[i]);
+  const std::string prefix = "blk." + std::to_string(layer) + ".";
+  // the layer's quantized tensors in name order, then stably by file offset
+  std::vector<const si::GgufTensor*> infos;
+  for (const auto& kv : g->index) {
+    const si::GgufTensor& t = g->tensors[kv.second];
+    if (kv.first.compare(0, prefix.size(), prefix) == 0 && !skip.count(kv.first) && t.type != 0) infos.push_back(&t);
+  }
+  std::stable_sort(infos.begin(), infos.end(),
+                   [](const si::GgufTensor* a, const si::GgufTensor* b) { return a->data_start < b->data_start; });
+  // nearby payloads are read together: a tensor starting within 4096 bytes
+  // of the current run's end extends it
+  std::vector<std::pair<uint64_t, uint64_t>> runs;
+  for (const si::GgufTensor* t : infos) {
+    const uint64_t end = t->data_start + t->data_len;
+    if (!runs.empty() && t->data_start <= runs.back().second + 4096)
+      runs.back().second = std::max(runs.back().second, end);
+    else
+      runs.push_back({t->data_start, end});
+  }
+  uint64_t total = 0;
+  for (const auto& r : runs) total += r.second - r.first;  // runs lie inside the file
+  auto p = std::make_unique<si_gguf_packed>();
+  p->bytes.resize(total);
+  std::map<std::string, std::pair<uint64_t, uint64_t>> ranges;
+  uint64_t off = 0;
+  for (const auto& r : runs) {
+    std::string err;
+    if (int rc = si::gguf_read(g, r.first, p->bytes.data() + off, r.second - r.first, &err))
+      return si::fail(nullptr, rc, "read packed staged layer: " + err);
+    for (const si::GgufTensor* t : infos)
+      if (t->data_start >= r.first && t->data_start + t->data_len <= r.second) {
+        const uint64_t a = off + (t->data_start - r.first);
+        ranges[t->name] = {a, a + t->data_len};
+      }
+    off += r.second - r.first;
+  }
+  for (const auto& kv : ranges) {
+    p->names.push_back(kv.first);
+    p->starts.push_back(kv.second.first);
+    p->ends.push_back(kv.second.second);
+  }
+  *out = p.release();
+  return SI_OK;
+}
+
+int si_gguf_packed_info(const si_gguf_packed* p, const void** bytes, uint64_t* nbytes, uint32_t* n_ranges) {
+  if (!p) return SI_E_INVALID;
+  if (bytes) *bytes = p->bytes.data();
+  if (nbytes) *nbytes = p->bytes.size();
+  if (n_ranges) *n_ranges = uint32_t(p->names.size());
+  return SI_OK;
+}
+
+int si_gguf_packed_range(const si_gguf_packed* p, uint32_t i, const char** name, uint64_t* start, uint64_t* end) {
+  if (!p || i >= p->names.size()) return si::fail(nullptr, SI_E_INVALID, "staged range index out of range");
+  if (name) *name = p->names[i].c_str();
+  if (start) *start = p->starts[i];
+  if (end) *end = p->ends[i];
+  return SI_OK;
+}
+
+void si_gguf_packed_free(si_gguf_packed* p) { delete p; }
 
 }  // extern "C"
 

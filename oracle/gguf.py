@@ -195,3 +195,33 @@ def layer_kind(tensor_names, layer: int, interval: int) -> str:
     if kind != want:
         raise GgufError(f"Qwen3.6 layer {layer} tensor kind disagrees with interval {interval}")
     return kind
+
+
+def stage_layer_packed(data: bytes, parsed: dict, layer: int, excluded=()) -> tuple:
+    """GgufModelStore::stage_qwen35_layer_packed (model.rs:920-985): the
+    non-F32 tensors of blk.<layer>. that are not excluded, ordered by file
+    offset, read as runs (a tensor starting within 4096 bytes of the current
+    run's end extends it), packed back to back. Returns (bytes, {name:
+    (start, end)}) with offsets into the packed bytes."""
+    by_name = {}
+    for t in parsed["tensors"]:  # a later duplicate name replaces the earlier one
+        by_name[t["name"]] = t
+    prefix = f"blk.{layer}."
+    infos = [by_name[n] for n in sorted(by_name)
+             if n.startswith(prefix) and n not in set(excluded) and by_name[n]["ggml_type"] != 0]
+    infos.sort(key=lambda t: t["data_start"])  # stable
+    runs = []
+    for t in infos:
+        if runs and t["data_start"] <= runs[-1][1] + 4096:
+            runs[-1][1] = max(runs[-1][1], t["data_end"])
+        else:
+            runs.append([t["data_start"], t["data_end"]])
+    out, ranges, off = bytearray(), {}, 0
+    for a, b in runs:
+        out += data[a:b]
+        for t in infos:
+            if t["data_start"] >= a and t["data_end"] <= b:
+                s = off + (t["data_start"] - a)
+                ranges[t["name"]] = (s, s + t["data_end"] - t["data_start"])
+        off += b - a
+    return bytes(out), ranges

@@ -125,3 +125,27 @@ def test_grouped_matvec_over_file_tensors(mai, ctx, tmp_path):
             ctx.gguf_quant_matvec_many_tensors(g, ["q4", "f"], x)
         with pytest.raises(mai.SiError, match="shapes or types differ"):
             ctx.gguf_quant_matvec_many_tensors(g, ["q4", "narrow"], x)
+
+
+def test_file_staging_pipeline(mai, ctx, tmp_path):
+    """stage_qwen35_layer_packed -> upload_staged_qwen_layer_private ->
+    matvec, the reference's staging-worker path, from a GGUF file."""
+    rng = np.random.default_rng(21)
+    q4 = random_blocks(rng, Q4, 96 * 512 // 256)
+    q6 = random_blocks(rng, Q6, 512 * 256 // 256)
+    other = random_blocks(rng, Q4, 64 * 512 // 256)
+    path = tmp_path / "s.gguf"
+    W.write(path, [("general.architecture", W.STRING, "qwen35")],
+            [("blk.2.ffn_up.weight", [512, 96], Q4, q4.tobytes()), ("blk.3.ffn_up.weight", [512, 64], Q4, other.tobytes()),
+             ("blk.2.ffn_down.weight", [256, 512], Q6, q6.tobytes())], alignment=256)
+    x512 = rng.normal(0, 1, 512).astype(np.float32)
+    x256 = rng.normal(0, 1, 256).astype(np.float32)
+    with mai.GgufFile(path) as g:
+        packed, ranges = g.stage_layer_packed(2)
+    assert sorted(ranges) == ["blk.2.ffn_down.weight", "blk.2.ffn_up.weight"]
+    layer = ctx.upload_staged_layer_private(packed, ranges)
+    up = layer.quant_weight("blk.2.ffn_up.weight", Q4)
+    down = layer.quant_weight("blk.2.ffn_down.weight", Q6)
+    assert rel_l2(ctx.gguf_quant_matvec_weight(up, 96, 512, x512), O.matvec(Q4, q4, 96, 512, x512)) < 1e-5
+    assert rel_l2(ctx.gguf_quant_matvec_weight(down, 512, 256, x256), O.matvec(Q6, q6, 512, 256, x256)) < 1e-5
+    layer.close()
