@@ -458,6 +458,11 @@ int si_gguf_stage_layer_packed(const si_gguf* g, uint32_t layer, const char* con
 int si_gguf_packed_info(const si_gguf_packed* p, const void** bytes, uint64_t* nbytes, uint32_t* n_ranges);
 int si_gguf_packed_range(const si_gguf_packed* p, uint32_t i, const char** name, uint64_t* start, uint64_t* end);
 void si_gguf_packed_free(si_gguf_packed* p);
+/* GgufModelStore::advise_qwen35_layer (model.rs:986-1024): ask the kernel to
+ * read ahead every tensor of blk.<layer>. (posix_fadvise WILLNEED over
+ * page-aligned payload ranges; a hint that moves no bytes). *advised = the
+ * page-aligned bytes named, as the reference returns. */
+int si_gguf_advise_layer(const si_gguf* g, uint32_t layer, uint64_t* advised);
 /* gguf_quant_matvec_many_tensors (metal.rs:4532-4638): n K-quant tensors of
  * an open GGUF file that share x (x_len must equal their column count), with
  * the reference's checks: same columns, rank 2, a K-quant type, a payload that

@@ -201,6 +201,7 @@ def lib():
         "si_gguf_packed_info": ([vp, vp, vp, vp], i32),
         "si_gguf_packed_range": ([vp, u32, vp, vp, vp], i32),
         "si_gguf_packed_free": ([vp], None),
+        "si_gguf_advise_layer": ([vp, u32, vp], i32),
         "si_gguf_q4_k_embedding": ([vp, vp, u64, u64, vp], i32),
         "si_sample_allocated": ([vp], i32),
         "si_gguf_quant_matmul_many_bytes": ([vp, u32, vp, u64, u64, u64, u64, vp, vp], i32),
@@ -898,6 +899,13 @@ class GgufFile:
         n, b, k = C.c_uint64(), C.c_uint64(), C.c_uint32()
         _gck(lib().si_gguf_tensor_payload(self.h, index, C.byref(n), C.byref(b), C.byref(k)))
         return n.value, (b.value if k.value else None)
+
+    def advise_layer(self, layer: int) -> int:
+        """GgufModelStore::advise_qwen35_layer: read-ahead hint for a layer;
+        returns the page-aligned bytes advised."""
+        n = C.c_uint64()
+        _gck(lib().si_gguf_advise_layer(self.h, layer, C.byref(n)))
+        return n.value
 
     def stage_layer_packed(self, layer: int, excluded=()):
         """GgufModelStore::stage_qwen35_layer_packed: (packed bytes, {name:

@@ -562,6 +562,25 @@ int si_gguf_packed_range(const si_gguf_packed* p, uint32_t i, const char** name,
 
 void si_gguf_packed_free(si_gguf_packed* p) { delete p; }
 
+int si_gguf_advise_layer(const si_gguf* g, uint32_t layer, uint64_t* advised) {
+  if (!g) return si::fail(nullptr, SI_E_INVALID, "invalid advise arguments");
+  const long page = sysconf(_SC_PAGESIZE);
+  if (page <= 0) return si::fail(nullptr, SI_E_INVALID, "page size is invalid");
+  const uint64_t ps = uint64_t(page);
+  const std::string prefix = "blk." + std::to_string(layer) + ".";
+  uint64_t total = 0;
+  for (const auto& kv : g->index) {
+    if (kv.first.compare(0, prefix.size(), prefix) != 0) continue;
+    const si::GgufTensor& t = g->tensors[kv.second];
+    const uint64_t a = t.data_start & ~(ps - 1), b = (t.data_start + t.data_len + ps - 1) & ~(ps - 1);
+    if (b <= a) continue;
+    (void)posix_fadvise(g->fd, off_t(a), off_t(b - a), POSIX_FADV_WILLNEED);  // a hint: its result is not an error
+    total += b - a;
+  }
+  if (advised) *advised = total;
+  return SI_OK;
+}
+
 }  // extern "C"
 
 namespace {

@@ -73,3 +73,22 @@ def test_packed_staging_read_failure(mai, layered):
         finally:
             mai.fault_inject(0)
         assert g.stage_layer_packed(0)[0].size > 0
+
+
+def test_advise_layer_counts_page_aligned_payloads(mai, layered):  # model.rs:986-1024
+    import os
+    path, data, parsed = layered
+    page = os.sysconf("SC_PAGE_SIZE")
+    want = {}
+    for layer in (0, 1, 10, 7):
+        by_name = {t["name"]: t for t in parsed["tensors"]}
+        total = 0
+        for name, t in by_name.items():
+            if name.startswith(f"blk.{layer}."):
+                a = t["data_start"] // page * page
+                b = -(-t["data_end"] // page) * page
+                total += max(b - a, 0)
+        want[layer] = total
+    with mai.GgufFile(path) as g:
+        assert {layer: g.advise_layer(layer) for layer in want} == want
+    assert want[0] > 0 and want[7] == 0
