@@ -463,6 +463,12 @@ void si_gguf_packed_free(si_gguf_packed* p);
  * page-aligned payload ranges; a hint that moves no bytes). *advised = the
  * page-aligned bytes named, as the reference returns. */
 int si_gguf_advise_layer(const si_gguf* g, uint32_t layer, uint64_t* advised);
+/* GgufModelStore::dequantize_q4_k / _q5_k / _q6_k (model.rs:792-850): the
+ * whole tensor `index`, which must be of `ggml_type`, dequantised
+ * (bit-exact); out_len = its element count. The reference's messages for a
+ * type mismatch and a short payload. */
+int si_gguf_dequantize_tensor(si_ctx* ctx, const si_gguf* g, uint64_t index, uint32_t ggml_type, float* out,
+                              uint64_t out_len);
 /* gguf_quant_matvec_many_tensors (metal.rs:4532-4638): n K-quant tensors of
  * an open GGUF file that share x (x_len must equal their column count), with
  * the reference's checks: same columns, rank 2, a K-quant type, a payload that

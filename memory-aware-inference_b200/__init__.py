@@ -202,6 +202,7 @@ def lib():
         "si_gguf_packed_range": ([vp, u32, vp, vp, vp], i32),
         "si_gguf_packed_free": ([vp], None),
         "si_gguf_advise_layer": ([vp, u32, vp], i32),
+        "si_gguf_dequantize_tensor": ([vp, vp, u64, u32, vp, u64], i32),
         "si_gguf_q4_k_embedding": ([vp, vp, u64, u64, vp], i32),
         "si_sample_allocated": ([vp], i32),
         "si_gguf_quant_matmul_many_bytes": ([vp, u32, vp, u64, u64, u64, u64, vp, vp], i32),
@@ -588,6 +589,14 @@ class CudaContext:
         ya = (C.c_void_p * max(len(idx), 1))(*[o.ctypes.data for o in outs])
         self._ck(lib().si_gguf_quant_matvec_many_tensors(self.h, gguf.h, len(idx), ia, _p(xs), xs.size, ya))
         return outs
+
+    def dequantize_gguf_tensor(self, gguf: "GgufFile", name_or_index, ggml_type: int) -> np.ndarray:
+        """GgufModelStore::dequantize_q4_k / _q5_k / _q6_k on the device."""
+        idx = gguf.find(name_or_index) if isinstance(name_or_index, str) else int(name_or_index)
+        n = int(np.prod(gguf.tensor_info(idx)["shape"], dtype=np.uint64))
+        out = np.empty(n, np.float32)
+        self._ck(lib().si_gguf_dequantize_tensor(self.h, gguf.h, idx, ggml_type, _p(out), n))
+        return out
 
     def q4_k_embedding_tensor(self, gguf: "GgufFile", name_or_index, token_id) -> np.ndarray:
         """MetalContext::q4_k_embedding_tensor over a tensor of an open GGUF file."""

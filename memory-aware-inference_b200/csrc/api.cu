@@ -1157,6 +1157,36 @@ int si_gguf_quant_matvec_many_tensors(si_ctx* ctx, const si_gguf* g, uint32_t n,
   return SI_OK;
 }
 
+int si_gguf_dequantize_tensor(si_ctx* ctx, const si_gguf* g, uint64_t index, uint32_t type, float* out,
+                              uint64_t out_len) {
+  if (!ctx) return SI_E_INVALID;
+  if (!g || (!out && out_len)) return fail(ctx, SI_E_INVALID, "invalid tensor dequant arguments");
+  if (index >= g->tensors.size()) return fail(ctx, SI_E_INVALID, "GGUF tensor index out of range");
+  const GgufTensor& t = g->tensors[index];
+  const uint32_t bb = block_bytes_of(type);
+  if (!bb) return fail(ctx, SI_E_UNSUPPORTED, "unsupported quantized type");
+  if (t.type != type)
+    return fail(ctx, SI_E_INVALID,
+                type == SI_GGML_TYPE_Q4_K
+                    ? "GGUF tensor " + t.name + " is not Q4_K (type " + std::to_string(t.type) + ")"
+                    : "GGUF tensor " + t.name + " has type " + std::to_string(t.type) + "; expected " +
+                          std::to_string(type));
+  uint64_t elements = 1;
+  for (uint64_t d : t.dims)
+    if (__builtin_mul_overflow(elements, d, &elements))
+      return fail(ctx, SI_E_INVALID, "GGUF tensor " + t.name + " element count overflows");
+  if (elements % 256) return fail(ctx, SI_E_INVALID, "GGUF tensor " + t.name + " has unknown payload size");
+  const uint64_t expected = elements / 256 * bb;
+  if (t.data_len < expected)
+    return fail(ctx, SI_E_INVALID, "GGUF tensor " + t.name + " has " + std::to_string(t.data_len) +
+                                       " bytes; expected at least " + std::to_string(expected));
+  if (out_len != elements) return fail(ctx, SI_E_INVALID, "dequantized output length is invalid");
+  std::vector<uint8_t> buf(expected);
+  std::string err;
+  if (int rc = gguf_read(g, t.data_start, buf.data(), expected, &err)) return fail(ctx, rc, err);
+  return si_dequantize(ctx, type, buf.data(), expected, elements, out);
+}
+
 int si_gguf_q4_k_embedding(si_ctx* ctx, const si_gguf* g, uint64_t index, uint64_t token, float* out) {
   if (!ctx || !g || !out) return fail(ctx, SI_E_INVALID, "invalid embedding arguments");
   if (index >= g->tensors.size()) return fail(ctx, SI_E_INVALID, "GGUF tensor index out of range");

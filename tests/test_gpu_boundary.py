@@ -149,3 +149,21 @@ def test_file_staging_pipeline(mai, ctx, tmp_path):
     assert rel_l2(ctx.gguf_quant_matvec_weight(up, 96, 512, x512), O.matvec(Q4, q4, 96, 512, x512)) < 1e-5
     assert rel_l2(ctx.gguf_quant_matvec_weight(down, 512, 256, x256), O.matvec(Q6, q6, 512, 256, x256)) < 1e-5
     layer.close()
+
+
+def test_dequantize_file_tensor(mai, ctx, tmp_path):  # model.rs:792-850
+    rng = np.random.default_rng(5)
+    q5 = random_blocks(rng, Q5, 24)
+    q6 = random_blocks(rng, Q6, 8)
+    path = tmp_path / "d.gguf"
+    W.write(path, [("general.architecture", W.STRING, "qwen35")],
+            [("a", [512, 12], Q5, q5.tobytes()), ("b", [256, 8], Q6, q6.tobytes())])
+    with mai.GgufFile(path) as g:
+        a = ctx.dequantize_gguf_tensor(g, "a", Q5)
+        assert np.array_equal(a.view(np.uint32), O.dequantize(Q5, q5, 512 * 12).view(np.uint32))
+        b = ctx.dequantize_gguf_tensor(g, "b", Q6)
+        assert np.array_equal(b.view(np.uint32), O.dequantize(Q6, q6, 256 * 8).view(np.uint32))
+        with pytest.raises(mai.SiError, match="GGUF tensor a is not Q4_K \\(type 13\\)"):
+            ctx.dequantize_gguf_tensor(g, "a", Q4)
+        with pytest.raises(mai.SiError, match="GGUF tensor b has type 14; expected 13"):
+            ctx.dequantize_gguf_tensor(g, "b", Q5)
