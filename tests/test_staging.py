@@ -92,3 +92,38 @@ def test_advise_layer_counts_page_aligned_payloads(mai, layered):  # model.rs:98
     with mai.GgufFile(path) as g:
         assert {layer: g.advise_layer(layer) for layer in want} == want
     assert want[0] > 0 and want[7] == 0
+
+
+def test_packed_staging_matches_restatement_on_random_files(mai, tmp_path):
+    """Random files: tensor order, sizes (some over the 4096-byte merge
+    gap), types (F32 among them), alignment, layer and exclusions."""
+    from hypothesis import given, settings, strategies as st
+
+    tensor = st.tuples(st.integers(0, 3), st.sampled_from(["a", "b", "c", "d", "e"]),
+                       st.sampled_from([Q4, Q6, F32]), st.integers(1, 40))
+
+    @settings(max_examples=150, deadline=None, derandomize=True)
+    @given(ts=st.lists(tensor, min_size=1, max_size=12), alignment=st.sampled_from([32, 64, 4096, 8192]),
+           layer=st.integers(0, 3), nexcl=st.integers(0, 3), seed=st.integers(0, 1 << 16))
+    def check(ts, alignment, layer, nexcl, seed):
+        rng = np.random.default_rng(seed)
+        tensors, names = [], set()
+        for lay, suffix, ty, n in ts:
+            name = f"blk.{lay}.{suffix}.weight"
+            if name in names:
+                continue
+            names.add(name)
+            size = {Q4: 144, Q6: 210, F32: 1024}[ty] * n
+            shape = [256, n] if ty != F32 else [256 * n]
+            tensors.append((name, shape, ty, blob(rng, size)))
+        path = tmp_path / f"r{seed}.gguf"
+        W.write(path, [("general.architecture", W.STRING, "qwen35")], tensors, alignment=alignment)
+        data = path.read_bytes()
+        parsed = OG.parse(data)
+        excl = sorted(names)[:nexcl]
+        want_bytes, want_ranges = OG.stage_layer_packed(data, parsed, layer, excl)
+        with mai.GgufFile(path) as g:
+            got, ranges = g.stage_layer_packed(layer, excl)
+        assert got.tobytes() == want_bytes and ranges == want_ranges
+
+    check()
