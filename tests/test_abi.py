@@ -60,3 +60,39 @@ def test_every_entry_point_is_documented_for_binders():
     names = sorted(set(re.findall(r"\b(si_[a-z0-9_]+)\s*\(", header)))
     missing = [n for n in names if not re.search(r"\b%s\b" % n, doc)]
     assert not missing, missing
+
+
+def test_plain_c_program_uses_the_abi(tmp_path):
+    """The header is C99 (-pedantic -Werror), and a C program linked against
+    the library plans the 27B shape without a device, as a cgo / FFI caller
+    would."""
+    import subprocess
+    load_package().lib()  # the library is built
+    lib_dir = os.path.join(REPO, "memory-aware-inference_b200")
+    src = tmp_path / "use_abi.c"
+    src.write_text(r"""
+#include <stdio.h>
+#include "si_cuda.h"
+int main(void) {
+  si_model_config c;
+  si_plan_info p;
+  si_retention keep = {0};
+  si_model_config_qwen36_27b(&c);
+  if (si_model_plan_dry(&c, 1, 0, 4ull << 30, 3, &p) != SI_OK) return 1;
+  keep.prefix_layers = 2;
+  keep.flags = SI_RETAIN_EXACT;
+  unsigned char resident[64];
+  si_plan_info q;
+  if (si_model_plan_dry_retained(&c, 1, 0, 0, 3, &keep, &q, resident) != SI_OK) return 2;
+  if (si_model_plan_dry(&c, 1, 0, 1ull << 30, 3, &p) != SI_E_BUDGET) return 3;
+  printf("%u %u %u %u\n", p.streamed_layers, q.resident_layers, resident[1], resident[2]);
+  return 0;
+}
+""")
+    exe = tmp_path / "use_abi"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", os.path.join(REPO, "include"),
+                    str(src), "-L", lib_dir, "-lsi_cuda", f"-Wl,-rpath,{lib_dir}", "-o", str(exe)], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, (r.returncode, r.stderr)
+    streamed_4gb, resident_exact, r1, r2 = map(int, r.stdout.split())
+    assert (streamed_4gb, resident_exact, r1, r2) == (55, 2, 1, 0)
