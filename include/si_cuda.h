@@ -4,7 +4,7 @@
  * (`MetalContext`, src/metal.rs) of vrlda/memory-aware-inference on the
  * batch-1 decode hot path. Every entry point names the reference method it
  * replaces (file:line inside the reference project). A Rust FFI crate binds
- * these symbols one-to-one (see INTEGRATION.md) and keeps the reference's
+ * these symbols one-to-one and keeps the reference's
  * `Result<Vec<f32>, String>` surface: a non-zero status maps to `Err` with the
  * text of si_last_error().
  *

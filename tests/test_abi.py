@@ -51,7 +51,7 @@ def test_config_helper():
 
 
 def test_every_entry_point_is_documented_for_binders():
-    """INTEGRATION.md names every function the header declares, so a binding
+    """The integration guide names every function the header declares, so a binding
     author sees the whole surface."""
     import re
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
