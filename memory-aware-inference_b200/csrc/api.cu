@@ -924,11 +924,12 @@ int si_attention_decode(si_ctx* ctx, const si_attention_decode_input* in, float*
   if (!ctx || !in) return SI_E_INVALID;
   std::lock_guard<std::mutex> lk(ctx->mu);
   const uint64_t qh = in->query_heads, kvh = in->key_value_heads, hd = in->head_dim;
-  if (qh == 0 || kvh == 0 || hd == 0 || qh % kvh)
+  if (qh > 0xffffffffull || kvh > 0xffffffffull || hd > 0xffffffffull || qh == 0 || kvh == 0 || hd == 0 ||
+      qh % kvh)
     return fail(ctx, SI_E_INVALID, "attention head dimensions are invalid");
   if (hd > 256 || qh / kvh > 8)
     return fail(ctx, SI_E_UNSUPPORTED, "attention head_dim > 256 or GQA group > 8 is not supported");
-  if (in->cached_tokens > in->cache_capacity_tokens)
+  if (in->cached_tokens > in->cache_capacity_tokens || in->cache_capacity_tokens > 0xffffffffull)
     return fail(ctx, SI_E_INVALID, "attention cached token count exceeds cache capacity");
   if (in->cached_tokens + 1 > kAttnMaxTokens)
     return fail(ctx, SI_E_UNSUPPORTED, "attention over more than 1048576 tokens is not supported");
