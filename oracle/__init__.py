@@ -258,3 +258,40 @@ class OracleModel:
         if n < 0:
             raise OracleError(f"generate failed with {n}")
         return out[:n].tolist()
+
+
+def _tensor_table(tensors):
+    """tensors: {tensor id: (numpy array, ggml type)} -> ctypes pointer/type arrays (23 ids)."""
+    ptrs = (C.c_void_p * 23)()
+    types = (C.c_uint32 * 23)()
+    for tid, (arr, ty) in tensors.items():
+        ptrs[tid] = arr.ctypes.data
+        types[tid] = ty
+    return ptrs, types
+
+
+def gdn_layer(config, tensors, x, conv_state, rec_state, gates=None, threads: int = 0):
+    """gdn_token_mixer (qwen35_runtime.rs:409-624) on one token: x is the mixer
+    input; conv_state ([channels][kernel-1]) and rec_state ([vh][128][128]) are
+    updated in place; gates, if given, is [g[vh], beta[vh]] used as is.
+    Returns the mixer output [hidden]."""
+    ptrs, types = _tensor_table(tensors)
+    out = np.empty(config.hidden, np.float32)
+    g = None if gates is None else np.ascontiguousarray(gates, np.float32)
+    _check(lib().or_gdn_layer(C.byref(config), ptrs, types, np.ascontiguousarray(x, np.float32), conv_state,
+                              rec_state, None if g is None else g.ctypes.data_as(C.c_void_p), out, threads),
+           "gdn_layer")
+    return out
+
+
+def attention_layer(config, tensors, x, position, kc, vc, cached, threads: int = 0):
+    """attention_token_mixer (qwen35_runtime.rs:628-867) over bf16 head-major
+    caches kc/vc ([kvh][kv_capacity][hd], uint16, appended in place at
+    `cached`). Returns (mixer output [hidden], new cached count)."""
+    ptrs, types = _tensor_table(tensors)
+    out = np.empty(config.hidden, np.float32)
+    n = C.c_size_t(cached)
+    _check(lib().or_attention_layer(C.byref(config), ptrs, types, np.ascontiguousarray(x, np.float32), position,
+                                    kc.ctypes.data_as(C.c_void_p), vc.ctypes.data_as(C.c_void_p), C.byref(n), out,
+                                    threads), "attention_layer")
+    return out, n.value

@@ -183,25 +183,43 @@ size_t row_bytes(uint32_t type, size_t cols) {
 
 // metal.rs:7476-7484 (the matvec test's CPU reference): dequantize, then a
 // sequential f32 sum of w*x per row. Rows run in parallel; each row's order
-// is the reference's.
+// is the reference's. Eight rows are summed side by side, one super-block of
+// columns at a time: each row keeps its own sequential chain (the same
+// additions in the same order), the eight independent chains only let the
+// core overlap them.
 void matvec(uint32_t type, const uint8_t* w, size_t rows, size_t cols, const float* x,
             float* y, int threads) {
-  size_t rb = row_bytes(type, cols);
+  constexpr size_t RG = 8;
+  const size_t rb = row_bytes(type, cols), bb = size_t(block_bytes(type)), nb = cols / kQK;
+  const long groups = long((rows + RG - 1) / RG);
 #pragma omp parallel num_threads(threads)
   {
-    std::vector<float> tmp(cols);
+    std::vector<float> tmp(RG * kQK);
 #pragma omp for schedule(static)
-    for (long r = 0; r < long(rows); ++r) {
-      const float* wr;
-      if (type == SI_GGML_TYPE_F32) {
-        wr = reinterpret_cast<const float*>(w + size_t(r) * rb);
-      } else {
-        deq_row(type, w + size_t(r) * rb, cols, tmp.data());
-        wr = tmp.data();
+    for (long gi = 0; gi < groups; ++gi) {
+      const size_t r0 = size_t(gi) * RG, nr = std::min(RG, rows - r0);
+      float s[RG] = {};
+      // F32 rows may end in a partial super-block of columns
+      const size_t nbt = type == SI_GGML_TYPE_F32 ? (cols + kQK - 1) / kQK : nb;
+      for (size_t b = 0; b < nbt; ++b) {
+        const int len = int(std::min<size_t>(kQK, cols - b * kQK));
+        const float* wr[RG];
+        for (size_t r = 0; r < RG; ++r) {
+          if (type == SI_GGML_TYPE_F32) {
+            wr[r] = reinterpret_cast<const float*>(w + (r0 + std::min(r, nr - 1)) * rb) + b * kQK;
+            continue;
+          }
+          deq_block(type, w + (r0 + std::min(r, nr - 1)) * rb + b * bb, tmp.data() + r * kQK);
+          wr[r] = tmp.data() + r * kQK;
+        }
+        const float* xb = x + b * kQK;
+        for (int c = 0; c < len; ++c) {
+          const float xv = xb[c];
+#pragma GCC unroll 8
+          for (size_t r = 0; r < RG; ++r) s[r] += wr[r][c] * xv;
+        }
       }
-      float s = 0.0f;
-      for (size_t c = 0; c < cols; ++c) s += wr[c] * x[c];
-      y[r] = s;
+      for (size_t r = 0; r < nr; ++r) y[r0 + r] = s[r];
     }
   }
 }
