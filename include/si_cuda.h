@@ -265,9 +265,79 @@ int si_attention_decode(si_ctx* ctx, const si_attention_decode_input* in, float*
  * most max(ceil((n+1)/256), min(ceil(n/64), 148/kvh)) splits for n cached
  * tokens) fail with SI_E_UNSUPPORTED. Calls share that array, so calls
  * that overlap on the GPU race. The first call on a device looks up the
- * array's address; make it before any stream capture. Errors are reported
+ * array's address; make it before any stream capture (a first call during a
+ * capture fails with SI_E_UNSUPPORTED). A split whose bounded wait for K/V
+ * tiles runs out (about 2 s) contributes nothing and sets a device error
+ * word; a later call made outside a capture, on a stream that has drained,
+ * returns SI_E_TIMEOUT for it and clears the word. Errors are reported
  * through si_global_last_error(). */
 int si_attention_decode_noalloc_dev(const si_attention_decode_input* in, float* out, void* stream);
+
+/* ---- whole token mixers of one decoder layer (device buffers) ----------- */
+/* The Gated DeltaNet token mixer of one layer (gdn_token_mixer,
+ * qwen35_runtime.rs:409-624): qkv and z projections of x, causal conv + SiLU,
+ * q/k L2 norms, key-head repeat, the gates, the recurrent update, the gated
+ * RMSNorm (w, not 1+w) and ssm_out. x is the mixer input (the block's
+ * attn_norm output); `out` receives the mixer output without the residual.
+ * Matrices are [rows][cols] GGUF K-quant rows; F32 tensors row-major. */
+typedef struct si_gdn_layer_desc {
+  uint64_t hidden;                 /* x / out width, a multiple of 256 */
+  uint32_t key_heads, value_heads; /* value head h uses key head h / (value_heads / key_heads) */
+  uint32_t head_dim;               /* 128 */
+  uint32_t conv_kernel;            /* 2..8 */
+  float epsilon;                   /* gated RMSNorm epsilon */
+  const void* qkv; uint32_t qkv_type; /* [(2 kh + vh) * 128][hidden]: q | k | v channels */
+  const void* z; uint32_t z_type;     /* [vh * 128][hidden] */
+  const void* out; uint32_t out_type; /* [hidden][vh * 128] */
+  const float* conv;               /* [(2 kh + vh) * 128][conv_kernel] */
+  const float* norm;               /* [128] gated-norm weight */
+  const float* alpha;              /* [vh][hidden]; these four are read only when gates == NULL */
+  const float* beta;               /* [vh][hidden] */
+  const float* a_log;              /* [vh] */
+  const float* dt_bias;            /* [vh] */
+} si_gdn_layer_desc;
+/* Floats of device workspace si_gdn_layer_dev needs: (2 kh + vh) * 128 + 2 vh * 128 + 2 vh. */
+uint64_t si_gdn_layer_workspace_floats(const si_gdn_layer_desc* desc);
+/* Device pointers throughout; enqueued on `stream` (NULL = the context's
+ * stream), nothing allocated or synchronised. conv_state_in/out are
+ * [(2 kh + vh) * 128][conv_kernel - 1] (chronological) and must differ;
+ * state is the f32 recurrent state [vh][128][128], updated in place. gates,
+ * if not NULL, is [g[vh], beta[vh]] used as is (g = -softplus(...) already,
+ * beta = sigmoid(...) already); else g and beta come from the alpha/beta
+ * projections, a_log and dt_bias (qwen35_runtime.rs:577-601). x and work are
+ * 16-byte aligned; work holds si_gdn_layer_workspace_floats(desc) floats. */
+int si_gdn_layer_dev(si_ctx* ctx, const si_gdn_layer_desc* desc, const float* x, const float* conv_state_in,
+                     float* conv_state_out, float* state, const float* gates, float* out, float* work,
+                     void* stream);
+
+/* The full-attention token mixer of one layer (attention_token_mixer,
+ * qwen35_runtime.rs:628-867) over a bf16 head-major KV cache
+ * [kv_heads][capacity][head_dim] (cache.rs:1-4): q (the first half of the q
+ * projection; the second half is the output gate), k and v projections; (1+w)
+ * head RMSNorm of q and k; partial RoPE on dims [0, rotary_dim) at `position`
+ * (metal.rs:1655-1679); attention over the cached tokens plus the new one
+ * (scores scaled by 1/sqrt(head_dim)); the new key and value appended at slot
+ * cached_tokens; out = o-proj of (attention * sigmoid(gate)), no residual. */
+typedef struct si_attention_layer_desc {
+  uint64_t hidden;                 /* x / out width, a multiple of 256 */
+  uint32_t query_heads, kv_heads, head_dim, rotary_dim;
+  float rope_theta, epsilon;
+  const void* q; uint32_t q_type;  /* [2 * qh * hd][hidden]: queries, then the gate */
+  const void* k; uint32_t k_type;  /* [kvh * hd][hidden] */
+  const void* v; uint32_t v_type;  /* [kvh * hd][hidden] */
+  const void* o; uint32_t o_type;  /* [hidden][qh * hd] */
+  const float* q_norm;             /* [hd] (1+w) */
+  const float* k_norm;             /* [hd] (1+w) */
+} si_attention_layer_desc;
+/* Floats of device workspace si_attention_layer_dev needs with
+ * `cached_tokens` tokens in the cache (0 when the arguments are invalid). */
+uint64_t si_attention_layer_workspace_floats(const si_attention_layer_desc* desc, uint64_t cached_tokens);
+/* Device pointers throughout; enqueued on `stream` (NULL = the context's
+ * stream), nothing allocated or synchronised. cached_tokens < capacity_tokens
+ * (SI_E_STATE otherwise). x and work are 16-byte aligned. */
+int si_attention_layer_dev(si_ctx* ctx, const si_attention_layer_desc* desc, const float* x, uint64_t position,
+                           uint16_t* key_cache, uint16_t* value_cache, uint64_t cached_tokens,
+                           uint64_t capacity_tokens, float* out, float* work, void* stream);
 
 /* ---- greedy argmax (runtime.rs:4301-4309) -------------------------------- */
 /* Largest finite value under f32::total_cmp; the last index among equals. */

@@ -26,6 +26,11 @@ LIB_PATH = os.path.join(_HERE, "libsi_cuda.so")
 GGML_TYPE_F32, GGML_TYPE_Q4_K, GGML_TYPE_Q5_K, GGML_TYPE_Q6_K = 0, 12, 13, 14
 BLOCK_BYTES = {GGML_TYPE_Q4_K: 144, GGML_TYPE_Q5_K: 176, GGML_TYPE_Q6_K: 210}
 CACHE_F32, CACHE_BF16 = 0, 1
+# tensor ids of one decoder layer and of the globals (si_cuda.h SI_T_*)
+(SI_T_ATTN_NORM, SI_T_POST_NORM, SI_T_FFN_GATE, SI_T_FFN_UP, SI_T_FFN_DOWN, SI_T_SSM_QKV, SI_T_SSM_Z,
+ SI_T_SSM_ALPHA, SI_T_SSM_BETA, SI_T_SSM_CONV, SI_T_SSM_A, SI_T_SSM_DT, SI_T_SSM_NORM, SI_T_SSM_OUT,
+ SI_T_ATTN_Q, SI_T_ATTN_K, SI_T_ATTN_V, SI_T_ATTN_O, SI_T_ATTN_QNORM, SI_T_ATTN_KNORM, SI_T_TOKEN_EMBD,
+ SI_T_OUTPUT_NORM, SI_T_OUTPUT, SI_T_COUNT) = range(24)
 SI_OK, SI_E_INVALID, SI_E_CUDA, SI_E_NOMEM, SI_E_BUDGET, SI_E_TIMEOUT, SI_E_COMM, SI_E_STATE, SI_E_UNSUPPORTED = \
     0, -1, -2, -3, -4, -5, -6, -7, -8
 CTX_FLAG_NCCL_COLLECTIVES = 1  # sharded models exchange vectors with NCCL, not NVLink peer stores
@@ -93,6 +98,24 @@ class SiAttentionDecodeInput(C.Structure):
                 ("new_keys", C.c_void_p), ("new_values", C.c_void_p), ("query_heads", C.c_uint64),
                 ("key_value_heads", C.c_uint64), ("head_dim", C.c_uint64), ("cached_tokens", C.c_uint64),
                 ("cache_capacity_tokens", C.c_uint64), ("cache_type", C.c_int)]
+
+
+class SiGdnLayerDesc(C.Structure):
+    """si_gdn_layer_desc: one Gated DeltaNet token mixer (qwen35_runtime.rs:409-624)."""
+    _fields_ = [("hidden", C.c_uint64), ("key_heads", C.c_uint32), ("value_heads", C.c_uint32),
+                ("head_dim", C.c_uint32), ("conv_kernel", C.c_uint32), ("epsilon", C.c_float),
+                ("qkv", C.c_void_p), ("qkv_type", C.c_uint32), ("z", C.c_void_p), ("z_type", C.c_uint32),
+                ("out", C.c_void_p), ("out_type", C.c_uint32), ("conv", C.c_void_p), ("norm", C.c_void_p),
+                ("alpha", C.c_void_p), ("beta", C.c_void_p), ("a_log", C.c_void_p), ("dt_bias", C.c_void_p)]
+
+
+class SiAttentionLayerDesc(C.Structure):
+    """si_attention_layer_desc: one full-attention token mixer (qwen35_runtime.rs:628-867)."""
+    _fields_ = [("hidden", C.c_uint64), ("query_heads", C.c_uint32), ("kv_heads", C.c_uint32),
+                ("head_dim", C.c_uint32), ("rotary_dim", C.c_uint32), ("rope_theta", C.c_float),
+                ("epsilon", C.c_float), ("q", C.c_void_p), ("q_type", C.c_uint32), ("k", C.c_void_p),
+                ("k_type", C.c_uint32), ("v", C.c_void_p), ("v_type", C.c_uint32), ("o", C.c_void_p),
+                ("o_type", C.c_uint32), ("q_norm", C.c_void_p), ("k_norm", C.c_void_p)]
 
 
 class SiModelConfig(C.Structure):
@@ -221,6 +244,10 @@ def lib():
         "si_attention_decode": ([vp, vp, vp], i32),
         "si_argmax": ([vp, vp, u64, vp], i32),
         "si_attention_decode_noalloc_dev": ([vp, vp, vp], i32),
+        "si_gdn_layer_workspace_floats": ([vp], u64),
+        "si_gdn_layer_dev": ([vp, vp, vp, vp, vp, vp, vp, vp, vp, vp], i32),
+        "si_attention_layer_workspace_floats": ([vp, u64], u64),
+        "si_attention_layer_dev": ([vp, vp, vp, u64, vp, vp, u64, u64, vp, vp, vp], i32),
         "si_model_config_qwen36_27b": ([vp], None),
         "si_model_create_synthetic": ([vp, vp, u64, vp], i32),
         "si_model_create_gguf": ([vp, C.c_char_p, u32, vp], i32),
@@ -719,6 +746,27 @@ class CudaContext:
 
     def dequantize_dev(self, ggml_type, w, elements, out, stream=None):
         self._ck(lib().si_dequantize_dev(self.h, ggml_type, _p(w), elements, _p(out), stream))
+
+    def gdn_layer_dev(self, desc: "SiGdnLayerDesc", x, conv_state_in, conv_state_out, state, gates, out, work,
+                      stream=None):
+        """si_gdn_layer_dev: one Gated DeltaNet token mixer on device buffers."""
+        self._ck(lib().si_gdn_layer_dev(self.h, C.byref(desc), _p(x), _p(conv_state_in), _p(conv_state_out),
+                                        _p(state), _p(gates), _p(out), _p(work), stream))
+
+    def attention_layer_dev(self, desc: "SiAttentionLayerDesc", x, position, key_cache, value_cache, cached_tokens,
+                            capacity_tokens, out, work, stream=None):
+        """si_attention_layer_dev: one full-attention token mixer on device buffers (bf16 cache)."""
+        self._ck(lib().si_attention_layer_dev(self.h, C.byref(desc), _p(x), position, _p(key_cache),
+                                              _p(value_cache), cached_tokens, capacity_tokens, _p(out), _p(work),
+                                              stream))
+
+
+def gdn_layer_workspace_floats(desc: "SiGdnLayerDesc") -> int:
+    return int(lib().si_gdn_layer_workspace_floats(C.byref(desc)))
+
+
+def attention_layer_workspace_floats(desc: "SiAttentionLayerDesc", cached_tokens: int) -> int:
+    return int(lib().si_attention_layer_workspace_floats(C.byref(desc), cached_tokens))
 
 
 def attention_decode_noalloc_dev(query, key_cache, value_cache, new_keys, new_values, query_heads,

@@ -89,6 +89,11 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// L2 prefetch of `bytes` (multiple of 16) at a 16-byte aligned address.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue (weight prefetch) while this one drains; block until the previous
 // kernel's results are visible before touching activations.

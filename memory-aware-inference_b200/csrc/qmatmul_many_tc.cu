@@ -80,10 +80,6 @@ __device__ __forceinline__ uint4 ldw_u4(const uint8_t* p, uint64_t pol) {
   return v;
 }
 
-// L2 prefetch of `bytes` (multiple of 16) at a 16-byte aligned address.
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
 
 __device__ __forceinline__ uint32_t ldw_u16(const uint8_t* p, uint64_t pol) {
   unsigned short v;
