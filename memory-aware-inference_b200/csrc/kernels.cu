@@ -198,15 +198,20 @@ void launch_gdn_step(float* state, const float* q, const float* k, const float* 
 
 // ---------------------------------------------------------------------------
 // Fused Gated DeltaNet layer step (qwen35_runtime.rs:541-620 + qwen35.rs).
-// One 128-thread CTA per value head h. Thread t owns channel t of the key
-// head's q and k, value channel t of h and state column t. Every global load
-// of the step (conv inputs, conv states and weights of three channels, the
-// gates, the 128 state values of the column) is issued up front, so the step
-// costs about one memory round trip; the q/k L2 norms are reduced across the
-// CTA. Per column, the recurrence keeps the reference's operation order
-// (qwen35.rs:163-225): S is read and written once.
+// Grid (value heads, kGdnSplit): CTA (h, c) owns value head h and state
+// columns [32c, 32c + 32). Its 128 threads each compute the conv + SiLU of one
+// q and one k channel of h's key head (every split needs the whole
+// normalised q and k), and the first 32 threads the conv of the CTA's 32 v
+// channels. For the recurrence, warp w holds rows [32w, 32w + 32) of the
+// CTA's 32 columns (lane = column, 32 registers), so a column's two dot
+// products (S^T k and S^T q) are four 32-term partial sums added in a fixed
+// order across the warps; the per-element updates keep the order of
+// qwen35.rs:163-225. Every global load of the step is issued up front after
+// the PDL wait, so the step costs about one memory round trip.
 // ---------------------------------------------------------------------------
 constexpr int kGdnD = 128;
+constexpr int kGdnSplit = 4;                 // column splits per value head
+constexpr int kGdnCols = kGdnD / kGdnSplit;  // 32 state columns per CTA
 
 template <int K>
 __device__ __forceinline__ float conv_silu_fixed(float xin, const float* st, const float* wc) {
@@ -218,24 +223,36 @@ __device__ __forceinline__ float conv_silu_fixed(float xin, const float* st, con
 
 template <int K>
 __global__ void __launch_bounds__(kGdnD) gdn_layer_kernel(const GdnLayerArgs a) {
-  __shared__ float qs[kGdnD], ks[kGdnD];
+  __shared__ float qs[kGdnD], ks[kGdnD], vs[kGdnCols];
   __shared__ float red[2][kGdnD / 32];
-  const uint32_t h = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  __shared__ float part[kGdnD / 32][kGdnCols];
+  __shared__ float delta_s[kGdnCols];
+  const uint32_t h = blockIdx.x, split = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const uint32_t kh = a.key_heads, vh = a.value_heads;
   const uint32_t rep = vh / kh, khead = h / rep;
   const uint32_t kw = kh * kGdnD;
-  const uint32_t cq = khead * kGdnD + t, ck = kw + cq, cv = 2 * kw + h * kGdnD + t;
+  const uint32_t col = split * kGdnCols + lane;  // this thread's state column
+  const uint32_t cq = khead * kGdnD + t, ck = kw + cq, cv = 2 * kw + h * kGdnD + col;
   pdl_launch_dependents();
   pdl_wait();
   // ---- every load of the step, independent of one another ----
-  float* S = a.state + uint64_t(h) * kGdnD * kGdnD + t;
-  float s[kGdnD];
+  float* S = a.state + uint64_t(h) * kGdnD * kGdnD + uint64_t(warp) * kGdnCols * kGdnD + col;
+  float s[kGdnCols];
 #pragma unroll
-  for (int i = 0; i < kGdnD; ++i) s[i] = S[uint64_t(i) * kGdnD];
+  for (int i = 0; i < kGdnCols; ++i) s[i] = S[uint64_t(i) * kGdnD];
   float xin[3], st[3][K - 1], wc[3][K];
   const uint32_t ch[3] = {cq, ck, cv};
+  const bool has_v = warp == 0;
 #pragma unroll
   for (int j = 0; j < 3; ++j) {
+    if (j == 2 && !has_v) {
+      xin[j] = 0.f;
+#pragma unroll
+      for (int u = 0; u + 1 < K; ++u) st[j][u] = 0.f;
+#pragma unroll
+      for (int u = 0; u < K; ++u) wc[j][u] = 0.f;
+      continue;
+    }
     xin[j] = a.qkv[ch[j]];
 #pragma unroll
     for (int u = 0; u + 1 < K; ++u) st[j][u] = a.conv_in[uint64_t(ch[j]) * (K - 1) + u];
@@ -256,12 +273,14 @@ __global__ void __launch_bounds__(kGdnD) gdn_layer_kernel(const GdnLayerArgs a) 
   // ---- conv + SiLU, conv state shift ----
   const float oq = conv_silu_fixed<K>(xin[0], st[0], wc[0]);
   const float ok = conv_silu_fixed<K>(xin[1], st[1], wc[1]);
-  const float vval = conv_silu_fixed<K>(xin[2], st[2], wc[2]);
+  if (has_v) vs[lane] = conv_silu_fixed<K>(xin[2], st[2], wc[2]);
   {
-    const bool write_qk = (h % rep) == 0;  // one value head per key head owns the q/k state
+    // one CTA per key head owns the q/k conv state; each split its v channels
+    const bool write_qk = (h % rep) == 0 && split == 0;
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
       if (j < 2 && !write_qk) continue;
+      if (j == 2 && !has_v) continue;
       float* so = a.conv_out + uint64_t(ch[j]) * (K - 1);
 #pragma unroll
       for (int u = 0; u + 2 < K; ++u) so[u] = st[j][u + 1];
@@ -293,29 +312,43 @@ __global__ void __launch_bounds__(kGdnD) gdn_layer_kernel(const GdnLayerArgs a) 
     beta = 1.0f / (1.0f + expf(-g_in3));
   }
   __syncthreads();
-  // ---- recurrence on column t ----
+  // ---- recurrence on column `col`, rows [32 warp, 32 warp + 32) ----
   const float decay = expf(g);
+  const float* kr = ks + warp * kGdnCols;
+  const float* qr = qs + warp * kGdnCols;
   float mem = 0.f;
 #pragma unroll
-  for (int i = 0; i < kGdnD; ++i) {
+  for (int i = 0; i < kGdnCols; ++i) {
     s[i] = __fmul_rn(s[i], decay);
-    mem = __fadd_rn(mem, __fmul_rn(s[i], ks[i]));
+    mem = __fadd_rn(mem, __fmul_rn(s[i], kr[i]));
   }
-  const float delta = __fmul_rn(__fsub_rn(vval, mem), beta);
+  part[warp][lane] = mem;
+  __syncthreads();
+  if (warp == 0) {
+    const float m = __fadd_rn(__fadd_rn(part[0][lane], part[1][lane]), __fadd_rn(part[2][lane], part[3][lane]));
+    delta_s[lane] = __fmul_rn(__fsub_rn(vs[lane], m), beta);
+  }
+  __syncthreads();
+  const float delta = delta_s[lane];
   float r = 0.f;
 #pragma unroll
-  for (int i = 0; i < kGdnD; ++i) {
-    s[i] = __fadd_rn(s[i], __fmul_rn(ks[i], delta));
-    r = __fadd_rn(r, __fmul_rn(s[i], qs[i]));
+  for (int i = 0; i < kGdnCols; ++i) {
+    s[i] = __fadd_rn(s[i], __fmul_rn(kr[i], delta));
+    r = __fadd_rn(r, __fmul_rn(s[i], qr[i]));
   }
 #pragma unroll
-  for (int i = 0; i < kGdnD; ++i) S[uint64_t(i) * kGdnD] = s[i];
-  a.core[h * kGdnD + t] = r;
+  for (int i = 0; i < kGdnCols; ++i) S[uint64_t(i) * kGdnD] = s[i];
+  __syncthreads();  // every warp has read part[] for the first reduction
+  part[warp][lane] = r;
+  __syncthreads();
+  if (warp == 0)
+    a.core[h * kGdnD + col] =
+        __fadd_rn(__fadd_rn(part[0][lane], part[1][lane]), __fadd_rn(part[2][lane], part[3][lane]));
 }
 
 void launch_gdn_layer(const GdnLayerArgs& a, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.value_heads);
+  cfg.gridDim = dim3(a.value_heads, kGdnSplit);
   cfg.blockDim = dim3(kGdnD);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
