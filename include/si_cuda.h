@@ -339,6 +339,44 @@ int si_attention_layer_dev(si_ctx* ctx, const si_attention_layer_desc* desc, con
                            uint16_t* key_cache, uint16_t* value_cache, uint64_t cached_tokens,
                            uint64_t capacity_tokens, float* out, float* work, void* stream);
 
+/* ---- row-sharded matvec with the all-gather inside the kernel ----------- */
+/* Row sharding of the matvec over the GPUs of one box is the BASELINE's
+ * multi-GPU partitioning of gguf_quant_matvec_weight (metal.rs:3923); the
+ * reference is single-GPU, so these have no reference counterpart.
+ * A peer buffer: `bytes` of device memory on every rank of the context's
+ * communicator (one rank without one), each rank's copy mapped into every
+ * other rank (CUDA IPC over NVLink). Collective: every rank calls it with the
+ * same size. */
+typedef struct si_peer_buffer si_peer_buffer;
+int si_peer_buffer_create(si_ctx* ctx, uint64_t bytes, si_peer_buffer** out);
+/* A group of `nranks` buffers all on this context's GPU standing in for the
+ * ranks, this process acting as rank `rank`: for testing the exchange on one
+ * GPU. The other ranks never run, so a sharded matvec's wait for them runs out
+ * after about wait_us microseconds (0 = the default of about 2 s) and the next
+ * si_ctx_synchronize reports SI_E_TIMEOUT. */
+int si_peer_buffer_create_local(si_ctx* ctx, uint64_t bytes, uint32_t nranks, uint32_t rank, uint64_t wait_us,
+                                si_peer_buffer** out);
+void si_peer_buffer_destroy(si_peer_buffer* buf);
+/* This rank's copy (device pointer). */
+void* si_peer_buffer_local(const si_peer_buffer* buf);
+/* y = W x with W row-sharded: this rank holds rows
+ * [rank * rows_per_rank, (rank + 1) * rows_per_rank) of W as w_shard (device
+ * memory) and x in full. Every rank's buffer receives the whole y (float32,
+ * nranks * rows_per_rank values) at byte offset y_offset (16-byte aligned).
+ * Q4_K shards run on the tensor-core matvec, whose epilogue stores each row
+ * into every rank's copy over NVLink; the launch ends once every rank's rows
+ * have landed (bounded wait; a timeout sets the context's error word). Other
+ * types: matvec, then a peer all-gather launch. Device pointers, enqueued on
+ * `stream` (NULL = the context's stream), nothing allocated or synchronised.
+ * Every rank must make the same calls in the same order. After SI_E_TIMEOUT
+ * the buffer's exchange state is lost: destroy it and create a new one. */
+int si_sharded_qmatvec_dev(si_ctx* ctx, si_peer_buffer* buf, uint32_t ggml_type, const void* w_shard,
+                           uint64_t rows_per_rank, uint64_t cols, const float* x, uint64_t y_offset, void* stream);
+/* Wait for the context's stream and report device errors (timed-out waits)
+ * of the `_dev` calls enqueued before (commit + wait of the reference's
+ * command buffers, metal.rs:2330-2335). */
+int si_ctx_synchronize(si_ctx* ctx);
+
 /* ---- greedy argmax (runtime.rs:4301-4309) -------------------------------- */
 /* Largest finite value under f32::total_cmp; the last index among equals. */
 int si_argmax(si_ctx* ctx, const float* logits, uint64_t n, uint32_t* index);

@@ -248,6 +248,12 @@ def lib():
         "si_gdn_layer_dev": ([vp, vp, vp, vp, vp, vp, vp, vp, vp, vp], i32),
         "si_attention_layer_workspace_floats": ([vp, u64], u64),
         "si_attention_layer_dev": ([vp, vp, vp, u64, vp, vp, u64, u64, vp, vp, vp], i32),
+        "si_peer_buffer_create": ([vp, u64, vp], i32),
+        "si_peer_buffer_create_local": ([vp, u64, u32, u32, u64, vp], i32),
+        "si_peer_buffer_destroy": ([vp], None),
+        "si_peer_buffer_local": ([vp], vp),
+        "si_sharded_qmatvec_dev": ([vp, vp, u32, vp, u64, u64, vp, u64, vp], i32),
+        "si_ctx_synchronize": ([vp], i32),
         "si_model_config_qwen36_27b": ([vp], None),
         "si_model_create_synthetic": ([vp, vp, u64, vp], i32),
         "si_model_create_gguf": ([vp, C.c_char_p, u32, vp], i32),
@@ -747,6 +753,28 @@ class CudaContext:
     def dequantize_dev(self, ggml_type, w, elements, out, stream=None):
         self._ck(lib().si_dequantize_dev(self.h, ggml_type, _p(w), elements, _p(out), stream))
 
+    def synchronize(self):
+        """si_ctx_synchronize: wait for the context's stream; device errors of earlier `_dev` calls."""
+        self._ck(lib().si_ctx_synchronize(self.h))
+
+    def peer_buffer(self, nbytes: int) -> "PeerBuffer":
+        """si_peer_buffer_create (collective over the context's communicator)."""
+        h = C.c_void_p()
+        self._ck(lib().si_peer_buffer_create(self.h, nbytes, C.byref(h)))
+        return PeerBuffer(self, h.value)
+
+    def peer_buffer_local(self, nbytes: int, nranks: int, rank: int, wait_us: int = 0) -> "PeerBuffer":
+        """si_peer_buffer_create_local: nranks buffers on this GPU, acting as `rank`."""
+        h = C.c_void_p()
+        self._ck(lib().si_peer_buffer_create_local(self.h, nbytes, nranks, rank, wait_us, C.byref(h)))
+        return PeerBuffer(self, h.value, group=nranks)
+
+    def sharded_qmatvec_dev(self, buf: "PeerBuffer", ggml_type, w_shard, rows_per_rank, cols, x, y_offset=0,
+                            stream=None):
+        """si_sharded_qmatvec_dev: row-sharded matvec, the whole y lands in every rank's buffer."""
+        self._ck(lib().si_sharded_qmatvec_dev(self.h, buf.h, ggml_type, _p(w_shard), rows_per_rank, cols, _p(x),
+                                              y_offset, stream))
+
     def gdn_layer_dev(self, desc: "SiGdnLayerDesc", x, conv_state_in, conv_state_out, state, gates, out, work,
                       stream=None):
         """si_gdn_layer_dev: one Gated DeltaNet token mixer on device buffers."""
@@ -759,6 +787,33 @@ class CudaContext:
         self._ck(lib().si_attention_layer_dev(self.h, C.byref(desc), _p(x), position, _p(key_cache),
                                               _p(value_cache), cached_tokens, capacity_tokens, _p(out), _p(work),
                                               stream))
+
+
+class PeerBuffer:
+    """si_peer_buffer: a device buffer on every rank, mapped into every other rank."""
+
+    def __init__(self, ctx, handle, group=None):
+        self.ctx = ctx
+        self.h = handle
+        self.group = group
+
+    @property
+    def local(self) -> int:
+        return lib().si_peer_buffer_local(self.h)
+
+    def close(self):
+        """Destroy the buffer. After its context was closed this only drops the
+        handle: si_peer_buffer_destroy would touch the destroyed context."""
+        if getattr(self, "h", None):
+            if getattr(self.ctx, "h", None):
+                lib().si_peer_buffer_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
 
 
 def gdn_layer_workspace_floats(desc: "SiGdnLayerDesc") -> int:

@@ -22,6 +22,23 @@ struct QmvSeg {
   uint32_t pad;
 };
 
+// Row-sharded output written straight into every rank's copy of the full
+// vector (NVLink peer memory mapped with CUDA IPC) by the matvec epilogue, then
+// a completion signal: each CTA adds 1 to its source slot in every rank's
+// signal words (system-scope release); the last CTA of the launch on each rank
+// waits (bounded) until every source has counted a whole grid more than at the
+// previous launch. The epoch is derived on the device from a ticket counter,
+// so a launch replayed from a CUDA graph synchronises like a fresh one.
+constexpr int kPeerMax = 8;
+struct PeerOut {
+  uint32_t n;                 // ranks; 0 = ordinary output
+  uint32_t rank;
+  float* y[kPeerMax];         // each rank's full vector, offset to this rank's rows
+  uint32_t* sig[kPeerMax];    // each rank's signal words (source s at [16 s])
+  uint32_t* ticket;           // this rank's ticket counter
+  long long wait_cycles;      // bound of the wait for the other ranks
+};
+
 struct QmvParams {
   uint32_t type;        // SI_GGML_TYPE_Q4_K / Q5_K / Q6_K
   uint32_t cols;        // multiple of 256
@@ -36,6 +53,7 @@ struct QmvParams {
   float eps;
   uint32_t head_dim;    // XM_GATED
   int* err;             // device error word
+  PeerOut peer;         // n > 0: sharded output (tensor-core Q4_K kernel only)
 };
 
 // Enqueue one launch. Returns SI_OK or SI_E_* with *msg filled.
@@ -45,6 +63,8 @@ int launch_qmv(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
 // Plain Q4_K matvec on the tensor cores (qmatvec_tc.cu): eligibility and
 // launch; launch_qmv routes eligible calls there.
 bool qmv_tc_eligible(const QmvParams& p);
+// The tensor-core kernel on any row count (the sharded matvec with peer output).
+bool qmv_tc_supported(const QmvParams& p);
 int launch_qmv_tc(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl, std::string* msg);
 
 // Batched matvec Y[k] = W X[k] (+ R[k]) for k < batch, one weight traversal.

@@ -69,7 +69,33 @@ struct TcArgs {
   uint32_t rows, nblk, ngroups, nctas;
   uint32_t mats;         // 1, or 2 for a SwiGLU pair (gate = map 0, up = map 1)
   int* err;
+  PeerOut peer;          // n > 0: the rows go to every rank's vector (NVLink stores)
 };
+
+// After every consumer's stores (bar.sync 1): the CTA's completion signal in
+// every rank's signal words, then, in the launch's last CTA on this rank, the
+// bounded wait for every rank's whole grid (PeerOut, qmatvec.cuh).
+__device__ __noinline__ void peer_complete(const PeerOut& po, uint32_t nctas, int* err) {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  for (uint32_t p = 0; p < po.n; ++p)
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(po.sig[p] + 16 * po.rank) : "memory");
+  const uint32_t old = atomicAdd(po.ticket, 1u);
+  if (old % nctas != nctas - 1) return;
+  const uint32_t target = (old / nctas + 1) * nctas;
+  const uint32_t* mine = po.sig[po.rank];
+  const long long t0 = clock64();
+  for (uint32_t s = 0; s < po.n; ++s) {
+    while (true) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + 16 * s) : "memory");
+      if (int32_t(v - target) >= 0) break;
+      if (clock64() - t0 > po.wait_cycles) {
+        if (err) atomicOr(err, KERR_TIMEOUT_FULL);
+        return;
+      }
+    }
+  }
+}
 
 // C = A B with a zero accumulator (no register moves to clear C).
 __device__ __forceinline__ void mma_u8s8_zero(int* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
@@ -370,8 +396,19 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
       o0 = yg / (1.0f + expf(-yg)) * upv[grp_w * 16 + g];
       o8 = yg8 / (1.0f + expf(-yg8)) * upv[grp_w * 16 + g + 8];
     }
-    if (row < a.rows) a.y[row] = a.resid ? a.resid[row] + o0 : o0;
-    if (row + 8 < a.rows) a.y[row + 8] = a.resid ? a.resid[row + 8] + o8 : o8;
+    if (a.peer.n) {
+      for (uint32_t p = 0; p < a.peer.n; ++p) {
+        if (row < a.rows) a.peer.y[p][row] = o0;
+        if (row + 8 < a.rows) a.peer.y[p][row + 8] = o8;
+      }
+    } else {
+      if (row < a.rows) a.y[row] = a.resid ? a.resid[row] + o0 : o0;
+      if (row + 8 < a.rows) a.y[row + 8] = a.resid ? a.resid[row + 8] + o8 : o8;
+    }
+  }
+  if (a.peer.n) {
+    asm volatile("bar.sync 1, %0;" ::"r"(kTcConsumers * 32) : "memory");
+    if (threadIdx.x == 0) peer_complete(a.peer, a.nctas, a.err);
   }
 }
 
@@ -403,6 +440,18 @@ static bool q4k_band_map(CUtensorMap* m, const void* w, uint32_t rows, uint32_t 
 // Q4_K matvecs with any x transform, residual epilogue and SwiGLU pairing; a
 // grouped call becomes one launch per segment (pairs: one launch), so every
 // row matches a single call on its segment bit for bit.
+bool qmv_tc_supported(const QmvParams& p) {
+  if (p.type != SI_GGML_TYPE_Q4_K || p.cols / 256 > kTcMaxBlocks || (reinterpret_cast<uintptr_t>(p.x) & 15))
+    return false;
+  if (p.xmode == XM_GATED && p.head_dim != 64 && p.head_dim != 128 && p.head_dim != 256) return false;
+  if ((p.xmode == XM_RMS1P || p.xmode == XM_GATED) && !p.xw) return false;
+  if ((p.xmode == XM_GATED || p.xmode == XM_SIGGATE) && !p.xaux) return false;
+  if (p.pair && (p.nseg != 2 || p.seg[0].rows != p.seg[1].rows)) return false;
+  for (uint32_t i = 0; i < p.nseg; ++i)
+    if ((reinterpret_cast<uintptr_t>(p.seg[i].w) & 15) || p.seg[i].rows < 16) return false;
+  return true;
+}
+
 bool qmv_tc_eligible(const QmvParams& p) {
   if (p.type != SI_GGML_TYPE_Q4_K || p.cols / 256 > kTcMaxBlocks || (reinterpret_cast<uintptr_t>(p.x) & 15))
     return false;
@@ -486,6 +535,7 @@ static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stre
   a.nctas = nctas;
   a.mats = mats;
   a.err = p.err;
+  a.peer = p.peer;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nctas);
   cfg.blockDim = dim3(kTcThreads);

@@ -30,3 +30,12 @@ def rel_l2(a, b):
     b = np.asarray(b, np.float64)
     den = np.linalg.norm(b)
     return float(np.linalg.norm(a - b) / (den if den > 0 else 1.0))
+
+
+def d2h_f32(ptr, n):
+    """n float32 values at a raw device address (a buffer the library allocated)."""
+    from cuda.bindings import runtime as rt
+    host = np.empty(n, np.float32)
+    err, = rt.cudaMemcpy(host.ctypes.data, ptr, n * 4, rt.cudaMemcpyKind.cudaMemcpyDeviceToHost)
+    assert int(err) == 0, err
+    return host

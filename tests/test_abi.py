@@ -53,6 +53,8 @@ def test_config_helper():
 # The C ABI's entry points. A change to the header's surface must be made
 # here too, on purpose: bindings (Rust FFI, ctypes) are written against it.
 ABI_ENTRY_POINTS = [
+    'si_peer_buffer_create', 'si_peer_buffer_create_local', 'si_peer_buffer_destroy', 'si_peer_buffer_local',
+    'si_sharded_qmatvec_dev', 'si_ctx_synchronize',
     'si_gdn_layer_workspace_floats', 'si_gdn_layer_dev', 'si_attention_layer_workspace_floats',
     'si_attention_layer_dev',
     'si_argmax', 'si_attention_decode', 'si_attention_decode_noalloc_dev', 'si_causal_conv1d_step',

@@ -69,3 +69,65 @@ def test_row_sharded_decode_matches_one_gpu(mai, transport):
         ids, lb = out[rank]
         assert ids == ref_ids, rank
         assert np.array_equal(np.frombuffer(lb, np.float32), ref_logits), rank
+
+
+def _sharded_worker(rank, world, uid, out):
+    import sys
+    import torch
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, here)
+    from conftest import load_package
+    from helpers import d2h_f32, random_blocks
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    mai = load_package()
+    torch.cuda.set_device(rank)
+    ctx = mai.CudaContext(rank)
+    ctx.comm_init(world, rank, uid)
+    res = {}
+    for name, ty, rows, cols in (("q4k", 12, 17408, 5120), ("q6k", 14, 5120, 17408)):
+        rng = np.random.default_rng(rows + ty)
+        w = random_blocks(rng, ty, rows * cols // 256).reshape(rows, -1)
+        x = rng.normal(0, 1, cols).astype(np.float32)
+        rl = rows // world
+        shard = torch.from_numpy(np.concatenate([w[rank * rl:(rank + 1) * rl].reshape(-1),
+                                                 np.zeros(64, np.uint8)])).to(f"cuda:{rank}")
+        xd = torch.from_numpy(x).to(f"cuda:{rank}")
+        buf = ctx.peer_buffer(rows * 4 + 1024)
+        ys = []
+        for _ in range(2):  # two calls: the signal counters carry over correctly
+            ctx.sharded_qmatvec_dev(buf, ty, shard, rl, cols, xd, 256)
+            ctx.synchronize()
+            ys.append(d2h_f32(buf.local + 256, rows).tobytes())
+        buf.close()
+        res[name] = ys
+    ctx.close()
+    out[rank] = res
+
+
+def test_sharded_matvec_gathers_into_every_rank(mai):
+    """si_sharded_qmatvec_dev on every GPU: Q4_K rows reach every rank from the
+    tensor-core matvec's epilogue (NVLink stores + in-kernel completion
+    signal), Q6_K through the matvec and the peer all-gather kernel. Every
+    rank ends with the same full vector, equal to the oracle within 1e-5."""
+    import torch
+    import torch.multiprocessing as mp
+    import oracle as O
+    from helpers import random_blocks, rel_l2
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least two GPUs")
+    world = 8 if n >= 8 else (4 if n >= 4 else 2)
+    uid = mai.CudaContext.comm_unique_id()
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_sharded_worker, args=(world, uid, out), nprocs=world, join=True)
+    for name, ty, rows, cols in (("q4k", 12, 17408, 5120), ("q6k", 14, 5120, 17408)):
+        rng = np.random.default_rng(rows + ty)
+        w = random_blocks(rng, ty, rows * cols // 256)
+        x = rng.normal(0, 1, cols).astype(np.float32)
+        ref = O.matvec(ty, w, rows, cols, x)
+        first = out[0][name][0]
+        for rank in range(world):
+            for yb in out[rank][name]:
+                assert yb == first, (name, rank)
+        assert rel_l2(np.frombuffer(first, np.float32), ref) < 1e-5, name

@@ -1,0 +1,78 @@
+"""The row-sharded matvec (si_sharded_qmatvec_dev) on one GPU.
+
+With one rank it is the plain matvec into the peer buffer. A group of
+buffers on this GPU standing in for two ranks (si_peer_buffer_create_local)
+exercises the exchange on one device: the matvec's epilogue stores this
+rank's rows into both ranks' copies of the vector, and, because the other
+rank never runs, the launch's bounded wait for it runs out after about a
+millisecond. The timeout is reported as SI_E_TIMEOUT by si_ctx_synchronize,
+and the context then works normally. No wait here is unbounded and nothing
+faults the GPU: the flag that is waited on is simply never set.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from helpers import d2h_f32, random_blocks, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def _read(ptr, n):
+    import torch
+    torch.cuda.synchronize()
+    return d2h_f32(ptr, n)
+
+
+def _matrix(rows, cols, seed=11):
+    rng = np.random.default_rng(seed)
+    w = random_blocks(rng, 12, rows * cols // 256)
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    return w, x
+
+
+def test_one_rank_sharded_matvec_is_the_matvec(mai, ctx):
+    import torch
+    rows, cols = 17408, 5120
+    w, x = _matrix(rows, cols)
+    wd = torch.from_numpy(np.concatenate([w, np.zeros(64, np.uint8)])).cuda()
+    xd = torch.from_numpy(x).cuda()
+    buf = ctx.peer_buffer(rows * 4 + 512)
+    try:
+        ctx.sharded_qmatvec_dev(buf, 12, wd, rows, cols, xd, 512)
+        ctx.synchronize()
+        got = _read(buf.local + 512, rows)
+        y = torch.empty(rows, device="cuda")
+        ctx.qmatvec_dev(12, wd, rows, cols, xd, y)
+        torch.cuda.synchronize()
+        assert np.array_equal(got, y.cpu().numpy())
+        assert rel_l2(got, O.matvec(12, w, rows, cols, x)) < 1e-5
+    finally:
+        buf.close()
+
+
+@pytest.mark.parametrize("rank", [0, 1])
+def test_two_rank_exchange_times_out_without_the_peer(mai, ctx, rank):
+    import torch
+    rows, cols, world = 4352, 5120, 2
+    w, x = _matrix(rows, cols, seed=21 + rank)
+    rl = rows // world
+    shard = np.concatenate([w.reshape(rows, -1)[rank * rl:(rank + 1) * rl].reshape(-1), np.zeros(64, np.uint8)])
+    wd = torch.from_numpy(shard).cuda()
+    xd = torch.from_numpy(x).cuda()
+    ref = O.matvec(12, w, rows, cols, x)[rank * rl:(rank + 1) * rl]
+    buf = ctx.peer_buffer_local(rows * 4, world, rank, wait_us=1000)
+    try:
+        ctx.sharded_qmatvec_dev(buf, 12, wd, rl, cols, xd, 0)
+        with pytest.raises(mai.SiError) as ei:
+            ctx.synchronize()
+        assert ei.value.status == mai.SI_E_TIMEOUT
+        # this rank's rows reached both ranks' copies before the wait ran out
+        local = _read(buf.local, rows)[rank * rl:(rank + 1) * rl]
+        assert rel_l2(local, ref) < 1e-5
+    finally:
+        buf.close()
+    # the context is usable after the timeout
+    got = ctx.q4_k_matvec(w, rows, cols, x)
+    assert rel_l2(got, O.matvec(12, w, rows, cols, x)) < 1e-5
+    ctx.synchronize()
