@@ -120,7 +120,7 @@ __device__ __forceinline__ uint32_t byte_of(uint32_t w, uint32_t j) { return __b
 __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
     qmv_tc_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
                   const __grid_constant__ CUtensorMap up_hi, const __grid_constant__ CUtensorMap up_lo,
-                  const TcArgs a) {
+                  const __grid_constant__ TcArgs a) {
   extern __shared__ __align__(128) uint8_t tsm[];
   uint8_t* ring = tsm;                                          // stages x tile_bytes
   uint8_t* xd = ring + kTcRingBytes;                            // [blk][8 sb][4 planes][32] s8
@@ -205,11 +205,33 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
     for (int w = 0; w < kTcConsumers; ++w) tot += s_red[w];
     rms_inv = 1.0f / sqrtf(tot / float(a.nblk * 256) + a.eps);
   }
-  for (uint32_t b = warp; b < a.nblk; b += kTcConsumers) {
+  // the x loads of the warp's first two blocks leave together (one L2 round
+  // trip instead of two for rows of up to 24 blocks)
+  float4 pre[2][2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const uint32_t b = warp + k * kTcConsumers;
+    if (b < a.nblk) {
+      const float4* xp = reinterpret_cast<const float4*>(a.x + b * 256 + lane * 8);
+      pre[k][0] = xp[0];
+      pre[k][1] = xp[1];
+    }
+  }
+  for (uint32_t b = warp, k = 0; b < a.nblk; b += kTcConsumers, ++k) {
     float v[8];
     const uint32_t e0 = b * 256 + lane * 8;
-    const float4* xp = reinterpret_cast<const float4*>(a.x + e0);
-    const float4 u0 = xp[0], u1 = xp[1];
+    float4 u0, u1;
+    if (k == 0) {
+      u0 = pre[0][0];
+      u1 = pre[0][1];
+    } else if (k == 1) {
+      u0 = pre[1][0];
+      u1 = pre[1][1];
+    } else {
+      const float4* xp = reinterpret_cast<const float4*>(a.x + e0);
+      u0 = xp[0];
+      u1 = xp[1];
+    }
     v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
     v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
     if (a.xmode == XM_RMS1P) {
@@ -283,8 +305,8 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
   uint32_t boff[4];
 #pragma unroll
   for (int jm = 0; jm < 4; ++jm) boff[jm] = ((g + jm) & 3) * 32 + 8 * c;
-  for (uint32_t i = half; i < a.nblk; i += split) {
-    const uint32_t n = i / split, s = half * kTcSlots + n % kTcSlots;
+  for (uint32_t i = half, n = 0; i < a.nblk; i += split, ++n) {  // n: this phase's block count
+    const uint32_t s = half * kTcSlots + n % kTcSlots;
     if (!active) break;
     if (!mbar_wait_bounded(&full[s], (n / kTcSlots) & 1)) {
       if (a.err) atomicOr(a.err, KERR_TIMEOUT_FULL);
