@@ -84,6 +84,25 @@ void note_async_submission(si_ctx* ctx) {
   ctx->async_submitted++;
 }
 
+static_assert(sizeof(si_ctx::qs_stream) / sizeof(cudaStream_t) == kQmvScratchSlots, "one stream per slot");
+
+void qscratch_for(si_ctx* ctx, cudaStream_t stream, void** p, uint64_t* bytes) {
+  *p = nullptr;
+  *bytes = 0;
+  if (!ctx->qscratch.p) return;
+  if (!stream) stream = ctx->stream;
+  std::lock_guard<std::mutex> lk(ctx->qs_mu);
+  ctx->qs_stream[0] = ctx->stream;
+  for (int i = 0; i < kQmvScratchSlots; ++i) {
+    if (ctx->qs_stream[i] == stream || !ctx->qs_stream[i]) {
+      ctx->qs_stream[i] = stream;
+      *p = static_cast<uint8_t*>(ctx->qscratch.p) + uint64_t(i) * kQmvScratchBytes;
+      *bytes = kQmvScratchBytes;
+      return;
+    }
+  }
+}
+
 void note_weights(si_ctx* ctx, int64_t delta) {
   uint64_t now = ctx->weights.fetch_add(uint64_t(delta)) + uint64_t(delta);
   uint64_t peak = ctx->peak_weights.load();
@@ -109,6 +128,8 @@ int sync_and_check(si_ctx* ctx, const char* what) {
   const int bits = *ctx->h_err;
   if (bits) {
     cudaMemset(ctx->d_err, 0, sizeof(int));
+    // a kernel that gave up may have left split-group counters behind
+    if (ctx->qscratch.p) cudaMemset(ctx->qscratch.p, 0, ctx->qscratch.cap);
     *ctx->h_err = 0;
     return fail(ctx, bits & (KERR_TIMEOUT_FULL | KERR_TIMEOUT_EMPTY | KERR_TIMEOUT_DRAIN)
                          ? SI_E_TIMEOUT
@@ -218,6 +239,11 @@ int si_ctx_create(int device, const si_ctx_config* cfg, si_ctx** out) {
     si_ctx_destroy(c);
     return rc;
   }
+  if (!c->qscratch.ensure(kQmvScratchBytes * kQmvScratchSlots) || cudaMemset(c->qscratch.p, 0, c->qscratch.cap) != cudaSuccess) {
+    int rc = fail(nullptr, SI_E_NOMEM, "context creation: matvec scratch allocation failed");
+    si_ctx_destroy(c);
+    return rc;
+  }
   cudaMemset(c->d_err, 0, 64);
   cudaMemset(c->d_argmax, 0, 64);
   cudaDeviceSynchronize();
@@ -234,6 +260,7 @@ void si_ctx_destroy(si_ctx* ctx) {
   for (auto& b : ctx->out) b.release();
   for (auto& b : ctx->wbuf) b.release();
   ctx->scratch.release();
+  ctx->qscratch.release();
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->h_err) cudaFreeHost(ctx->h_err);
   if (ctx->h_stage) cudaFreeHost(ctx->h_stage);
@@ -455,6 +482,7 @@ static int qmatvec_dev_impl(si_ctx* ctx, uint32_t type, const void* w_dev, uint6
   p.xmode = XM_RAW;
   p.x = x_dev;
   p.err = ctx->d_err;
+  qscratch_for(ctx, stream ? static_cast<cudaStream_t>(stream) : ctx->stream, &p.scratch, &p.scratch_bytes);
   std::string msg;
   // Programmatic dependent launch: back-to-back matvecs overlap the next
   // kernel's weight prefetch with this one's tail (x/y are read/written only
@@ -488,6 +516,7 @@ int si_gguf_quant_matvec_bytes(si_ctx* ctx, uint32_t type, const void* w, uint64
   p.items = uint32_t(rows);
   p.x = ctx->in[0].as<float>();
   p.err = ctx->d_err;
+  qscratch_for(ctx, ctx->stream, &p.scratch, &p.scratch_bytes);
   std::string msg;
   if ((rc = launch_qmv(p, ctx->stream, ctx->sm_count, false, &msg))) return fail(ctx, rc, msg);
   if ((rc = d2h(ctx, y, ctx->out[0].p, rows * 4, "matvec readback"))) return rc;
@@ -539,6 +568,7 @@ int si_gguf_quant_matvec_many_weights(si_ctx* ctx, uint32_t n, const si_weight* 
   p.items = uint32_t(total);
   p.x = ctx->in[0].as<float>();
   p.err = ctx->d_err;
+  qscratch_for(ctx, ctx->stream, &p.scratch, &p.scratch_bytes);
   std::string msg;
   if ((rc = launch_qmv(p, ctx->stream, ctx->sm_count, false, &msg))) return fail(ctx, rc, msg);
   off = 0;
@@ -576,6 +606,7 @@ static int qmm_host(si_ctx* ctx, uint32_t type, const uint8_t* w_dev, uint64_t r
   p.y = ctx->out[0].as<float>();
   p.ldy = rows;
   p.err = ctx->d_err;
+  qscratch_for(ctx, ctx->stream, &p.qscratch, &p.qscratch_bytes);
   const uint64_t need = qmm_tc_scratch_bytes(uint32_t(rows), uint32_t(cols), uint32_t(batch), ctx->sm_count);
   if (ctx->scratch.ensure(need)) {
     p.scratch = ctx->scratch.p;
@@ -636,6 +667,7 @@ static int qmatmul_many_dev_impl(si_ctx* ctx, uint32_t type, const void* w_dev, 
   p.y = y_dev;
   p.ldy = rows;
   p.err = ctx->d_err;
+  qscratch_for(ctx, stream ? static_cast<cudaStream_t>(stream) : ctx->stream, &p.qscratch, &p.qscratch_bytes);
   // the tensor-core form's scratch is the context's (calls on one context
   // are serialised on the host, and kernels on one stream in order)
   const uint64_t need = qmm_tc_scratch_bytes(uint32_t(rows), uint32_t(cols), uint32_t(batch), ctx->sm_count);
@@ -703,6 +735,7 @@ static int fused_gate_up_dev_impl(si_ctx* ctx, uint32_t type, const void* gate_d
   p.items = uint32_t(rows);
   p.x = x_dev;
   p.err = ctx->d_err;
+  qscratch_for(ctx, stream ? static_cast<cudaStream_t>(stream) : ctx->stream, &p.scratch, &p.scratch_bytes);
   std::string msg;
   rc = launch_qmv(p, stream ? static_cast<cudaStream_t>(stream) : ctx->stream, ctx->sm_count, true, &msg);
   return rc ? fail(ctx, rc, msg) : SI_OK;

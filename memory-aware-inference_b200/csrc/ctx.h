@@ -73,6 +73,14 @@ struct si_ctx {
   std::mutex mu;         // serialises host-memory entry points
   std::mutex upload_mu;  // serialises weight uploads from staging threads
   si::DevBuf in[6], out[3], wbuf[3], scratch;
+  // partial sums of the matvec rows whose blocks span several CTAs, and the
+  // per-group counters (zero between launches): kQmvScratchSlots slots, slot 0
+  // for the context's stream, the others handed to the first other streams
+  // that launch a matvec (a slot is never shared by two streams, so launches
+  // on different streams cannot meet in it)
+  si::DevBuf qscratch;
+  std::mutex qs_mu;
+  cudaStream_t qs_stream[8] = {};
   // telemetry
   std::atomic<uint64_t> allocated{0}, peak_allocated{0}, peak_weights{0}, weights{0};
   std::atomic<uint64_t> peak_kv{0}, peak_scratch{0}, submitted{0}, waited{0}, wait_nanos{0}, async_submitted{0};
@@ -90,4 +98,7 @@ int sync_and_check(si_ctx* ctx, const char* what);
 void note_alloc(si_ctx* ctx, int64_t delta);
 void note_weights(si_ctx* ctx, int64_t delta);
 void note_async_submission(si_ctx* ctx);
+// The split-group scratch slot of `stream` (null: none is free; the matvec
+// then runs without it).
+void qscratch_for(si_ctx* ctx, cudaStream_t stream, void** p, uint64_t* bytes);
 }  // namespace si

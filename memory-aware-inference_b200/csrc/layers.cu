@@ -145,6 +145,7 @@ int si_gdn_layer_dev(si_ctx* ctx, const si_gdn_layer_desc* d, const float* x, co
   p.x = x;
   p.eps = d->epsilon;
   p.err = ctx->d_err;
+  si::qscratch_for(ctx, s, &p.scratch, &p.scratch_bytes);
   const uint32_t types[2] = {d->qkv_type, d->z_type};
   if (int rc = group_matvec(ctx, p, types, s)) return rc;
   if (!gates) {
@@ -180,6 +181,7 @@ int si_gdn_layer_dev(si_ctx* ctx, const si_gdn_layer_desc* d, const float* x, co
   o.head_dim = 128;
   o.eps = d->epsilon;
   o.err = ctx->d_err;
+  si::qscratch_for(ctx, s, &o.scratch, &o.scratch_bytes);
   std::string msg;
   if (int rc = launch_qmv(o, s, ctx->sm_count, true, &msg)) return fail(ctx, rc, msg);
   if (cudaError_t e = cudaGetLastError()) return cuda_fail(ctx, e, "GDN layer launch");
@@ -226,6 +228,7 @@ int si_attention_layer_dev(si_ctx* ctx, const si_attention_layer_desc* d, const 
   p.x = x;
   p.eps = d->epsilon;
   p.err = ctx->d_err;
+  si::qscratch_for(ctx, s, &p.scratch, &p.scratch_bytes);
   const uint32_t types[3] = {d->q_type, d->k_type, d->v_type};
   if (int rc = group_matvec(ctx, p, types, s)) return rc;
   AttnArgs a = {};
@@ -264,6 +267,7 @@ int si_attention_layer_dev(si_ctx* ctx, const si_attention_layer_desc* d, const 
   o.xaux = qg + qw;
   o.eps = d->epsilon;
   o.err = ctx->d_err;
+  si::qscratch_for(ctx, s, &o.scratch, &o.scratch_bytes);
   std::string msg;
   if (int rc = launch_qmv(o, s, ctx->sm_count, true, &msg)) return fail(ctx, rc, msg);
   if (cudaError_t e = cudaGetLastError()) return cuda_fail(ctx, e, "attention layer launch");

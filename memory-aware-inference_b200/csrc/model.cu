@@ -1198,6 +1198,7 @@ QmvParams qmv_base(si_model* m, uint32_t type, uint32_t cols) {
   p.cols = cols;
   p.nseg = 1;
   p.err = m->ctx->d_err;
+  si::qscratch_for(m->ctx, m->ctx->stream, &p.scratch, &p.scratch_bytes);
   p.eps = m->c.rms_eps;
   return p;
 }
@@ -1592,6 +1593,7 @@ int run_qmm(si_model* m, uint32_t type, const uint8_t* w, uint32_t rows, uint32_
   p.scratch = m->b_qmm;
   p.scratch_bytes = m->b_qmm_bytes;
   p.err = m->ctx->d_err;
+  si::qscratch_for(m->ctx, m->ctx->stream, &p.qscratch, &p.qscratch_bytes);
   std::string msg;
   int rc = launch_qmm(p, m->ctx->stream, m->ctx->sm_count, true, &msg);
   return rc ? fail(m->ctx, rc, msg) : SI_OK;

@@ -160,6 +160,7 @@ int si_sharded_qmatvec_dev(si_ctx* ctx, si_peer_buffer* b, uint32_t type, const 
   p.xmode = si::XM_RAW;
   p.x = x;
   p.err = ctx->d_err;
+  si::qscratch_for(ctx, s, &p.scratch, &p.scratch_bytes);
   std::string msg;
   int rc;
   if (b->n == 1) {

@@ -217,6 +217,8 @@ int launch_qmm(const QmmParams& p, cudaStream_t s, int sm_count, bool pdl, std::
     q.xmode = XM_RAW;
     q.x = p.x;
     q.err = p.err;
+    q.scratch = p.qscratch;
+    q.scratch_bytes = p.qscratch_bytes;
     return launch_qmv(q, s, sm_count, pdl, msg);
   }
   if (qmm_tc_eligible(p)) {

@@ -856,6 +856,10 @@ int launch_qmv(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
       return pair ? launch_t<SI_GGML_TYPE_Q5_K, 2>(p, stream, sm_count, pdl, msg)
                   : launch_t<SI_GGML_TYPE_Q5_K, 1>(p, stream, sm_count, pdl, msg);
     case SI_GGML_TYPE_Q6_K:
+      if (qmv_tc6_eligible(p)) {
+        const int rc = launch_qmv_tc6(p, stream, sm_count, pdl, msg);
+        if (rc != SI_E_UNSUPPORTED) return rc;
+      }
       return pair ? launch_t<SI_GGML_TYPE_Q6_K, 2>(p, stream, sm_count, pdl, msg)
                   : launch_t<SI_GGML_TYPE_Q6_K, 1>(p, stream, sm_count, pdl, msg);
     default:

@@ -54,11 +54,25 @@ struct QmvParams {
   uint32_t head_dim;    // XM_GATED
   int* err;             // device error word
   PeerOut peer;         // n > 0: sharded output (tensor-core Q4_K kernel only)
+  void* scratch;        // the context's split-group scratch (zeroed counters first), may be null
+  uint64_t scratch_bytes;
 };
 
 // Enqueue one launch. Returns SI_OK or SI_E_* with *msg filled.
 int launch_qmv(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
                std::string* msg);
+
+// Q6_K matvec on the tensor cores (qmatvec_tc6.cu): eligibility and launch;
+// launch_qmv routes eligible Q6_K calls there.
+// Measured on B200: the CUDA-core kernel stays ahead only on short matrices
+// (1,024 rows of 20 or 48 blocks), so the tensor cores take 2,048 rows and
+// more, or rows of 64 blocks and more (256 rows at least).
+constexpr uint32_t kTc6MinRows = 256, kTc6AnyWidthRows = 2048, kTc6WideBlocks = 64;
+constexpr uint64_t kQmvScratchBytes = 2ull << 20;  // one stream's split-group scratch
+constexpr int kQmvScratchSlots = 8;                // streams per context with their own scratch
+bool qmv_tc6_eligible(const QmvParams& p);
+uint64_t qmv_tc6_scratch_bytes(uint32_t sm_count);  // the scratch a launch's split needs
+int launch_qmv_tc6(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl, std::string* msg);
 
 // Plain Q4_K matvec on the tensor cores (qmatvec_tc.cu): eligibility and
 // launch; launch_qmv routes eligible calls there.
@@ -79,6 +93,8 @@ struct QmmParams {
   void* scratch;        // device scratch for the tensor-core form (256-byte aligned), may be null
   uint64_t scratch_bytes;
   int* err;
+  void* qscratch;       // the context's matvec scratch (batch 1 goes to the matvec family)
+  uint64_t qscratch_bytes;
 };
 int launch_qmm(const QmmParams& p, cudaStream_t stream, int sm_count, bool pdl, std::string* msg);
 // Tensor-core form for Q4_K (qmatmul_many_tc.cu): scratch it needs, whether a

@@ -349,3 +349,67 @@ def test_argmax_semantics(ctx):  # runtime.rs:4301-4309
     import mai_b200 as M
     with pytest.raises(M.SiError, match="no finite"):
         ctx.argmax([np.nan, np.inf])
+
+
+@pytest.mark.parametrize("rows,cols", [
+    (256, 1024), (300, 3072), (1000, 5120), (4099, 1024), (5120, 17408), (2560, 17408), (640, 18432),
+    (5121, 12288), (20000, 13312), (300, 12288), (3000, 256), (4096, 3072), (2048, 1024), (17408, 5120),
+    (1024, 5120), (2049, 6144),
+])
+def test_q6k_tensor_core_matvec_shapes(ctx, rows, cols):
+    """Q6_K matvecs whose rows hold a multiple of 4 super-blocks (at most 72)
+    with 2,048 rows and more, or 64 blocks and more, run on the tensor cores
+    (qmv_tc6_kernel): rows 8 mod 16 bytes long (4, 12, 20, 52, 68 blocks:
+    even/odd row maps) and 16-byte multiples (8, 24, 72 blocks), 32-row groups
+    shared by neighbouring CTAs, ragged last groups (5121, 2049 rows), one
+    chunk per row (4 blocks). The other shapes stay on the CUDA-core kernel
+    and must agree just the same."""
+    rng = np.random.default_rng(rows * 3 + cols)
+    w = random_blocks(rng, 14, rows * cols // 256)
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    ref = O.matvec(14, w, rows, cols, x)
+    got = ctx.q6_k_matvec(w, rows, cols, x)
+    assert rel_l2(got, ref) < TOL
+    assert np.max(np.abs(got - ref)) / np.abs(ref).max() < 1e-5
+
+
+def test_q6k_head_shape_rows_match_oracle(ctx):
+    """The 27B output head's shape (248320 x 5120 Q6_K, 1.04 GB): rows sampled
+    at the start, middle and end against the oracle."""
+    import torch
+    rng = np.random.default_rng(248320)
+    rows, cols = 248320, 5120
+    w = random_blocks(rng, 14, rows * cols // 256)
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    wd = torch.from_numpy(np.concatenate([w, np.zeros(64, np.uint8)])).cuda()
+    y = torch.empty(rows, device="cuda")
+    ctx.qmatvec_dev(14, wd, rows, cols, torch.from_numpy(x).cuda(), y)
+    torch.cuda.synchronize()
+    yc = y.cpu().numpy()
+    rb = cols // 256 * 210
+    for r0 in (0, rows // 2 + 8, rows - 200):
+        ref = O.matvec(14, w[r0 * rb:(r0 + 200) * rb], 200, cols, x)
+        assert rel_l2(yc[r0:r0 + 200], ref) < TOL, r0
+
+
+def test_q6k_split_groups_on_concurrent_streams(ctx):
+    """Tensor-core Q6_K matvecs queued on two streams at once: each stream
+    finishes its straddling groups in its own scratch slot, so neither run
+    disturbs the other's rows."""
+    import torch
+    rng = np.random.default_rng(77)
+    rows, cols = 5120, 17408
+    ws = [random_blocks(rng, 14, rows * cols // 256) for _ in range(2)]
+    xs = [rng.normal(0, 1, cols).astype(np.float32) for _ in range(2)]
+    wd = [torch.from_numpy(np.concatenate([w, np.zeros(64, np.uint8)])).cuda() for w in ws]
+    xd = [torch.from_numpy(x).cuda() for x in xs]
+    ys = [torch.empty(rows, device="cuda") for _ in range(2)]
+    ref = [ctx.q6_k_matvec(w, rows, cols, x) for w, x in zip(ws, xs)]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    torch.cuda.synchronize()
+    for _ in range(20):
+        for k in range(2):
+            ctx.qmatvec_dev(14, wd[k], rows, cols, xd[k], ys[k], streams[k].cuda_stream)
+    torch.cuda.synchronize()
+    for k in range(2):
+        assert np.array_equal(ys[k].cpu().numpy(), ref[k])
