@@ -9,9 +9,10 @@ weights from DRAM. The K timed launches are captured once into a CUDA graph
 and replayed back to back (the host's per-call cost is not measured), timed
 with CUDA events on the replaying stream. `e2e` is the same metric through the public API with host buffers
 (gguf_quant_matvec_weight: H2D of x, kernel, D2H of y, synchronised each
-call). At N GPUs (torchrun) every rank runs the workload on its own
-matrices (independent matvecs, no collective on the data path): weak
-scaling, value = bytes of all ranks / max-over-ranks time.
+call). At N > 1 GPUs (torchrun) the step is the same 17408 x 5120 matvec
+row-sharded over the ranks (17408/N rows each) with y all-gathered inside the
+matvec kernel (si_sharded_qmatvec_dev, NVLink peer stores): strong scaling,
+value = the matrix's bytes / max-over-ranks step time.
 
 `--impl reference` times the reference's CPU path (the oracle's C++
 restatement of quant.rs + the matvec test reference, all host threads) on the
@@ -182,6 +183,150 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_sharded(args, world, rank, local):
+    """N > 1 GPUs: config 1 row-sharded (17408/N rows per rank) with the
+    all-gather of y inside the matvec kernel (si_sharded_qmatvec_dev: each
+    rank's tensor-core matvec stores its rows into every rank's copy of y over
+    NVLink; the launch ends when all ranks' rows have landed). Strong scaling:
+    one step is the whole 17408 x 5120 matvec with y complete on every rank;
+    value = the matrix's algorithmic bytes / max-over-ranks step time."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from cuda.bindings import runtime as rt
+    from __graft_entry__ import _load_package
+    mai = _load_package()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = mai.CudaContext(local)
+    uid = [mai.CudaContext.comm_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    ctx.comm_init(world, rank, uid[0])
+    rl = ROWS // world
+    rng = np.random.default_rng(1)  # every rank draws the same matrix and keeps its rows
+    host_w = make_weights(rng, mai).reshape(ROWS, -1)
+    x_host = rng.normal(0, 1, COLS).astype(np.float32)
+    shard = np.ascontiguousarray(host_w[rank * rl:(rank + 1) * rl].reshape(-1))
+    copies = NCOPIES * world  # > L2 per rank: 8 x N copies of a 1/N shard
+    weights = [torch.cat([torch.from_numpy(shard), torch.zeros(64, dtype=torch.uint8)]).to(dev) for _ in range(copies)]
+    x = torch.from_numpy(x_host).to(dev)
+    buf = ctx.peer_buffer(ROWS * 4 + 256)
+    yoff = 256
+    cap = torch.cuda.Stream(device=dev)
+
+    def call(i, st):
+        ctx.sharded_qmatvec_dev(buf, mai.GGML_TYPE_Q4_K, weights[i % copies], rl, COLS, x, yoff, st)
+    with torch.cuda.stream(cap):
+        for i in range(args.warmup):
+            call(i, cap.cuda_stream)
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cap):
+        for i in range(args.steps):
+            call(i, cap.cuda_stream)
+    with torch.cuda.stream(cap):
+        graph.replay()  # uploads the graph: warm-up
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    t_soak = time.time()
+    while time.time() - t_soak < 0.6:
+        with torch.cuda.stream(cap):
+            graph.replay()
+        torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(cap):
+        e0.record(cap)
+        graph.replay()
+        e1.record(cap)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    dist.barrier()
+    ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(ms, world)
+    sampler.stop()
+    clocks = sampler.summary(t_soak, t_wall1)
+    ctx.synchronize()  # raises if a bounded wait ran out
+    y_dev = np.empty(ROWS, np.float32)
+    err, = rt.cudaMemcpy(y_dev.ctypes.data, buf.local + yoff, ROWS * 4, rt.cudaMemcpyKind.cudaMemcpyDeviceToHost)
+    # e2e: host x in (pinned), sharded matvec, the whole y back to the host, per step
+    xp = torch.from_numpy(x_host).pin_memory()
+    yp = torch.empty(ROWS, dtype=torch.float32).pin_memory()
+    cs = torch.cuda.ExternalStream(ctx.stream, device=dev)
+    e2e_steps = max(20, min(args.steps, 200))
+
+    def e2e_step():
+        with torch.cuda.stream(cs):
+            x.copy_(xp, non_blocking=True)
+        ctx.sharded_qmatvec_dev(buf, mai.GGML_TYPE_Q4_K, weights[0], rl, COLS, x, yoff)
+        rt.cudaMemcpyAsync(yp.data_ptr(), buf.local + yoff, ROWS * 4, rt.cudaMemcpyKind.cudaMemcpyDeviceToHost,
+                           ctx.stream)
+        rt.cudaStreamSynchronize(ctx.stream)
+    for _ in range(3):
+        e2e_step()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = max_over_ranks((time.perf_counter() - t0) / e2e_steps, world)
+    ctx.synchronize()
+    e2e_ok = bool(np.array_equal(yp.numpy(), y_dev))
+    line = None
+    if rank == 0:
+        import oracle as O
+        ref = O.matvec(12, host_w.reshape(-1)[:64 * 2880], 64, COLS, x_host)
+        last = O.matvec(12, host_w.reshape(-1)[(ROWS - 64) * 2880:], 64, COLS, x_host)
+        rel = float(np.linalg.norm(np.concatenate([y_dev[:64] - ref, y_dev[-64:] - last])) /
+                    np.linalg.norm(np.concatenate([ref, last])))
+        peak, peak_kind = load_peaks()
+        per_step_s = ms_max / 1e3 / args.steps
+        line = {
+            "metric": METRIC, "value": round(ALG_BYTES / per_step_s / 1e9, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 6),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8->f32",
+            "data": "synthetic (seeded GGUF Q4_K super-blocks: uniform bytes, |N(0,0.02)| fp16 d/dmin; x ~ N(0,1))",
+            "config": {"workload": "q4k_matvec_17408x5120 (BASELINE config 1), row-sharded", "rows": ROWS,
+                       "cols": COLS, "rows_per_rank": rl,
+                       "l2": f"{copies} distinct weight shards per rank ({copies * rl * 2880 / 1e6:.0f} MB > 126 MB L2) cycled",
+                       "timing": "K steps captured in one CUDA graph per rank, CUDA events around its replay, max over ranks",
+                       "parallelism": f"row-sharded x{world}; y all-gathered inside the matvec kernel (NVLink peer stores)"},
+            "roofline": {"bound": "hbm", "achieved": round(ALG_BYTES / world / per_step_s / 1e9, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(ALG_BYTES / world / per_step_s / 1e9 / peak, 4),
+                         "peak_kind": peak_kind, "traffic": None,
+                         "note": "per GPU: 1/N of the matrix per step against one GPU's HBM peak"},
+            "cpu_baseline": None,
+            "e2e": {"value": round(ALG_BYTES / e2e_s / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": COLS * 4,
+                    "d2h_bytes_per_step": ROWS * 4, "y_equals_graph_run": e2e_ok,
+                    "api": "si_sharded_qmatvec_dev (host x in, whole y out on every rank, synchronised per step)"},
+            "parity_rel_l2_first_last_rows": rel,
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+        }
+    # the pinned buffers were last used on the context's stream: free them
+    # (torch records an event on that stream) before the stream goes away
+    torch.cuda.synchronize()
+    del xp, yp, cs, e2e_step
+    buf.close()
+    del weights
+    torch.cuda.empty_cache()
+    ctx.close()
+
+    def guarded(fn, *a):
+        try:
+            return fn(*a)
+        except Exception as e:  # noqa: BLE001 - recorded, not hidden
+            return {"error": f"{type(e).__name__}: {e}"[:300]}
+    dec = guarded(run_decode, args, mai, torch, np, world, rank, local) if not args.no_decode else None
+    res = guarded(run_decode, args, mai, torch, np, world, rank, local, 0.0) if not args.no_decode else None
+    if rank == 0:
+        line["decode"] = dec
+        line["decode_resident"] = res
+        print(json.dumps(line), flush=True)
+
+
 def run_ours(args, world, rank, local):
     import numpy as np
     import torch
@@ -316,9 +461,11 @@ def run_ours(args, world, rank, local):
         kern.update(layers if "error" not in layers else {"layers": layers})
     ctx.close()
     dec = guarded(run_decode, args, mai, torch, np, world, rank, local) if not args.no_decode else None
+    res = guarded(run_decode, args, mai, torch, np, world, rank, local, 0.0) if not args.no_decode else None
     if rank == 0:
         line["kernels"] = kern
         line["decode"] = dec
+        line["decode_resident"] = res
         print(json.dumps(line), flush=True)
 
 
@@ -588,11 +735,15 @@ def measure_verify(m, cfg, prompt, np, decode_tps, K=8, windows=8):
         return {"error": f"{type(e).__name__}: {e}"[:300]}
 
 
-def run_decode(args, mai, torch, np, world, rank, local):
+def run_decode(args, mai, torch, np, world, rank, local, budget_gb=None):
     """64-layer Qwen3.6-27B-shaped Q4_K_M synthetic model,
     16-token random prompt + 128 greedy tokens, 4 GB HBM budget per GPU with a
-    depth-3 staging ring; row-sharded over the ranks with NCCL."""
-    budget = int(args.budget_gb * (1 << 30))
+    depth-3 staging ring; row-sharded over the ranks with NCCL. budget_gb = 0:
+    no budget (every layer resident), the fully-resident figure; only the
+    budgeted run also takes the speculative-verify and CPU figures."""
+    resident = budget_gb == 0.0
+    budget_gb = args.budget_gb if budget_gb is None else budget_gb
+    budget = int(budget_gb * (1 << 30))
     ctx = mai.CudaContext(local, hbm_budget_bytes=budget, stage_depth=3)
     if world > 1:
         import torch.distributed as dist
@@ -626,16 +777,16 @@ def run_decode(args, mai, torch, np, world, rank, local):
     res = {"workload": "qwen36_27b_shape_q4_k_m (BASELINE config 5)", "tokens_per_s": round((len(ids) - 1) / dec_s, 3),
            "steps_per_s": round(steps / tot_s, 3), "prompt_tokens": len(prompt), "generated": len(ids),
            "n_gpus": world, "parallelism": f"row-sharded x{world} (NCCL all-gather)" if world > 1 else "1 GPU",
-           "hbm_budget_gb": args.budget_gb, "stage_depth": 3, "build_s": round(build_s, 1), "plan": plan,
+           "hbm_budget_gb": budget_gb if budget else "none (all layers resident)", "stage_depth": 3, "build_s": round(build_s, 1), "plan": plan,
            "first_ids": ids[:8]}
     if streamed:
         gbs = streamed * steps / tot_s / 1e9
         res["streamed_GBps_per_gpu"] = round(gbs, 1)
         res["h2d_roofline"] = {"bound": "pcie/c2c (pinned H2D)", "measured_h2d_GBps": round(h2d, 1),
                                "frac": round(gbs / h2d, 3)}
-    if world == 1:
+    if world == 1 and not resident:
         res["verify"] = measure_verify(m, cfg, prompt, np, res["tokens_per_s"])
-    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+    if world == 1 and rank == 0 and not args.no_cpu_baseline and not resident:
         import oracle as O
         orc = O.OracleModel(m.config, m.host_tensor)
         h = orc.embed(prompt[0])
@@ -669,6 +820,8 @@ def main():
     world, rank, local = dist_init(args)
     if args.impl == "reference":
         run_reference(args, world, rank)
+    elif world > 1:
+        run_sharded(args, world, rank, local)
     else:
         run_ours(args, world, rank, local)
     if world > 1:

@@ -4,10 +4,11 @@
 // A peer buffer is one device allocation per rank of a context's communicator,
 // mapped into every other rank with CUDA IPC (the handles travel over NCCL),
 // laid out as
-//   [0, D)              data (D = the requested bytes rounded up to 256)
-//   [D, D + 512)        signal words of the in-kernel exchange, 64 B per source rank
-//   [D + 512, D + 576)  this rank's CTA ticket
-//   [D + 1024, D + 1536) flags of the stand-alone peer all-gather (fallback)
+//   [0, D)                data (D = the requested bytes rounded up to 256)
+//   [D, D + 8192)         flag words of the in-kernel exchange: per source rank
+//                         256 words, one per CTA of the sending launch
+//   [D + 8192, D + 8256)  this rank's CTA ticket
+//   [D + 9216, D + 9728)  flags of the stand-alone peer all-gather (fallback)
 // si_sharded_qmatvec_dev runs the Q4_K tensor-core matvec on this rank's rows;
 // its epilogue stores each row into every rank's copy of the output vector
 // over NVLink, and the launch completes only once every rank's rows have
@@ -44,7 +45,8 @@ struct si_peer_buffer {
 
 namespace {
 
-constexpr uint64_t kSigOff = 0, kTicketOff = 512, kFlagOff = 1024, kTail = 2048;
+constexpr uint64_t kSigOff = 0, kTicketOff = 4ull * si::kPeerSigStride * si::kPeerMax, kFlagOff = kTicketOff + 1024,
+                   kTail = kFlagOff + 1024;
 
 uint64_t round256(uint64_t v) { return (v + 255) & ~255ull; }
 
@@ -176,9 +178,8 @@ int si_sharded_qmatvec_dev(si_ctx* ctx, si_peer_buffer* b, uint32_t type, const 
     }
     q.peer.ticket = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(b->peers[b->rank]) + b->data_bytes + kTicketOff);
     q.peer.wait_cycles = b->wait_cycles;
-    if (si::qmv_tc_supported(q)) {
-      rc = si::launch_qmv_tc(q, s, ctx->sm_count, true, &msg);
-    } else {
+    rc = si::qmv_tc_supported(q) ? si::launch_qmv_tc(q, s, ctx->sm_count, true, &msg) : SI_E_UNSUPPORTED;
+    if (rc == SI_E_UNSUPPORTED) {
       // the matvec into this rank's slice, then the stand-alone peer all-gather
       rc = si::launch_qmv(p, s, ctx->sm_count, true, &msg);
       if (!rc) {

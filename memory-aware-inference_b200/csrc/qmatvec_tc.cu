@@ -72,23 +72,37 @@ struct TcArgs {
   PeerOut peer;          // n > 0: the rows go to every rank's vector (NVLink stores)
 };
 
-// After every consumer's stores (bar.sync 1): the CTA's completion signal in
-// every rank's signal words, then, in the launch's last CTA on this rank, the
-// bounded wait for every rank's whole grid (PeerOut, qmatvec.cuh).
-__device__ __noinline__ void peer_complete(const PeerOut& po, uint32_t nctas, int* err) {
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
-  for (uint32_t p = 0; p < po.n; ++p)
-    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(po.sig[p] + 16 * po.rank) : "memory");
-  const uint32_t old = atomicAdd(po.ticket, 1u);
-  if (old % nctas != nctas - 1) return;
-  const uint32_t target = (old / nctas + 1) * nctas;
+// After every consumer's stores (bar.sync 1), called by all `nthreads`
+// consumer threads: thread 0 takes the CTA's ticket (the launch's epoch is
+// ticket / nctas + 1), makes the CTA's row stores visible to every GPU
+// (fence.acq_rel.sys) and writes the epoch into this CTA's own flag word of
+// every rank: plain stores to distinct words, no atomics on shared remote
+// words. The launch's last CTA on this rank then waits, bounded, with all its
+// threads polling a share of the n x nctas flags of its own block (PeerOut,
+// qmatvec.cuh).
+__device__ __noinline__ void peer_complete(const PeerOut& po, uint32_t nctas, int* err, uint32_t nthreads) {
+  __shared__ uint32_t s_epoch;  // the epoch to wait for; 0: not the last CTA
+  if (threadIdx.x == 0) {
+    const uint32_t old = atomicAdd(po.ticket, 1u);
+    const uint32_t epoch = old / nctas + 1;
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (uint32_t p = 0; p < po.n; ++p)
+      asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(po.sig[p] + kPeerSigStride * po.rank + blockIdx.x),
+                   "r"(epoch)
+                   : "memory");
+    s_epoch = old % nctas == nctas - 1 ? epoch : 0u;
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+  const uint32_t epoch = s_epoch;
+  if (epoch == 0) return;
   const uint32_t* mine = po.sig[po.rank];
   const long long t0 = clock64();
-  for (uint32_t s = 0; s < po.n; ++s) {
+  for (uint32_t i = threadIdx.x; i < po.n * nctas; i += nthreads) {
+    const uint32_t* f = mine + kPeerSigStride * (i / nctas) + i % nctas;
     while (true) {
       uint32_t v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + 16 * s) : "memory");
-      if (int32_t(v - target) >= 0) break;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      if (int32_t(v - epoch) >= 0) break;
       if (clock64() - t0 > po.wait_cycles) {
         if (err) atomicOr(err, KERR_TIMEOUT_FULL);
         return;
@@ -430,7 +444,7 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
   }
   if (a.peer.n) {
     asm volatile("bar.sync 1, %0;" ::"r"(kTcConsumers * 32) : "memory");
-    if (threadIdx.x == 0) peer_complete(a.peer, a.nctas, a.err);
+    peer_complete(a.peer, a.nctas, a.err, kTcConsumers * 32);
   }
 }
 
@@ -524,7 +538,7 @@ static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stre
   uint32_t nctas = std::min<uint32_t>(ngroups, uint32_t(sm_count) * fit);
   // at most kTcGroups virtual groups per CTA
   while ((ngroups + nctas - 1) / nctas * mats > uint32_t(kTcGroups)) ++nctas;
-  if (nctas > ngroups) return SI_E_UNSUPPORTED;
+  if (nctas > ngroups || (p.peer.n && nctas > kPeerSigStride)) return SI_E_UNSUPPORTED;
   const uint32_t ngmax = (ngroups + nctas - 1) / nctas;
   const uint32_t lo_band = 16 * (ngmax > 1 ? ngmax - 1 : 1);
   CUtensorMap hi, lo, uhi, ulo;
