@@ -1159,7 +1159,7 @@ __global__ void __launch_bounds__(256) p2p_allgather_kernel(const P2PGather g) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(g.epoch) : "memory");
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) {
-    const long long t0 = clock64();
+    const long long t0 = clock64(), bound = g.wait_cycles > 0 ? g.wait_cycles : kWaitCycles;
     for (uint32_t q = 0; q < g.n; ++q) {
       if (q == g.rank) continue;
       const uint32_t* f = reinterpret_cast<const uint32_t*>(g.block[g.rank] + g.flag_off + 64ull * q);
@@ -1167,7 +1167,7 @@ __global__ void __launch_bounds__(256) p2p_allgather_kernel(const P2PGather g) {
         uint32_t v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
         if (int32_t(v - g.epoch) >= 0) break;
-        if (clock64() - t0 > kWaitCycles) {
+        if (clock64() - t0 > bound) {
           if (g.err) atomicOr(g.err, KERR_TIMEOUT_FULL);
           return;
         }

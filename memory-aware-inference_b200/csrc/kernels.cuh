@@ -94,6 +94,7 @@ struct P2PGather {
   uint32_t n, rank, epoch;
   uint64_t flag_off;             // byte offset of the flag words (64 B per rank)
   int* err;
+  long long wait_cycles;         // bound of the wait for the other ranks (0: kWaitCycles)
 };
 void launch_p2p_allgather(const P2PGather& g, cudaStream_t s);
 

@@ -5,10 +5,10 @@
 // mapped into every other rank with CUDA IPC (the handles travel over NCCL),
 // laid out as
 //   [0, D)                data (D = the requested bytes rounded up to 256)
-//   [D, D + 8192)         flag words of the in-kernel exchange: per source rank
-//                         256 words, one per CTA of the sending launch
-//   [D + 8192, D + 8256)  this rank's CTA ticket
-//   [D + 9216, D + 9728)  flags of the stand-alone peer all-gather (fallback)
+//   [D, D + 16384)          flag words of the in-kernel exchange: per source rank
+//                           512 words, one per CTA of the sending launch
+//   [D + 16384, D + 16448)  this rank's CTA ticket
+//   [D + 17408, D + 17920)  flags of the stand-alone peer all-gather (fallback)
 // si_sharded_qmatvec_dev runs the Q4_K tensor-core matvec on this rank's rows;
 // its epilogue stores each row into every rank's copy of the output vector
 // over NVLink, and the launch completes only once every rank's rows have
@@ -193,6 +193,7 @@ int si_sharded_qmatvec_dev(si_ctx* ctx, si_peer_buffer* b, uint32_t type, const 
         g.epoch = ++b->host_epoch;
         g.flag_off = b->data_bytes + kFlagOff;
         g.err = ctx->d_err;
+        g.wait_cycles = b->wait_cycles;
         si::launch_p2p_allgather(g, s);
       }
     }

@@ -30,7 +30,7 @@ struct QmvSeg {
 // previous launch. The epoch is derived on the device from a ticket counter,
 // so a launch replayed from a CUDA graph synchronises like a fresh one.
 constexpr int kPeerMax = 8;
-constexpr uint32_t kPeerSigStride = 256;  // flag words per source rank (one per CTA of a launch)
+constexpr uint32_t kPeerSigStride = 512;  // flag words per source rank (one per CTA of a launch)
 struct PeerOut {
   uint32_t n;                 // ranks; 0 = ordinary output
   uint32_t rank;

@@ -76,3 +76,35 @@ def test_two_rank_exchange_times_out_without_the_peer(mai, ctx, rank):
     got = ctx.q4_k_matvec(w, rows, cols, x)
     assert rel_l2(got, O.matvec(12, w, rows, cols, x)) < 1e-5
     ctx.synchronize()
+
+
+@pytest.mark.parametrize("rows_per_rank", [2176, 4352, 8704])
+def test_config1_shards_take_the_fused_exchange(mai, ctx, rows_per_rank):
+    """The shards of config 1 at 8, 4 and 2 ranks (up to two CTAs per SM) run
+    the matvec whose epilogue does the exchange, not the matvec plus the
+    stand-alone all-gather: that kernel alone writes the per-CTA flag words
+    at the start of the buffer's tail (CTA 0's word of source rank 0 holds
+    the launch's epoch, 1). Either path honours the buffer's wait bound."""
+    import time
+    import torch
+    cols, world = 5120, 2
+    w, x = _matrix(rows_per_rank, cols, seed=rows_per_rank)
+    wd = torch.from_numpy(np.concatenate([w, np.zeros(64, np.uint8)])).cuda()
+    xd = torch.from_numpy(x).cuda()
+    nbytes = world * rows_per_rank * 4
+    buf = ctx.peer_buffer_local(nbytes, world, 0, wait_us=1000)
+    try:
+        t0 = time.perf_counter()
+        ctx.sharded_qmatvec_dev(buf, 12, wd, rows_per_rank, cols, xd, 0)
+        with pytest.raises(mai.SiError) as ei:
+            ctx.synchronize()
+        assert ei.value.status == mai.SI_E_TIMEOUT
+        assert time.perf_counter() - t0 < 1.0
+        data_bytes = (nbytes + 255) // 256 * 256
+        flag = _read(buf.local + data_bytes, 1).view(np.uint32)[0]
+        assert flag == 1
+        got = _read(buf.local, rows_per_rank)
+        assert rel_l2(got, O.matvec(12, w, rows_per_rank, cols, x)) < 1e-5
+    finally:
+        buf.close()
+    ctx.synchronize()
