@@ -5,10 +5,9 @@
 // mapped into every other rank with CUDA IPC (the handles travel over NCCL),
 // laid out as
 //   [0, D)                data (D = the requested bytes rounded up to 256)
-//   [D, D + 16384)          flag words of the in-kernel exchange: per source rank
-//                           512 words, one per CTA of the sending launch
-//   [D + 16384, D + 16448)  this rank's CTA ticket
-//   [D + 17408, D + 17920)  flags of the stand-alone peer all-gather (fallback)
+//   [D, D + 512)          flag words of the in-kernel exchange, 64 B per source rank
+//   [D + 512, D + 576)    this rank's CTA ticket
+//   [D + 1536, D + 2048)  flags of the stand-alone peer all-gather (fallback)
 // si_sharded_qmatvec_dev runs the Q4_K tensor-core matvec on this rank's rows;
 // its epilogue stores each row into every rank's copy of the output vector
 // over NVLink, and the launch completes only once every rank's rows have

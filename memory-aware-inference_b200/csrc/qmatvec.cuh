@@ -30,12 +30,12 @@ struct QmvSeg {
 // previous launch. The epoch is derived on the device from a ticket counter,
 // so a launch replayed from a CUDA graph synchronises like a fresh one.
 constexpr int kPeerMax = 8;
-constexpr uint32_t kPeerSigStride = 512;  // flag words per source rank (one per CTA of a launch)
+constexpr uint32_t kPeerSigStride = 16;  // words between source ranks' flags (64 B apart)
 struct PeerOut {
   uint32_t n;                 // ranks; 0 = ordinary output
   uint32_t rank;
   float* y[kPeerMax];         // each rank's full vector, offset to this rank's rows
-  uint32_t* sig[kPeerMax];    // each rank's flag words: source s, CTA c at [kPeerSigStride s + c]
+  uint32_t* sig[kPeerMax];    // each rank's flag words: source s at [kPeerSigStride s]
   uint32_t* ticket;           // this rank's ticket counter
   long long wait_cycles;      // bound of the wait for the other ranks
 };

@@ -82,9 +82,9 @@ def test_two_rank_exchange_times_out_without_the_peer(mai, ctx, rank):
 def test_config1_shards_take_the_fused_exchange(mai, ctx, rows_per_rank):
     """The shards of config 1 at 8, 4 and 2 ranks (up to two CTAs per SM) run
     the matvec whose epilogue does the exchange, not the matvec plus the
-    stand-alone all-gather: that kernel alone writes the per-CTA flag words
-    at the start of the buffer's tail (CTA 0's word of source rank 0 holds
-    the launch's epoch, 1). Either path honours the buffer's wait bound."""
+    stand-alone all-gather: that kernel alone writes the exchange's flag
+    words at the start of the buffer's tail (source rank 0's word holds the
+    launch's epoch, 1). Either path honours the buffer's wait bound."""
     import time
     import torch
     cols, world = 5120, 2
