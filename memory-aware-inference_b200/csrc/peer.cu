@@ -4,14 +4,18 @@
 // A peer buffer is one device allocation per rank of a context's communicator,
 // mapped into every other rank with CUDA IPC (the handles travel over NCCL),
 // laid out as
-//   [0, D)                data (D = the requested bytes rounded up to 256)
-//   [D, D + 512)          flag words of the in-kernel exchange, 64 B per source rank
-//   [D + 512, D + 576)    this rank's CTA ticket
-//   [D + 1536, D + 2048)  flags of the stand-alone peer all-gather (fallback)
+//   [0, D)                   data (D = the requested bytes rounded up to 256)
+//   [D + 512, D + 516)       this rank's CTA ticket of the in-kernel exchange
+//   [D + 576, D + 580)       launches of the in-kernel exchange so far (epoch)
+//   [D + 1536, D + 2048)     flags of the stand-alone peer all-gather (fallback)
+//   [D + 2560, D + 2560 + 4D) exchange words: two parity halves of D/4 8-byte
+//                            words, word i standing for float i of the data
 // si_sharded_qmatvec_dev runs the Q4_K tensor-core matvec on this rank's rows;
-// its epilogue stores each row into every rank's copy of the output vector
-// over NVLink, and the launch completes only once every rank's rows have
-// arrived (PeerOut in qmatvec.cuh). Other types, and shapes that kernel does
+// its epilogue stores each row, tagged with the launch's epoch, into every
+// rank's exchange words over NVLink, and each CTA unpacks its slice of the
+// gathered vector into the data once every rank's rows have arrived, so the
+// launch completes with the whole vector on every rank (PeerOut in
+// qmatvec.cuh). Other types, and shapes that kernel does
 // not take, run the matvec into the local slice and then the stand-alone
 // peer all-gather kernel (one launch more).
 //
@@ -44,8 +48,10 @@ struct si_peer_buffer {
 
 namespace {
 
-constexpr uint64_t kSigOff = 0, kTicketOff = 4ull * si::kPeerSigStride * si::kPeerMax, kFlagOff = kTicketOff + 1024,
-                   kTail = kFlagOff + 1024;
+constexpr uint64_t kTicketOff = 512, kEpochOff = 576, kFlagOff = 1536, kTail = 2560;
+
+// bytes of one rank's allocation: data, tail, exchange words
+uint64_t alloc_bytes(uint64_t data_bytes) { return data_bytes + kTail + 4 * data_bytes; }
 
 uint64_t round256(uint64_t v) { return (v + 255) & ~255ull; }
 
@@ -77,7 +83,7 @@ int si_peer_buffer_create(si_ctx* ctx, uint64_t bytes, si_peer_buffer** out) {
   b->bytes = bytes;
   b->data_bytes = round256(bytes);
   void* local = nullptr;
-  if (int rc = alloc_zeroed(ctx, b->data_bytes + kTail, &local)) {
+  if (int rc = alloc_zeroed(ctx, alloc_bytes(b->data_bytes), &local)) {
     delete b;
     return rc;
   }
@@ -114,7 +120,7 @@ int si_peer_buffer_create_local(si_ctx* ctx, uint64_t bytes, uint32_t nranks, ui
   if (wait_us) b->wait_cycles = (long long)(wait_us < 1000000000ull ? wait_us : 1000000000ull) * 2000;
   for (uint32_t p = 0; p < nranks; ++p) {
     void* m = nullptr;
-    if (int rc = alloc_zeroed(ctx, b->data_bytes + kTail, &m)) {
+    if (int rc = alloc_zeroed(ctx, alloc_bytes(b->data_bytes), &m)) {
       si_peer_buffer_destroy(b);
       return rc;
     }
@@ -133,7 +139,7 @@ void si_peer_buffer_destroy(si_peer_buffer* b) {
   if (b->ipc) si::comm_p2p_unmap(b->ctx, b->peers);
   for (void* m : b->owned) {
     cudaFree(m);
-    si::note_alloc(b->ctx, -int64_t(b->data_bytes + kTail));
+    si::note_alloc(b->ctx, -int64_t(alloc_bytes(b->data_bytes)));
   }
   delete b;
 }
@@ -172,10 +178,15 @@ int si_sharded_qmatvec_dev(si_ctx* ctx, si_peer_buffer* b, uint32_t type, const 
     q.peer.rank = uint32_t(b->rank);
     for (int r = 0; r < b->n; ++r) {
       uint8_t* base = static_cast<uint8_t*>(b->peers[r]);
-      q.peer.y[r] = reinterpret_cast<float*>(base + slice);
-      q.peer.sig[r] = reinterpret_cast<uint32_t*>(base + b->data_bytes + kSigOff);
+      q.peer.ll[r] = reinterpret_cast<uint64_t*>(base + b->data_bytes + kTail) + y_offset / 4;
     }
-    q.peer.ticket = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(b->peers[b->rank]) + b->data_bytes + kTicketOff);
+    uint8_t* mine = static_cast<uint8_t*>(b->peers[b->rank]);
+    q.peer.parity_stride = b->data_bytes / 4;
+    q.peer.y = reinterpret_cast<float*>(mine + y_offset);
+    q.peer.row0 = uint32_t(uint64_t(b->rank) * rows_per_rank);
+    q.peer.total = uint32_t(uint64_t(b->n) * rows_per_rank);
+    q.peer.ticket = reinterpret_cast<uint32_t*>(mine + b->data_bytes + kTicketOff);
+    q.peer.epoch = reinterpret_cast<uint32_t*>(mine + b->data_bytes + kEpochOff);
     q.peer.wait_cycles = b->wait_cycles;
     rc = si::qmv_tc_supported(q) ? si::launch_qmv_tc(q, s, ctx->sm_count, true, &msg) : SI_E_UNSUPPORTED;
     if (rc == SI_E_UNSUPPORTED) {

@@ -22,22 +22,31 @@ struct QmvSeg {
   uint32_t pad;
 };
 
-// Row-sharded output written straight into every rank's copy of the full
-// vector (NVLink peer memory mapped with CUDA IPC) by the matvec epilogue, then
-// a completion signal: each CTA adds 1 to its source slot in every rank's
-// signal words (system-scope release); the last CTA of the launch on each rank
-// waits (bounded) until every source has counted a whole grid more than at the
-// previous launch. The epoch is derived on the device from a ticket counter,
-// so a launch replayed from a CUDA graph synchronises like a fresh one.
+// Row-sharded output gathered by the matvec kernel itself over NVLink peer
+// memory (mapped with CUDA IPC), with no fence on the data path: the epilogue
+// stores each of this rank's rows into every rank's exchange words as one
+// 8-byte word {value, launch epoch} (a single 64-bit store, so the value and
+// its epoch land together), and every CTA then waits, bounded, for the words
+// of its slice of the whole gathered vector to carry this launch's epoch and
+// unpacks them into the float vector y. The words alternate between two
+// parity halves (epoch & 1): a rank's launch k + 2 cannot start before every
+// rank has finished launch k, so a word is never overwritten while it is
+// still awaited. The epoch is this rank's count of launches on the buffer,
+// read from `epoch` on the device (after the previous grid has finished) and
+// advanced by the launch's last CTA, so a launch replayed from a CUDA graph
+// synchronises like a fresh one.
 constexpr int kPeerMax = 8;
-constexpr uint32_t kPeerSigStride = 16;  // words between source ranks' flags (64 B apart)
 struct PeerOut {
   uint32_t n;                 // ranks; 0 = ordinary output
   uint32_t rank;
-  float* y[kPeerMax];         // each rank's full vector, offset to this rank's rows
-  uint32_t* sig[kPeerMax];    // each rank's flag words: source s at [kPeerSigStride s]
-  uint32_t* ticket;           // this rank's ticket counter
-  long long wait_cycles;      // bound of the wait for the other ranks
+  uint64_t* ll[kPeerMax];     // each rank's exchange words of the gathered vector (parity half 0)
+  uint64_t parity_stride;     // words between the two parity halves
+  float* y;                   // this rank's gathered vector (every rank's rows)
+  uint32_t row0;              // this rank's first row in the gathered vector
+  uint32_t total;             // rows of the gathered vector
+  uint32_t* ticket;           // CTAs of the current launch that have finished (zero between launches)
+  uint32_t* epoch;            // launches completed on this buffer by this rank
+  long long wait_cycles;      // bound of each CTA's wait for the other ranks' rows
 };
 
 struct QmvParams {

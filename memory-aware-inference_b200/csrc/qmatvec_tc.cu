@@ -72,48 +72,45 @@ struct TcArgs {
   PeerOut peer;          // n > 0: the rows go to every rank's vector (NVLink stores)
 };
 
-// After every consumer's stores (bar.sync 1), called by all `nthreads`
-// consumer threads. Thread 0 orders the CTA's row stores (local and over
-// NVLink) before its ticket with a GPU-scope fence: fence + relaxed atomic is
-// a release, and a GPU-scope fence completes only once the CTA's stores to
-// peer memory are performed. The launch's last CTA (ticket % nctas == nctas -
-// 1; the launch's epoch is ticket / nctas + 1) has thereby acquired every
-// other CTA's stores; its one system-scope fence, cumulative over them, puts
-// all of the launch's rows before the epoch it then writes into its flag word
-// of every rank. That CTA then waits, bounded, until every rank's flag word
-// in its own block carries the epoch (PeerOut, qmatvec.cuh). One system-scope
-// fence per launch instead of one per CTA: on B200 the per-CTA form cost
-// 6.4 us of an 18-us two-GPU step.
-__device__ __noinline__ void peer_complete(const PeerOut& po, uint32_t nctas, int* err, uint32_t nthreads) {
-  __shared__ uint32_t s_epoch;  // the epoch to wait for; 0: not the last CTA
-  if (threadIdx.x == 0) {
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    const uint32_t old = atomicAdd(po.ticket, 1u);
-    const uint32_t epoch = old / nctas + 1;
-    const bool last = old % nctas == nctas - 1;
-    if (last) {
-      asm volatile("fence.acq_rel.sys;" ::: "memory");
-      for (uint32_t p = 0; p < po.n; ++p)
-        asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(po.sig[p] + kPeerSigStride * po.rank), "r"(epoch)
-                     : "memory");
+// After the CTA's own rows have gone out, called by all `nthreads` consumer
+// threads: the CTA's slice of the gathered vector, word by word, as soon as
+// each word carries this launch's epoch (bounded), unpacked into y; then the
+// CTA's ticket, the launch's last CTA resetting it and advancing the epoch
+// (PeerOut, qmatvec.cuh).
+__device__ __noinline__ void peer_gather(const PeerOut& po, uint32_t nctas, uint32_t epoch, int* err,
+                                         uint32_t nthreads) {
+  const uint32_t lo = uint32_t(uint64_t(blockIdx.x) * po.total / nctas);
+  const uint32_t hi = uint32_t(uint64_t(blockIdx.x + 1) * po.total / nctas);
+  const uint64_t* w = po.ll[po.rank] + (epoch & 1) * po.parity_stride;
+  const long long t0 = clock64();
+  for (uint32_t i = lo + threadIdx.x; i < hi; i += nthreads) {
+    uint64_t v;
+    while (true) {
+      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(w + i) : "memory");
+      if (uint32_t(v >> 32) == epoch) break;
+      if (clock64() - t0 > po.wait_cycles) break;
     }
-    s_epoch = last ? epoch : 0u;
+    if (uint32_t(v >> 32) != epoch) {
+      if (err) atomicOr(err, KERR_TIMEOUT_FULL);
+      break;
+    }
+    po.y[i] = __uint_as_float(uint32_t(v));
   }
   asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
-  const uint32_t epoch = s_epoch;
-  if (epoch == 0 || threadIdx.x >= po.n) return;
-  // thread s: source rank s's flag word in this rank's block
-  const uint32_t* f = po.sig[po.rank] + kPeerSigStride * threadIdx.x;
-  const long long t0 = clock64();
-  while (true) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-    if (int32_t(v - epoch) >= 0) break;
-    if (clock64() - t0 > po.wait_cycles) {
-      if (err) atomicOr(err, KERR_TIMEOUT_FULL);
-      return;
+  if (threadIdx.x == 0) {
+    // every CTA has read the epoch (at its start) before the last ticket
+    if (atomicAdd(po.ticket, 1u) == nctas - 1) {
+      *po.ticket = 0;
+      asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(po.epoch), "r"(epoch) : "memory");
     }
   }
+}
+
+__device__ __forceinline__ void peer_store_row(const PeerOut& po, uint32_t epoch, uint32_t row, float v) {
+  const uint64_t word = (uint64_t(epoch) << 32) | __float_as_uint(v);
+  const uint64_t at = (epoch & 1) * po.parity_stride + po.row0 + row;
+  for (uint32_t p = 0; p < po.n; ++p)
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(po.ll[p] + at), "l"(word) : "memory");
 }
 
 // C = A B with a zero accumulator (no register moves to clear C).
@@ -206,6 +203,10 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
   // ---- x (transformed as xmode says) -> digit planes, sub-block sums,
   //      block scales (consumer warps) ----
   pdl_wait();
+  // the launch's epoch (PeerOut): the previous grid has finished, so its
+  // last CTA's advance is visible
+  __shared__ uint32_t s_epoch;
+  if (a.peer.n && threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile uint32_t*>(a.peer.epoch) + 1;
   float rms_inv = 1.f;
   if (a.xmode == XM_RMS1P) {
     // (1+w) RMSNorm over the whole vector (qwen35.rs:53-86, heads = 1)
@@ -438,19 +439,14 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
       o8 = yg8 / (1.0f + expf(-yg8)) * upv[grp_w * 16 + g + 8];
     }
     if (a.peer.n) {
-      for (uint32_t p = 0; p < a.peer.n; ++p) {
-        if (row < a.rows) a.peer.y[p][row] = o0;
-        if (row + 8 < a.rows) a.peer.y[p][row + 8] = o8;
-      }
+      if (row < a.rows) peer_store_row(a.peer, s_epoch, row, o0);
+      if (row + 8 < a.rows) peer_store_row(a.peer, s_epoch, row + 8, o8);
     } else {
       if (row < a.rows) a.y[row] = a.resid ? a.resid[row] + o0 : o0;
       if (row + 8 < a.rows) a.y[row + 8] = a.resid ? a.resid[row + 8] + o8 : o8;
     }
   }
-  if (a.peer.n) {
-    asm volatile("bar.sync 1, %0;" ::"r"(kTcConsumers * 32) : "memory");
-    peer_complete(a.peer, a.nctas, a.err, kTcConsumers * 32);
-  }
+  if (a.peer.n) peer_gather(a.peer, a.nctas, s_epoch, a.err, kTcConsumers * 32);
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 tc_encoder() {

@@ -82,9 +82,10 @@ def test_two_rank_exchange_times_out_without_the_peer(mai, ctx, rank):
 def test_config1_shards_take_the_fused_exchange(mai, ctx, rows_per_rank):
     """The shards of config 1 at 8, 4 and 2 ranks (up to two CTAs per SM) run
     the matvec whose epilogue does the exchange, not the matvec plus the
-    stand-alone all-gather: that kernel alone writes the exchange's flag
-    words at the start of the buffer's tail (source rank 0's word holds the
-    launch's epoch, 1). Either path honours the buffer's wait bound."""
+    stand-alone all-gather: that kernel alone writes the exchange words that
+    follow the buffer's 2,560-byte tail (the first launch, epoch 1, uses
+    parity half 1, whose word 0 holds {y[0], 1}). Either path honours the
+    buffer's wait bound."""
     import time
     import torch
     cols, world = 5120, 2
@@ -101,9 +102,9 @@ def test_config1_shards_take_the_fused_exchange(mai, ctx, rows_per_rank):
         assert ei.value.status == mai.SI_E_TIMEOUT
         assert time.perf_counter() - t0 < 1.0
         data_bytes = (nbytes + 255) // 256 * 256
-        flag = _read(buf.local + data_bytes, 1).view(np.uint32)[0]
-        assert flag == 1
+        word = _read(buf.local + data_bytes + 2560 + 8 * (data_bytes // 4), 2).view(np.uint32)
         got = _read(buf.local, rows_per_rank)
+        assert word[1] == 1 and word[0] == got[:1].view(np.uint32)[0]
         assert rel_l2(got, O.matvec(12, w, rows_per_rank, cols, x)) < 1e-5
     finally:
         buf.close()
