@@ -510,13 +510,33 @@ bool qmv_tc_eligible(const QmvParams& p) {
 static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stream, int sm_count, bool pdl,
                              std::string* msg);
 
+static uint32_t tc_smem_bytes(uint32_t nblk) {
+  return kTcRingBytes + nblk * 1024 + nblk * 8 * 4 + ((nblk + 1) & ~1u) * 4 + 2 * kTcMaxStages * 8 + nblk * 8;
+}
+
+// CTAs of one launch over `rows` rows (0: the shape does not fit): up to
+// kTcCtasPerSm per SM as shared memory allows, at most kTcGroups virtual
+// 16-row groups each (a SwiGLU pair stages gate and up groups alike)
+static uint32_t tc_grid(uint32_t rows, uint32_t nblk, uint32_t mats, int sm_count, uint32_t* resident = nullptr) {
+  static int smem_per_sm = 0;
+  if (smem_per_sm == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  }
+  const uint32_t ngroups = (rows + 15) / 16;
+  const uint32_t fit = std::max(1u, std::min<uint32_t>(kTcCtasPerSm, uint32_t(smem_per_sm) / (tc_smem_bytes(nblk) + 1024)));
+  uint32_t nctas = std::min<uint32_t>(ngroups, uint32_t(sm_count) * fit);
+  if (resident) *resident = uint32_t(sm_count) * fit;
+  while ((ngroups + nctas - 1) / nctas * mats > uint32_t(kTcGroups)) ++nctas;
+  return nctas > ngroups ? 0u : nctas;
+}
+
 int launch_qmv_tc(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl, std::string* msg) {
   // every launch must fit before anything is launched (the caller may fall back)
   const uint32_t mats = p.pair ? 2 : 1;
-  for (uint32_t i = 0; i < (p.pair ? 1u : p.nseg); ++i) {
-    const uint32_t ngroups = (p.seg[i].rows + 15) / 16;
-    if ((ngroups + uint32_t(sm_count) - 1) / uint32_t(sm_count) * mats > uint32_t(kTcGroups)) return SI_E_UNSUPPORTED;
-  }
+  for (uint32_t i = 0; i < (p.pair ? 1u : p.nseg); ++i)
+    if (tc_grid(p.seg[i].rows, p.cols / 256, mats, sm_count) == 0) return SI_E_UNSUPPORTED;
   for (uint32_t i = 0; i < (p.pair ? 1u : p.nseg); ++i)
     if (int rc = launch_qmv_tc_seg(p, i, stream, sm_count, pdl, msg)) return rc;
   return SI_OK;
@@ -526,20 +546,12 @@ static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stre
                              std::string* msg) {
   const uint32_t rows = p.seg[seg].rows, nblk = p.cols / 256, mats = p.pair ? 2 : 1;
   const uint32_t ngroups = (rows + 15) / 16;
-  const uint32_t smem = kTcRingBytes + nblk * 1024 + nblk * 8 * 4 + ((nblk + 1) & ~1u) * 4 +
-                        2 * kTcMaxStages * 8 + nblk * 8;
-  // CTAs per SM that fit (wide rows carry more x digits than two CTAs can hold)
-  static int smem_per_sm = 0;
-  if (smem_per_sm == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-  }
-  const uint32_t fit = std::max(1u, std::min<uint32_t>(kTcCtasPerSm, uint32_t(smem_per_sm) / (smem + 1024)));
-  uint32_t nctas = std::min<uint32_t>(ngroups, uint32_t(sm_count) * fit);
-  // at most kTcGroups virtual groups per CTA
-  while ((ngroups + nctas - 1) / nctas * mats > uint32_t(kTcGroups)) ++nctas;
-  if (nctas > ngroups) return SI_E_UNSUPPORTED;
+  const uint32_t smem = tc_smem_bytes(nblk);
+  uint32_t resident = 0;
+  const uint32_t nctas = tc_grid(rows, nblk, mats, sm_count, &resident);
+  // every CTA of a peer exchange waits for the other ranks' rows: the whole
+  // grid must be resident at once
+  if (nctas == 0 || (p.peer.n && nctas > resident)) return SI_E_UNSUPPORTED;
   const uint32_t ngmax = (ngroups + nctas - 1) / nctas;
   const uint32_t lo_band = 16 * (ngmax > 1 ? ngmax - 1 : 1);
   CUtensorMap hi, lo, uhi, ulo;

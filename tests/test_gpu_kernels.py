@@ -175,6 +175,19 @@ def test_fused_gate_up_matches_oracle(ctx):
     assert rel_l2(ctx.q4_k_fused_gate_up(g, u, rows, cols, x), O.fused_gate_up(g, u, rows, cols, x)) < TOL
 
 
+@pytest.mark.parametrize("rows", [17408, 17400, 9000])
+def test_fused_gate_up_tensor_core_two_ctas_per_sm(ctx, rows):
+    """SwiGLU pairs of more row groups than four per SM (the 27B gate/up,
+    17,408 x 5,120, and ragged variants) run on the tensor cores at two CTAs
+    per SM, each staging at most four gate and four up groups."""
+    rng = np.random.default_rng(rows)
+    cols = 5120
+    g = random_blocks(rng, 12, rows * cols // 256)
+    u = random_blocks(rng, 12, rows * cols // 256)
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    assert rel_l2(ctx.q4_k_fused_gate_up(g, u, rows, cols, x), O.fused_gate_up(g, u, rows, cols, x)) < TOL
+
+
 def test_fused_gate_up_reference_pattern(ctx):  # metal.rs:7496-7540
     rows, cols = 2, 256
     gate = np.zeros(rows * 144, np.uint8)
