@@ -117,6 +117,10 @@ struct si_model {
   void* peer_block[kP2PMaxRanks] = {};
   uint32_t p2p_epoch = 0;
   uint64_t flag_off = 0;
+  // in-kernel all-gather of the Q4_K matvecs' outputs (PeerOut): offsets in
+  // the scratch block of the CTA ticket, the launch epoch and the exchange
+  // words of the hidden and activation vectors (two parity halves each)
+  uint64_t xchg_ticket_off = 0, xchg_epoch_off = 0, ll_hidden_off = 0, ll_act_off = 0;
   std::vector<float> rope_host;
   bool accounted = false;  // device bytes recorded in the context telemetry
   // measured planner trace (si_model_trace_begin / _end)
@@ -364,6 +368,15 @@ uint64_t batch_qmm_bytes(const si_model& m) {
   return b;
 }
 
+// The exchange area of a sharded model (n > 1; it takes the place of the
+// verifier's buffers, which only one GPU has): ticket and epoch words, then
+// 8-byte exchange words for two parity halves of the hidden and of the
+// activation vector.
+uint64_t xchg_bytes(const si_model& m) {
+  if (m.n == 1) return 0;
+  return 256 + 512 + align256(16ull * m.c.hidden) + align256(16ull * m.c.intermediate);
+}
+
 uint64_t batch_bytes(const si_model& m) {
   const std::vector<uint64_t> f = batch_float_counts(m);
   if (f.empty()) return 0;
@@ -414,7 +427,7 @@ int compute_plan(si_model* m, uint64_t budget, uint32_t depth, const Retention* 
   }
   uint64_t scratch_bytes = 4 * 256 + 64 * kP2PMaxRanks;  // token, argmax keys, peer flags
   for (uint64_t f : scratch_float_counts(*m)) scratch_bytes += align256(f * 4);
-  scratch_bytes += batch_bytes(*m);
+  scratch_bytes += batch_bytes(*m) + xchg_bytes(*m);
   uint64_t max_layer = 0, all_layers = 0;
   for (uint32_t l = 0; l < c.layers; ++l) {
     max_layer = std::max(max_layer, m->layout[l].bytes);
@@ -769,6 +782,13 @@ int create_model(si_ctx* ctx, const si_model_config* cfg, uint64_t seed,
     m->d_key = reinterpret_cast<unsigned long long*>(s + 256);
     m->d_keys = reinterpret_cast<unsigned long long*>(s + 512);
     m->flag_off = uint64_t(s + 1024 - m->scratch_block);
+    if (m->n > 1) {
+      const uint64_t x0 = align256(m->flag_off + 64 * kP2PMaxRanks);
+      m->xchg_ticket_off = x0;
+      m->xchg_epoch_off = x0 + 256;
+      m->ll_hidden_off = x0 + 512;
+      m->ll_act_off = m->ll_hidden_off + align256(16ull * c.hidden);
+    }
     const std::vector<uint64_t> bf = batch_float_counts(*m);
     if (!bf.empty()) {
       uint8_t* b = m->scratch_block + align256(m->flag_off + 64 * kP2PMaxRanks);
@@ -1259,10 +1279,46 @@ int gather(si_model* m, const float* s1, float* r1, uint32_t n1, const float* s2
   return e == cudaSuccess ? SI_OK : cuda_fail(m->ctx, e, "peer all-gather launch");
 }
 
+// A Q4_K matvec (or SwiGLU pair) of this rank's rows whose epilogue gathers
+// the whole vector into `full` on every rank over NVLink (PeerOut): no
+// stand-alone all-gather launch. `ll_off` locates the vector's exchange words
+// in every rank's scratch block. SI_E_UNSUPPORTED (nothing launched) when the
+// peer mapping is absent or the tensor-core kernel does not take the call.
+int exchange_qmv(si_model* m, QmvParams p, float* full, uint64_t ll_off, uint32_t full_len) {
+  if (!m->p2p || m->n < 2 || m->n > kPeerMax) return SI_E_UNSUPPORTED;
+  p.peer.n = uint32_t(m->n);
+  p.peer.rank = uint32_t(m->r);
+  for (int i = 0; i < m->n; ++i)
+    p.peer.ll[i] = reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(m->peer_block[i]) + ll_off);
+  p.peer.parity_stride = full_len;
+  p.peer.y = full;
+  p.peer.row0 = uint32_t(m->r) * p.seg[0].rows;
+  p.peer.total = uint32_t(m->n) * p.seg[0].rows;
+  p.peer.ticket = reinterpret_cast<uint32_t*>(m->scratch_block + m->xchg_ticket_off);
+  p.peer.epoch = reinterpret_cast<uint32_t*>(m->scratch_block + m->xchg_epoch_off);
+  p.peer.wait_cycles = kWaitCycles;
+  // only where one GPU would run the whole matrix on the tensor-core kernel
+  // too (the kernel is chosen by the full shape, not the shard)
+  QmvParams whole = p;
+  whole.peer = PeerOut{};
+  for (uint32_t i = 0; i < whole.nseg; ++i) whole.seg[i].rows = full_len;
+  if (p.peer.total != full_len || !qmv_tc_eligible(whole) || !qmv_tc_supported(p)) return SI_E_UNSUPPORTED;
+  std::string msg;
+  const int rc = launch_qmv_tc(p, m->ctx->stream, m->ctx->sm_count, true, &msg);
+  if (rc == SI_E_UNSUPPORTED) return rc;
+  return rc ? fail(m->ctx, rc, msg) : SI_OK;
+}
+
 int residual_matvec(si_model* m, QmvParams p, const uint8_t* w) {
   const uint32_t r0 = m->H_l * uint32_t(m->r);
   p.seg[0] = {w, m->n > 1 ? m->slice : m->hidden + r0, m->hidden + r0, m->H_l, 0};
   p.items = m->H_l;
+  if (m->n > 1) {
+    // the residual rows are read by the CTA that owns them before their new
+    // value leaves, so the gather may write `hidden` in place
+    const int xrc = exchange_qmv(m, p, m->hidden, m->ll_hidden_off, m->c.hidden);
+    if (xrc != SI_E_UNSUPPORTED) return xrc;
+  }
   int rc = run_qmv(m, p);
   if (rc) return rc;
   if (m->n > 1) return gather(m, m->slice, m->hidden, m->H_l);
@@ -1282,7 +1338,17 @@ int mlp(si_model* m, uint32_t l, const uint8_t* base) {
   p.x = m->hidden;
   p.xw = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_POST_NORM));
   int rc;
-  if (tg == tu) {
+  const float* act = m->act;
+  bool gathered = false;
+  if (tg == tu && m->n > 1) {
+    rc = exchange_qmv(m, p, m->act_full, m->ll_act_off, c.intermediate);
+    gathered = rc == SI_OK;
+    if (rc != SI_E_UNSUPPORTED && rc != SI_OK) return rc;
+    if (gathered) act = m->act_full;
+  }
+  if (gathered) {
+    rc = SI_OK;
+  } else if (tg == tu) {
     rc = run_qmv(m, p);  // fused SwiGLU pair
   } else {
     p.pair = 0;
@@ -1292,8 +1358,7 @@ int mlp(si_model* m, uint32_t l, const uint8_t* base) {
     if (!rc) launch_swiglu(m->act, m->up, m->act, m->I_l, m->ctx->stream);
   }
   if (rc) return rc;
-  const float* act = m->act;
-  if (m->n > 1) {
+  if (m->n > 1 && !gathered) {
     if ((rc = gather(m, m->act, m->act_full, m->I_l))) return rc;
     act = m->act_full;
   }

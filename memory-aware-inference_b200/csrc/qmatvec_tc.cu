@@ -439,8 +439,8 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
       o8 = yg8 / (1.0f + expf(-yg8)) * upv[grp_w * 16 + g + 8];
     }
     if (a.peer.n) {
-      if (row < a.rows) peer_store_row(a.peer, s_epoch, row, o0);
-      if (row + 8 < a.rows) peer_store_row(a.peer, s_epoch, row + 8, o8);
+      if (row < a.rows) peer_store_row(a.peer, s_epoch, row, a.resid ? a.resid[row] + o0 : o0);
+      if (row + 8 < a.rows) peer_store_row(a.peer, s_epoch, row + 8, a.resid ? a.resid[row + 8] + o8 : o8);
     } else {
       if (row < a.rows) a.y[row] = a.resid ? a.resid[row] + o0 : o0;
       if (row + 8 < a.rows) a.y[row + 8] = a.resid ? a.resid[row + 8] + o8 : o8;

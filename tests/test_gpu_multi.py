@@ -21,8 +21,14 @@ PROMPT = [3, 141, 59, 2653, 17]
 STEPS = 12
 
 
-def _decode(mai, ctx):
-    m = mai.Model(ctx, mai.qwen36_27b_config(**CFG), seed=77)
+# hidden and intermediate of 4096 rows and more: one GPU runs these matrices
+# on the tensor-core matvec, so the sharded model gathers the activation and
+# the hidden vector inside that kernel (no stand-alone all-gather)
+CFG_EXCHANGE = dict(CFG, hidden=4096, intermediate=8192, layers=4, attn_q_heads=16)
+
+
+def _decode(mai, ctx, cfg=CFG):
+    m = mai.Model(ctx, mai.qwen36_27b_config(**cfg), seed=77)
     try:
         m.reset()
         ids = m.generate(PROMPT, STEPS)
@@ -34,7 +40,7 @@ def _decode(mai, ctx):
         m.close()
 
 
-def _worker(rank, world, uid, flags, out):
+def _worker(rank, world, uid, flags, out, cfg=CFG):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
     sys.path.insert(0, here)
@@ -43,7 +49,7 @@ def _worker(rank, world, uid, flags, out):
     mai = load_package()
     ctx = mai.CudaContext(rank, flags=flags)
     ctx.comm_init(world, rank, uid)
-    ids, logits = _decode(mai, ctx)
+    ids, logits = _decode(mai, ctx, cfg)
     ctx.close()
     out[rank] = (ids, logits.tobytes())
 
@@ -69,6 +75,33 @@ def test_row_sharded_decode_matches_one_gpu(mai, transport):
         ids, lb = out[rank]
         assert ids == ref_ids, rank
         assert np.array_equal(np.frombuffer(lb, np.float32), ref_logits), rank
+
+
+def test_row_sharded_decode_with_in_kernel_gather(mai):
+    """Sharded decode whose Q4_K gate/up pairs and residual matvecs gather
+    their outputs inside the tensor-core matvec. Its shards add their blocks
+    in another order than the whole matrix does on one GPU (the kernel
+    splits a row's blocks over as many warps as its CTA has room for), so the
+    logits agree within 1e-4 rather than bit for bit, and the greedy IDs
+    agree exactly."""
+    import torch
+    import torch.multiprocessing as mp
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least two GPUs")
+    world = 8 if n >= 8 else (4 if n >= 4 else 2)
+    uid = mai.CudaContext.comm_unique_id()
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_worker, args=(world, uid, 0, out, CFG_EXCHANGE), nprocs=world, join=True)
+    ctx = mai.CudaContext(0)
+    ref_ids, ref_logits = _decode(mai, ctx, CFG_EXCHANGE)
+    ctx.close()
+    for rank in range(world):
+        ids, lb = out[rank]
+        got = np.frombuffer(lb, np.float32)
+        assert ids == ref_ids, rank
+        assert np.linalg.norm(got - ref_logits) / np.linalg.norm(ref_logits) < 1e-4, rank
 
 
 def _sharded_worker(rank, world, uid, out):
