@@ -431,17 +431,40 @@ typedef struct si_plan_info {
  * stays whole; with it every other layer streams through the ring, as in the
  * reference. A retained set that the budget cannot hold beside the head, the
  * ring, state and scratch is refused with SI_E_BUDGET; a listed layer past the
- * model's depth with SI_E_INVALID. The reference's tensor-level forms (gate/up
- * only, down only, attention only, Q6_K tensors only) are not offered: the ring
- * streams whole packed layers. */
+ * model's depth with SI_E_INVALID.
+ *
+ * With SI_RETAIN_TENSORS the fields after `flags` are read too: the
+ * reference's tensor-level forms, which it applies only when no layers are
+ * retained by count (retained_layers == 0, qwen35_runtime.rs:1565-1640), and
+ * neither are they here when prefix_layers != 0. Of every streamed layer the
+ * selected tensors stay resident and only the rest goes through the ring:
+ *   mlp_layers                gate and up of layers 0..mlp_layers-1
+ *                             (SI_RETAIN_MLP_LAYERS, 1646-1649);
+ *   mlp_stride, mlp_offset    gate and up of the stride layers
+ *                             (SI_RETAIN_MLP_STRIDE / _OFFSET, 1650-1655);
+ *   q6_layers                 every Q6_K tensor of layers 0..q6_layers-1
+ *                             (SI_RETAIN_Q6_LAYERS, 1656-1662);
+ *   down_stride, down_offset  ffn_down of the stride layers
+ *                             (SI_RETAIN_DOWN_STRIDE / _OFFSET, 1667-1671);
+ *   attention_stride, _offset q, k, v and output projections of the stride
+ *                             layers that are full-attention layers
+ *                             (SI_RETAIN_ATTENTION_STRIDE / _OFFSET, 1672-1682).
+ * A stride of 0 selects nothing. The selected tensors count against the
+ * budget like retained layers (SI_E_BUDGET when they do not fit). */
 typedef struct si_retention {
   uint32_t prefix_layers;
   uint32_t stride, offset;
   const uint32_t* layers; /* may be NULL when n_layers is 0 */
   uint32_t n_layers;
   uint32_t flags;         /* SI_RETAIN_* */
+  /* read only with SI_RETAIN_TENSORS */
+  uint32_t mlp_layers, mlp_stride, mlp_offset;
+  uint32_t q6_layers;
+  uint32_t down_stride, down_offset;
+  uint32_t attention_stride, attention_offset;
 } si_retention;
 #define SI_RETAIN_EXACT 1u
+#define SI_RETAIN_TENSORS 2u
 /* The policy for models created on `ctx` afterwards; NULL restores the
  * default (the budget-filled prefix). */
 int si_ctx_set_retention(si_ctx* ctx, const si_retention* r);
@@ -476,6 +499,10 @@ int si_model_plan_dry_retained(const si_model_config* c, int nranks, int rank, u
                                uint8_t* resident);
 /* Which layers of a created model are resident (layers flags, as above). */
 int si_model_resident_layers(const si_model* m, uint8_t* resident, uint32_t layers);
+/* Bytes of each layer that stay resident while the rest of the layer streams
+ * (the tensor-level retention above; 0 for whole-resident and plainly
+ * streamed layers): `layers` u64 values. */
+int si_model_resident_part_bytes(const si_model* m, uint64_t* part_bytes, uint32_t layers);
 /* Full-tensor row ranges [begin, end) that rank `rank` of `nranks` holds of a
  * tensor (ranges: 2*max_ranges u64). No device needed. */
 int si_model_shard_rows(const si_model_config* c, int nranks, int rank, uint32_t layer,

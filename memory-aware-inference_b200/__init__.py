@@ -142,21 +142,35 @@ class SiPlanInfo(C.Structure):
 
 class SiRetention(C.Structure):
     _fields_ = [("prefix_layers", C.c_uint32), ("stride", C.c_uint32), ("offset", C.c_uint32),
-                ("layers", C.POINTER(C.c_uint32)), ("n_layers", C.c_uint32), ("flags", C.c_uint32)]
+                ("layers", C.POINTER(C.c_uint32)), ("n_layers", C.c_uint32), ("flags", C.c_uint32),
+                ("mlp_layers", C.c_uint32), ("mlp_stride", C.c_uint32), ("mlp_offset", C.c_uint32),
+                ("q6_layers", C.c_uint32), ("down_stride", C.c_uint32), ("down_offset", C.c_uint32),
+                ("attention_stride", C.c_uint32), ("attention_offset", C.c_uint32)]
 
 
 RETAIN_EXACT = 1
+RETAIN_TENSORS = 2
 
 
-def retention(prefix_layers: int = 0, stride: int = 0, offset: int = 0, layers=(), exact: bool = False):
-    """A whole-layer retention policy (si_retention): the first
+def retention(prefix_layers: int = 0, stride: int = 0, offset: int = 0, layers=(), exact: bool = False,
+              mlp_layers: int = 0, mlp_stride: int = 0, mlp_offset: int = 0, q6_layers: int = 0,
+              down_stride: int = 0, down_offset: int = 0, attention_stride: int = 0, attention_offset: int = 0):
+    """A retention policy (si_retention). Whole layers: the first
     `prefix_layers` layers (retained_layers), every layer with
     layer % stride == offset % stride (retains_stride_layer), and the listed
     `layers` (SI_RETAIN_FULL_LAYERS) stay resident; `exact` streams all
-    others (qwen35_runtime.rs:1552-1733, 2270-2280)."""
+    others (qwen35_runtime.rs:1552-1733, 2270-2280). Tensors (only while
+    prefix_layers is 0, as in the reference, 1565-1682): gate/up of the first
+    `mlp_layers` layers or of the mlp stride layers, every Q6_K tensor of the
+    first `q6_layers` layers, ffn_down of the down stride layers and the
+    q/k/v/output projections of the attention stride layers stay resident
+    while the rest of their layer streams."""
     arr = (C.c_uint32 * max(len(layers), 1))(*layers)
-    r = SiRetention(prefix_layers, stride, offset, C.cast(arr, C.POINTER(C.c_uint32)), len(layers),
-                    RETAIN_EXACT if exact else 0)
+    tensors = any((mlp_layers, mlp_stride, q6_layers, down_stride, attention_stride))
+    flags = (RETAIN_EXACT if exact else 0) | (RETAIN_TENSORS if tensors else 0)
+    r = SiRetention(prefix_layers, stride, offset, C.cast(arr, C.POINTER(C.c_uint32)), len(layers), flags,
+                    mlp_layers, mlp_stride, mlp_offset, q6_layers, down_stride, down_offset,
+                    attention_stride, attention_offset)
     r._keep = arr
     return r
 
@@ -198,6 +212,7 @@ def lib():
         "si_weight_upload": ([vp, vp, u64, u32, vp], i32),
         "si_weight_bind_host": ([vp, vp, u64, u32, vp], i32),
         "si_weight_free": ([vp], None),
+        "si_model_resident_part_bytes": ([vp, vp, u32], i32),
         "si_weight_bytes": ([vp], u64),
         "si_weight_type": ([vp], u32),
         "si_weight_device_ptr": ([vp], vp),
@@ -1180,6 +1195,13 @@ class Model:
         flags = (C.c_uint8 * max(self.config.layers, 1))()
         self.ctx._ck(lib().si_model_resident_layers(self.h, flags, self.config.layers))
         return [bool(flags[i]) for i in range(self.config.layers)]
+
+    def resident_part_bytes(self) -> list:
+        """Per layer, the bytes kept resident of a streamed layer by a
+        tensor-level policy (si_model_resident_part_bytes)."""
+        vals = (C.c_uint64 * max(self.config.layers, 1))()
+        self.ctx._ck(lib().si_model_resident_part_bytes(self.h, vals, self.config.layers))
+        return [int(vals[i]) for i in range(self.config.layers)]
 
     def host_tensor(self, layer: int, tensor: int):
         """(address, bytes, ggml_type) of this rank's pinned host copy of a tensor."""

@@ -46,6 +46,9 @@ struct Retention {
   bool set = false;
   uint32_t prefix = 0, stride = 0, offset = 0, flags = 0;
   std::vector<uint32_t> layers;
+  // tensor-level forms (SI_RETAIN_TENSORS; si_retention in si_cuda.h)
+  uint32_t mlp_layers = 0, mlp_stride = 0, mlp_offset = 0, q6_layers = 0;
+  uint32_t down_stride = 0, down_offset = 0, attention_stride = 0, attention_offset = 0;
 };
 
 }  // namespace si

@@ -121,6 +121,10 @@ struct si_model {
   // the scratch block of the CTA ticket, the launch epoch and the exchange
   // words of the hidden and activation vectors (two parity halves each)
   uint64_t xchg_ticket_off = 0, xchg_epoch_off = 0, ll_hidden_off = 0, ll_act_off = 0;
+  // tensor-level retention: of a streamed layer l the packed bytes
+  // [0, part_bytes[l]) stay resident at dev_part[l] (the ring copies the rest)
+  std::vector<uint64_t> part_bytes;
+  std::vector<uint8_t*> dev_part;
   std::vector<float> rope_host;
   bool accounted = false;  // device bytes recorded in the context telemetry
   // measured planner trace (si_model_trace_begin / _end)
@@ -393,7 +397,7 @@ int retention_from(const si_retention* r, Retention* out, std::string* err) {
     *err = "retention policy lists layers without an array";
     return SI_E_INVALID;
   }
-  if (r->flags & ~SI_RETAIN_EXACT) {
+  if (r->flags & ~(SI_RETAIN_EXACT | SI_RETAIN_TENSORS)) {
     *err = "unknown retention flags " + std::to_string(r->flags);
     return SI_E_INVALID;
   }
@@ -403,7 +407,65 @@ int retention_from(const si_retention* r, Retention* out, std::string* err) {
   out->offset = r->offset;
   out->flags = r->flags;
   out->layers.assign(r->layers, r->layers + r->n_layers);
+  if (r->flags & SI_RETAIN_TENSORS) {
+    out->mlp_layers = r->mlp_layers;
+    out->mlp_stride = r->mlp_stride;
+    out->mlp_offset = r->mlp_offset;
+    out->q6_layers = r->q6_layers;
+    out->down_stride = r->down_stride;
+    out->down_offset = r->down_offset;
+    out->attention_stride = r->attention_stride;
+    out->attention_offset = r->attention_offset;
+  }
   return SI_OK;
+}
+
+bool retains_stride_layer(uint32_t layer, uint32_t stride, uint32_t offset) {
+  return stride != 0 && layer % stride == offset % stride;  // qwen35_runtime.rs:2270-2272
+}
+
+// The tensors of layer l that a tensor-level policy keeps resident
+// (qwen35_runtime.rs:1646-1682), as a bit mask of tensor ids. The reference
+// applies these forms only when no layers are retained by count (1565).
+uint32_t tensor_selection(const si_model& m, const Retention* ret, uint32_t l) {
+  if (!ret || !ret->set || ret->prefix != 0) return 0;
+  const LayerLayout& L = m.layout[l];
+  uint32_t mask = 0;
+  auto add = [&](int id) {
+    if (L.t[id].present) mask |= 1u << id;
+  };
+  if (l < ret->mlp_layers || retains_stride_layer(l, ret->mlp_stride, ret->mlp_offset)) {
+    add(SI_T_FFN_GATE);
+    add(SI_T_FFN_UP);
+  }
+  if (l < ret->q6_layers)
+    for (int id = 0; id < SI_T_COUNT; ++id)
+      if (L.t[id].present && L.t[id].type == SI_GGML_TYPE_Q6_K) add(id);
+  if (retains_stride_layer(l, ret->down_stride, ret->down_offset)) add(SI_T_FFN_DOWN);
+  if (!L.gdn && retains_stride_layer(l, ret->attention_stride, ret->attention_offset)) {
+    add(SI_T_ATTN_Q);
+    add(SI_T_ATTN_K);
+    add(SI_T_ATTN_V);
+    add(SI_T_ATTN_O);
+  }
+  return mask;
+}
+
+// Packs the selected tensors of a layer first (each tensor still spans
+// align256(bytes + 64), so the layer's size does not change) and returns the
+// bytes they occupy: the part that stays resident when the layer streams.
+uint64_t pack_selected_first(LayerLayout* L, uint32_t mask) {
+  uint64_t off = 0, part = 0;
+  for (int pass = 0; pass < 2; ++pass) {  // pass 0: the selected tensors, pass 1: the others
+    for (int id = 0; id < SI_T_COUNT; ++id) {
+      LocalTensor& t = L->t[id];
+      if (!t.present || (((mask >> id) & 1u) != 0) != (pass == 0)) continue;
+      t.offset = off;
+      off = align256(off + t.bytes + 64);
+    }
+    if (pass == 0) part = off;
+  }
+  return part;
 }
 
 // Residency plan inside `budget` (0 = unbounded): the output head and as many
@@ -456,6 +518,14 @@ int compute_plan(si_model* m, uint64_t budget, uint32_t depth, const Retention* 
         n_want++;
       }
   }
+  // the tensor-level parts of the layers not retained whole: their selected
+  // tensors are packed first and stay resident if the layer streams
+  std::vector<uint64_t> part(c.layers, 0);
+  uint64_t parts_total = 0;
+  for (uint32_t l = 0; l < c.layers; ++l) {
+    part[l] = pack_selected_first(&m->layout[l], want[l] ? 0u : tensor_selection(*m, ret, l));
+    parts_total += part[l];
+  }
   uint64_t resident = globals_bytes;
   std::vector<bool> res(c.layers, false);
   bool ring = false;
@@ -478,13 +548,14 @@ int compute_plan(si_model* m, uint64_t budget, uint32_t depth, const Retention* 
       return SI_E_BUDGET;
     }
     uint64_t left = budget == 0 ? UINT64_MAX : budget - fixed;
-    if (want_bytes > left) {
+    if (want_bytes + parts_total > left) {
       *err = "HBM budget " + std::to_string(budget) + " B leaves " + std::to_string(left) +
              " B beside the output head, ring, state and scratch, but the " + std::to_string(n_want) +
-             " retained layers need " + std::to_string(want_bytes) + " B";
+             " retained layers need " + std::to_string(want_bytes) + " B and the retained tensors of the others " +
+             std::to_string(parts_total) + " B";
       return SI_E_BUDGET;
     }
-    left -= want_bytes;
+    left -= want_bytes + parts_total;
     for (uint32_t l = 0; l < c.layers; ++l)
       if (want[l]) {
         res[l] = true;
@@ -493,13 +564,20 @@ int compute_plan(si_model* m, uint64_t budget, uint32_t depth, const Retention* 
     if (!exact) {
       for (uint32_t l = 0; l < c.layers; ++l) {
         if (res[l]) continue;
-        if (m->layout[l].bytes > left) break;
+        const uint64_t cost = m->layout[l].bytes - part[l];  // its part is already set aside
+        if (cost > left) break;
         res[l] = true;
-        left -= m->layout[l].bytes;
+        left -= cost;
         resident += m->layout[l].bytes;
       }
     }
   }
+  m->part_bytes.assign(c.layers, 0);
+  for (uint32_t l = 0; l < c.layers; ++l)
+    if (!res[l]) {
+      m->part_bytes[l] = part[l];
+      resident += part[l];
+    }
   m->plan = si_plan_info{};
   m->plan.budget_bytes = budget;
   m->plan.resident_weight_bytes = resident;
@@ -514,7 +592,7 @@ int compute_plan(si_model* m, uint64_t budget, uint32_t depth, const Retention* 
       m->plan.resident_layers++;
     } else {
       m->plan.streamed_layers++;
-      m->plan.streamed_bytes_per_token += m->layout[l].bytes;
+      m->plan.streamed_bytes_per_token += m->layout[l].bytes - m->part_bytes[l];
       m->streamed.push_back(l);
     }
   }
@@ -721,8 +799,17 @@ int create_model(si_ctx* ctx, const si_model_config* cfg, uint64_t seed,
   m->dev_layer.assign(c.layers + 1, nullptr);
   {
     uint64_t off = 0;
+    m->dev_part.assign(c.layers, nullptr);
     for (uint32_t l = 0; l <= c.layers; ++l) {
-      if (l < c.layers && !res[l]) continue;
+      if (l < c.layers && !res[l]) {
+        // a streamed layer's retained tensors (packed first)
+        const uint64_t pb = m->part_bytes[l];
+        if (pb == 0) continue;
+        m->dev_part[l] = m->dev_resident + off;
+        cudaMemcpyAsync(m->dev_part[l], m->host[l], pb, cudaMemcpyHostToDevice, ctx->copy_stream);
+        off += pb;
+        continue;
+      }
       m->dev_layer[l] = m->dev_resident + off;
       cudaMemcpyAsync(m->dev_layer[l], m->host[l], m->layout[l].bytes, cudaMemcpyHostToDevice, ctx->copy_stream);
       off += m->layout[l].bytes;
@@ -993,6 +1080,13 @@ extern "C" int si_model_resident_layers(const si_model* m, uint8_t* resident, ui
   return SI_OK;
 }
 
+extern "C" int si_model_resident_part_bytes(const si_model* m, uint64_t* part_bytes, uint32_t layers) {
+  if (!m || !part_bytes) return SI_E_INVALID;
+  if (layers != m->c.layers) return fail(m->ctx, SI_E_INVALID, "resident-part query needs one value per layer");
+  for (uint32_t l = 0; l < layers; ++l) part_bytes[l] = m->dev_part.empty() || !m->dev_part[l] ? 0 : m->part_bytes[l];
+  return SI_OK;
+}
+
 extern "C" int si_ctx_set_retention(si_ctx* ctx, const si_retention* r) {
   if (!ctx) return SI_E_INVALID;
   Retention ret;
@@ -1166,11 +1260,14 @@ void issue_copy(si_model* m, uint64_t occ) {
     if (m->slot_layer[s] >= 0)
       m->tr_recs.push_back({SI_ACT_EVICT, m->slot_layer[s], int(s), e0, e0, m->layout[m->slot_layer[s]].bytes});
   }
-  cudaMemcpyAsync(m->slot[s], m->host[l], m->layout[l].bytes, cudaMemcpyHostToDevice, m->ctx->copy_stream);
+  // the layer's retained part stays where it is: only [part, bytes) travels
+  const uint64_t pb = m->part_bytes[l];
+  cudaMemcpyAsync(m->slot[s] + pb, m->host[l] + pb, m->layout[l].bytes - pb, cudaMemcpyHostToDevice,
+                  m->ctx->copy_stream);
   cudaEventRecord(m->copy_done[s], m->ctx->copy_stream);
   if (m->tracing) {
     cudaEventRecord(e1, m->ctx->copy_stream);
-    m->tr_recs.push_back({SI_ACT_PREFETCH, int(l), int(s), e0, e1, m->layout[l].bytes});
+    m->tr_recs.push_back({SI_ACT_PREFETCH, int(l), int(s), e0, e1, m->layout[l].bytes - pb});
   }
   m->slot_layer[s] = int(l);
 }
@@ -1208,8 +1305,13 @@ void ring_prime(si_model* m) {
   while (m->occ_issued < m->occ_next + m->depth) issue_copy(m, m->occ_issued++);
 }
 
+// The device address of a tensor of a layer whose packed bytes are at `base`
+// (its resident copy or its ring slot); a streamed layer's retained tensors
+// (below part_bytes) are at dev_part instead.
 const uint8_t* tensor_ptr(const si_model* m, const uint8_t* base, uint32_t layer, int id) {
-  return base + m->layout[layer].t[id].offset;
+  const uint64_t off = m->layout[layer].t[id].offset;
+  if (layer < m->part_bytes.size() && off < m->part_bytes[layer] && m->dev_part[layer]) return m->dev_part[layer] + off;
+  return base + off;
 }
 
 QmvParams qmv_base(si_model* m, uint32_t type, uint32_t cols) {

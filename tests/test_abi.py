@@ -74,7 +74,7 @@ ABI_ENTRY_POINTS = [
     'si_model_create_gguf', 'si_model_create_synthetic', 'si_model_decode_hidden', 'si_model_decode_token',
     'si_model_decode_tokens_many', 'si_model_destroy', 'si_model_embed', 'si_model_generate',
     'si_model_host_tensor', 'si_model_logits', 'si_model_logits_many', 'si_model_plan', 'si_model_plan_dry',
-    'si_model_plan_dry_retained', 'si_model_reset', 'si_model_resident_layers', 'si_model_restore_states',
+    'si_model_plan_dry_retained', 'si_model_reset', 'si_model_resident_layers', 'si_model_resident_part_bytes', 'si_model_restore_states',
     'si_model_shard_rows', 'si_model_snapshot_free', 'si_model_snapshot_states', 'si_model_trace_begin',
     'si_model_trace_end', 'si_model_verify_many', 'si_plan_sequential_layers', 'si_q4_k_embedding_row',
     'si_q4_k_fused_gate_up', 'si_q4_k_fused_gate_up_weights', 'si_q4_k_matvec', 'si_q5_k_matvec',

@@ -86,6 +86,39 @@ def test_interleaved_retention_gives_identical_ids(mai, ctx, small_model):
     c2.close()
 
 
+@pytest.mark.parametrize("policy", [
+    dict(mlp_layers=5), dict(mlp_stride=3, mlp_offset=1), dict(down_stride=2, down_offset=1),
+    dict(attention_stride=4, attention_offset=3), dict(q6_layers=8),
+    dict(mlp_stride=2, down_stride=2, down_offset=1, attention_stride=4, attention_offset=3),
+])
+def test_tensor_retention_gives_identical_ids(mai, small_model, policy):
+    """Tensor-level retention (qwen35_runtime.rs:1646-1682): every layer
+    streams (exact, no whole layers kept), while the policy's tensors of each
+    layer stay resident and only the rest goes through the ring. The kernels
+    and their arithmetic are those of the resident model, so the greedy IDs
+    and the logits are identical."""
+    c2 = mai.CudaContext(0, stage_depth=2)
+    c2.set_retention(mai.retention(exact=True, **policy))
+    m2 = mai.Model(c2, small_config(mai), seed=1234)
+    try:
+        assert m2.resident_layers() == [False] * 8
+        parts = m2.resident_part_bytes()
+        assert any(parts) and all(p % 256 == 0 for p in parts)
+        plan = m2.plan()
+        assert plan["streamed_layers"] == 8
+        small_model.reset()
+        prompt = [3, 141, 59, 2653]
+        assert m2.generate(prompt, 12) == small_model.generate(prompt, 12)
+        m2.reset()
+        small_model.reset()
+        h2 = m2.decode_hidden(0, m2.embed_token(prompt[0]))
+        h1 = small_model.decode_hidden(0, small_model.embed_token(prompt[0]))
+        assert np.array_equal(m2.logits(h2), small_model.logits(h1))
+    finally:
+        m2.close()
+        c2.close()
+
+
 def test_budget_too_small_is_rejected(mai):
     import mai_b200 as M
     c2 = mai.CudaContext(0, hbm_budget_bytes=1 << 20)

@@ -176,3 +176,102 @@ def test_plan_invariants_hold_for_random_policies(mai):
         assert p["stage_depth"] == (0 if not p["streamed_layers"] else (min(depth, 4) if depth else 3))
 
     check()
+
+
+# ---- tensor-level forms (SI_RETAIN_TENSORS; qwen35_runtime.rs:1646-1682) ----
+
+def _span(nbytes):
+    """Bytes one tensor occupies in a packed layer buffer: 256-aligned, with
+    64 bytes of read-ahead padding."""
+    return (nbytes + 64 + 255) // 256 * 256
+
+
+def _q4k(rows, cols):
+    return rows * cols // 256 * 144
+
+
+def _q6k(rows, cols):
+    return rows * cols // 256 * 210
+
+
+@pytest.fixture(scope="module")
+def stream_all(mai, cfg):
+    """Every layer streams, only the output head is resident."""
+    return mai.plan_dry(cfg, retention=mai.retention(exact=True))
+
+
+def test_mlp_policy_keeps_gate_and_up_of_every_layer(mai, cfg, stream_all, whole):
+    """SI_RETAIN_MLP_STRIDE = 1: gate and up of all 64 layers resident, the
+    rest of every layer streamed once per token."""
+    p = mai.plan_dry(cfg, retention=mai.retention(exact=True, mlp_stride=1))
+    gate_up = 2 * _span(_q4k(cfg.intermediate, cfg.hidden))
+    assert p["resident"] == [False] * cfg.layers and p["streamed_layers"] == cfg.layers
+    assert p["resident_weight_bytes"] - stream_all["resident_weight_bytes"] == cfg.layers * gate_up
+    assert stream_all["streamed_bytes_per_token"] - p["streamed_bytes_per_token"] == cfg.layers * gate_up
+    assert p["resident_weight_bytes"] + p["streamed_bytes_per_token"] == whole["resident_weight_bytes"]
+
+
+def test_mlp_prefix_and_stride(mai, cfg, stream_all):
+    """SI_RETAIN_MLP_LAYERS = 3 with SI_RETAIN_MLP_STRIDE 10 / offset 5:
+    layers 0, 1, 2 and 5, 15, ..., 55 (3 + 6 layers)."""
+    p = mai.plan_dry(cfg, retention=mai.retention(exact=True, mlp_layers=3, mlp_stride=10, mlp_offset=5))
+    gate_up = 2 * _span(_q4k(cfg.intermediate, cfg.hidden))
+    assert p["resident_weight_bytes"] - stream_all["resident_weight_bytes"] == 9 * gate_up
+
+
+def test_down_stride_keeps_ffn_down_only(mai, cfg, stream_all):
+    p = mai.plan_dry(cfg, retention=mai.retention(exact=True, down_stride=4, down_offset=2))
+    down = _span(_q6k(cfg.hidden, cfg.intermediate))
+    assert p["resident_weight_bytes"] - stream_all["resident_weight_bytes"] == 16 * down
+
+
+def test_attention_stride_skips_gdn_layers(mai, cfg, stream_all):
+    """SI_RETAIN_ATTENTION_STRIDE = 1 selects the q/k/v/output projections
+    wherever they exist: only the 16 full-attention layers have them."""
+    p = mai.plan_dry(cfg, retention=mai.retention(exact=True, attention_stride=1))
+    qw = cfg.attn_q_heads * cfg.attn_head_dim
+    kvw = cfg.attn_kv_heads * cfg.attn_head_dim
+    proj = _span(_q4k(2 * qw, cfg.hidden)) + 2 * _span(_q4k(kvw, cfg.hidden)) + _span(_q4k(cfg.hidden, qw))
+    assert p["resident_weight_bytes"] - stream_all["resident_weight_bytes"] == 16 * proj
+    # the GDN layers (l % 4 != 3) give nothing: stride 4 offset 0 selects none
+    q = mai.plan_dry(cfg, retention=mai.retention(exact=True, attention_stride=4, attention_offset=0))
+    assert q["resident_weight_bytes"] == stream_all["resident_weight_bytes"]
+
+
+def test_q6_policy_keeps_the_q6k_tensors_of_the_first_layers(mai, cfg, stream_all):
+    """SI_RETAIN_Q6_LAYERS = 4: every Q6_K tensor of layers 0..3 (here each
+    layer's ffn_down)."""
+    p = mai.plan_dry(cfg, retention=mai.retention(exact=True, q6_layers=4))
+    assert p["resident_weight_bytes"] - stream_all["resident_weight_bytes"] == 4 * _span(
+        _q6k(cfg.hidden, cfg.intermediate))
+
+
+def test_tensor_forms_only_without_a_retained_prefix(mai, cfg):
+    """The reference reads the tensor-level settings only when
+    retained_layers is 0 (qwen35_runtime.rs:1565)."""
+    a = mai.plan_dry(cfg, retention=mai.retention(exact=True, prefix_layers=2))
+    b = mai.plan_dry(cfg, retention=mai.retention(exact=True, prefix_layers=2, mlp_stride=1, down_stride=1))
+    assert a == b
+
+
+def test_tensor_forms_count_against_the_budget(mai, cfg):
+    with pytest.raises(mai.SiError, match="retained tensors of the others") as e:
+        mai.plan_dry(cfg, budget=4 * GB, retention=mai.retention(exact=True, mlp_stride=1))
+    assert e.value.status == mai.SI_E_BUDGET
+    # without EXACT the rest of the budget goes to leading layers, each costing
+    # its bytes less the part already set aside
+    p = mai.plan_dry(cfg, budget=12 * GB, retention=mai.retention(mlp_stride=2))
+    lead = [l for l in range(cfg.layers) if p["resident"][l]]
+    assert lead == list(range(len(lead))) and 0 < len(lead) < cfg.layers
+    fixed = p["resident_weight_bytes"] + p["ring_bytes"] + p["state_bytes"] + p["scratch_bytes"]
+    assert fixed <= 12 * GB
+
+
+def test_sharded_ranks_keep_their_shard_of_the_same_tensors(mai, cfg, stream_all):
+    """Row-sharded over 4 ranks each rank keeps its quarter of gate and up."""
+    r = mai.retention(exact=True, mlp_stride=1)
+    for k in range(4):
+        base = mai.plan_dry(cfg, 4, k, 0, 3, mai.retention(exact=True))
+        p = mai.plan_dry(cfg, 4, k, 0, 3, r)
+        assert p["resident_weight_bytes"] - base["resident_weight_bytes"] == \
+            cfg.layers * 2 * _span(_q4k(cfg.intermediate // 4, cfg.hidden))
