@@ -50,6 +50,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <string>
 
 #include "common.cuh"
@@ -131,9 +132,18 @@ __device__ __forceinline__ uint32_t q6_word(uint32_t l, uint32_t h) {
   return lo | hi;
 }
 
-// Sign-extended byte `sel` (0..3) of a word.
-__device__ __forceinline__ int sbyte(uint32_t w, uint32_t sel) {
-  return int(w << (24 - 8 * sel)) >> 24;
+// prmt selector that moves byte k (0..3) of a word into byte 0 and fills the
+// other bytes with its sign (PTX prmt.b32: a selector nibble's bit 3
+// replicates the sign of the byte its bits 2:0 choose).
+__host__ __device__ constexpr uint32_t sx_sel(uint32_t k) {
+  return k | ((k | 8u) << 4) | ((k | 8u) << 8) | ((k | 8u) << 12);
+}
+
+// The sign-extended byte that `sel` (an sx_sel value) picks from a word.
+__device__ __forceinline__ int sbyte_p(uint32_t w, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(sel));
+  return int(r);
 }
 
 __global__ void __launch_bounds__(kT6Threads, 1)
@@ -293,7 +303,8 @@ __global__ void __launch_bounds__(kT6Threads, 1)
 
   const uint32_t g = uint32_t(lane) >> 2, c = uint32_t(lane) & 3;
   const uint32_t hi = c >> 1;                            // lanes 2, 3: the chunk's second scale group
-  const uint32_t sel0 = hi, sel1 = 2 + hi;               // scale byte of an even / odd m inside its word
+  // scale byte of an even / odd m inside its word, as prmt selectors
+  const uint32_t sel0 = sx_sel(hi), sel1 = sx_sel(2 + hi);
   const uint32_t slot = uint32_t(warp) % kT6Slots, half = uint32_t(warp) / kT6Slots;
   // this warp's block inside a chunk starts 210 slot bytes in: 2-byte aligned for odd slots
   const uint32_t boff8 = slot * 210;
@@ -324,90 +335,103 @@ __global__ void __launch_bounds__(kT6Threads, 1)
       if (a.err) atomicOr(a.err, KERR_TIMEOUT_FULL);
       alive = false;
     }
+    // the stage's arithmetic, for a slot whose rows start 4-byte aligned
+    // (even slots: one shared load per word) or 2 bytes past (odd slots)
+    auto stage_math = [&](auto aligned) {
+      constexpr bool AL = decltype(aligned)::value;
+      auto LD = [&](const uint8_t* r, uint32_t off) -> uint32_t {
+        if constexpr (AL) return *reinterpret_cast<const uint32_t*>(r + off);
+        else return ld_row32(r, off, 16);
+      };
+        const uint8_t* r0 = ring + s * kT6StagePitch + line0 + bal;
+        const uint8_t* r8 = ring + s * kT6StagePitch + line8 + bal;
+        uint32_t sw0[4], sw8[4];
+  #pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          sw0[k] = LD(r0, 192 + 4 * k);
+          sw8[k] = LD(r8, 192 + 4 * k);
+        }
+        const float d0 = half_bits_to_float(LD(r0, 208));
+        const float d8 = half_bits_to_float(LD(r8, 208));
+        int acc[4] = {0, 0, 0, 0};
+        const uint8_t* xb = xd + b * kT6DigBlock + boff;
+  #pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t l0[2][2], l8[2][2], h0[2], h8[2];
+  #pragma unroll
+          for (int kk = 0; kk < 2; ++kk) {
+            h0[kk] = LD(r0, 128 + hf * 32 + 16 * kk + 4 * c);
+            h8[kk] = LD(r8, 128 + hf * 32 + 16 * kk + 4 * c);
+  #pragma unroll
+            for (int mm = 0; mm < 2; ++mm) {
+              l0[mm][kk] = LD(r0, hf * 64 + mm * 32 + 16 * kk + 4 * c);
+              l8[mm][kk] = LD(r8, hf * 64 + mm * 32 + 16 * kk + 4 * c);
+            }
+          }
+  #pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            uint32_t A[4];
+            if (m == 0) {
+              A[0] = q6_word<0>(l0[0][0], h0[0]); A[1] = q6_word<0>(l8[0][0], h8[0]);
+              A[2] = q6_word<0>(l0[0][1], h0[1]); A[3] = q6_word<0>(l8[0][1], h8[1]);
+            } else if (m == 1) {
+              A[0] = q6_word<1>(l0[1][0], h0[0]); A[1] = q6_word<1>(l8[1][0], h8[0]);
+              A[2] = q6_word<1>(l0[1][1], h0[1]); A[3] = q6_word<1>(l8[1][1], h8[1]);
+            } else if (m == 2) {
+              A[0] = q6_word<2>(l0[0][0], h0[0]); A[1] = q6_word<2>(l8[0][0], h8[0]);
+              A[2] = q6_word<2>(l0[0][1], h0[1]); A[3] = q6_word<2>(l8[0][1], h8[1]);
+            } else {
+              A[0] = q6_word<3>(l0[1][0], h0[0]); A[1] = q6_word<3>(l8[1][0], h8[0]);
+              A[2] = q6_word<3>(l0[1][1], h0[1]); A[3] = q6_word<3>(l8[1][1], h8[1]);
+            }
+            const uint32_t bw = (b_lo || b_hi) ? *reinterpret_cast<const uint32_t*>(xb + (hf * 4 + m) * 96) : 0u;
+            int C[4];
+            mma_u8s8(C, A, b_lo ? bw : 0u, b_hi ? bw : 0u);
+            // scale sc[hf * 8 + 2m + hi]: word hf * 2 + m / 2, byte (m & 1) * 2 + hi
+            const uint32_t wsel = hf * 2 + (m >> 1), bsel = (m & 1) ? sel1 : sel0;
+            const int s0 = sbyte_p(sw0[wsel], bsel), s8 = sbyte_p(sw8[wsel], bsel);
+            acc[0] += s0 * C[0];
+            acc[1] += s0 * C[1];
+            acc[2] += s8 * C[2];
+            acc[3] += s8 * C[3];
+          }
+        }
+        // digit columns: lanes c = 0, 2 hold planes 0 and 1, lanes c = 1, 3 plane 2
+        float f0 = (c & 1) ? 65536.f * float(acc[0]) : fmaf(256.f, float(acc[1]), float(acc[0]));
+        float f8 = (c & 1) ? 65536.f * float(acc[2]) : fmaf(256.f, float(acc[3]), float(acc[2]));
+        f0 += __shfl_xor_sync(0xffffffffu, f0, 1);
+        f8 += __shfl_xor_sync(0xffffffffu, f8, 1);
+        f0 += __shfl_xor_sync(0xffffffffu, f0, 2);
+        f8 += __shfl_xor_sync(0xffffffffu, f8, 2);
+        // -32 offset: lane c takes groups 4c..4c+3 (scale word c)
+        const float4 xg = *reinterpret_cast<const float4*>(xs16 + b * 16 + 4 * c);
+        const uint32_t w0c = c == 0 ? sw0[0] : c == 1 ? sw0[1] : c == 2 ? sw0[2] : sw0[3];
+        const uint32_t w8c = c == 0 ? sw8[0] : c == 1 ? sw8[1] : c == 2 ? sw8[2] : sw8[3];
+        float mt0 = float(sbyte_p(w0c, sx_sel(0))) * xg.x + float(sbyte_p(w0c, sx_sel(1))) * xg.y;
+        mt0 += float(sbyte_p(w0c, sx_sel(2))) * xg.z + float(sbyte_p(w0c, sx_sel(3))) * xg.w;
+        float mt8 = float(sbyte_p(w8c, sx_sel(0))) * xg.x + float(sbyte_p(w8c, sx_sel(1))) * xg.y;
+        mt8 += float(sbyte_p(w8c, sx_sel(2))) * xg.z + float(sbyte_p(w8c, sx_sel(3))) * xg.w;
+        mt0 += __shfl_xor_sync(0xffffffffu, mt0, 1);
+        mt8 += __shfl_xor_sync(0xffffffffu, mt8, 1);
+        mt0 += __shfl_xor_sync(0xffffffffu, mt0, 2);
+        mt8 += __shfl_xor_sync(0xffffffffu, mt8, 2);
+        const float es = escale[b];
+        const float c0 = d0 * fmaf(-32.f, mt0, es * f0), c8 = d8 * fmaf(-32.f, mt8, es * f8);
+        yg += c0;
+        yg8 += c8;
+        if (!head && c == 0) {
+          // a later CTA finishes this group: keep the contribution itself
+          const uint32_t hc = t6_cta_of(grp * a.nchunks, U, a.nctas);
+          float* pp = a.part + ((uint64_t(hc) * kT6Warps + warp) * (a.nchunks + 1) + 1 + ch) * 16;
+          pp[g] = c0;
+          pp[g + 8] = c8;
+        }
+    };
     if (has && alive) {
-      const uint8_t* r0 = ring + s * kT6StagePitch + line0 + bal;
-      const uint8_t* r8 = ring + s * kT6StagePitch + line8 + bal;
-      uint32_t sw0[4], sw8[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        sw0[k] = ld_row32(r0, 192 + 4 * k, sh);
-        sw8[k] = ld_row32(r8, 192 + 4 * k, sh);
-      }
-      const float d0 = half_bits_to_float(ld_row32(r0, 208, sh));
-      const float d8 = half_bits_to_float(ld_row32(r8, 208, sh));
-      int acc[4] = {0, 0, 0, 0};
-      const uint8_t* xb = xd + b * kT6DigBlock + boff;
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        uint32_t l0[2][2], l8[2][2], h0[2], h8[2];
-#pragma unroll
-        for (int kk = 0; kk < 2; ++kk) {
-          h0[kk] = ld_row32(r0, 128 + hf * 32 + 16 * kk + 4 * c, sh);
-          h8[kk] = ld_row32(r8, 128 + hf * 32 + 16 * kk + 4 * c, sh);
-#pragma unroll
-          for (int mm = 0; mm < 2; ++mm) {
-            l0[mm][kk] = ld_row32(r0, hf * 64 + mm * 32 + 16 * kk + 4 * c, sh);
-            l8[mm][kk] = ld_row32(r8, hf * 64 + mm * 32 + 16 * kk + 4 * c, sh);
-          }
-        }
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          uint32_t A[4];
-          if (m == 0) {
-            A[0] = q6_word<0>(l0[0][0], h0[0]); A[1] = q6_word<0>(l8[0][0], h8[0]);
-            A[2] = q6_word<0>(l0[0][1], h0[1]); A[3] = q6_word<0>(l8[0][1], h8[1]);
-          } else if (m == 1) {
-            A[0] = q6_word<1>(l0[1][0], h0[0]); A[1] = q6_word<1>(l8[1][0], h8[0]);
-            A[2] = q6_word<1>(l0[1][1], h0[1]); A[3] = q6_word<1>(l8[1][1], h8[1]);
-          } else if (m == 2) {
-            A[0] = q6_word<2>(l0[0][0], h0[0]); A[1] = q6_word<2>(l8[0][0], h8[0]);
-            A[2] = q6_word<2>(l0[0][1], h0[1]); A[3] = q6_word<2>(l8[0][1], h8[1]);
-          } else {
-            A[0] = q6_word<3>(l0[1][0], h0[0]); A[1] = q6_word<3>(l8[1][0], h8[0]);
-            A[2] = q6_word<3>(l0[1][1], h0[1]); A[3] = q6_word<3>(l8[1][1], h8[1]);
-          }
-          const uint32_t bw = (b_lo || b_hi) ? *reinterpret_cast<const uint32_t*>(xb + (hf * 4 + m) * 96) : 0u;
-          int C[4];
-          mma_u8s8(C, A, b_lo ? bw : 0u, b_hi ? bw : 0u);
-          // scale sc[hf * 8 + 2m + hi]: word hf * 2 + m / 2, byte (m & 1) * 2 + hi
-          const uint32_t wsel = hf * 2 + (m >> 1), bsel = (m & 1) ? sel1 : sel0;
-          const int s0 = sbyte(sw0[wsel], bsel), s8 = sbyte(sw8[wsel], bsel);
-          acc[0] += s0 * C[0];
-          acc[1] += s0 * C[1];
-          acc[2] += s8 * C[2];
-          acc[3] += s8 * C[3];
-        }
-      }
-      // digit columns: lanes c = 0, 2 hold planes 0 and 1, lanes c = 1, 3 plane 2
-      float f0 = (c & 1) ? 65536.f * float(acc[0]) : fmaf(256.f, float(acc[1]), float(acc[0]));
-      float f8 = (c & 1) ? 65536.f * float(acc[2]) : fmaf(256.f, float(acc[3]), float(acc[2]));
-      f0 += __shfl_xor_sync(0xffffffffu, f0, 1);
-      f8 += __shfl_xor_sync(0xffffffffu, f8, 1);
-      f0 += __shfl_xor_sync(0xffffffffu, f0, 2);
-      f8 += __shfl_xor_sync(0xffffffffu, f8, 2);
-      // -32 offset: lane c takes groups 4c..4c+3 (scale word c)
-      const float4 xg = *reinterpret_cast<const float4*>(xs16 + b * 16 + 4 * c);
-      const uint32_t w0c = c == 0 ? sw0[0] : c == 1 ? sw0[1] : c == 2 ? sw0[2] : sw0[3];
-      const uint32_t w8c = c == 0 ? sw8[0] : c == 1 ? sw8[1] : c == 2 ? sw8[2] : sw8[3];
-      float mt0 = float(sbyte(w0c, 0)) * xg.x + float(sbyte(w0c, 1)) * xg.y;
-      mt0 += float(sbyte(w0c, 2)) * xg.z + float(sbyte(w0c, 3)) * xg.w;
-      float mt8 = float(sbyte(w8c, 0)) * xg.x + float(sbyte(w8c, 1)) * xg.y;
-      mt8 += float(sbyte(w8c, 2)) * xg.z + float(sbyte(w8c, 3)) * xg.w;
-      mt0 += __shfl_xor_sync(0xffffffffu, mt0, 1);
-      mt8 += __shfl_xor_sync(0xffffffffu, mt8, 1);
-      mt0 += __shfl_xor_sync(0xffffffffu, mt0, 2);
-      mt8 += __shfl_xor_sync(0xffffffffu, mt8, 2);
-      const float es = escale[b];
-      const float c0 = d0 * fmaf(-32.f, mt0, es * f0), c8 = d8 * fmaf(-32.f, mt8, es * f8);
-      yg += c0;
-      yg8 += c8;
-      if (!head && c == 0) {
-        // a later CTA finishes this group: keep the contribution itself
-        const uint32_t hc = t6_cta_of(grp * a.nchunks, U, a.nctas);
-        float* pp = a.part + ((uint64_t(hc) * kT6Warps + warp) * (a.nchunks + 1) + 1 + ch) * 16;
-        pp[g] = c0;
-        pp[g + 8] = c8;
-      }
+      if (sh == 0)
+        stage_math(std::true_type{});
+      else
+        stage_math(std::false_type{});
     } else if (!head && c == 0) {
       const uint32_t hc = t6_cta_of(grp * a.nchunks, U, a.nctas);
       float* pp = a.part + ((uint64_t(hc) * kT6Warps + warp) * (a.nchunks + 1) + 1 + ch) * 16;
