@@ -155,7 +155,14 @@ int si_gguf_quant_matvec_weight(si_ctx* ctx, const si_weight* w, uint64_t rows, 
 int si_gguf_quant_matvec_many_weights(si_ctx* ctx, uint32_t n, const si_weight* const* w,
                                       const uint64_t* rows, const uint64_t* cols,
                                       const float* x, float* const* y);
-/* Device form: `w_dev` holds rows*cols/256 blocks of `ggml_type`. */
+/* Device form: `w_dev` holds rows*cols/256 blocks of `ggml_type`.
+ * Calls of the device forms on one context may run on different streams at
+ * once: a Q6_K matvec of 2,048+ rows (or 64+ blocks per row) finishes the row
+ * groups it shares between CTAs in a scratch slot of the context that belongs
+ * to the launching stream (8 slots; past the eighth stream a call runs
+ * without one, slower). A CUDA graph that captured such a call keeps the
+ * capture stream's slot: replay it on that stream, or not at the same time
+ * as other calls on that stream. */
 int si_qmatvec_dev(si_ctx* ctx, uint32_t ggml_type, const void* w_dev, uint64_t rows,
                    uint64_t cols, const float* x_dev, float* y_dev, void* stream);
 /* Batched matvec for up to 8 inputs with one traversal of the weights
