@@ -68,6 +68,12 @@ struct TcArgs {
   uint32_t head_dim;     // XM_GATED (64, 128 or 256)
   uint32_t rows, nblk, ngroups, nctas;
   uint32_t mats;         // 1, or 2 for a SwiGLU pair (gate = map 0, up = map 1)
+  // two segments sharing x in one launch (mats 1, no peer output): CTAs
+  // [0, nctas0) run segment 0 (maps 0, y, resid, rows, ngroups), the others
+  // segment 1 (maps 1, y1, resid1, rows1, ngroups1); nctas0 = 0: one segment
+  uint32_t nctas0, rows1, ngroups1;
+  float* y1;
+  const float* resid1;
   int* err;
   PeerOut peer;          // n > 0: the rows go to every rank's vector (NVLink stores)
 };
@@ -147,13 +153,20 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
   uint64_t* xready = empty + kTcMaxStages;                      // [blk]: digits of block written
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t cta = blockIdx.x;
-  const uint32_t g0 = uint32_t(uint64_t(cta) * a.ngroups / a.nctas);
-  const uint32_t g1 = uint32_t(uint64_t(cta + 1) * a.ngroups / a.nctas);
+  // this CTA's segment, its index among the segment's CTAs, their count
+  const bool seg1 = a.nctas0 != 0 && blockIdx.x >= a.nctas0;
+  const uint32_t cta = seg1 ? blockIdx.x - a.nctas0 : blockIdx.x;
+  const uint32_t sctas = seg1 ? a.nctas - a.nctas0 : (a.nctas0 ? a.nctas0 : a.nctas);
+  const uint32_t sgroups = seg1 ? a.ngroups1 : a.ngroups;
+  const uint32_t g0 = uint32_t(uint64_t(cta) * sgroups / sctas);
+  const uint32_t g1 = uint32_t(uint64_t(cta + 1) * sgroups / sctas);
   const uint32_t ng = g1 - g0;                                   // 16-row groups of this CTA
-  const uint32_t ngmax = (a.ngroups + a.nctas - 1) / a.nctas;
-  const CUtensorMap* map = ng == ngmax ? &map_hi : &map_lo;
+  const uint32_t ngmax = (sgroups + sctas - 1) / sctas;
+  const CUtensorMap* map = seg1 ? (ng == ngmax ? &up_hi : &up_lo) : (ng == ngmax ? &map_hi : &map_lo);
   const CUtensorMap* map_up = ng == ngmax ? &up_hi : &up_lo;
+  float* const out_y = seg1 ? a.y1 : a.y;
+  const float* const out_resid = seg1 ? a.resid1 : a.resid;
+  const uint32_t out_rows = seg1 ? a.rows1 : a.rows;
   // "virtual groups": the CTA's row groups of each matrix (a SwiGLU pair has
   // the same rows of gate and up, staged one after the other)
   const uint32_t nv = ng * a.mats, nvmax = ngmax * a.mats;
@@ -439,11 +452,11 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
       o8 = yg8 / (1.0f + expf(-yg8)) * upv[grp_w * 16 + g + 8];
     }
     if (a.peer.n) {
-      if (row < a.rows) peer_store_row(a.peer, s_epoch, row, a.resid ? a.resid[row] + o0 : o0);
-      if (row + 8 < a.rows) peer_store_row(a.peer, s_epoch, row + 8, a.resid ? a.resid[row + 8] + o8 : o8);
+      if (row < out_rows) peer_store_row(a.peer, s_epoch, row, out_resid ? out_resid[row] + o0 : o0);
+      if (row + 8 < out_rows) peer_store_row(a.peer, s_epoch, row + 8, out_resid ? out_resid[row + 8] + o8 : o8);
     } else {
-      if (row < a.rows) a.y[row] = a.resid ? a.resid[row] + o0 : o0;
-      if (row + 8 < a.rows) a.y[row + 8] = a.resid ? a.resid[row + 8] + o8 : o8;
+      if (row < out_rows) out_y[row] = out_resid ? out_resid[row] + o0 : o0;
+      if (row + 8 < out_rows) out_y[row + 8] = out_resid ? out_resid[row + 8] + o8 : o8;
     }
   }
   if (a.peer.n) peer_gather(a.peer, a.nctas, s_epoch, a.err, kTcConsumers * 32);
@@ -507,7 +520,7 @@ bool qmv_tc_eligible(const QmvParams& p) {
   return true;
 }
 
-static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stream, int sm_count, bool pdl,
+static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, int seg2, cudaStream_t stream, int sm_count, bool pdl,
                              std::string* msg);
 
 static uint32_t tc_smem_bytes(uint32_t nblk) {
@@ -537,27 +550,56 @@ int launch_qmv_tc(const QmvParams& p, cudaStream_t stream, int sm_count, bool pd
   const uint32_t mats = p.pair ? 2 : 1;
   for (uint32_t i = 0; i < (p.pair ? 1u : p.nseg); ++i)
     if (tc_grid(p.seg[i].rows, p.cols / 256, mats, sm_count) == 0) return SI_E_UNSUPPORTED;
-  for (uint32_t i = 0; i < (p.pair ? 1u : p.nseg); ++i)
-    if (int rc = launch_qmv_tc_seg(p, i, stream, sm_count, pdl, msg)) return rc;
+  // segments of a grouped call two to a launch (they share x and its
+  // prologue); a SwiGLU pair or a peer exchange is one launch of one matrix
+  const uint32_t nl = p.pair ? 1u : p.nseg, step = (p.pair || p.peer.n) ? 1u : 2u;
+  for (uint32_t i = 0; i < nl; i += step)
+    if (int rc = launch_qmv_tc_seg(p, i, step == 2 && i + 1 < nl ? int(i + 1) : -1, stream, sm_count, pdl, msg))
+      return rc;
   return SI_OK;
 }
 
-static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stream, int sm_count, bool pdl,
+// The band maps of one matrix split over `nctas` CTAs: boxes of the largest
+// band (16 ngmax rows) and of the one below it.
+static bool tc_band_maps(CUtensorMap* hi, CUtensorMap* lo, const uint8_t* w, uint32_t rows, uint32_t nblk,
+                         uint32_t nctas) {
+  const uint32_t ngroups = (rows + 15) / 16, ngmax = (ngroups + nctas - 1) / nctas;
+  const uint32_t lo_band = 16 * (ngmax > 1 ? ngmax - 1 : 1);
+  return q4k_band_map(hi, w, rows, nblk, 16 * ngmax) && q4k_band_map(lo, w, rows, nblk, lo_band);
+}
+
+static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, int seg2, cudaStream_t stream, int sm_count, bool pdl,
                              std::string* msg) {
   const uint32_t rows = p.seg[seg].rows, nblk = p.cols / 256, mats = p.pair ? 2 : 1;
   const uint32_t ngroups = (rows + 15) / 16;
   const uint32_t smem = tc_smem_bytes(nblk);
-  uint32_t resident = 0;
-  const uint32_t nctas = tc_grid(rows, nblk, mats, sm_count, &resident);
-  // every CTA of a peer exchange waits for the other ranks' rows: the whole
-  // grid must be resident at once
-  if (nctas == 0 || (p.peer.n && nctas > resident)) return SI_E_UNSUPPORTED;
-  const uint32_t ngmax = (ngroups + nctas - 1) / nctas;
-  const uint32_t lo_band = 16 * (ngmax > 1 ? ngmax - 1 : 1);
+  uint32_t resident = 0, nctas = 0, nctas0 = 0, rows1 = 0, ngroups1 = 0;
+  if (seg2 < 0) {
+    nctas = tc_grid(rows, nblk, mats, sm_count, &resident);
+    // every CTA of a peer exchange waits for the other ranks' rows: the whole
+    // grid must be resident at once
+    if (nctas == 0 || (p.peer.n && nctas > resident)) return SI_E_UNSUPPORTED;
+  } else {
+    // the grid of the two segments' rows together, shared in proportion to
+    // their row groups, each segment at most kTcGroups groups per CTA
+    rows1 = p.seg[seg2].rows;
+    ngroups1 = (rows1 + 15) / 16;
+    const uint32_t total = tc_grid(rows + rows1, nblk, 1, sm_count, &resident);
+    if (total < 2) return SI_E_UNSUPPORTED;
+    nctas0 = uint32_t((uint64_t(total) * ngroups + (ngroups + ngroups1) / 2) / (ngroups + ngroups1));
+    nctas0 = std::min(std::max(nctas0, (ngroups + kTcGroups - 1) / uint32_t(kTcGroups)), ngroups);
+    nctas0 = std::max(nctas0, 1u);
+    uint32_t nctas1 = total > nctas0 ? total - nctas0 : 1u;
+    nctas1 = std::min(std::max(nctas1, (ngroups1 + kTcGroups - 1) / uint32_t(kTcGroups)), ngroups1);
+    nctas = nctas0 + std::max(nctas1, 1u);
+  }
   CUtensorMap hi, lo, uhi, ulo;
-  if (!q4k_band_map(&hi, p.seg[seg].w, rows, nblk, 16 * ngmax) || !q4k_band_map(&lo, p.seg[seg].w, rows, nblk, lo_band))
-    return SI_E_UNSUPPORTED;
-  if (mats == 2) {
+  if (!tc_band_maps(&hi, &lo, p.seg[seg].w, rows, nblk, nctas0 ? nctas0 : nctas)) return SI_E_UNSUPPORTED;
+  if (seg2 >= 0) {
+    if (!tc_band_maps(&uhi, &ulo, p.seg[seg2].w, rows1, nblk, nctas - nctas0)) return SI_E_UNSUPPORTED;
+  } else if (mats == 2) {
+    const uint32_t ngmax = (ngroups + nctas - 1) / nctas;
+    const uint32_t lo_band = 16 * (ngmax > 1 ? ngmax - 1 : 1);
     if (!q4k_band_map(&uhi, p.seg[1].w, rows, nblk, 16 * ngmax) || !q4k_band_map(&ulo, p.seg[1].w, rows, nblk, lo_band))
       return SI_E_UNSUPPORTED;
   } else {
@@ -583,6 +625,13 @@ static int launch_qmv_tc_seg(const QmvParams& p, uint32_t seg, cudaStream_t stre
   a.ngroups = ngroups;
   a.nctas = nctas;
   a.mats = mats;
+  if (seg2 >= 0) {
+    a.nctas0 = nctas0;
+    a.rows1 = rows1;
+    a.ngroups1 = ngroups1;
+    a.y1 = p.seg[seg2].y;
+    a.resid1 = p.seg[seg2].resid;
+  }
   a.err = p.err;
   a.peer = p.peer;
   cudaLaunchConfig_t cfg = {};
