@@ -264,6 +264,58 @@ __global__ void __launch_bounds__(kGdnD) gdn_layer_kernel(const GdnLayerArgs a) 
     g_in0 = a.gates[h];
     g_in1 = a.gates[vh + h];
     g_in2 = g_in3 = 0.f;
+  } else if (a.alpha_w) {
+    // this head's alpha and beta projections (qwen35_runtime.rs:409-446):
+    // rows alpha_w[h], beta_w[h] against x * (1 + norm) * rsqrt(mean x^2 + eps),
+    // the RMS factor applied to the two dot products at the end
+    const uint32_t cols = a.ab_cols;
+    const float* wa = a.alpha_w + uint64_t(h) * cols;
+    const float* wb = a.beta_w + uint64_t(h) * cols;
+    float ss = 0.f, da = 0.f, db = 0.f;
+    if ((cols & 3) == 0 && ((reinterpret_cast<uintptr_t>(wa) | reinterpret_cast<uintptr_t>(wb) |
+                             reinterpret_cast<uintptr_t>(a.ab_x) | reinterpret_cast<uintptr_t>(a.ab_norm)) & 15) == 0) {
+      const float4* x4 = reinterpret_cast<const float4*>(a.ab_x);
+      const float4* n4 = reinterpret_cast<const float4*>(a.ab_norm);
+      const float4* a4 = reinterpret_cast<const float4*>(wa);
+      const float4* b4 = reinterpret_cast<const float4*>(wb);
+      for (uint32_t i = t; i < cols / 4; i += kGdnD) {
+        const float4 xv = x4[i], nv = __ldg(n4 + i), av = __ldg(a4 + i), bv = __ldg(b4 + i);
+        ss += xv.x * xv.x + xv.y * xv.y + xv.z * xv.z + xv.w * xv.w;
+        const float y0 = xv.x * (1.0f + nv.x), y1 = xv.y * (1.0f + nv.y), y2 = xv.z * (1.0f + nv.z),
+                    y3 = xv.w * (1.0f + nv.w);
+        da += av.x * y0 + av.y * y1 + av.z * y2 + av.w * y3;
+        db += bv.x * y0 + bv.y * y1 + bv.z * y2 + bv.w * y3;
+      }
+    } else {
+      for (uint32_t i = t; i < cols; i += kGdnD) {
+        const float xv = a.ab_x[i], y = xv * (1.0f + a.ab_norm[i]);
+        ss += xv * xv;
+        da += wa[i] * y;
+        db += wb[i] * y;
+      }
+    }
+    __shared__ float abred[3][kGdnD / 32];
+    ss = warp_sum(ss);
+    da = warp_sum(da);
+    db = warp_sum(db);
+    if (lane == 0) {
+      abred[0][warp] = ss;
+      abred[1][warp] = da;
+      abred[2][warp] = db;
+    }
+    __syncthreads();
+    float tss = 0.f, tda = 0.f, tdb = 0.f;
+#pragma unroll
+    for (int w = 0; w < kGdnD / 32; ++w) {
+      tss += abred[0][w];
+      tda += abred[1][w];
+      tdb += abred[2][w];
+    }
+    const float inv = 1.0f / sqrtf(tss / float(cols) + a.ab_eps);
+    g_in0 = tda * inv;
+    g_in1 = a.dt_bias[h];
+    g_in2 = a.a_log[h];
+    g_in3 = tdb * inv;
   } else {
     g_in0 = a.alpha[h];
     g_in1 = a.dt_bias[h];

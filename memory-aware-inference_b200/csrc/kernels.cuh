@@ -37,6 +37,14 @@ struct GdnLayerArgs {
   const float* gates;      // if non-null: [g[vh], beta[vh]] supplied directly
   const float* alpha;      // else: alpha/beta projection outputs [vh] each
   const float* beta_logit;
+  // else, with alpha_w set, the projections are made here: alpha_w / beta_w
+  // F32 rows [vh][ab_cols] over the (1+w) RMSNorm (ab_norm, ab_eps) of ab_x
+  const float* alpha_w;
+  const float* beta_w;
+  const float* ab_x;
+  const float* ab_norm;
+  uint32_t ab_cols;
+  float ab_eps;
   const float* a_log;
   const float* dt_bias;
   float* core;             // [vh*128]

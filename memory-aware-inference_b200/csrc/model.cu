@@ -1485,26 +1485,27 @@ int gdn_layer(si_model* m, uint32_t l, const uint8_t* base) {
   const uint32_t types[2] = {type_of(m, l, SI_T_SSM_QKV), type_of(m, l, SI_T_SSM_Z)};
   int rc = run_group(m, p, types);
   if (rc) return rc;
-  // alpha and beta (F32 rows, adjacent in the packed layer), one launch
-  launch_f32_matvec_norm2(reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_ALPHA)), m->ab,
-                          reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_BETA)), m->ab + m->vh_l,
-                          m->vh_l, c.hidden, m->hidden, attn_norm, c.rms_eps, m->ctx->stream);
   GdnLayerArgs g = {};
+  // alpha and beta (F32 rows) are projected inside the GDN step kernel
+  g.alpha_w = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_ALPHA));
+  g.beta_w = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_BETA));
+  g.ab_x = m->hidden;
+  g.ab_norm = attn_norm;
+  g.ab_cols = c.hidden;
+  g.ab_eps = c.rms_eps;
   g.qkv = m->qkv;
   g.conv_w = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_CONV));
   const uint32_t par = m->conv_parity[l];
   g.conv_in = m->conv[par][l];
   g.conv_out = m->conv[par ^ 1][l];
   g.state = m->rec[l];
-  g.alpha = m->ab;
-  g.beta_logit = m->ab + m->vh_l;
   g.a_log = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_A));
   g.dt_bias = reinterpret_cast<const float*>(tensor_ptr(m, base, l, SI_T_SSM_DT));
   g.core = m->core;
   g.key_heads = m->kh_l;
   g.value_heads = m->vh_l;
   g.kernel = c.conv_kernel;
-  launch_gdn_layer(g, m->ctx->stream, false);
+  launch_gdn_layer(g, m->ctx->stream, true);
   m->conv_parity[l] = par ^ 1;
   const float* core = m->core;
   const float* z = m->z;
