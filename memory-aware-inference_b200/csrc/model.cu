@@ -1381,7 +1381,7 @@ int gather(si_model* m, const float* s1, float* r1, uint32_t n1, const float* s2
   return e == cudaSuccess ? SI_OK : cuda_fail(m->ctx, e, "peer all-gather launch");
 }
 
-// A Q4_K matvec (or SwiGLU pair) of this rank's rows whose epilogue gathers
+// A Q4_K or Q6_K matvec (or Q4_K SwiGLU pair) of this rank's rows whose epilogue gathers
 // the whole vector into `full` on every rank over NVLink (PeerOut): no
 // stand-alone all-gather launch. `ll_off` locates the vector's exchange words
 // in every rank's scratch block. SI_E_UNSUPPORTED (nothing launched) when the
@@ -1404,9 +1404,13 @@ int exchange_qmv(si_model* m, QmvParams p, float* full, uint64_t ll_off, uint32_
   QmvParams whole = p;
   whole.peer = PeerOut{};
   for (uint32_t i = 0; i < whole.nseg; ++i) whole.seg[i].rows = full_len;
-  if (p.peer.total != full_len || !qmv_tc_eligible(whole) || !qmv_tc_supported(p)) return SI_E_UNSUPPORTED;
+  if (p.peer.total != full_len) return SI_E_UNSUPPORTED;
+  const bool q6 = p.type == SI_GGML_TYPE_Q6_K;
+  if (q6 ? !(qmv_tc6_eligible(whole) && qmv_tc6_eligible(p)) : !(qmv_tc_eligible(whole) && qmv_tc_supported(p)))
+    return SI_E_UNSUPPORTED;
   std::string msg;
-  const int rc = launch_qmv_tc(p, m->ctx->stream, m->ctx->sm_count, true, &msg);
+  const int rc = q6 ? launch_qmv_tc6(p, m->ctx->stream, m->ctx->sm_count, true, &msg)
+                    : launch_qmv_tc(p, m->ctx->stream, m->ctx->sm_count, true, &msg);
   if (rc == SI_E_UNSUPPORTED) return rc;
   return rc ? fail(m->ctx, rc, msg) : SI_OK;
 }

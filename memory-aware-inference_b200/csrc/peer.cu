@@ -10,7 +10,8 @@
 //   [D + 1536, D + 2048)     flags of the stand-alone peer all-gather (fallback)
 //   [D + 2560, D + 2560 + 4D) exchange words: two parity halves of D/4 8-byte
 //                            words, word i standing for float i of the data
-// si_sharded_qmatvec_dev runs the Q4_K tensor-core matvec on this rank's rows;
+// si_sharded_qmatvec_dev runs the Q4_K (or, for the shapes it takes, the Q6_K)
+// tensor-core matvec on this rank's rows;
 // its epilogue stores each row, tagged with the launch's epoch, into every
 // rank's exchange words over NVLink, and each CTA unpacks its slice of the
 // gathered vector into the data once every rank's rows have arrived, so the
@@ -188,7 +189,10 @@ int si_sharded_qmatvec_dev(si_ctx* ctx, si_peer_buffer* b, uint32_t type, const 
     q.peer.ticket = reinterpret_cast<uint32_t*>(mine + b->data_bytes + kTicketOff);
     q.peer.epoch = reinterpret_cast<uint32_t*>(mine + b->data_bytes + kEpochOff);
     q.peer.wait_cycles = b->wait_cycles;
-    rc = si::qmv_tc_supported(q) ? si::launch_qmv_tc(q, s, ctx->sm_count, true, &msg) : SI_E_UNSUPPORTED;
+    if (type == SI_GGML_TYPE_Q6_K)
+      rc = si::qmv_tc6_eligible(q) ? si::launch_qmv_tc6(q, s, ctx->sm_count, true, &msg) : SI_E_UNSUPPORTED;
+    else
+      rc = si::qmv_tc_supported(q) ? si::launch_qmv_tc(q, s, ctx->sm_count, true, &msg) : SI_E_UNSUPPORTED;
     if (rc == SI_E_UNSUPPORTED) {
       // the matvec into this rank's slice, then the stand-alone peer all-gather
       rc = si::launch_qmv(p, s, ctx->sm_count, true, &msg);

@@ -831,6 +831,11 @@ int launch_qmv(const QmvParams& p, cudaStream_t stream, int sm_count, bool pdl,
     if (msg) *msg = "gated-norm head dimension is invalid";
     return SI_E_INVALID;
   }
+  if (p.peer.n) {
+    // the exchange lives in the tensor-core kernels, which their callers launch directly
+    if (msg) *msg = "a matvec with a peer exchange goes to launch_qmv_tc or launch_qmv_tc6";
+    return SI_E_UNSUPPORTED;
+  }
   const bool pair = p.pair != 0;
   switch (p.type) {
     case SI_GGML_TYPE_Q4_K:

@@ -36,6 +36,7 @@
 
 #include "common.cuh"
 #include "qmatvec.cuh"
+#include "peer_exchange.cuh"
 
 namespace si {
 
@@ -77,47 +78,6 @@ struct TcArgs {
   int* err;
   PeerOut peer;          // n > 0: the rows go to every rank's vector (NVLink stores)
 };
-
-// After the CTA's own rows have gone out, called by all `nthreads` consumer
-// threads: the CTA's slice of the gathered vector, word by word, as soon as
-// each word carries this launch's epoch (bounded), unpacked into y; then the
-// CTA's ticket, the launch's last CTA resetting it and advancing the epoch
-// (PeerOut, qmatvec.cuh).
-__device__ __noinline__ void peer_gather(const PeerOut& po, uint32_t nctas, uint32_t epoch, int* err,
-                                         uint32_t nthreads) {
-  const uint32_t lo = uint32_t(uint64_t(blockIdx.x) * po.total / nctas);
-  const uint32_t hi = uint32_t(uint64_t(blockIdx.x + 1) * po.total / nctas);
-  const uint64_t* w = po.ll[po.rank] + (epoch & 1) * po.parity_stride;
-  const long long t0 = clock64();
-  for (uint32_t i = lo + threadIdx.x; i < hi; i += nthreads) {
-    uint64_t v;
-    while (true) {
-      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(w + i) : "memory");
-      if (uint32_t(v >> 32) == epoch) break;
-      if (clock64() - t0 > po.wait_cycles) break;
-    }
-    if (uint32_t(v >> 32) != epoch) {
-      if (err) atomicOr(err, KERR_TIMEOUT_FULL);
-      break;
-    }
-    po.y[i] = __uint_as_float(uint32_t(v));
-  }
-  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
-  if (threadIdx.x == 0) {
-    // every CTA has read the epoch (at its start) before the last ticket
-    if (atomicAdd(po.ticket, 1u) == nctas - 1) {
-      *po.ticket = 0;
-      asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(po.epoch), "r"(epoch) : "memory");
-    }
-  }
-}
-
-__device__ __forceinline__ void peer_store_row(const PeerOut& po, uint32_t epoch, uint32_t row, float v) {
-  const uint64_t word = (uint64_t(epoch) << 32) | __float_as_uint(v);
-  const uint64_t at = (epoch & 1) * po.parity_stride + po.row0 + row;
-  for (uint32_t p = 0; p < po.n; ++p)
-    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(po.ll[p] + at), "l"(word) : "memory");
-}
 
 // C = A B with a zero accumulator (no register moves to clear C).
 __device__ __forceinline__ void mma_u8s8_zero(int* c, const uint32_t* a, uint32_t b0, uint32_t b1) {

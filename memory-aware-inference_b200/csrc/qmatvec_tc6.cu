@@ -55,6 +55,7 @@
 
 #include "common.cuh"
 #include "qmatvec.cuh"
+#include "peer_exchange.cuh"
 
 namespace si {
 
@@ -89,6 +90,7 @@ struct T6Args {
   uint32_t* counters;  // [nctas] CTAs finished with the group (zero between launches)
   float* part;       // [nctas][16 warps][nchunks + 1][16] the head's sums, the others' contributions
   int* err;
+  PeerOut peer;      // n > 0: the rows are gathered into every rank's vector (peer_exchange.cuh)
 };
 
 // CTA holding unit u under the even split of U units over G CTAs.
@@ -210,6 +212,9 @@ __global__ void __launch_bounds__(kT6Threads, 1)
 
   // ---- consumers ----
   pdl_wait();
+  // the launch's epoch of the peer exchange (the previous grid has finished)
+  __shared__ uint32_t s_epoch;
+  if (a.peer.n && threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile uint32_t*>(a.peer.epoch) + 1;
   float rms_inv = 1.f;
   if (a.xmode == XM_RMS1P) {
     // (1+w) RMSNorm over the whole vector (qwen35.rs:53-86, heads = 1)
@@ -497,12 +502,19 @@ __global__ void __launch_bounds__(kT6Threads, 1)
 #pragma unroll
         for (int w = 1; w < kT6Slots; ++w) tot += rh[w * 16];
         const uint32_t row = grp * 32 + uint32_t(lane);
-        if (row < a.rows) a.y[row] = a.resid ? a.resid[row] + tot : tot;
+        if (row < a.rows) {
+          const float v = a.resid ? a.resid[row] + tot : tot;
+          if (a.peer.n)
+            peer_store_row(a.peer, s_epoch, row, v);
+          else
+            a.y[row] = v;
+        }
       }
       asm volatile("bar.sync 1, %0;" ::"r"(kT6Warps * 32) : "memory");
       yg = yg8 = 0.f;
     }
   }
+  if (a.peer.n) peer_gather(a.peer, a.nctas, s_epoch, a.err, kT6Warps * 32);
 }
 
 }  // namespace
@@ -536,7 +548,7 @@ static bool t6_map(CUtensorMap* m, const void* base, uint64_t elems, uint64_t li
 
 bool qmv_tc6_eligible(const QmvParams& p) {
   const uint32_t nblk = p.cols / 256;
-  if (p.type != SI_GGML_TYPE_Q6_K || p.pair || p.nseg != 1 || p.peer.n || nblk > kT6MaxBlocks || nblk % 4 ||
+  if (p.type != SI_GGML_TYPE_Q6_K || p.pair || p.nseg != 1 || nblk > kT6MaxBlocks || nblk % 4 ||
       (reinterpret_cast<uintptr_t>(p.x) & 15) || p.seg[0].rows < kTc6MinRows ||
       (reinterpret_cast<uintptr_t>(p.seg[0].w) & 15))
     return false;
@@ -602,6 +614,7 @@ int launch_qmv_tc6(const QmvParams& p, cudaStream_t stream, int sm_count, bool p
     a.nctas = std::min<uint32_t>(ngroups, uint32_t(sm_count));
   }
   a.err = p.err;
+  a.peer = p.peer;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.nctas);
   cfg.blockDim = dim3(kT6Threads);

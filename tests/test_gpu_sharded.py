@@ -109,3 +109,32 @@ def test_config1_shards_take_the_fused_exchange(mai, ctx, rows_per_rank):
     finally:
         buf.close()
     ctx.synchronize()
+
+
+def test_q6k_shard_takes_the_fused_exchange(mai, ctx):
+    """A Q6_K shard of the 27B ffn_down at two ranks (2560 x 17408) runs the
+    Q6_K tensor-core matvec with the exchange in the kernel: its rows are in
+    the exchange words (epoch 1, parity half 1) and unpacked into this
+    rank's slice before the bounded wait for the absent rank runs out."""
+    import torch
+    rows, cols, world = 2560, 17408, 2
+    rng = np.random.default_rng(2560)
+    w = random_blocks(rng, 14, rows * cols // 256)
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    wd = torch.from_numpy(np.concatenate([w, np.zeros(64, np.uint8)])).cuda()
+    xd = torch.from_numpy(x).cuda()
+    nbytes = world * rows * 4
+    buf = ctx.peer_buffer_local(nbytes, world, 0, wait_us=1000)
+    try:
+        ctx.sharded_qmatvec_dev(buf, 14, wd, rows, cols, xd, 0)
+        with pytest.raises(mai.SiError) as ei:
+            ctx.synchronize()
+        assert ei.value.status == mai.SI_E_TIMEOUT
+        data_bytes = (nbytes + 255) // 256 * 256
+        word = _read(buf.local + data_bytes + 2560 + 8 * (data_bytes // 4), 2).view(np.uint32)
+        got = _read(buf.local, rows)
+        assert word[1] == 1 and word[0] == got[:1].view(np.uint32)[0]
+        assert rel_l2(got, O.matvec(14, w, rows, cols, x)) < 1e-5
+    finally:
+        buf.close()
+    ctx.synchronize()
