@@ -11,6 +11,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "peer_exchange.cuh"
 
 namespace si {
 
@@ -235,6 +236,9 @@ __global__ void __launch_bounds__(kGdnD) gdn_layer_kernel(const GdnLayerArgs a) 
   const uint32_t cq = khead * kGdnD + t, ck = kw + cq, cv = 2 * kw + h * kGdnD + col;
   pdl_launch_dependents();
   pdl_wait();
+  // the launch's epoch of the peer exchange (the previous grid has finished)
+  __shared__ uint32_t s_epoch;
+  if (a.xcore.n && t == 0) s_epoch = *reinterpret_cast<volatile uint32_t*>(a.xcore.epoch) + 1;
   // ---- every load of the step, independent of one another ----
   float* S = a.state + uint64_t(h) * kGdnD * kGdnD + uint64_t(warp) * kGdnCols * kGdnD + col;
   float s[kGdnCols];
@@ -393,9 +397,24 @@ __global__ void __launch_bounds__(kGdnD) gdn_layer_kernel(const GdnLayerArgs a) 
   __syncthreads();  // every warp has read part[] for the first reduction
   part[warp][lane] = r;
   __syncthreads();
-  if (warp == 0)
-    a.core[h * kGdnD + col] =
-        __fadd_rn(__fadd_rn(part[0][lane], part[1][lane]), __fadd_rn(part[2][lane], part[3][lane]));
+  if (warp == 0) {
+    const float o = __fadd_rn(__fadd_rn(part[0][lane], part[1][lane]), __fadd_rn(part[2][lane], part[3][lane]));
+    if (a.xcore.n) {
+      // this rank's core and z rows leave for every rank
+      const uint32_t row = h * kGdnD + col;
+      peer_store_row(a.xcore, s_epoch, row, o);
+      peer_store_row(a.xz, s_epoch, row, a.z_in[row]);
+    } else {
+      a.core[h * kGdnD + col] = o;
+    }
+  }
+  if (a.xcore.n) {
+    // this CTA's slices of the gathered core and z, then its ticket
+    const uint32_t cta = blockIdx.y * gridDim.x + blockIdx.x, nctas = gridDim.x * gridDim.y;
+    peer_unpack(a.xcore, cta, nctas, s_epoch, a.err, t, kGdnD);
+    peer_unpack(a.xz, cta, nctas, s_epoch, a.err, t, kGdnD);
+    peer_ticket(a.xcore, nctas, s_epoch, t, kGdnD);
+  }
 }
 
 void launch_gdn_layer(const GdnLayerArgs& a, cudaStream_t s, bool pdl) {

@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "qmatvec.cuh"  // PeerOut
+
 namespace si {
 
 // Bit-exact dequantization of `elements` values (quant.rs:18-174).
@@ -49,6 +51,14 @@ struct GdnLayerArgs {
   const float* dt_bias;
   float* core;             // [vh*128]
   uint32_t key_heads, value_heads, kernel;
+  // row-sharded model (xcore.n > 0): this rank's core rows and its z rows
+  // (z_in, [vh*128], the z projection's output) are gathered inside this
+  // kernel into every rank's full core and z vectors (xcore.y, xz.y), with
+  // the in-kernel exchange of the tensor-core matvecs (peer_exchange.cuh;
+  // the two share the ticket and the epoch)
+  PeerOut xcore, xz;
+  const float* z_in;
+  int* err;                // device error word for a timed-out exchange (may be null)
 };
 void launch_gdn_layer(const GdnLayerArgs& a, cudaStream_t s, bool pdl);
 

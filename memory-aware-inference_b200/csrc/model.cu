@@ -120,7 +120,7 @@ struct si_model {
   // in-kernel all-gather of the Q4_K matvecs' outputs (PeerOut): offsets in
   // the scratch block of the CTA ticket, the launch epoch and the exchange
   // words of the hidden and activation vectors (two parity halves each)
-  uint64_t xchg_ticket_off = 0, xchg_epoch_off = 0, ll_hidden_off = 0, ll_act_off = 0;
+  uint64_t xchg_ticket_off = 0, xchg_epoch_off = 0, ll_hidden_off = 0, ll_act_off = 0, ll_core_off = 0, ll_z_off = 0;
   // tensor-level retention: of a streamed layer l the packed bytes
   // [0, part_bytes[l]) stay resident at dev_part[l] (the ring copies the rest)
   std::vector<uint64_t> part_bytes;
@@ -374,11 +374,12 @@ uint64_t batch_qmm_bytes(const si_model& m) {
 
 // The exchange area of a sharded model (n > 1; it takes the place of the
 // verifier's buffers, which only one GPU has): ticket and epoch words, then
-// 8-byte exchange words for two parity halves of the hidden and of the
-// activation vector.
+// 8-byte exchange words for two parity halves of the hidden, the activation,
+// the GDN core and the z vector.
 uint64_t xchg_bytes(const si_model& m) {
   if (m.n == 1) return 0;
-  return 256 + 512 + align256(16ull * m.c.hidden) + align256(16ull * m.c.intermediate);
+  const uint64_t vw = uint64_t(m.c.gdn_value_heads) * 128;
+  return 256 + 512 + align256(16ull * m.c.hidden) + align256(16ull * m.c.intermediate) + 2 * align256(16 * vw);
 }
 
 uint64_t batch_bytes(const si_model& m) {
@@ -875,6 +876,8 @@ int create_model(si_ctx* ctx, const si_model_config* cfg, uint64_t seed,
       m->xchg_epoch_off = x0 + 256;
       m->ll_hidden_off = x0 + 512;
       m->ll_act_off = m->ll_hidden_off + align256(16ull * c.hidden);
+      m->ll_core_off = m->ll_act_off + align256(16ull * c.intermediate);
+      m->ll_z_off = m->ll_core_off + align256(16ull * c.gdn_value_heads * 128);
     }
     const std::vector<uint64_t> bf = batch_float_counts(*m);
     if (!bf.empty()) {
@@ -1509,13 +1512,36 @@ int gdn_layer(si_model* m, uint32_t l, const uint8_t* base) {
   g.key_heads = m->kh_l;
   g.value_heads = m->vh_l;
   g.kernel = c.conv_kernel;
+  g.err = m->ctx->d_err;
+  // sharded over NVLink peers: core and z are gathered inside the GDN kernel
+  const bool xg = m->n > 1 && m->p2p && m->n <= kPeerMax;
+  if (xg) {
+    const uint32_t vw = c.gdn_value_heads * 128;
+    PeerOut* xs[2] = {&g.xcore, &g.xz};
+    const uint64_t offs[2] = {m->ll_core_off, m->ll_z_off};
+    float* fulls[2] = {m->core_full, m->z_full};
+    for (int k = 0; k < 2; ++k) {
+      PeerOut& po = *xs[k];
+      po.n = uint32_t(m->n);
+      po.rank = uint32_t(m->r);
+      for (int i = 0; i < m->n; ++i)
+        po.ll[i] = reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(m->peer_block[i]) + offs[k]);
+      po.parity_stride = vw;
+      po.y = fulls[k];
+      po.row0 = uint32_t(m->r) * vw_l;
+      po.total = vw;
+      po.ticket = reinterpret_cast<uint32_t*>(m->scratch_block + m->xchg_ticket_off);
+      po.epoch = reinterpret_cast<uint32_t*>(m->scratch_block + m->xchg_epoch_off);
+      po.wait_cycles = kWaitCycles;
+    }
+    g.z_in = m->z;
+  }
   launch_gdn_layer(g, m->ctx->stream, true);
   m->conv_parity[l] = par ^ 1;
   const float* core = m->core;
   const float* z = m->z;
   if (m->n > 1) {
-    if ((rc = gather(m, m->core, m->core_full, vw_l, m->z, m->z_full, vw_l)))
-      return rc;
+    if (!xg && (rc = gather(m, m->core, m->core_full, vw_l, m->z, m->z_full, vw_l))) return rc;
     core = m->core_full;
     z = m->z_full;
   }
