@@ -1013,12 +1013,16 @@ constexpr int kMergePerLane = 19;
 constexpr uint32_t kMergeBatch = kMergeWarps * kMergePerLane;  // 152 splits
 constexpr uint32_t kMergeMaxSplits = 4096;
 
-__global__ void __launch_bounds__(kMergeDims * kMergeWarps) attn_merge_kernel(const AttnArgs a, uint32_t nsplit) {
+__global__ void __launch_bounds__(kMergeDims * kMergeWarps)
+    attn_merge_kernel(const __grid_constant__ AttnArgs a, uint32_t nsplit) {
   __shared__ float sw[kMergeMaxSplits];
   __shared__ float red[kMergeWarps][kMergeDims + 1];
   __shared__ float rm[kMergeWarps], rl[kMergeWarps];
+  __shared__ uint32_t s_epoch;
   pdl_launch_dependents();
   pdl_wait();
+  // the launch's epoch of the peer exchange (the previous grid has finished)
+  if (a.xatt.n && threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile uint32_t*>(a.xatt.epoch) + 1;
   const uint32_t qhd = blockIdx.x, hd = a.hd;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t d = blockIdx.y * kMergeDims + lane;
@@ -1083,7 +1087,23 @@ __global__ void __launch_bounds__(kMergeDims * kMergeWarps) attn_merge_kernel(co
       L += rl[w];
       o += red[w][lane];
     }
-    if (live) a.out[uint64_t(qhd) * hd + d] = o / L;
+    if (live) {
+      const uint32_t row = qhd * hd + d;
+      if (a.xatt.n) {
+        // this rank's output and gate rows leave for every rank
+        peer_store_row(a.xatt, s_epoch, row, o / L);
+        peer_store_row(a.xgate, s_epoch, row, a.gate_in[row]);
+      } else {
+        a.out[uint64_t(qhd) * hd + d] = o / L;
+      }
+    }
+  }
+  if (a.xatt.n) {
+    // this CTA's slices of the gathered output and gate, then its ticket
+    const uint32_t cta = blockIdx.y * gridDim.x + blockIdx.x, nctas = gridDim.x * gridDim.y;
+    peer_unpack(a.xatt, cta, nctas, s_epoch, a.err, threadIdx.x, blockDim.x);
+    peer_unpack(a.xgate, cta, nctas, s_epoch, a.err, threadIdx.x, blockDim.x);
+    peer_ticket(a.xatt, nctas, s_epoch, threadIdx.x, blockDim.x);
   }
 }
 

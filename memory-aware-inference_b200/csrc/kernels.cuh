@@ -85,6 +85,11 @@ struct AttnArgs {
   float* out;              // [qh*hd]
   uint32_t chunk;          // tokens per split (generic kernel)
   int* err;                // device error word for timed-out waits (may be null)
+  // row-sharded model (xatt.n > 0): the merge stores this rank's output rows
+  // and its gate rows (gate_in, [qh*hd]) as exchange words and gathers every
+  // rank's into xatt.y / xgate.y (peer_exchange.cuh), instead of writing out
+  PeerOut xatt, xgate;
+  const float* gate_in;
 };
 // Longest cache (cached tokens + 1) the attention entry points accept: the
 // generic kernel's 256-token chunks times the merge kernel's split limit.

@@ -120,7 +120,8 @@ struct si_model {
   // in-kernel all-gather of the Q4_K matvecs' outputs (PeerOut): offsets in
   // the scratch block of the CTA ticket, the launch epoch and the exchange
   // words of the hidden and activation vectors (two parity halves each)
-  uint64_t xchg_ticket_off = 0, xchg_epoch_off = 0, ll_hidden_off = 0, ll_act_off = 0, ll_core_off = 0, ll_z_off = 0;
+  uint64_t xchg_ticket_off = 0, xchg_epoch_off = 0, ll_hidden_off = 0, ll_act_off = 0, ll_core_off = 0, ll_z_off = 0,
+           ll_att_off = 0, ll_gate_off = 0;
   // tensor-level retention: of a streamed layer l the packed bytes
   // [0, part_bytes[l]) stay resident at dev_part[l] (the ring copies the rest)
   std::vector<uint64_t> part_bytes;
@@ -375,11 +376,12 @@ uint64_t batch_qmm_bytes(const si_model& m) {
 // The exchange area of a sharded model (n > 1; it takes the place of the
 // verifier's buffers, which only one GPU has): ticket and epoch words, then
 // 8-byte exchange words for two parity halves of the hidden, the activation,
-// the GDN core and the z vector.
+// the GDN core and z, and the attention output and gate vectors.
 uint64_t xchg_bytes(const si_model& m) {
   if (m.n == 1) return 0;
-  const uint64_t vw = uint64_t(m.c.gdn_value_heads) * 128;
-  return 256 + 512 + align256(16ull * m.c.hidden) + align256(16ull * m.c.intermediate) + 2 * align256(16 * vw);
+  const uint64_t vw = uint64_t(m.c.gdn_value_heads) * 128, qw = uint64_t(m.c.attn_q_heads) * m.c.attn_head_dim;
+  return 256 + 512 + align256(16ull * m.c.hidden) + align256(16ull * m.c.intermediate) + 2 * align256(16 * vw) +
+         2 * align256(16 * qw);
 }
 
 uint64_t batch_bytes(const si_model& m) {
@@ -878,6 +880,8 @@ int create_model(si_ctx* ctx, const si_model_config* cfg, uint64_t seed,
       m->ll_act_off = m->ll_hidden_off + align256(16ull * c.hidden);
       m->ll_core_off = m->ll_act_off + align256(16ull * c.intermediate);
       m->ll_z_off = m->ll_core_off + align256(16ull * c.gdn_value_heads * 128);
+      m->ll_att_off = m->ll_z_off + align256(16ull * c.gdn_value_heads * 128);
+      m->ll_gate_off = m->ll_att_off + align256(16ull * c.attn_q_heads * c.attn_head_dim);
     }
     const std::vector<uint64_t> bf = batch_float_counts(*m);
     if (!bf.empty()) {
@@ -1418,6 +1422,28 @@ int exchange_qmv(si_model* m, QmvParams p, float* full, uint64_t ll_off, uint32_
   return rc ? fail(m->ctx, rc, msg) : SI_OK;
 }
 
+// The exchange of one gathered vector of the sharded model (PeerOut): its
+// words at `ll_off` in every rank's scratch block, this rank's `local` rows
+// at rank * local of the `total`-row vector `full`.
+PeerOut xchg_out(si_model* m, uint64_t ll_off, float* full, uint32_t local, uint32_t total) {
+  PeerOut po = {};
+  po.n = uint32_t(m->n);
+  po.rank = uint32_t(m->r);
+  for (int i = 0; i < m->n; ++i)
+    po.ll[i] = reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(m->peer_block[i]) + ll_off);
+  po.parity_stride = total;
+  po.y = full;
+  po.row0 = uint32_t(m->r) * local;
+  po.total = total;
+  po.ticket = reinterpret_cast<uint32_t*>(m->scratch_block + m->xchg_ticket_off);
+  po.epoch = reinterpret_cast<uint32_t*>(m->scratch_block + m->xchg_epoch_off);
+  po.wait_cycles = kWaitCycles;
+  return po;
+}
+
+// Whether the sharded model's kernels gather their outputs themselves.
+bool in_kernel_gathers(const si_model* m) { return m->n > 1 && m->p2p && m->n <= kPeerMax; }
+
 int residual_matvec(si_model* m, QmvParams p, const uint8_t* w) {
   const uint32_t r0 = m->H_l * uint32_t(m->r);
   p.seg[0] = {w, m->n > 1 ? m->slice : m->hidden + r0, m->hidden + r0, m->H_l, 0};
@@ -1514,26 +1540,11 @@ int gdn_layer(si_model* m, uint32_t l, const uint8_t* base) {
   g.kernel = c.conv_kernel;
   g.err = m->ctx->d_err;
   // sharded over NVLink peers: core and z are gathered inside the GDN kernel
-  const bool xg = m->n > 1 && m->p2p && m->n <= kPeerMax;
+  const bool xg = in_kernel_gathers(m);
   if (xg) {
     const uint32_t vw = c.gdn_value_heads * 128;
-    PeerOut* xs[2] = {&g.xcore, &g.xz};
-    const uint64_t offs[2] = {m->ll_core_off, m->ll_z_off};
-    float* fulls[2] = {m->core_full, m->z_full};
-    for (int k = 0; k < 2; ++k) {
-      PeerOut& po = *xs[k];
-      po.n = uint32_t(m->n);
-      po.rank = uint32_t(m->r);
-      for (int i = 0; i < m->n; ++i)
-        po.ll[i] = reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(m->peer_block[i]) + offs[k]);
-      po.parity_stride = vw;
-      po.y = fulls[k];
-      po.row0 = uint32_t(m->r) * vw_l;
-      po.total = vw;
-      po.ticket = reinterpret_cast<uint32_t*>(m->scratch_block + m->xchg_ticket_off);
-      po.epoch = reinterpret_cast<uint32_t*>(m->scratch_block + m->xchg_epoch_off);
-      po.wait_cycles = kWaitCycles;
-    }
+    g.xcore = xchg_out(m, m->ll_core_off, m->core_full, vw_l, vw);
+    g.xz = xchg_out(m, m->ll_z_off, m->z_full, vw_l, vw);
     g.z_in = m->z;
   }
   launch_gdn_layer(g, m->ctx->stream, true);
@@ -1594,13 +1605,21 @@ int attn_layer(si_model* m, uint32_t l, const uint8_t* base, uint64_t position) 
   a.out = m->att;
   a.chunk = 256;
   a.err = m->ctx->d_err;
+  // sharded over NVLink peers: output and gate are gathered inside the merge
+  const bool xg = in_kernel_gathers(m);
+  if (xg) {
+    const uint32_t qw = c.attn_q_heads * hd;
+    a.xatt = xchg_out(m, m->ll_att_off, m->att_full, qw_l, qw);
+    a.xgate = xchg_out(m, m->ll_gate_off, m->gate_full, qw_l, qw);
+    a.gate_in = m->qg + qw_l;  // the gate half of the local q projection
+  }
   launch_attention(a, m->ctx->stream, true);
   m->cached[l]++;
   const float* att = m->att;
   const float* gate = m->qg + qw_l;
   if (m->n > 1) {
     // gate half of the local q projection is contiguous after the queries
-    if ((rc = gather(m, m->att, m->att_full, qw_l, m->qg + qw_l, m->gate_full, qw_l)))
+    if (!xg && (rc = gather(m, m->att, m->att_full, qw_l, m->qg + qw_l, m->gate_full, qw_l)))
       return rc;
     att = m->att_full;
     gate = m->gate_full;
