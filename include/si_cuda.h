@@ -353,7 +353,9 @@ int si_attention_layer_dev(si_ctx* ctx, const si_attention_layer_desc* desc, con
  * A peer buffer: `bytes` of device memory on every rank of the context's
  * communicator (one rank without one), each rank's copy mapped into every
  * other rank (CUDA IPC over NVLink). Collective: every rank calls it with the
- * same size. */
+ * same size. Each rank's allocation also holds the in-kernel exchange's
+ * words (two 8-byte words per float of the data) and its counters: about
+ * five times `bytes` in all. */
 typedef struct si_peer_buffer si_peer_buffer;
 int si_peer_buffer_create(si_ctx* ctx, uint64_t bytes, si_peer_buffer** out);
 /* A group of `nranks` buffers all on this context's GPU standing in for the
@@ -370,10 +372,12 @@ void* si_peer_buffer_local(const si_peer_buffer* buf);
  * [rank * rows_per_rank, (rank + 1) * rows_per_rank) of W as w_shard (device
  * memory) and x in full. Every rank's buffer receives the whole y (float32,
  * nranks * rows_per_rank values) at byte offset y_offset (16-byte aligned).
- * Q4_K shards run on the tensor-core matvec, whose epilogue stores each row
- * into every rank's copy over NVLink; the launch ends once every rank's rows
- * have landed (bounded wait; a timeout sets the context's error word). Other
- * types: matvec, then a peer all-gather launch. Device pointers, enqueued on
+ * Q4_K shards, and the Q6_K shards its tensor-core kernel takes, gather y
+ * inside the matvec: each row leaves as an 8-byte {value, epoch} word for
+ * every rank over NVLink, and each CTA unpacks its slice of y as the words
+ * arrive, so the launch ends with the whole y on every rank (bounded wait; a
+ * timeout sets the context's error word). Other types and shapes: matvec,
+ * then a peer all-gather launch. Device pointers, enqueued on
  * `stream` (NULL = the context's stream), nothing allocated or synchronised.
  * Every rank must make the same calls in the same order. After SI_E_TIMEOUT
  * the buffer's exchange state is lost: destroy it and create a new one. */
